@@ -1,0 +1,120 @@
+/*
+ * rq.h -- C ABI of librq, the B200 (sm_100a) quantized-linear and sparse-MoE
+ * library behind rustyllm's q4_kernel / StreamingLlamaQuantized /
+ * StreamingMixtral APIs.
+ *
+ * Conventions
+ *   - Every entry point returns int: RQ_OK (0) on success, otherwise an
+ *     RQ_ERR_* code; rq_last_error() then returns a thread-local message.
+ *     This maps onto the reference's `Error::Msg(String)` (src/error.rs:4-29)
+ *     the way q4_kernel.rs:90-107 builds its messages.  Nothing aborts.
+ *   - Weights are GGML block bytes exactly as they sit in a GGUF tensor
+ *     (Q4_0 = 18-byte blocks of 32, Q4_K = 144-byte super-blocks of 256,
+ *     Q3_K = 110-byte super-blocks of 256), row-major [out][in/block].
+ *     The library copies them to the GPU and owns the device copy.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
+ *   - Activation pointers (x, y) may be host or device memory; host pointers
+ *     are staged through device memory and the call returns with y filled.
+ *     Device pointers: the call is asynchronous on `stream`.
+ *   - One rq_ctx per device; calls on one ctx are serialised by the caller
+ *     (the reference's single-writer generate loop,
+ *     src/streaming_quantized.rs:345-351).  Weight handles are read-only
+ *     during forward calls and may be shared between threads.
+ */
+#ifndef RQ_H
+#define RQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define RQ_API
+#else
+#define RQ_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct rq_ctx rq_ctx;
+typedef struct rq_weight rq_weight;
+typedef struct rq_moe rq_moe;
+
+enum rq_status {
+    RQ_OK = 0,
+    RQ_ERR_INVALID = 1,     /* bad argument, shape or type */
+    RQ_ERR_CUDA = 2,        /* CUDA runtime error */
+    RQ_ERR_UNSUPPORTED = 3, /* valid request the library does not implement */
+    RQ_ERR_OOM = 4,         /* device allocation failed */
+    RQ_ERR_TIMEOUT = 5,     /* a bounded device or host wait gave up */
+    RQ_ERR_NCCL = 6         /* collective failed */
+};
+
+/* GGML type ids (ggml_type / candle GgmlDType numbering). */
+enum rq_ggml_type { RQ_Q4_0 = 2, RQ_Q3_K = 11, RQ_Q4_K = 12 };
+
+/* ---------------------------------------------------------------- context */
+
+/* Create a context on CUDA device `device`.  Replaces the implicit candle
+ * Device::Cuda(n) of src/inference.rs:56-70. */
+RQ_API int rq_init(int device, rq_ctx** out);
+RQ_API int rq_destroy(rq_ctx* ctx);
+
+/* Copy the calling thread's last error message into buf (NUL-terminated,
+ * truncated to n).  Returns the full message length. */
+RQ_API int rq_last_error(char* buf, size_t n);
+
+/* "rq <version> sm_100a" */
+RQ_API const char* rq_version(void);
+
+/* Bytes / elements per GGML block; 0 for an unknown type. */
+RQ_API size_t rq_block_bytes(int ggml_type);
+RQ_API int rq_block_elems(int ggml_type);
+
+/* ---------------------------------------------------------------- weights */
+
+/* Upload GGML blocks [out][in/block] (host or device pointer, nbytes must be
+ * exactly out*in/block*block_bytes).  Replaces QMatMul::from_arc over a
+ * GgufLayer tensor (src/streaming_quantized.rs:63-70) and
+ * ParallelQ4Linear::from_qtensor (src/q4_kernel.rs:89-171); in must be a
+ * multiple of the block size (src/q4_kernel.rs:104-108). */
+RQ_API int rq_weight_upload(rq_ctx* ctx, int ggml_type, const void* blocks, size_t nbytes,
+                     int64_t out, int64_t in, rq_weight** w);
+
+/* Quantize an f32 matrix [out][in] that is already on this device straight
+ * into a device weight (no host round trip).  Q4_0 follows the rule of
+ * src/q4_kernel.rs:137-163; Q4_K/Q3_K use librq's deterministic quantizer
+ * (the counterpart of candle's QTensor::quantize, src/quantize.rs:131). */
+RQ_API int rq_weight_quantize(rq_ctx* ctx, int ggml_type, const float* w_dev, int64_t out, int64_t in,
+                       rq_weight** w, void* stream);
+
+/* Copy a device weight back as GGML blocks into host memory. */
+RQ_API int rq_weight_download(rq_ctx* ctx, const rq_weight* w, void* blocks_host, size_t nbytes);
+
+RQ_API int rq_weight_free(rq_ctx* ctx, rq_weight* w);
+
+/* Any of the out-pointers may be NULL.  device_bytes counts the library's
+ * device copy (equal to the GGML byte count, plus 2 pad bytes per Q3_K
+ * super-block). */
+RQ_API int rq_weight_info(const rq_weight* w, int* ggml_type, int64_t* out, int64_t* in,
+                   size_t* device_bytes);
+
+/* y[out][in] = dequantized weight in f32, bit-identical to GGML's dequant
+ * (QTensor::dequantize, used at src/q4_kernel.rs:120-122). */
+RQ_API int rq_dequantize(rq_ctx* ctx, const rq_weight* w, float* y, void* stream);
+
+/* ----------------------------------------------------------------- linear */
+
+/* y[M][out] = x[M][in] * W^T in f32.  Replaces QMatMul::forward
+ * (src/streaming_quantized.rs:201-203,256,277-278) and
+ * ParallelQ4Linear::forward (src/q4_kernel.rs:183-256).  M=1 is the decode
+ * matvec; M=K+1 the speculative verify (examples/spec_decode_70b.rs:238);
+ * larger M the prefill (src/streaming_quantized.rs:569-575). */
+RQ_API int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t M,
+              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RQ_H */

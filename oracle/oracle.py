@@ -1,0 +1,190 @@
+"""ctypes wrapper over the CPU oracle (``rq_oracle.c``).
+
+TEST INFRASTRUCTURE ONLY: the checker for the CUDA path.  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg import this
+module; the product library never calls it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+
+Q4_0, Q3_K, Q4_K = 2, 11, 12
+BLOCK_BYTES = {Q4_0: 18, Q3_K: 110, Q4_K: 144}
+BLOCK_ELEMS = {Q4_0: 32, Q3_K: 256, Q4_K: 256}
+
+_lib = None
+
+
+def build() -> str:
+    """Compile the oracle in place (make); returns the library path."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P, I64, I, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+        L.rqo_quantize.argtypes = [I, P, I64, I64, P]
+        L.rqo_dequantize.argtypes = [I, P, I64, I64, P]
+        L.rqo_matmul_ref.argtypes = [I, P, I64, I64, P, I64, P, I]
+        L.rqo_linear_threaded.argtypes = [I, P, I64, I64, P, I64, P, I]
+        L.rqo_dot_q4_0_scalar.argtypes = [P, P, I64]
+        L.rqo_dot_q4_0_scalar.restype = F
+        L.rqo_dot_q4_0_avx2order.argtypes = [P, P, I64]
+        L.rqo_dot_q4_0_avx2order.restype = F
+        L.rqo_f32_to_f16_n.argtypes = [P, P, I64]
+        L.rqo_f16_to_f32_n.argtypes = [P, P, I64]
+        L.rqo_router_logits.argtypes = [P, I64, I64, P, I, P]
+        L.rqo_route_topk.argtypes = [P, I64, I, I, P, P]
+        L.rqo_permute.argtypes = [P, P, I64, I, I, P, P, P]
+        L.rqo_moe_forward.argtypes = [P, I64, I64, I64, I, I, P, I, P, P, P, P, P, P, P, I]
+        L.rqo_silu.argtypes = [F]
+        L.rqo_silu.restype = F
+        for fn in ("rqo_quantize", "rqo_dequantize", "rqo_matmul_ref", "rqo_linear_threaded",
+                   "rqo_moe_forward"):
+            getattr(L, fn).restype = I
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def row_bytes(qtype: int, n_in: int) -> int:
+    return n_in // BLOCK_ELEMS[qtype] * BLOCK_BYTES[qtype]
+
+
+def quantize(qtype: int, w: np.ndarray) -> np.ndarray:
+    """f32 [rows, in] -> GGML block bytes uint8 [rows, row_bytes]."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, n_in = w.shape
+    out = np.zeros((rows, row_bytes(qtype, n_in)), dtype=np.uint8)
+    rc = lib().rqo_quantize(qtype, _p(w), rows, n_in, _p(out))
+    if rc != 0:
+        raise ValueError(f"rqo_quantize failed ({rc})")
+    return out
+
+
+def dequantize(qtype: int, blocks: np.ndarray, rows: int, n_in: int) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    assert blocks.size == rows * row_bytes(qtype, n_in)
+    out = np.empty((rows, n_in), dtype=np.float32)
+    rc = lib().rqo_dequantize(qtype, _p(blocks), rows, n_in, _p(out))
+    if rc != 0:
+        raise ValueError(f"rqo_dequantize failed ({rc})")
+    return out
+
+
+def matmul_ref(qtype: int, blocks: np.ndarray, n_out: int, n_in: int, x: np.ndarray,
+               acc64: bool = False) -> np.ndarray:
+    """y = x @ deq(W).T, dequantize then dot (f32 or f64 accumulation)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, n_in)
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    y = np.empty((x.shape[0], n_out), dtype=np.float32)
+    rc = lib().rqo_matmul_ref(qtype, _p(blocks), n_out, n_in, _p(x), x.shape[0], _p(y), int(acc64))
+    if rc != 0:
+        raise ValueError(f"rqo_matmul_ref failed ({rc})")
+    return y
+
+
+def linear_threaded(qtype: int, blocks: np.ndarray, n_out: int, n_in: int, x: np.ndarray,
+                    nthreads: int = 0, y: np.ndarray | None = None) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, n_in)
+    if y is None:
+        y = np.empty((x.shape[0], n_out), dtype=np.float32)
+    rc = lib().rqo_linear_threaded(qtype, _p(blocks), n_out, n_in, _p(x), x.shape[0], _p(y),
+                                   nthreads)
+    if rc != 0:
+        raise ValueError(f"rqo_linear_threaded failed ({rc})")
+    return y
+
+
+def dot_q4_0_scalar(w_row: np.ndarray, x_row: np.ndarray) -> float:
+    nb = x_row.size // 32
+    return float(lib().rqo_dot_q4_0_scalar(_p(w_row), _p(x_row), nb))
+
+
+def dot_q4_0_avx2order(w_row: np.ndarray, x_row: np.ndarray) -> float:
+    nb = x_row.size // 32
+    return float(lib().rqo_dot_q4_0_avx2order(_p(w_row), _p(x_row), nb))
+
+
+def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    h = np.empty(x.shape, dtype=np.uint16)
+    lib().rqo_f32_to_f16_n(_p(x), _p(h), x.size)
+    return h
+
+
+def f16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    x = np.empty(h.shape, dtype=np.float32)
+    lib().rqo_f16_to_f32_n(_p(h), _p(x), h.size)
+    return x
+
+
+def router_logits(x: np.ndarray, wr: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    wr = np.ascontiguousarray(wr, dtype=np.float32)
+    T, H = x.shape
+    E = wr.shape[0]
+    out = np.empty((T, E), dtype=np.float32)
+    lib().rqo_router_logits(_p(x), T, H, _p(wr), E, _p(out))
+    return out
+
+
+def route_topk(logits: np.ndarray, k: int):
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    T, E = logits.shape
+    ids = np.empty((T, k), dtype=np.int32)
+    w = np.empty((T, k), dtype=np.float32)
+    lib().rqo_route_topk(_p(logits), T, E, k, _p(ids), _p(w))
+    return ids, w
+
+
+def permute(ids: np.ndarray, weights: np.ndarray, E: int):
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    weights = np.ascontiguousarray(weights, dtype=np.float32)
+    T, k = ids.shape
+    offs = np.empty(E + 1, dtype=np.int32)
+    rows = np.empty(T * k, dtype=np.int32)
+    sw = np.empty(T * k, dtype=np.float32)
+    lib().rqo_permute(_p(ids), _p(weights), T, E, k, _p(offs), _p(rows), _p(sw))
+    return offs, rows, sw
+
+
+def moe_forward(x: np.ndarray, wr: np.ndarray, qtype: int, w1: list, w3: list, w2: list,
+                F: int, k: int = 2, nthreads: int = 0):
+    """Full SparseMoe layer on the CPU; returns (y, ids, perm, offsets)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    wr = np.ascontiguousarray(wr, dtype=np.float32)
+    T, H = x.shape
+    E = wr.shape[0]
+    arr_t = ctypes.c_void_p * E
+    keep = [np.ascontiguousarray(a, dtype=np.uint8) for a in (*w1, *w3, *w2)]
+    p1 = arr_t(*[_p(a) for a in keep[:E]])
+    p3 = arr_t(*[_p(a) for a in keep[E:2 * E]])
+    p2 = arr_t(*[_p(a) for a in keep[2 * E:]])
+    y = np.empty((T, H), dtype=np.float32)
+    ids = np.empty((T, k), dtype=np.int32)
+    perm = np.empty(T * k, dtype=np.int32)
+    offs = np.empty(E + 1, dtype=np.int32)
+    rc = lib().rqo_moe_forward(_p(x), T, H, F, E, k, _p(wr), qtype, ctypes.cast(p1, ctypes.c_void_p),
+                               ctypes.cast(p3, ctypes.c_void_p), ctypes.cast(p2, ctypes.c_void_p),
+                               _p(y), _p(ids), _p(perm), _p(offs), nthreads)
+    if rc != 0:
+        raise ValueError(f"rqo_moe_forward failed ({rc})")
+    return y, ids, perm, offs

@@ -1,0 +1,90 @@
+/*
+ * rq_oracle.h -- CPU oracle for the quantized-linear / sparse-MoE path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker: the tests, the
+ * smoke check and the bench's CPU-baseline leg load it.  The product
+ * (librq.so) never links or calls it.
+ *
+ * It restates, in plain C, the arithmetic rustyllm runs on the CPU:
+ *   - Q4_0 repack quantizer            src/q4_kernel.rs:137-163
+ *   - Q4_0 scalar dot                  src/q4_kernel.rs:274-293
+ *   - Q4_0 AVX2 dot (lane order)       src/q4_kernel.rs:300-360
+ *   - row-chunked threaded forward     src/q4_kernel.rs:207-243
+ *   - GGML Q4_K / Q3_K dequantization  (candle-core 0.10.2 k-quants, reached
+ *     through QMatMul at src/streaming_quantized.rs:63-70); pinned bit-for-bit
+ *     against gguf-py 0.19.0 golden vectors in tests/golden/
+ *   - SparseMoe routing/permute/combine src/streaming_mixtral.rs:280-319
+ *
+ * Parity pins: Q4_0 follows the in-repo rule exactly.  Q4_K/Q3_K dequant is
+ * pinned to gguf-py's published dequantizer.  The Q4_K/Q3_K *quantizer* here
+ * is this project's own deterministic rule (candle's QTensor::quantize source
+ * is not available); every parity test feeds identical block bytes to the
+ * CPU and the GPU, so quantizer equality with candle is not needed for them.
+ */
+#ifndef RQ_ORACLE_H
+#define RQ_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { RQO_Q4_0 = 2, RQO_Q3_K = 11, RQO_Q4_K = 12 };
+
+uint16_t rqo_f32_to_f16(float f);
+float rqo_f16_to_f32(uint16_t h);
+void rqo_f32_to_f16_n(const float* x, uint16_t* h, int64_t n);
+void rqo_f16_to_f32_n(const uint16_t* h, float* x, int64_t n);
+
+/* bytes per block / elements per block of a GGML type; 0 if unknown */
+int64_t rqo_block_bytes(int type);
+int64_t rqo_block_elems(int type);
+
+/* quantize rows x f32 [rows][in] -> GGML blocks (row-major) */
+int rqo_quantize(int type, const float* x, int64_t rows, int64_t in, uint8_t* out);
+/* dequantize GGML blocks -> f32 [rows][in] */
+int rqo_dequantize(int type, const uint8_t* blocks, int64_t rows, int64_t in, float* out);
+
+/* y[m][o] = sum_k x[m][k] * deq(W)[o][k], dequantize-then-dot.
+ * acc64 = 0: f32 accumulation in ascending k; acc64 = 1: double accumulation. */
+int rqo_matmul_ref(int type, const uint8_t* blocks, int64_t out, int64_t in,
+                   const float* x, int64_t M, float* y, int acc64);
+
+/* q4_kernel.rs dot restatements, one row */
+float rqo_dot_q4_0_scalar(const uint8_t* w_row, const float* x_row, int64_t blocks_per_row);
+float rqo_dot_q4_0_avx2order(const uint8_t* w_row, const float* x_row, int64_t blocks_per_row);
+
+/* Threaded CPU forward, the CPU baseline.  Chunking follows
+ * q4_kernel.rs:207-243.  Q4_0 uses the AVX2-order dot; Q4_K/Q3_K use a
+ * dequant-fused f32 dot with 8 lanes.  nthreads <= 0 -> all cores. */
+int rqo_linear_threaded(int type, const uint8_t* blocks, int64_t out, int64_t in,
+                        const float* x, int64_t M, float* y, int nthreads);
+
+/* ---- sparse MoE (streaming_mixtral.rs:280-319) ---- */
+/* Router logits in the canonical order the GPU router kernel uses
+ * (32 strided f32 partials with fmaf, butterfly combine); see rq_oracle.c. */
+void rqo_router_logits(const float* x, int64_t T, int64_t H, const float* wr, int E, float* logits);
+/* softmax + stable descending top-k with renormalised weights.
+ * ids[T][k] in rank order, weights[T][k]. */
+void rqo_route_topk(const float* logits, int64_t T, int E, int k, int32_t* ids, float* weights);
+/* Bucket rows per expert in ascending token order.  offsets[E+1]; rows[T*k]
+ * holds token ids; slot_w[T*k] the matching routing weights. */
+void rqo_permute(const int32_t* ids, const float* weights, int64_t T, int E, int k,
+                 int32_t* offsets, int32_t* rows, float* slot_w);
+/* Full layer: route -> permute -> SwiGLU experts (w1=gate, w3=up, w2=down,
+ * all Q4_K) -> weighted combine in ascending expert order.
+ * w1/w3 blocks: [E] pointers to [F][H] weights; w2: [E] pointers to [H][F]. */
+int rqo_moe_forward(const float* x, int64_t T, int64_t H, int64_t F, int E, int k,
+                    const float* wr, int wtype, const uint8_t* const* w1,
+                    const uint8_t* const* w3, const uint8_t* const* w2, float* y,
+                    int32_t* ids_out, int32_t* perm_out, int32_t* offsets_out,
+                    int nthreads);
+
+/* silu in f32: x / (1 + exp(-x)) (candle_nn::ops::silu) */
+float rqo_silu(float x);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

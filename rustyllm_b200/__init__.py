@@ -1,0 +1,10 @@
+"""rustyllm_b200: B200-native (sm_100a) quantized-linear hot path for rustyllm.
+
+The compute lives in librq.so (hand-written CUDA behind the C ABI of
+include/rq.h); this package is the host-side mirror of the reference's API.
+"""
+from ._lib import Q3_K, Q4_0, Q4_K, RqError, lib
+from .linear import Context, ParallelQ4Linear, QMatMul, QTensor, QWeight
+
+__all__ = ["Q3_K", "Q4_0", "Q4_K", "RqError", "lib", "Context", "ParallelQ4Linear", "QMatMul",
+           "QTensor", "QWeight"]

@@ -1,0 +1,90 @@
+"""ctypes binding of librq.so (the C ABI declared in include/rq.h).
+
+The library is built in place (``rustyllm_b200/librq.so``).  Loading fails
+loudly when it is missing: there is no CPU fallback behind this package.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "librq.so")
+HEADERS = [os.path.join(os.path.dirname(HERE), "include", h) for h in ("rq.h",)]
+
+RQ_OK = 0
+Q4_0, Q3_K, Q4_K = 2, 11, 12
+TYPE_NAMES = {Q4_0: "Q4_0", Q3_K: "Q3_K", Q4_K: "Q4_K"}
+BLOCK_BYTES = {Q4_0: 18, Q3_K: 110, Q4_K: 144}
+BLOCK_ELEMS = {Q4_0: 32, Q3_K: 256, Q4_K: 256}
+
+
+class RqError(RuntimeError):
+    """A non-zero status from librq; the message is rq_last_error()
+    (the counterpart of the reference's ``Error::Msg``)."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"rq: {msg} (status {code})")
+        self.code = code
+
+
+P, I64, I, SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+PP = ctypes.POINTER(ctypes.c_void_p)
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "rq_init": (I, [I, PP]),
+    "rq_destroy": (I, [P]),
+    "rq_last_error": (I, [ctypes.c_char_p, SZ]),
+    "rq_version": (ctypes.c_char_p, []),
+    "rq_block_bytes": (SZ, [I]),
+    "rq_block_elems": (I, [I]),
+    "rq_weight_upload": (I, [P, I, P, SZ, I64, I64, PP]),
+    "rq_weight_quantize": (I, [P, I, P, I64, I64, PP, P]),
+    "rq_weight_download": (I, [P, P, P, SZ]),
+    "rq_weight_free": (I, [P, P]),
+    "rq_weight_info": (I, [P, ctypes.POINTER(I), ctypes.POINTER(I64), ctypes.POINTER(I64),
+                           ctypes.POINTER(SZ)]),
+    "rq_dequantize": (I, [P, P, P, P]),
+    "rq_linear": (I, [P, P, P, P, I64, P]),
+}
+
+_lib = None
+
+
+def declared_symbols() -> list[str]:
+    """Entry points declared in include/*.h (parsed from the headers)."""
+    names = []
+    for h in HEADERS:
+        with open(h) as f:
+            txt = f.read()
+        names += re.findall(r"^RQ_API\s+[\w\s\*]+?\b(rq_\w+)\s*\(", txt, flags=re.M)
+    return names
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"librq.so not built at {LIB_PATH}; run __graft_entry__.build() "
+                          "(make -C rustyllm_b200/csrc)")
+    L = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(1024)
+    lib().rq_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int) -> None:
+    if rc != RQ_OK:
+        raise RqError(rc, last_error())

@@ -1,0 +1,365 @@
+// rq_api.cu -- the extern "C" boundary of librq (declared in include/rq.h):
+// contexts, error reporting, weight upload / download, dispatch.
+
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "rq_internal.cuh"
+
+namespace rq {
+
+static thread_local char g_err[1024] = "";
+
+int set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return RQ_OK;
+    return set_error(e == cudaErrorMemoryAllocation ? RQ_ERR_OOM : RQ_ERR_CUDA, "%s: %s (%s)", what,
+                     cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+namespace {
+
+// Makes ctx->device current for the duration of a call and restores the
+// caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = (prev == dev) || cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+enum class Mem { Host, Device };
+
+Mem mem_kind(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();  // clear the sticky-free error of an unknown pointer
+        return Mem::Host;
+    }
+    return (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) ? Mem::Device
+                                                                                : Mem::Host;
+}
+
+bool valid_type(int t) { return t == RQ_Q4_0 || t == RQ_Q4_K || t == RQ_Q3_K; }
+
+const char* type_name(int t) {
+    switch (t) {
+    case RQ_Q4_0: return "Q4_0";
+    case RQ_Q4_K: return "Q4_K";
+    case RQ_Q3_K: return "Q3_K";
+    default: return "?";
+    }
+}
+
+int check_shape(int type, int64_t out, int64_t in) {
+    if (!valid_type(type))
+        return set_error(RQ_ERR_UNSUPPORTED, "unsupported ggml type %d (Q4_0=2, Q3_K=11, Q4_K=12)", type);
+    TypeInfo ti = type_info(type);
+    if (out <= 0 || in <= 0)
+        return set_error(RQ_ERR_INVALID, "weight shape [%lld, %lld] must be positive", (long long)out,
+                         (long long)in);
+    if (in % ti.block_elems)
+        return set_error(RQ_ERR_INVALID, "in_features %lld not divisible by %d (%s)", (long long)in,
+                         ti.block_elems, type_name(type));
+    return RQ_OK;
+}
+
+// A weight that views rows [r0, r0+n) of w.
+rq_weight row_view(const rq_weight* w, int64_t r0, int64_t n) {
+    TypeInfo ti = type_info(w->type);
+    rq_weight v = *w;
+    v.out = n;
+    v.qs = w->qs + r0 * w->nblk * ti.qs_bytes;
+    v.hdr = w->hdr + r0 * w->nblk * ti.hdr_bytes;
+    return v;
+}
+
+int alloc_weight(rq_ctx* ctx, int type, int64_t out, int64_t in, rq_weight** res) {
+    TypeInfo ti = type_info(type);
+    rq_weight* w = new (std::nothrow) rq_weight();
+    if (!w) return set_error(RQ_ERR_OOM, "host allocation failed");
+    w->type = type;
+    w->out = out;
+    w->in = in;
+    w->nblk = in / ti.block_elems;
+    w->device = ctx->device;
+    size_t qsz = (size_t)out * w->nblk * ti.qs_bytes;
+    size_t hsz = (size_t)out * w->nblk * ti.hdr_bytes;
+    size_t qpad = (qsz + 255) & ~(size_t)255;
+    w->bytes = qpad + hsz;
+    cudaError_t e = cudaMalloc(&w->base, w->bytes);
+    if (e != cudaSuccess) {
+        delete w;
+        return cuda_error(e, "cudaMalloc(weight)");
+    }
+    w->qs = (uint8_t*)w->base;
+    w->hdr = (uint8_t*)w->base + qpad;
+    if (type == RQ_Q3_K) {  // pad bytes of the Q3_K headers stay zero
+        e = cudaMemset(w->hdr, 0, hsz);
+        if (e != cudaSuccess) {
+            cudaFree(w->base);
+            delete w;
+            return cuda_error(e, "cudaMemset(weight)");
+        }
+    }
+    *res = w;
+    return RQ_OK;
+}
+
+constexpr size_t kStageBytes = 64u << 20;  // host<->device staging chunk
+
+}  // namespace
+
+int ensure_workspace(rq_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->ws_bytes) return RQ_OK;
+    if (ctx->ws) {
+        cudaError_t e = cudaFree(ctx->ws);  // implicit device sync: no kernel still uses it
+        ctx->ws = nullptr;
+        ctx->ws_bytes = 0;
+        if (e != cudaSuccess) return cuda_error(e, "cudaFree(workspace)");
+    }
+    size_t sz = std::max(bytes, (size_t)4 << 20);
+    cudaError_t e = cudaMalloc(&ctx->ws, sz);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(workspace)");
+    ctx->ws_bytes = sz;
+    return RQ_OK;
+}
+
+}  // namespace rq
+
+using namespace rq;
+
+extern "C" {
+
+int rq_last_error(char* buf, size_t n) {
+    size_t len = strlen(g_err);
+    if (buf && n) {
+        size_t c = std::min(len, n - 1);
+        memcpy(buf, g_err, c);
+        buf[c] = 0;
+    }
+    return (int)len;
+}
+
+const char* rq_version(void) { return "rq 0.1.0 sm_100a"; }
+
+size_t rq_block_bytes(int t) { return valid_type(t) ? (size_t)type_info(t).block_bytes : 0; }
+int rq_block_elems(int t) { return valid_type(t) ? type_info(t).block_elems : 0; }
+
+int rq_init(int device, rq_ctx** out) {
+    if (!out) return set_error(RQ_ERR_INVALID, "rq_init: out is NULL");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= n)
+        return set_error(RQ_ERR_INVALID, "device %d out of range (%d CUDA devices)", device, n);
+    DeviceGuard g(device);
+    if (!g.ok) return set_error(RQ_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetDeviceProperties");
+    if (prop.major != 10)
+        return set_error(RQ_ERR_UNSUPPORTED, "device %d is sm_%d%d; librq is built for sm_100a only",
+                         device, prop.major, prop.minor);
+    rq_ctx* c = new (std::nothrow) rq_ctx();
+    if (!c) return set_error(RQ_ERR_OOM, "host allocation failed");
+    c->device = device;
+    c->own_stream = nullptr;
+    c->ws = nullptr;
+    c->ws_bytes = 0;
+    c->sm_count = prop.multiProcessorCount;
+    *out = c;
+    return RQ_OK;
+}
+
+int rq_destroy(rq_ctx* ctx) {
+    if (!ctx) return RQ_OK;
+    DeviceGuard g(ctx->device);
+    if (ctx->ws) cudaFree(ctx->ws);
+    delete ctx;
+    return RQ_OK;
+}
+
+int rq_weight_upload(rq_ctx* ctx, int type, const void* blocks, size_t nbytes, int64_t out,
+                     int64_t in, rq_weight** res) {
+    if (!ctx || !blocks || !res) return set_error(RQ_ERR_INVALID, "rq_weight_upload: NULL argument");
+    *res = nullptr;
+    int rc = check_shape(type, out, in);
+    if (rc) return rc;
+    TypeInfo ti = type_info(type);
+    const int64_t row_bytes = in / ti.block_elems * ti.block_bytes;
+    if ((int64_t)nbytes != out * row_bytes)
+        return set_error(RQ_ERR_INVALID, "rq_weight_upload: %zu bytes given, %s [%lld, %lld] needs %lld",
+                         nbytes, type_name(type), (long long)out, (long long)in,
+                         (long long)(out * row_bytes));
+    DeviceGuard g(ctx->device);
+    rq_weight* w = nullptr;
+    rc = alloc_weight(ctx, type, out, in, &w);
+    if (rc) return rc;
+    const uint8_t* src = (const uint8_t*)blocks;
+    if (mem_kind(blocks) == Mem::Device) {
+        rc = launch_repack(w, src, 0, out, 0);
+        if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "repack");
+    } else {
+        int64_t rows_per = std::max<int64_t>(1, (int64_t)kStageBytes / row_bytes);
+        rows_per = std::min(rows_per, out);
+        uint8_t* stage = nullptr;
+        rc = cuda_error(cudaMalloc(&stage, (size_t)(rows_per * row_bytes)), "cudaMalloc(stage)");
+        for (int64_t r0 = 0; !rc && r0 < out; r0 += rows_per) {
+            int64_t n = std::min(rows_per, out - r0);
+            rc = cuda_error(cudaMemcpy(stage, src + r0 * row_bytes, (size_t)(n * row_bytes),
+                                       cudaMemcpyHostToDevice), "upload copy");
+            if (!rc) {
+                rq_weight v = row_view(w, r0, n);
+                rc = launch_repack(&v, stage, 0, n, 0);
+            }
+            if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "repack");
+        }
+        if (stage) cudaFree(stage);
+    }
+    if (rc) {
+        cudaFree(w->base);
+        delete w;
+        return rc;
+    }
+    *res = w;
+    return RQ_OK;
+}
+
+int rq_weight_quantize(rq_ctx* ctx, int type, const float* w_dev, int64_t out, int64_t in,
+                       rq_weight** res, void* stream) {
+    if (!ctx || !w_dev || !res) return set_error(RQ_ERR_INVALID, "rq_weight_quantize: NULL argument");
+    *res = nullptr;
+    int rc = check_shape(type, out, in);
+    if (rc) return rc;
+    if (mem_kind(w_dev) != Mem::Device)
+        return set_error(RQ_ERR_INVALID, "rq_weight_quantize: w must be device memory");
+    if ((reinterpret_cast<uintptr_t>(w_dev) & 15) != 0)
+        return set_error(RQ_ERR_INVALID, "rq_weight_quantize: w must be 16-byte aligned");
+    DeviceGuard g(ctx->device);
+    rq_weight* w = nullptr;
+    rc = alloc_weight(ctx, type, out, in, &w);
+    if (rc) return rc;
+    rc = launch_quantize(w, w_dev, (cudaStream_t)stream);
+    if (rc) {
+        cudaFree(w->base);
+        delete w;
+        return rc;
+    }
+    *res = w;
+    return RQ_OK;
+}
+
+int rq_weight_download(rq_ctx* ctx, const rq_weight* w, void* blocks_host, size_t nbytes) {
+    if (!ctx || !w || !blocks_host) return set_error(RQ_ERR_INVALID, "rq_weight_download: NULL argument");
+    TypeInfo ti = type_info(w->type);
+    const int64_t row_bytes = w->nblk * ti.block_bytes;
+    if ((int64_t)nbytes != w->out * row_bytes)
+        return set_error(RQ_ERR_INVALID, "rq_weight_download: buffer is %zu bytes, weight has %lld",
+                         nbytes, (long long)(w->out * row_bytes));
+    DeviceGuard g(ctx->device);
+    int64_t rows_per = std::min<int64_t>(w->out, std::max<int64_t>(1, (int64_t)kStageBytes / row_bytes));
+    uint8_t* stage = nullptr;
+    int rc = cuda_error(cudaMalloc(&stage, (size_t)(rows_per * row_bytes)), "cudaMalloc(stage)");
+    for (int64_t r0 = 0; !rc && r0 < w->out; r0 += rows_per) {
+        int64_t n = std::min(rows_per, w->out - r0);
+        rq_weight v = row_view(w, r0, n);
+        rc = launch_unpack(&v, stage, 0, n, 0);
+        if (!rc)
+            rc = cuda_error(cudaMemcpy((uint8_t*)blocks_host + r0 * row_bytes, stage,
+                                       (size_t)(n * row_bytes), cudaMemcpyDeviceToHost),
+                            "download copy");
+    }
+    if (stage) cudaFree(stage);
+    return rc;
+}
+
+int rq_weight_free(rq_ctx* ctx, rq_weight* w) {
+    if (!w) return RQ_OK;
+    DeviceGuard g(ctx ? ctx->device : w->device);
+    cudaError_t e = cudaFree(w->base);
+    delete w;
+    return cuda_error(e, "cudaFree(weight)");
+}
+
+int rq_weight_info(const rq_weight* w, int* type, int64_t* out, int64_t* in, size_t* device_bytes) {
+    if (!w) return set_error(RQ_ERR_INVALID, "rq_weight_info: NULL weight");
+    TypeInfo ti = type_info(w->type);
+    if (type) *type = w->type;
+    if (out) *out = w->out;
+    if (in) *in = w->in;
+    if (device_bytes) *device_bytes = (size_t)(w->out * w->nblk * (ti.qs_bytes + ti.hdr_bytes));
+    return RQ_OK;
+}
+
+int rq_dequantize(rq_ctx* ctx, const rq_weight* w, float* y, void* stream) {
+    if (!ctx || !w || !y) return set_error(RQ_ERR_INVALID, "rq_dequantize: NULL argument");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (mem_kind(y) == Mem::Device) return launch_dequant(w, y, st);
+    const int64_t row_f = w->in * (int64_t)sizeof(float);
+    int64_t rows_per = std::min<int64_t>(w->out, std::max<int64_t>(1, (int64_t)kStageBytes / row_f));
+    int rc = ensure_workspace(ctx, (size_t)(rows_per * row_f));
+    for (int64_t r0 = 0; !rc && r0 < w->out; r0 += rows_per) {
+        int64_t n = std::min(rows_per, w->out - r0);
+        rq_weight v = row_view(w, r0, n);
+        rc = launch_dequant(&v, (float*)ctx->ws, st);
+        if (!rc)
+            rc = cuda_error(cudaMemcpyAsync(y + r0 * w->in, ctx->ws, (size_t)(n * row_f),
+                                            cudaMemcpyDeviceToHost, st), "dequant copy");
+        if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "dequant sync");
+    }
+    return rc;
+}
+
+int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t M, void* stream) {
+    if (!ctx || !w || !x || !y) return set_error(RQ_ERR_INVALID, "rq_linear: NULL argument");
+    if (M < 0) return set_error(RQ_ERR_INVALID, "rq_linear: M = %lld", (long long)M);
+    if (M == 0) return RQ_OK;
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool x_dev = mem_kind(x) == Mem::Device, y_dev = mem_kind(y) == Mem::Device;
+    const size_t xq_sz = xq_bytes(M, w->in);
+    const size_t x_sz = x_dev ? 0 : (size_t)(M * w->in) * sizeof(float);
+    const size_t y_sz = y_dev ? 0 : (size_t)(M * w->out) * sizeof(float);
+    int rc = ensure_workspace(ctx, xq_sz + x_sz + y_sz + 512);
+    if (rc) return rc;
+    uint8_t* ws = (uint8_t*)ctx->ws;
+    XQ xq;
+    xq.planes = (int8_t*)ws;
+    xq.stats = (float4*)(ws + (((size_t)M * 3 * w->in + 255) & ~(size_t)255));
+    float* xd = x_dev ? const_cast<float*>(x) : (float*)(ws + ((xq_sz + 255) & ~(size_t)255));
+    float* yd = y_dev ? y : (float*)((uint8_t*)xd + (x_dev ? 0 : ((x_sz + 255) & ~(size_t)255)));
+    if (!y_dev && x_dev) yd = (float*)(ws + ((xq_sz + 255) & ~(size_t)255));
+    if (!x_dev) {
+        rc = cuda_error(cudaMemcpyAsync(xd, x, x_sz, cudaMemcpyHostToDevice, st), "x copy");
+        if (rc) return rc;
+    }
+    rc = launch_xquant(xd, M, w->in, xq, st);
+    if (!rc) rc = launch_linear(w, xq, yd, M, ctx->sm_count, st);
+    if (rc) return rc;
+    if (!y_dev) {
+        rc = cuda_error(cudaMemcpyAsync(y, yd, y_sz, cudaMemcpyDeviceToHost, st), "y copy");
+        if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "rq_linear sync");
+    }
+    return rc;
+}
+
+}  // extern "C"

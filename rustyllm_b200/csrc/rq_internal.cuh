@@ -1,0 +1,105 @@
+// rq_internal.cuh -- shared definitions of librq (not part of the ABI).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/rq.h"
+
+namespace rq {
+
+// ------------------------------------------------------------ device layout
+//
+// A weight lives on the GPU split into two arrays, both row-major over
+// [out][nblk] (nblk = in / block elements):
+//   qs  : the quant bytes of each block, 16-byte aligned per block so that
+//         128-bit loads are aligned and coalesced;
+//   hdr : the per-block scale bytes.
+//   Q4_K  qs 128 B (GGML bytes 16..143)     hdr 16 B (d, dmin, 12 scale bytes)
+//   Q3_K  qs  96 B (hmask 32 + qs 64)       hdr 16 B (12 scale bytes, d, 2 pad)
+//   Q4_0  qs  16 B (GGML bytes 2..17)       hdr  2 B (d)
+// Bytes keep their GGML order inside each part, so the total equals the GGML
+// size (Q3_K adds 2 pad bytes per super-block).
+struct TypeInfo {
+    int type;
+    int block_elems;  // 32 or 256
+    int block_bytes;  // GGML bytes per block
+    int qs_bytes;     // device quant bytes per block
+    int hdr_bytes;    // device header bytes per block
+};
+
+__host__ __device__ inline TypeInfo type_info(int t) {
+    switch (t) {
+    case RQ_Q4_K: return TypeInfo{RQ_Q4_K, 256, 144, 128, 16};
+    case RQ_Q3_K: return TypeInfo{RQ_Q3_K, 256, 110, 96, 16};
+    case RQ_Q4_0: return TypeInfo{RQ_Q4_0, 32, 18, 16, 2};
+    default: return TypeInfo{0, 0, 0, 0, 0};
+    }
+}
+
+// ------------------------------------------------------ activation staging
+//
+// The linear kernels consume activations pre-quantized per 32-element block
+// into a 24-bit fixed-point value X = rint(x * 127*65536 / amax) split into
+// three balanced signed bytes (X = 65536*x1 + 256*x2 + x3), stored as three
+// int8 planes, plus per block: sx = amax / (127*65536), the f32 sum of the
+// first 16, of the last 16 elements.  |x - X*sx| <= ~1.5*sx, i.e. about
+// 2e-7 of the block's largest magnitude, so the integer dot products that
+// follow lose nothing measurable against the f32 path.
+constexpr float kXQScale = 8323072.0f;  // 127 * 65536
+
+struct XQ {             // one activation matrix [M][in] in staged form
+    int8_t* planes;     // [M][3][in]
+    float4* stats;      // [M][in/32] : (sx, sum16a, sum16b, 0)
+};
+
+inline size_t xq_bytes(int64_t M, int64_t in) {
+    size_t p = (size_t)M * 3 * (size_t)in;
+    p = (p + 255) & ~(size_t)255;
+    return p + (size_t)M * (size_t)(in / 32) * sizeof(float4);
+}
+
+}  // namespace rq
+
+struct rq_weight {
+    int type;
+    int64_t out, in, nblk;
+    uint8_t* qs;
+    uint8_t* hdr;
+    void* base;   // single allocation holding qs and hdr
+    size_t bytes; // allocation size
+    int device;
+};
+
+struct rq_ctx {
+    int device;
+    cudaStream_t own_stream;  // used for host-pointer calls when stream == NULL
+    void* ws;                 // workspace (activation staging, host-path buffers)
+    size_t ws_bytes;
+    int sm_count;
+};
+
+namespace rq {
+
+// error handling (rq_api.cu)
+int set_error(int code, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+int ensure_workspace(rq_ctx* ctx, size_t bytes);
+
+// layout kernels (rq_layout.cu)
+int launch_repack(const rq_weight* w, const uint8_t* raw_dev, int64_t row0, int64_t rows,
+                  cudaStream_t st);
+int launch_unpack(const rq_weight* w, uint8_t* raw_dev, int64_t row0, int64_t rows,
+                  cudaStream_t st);
+int launch_dequant(const rq_weight* w, float* y, cudaStream_t st);
+int launch_quantize(const rq_weight* w, const float* x, cudaStream_t st);
+
+// linear kernels (rq_matvec.cu)
+int launch_xquant(const float* x, int64_t M, int64_t in, XQ xq, cudaStream_t st);
+int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count,
+                  cudaStream_t st);
+
+}  // namespace rq

@@ -1,0 +1,383 @@
+// rq_layout.cu -- GGML <-> device layout, exact dequantization, and the
+// on-device quantizers.
+//
+// This translation unit is compiled with -fmad=false and spells every
+// rounding step with __f*_rn intrinsics: dequantization must be bit-identical
+// to GGML's (w = (d*sc)*q - (dmin*m), two roundings), and the quantizers must
+// produce the same bytes as the CPU quantizer on the same f32 input.
+
+#include "rq_internal.cuh"
+
+namespace rq {
+namespace {
+
+// --------------------------------------------------------------- repacking
+
+// Map byte b of a GGML block to (is_header, offset) in the device layout.
+__device__ __forceinline__ bool ggml_byte_slot(int type, int b, int* off) {
+    if (type == RQ_Q4_K) {  // [d dmin scales(12)] [qs 128]
+        if (b < 16) { *off = b; return true; }
+        *off = b - 16; return false;
+    }
+    if (type == RQ_Q3_K) {  // [hmask 32][qs 64][scales 12][d 2]
+        if (b < 96) { *off = b; return false; }
+        *off = b - 96; return true;  // scales 0..11, d 12..13
+    }
+    // Q4_0: [d 2][qs 16]
+    if (b < 2) { *off = b; return true; }
+    *off = b - 2; return false;
+}
+
+__global__ void repack_kernel(int type, int bb, int qsb, int hb, const uint8_t* __restrict__ raw,
+                              uint8_t* __restrict__ qs, uint8_t* __restrict__ hdr, int64_t blk0,
+                              int64_t nbytes) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (; i < nbytes; i += stride) {
+        int64_t blk = i / bb + blk0;
+        int b = (int)(i % bb);
+        int off;
+        if (ggml_byte_slot(type, b, &off)) hdr[blk * hb + off] = raw[i];
+        else qs[blk * qsb + off] = raw[i];
+    }
+}
+
+__global__ void unpack_kernel(int type, int bb, int qsb, int hb, uint8_t* __restrict__ raw,
+                              const uint8_t* __restrict__ qs, const uint8_t* __restrict__ hdr,
+                              int64_t blk0, int64_t nbytes) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (; i < nbytes; i += stride) {
+        int64_t blk = i / bb + blk0;
+        int b = (int)(i % bb);
+        int off;
+        raw[i] = ggml_byte_slot(type, b, &off) ? hdr[blk * hb + off] : qs[blk * qsb + off];
+    }
+}
+
+// ----------------------------------------------------------- dequantization
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t* s, int* sc, int* m) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 0x0f) | ((s[j - 4] >> 6) << 4);
+        *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+// One thread per 32 output elements.
+__global__ void dequant_kernel(int type, const uint8_t* __restrict__ qs,
+                               const uint8_t* __restrict__ hdr, int64_t out, int64_t in,
+                               float* __restrict__ y) {
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t n32 = out * in / 32;
+    if (t >= n32) return;
+    float v[32];
+    if (type == RQ_Q4_K) {
+        int64_t sbi = t / 8;  // super-block index, row-major over [out][nblk]
+        int s = (int)(t % 8); // sub-block
+        const uint8_t* h = hdr + sbi * 16;
+        const uint8_t* q = qs + sbi * 128 + 32 * (s / 2);
+        float d = h2f((uint16_t)(h[0] | (h[1] << 8)));
+        float dmin = h2f((uint16_t)(h[2] | (h[3] << 8)));
+        int sc, m;
+        q4k_scale_min(s, h + 4, &sc, &m);
+        float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+        int shift = (s & 1) * 4;
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = __fsub_rn(__fmul_rn(d1, (float)((q[j] >> shift) & 15)), m1);
+    } else if (type == RQ_Q3_K) {
+        int64_t sbi = t / 8;
+        int c = (int)(t % 8);  // 32-element chunk: h = c/4, s = c%4
+        const uint8_t* hm = qs + sbi * 96;
+        const uint8_t* q = hm + 32;
+        const uint8_t* h = hdr + sbi * 16;
+        float d = h2f((uint16_t)(h[12] | (h[13] << 8)));
+        int hh = c / 4, s = c % 4;
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            int sub = 2 * c + half;  // 16-element sub-block
+            int lo = sub < 8 ? (h[sub] & 15) : (h[sub - 8] >> 4);
+            int hi = (h[8 + (sub % 4)] >> (2 * (sub / 4))) & 3;
+            float dl = __fmul_rn(d, (float)((lo | (hi << 4)) - 32));
+#pragma unroll
+            for (int jj = 0; jj < 16; jj++) {
+                int j = 16 * half + jj;
+                int low = (q[32 * hh + j] >> (2 * s)) & 3;
+                int hb = (hm[j] >> c) & 1;
+                v[j] = __fmul_rn(dl, (float)(low - (hb ? 0 : 4)));
+            }
+        }
+    } else {  // Q4_0
+        const uint8_t* q = qs + t * 16;
+        float d = h2f((uint16_t)(hdr[2 * t] | (hdr[2 * t + 1] << 8)));
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            v[j] = __fmul_rn(d, (float)((q[j] & 15) - 8));
+            v[j + 16] = __fmul_rn(d, (float)((q[j] >> 4) - 8));
+        }
+    }
+    float4* dst = reinterpret_cast<float4*>(y + t * 32);
+#pragma unroll
+    for (int k = 0; k < 8; k++) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+
+// --------------------------------------------------------------- quantizers
+//
+// Same f32 operations, in the same order, as the CPU quantizer
+// (quantize_q4_k_block / quantize_q3_k_block / the Q4_0 rule of
+// src/q4_kernel.rs:137-163), so equal input gives equal bytes.
+
+// Q4_K: one warp per super-block; lane l holds elements 8l..8l+7
+// (sub-block l/4, group l/8).
+__global__ void quant_q4k_kernel(const float* __restrict__ x, int64_t nsb_total,
+                                 uint8_t* __restrict__ qs, uint8_t* __restrict__ hdr) {
+    int64_t sbi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    int lane = threadIdx.x & 31;
+    if (sbi >= nsb_total) return;  // warp-uniform
+    const float4* src = reinterpret_cast<const float4*>(x + sbi * 256 + 8 * lane);
+    float4 a = src[0], b = src[1];
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float mn = v[0], mx = v[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) { mn = fminf(mn, v[i]); mx = fmaxf(mx, v[i]); }
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (mn > 0.0f) mn = 0.0f;
+    float scale = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+    float mins = -mn;
+    float max_scale = scale, max_min = mins;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        max_scale = fmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, o));
+        max_min = fmaxf(max_min, __shfl_xor_sync(0xffffffffu, max_min, o));
+    }
+    float inv_scale = max_scale > 0.0f ? __fdiv_rn(63.0f, max_scale) : 0.0f;
+    float inv_min = max_min > 0.0f ? __fdiv_rn(63.0f, max_min) : 0.0f;
+    int ls = min(63, __float2int_rn(__fmul_rn(inv_scale, scale)));
+    int lm = min(63, __float2int_rn(__fmul_rn(inv_min, mins)));
+    __half dh = __float2half_rn(__fdiv_rn(max_scale, 63.0f));
+    __half mh = __float2half_rn(__fdiv_rn(max_min, 63.0f));
+    float d = __half2float(dh), dmin = __half2float(mh);
+    float dl = __fmul_rn(d, (float)ls), ml = __fmul_rn(dmin, (float)lm);
+    uint32_t pk[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        int q = 0;
+        if (dl != 0.0f) q = min(15, max(0, __float2int_rn(__fdiv_rn(__fadd_rn(v[i], ml), dl))));
+        pk[i / 4] |= (uint32_t)q << (8 * (i % 4));
+    }
+    // lanes with (l%8) < 4 hold low nibbles of bytes 8*(l%8)..+7 of group l/8,
+    // the partner lane l^4 the high nibbles.
+    uint32_t p0 = __shfl_xor_sync(0xffffffffu, pk[0], 4);
+    uint32_t p1 = __shfl_xor_sync(0xffffffffu, pk[1], 4);
+    if ((lane & 7) < 4) {
+        uint2 outv = make_uint2(pk[0] | (p0 << 4), pk[1] | (p1 << 4));
+        *reinterpret_cast<uint2*>(qs + sbi * 128 + 32 * (lane / 8) + 8 * (lane & 7)) = outv;
+    }
+    int all_ls[8], all_lm[8];
+#pragma unroll
+    for (int s = 0; s < 8; s++) {
+        all_ls[s] = __shfl_sync(0xffffffffu, ls, 4 * s);
+        all_lm[s] = __shfl_sync(0xffffffffu, lm, 4 * s);
+    }
+    if (lane == 0) {
+        uint8_t hb[16];
+        uint16_t dbits = __half_as_ushort(dh), mbits = __half_as_ushort(mh);
+        hb[0] = (uint8_t)dbits; hb[1] = (uint8_t)(dbits >> 8);
+        hb[2] = (uint8_t)mbits; hb[3] = (uint8_t)(mbits >> 8);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            hb[4 + j] = (uint8_t)(all_ls[j] | ((all_ls[j + 4] >> 4) << 6));
+            hb[8 + j] = (uint8_t)(all_lm[j] | ((all_lm[j + 4] >> 4) << 6));
+            hb[12 + j] = (uint8_t)((all_ls[j + 4] & 15) | ((all_lm[j + 4] & 15) << 4));
+        }
+        uint4 hv;
+        hv.x = hb[0] | (hb[1] << 8) | (hb[2] << 16) | ((uint32_t)hb[3] << 24);
+        hv.y = hb[4] | (hb[5] << 8) | (hb[6] << 16) | ((uint32_t)hb[7] << 24);
+        hv.z = hb[8] | (hb[9] << 8) | (hb[10] << 16) | ((uint32_t)hb[11] << 24);
+        hv.w = hb[12] | (hb[13] << 8) | (hb[14] << 16) | ((uint32_t)hb[15] << 24);
+        *reinterpret_cast<uint4*>(hdr + sbi * 16) = hv;
+    }
+}
+
+// Q3_K: one warp per super-block; lane l holds elements 8l..8l+7
+// (16-element sub-block l/2; 32-element chunk c = l/4: h = c/4, s = c%4;
+// byte offset j = 8*(l%4) .. +7).
+__global__ void quant_q3k_kernel(const float* __restrict__ x, int64_t nsb_total,
+                                 uint8_t* __restrict__ qs, uint8_t* __restrict__ hdr) {
+    int64_t sbi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    int lane = threadIdx.x & 31;
+    if (sbi >= nsb_total) return;
+    const float4* src = reinterpret_cast<const float4*>(x + sbi * 256 + 8 * lane);
+    float4 a = src[0], b = src[1];
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float ma = 0.0f, mv = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float av = fabsf(v[i]);
+        if (av > ma) { ma = av; mv = v[i]; }
+    }
+    // sub-block = lanes (2k, 2k+1); the first strict maximum wins
+    float ma_o = __shfl_xor_sync(0xffffffffu, ma, 1);
+    float mv_o = __shfl_xor_sync(0xffffffffu, mv, 1);
+    if (lane & 1) {  // upper half: keep own only if strictly larger than lower
+        if (!(ma > ma_o)) { ma = ma_o; mv = mv_o; }
+    } else {
+        if (ma_o > ma) { ma = ma_o; mv = mv_o; }
+    }
+    float scale = __fdiv_rn(mv, -4.0f);
+    // first sub-block with the largest |scale|
+    float best = fabsf(scale);
+    float best_s = scale;
+    int best_i = lane >> 1;
+#pragma unroll
+    for (int o = 2; o < 32; o <<= 1) {
+        float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        float os = __shfl_xor_sync(0xffffffffu, best_s, o);
+        int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (ob > best || (ob == best && oi < best_i)) { best = ob; best_s = os; best_i = oi; }
+    }
+    float max_scale = best > 0.0f ? best_s : 0.0f;
+    float iscale = max_scale != 0.0f ? __fdiv_rn(-32.0f, max_scale) : 0.0f;
+    int l = __float2int_rn(__fmul_rn(iscale, scale));
+    l = max(-32, min(31, l));
+    __half dh = __float2half_rn(iscale != 0.0f ? __fdiv_rn(1.0f, iscale) : 0.0f);
+    float d = __half2float(dh);
+    float dl = __fmul_rn(d, (float)l);
+    int c = lane / 4, s = c % 4, hh = c / 4;
+    unsigned long long qpart = 0ull, hpart = 0ull;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        int q = 0;
+        if (dl != 0.0f) q = max(-4, min(3, __float2int_rn(__fdiv_rn(v[i], dl))));
+        int u = q + 4;
+        qpart |= (unsigned long long)((u & 3) << (2 * s)) << (8 * i);
+        hpart |= (unsigned long long)((u >> 2) << c) << (8 * i);
+    }
+    // OR the 2-bit fields of the 4 shift groups (lanes differing in bits 2,3)
+    qpart |= __shfl_xor_sync(0xffffffffu, qpart, 4);
+    qpart |= __shfl_xor_sync(0xffffffffu, qpart, 8);
+    // OR the high bits of all 8 chunks (lanes differing in bits 2,3,4)
+    hpart |= __shfl_xor_sync(0xffffffffu, hpart, 4);
+    hpart |= __shfl_xor_sync(0xffffffffu, hpart, 8);
+    hpart |= __shfl_xor_sync(0xffffffffu, hpart, 16);
+    uint8_t* base = qs + sbi * 96;
+    if (s == 0) *reinterpret_cast<unsigned long long*>(base + 32 + 32 * hh + 8 * (lane & 3)) = qpart;
+    if (c == 0) *reinterpret_cast<unsigned long long*>(base + 8 * (lane & 3)) = hpart;
+    int all_l[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) all_l[k] = __shfl_sync(0xffffffffu, l, 2 * k) + 32;
+    if (lane == 0) {
+        uint8_t sb[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) sb[k] = 0;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            int vv = all_l[k];
+            if (k < 8) sb[k] |= (uint8_t)(vv & 15);
+            else sb[k - 8] |= (uint8_t)((vv & 15) << 4);
+            sb[8 + (k % 4)] |= (uint8_t)((vv >> 4) << (2 * (k / 4)));
+        }
+        uint16_t dbits = __half_as_ushort(dh);
+        sb[12] = (uint8_t)dbits;
+        sb[13] = (uint8_t)(dbits >> 8);
+        sb[14] = 0;
+        sb[15] = 0;
+        uint4 hv;
+        hv.x = sb[0] | (sb[1] << 8) | (sb[2] << 16) | ((uint32_t)sb[3] << 24);
+        hv.y = sb[4] | (sb[5] << 8) | (sb[6] << 16) | ((uint32_t)sb[7] << 24);
+        hv.z = sb[8] | (sb[9] << 8) | (sb[10] << 16) | ((uint32_t)sb[11] << 24);
+        hv.w = sb[12] | (sb[13] << 8) | (sb[14] << 16) | ((uint32_t)sb[15] << 24);
+        *reinterpret_cast<uint4*>(hdr + sbi * 16) = hv;
+    }
+}
+
+// Q4_0: one thread per 32-element block (src/q4_kernel.rs:137-163).
+__global__ void quant_q40_kernel(const float* __restrict__ x, int64_t nblk_total,
+                                 uint8_t* __restrict__ qs, uint8_t* __restrict__ hdr) {
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= nblk_total) return;
+    const float* c = x + t * 32;
+    float max_abs = 0.0f, max_signed = 0.0f;
+    for (int i = 0; i < 32; i++) {
+        float a = fabsf(c[i]);
+        if (a > max_abs) { max_abs = a; max_signed = c[i]; }
+    }
+    float d = __fdiv_rn(max_signed, -8.0f);
+    float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    __half dh = __float2half_rn(d);
+    uint16_t bits = __half_as_ushort(dh);
+    hdr[2 * t] = (uint8_t)bits;
+    hdr[2 * t + 1] = (uint8_t)(bits >> 8);
+    uint8_t* q = qs + t * 16;
+    for (int i = 0; i < 16; i++) {
+        float a = __fadd_rn(__fmul_rn(c[i], id), 8.5f);
+        float b = __fadd_rn(__fmul_rn(c[i + 16], id), 8.5f);
+        a = (a != a) ? 0.0f : fminf(fmaxf(a, 0.0f), 15.0f);
+        b = (b != b) ? 0.0f : fminf(fmaxf(b, 0.0f), 15.0f);
+        q[i] = (uint8_t)(__float2uint_rz(a) | (__float2uint_rz(b) << 4));
+    }
+}
+
+int grid_for(int64_t n, int threads) {
+    int64_t g = (n + threads - 1) / threads;
+    return (int)(g > (1 << 30) ? (1 << 30) : g);
+}
+
+}  // namespace
+
+int launch_repack(const rq_weight* w, const uint8_t* raw_dev, int64_t row0, int64_t rows,
+                  cudaStream_t st) {
+    TypeInfo ti = type_info(w->type);
+    int64_t nbytes = rows * w->nblk * ti.block_bytes;
+    if (nbytes == 0) return RQ_OK;
+    int64_t grid = (nbytes + 255) / 256;
+    if (grid > 148 * 64) grid = 148 * 64;
+    repack_kernel<<<(unsigned)grid, 256, 0, st>>>(w->type, ti.block_bytes, ti.qs_bytes, ti.hdr_bytes,
+                                                  raw_dev, w->qs, w->hdr, row0 * w->nblk, nbytes);
+    return cuda_error(cudaGetLastError(), "repack kernel");
+}
+
+int launch_unpack(const rq_weight* w, uint8_t* raw_dev, int64_t row0, int64_t rows,
+                  cudaStream_t st) {
+    TypeInfo ti = type_info(w->type);
+    int64_t nbytes = rows * w->nblk * ti.block_bytes;
+    if (nbytes == 0) return RQ_OK;
+    int64_t grid = (nbytes + 255) / 256;
+    if (grid > 148 * 64) grid = 148 * 64;
+    unpack_kernel<<<(unsigned)grid, 256, 0, st>>>(w->type, ti.block_bytes, ti.qs_bytes, ti.hdr_bytes,
+                                                  raw_dev, w->qs, w->hdr, row0 * w->nblk, nbytes);
+    return cuda_error(cudaGetLastError(), "unpack kernel");
+}
+
+int launch_dequant(const rq_weight* w, float* y, cudaStream_t st) {
+    int64_t n32 = w->out * w->in / 32;
+    if (n32 == 0) return RQ_OK;
+    dequant_kernel<<<grid_for(n32, 256), 256, 0, st>>>(w->type, w->qs, w->hdr, w->out, w->in, y);
+    return cuda_error(cudaGetLastError(), "dequant kernel");
+}
+
+int launch_quantize(const rq_weight* w, const float* x, cudaStream_t st) {
+    if (w->out * w->in == 0) return RQ_OK;
+    if (w->type == RQ_Q4_K || w->type == RQ_Q3_K) {
+        int64_t nsb = w->out * w->nblk;
+        int64_t threads = nsb * 32;
+        if (w->type == RQ_Q4_K)
+            quant_q4k_kernel<<<grid_for(threads, 256), 256, 0, st>>>(x, nsb, w->qs, w->hdr);
+        else
+            quant_q3k_kernel<<<grid_for(threads, 256), 256, 0, st>>>(x, nsb, w->qs, w->hdr);
+    } else {
+        int64_t nb = w->out * w->nblk;
+        quant_q40_kernel<<<grid_for(nb, 128), 128, 0, st>>>(x, nb, w->qs, w->hdr);
+    }
+    return cuda_error(cudaGetLastError(), "quantize kernel");
+}
+
+}  // namespace rq
