@@ -313,7 +313,11 @@ int rq_dequantize(rq_ctx* ctx, const rq_weight* w, float* y, void* stream) {
     if (!ctx || !w || !y) return set_error(RQ_ERR_INVALID, "rq_dequantize: NULL argument");
     DeviceGuard g(ctx->device);
     cudaStream_t st = (cudaStream_t)stream;
-    if (mem_kind(y) == Mem::Device) return launch_dequant(w, y, st);
+    if (mem_kind(y) == Mem::Device) {
+        if ((reinterpret_cast<uintptr_t>(y) & 15) != 0)
+            return set_error(RQ_ERR_INVALID, "rq_dequantize: device y must be 16-byte aligned");
+        return launch_dequant(w, y, st);
+    }
     const int64_t row_f = w->in * (int64_t)sizeof(float);
     int64_t rows_per = std::min<int64_t>(w->out, std::max<int64_t>(1, (int64_t)kStageBytes / row_f));
     int rc = ensure_workspace(ctx, (size_t)(rows_per * row_f));

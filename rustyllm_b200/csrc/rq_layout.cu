@@ -158,6 +158,10 @@ __global__ void quant_q4k_kernel(const float* __restrict__ x, int64_t nsb_total,
         max_scale = fmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, o));
         max_min = fmaxf(max_min, __shfl_xor_sync(0xffffffffu, max_min, o));
     }
+    // the CPU quantizer starts both maxima at +0.0 and only replaces them
+    // with larger values: an all-zero (or all -0.0) set stays +0.0
+    if (!(max_scale > 0.0f)) max_scale = 0.0f;
+    if (!(max_min > 0.0f)) max_min = 0.0f;
     float inv_scale = max_scale > 0.0f ? __fdiv_rn(63.0f, max_scale) : 0.0f;
     float inv_min = max_min > 0.0f ? __fdiv_rn(63.0f, max_min) : 0.0f;
     int ls = min(63, __float2int_rn(__fmul_rn(inv_scale, scale)));
@@ -312,10 +316,9 @@ __global__ void quant_q40_kernel(const float* __restrict__ x, int64_t nblk_total
     }
     float d = __fdiv_rn(max_signed, -8.0f);
     float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    __half dh = __float2half_rn(d);
-    uint16_t bits = __half_as_ushort(dh);
-    hdr[2 * t] = (uint8_t)bits;
-    hdr[2 * t + 1] = (uint8_t)(bits >> 8);
+    // the header array is 256-byte aligned, so block t's f16 scale is a
+    // naturally aligned 16-bit word
+    reinterpret_cast<__half*>(hdr)[t] = __float2half_rn(d);
     uint8_t* q = qs + t * 16;
     for (int i = 0; i < 16; i++) {
         float a = __fadd_rn(__fmul_rn(c[i], id), 8.5f);

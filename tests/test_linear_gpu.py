@@ -85,7 +85,9 @@ def test_gpu_quantizer_matches_oracle_bytes(oracle, rq_ctx, qtype):
     wd = torch.from_numpy(w).cuda()
     qw = QWeight.quantize(rq_ctx, qtype, wd)
     torch.cuda.synchronize()
-    assert np.array_equal(qw.download(), oracle.quantize(qtype, w))
+    got, want = qw.download(), oracle.quantize(qtype, w)
+    bad = np.argwhere(got != want)
+    assert bad.size == 0, f"{len(bad)} bytes differ, first (row, byte): {bad[:8].tolist()}"
 
 
 def test_device_pointers_and_streams(oracle, rq_ctx):
