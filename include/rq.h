@@ -114,6 +114,30 @@ RQ_API int rq_dequantize(rq_ctx* ctx, const rq_weight* w, float* y, void* stream
 RQ_API int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t M,
               void* stream);
 
+/* rq_linear for callers that cannot allocate device memory.  No counterpart
+ * in the reference.
+ *
+ * rq_linear stages activations in a workspace it grows with cudaMalloc.
+ * Callers whose device memory is owned by someone else (a serving engine
+ * that reserves nearly all HBM up front, a framework allocator such as
+ * candle's CUDA device) or whose decode loop cannot afford a cudaMalloc
+ * that may synchronise the device use this entry point instead: it calls no
+ * cudaMalloc, cudaFree or other allocating routine.  Its staging area is a
+ * static 2 MiB device array that every GPU loading librq holds until exit.
+ *
+ *   - x [M][in] and y [M][out] must be device memory on w's device;
+ *   - M * in is limited by the 2 MiB array at 3.5 bytes per element (plus
+ *     alignment); larger requests fail with RQ_ERR_INVALID and a message;
+ *   - the first call on a device resolves the array's device address
+ *     (cudaGetSymbolAddress): make that first call before any stream
+ *     capture;
+ *   - all calls on a device share the one array, which keeps the last
+ *     call's contents: calls that overlap on the GPU (other streams,
+ *     threads) race on it, so serialise them.
+ * Results equal rq_linear's (same kernels). */
+RQ_API int rq_linear_noalloc(const rq_weight* w, const float* x, float* y, int64_t M,
+                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

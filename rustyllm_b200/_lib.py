@@ -48,6 +48,7 @@ SIGNATURES = {
                            ctypes.POINTER(SZ)]),
     "rq_dequantize": (I, [P, P, P, P]),
     "rq_linear": (I, [P, P, P, P, I64, P]),
+    "rq_linear_noalloc": (I, [P, P, P, I64, P]),
 }
 
 _lib = None
