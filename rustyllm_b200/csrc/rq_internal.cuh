@@ -97,6 +97,11 @@ int launch_unpack(const rq_weight* w, uint8_t* raw_dev, int64_t row0, int64_t ro
 int launch_dequant(const rq_weight* w, float* y, cudaStream_t st);
 int launch_quantize(const rq_weight* w, const float* x, cudaStream_t st);
 
+// bulk-copy pipelined matvec (rq_mv_pipe.cu); err may be NULL
+bool pipe_supported(const rq_weight* w);
+int launch_matvec_pipe(const rq_weight* w, XQ xq, float* y, int sm_count, cudaStream_t st,
+                       int* err = nullptr);
+
 // linear kernels (rq_matvec.cu)
 int launch_xquant(const float* x, int64_t M, int64_t in, XQ xq, cudaStream_t st);
 int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count,

@@ -1,0 +1,353 @@
+// rq_mv_common.cuh -- per-lane dot-product pieces shared by the matvec
+// kernels (register-streaming fallback in rq_matvec.cu, bulk-copy pipeline in
+// rq_mv_pipe.cu).
+//
+// A K-slice is 2048 elements.  Within a slice lane l owns 64 elements:
+//   Q4_K: group l (super-block l/4, 64-element group l%4): 32 quant bytes
+//         [32l, 32l+32) of the slice, header of super-block l/4;
+//   Q3_K: quarter l%4 of super-block l/4 (h = bit 1, u = bit 0): elements
+//         128h + 32s + 16u + jj (s, jj in 0..3, 0..15);
+//   Q4_0: blocks 2l and 2l+1 of the slice.
+// The activation planes of those 64 elements stay in registers (48 words)
+// for every row the lane processes.
+#pragma once
+
+#include "rq_internal.cuh"
+
+namespace rq {
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// d1*65536 + d2*256 + d3 with one final rounding
+__device__ __forceinline__ float fix24(int d1, int d2, int d3) {
+    return fmaf((float)d1, 65536.0f, (float)(d2 * 256 + d3));
+}
+
+// ------------------------------------------------------ transpose reduction
+// v[0..N) are this lane's partials for N rows.  Afterwards v[0] holds the
+// full 32-lane sum of row row_of_lane<N>(lane), on the lanes for which
+// lane_writes<N>(lane) is true.
+template <int N, int CNT, int OFF>
+__device__ __forceinline__ void transpose_reduce_step(float (&v)[N], int lane) {
+    if constexpr (OFF > 0) {
+        if constexpr (CNT > 1) {
+            constexpr int HALF = CNT / 2;
+            const bool upper = (lane & OFF) != 0;
+#pragma unroll
+            for (int i = 0; i < HALF; i++) {
+                const float send = upper ? v[i] : v[i + HALF];
+                const float keep = upper ? v[i + HALF] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+            }
+            transpose_reduce_step<N, HALF, OFF / 2>(v, lane);
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], OFF);
+            transpose_reduce_step<N, 1, OFF / 2>(v, lane);
+        }
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void transpose_reduce(float (&v)[N], int lane) {
+    transpose_reduce_step<N, N, 16>(v, lane);
+}
+
+template <int N>
+__device__ __forceinline__ int row_of_lane(int lane) {
+    int row = 0, cnt = N;
+#pragma unroll
+    for (int off = 16; off >= 1 && cnt > 1; off >>= 1) {
+        cnt >>= 1;
+        if (lane & off) row += cnt;
+    }
+    return row;
+}
+
+template <int N>
+__device__ __forceinline__ bool lane_writes(int lane) {
+    constexpr int used = (N >= 32) ? 5 : (N >= 16) ? 4 : (N >= 8) ? 3 : (N >= 4) ? 2 : (N >= 2) ? 1 : 0;
+    return (lane & ((1 << (5 - used)) - 1)) == 0;
+}
+
+// ------------------------------------------------------------------- Q4_K
+
+struct Q4KLane {
+    uint32_t p[3][16];  // planes of elements 64g .. 64g+63 of the super-block
+    float sxl, xsl, sxh, xsh;
+    uint32_t mL, mH;
+    int sh;
+    bool hiG;
+};
+
+__device__ __forceinline__ void q4k_lane_setup(Q4KLane& L, const int8_t* planes,
+                                               const float4* stats, int64_t in, int64_t sb,
+                                               int g) {
+    const int64_t pos = sb * 256 + 64 * g;
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+        const uint4* src = reinterpret_cast<const uint4*>(planes + p * in + pos);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint4 u = src[k];
+            L.p[p][4 * k] = u.x; L.p[p][4 * k + 1] = u.y;
+            L.p[p][4 * k + 2] = u.z; L.p[p][4 * k + 3] = u.w;
+        }
+    }
+    const float4 lo = stats[sb * 8 + 2 * g];
+    const float4 hi = stats[sb * 8 + 2 * g + 1];
+    L.sxl = lo.x;
+    L.xsl = lo.y + lo.z;
+    L.sxh = hi.x * 0.0625f;  // high nibbles are masked in place: 16*q
+    L.xsh = hi.y + hi.z;
+    L.hiG = g >= 2;
+    L.sh = 16 * (g & 1);
+    L.mL = L.hiG ? 0x0F0Fu : 0x3F3Fu;
+    L.mH = L.hiG ? 0x3030u : 0u;
+}
+
+// One row: 32 quant bytes (qa, qb) of the lane's group and the super-block
+// header h.  Returns the lane's contribution to y[row].
+__device__ __forceinline__ float q4k_lane_row(const Q4KLane& L, uint4 qa, uint4 qb, uint4 h) {
+    const uint32_t wv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    int l1 = 0, l2 = 0, l3 = 0, h1 = 0, h2 = 0, h3 = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const uint32_t lo = wv[k] & 0x0F0F0F0Fu;
+        const uint32_t hi = wv[k] & 0xF0F0F0F0u;
+        l1 = dp4a_us(lo, L.p[0][k], l1);
+        l2 = dp4a_us(lo, L.p[1][k], l2);
+        l3 = dp4a_us(lo, L.p[2][k], l3);
+        h1 = dp4a_us(hi, L.p[0][8 + k], h1);
+        h2 = dp4a_us(hi, L.p[1][8 + k], h2);
+        h3 = dp4a_us(hi, L.p[2][8 + k], h3);
+    }
+    const float fl = fix24(l1, l2, l3) * L.sxl;
+    const float fh = fix24(h1, h2, h3) * L.sxh;
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+    // 6-bit (scale, min) of sub-blocks 2g, 2g+1 (GGML Q4_K packing)
+    const uint32_t A = L.hiG ? h.w : h.y;
+    const uint32_t B = L.hiG ? (h.w >> 4) : h.z;
+    const uint32_t scp = ((A >> L.sh) & L.mL) | ((h.y >> (L.sh + 2)) & L.mH);
+    const uint32_t mp = ((B >> L.sh) & L.mL) | ((h.z >> (L.sh + 2)) & L.mH);
+    const float sc0 = (float)(scp & 0xFFu), sc1 = (float)((scp >> 8) & 0xFFu);
+    const float m0 = (float)(mp & 0xFFu), m1 = (float)((mp >> 8) & 0xFFu);
+    return dd.x * fmaf(sc0, fl, sc1 * fh) - dd.y * fmaf(m0, L.xsl, m1 * L.xsh);
+}
+
+// Q4_K lane for the shared-memory pipeline.  The lane's 32 quant bytes are
+// read as two 16-byte halves in a lane-dependent order (half h1 first, h1 =
+// bit 2 of the lane) so each quarter-warp's 128-bit shared loads hit distinct
+// banks; the activation words are stored in the same order at set-up, so no
+// per-row register swap is needed.  The four 6-bit values of sub-blocks
+// (2g, 2g+1) are gathered with two byte permutes and lane-constant masks.
+struct Q4KPLane {
+    uint32_t xa[3][8];  // half A: [plane][0..3 low-nibble words, 4..7 high-nibble words]
+    uint32_t xb[3][8];  // half B
+    float sxl, xsl, sxh, xsh;
+    uint32_t sel1, sel2, mA, mB, mC;
+    bool hiG;
+};
+
+__device__ __forceinline__ void q4kp_lane_setup(Q4KPLane& L, const int8_t* planes,
+                                                const float4* stats, int64_t in, int64_t sb,
+                                                int g, int h1, bool valid) {
+    const int64_t pos = sb * 256 + 64 * g;
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+        const int8_t* base = planes + p * in + pos;
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            const int hsel = half == 0 ? h1 : 1 - h1;
+            uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = make_uint4(0u, 0u, 0u, 0u);
+            if (valid) {
+                lo = *reinterpret_cast<const uint4*>(base + 16 * hsel);
+                hi = *reinterpret_cast<const uint4*>(base + 32 + 16 * hsel);
+            }
+            uint32_t* dst = half == 0 ? L.xa[p] : L.xb[p];
+            dst[0] = lo.x; dst[1] = lo.y; dst[2] = lo.z; dst[3] = lo.w;
+            dst[4] = hi.x; dst[5] = hi.y; dst[6] = hi.z; dst[7] = hi.w;
+        }
+    }
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+    if (valid) {
+        lo = stats[sb * 8 + 2 * g];
+        hi = stats[sb * 8 + 2 * g + 1];
+    }
+    L.sxl = lo.x;
+    L.xsl = lo.y + lo.z;
+    L.sxh = hi.x * 0.0625f;  // high nibbles are masked in place: 16*q
+    L.xsh = hi.y + hi.z;
+    L.hiG = g >= 2;
+    const uint32_t j = 2u * (uint32_t)(g & 1);
+    // g < 2:  bytes [s[j], s[j+1], s[j+4], s[j+5]] of (h.y, h.z)
+    // g >= 2: bytes [s[j+8], s[j+9], s[j+8], s[j+9]] of h.w (j relative), and
+    //         top bits from [s[j], s[j+1], s[j+4], s[j+5]] of (h.y, h.z)
+    const uint32_t yz = j | ((j + 1) << 4) | ((j + 4) << 8) | ((j + 5) << 12);
+    L.sel1 = L.hiG ? (j | ((j + 1) << 4) | (j << 8) | ((j + 1) << 12)) : yz;
+    L.sel2 = yz;
+    L.mA = L.hiG ? 0x00000F0Fu : 0x3F3F3F3Fu;
+    L.mB = L.hiG ? 0x0F0F0000u : 0u;
+    L.mC = L.hiG ? 0x30303030u : 0u;
+}
+
+__device__ __forceinline__ float q4kp_lane_row(const Q4KPLane& L, uint4 qa, uint4 qb, uint4 h,
+                                               float part) {
+    const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w};
+    const uint32_t wb[4] = {qb.x, qb.y, qb.z, qb.w};
+    int l1 = 0, l2 = 0, l3 = 0, h1 = 0, h2 = 0, h3 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const uint32_t lo = wa[k] & 0x0F0F0F0Fu, hi = wa[k] & 0xF0F0F0F0u;
+        l1 = dp4a_us(lo, L.xa[0][k], l1);
+        l2 = dp4a_us(lo, L.xa[1][k], l2);
+        l3 = dp4a_us(lo, L.xa[2][k], l3);
+        h1 = dp4a_us(hi, L.xa[0][4 + k], h1);
+        h2 = dp4a_us(hi, L.xa[1][4 + k], h2);
+        h3 = dp4a_us(hi, L.xa[2][4 + k], h3);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const uint32_t lo = wb[k] & 0x0F0F0F0Fu, hi = wb[k] & 0xF0F0F0F0u;
+        l1 = dp4a_us(lo, L.xb[0][k], l1);
+        l2 = dp4a_us(lo, L.xb[1][k], l2);
+        l3 = dp4a_us(lo, L.xb[2][k], l3);
+        h1 = dp4a_us(hi, L.xb[0][4 + k], h1);
+        h2 = dp4a_us(hi, L.xb[1][4 + k], h2);
+        h3 = dp4a_us(hi, L.xb[2][4 + k], h3);
+    }
+    const float fl = fix24(l1, l2, l3) * L.sxl;
+    const float fh = fix24(h1, h2, h3) * L.sxh;
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+    const uint32_t x1 = __byte_perm(L.hiG ? h.w : h.y, h.z, L.sel1);
+    const uint32_t x2 = __byte_perm(h.y, h.z, L.sel2);
+    const uint32_t w = (x1 & L.mA) | ((x1 >> 4) & L.mB) | ((x2 >> 2) & L.mC);  // [sc0, sc1, m0, m1]
+    const float sc0 = (float)(w & 0xFFu), sc1 = (float)((w >> 8) & 0xFFu);
+    const float m0 = (float)((w >> 16) & 0xFFu), m1 = (float)(w >> 24);
+    part = fmaf(dd.x, fmaf(sc0, fl, sc1 * fh), part);
+    return fmaf(-dd.y, fmaf(m0, L.xsl, m1 * L.xsh), part);
+}
+
+// ------------------------------------------------------------------- Q3_K
+
+struct Q3KLane {
+    uint32_t p[3][4][4];  // [plane][run s][word]
+    float sx[4], xs16[4];
+    int h, u;
+};
+
+__device__ __forceinline__ void q3k_lane_setup(Q3KLane& L, const int8_t* planes,
+                                               const float4* stats, int64_t in, int64_t sb,
+                                               int qq) {
+    L.h = qq >> 1;
+    L.u = qq & 1;
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int64_t pos = sb * 256 + 128 * L.h + 32 * s + 16 * L.u;
+#pragma unroll
+        for (int p = 0; p < 3; p++) {
+            const uint4 v = *reinterpret_cast<const uint4*>(planes + p * in + pos);
+            L.p[p][s][0] = v.x; L.p[p][s][1] = v.y; L.p[p][s][2] = v.z; L.p[p][s][3] = v.w;
+        }
+        const float4 st = stats[sb * 8 + 4 * L.h + s];
+        L.sx[s] = st.x;
+        L.xs16[s] = L.u ? st.z : st.y;
+    }
+}
+
+// hm: hmask bytes [16u, +16); qv: 2-bit quant bytes [32h+16u, +16);
+// hd: header (scales 0..11, d at 12..13).
+__device__ __forceinline__ float q3k_lane_row(const Q3KLane& L, uint4 hm, uint4 qv, uint4 hd) {
+    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+    const uint32_t hw[4] = {hm.x, hm.y, hm.z, hm.w};
+    const float d = __half2float(__ushort_as_half((unsigned short)(hd.w & 0xFFFFu)));
+    const uint32_t lo8[2] = {hd.x, hd.y};
+    float acc = 0.0f;
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        int a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint32_t hq = (hw[c] >> (4 * L.h)) & 0x0F0F0F0Fu;
+            const uint32_t ql = (qw[c] >> (2 * s)) & 0x03030303u;
+            const uint32_t hb = (s <= 2 ? (hq << (2 - s)) : (hq >> 1)) & 0x04040404u;
+            const uint32_t q = ql | hb;  // q + 4 in 0..7
+            a1 = dp4a_us(q, L.p[0][s][c], a1);
+            a2 = dp4a_us(q, L.p[1][s][c], a2);
+            a3 = dp4a_us(q, L.p[2][s][c], a3);
+        }
+        // 6-bit scale of 16-element sub-block 8h + 2s + u
+        const int k = L.u + 2 * s;
+        const int lo4 = (int)((lo8[k >> 2] >> (8 * (k & 3) + 4 * L.h)) & 15u);
+        const int kb = L.u + 2 * (s & 1);
+        const int hi2 = (int)((hd.z >> (8 * kb + 2 * (2 * L.h + (s >> 1)))) & 3u);
+        const float scale = (float)((lo4 | (hi2 << 4)) - 32);
+        acc = fmaf(scale, fmaf(fix24(a1, a2, a3), L.sx[s], -4.0f * L.xs16[s]), acc);
+    }
+    return d * acc;
+}
+
+// ------------------------------------------------------------------- Q4_0
+
+struct Q40Lane {
+    uint32_t p[3][16];
+    float sx0, sx1, xs0, xs1;
+    bool has1;
+};
+
+__device__ __forceinline__ void q40_lane_setup(Q40Lane& L, const int8_t* planes,
+                                               const float4* stats, int64_t in, int64_t nblk,
+                                               int64_t b0) {
+    L.has1 = b0 + 1 < nblk;
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+        const uint4* src = reinterpret_cast<const uint4*>(planes + p * in + b0 * 32);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            uint4 v = (k < 2 || L.has1) ? src[k] : make_uint4(0u, 0u, 0u, 0u);
+            L.p[p][4 * k] = v.x; L.p[p][4 * k + 1] = v.y;
+            L.p[p][4 * k + 2] = v.z; L.p[p][4 * k + 3] = v.w;
+        }
+    }
+    const float4 st0 = stats[b0];
+    const float4 st1 = L.has1 ? stats[b0 + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
+    L.sx0 = st0.x * 0.0625f;
+    L.sx1 = st1.x * 0.0625f;
+    L.xs0 = 8.0f * (st0.y + st0.z);
+    L.xs1 = 8.0f * (st1.y + st1.z);
+}
+
+// qa, qb: quant bytes of blocks b0, b0+1; d0, d1: their f16 scales.
+__device__ __forceinline__ float q40_lane_row(const Q40Lane& L, uint4 qa, uint4 qb, uint16_t d0b,
+                                              uint16_t d1b) {
+    const uint32_t wv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    int a[2][3];
+#pragma unroll
+    for (int blk = 0; blk < 2; blk++) {
+        int e1 = 0, e2 = 0, e3 = 0, f1 = 0, f2 = 0, f3 = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t w = wv[4 * blk + k];
+            const uint32_t lo = w & 0x0F0F0F0Fu, hi = w & 0xF0F0F0F0u;
+            e1 = dp4a_us(lo, L.p[0][8 * blk + k], e1);
+            e2 = dp4a_us(lo, L.p[1][8 * blk + k], e2);
+            e3 = dp4a_us(lo, L.p[2][8 * blk + k], e3);
+            f1 = dp4a_us(hi, L.p[0][8 * blk + 4 + k], f1);
+            f2 = dp4a_us(hi, L.p[1][8 * blk + 4 + k], f2);
+            f3 = dp4a_us(hi, L.p[2][8 * blk + 4 + k], f3);
+        }
+        a[blk][0] = 16 * e1 + f1;  // 16 * sum(q * x_plane)
+        a[blk][1] = 16 * e2 + f2;
+        a[blk][2] = 16 * e3 + f3;
+    }
+    const float d0 = __half2float(__ushort_as_half(d0b));
+    const float d1 = __half2float(__ushort_as_half(d1b));
+    const float v0 = fmaf(fix24(a[0][0], a[0][1], a[0][2]), L.sx0, -L.xs0);
+    const float v1 = fmaf(fix24(a[1][0], a[1][1], a[1][2]), L.sx1, -L.xs1);
+    return fmaf(d0, v0, d1 * v1);
+}
+
+}  // namespace rq
