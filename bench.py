@@ -3,8 +3,9 @@
 
 A step is one pass of the decode hot path over one 70B layer's seven
 quantized linears (q, k, v, o: 8192->8192/1024/1024/8192; gate, up:
-8192->28672; down: 28672->8192), each called through librq's public entry
-point rq_linear with device-resident activations.  Weights are random
+8192->28672; down: 28672->8192) through librq's public entry points with
+device-resident activations, grouped as a decoder issues them: q/k/v in one
+rq_linear_batch call on their shared x, o, gate/up in one batch call, down.  Weights are random
 N(0, 0.02) f32 quantized to Q4_K on the device; x ~ N(0, 1).  Steps rotate
 over 4 distinct layer copies (1.93 GB > 126 MB L2), so every weight byte
 comes from HBM.  value = algorithmic bytes (weights + x + y) per step / time.
@@ -197,6 +198,8 @@ def run_reference(args) -> None:
 
 
 def run_gpu(args) -> None:
+    import ctypes
+
     import torch
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -222,40 +225,67 @@ def run_gpu(args) -> None:
             del wf
         weights.append(layer)
     torch.cuda.synchronize()
-    xs = [torch.randn(1, i, device=dev, generator=g) for _, i, _ in SHAPES]
+    # activations: q/k/v share one x, gate/up share one x (as QAttn / QMlp do)
+    x_attn = torch.randn(1, 8192, device=dev, generator=g)
+    x_o = torch.randn(1, 8192, device=dev, generator=g)
+    x_mlp = torch.randn(1, 8192, device=dev, generator=g)
+    x_down = torch.randn(1, 28672, device=dev, generator=g)
+    xs = [x_attn, x_attn, x_attn, x_o, x_mlp, x_mlp, x_down]
     ys = [torch.empty(1, o, device=dev) for _, _, o in SHAPES]
     stream = torch.cuda.Stream(device=dev)
+    arr = lambda vals: (ctypes.c_void_p * len(vals))(*vals)  # noqa: E731
+    groups = [(0, 1, 2), (3,), (4, 5), (6,)]  # q/k/v batched, o, gate/up batched, down
+
+    def launch_group(c, grp, st):
+        if len(grp) == 1:
+            k = grp[0]
+            check(L.rq_linear(ctx.handle, weights[c][k].handle, xs[k].data_ptr(),
+                              ys[k].data_ptr(), 1, st))
+        else:
+            check(L.rq_linear_batch(ctx.handle, len(grp),
+                                    arr([weights[c][k].handle.value for k in grp]),
+                                    arr([xs[k].data_ptr() for k in grp]),
+                                    arr([ys[k].data_ptr() for k in grp]), st))
 
     def launch_layer(c, st):
-        for k, (n, i, o) in enumerate(SHAPES):
-            check(L.rq_linear(ctx.handle, weights[c][k].handle, xs[k].data_ptr(), ys[k].data_ptr(),
-                              1, st))
+        for grp in groups:
+            launch_group(c, grp, st)
 
-    # warm the workspace outside capture, then capture one graph per layer copy
+    def capture(fn):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            fn(torch.cuda.current_stream().cuda_stream)
+        return gr
+
+    # warm the workspace and kernel attributes outside capture
     with torch.cuda.stream(stream):
         for c in range(N_COPIES):
             launch_layer(c, stream.cuda_stream)
+            for k in range(len(SHAPES)):
+                launch_group(c, (k,), stream.cuda_stream)
     stream.synchronize()
-    graphs = []
-    for c in range(N_COPIES):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            launch_layer(c, torch.cuda.current_stream().cuda_stream)
-        graphs.append(gr)
-    # dominant kernel: gate_proj matvec, rotating copies
-    kg = 4
-    gate = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gate, stream=stream):
-        st = torch.cuda.current_stream().cuda_stream
-        for c in range(N_COPIES):
-            check(L.rq_linear(ctx.handle, weights[c][kg].handle, xs[kg].data_ptr(),
-                              ys[kg].data_ptr(), 1, st))
+    graphs = [capture(lambda st, c=c: launch_layer(c, st)) for c in range(N_COPIES)]
+    # per-shape single calls and the dominant launch (gate+up batched), each
+    # over the rotating copies
+    shape_graphs = [capture(lambda st, k=k: [launch_group(c, (k,), st) for c in range(N_COPIES)])
+                    for k in range(len(SHAPES))]
+    dom = capture(lambda st: [launch_group(c, (4, 5), st) for c in range(N_COPIES)])
+
+    def timed(fn, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for r in range(reps):
+                fn(r)
+            e1.record(stream)
+        stream.synchronize()
+        return e0.elapsed_time(e1)
 
     with torch.cuda.stream(stream):
         for s in range(max(args.warmup, 3)):
             graphs[s % N_COPIES].replay()
-        for _ in range(3):
-            gate.replay()
+        for gr in shape_graphs + [dom]:
+            gr.replay()
     stream.synchronize()
 
     def barrier():
@@ -267,25 +297,14 @@ def run_gpu(args) -> None:
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for s in range(args.steps):
-            graphs[s % N_COPIES].replay()
-        e1.record(stream)
-    stream.synchronize()
-    ms_total = e0.elapsed_time(e1)
-    # dominant kernel timing (same stream)
+    ms_total = timed(lambda s: graphs[s % N_COPIES].replay(), args.steps)
     reps = max(10, args.steps // 4)
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        k0.record(stream)
-        for _ in range(reps):
-            gate.replay()
-        k1.record(stream)
-    stream.synchronize()
+    dom_ms = timed(lambda r: dom.replay(), reps) / (reps * N_COPIES)
+    per_shape = {}
+    for k, (n, i, o) in enumerate(SHAPES):
+        t = timed(lambda r, k=k: shape_graphs[k].replay(), reps) / (reps * N_COPIES)
+        per_shape[n] = round((Q4K_BYTES(i, o) + 4 * (i + o)) / (t / 1e3) / 1e9, 1)
     clk = clocks.stop()
-    gate_ms = k0.elapsed_time(k1) / (reps * N_COPIES)
     barrier()
     torch.cuda.synchronize()
 
@@ -295,8 +314,8 @@ def run_gpu(args) -> None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms_step = float(t.item())
 
-    # e2e: same step through the public call with HOST buffers (pinned),
-    # host->device of x and device->host of y inside the timed region
+    # e2e: the seven linears through the public call with HOST buffers
+    # (pinned), host->device of x and device->host of y inside the timed region
     xh = [torch.randn(1, i, generator=torch.Generator().manual_seed(7)).pin_memory()
           for _, i, _ in SHAPES]
     yh = [torch.empty(1, o).pin_memory() for _, _, o in SHAPES]
@@ -325,15 +344,15 @@ def run_gpu(args) -> None:
     value = sb * world / (ms_step / 1e3) / 1e9
     e2e_val = sb * world / (e2e_ms / 1e3) / 1e9
     pk = peaks()
-    gate_bytes = Q4K_BYTES(8192, 28672) + 4 * (8192 + 28672)
-    achieved = gate_bytes / (gate_ms / 1e3) / 1e9
+    dom_bytes = 2 * Q4K_BYTES(8192, 28672) + 4 * (8192 + 2 * 28672)
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host = {n: weights[0][k].download() for k, (n, _, _) in enumerate(SHAPES)}
         cpu = cpu_baseline(host, seconds=args.cpu_seconds)
     if rank == 0:
         traffic = None
-        tp = os.path.join(ROOT, "profiles", "traffic_q4k_gate.json")
+        tp = os.path.join(ROOT, "profiles", "traffic_q4k_gate_up.json")
         if os.path.exists(tp):
             with open(tp) as f:
                 traffic = json.load(f).get("bytes_per_launch")
@@ -345,25 +364,28 @@ def run_gpu(args) -> None:
             "data": "synthetic: W ~ N(0,0.02) f32 quantized to Q4_K on device (seeded), x ~ N(0,1)",
             "config": {"workload": WORKLOAD, "batch_m": 1, "weight_format": "GGML Q4_K",
                        "bytes_per_step": sb,
+                       "launch_grouping": "q/k/v batched on their shared x, o, gate/up batched "
+                                          "on their shared x, down (4 rq_linear[_batch] calls)",
                        "l2": f"inputs larger than L2: {N_COPIES} rotating layer copies, "
                              f"{N_COPIES * sb / 1e9:.2f} GB per rotation vs 126 MB L2",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "pct_of_hbm_peak": round(100 * value / world / pk["hbm_gbs"], 1)},
+                       "pct_of_hbm_peak": round(100 * value / world / pk["hbm_gbs"], 1),
+                       "per_shape_single_call_gbs": per_shape},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                          "traffic": traffic,
-                         "kernel": "rq_linear gate_proj 8192->28672 (xquant + mv_q4k), "
+                         "kernel": "rq_linear_batch gate+up 2x(8192->28672): xquant + mv_pipe, "
                                    f"peak {pk['source']}"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": sum(4 * i for _, i, _ in SHAPES),
                     "d2h_bytes_per_step": sum(4 * o for _, _, o in SHAPES)},
-            "gpu_launches": args.steps * len(SHAPES) * 2,
+            "gpu_launches": args.steps * 2 * len(groups),
             "clocks": clk,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    del graphs, gate
+    del graphs, shape_graphs, dom
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()

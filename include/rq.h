@@ -83,7 +83,8 @@ RQ_API int rq_weight_upload(rq_ctx* ctx, int ggml_type, const void* blocks, size
                      int64_t out, int64_t in, rq_weight** w);
 
 /* Quantize an f32 matrix [out][in] that is already on this device straight
- * into a device weight (no host round trip).  Q4_0 follows the rule of
+ * into a device weight (no host round trip); the call returns once the
+ * weight is written.  Q4_0 follows the rule of
  * src/q4_kernel.rs:137-163; Q4_K/Q3_K use librq's deterministic quantizer
  * (the counterpart of candle's QTensor::quantize, src/quantize.rs:131). */
 RQ_API int rq_weight_quantize(rq_ctx* ctx, int ggml_type, const float* w_dev, int64_t out, int64_t in,
@@ -113,6 +114,16 @@ RQ_API int rq_dequantize(rq_ctx* ctx, const rq_weight* w, float* y, void* stream
  * larger M the prefill (src/streaming_quantized.rs:569-575). */
 RQ_API int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t M,
               void* stream);
+
+/* n (1..8) independent decode matvecs y_i[1][out_i] = x_i[1][in] * W_i^T in
+ * one launch, for weights of the same type and in_features -- the q/k/v
+ * projections of QAttn::forward (src/streaming_quantized.rs:201-203) or the
+ * gate/up projections of QMlp::forward (:277), which read the same x.  The
+ * weights are streamed back to back without a pipeline drain between them;
+ * x_i may alias one another.  x and y must be device memory on the context's
+ * device.  Results equal n rq_linear calls with M = 1. */
+RQ_API int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const float* const* x,
+                           float* const* y, void* stream);
 
 /* rq_linear for callers that cannot allocate device memory.  No counterpart
  * in the reference.

@@ -258,6 +258,9 @@ int rq_weight_quantize(rq_ctx* ctx, int type, const float* w_dev, int64_t out, i
     rc = alloc_weight(ctx, type, out, in, &w);
     if (rc) return rc;
     rc = launch_quantize(w, w_dev, (cudaStream_t)stream);
+    // the weight is complete when the call returns (linear kernels start
+    // streaming weights before they wait for the preceding kernel)
+    if (!rc) rc = cuda_error(cudaStreamSynchronize((cudaStream_t)stream), "rq_weight_quantize sync");
     if (rc) {
         cudaFree(w->base);
         delete w;
@@ -364,6 +367,51 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
         if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "rq_linear sync");
     }
     return rc;
+}
+
+int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const float* const* x,
+                    float* const* y, void* stream) {
+    if (!ctx || !w || !x || !y) return set_error(RQ_ERR_INVALID, "rq_linear_batch: NULL argument");
+    if (n < 1 || n > kMaxJobs)
+        return set_error(RQ_ERR_INVALID, "rq_linear_batch: n = %d (1..%d)", n, kMaxJobs);
+    for (int j = 0; j < n; j++) {
+        if (!w[j] || !x[j] || !y[j]) return set_error(RQ_ERR_INVALID, "rq_linear_batch: NULL entry %d", j);
+        if (w[j]->type != w[0]->type || w[j]->in != w[0]->in || w[j]->device != w[0]->device)
+            return set_error(RQ_ERR_INVALID,
+                             "rq_linear_batch: weight %d differs from weight 0 in type, in_features or device", j);
+        if (mem_kind(x[j]) != Mem::Device || mem_kind(y[j]) != Mem::Device)
+            return set_error(RQ_ERR_INVALID, "rq_linear_batch: x and y must be device memory");
+    }
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!pipe_supported(w[0])) {  // shapes the pipeline does not take: one call each
+        for (int j = 0; j < n; j++) {
+            int rc = rq_linear(ctx, w[j], x[j], y[j], 1, stream);
+            if (rc) return rc;
+        }
+        return RQ_OK;
+    }
+    // stage each distinct activation row once
+    const float* rows[kMaxJobs];
+    int row_of[kMaxJobs], nrows = 0;
+    for (int j = 0; j < n; j++) {
+        int r = 0;
+        while (r < nrows && rows[r] != x[j]) r++;
+        if (r == nrows) rows[nrows++] = x[j];
+        row_of[j] = r;
+    }
+    const int64_t in = w[0]->in;
+    int rc = ensure_workspace(ctx, xq_bytes(nrows, in));
+    if (rc) return rc;
+    XQ xq;
+    xq.planes = (int8_t*)ctx->ws;
+    xq.stats = (float4*)((uint8_t*)ctx->ws + (((size_t)nrows * 3 * in + 255) & ~(size_t)255));
+    rc = launch_xquant_rows(rows, nrows, in, xq, st);
+    if (rc) return rc;
+    XQ xqs[kMaxJobs];
+    for (int j = 0; j < n; j++)
+        xqs[j] = XQ{xq.planes + (int64_t)row_of[j] * 3 * in, xq.stats + (int64_t)row_of[j] * (in / 32)};
+    return launch_matvec_pipe(w, xqs, y, n, ctx->sm_count, st);
 }
 
 }  // extern "C"

@@ -97,14 +97,26 @@ int launch_unpack(const rq_weight* w, uint8_t* raw_dev, int64_t row0, int64_t ro
 int launch_dequant(const rq_weight* w, float* y, cudaStream_t st);
 int launch_quantize(const rq_weight* w, const float* x, cudaStream_t st);
 
-// bulk-copy pipelined matvec (rq_mv_pipe.cu); err may be NULL
+// bulk-copy pipelined matvec (rq_mv_pipe.cu): up to kMaxJobs independent
+// M=1 matvecs with the same type and K in one launch; err may be NULL
+constexpr int kMaxJobs = 8;
+struct PipeJob {
+    const uint8_t* qs;
+    const uint8_t* hdr;
+    XQ xq;  // the staged activation row of this job
+    float* y;
+    int64_t out;
+};
 bool pipe_supported(const rq_weight* w);
-int launch_matvec_pipe(const rq_weight* w, XQ xq, float* y, int sm_count, cudaStream_t st,
-                       int* err = nullptr);
+int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
+                       int sm_count, cudaStream_t st, int* err = nullptr);
 
-// linear kernels (rq_matvec.cu)
+// linear kernels (rq_matvec.cu).  launch_linear runs y = x W^T for M staged
+// activation rows (launch_xquant first).  launch_xquant_rows stages up to
+// kMaxJobs separate rows (row j of `in` floats at xs[j]) into consecutive
+// rows of xq in one launch.
 int launch_xquant(const float* x, int64_t M, int64_t in, XQ xq, cudaStream_t st);
-int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count,
-                  cudaStream_t st);
+int launch_xquant_rows(const float* const* xs, int n, int64_t in, XQ xq, cudaStream_t st);
+int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, cudaStream_t st);
 
 }  // namespace rq

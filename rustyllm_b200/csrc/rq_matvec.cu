@@ -12,6 +12,8 @@
 //     transpose reduction, then across warps in shared memory in a fixed
 //     order, so results are deterministic.
 
+#include <algorithm>
+
 #include "rq_mv_common.cuh"
 
 namespace rq {
@@ -31,15 +33,20 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 // programmatic dependent: it first waits for the preceding kernel (which may
 // produce x), then lets the following matvec launch so that its weight
 // streaming overlaps this kernel.
-__global__ void xquant_kernel(const float* __restrict__ x, int64_t M, int64_t in,
-                              int8_t* __restrict__ planes, float4* __restrict__ stats) {
+struct XRows {  // activation rows to stage: row m starts at x[m] (or x[0] + m*in)
+    const float* x[kMaxJobs];
+    int listed;    // 0: rows are consecutive from x[0]
+};
+
+__global__ void xquant_kernel(XRows rows, int64_t M, int64_t in, int8_t* __restrict__ planes,
+                              float4* __restrict__ stats) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     int64_t nb = in / 32;
     int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= M * nb) return;
     int64_t m = t / nb, b = t % nb;
-    const float* src = x + m * in + b * 32;
+    const float* src = (rows.listed ? rows.x[m] : rows.x[0] + m * in) + b * 32;
     float v[32];
     if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
 #pragma unroll
@@ -240,7 +247,8 @@ int launch_matvec_regs(const rq_weight* w, XQ xq, float* y, int sm_count, cudaSt
 
 }  // namespace
 
-int launch_xquant(const float* x, int64_t M, int64_t in, XQ xq, cudaStream_t st) {
+namespace {
+int launch_xquant_impl(const XRows& rows, int64_t M, int64_t in, XQ xq, cudaStream_t st) {
     int64_t n = M * (in / 32);
     if (n == 0) return RQ_OK;
     cudaLaunchConfig_t cfg = {};
@@ -252,17 +260,47 @@ int launch_xquant(const float* x, int64_t M, int64_t in, XQ xq, cudaStream_t st)
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_error(cudaLaunchKernelEx(&cfg, xquant_kernel, x, M, in, xq.planes, xq.stats),
+    return cuda_error(cudaLaunchKernelEx(&cfg, xquant_kernel, rows, M, in, xq.planes, xq.stats),
                       "xquant kernel");
 }
+}  // namespace
 
-int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count,
-                  cudaStream_t st) {
+int launch_xquant(const float* x, int64_t M, int64_t in, XQ xq, cudaStream_t st) {
+    XRows rows{};
+    rows.x[0] = x;
+    rows.listed = 0;
+    return launch_xquant_impl(rows, M, in, xq, st);
+}
+
+int launch_xquant_rows(const float* const* xs, int n, int64_t in, XQ xq, cudaStream_t st) {
+    if (n < 1 || n > kMaxJobs) return set_error(RQ_ERR_INVALID, "xquant: %d rows", n);
+    XRows rows{};
+    for (int j = 0; j < n; j++) rows.x[j] = xs[j];
+    rows.listed = 1;
+    return launch_xquant_impl(rows, n, in, xq, st);
+}
+
+int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, cudaStream_t st) {
+    if (pipe_supported(w)) {
+        // every activation row is one job of the pipelined kernel
+        for (int64_t m0 = 0; m0 < M; m0 += kMaxJobs) {
+            const int n = (int)std::min<int64_t>(kMaxJobs, M - m0);
+            const rq_weight* ws[kMaxJobs];
+            XQ xqs[kMaxJobs];
+            float* ys[kMaxJobs];
+            for (int j = 0; j < n; j++) {
+                ws[j] = w;
+                xqs[j] = XQ{xq.planes + (m0 + j) * 3 * w->in, xq.stats + (m0 + j) * (w->in / 32)};
+                ys[j] = y + (m0 + j) * w->out;
+            }
+            int rc = launch_matvec_pipe(ws, xqs, ys, n, sm_count, st);
+            if (rc) return rc;
+        }
+        return RQ_OK;
+    }
     for (int64_t m = 0; m < M; m++) {
         XQ row{xq.planes + m * 3 * w->in, xq.stats + m * (w->in / 32)};
-        float* yr = y + m * w->out;
-        int rc = pipe_supported(w) ? launch_matvec_pipe(w, row, yr, sm_count, st)
-                                   : launch_matvec_regs(w, row, yr, sm_count, st);
+        int rc = launch_matvec_regs(w, row, y + m * w->out, sm_count, st);
         if (rc) return rc;
     }
     return RQ_OK;

@@ -1,23 +1,28 @@
 // rq_mv_pipe.cu -- M=1 matvec with weights staged through shared memory by
 // bulk asynchronous copies (cp.async.bulk, the non-tensor TMA path).
 //
-// One persistent CTA per SM owns a contiguous range of output rows, so its
-// weight bytes are two contiguous byte ranges (quant part and header part of
-// the device layout).  Warp 0, lane 0 is the producer: it streams stages of
-// RS whole rows into a ring of NSTAGE shared-memory buffers (~200 KB in
-// flight per SM, independent of registers), signalling an mbarrier per stage
-// with the byte count.  Consumer warp (s, g) keeps the activation planes of
-// K-slice s in registers and processes rows g, g+G, ... of every stage, then
-// releases the buffer through the stage's "empty" mbarrier.  Per-row lane
-// partials are transpose-reduced within the warp and written to a per-CTA
-// table [row][slice]; after the last stage the table is summed in slice
-// order (deterministic) and y is written.
+// One launch runs up to kMaxJobs independent matvecs with the same weight
+// type and K (the q/k/v or gate/up linears of one layer, or the rows of a
+// small batch).  One persistent CTA per SM owns a contiguous range of output
+// rows of every job, so its weight bytes are contiguous byte ranges of the
+// device layout.  Warp 0, lane 0 is the producer: it streams stages of RS
+// whole rows, job after job without a pause, into a ring of NSTAGE
+// shared-memory buffers (~200 KB in flight per SM, independent of
+// registers), each stage signalling an mbarrier with its byte count.
+// Consumer warp (s, g) owns K-slice s (2048 elements) and rows g, g+G, ... of
+// every stage.  Each lane keeps the staged activation planes (24-bit fixed
+// point in three int8 planes, written by the staging kernel) of its 64
+// elements in registers, multiplies them with the 4-bit quants by dp4a, and
+// releases the buffer through the stage's "empty" mbarrier.  Per-row lane partials are transpose-reduced within the
+// warp into a per-CTA table [row][slice]; after the last stage the table is
+// summed in slice order (deterministic) and y is written.
 //
-// Launched as a programmatic dependent of the activation-staging kernel: the
-// producer starts streaming weights at once (weights do not depend on the
-// preceding kernel), consumers wait (griddepcontrol.wait) before reading the
-// planes.  Every mbarrier wait is bounded (~1 s); on expiry the kernel sets
-// the error word, drains its in-flight copies and exits.
+// Programmatic dependent launch: every CTA allows the next kernel in the
+// stream to launch at once; the producer streams weights immediately
+// (weights are written only by synchronous librq calls), while consumers
+// wait (griddepcontrol.wait) for the staging kernel before reading planes.
+// Every mbarrier wait is bounded (~1 s); on expiry the kernel sets the error
+// word, drains its in-flight copies and exits.
 
 #include <algorithm>
 
@@ -36,13 +41,10 @@ constexpr int kBarBytes = 2 * 32 * 8;  // up to 32 stages: full + empty barriers
 constexpr long long kWaitCycles = 1ll << 31;
 
 struct PipeParams {
-    const uint8_t* qs;
-    const uint8_t* hdr;
-    const int8_t* planes;
-    const float4* stats;
-    float* y;
+    PipeJob jobs[kMaxJobs];
+    int njobs;
     int* err;
-    int64_t out, nblk, in;
+    int64_t nblk, in;
     int S, G, RS, nstage;
     uint32_t qrow, hrow;  // device bytes per weight row (quant part, header part)
     uint32_t stage_bytes, red_off, ring_off;
@@ -88,6 +90,13 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         : "memory");
 }
 
+__device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) {
+    const int64_t b = (int64_t)blockIdx.x * j.out / gridDim.x;
+    const int64_t e = (int64_t)(blockIdx.x + 1) * j.out / gridDim.x;
+    *rb = b;
+    *n = (int)(e - b);
+}
+
 template <int TYPE>
 struct LaneOf;
 template <>
@@ -97,55 +106,78 @@ struct LaneOf<RQ_Q3_K> { using T = Q3KLane; };
 template <>
 struct LaneOf<RQ_Q4_0> { using T = Q40Lane; };
 
-// Set up lane data for K-slice s; returns whether the lane has valid data.
+// Per-lane constants of K-slice s: activation planes and the lane's
+// shared-memory byte offsets inside a row.  Lanes past the end of a partial
+// slice get zero activations and read the slice's first block, so the row
+// loop needs no per-lane branch.
+struct LaneOffsets {
+    uint32_t qa, qb, h;
+};
+
 template <int TYPE>
-__device__ __forceinline__ bool lane_setup(typename LaneOf<TYPE>::T& L, const PipeParams& p, int s,
-                                           int lane) {
+__device__ __forceinline__ void lane_setup(typename LaneOf<TYPE>::T& L, LaneOffsets& o,
+                                           const PipeParams& p, const XQ& xq, int s, int lane) {
     if constexpr (TYPE == RQ_Q4_0) {
         const int64_t b0 = (int64_t)s * 64 + 2 * lane;
-        if (b0 >= p.nblk) return false;
-        q40_lane_setup(L, p.planes, p.stats, p.in, p.nblk, b0);
-        return true;
-    } else if constexpr (TYPE == RQ_Q4_K) {
-        // lanes past the end of a partial slice get zero activations and read
-        // the slice's first group, so the row loop needs no per-lane branch
-        const int64_t sb = (int64_t)s * 8 + (lane >> 2);
-        const bool valid = sb < p.nblk;
-        q4kp_lane_setup(L, p.planes, p.stats, p.in, valid ? sb : 0, lane & 3, (lane >> 2) & 1, valid);
-        return true;
+        const bool valid = b0 < p.nblk;
+        if (valid) {
+            q40_lane_setup(L, xq.planes, xq.stats, p.in, p.nblk, b0);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 3; q++)
+#pragma unroll
+                for (int w = 0; w < 16; w++) L.p[q][w] = 0u;
+            L.sx0 = L.sx1 = L.xs0 = L.xs1 = 0.0f;
+            L.has1 = false;
+        }
+        const uint32_t l = valid ? (uint32_t)lane : 0u;
+        o.qa = (uint32_t)(s * 1024) + 32u * l + 16u * ((l >> 2) & 1u);
+        o.qb = o.qa ^ 16u;
+        o.h = (uint32_t)(s * 128) + 4u * l;
     } else {
         const int64_t sb = (int64_t)s * 8 + (lane >> 2);
-        if (sb >= p.nblk) return false;
-        q3k_lane_setup(L, p.planes, p.stats, p.in, sb, lane & 3);
-        return true;
+        const bool valid = sb < p.nblk;
+        const uint32_t sbl = valid ? (uint32_t)(lane >> 2) : 0u;
+        if constexpr (TYPE == RQ_Q4_K) {
+            q4kp_lane_setup(L, xq.planes, xq.stats, p.in, valid ? sb : 0, lane & 3, (lane >> 2) & 1, valid);
+            o.qa = (uint32_t)(s * 1024) + 128u * sbl + 32u * (uint32_t)(lane & 3) + 16u * ((lane >> 2) & 1u);
+            o.qb = o.qa ^ 16u;
+        } else {
+            q3k_lane_setup(L, xq.planes, xq.stats, p.in, valid ? sb : 0, lane & 3);
+            if (!valid) {
+#pragma unroll
+                for (int q = 0; q < 3; q++)
+#pragma unroll
+                    for (int r = 0; r < 4; r++)
+#pragma unroll
+                        for (int c = 0; c < 4; c++) L.p[q][r][c] = 0u;
+#pragma unroll
+                for (int r = 0; r < 4; r++) L.sx[r] = L.xs16[r] = 0.0f;
+            }
+            o.qa = (uint32_t)(s * 768) + 96u * sbl + 16u * (uint32_t)L.u;  // hmask
+            o.qb = (uint32_t)(s * 768) + 96u * sbl + 32u + 32u * (uint32_t)L.h + 16u * (uint32_t)L.u;
+        }
+        o.h = (uint32_t)(s * 128) + 16u * sbl;
     }
 }
 
-// Lane contribution of one row held in shared memory (sq: the row's quant
-// bytes, sh: its header bytes).
+// Lane contribution of one row held in shared memory (q: the row's quant
+// bytes, h: its header bytes).
 template <int TYPE>
-__device__ __forceinline__ float lane_row(const typename LaneOf<TYPE>::T& L, const uint8_t* sq,
-                                          const uint8_t* sh, int s, int lane) {
-    // the two 16-byte halves of a lane's 32 bytes are read in an order that
-    // keeps each quarter-warp's 128-bit loads on distinct banks
-    const int h1 = (lane >> 2) & 1;
+__device__ __forceinline__ float lane_row(const typename LaneOf<TYPE>::T& L, const LaneOffsets& o,
+                                          const uint8_t* q, const uint8_t* h) {
+    const uint4 a = *reinterpret_cast<const uint4*>(q + o.qa);
+    const uint4 b = *reinterpret_cast<const uint4*>(q + o.qb);
     if constexpr (TYPE == RQ_Q4_K) {
-        return 0.0f;  // Q4_K rows go through the hoisted path in the kernel
+        return q4kp_lane_row(L, a, b, *reinterpret_cast<const uint4*>(h + o.h), 0.0f);
     } else if constexpr (TYPE == RQ_Q3_K) {
-        const uint8_t* b = sq + s * 768 + 96 * (lane >> 2);
-        const uint4 hm = *reinterpret_cast<const uint4*>(b + 16 * L.u);
-        const uint4 qv = *reinterpret_cast<const uint4*>(b + 32 + 32 * L.h + 16 * L.u);
-        const uint4 hd = *reinterpret_cast<const uint4*>(sh + s * 128 + 16 * (lane >> 2));
-        return q3k_lane_row(L, hm, qv, hd);
+        return q3k_lane_row(L, a, b, *reinterpret_cast<const uint4*>(h + o.h));
     } else {
-        // the pipeline takes Q4_0 only when blocks per row is a multiple of 8,
-        // so both blocks of a lane exist
-        const uint8_t* q = sq + s * 1024 + 32 * lane;
-        const uint4 first = *reinterpret_cast<const uint4*>(q + 16 * h1);
-        const uint4 second = *reinterpret_cast<const uint4*>(q + 16 * (1 - h1));
-        const uint32_t dd = *reinterpret_cast<const uint32_t*>(sh + s * 128 + 4 * lane);
-        return q40_lane_row(L, h1 ? second : first, h1 ? first : second, (uint16_t)(dd & 0xFFFFu),
-                            (uint16_t)(dd >> 16));
+        // a is the half selected by lane bit 2; swap back to blocks (b0, b0+1)
+        const bool swap = (o.qa & 16u) != 0u;
+        const uint32_t dd = *reinterpret_cast<const uint32_t*>(h + o.h);
+        return q40_lane_row(L, swap ? b : a, swap ? a : b, (uint16_t)(dd & 0xFFFFu),
+                            L.has1 ? (uint16_t)(dd >> 16) : (uint16_t)0);
     }
 }
 
@@ -155,11 +187,10 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
     float* red = reinterpret_cast<float*>(smem + p.red_off);
     uint8_t* ring = smem + p.ring_off;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t r_begin = (int64_t)blockIdx.x * p.out / gridDim.x;
-    const int64_t r_end = (int64_t)(blockIdx.x + 1) * p.out / gridDim.x;
-    const int nrows = (int)(r_end - r_begin);
-    const int nst = (nrows + p.RS - 1) / p.RS;
     const uint32_t full0 = smem_u32(smem), empty0 = full0 + 8 * p.nstage;
+    // the next kernel in the stream may launch now; it waits for this grid
+    // before touching anything this grid writes
+    asm volatile("griddepcontrol.launch_dependents;");
     if (threadIdx.x == 0) {
         for (int i = 0; i < p.nstage; i++) {
             mbar_init(full0 + 8 * i, 1);
@@ -173,101 +204,88 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         if (lane == 0) {
             uint64_t pol;
             asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-            int issued = 0;
+            int it = 0;
             bool ok = true;
-            for (int it = 0; it < nst; it++) {
-                const int slot = it % p.nstage, use = it / p.nstage;
-                if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
-                const int rows = min(p.RS, nrows - it * p.RS);
-                const int64_t r0 = r_begin + (int64_t)it * p.RS;
-                const uint32_t qb = (uint32_t)rows * p.qrow, hb = (uint32_t)rows * p.hrow;
-                const uint32_t dst = smem_u32(ring) + (uint32_t)slot * p.stage_bytes;
-                mbar_expect_tx(full0 + 8 * slot, qb + hb);
-                bulk_g2s(dst, p.qs + r0 * p.qrow, qb, full0 + 8 * slot, pol);
-                bulk_g2s(dst + (uint32_t)p.RS * p.qrow, p.hdr + r0 * p.hrow, hb, full0 + 8 * slot, pol);
-                issued = it + 1;
+            for (int j = 0; j < p.njobs && ok; j++) {
+                const PipeJob& jb = p.jobs[j];
+                int64_t rb;
+                int nrows;
+                job_rows(jb, &rb, &nrows);
+                for (int r0 = 0; r0 < nrows; r0 += p.RS, it++) {
+                    const int slot = it % p.nstage, use = it / p.nstage;
+                    if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
+                    const int rows = min(p.RS, nrows - r0);
+                    const int64_t row = rb + r0;
+                    const uint32_t qb = (uint32_t)rows * p.qrow, hb = (uint32_t)rows * p.hrow;
+                    const uint32_t dst = smem_u32(ring) + (uint32_t)slot * p.stage_bytes;
+                    mbar_expect_tx(full0 + 8 * slot, qb + hb);
+                    bulk_g2s(dst, jb.qs + row * p.qrow, qb, full0 + 8 * slot, pol);
+                    bulk_g2s(dst + (uint32_t)p.RS * p.qrow, jb.hdr + row * p.hrow, hb, full0 + 8 * slot, pol);
+                }
             }
-            // let the next kernel in the stream start its own prologue
-            asm volatile("griddepcontrol.launch_dependents;");
             // no bulk copy may still be landing when the CTA exits
-            for (int it = max(0, issued - p.nstage); it < issued; it++)
-                if (!mbar_wait(full0 + 8 * (it % p.nstage), (it / p.nstage) & 1)) ok = false;
+            for (int k = max(0, it - p.nstage); k < it; k++)
+                if (!mbar_wait(full0 + 8 * (k % p.nstage), (k / p.nstage) & 1)) ok = false;
             if (!ok && p.err) atomicExch(p.err, 1);
         }
     } else if (warp - 1 < p.S * p.G) {
         const int c = warp - 1;
         const int s = c % p.S, g = c / p.S;
         typename LaneOf<TYPE>::T L;
+        LaneOffsets o;
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        const bool valid = lane_setup<TYPE>(L, p, s, lane);
-        if constexpr (TYPE == RQ_Q4_K) {
-            // lane-constant shared-memory offsets within a row
-            const int64_t sbl = (int64_t)s * 8 + (lane >> 2) < p.nblk ? (lane >> 2) : 0;
-            const uint32_t offA = (uint32_t)(s * 1024 + 128 * sbl + 32 * (lane & 3) + 16 * ((lane >> 2) & 1));
-            const uint32_t offB = offA ^ 16u;
-            const uint32_t offH = (uint32_t)(s * 128 + 16 * sbl);
-            for (int it = 0; it < nst; it++) {
+        const int8_t* cur_x = nullptr;
+        int it = 0, roff = 0;
+        bool ok = true;
+        for (int j = 0; j < p.njobs && ok; j++) {
+            const PipeJob& jb = p.jobs[j];
+            int64_t rb;
+            int nrows;
+            job_rows(jb, &rb, &nrows);
+            if (jb.xq.planes != cur_x) {  // jobs that share x keep the planes
+                lane_setup<TYPE>(L, o, p, jb.xq, s, lane);
+                cur_x = jb.xq.planes;
+            }
+            for (int r0 = 0; r0 < nrows; r0 += p.RS, it++) {
                 const int slot = it % p.nstage, use = it / p.nstage;
                 if (!mbar_wait(full0 + 8 * slot, use & 1)) {
                     if (lane == 0 && p.err) atomicExch(p.err, 1);
+                    ok = false;
                     break;
                 }
                 const uint8_t* sq = ring + (size_t)slot * p.stage_bytes;
                 const uint8_t* sh = sq + (size_t)p.RS * p.qrow;
-                const int rows = min(p.RS, nrows - it * p.RS);
+                const int rows = min(p.RS, nrows - r0);
                 float part[RPW];
 #pragma unroll
-                for (int j = 0; j < RPW; j++) {
-                    const int r = g + j * p.G;  // warp-uniform
-                    part[j] = 0.0f;
-                    if (r < rows) {
-                        const uint8_t* q = sq + (size_t)r * p.qrow;
-                        const uint4 qa = *reinterpret_cast<const uint4*>(q + offA);
-                        const uint4 qb = *reinterpret_cast<const uint4*>(q + offB);
-                        const uint4 h = *reinterpret_cast<const uint4*>(sh + (size_t)r * p.hrow + offH);
-                        part[j] = q4kp_lane_row(L, qa, qb, h, 0.0f);
-                    }
+                for (int i = 0; i < RPW; i++) {
+                    const int r = g + i * p.G;  // warp-uniform
+                    part[i] = r < rows ? lane_row<TYPE>(L, o, sq + (size_t)r * p.qrow, sh + (size_t)r * p.hrow)
+                                       : 0.0f;
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty0 + 8 * slot);
                 transpose_reduce<RPW>(part, lane);
                 if (lane_writes<RPW>(lane)) {
                     const int r = g + row_of_lane<RPW>(lane) * p.G;
-                    if (r < rows) red[(it * p.RS + r) * p.S + s] = part[0];
+                    if (r < rows) red[(roff + r0 + r) * p.S + s] = part[0];
                 }
             }
-        } else
-        for (int it = 0; it < nst; it++) {
-            const int slot = it % p.nstage, use = it / p.nstage;
-            if (!mbar_wait(full0 + 8 * slot, use & 1)) {
-                if (lane == 0 && p.err) atomicExch(p.err, 1);
-                break;
-            }
-            const uint8_t* sq = ring + (size_t)slot * p.stage_bytes;
-            const uint8_t* sh = sq + (size_t)p.RS * p.qrow;
-            const int rows = min(p.RS, nrows - it * p.RS);
-            float part[RPW];
-#pragma unroll
-            for (int j = 0; j < RPW; j++) {
-                const int r = g + j * p.G;
-                part[j] = (valid && r < rows)
-                              ? lane_row<TYPE>(L, sq + (size_t)r * p.qrow, sh + (size_t)r * p.hrow, s, lane)
-                              : 0.0f;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(empty0 + 8 * slot);
-            transpose_reduce<RPW>(part, lane);
-            if (lane_writes<RPW>(lane)) {
-                const int r = g + row_of_lane<RPW>(lane) * p.G;
-                if (r < rows) red[(it * p.RS + r) * p.S + s] = part[0];
-            }
+            roff += nrows;
         }
     }
     __syncthreads();
-    for (int t = threadIdx.x; t < nrows; t += blockDim.x) {
-        float acc = 0.0f;
-        for (int s = 0; s < p.S; s++) acc += red[t * p.S + s];
-        p.y[r_begin + t] = acc;
+    int roff = 0;
+    for (int j = 0; j < p.njobs; j++) {
+        int64_t rb;
+        int nrows;
+        job_rows(p.jobs[j], &rb, &nrows);
+        for (int t = threadIdx.x; t < nrows; t += blockDim.x) {
+            float acc = 0.0f;
+            for (int s = 0; s < p.S; s++) acc += red[(roff + t) * p.S + s];
+            p.jobs[j].y[rb + t] = acc;
+        }
+        roff += nrows;
     }
 }
 
@@ -314,23 +332,27 @@ bool pipe_supported(const rq_weight* w) {
     return true;
 }
 
-int launch_matvec_pipe(const rq_weight* w, XQ xq, float* y, int sm_count, cudaStream_t st,
-                       int* err) {
-    TypeInfo ti = type_info(w->type);
+int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
+                       int sm_count, cudaStream_t st, int* err) {
+    if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "matvec pipeline: %d jobs", njobs);
+    const rq_weight* w0 = ws[0];
+    TypeInfo ti = type_info(w0->type);
     PipeParams p;
-    p.qs = w->qs;
-    p.hdr = w->hdr;
-    p.planes = xq.planes;
-    p.stats = xq.stats;
-    p.y = y;
+    p.njobs = njobs;
+    for (int j = 0; j < njobs; j++) {
+        p.jobs[j].qs = ws[j]->qs;
+        p.jobs[j].hdr = ws[j]->hdr;
+        p.jobs[j].xq = xqs[j];
+        p.jobs[j].y = ys[j];
+        p.jobs[j].out = ws[j]->out;
+    }
     p.err = err;
-    p.out = w->out;
-    p.nblk = w->nblk;
-    p.in = w->in;
-    p.S = (int)((w->in + 2047) / 2048);
+    p.nblk = w0->nblk;
+    p.in = w0->in;
+    p.S = (int)((w0->in + 2047) / 2048);
     p.G = std::max(1, kMaxConsumerWarps / p.S);
-    p.qrow = (uint32_t)(w->nblk * ti.qs_bytes);
-    p.hrow = (uint32_t)(w->nblk * ti.hdr_bytes);
+    p.qrow = (uint32_t)(w0->nblk * ti.qs_bytes);
+    p.hrow = (uint32_t)(w0->nblk * ti.hdr_bytes);
     const uint32_t rowb = p.qrow + p.hrow;
     // RS = RPW * G whole rows per stage; four rows per consumer warp unless
     // a stage would exceed ~72 KB (at least three stages must fit)
@@ -338,22 +360,25 @@ int launch_matvec_pipe(const rq_weight* w, XQ xq, float* y, int sm_count, cudaSt
     while (rpw > 1 && (uint64_t)rpw * p.G * rowb > 72 * 1024) rpw /= 2;
     p.RS = rpw * p.G;
     p.stage_bytes = (uint32_t)p.RS * rowb;
-    int grid = (int)std::min<int64_t>(w->out, sm_count);
-    // per-CTA partial table [rows][S] floats, at most 32 KB
-    int64_t rows_cap = (w->out + grid - 1) / grid;
-    while (rows_cap * p.S * 4 > 32 * 1024) {
-        grid *= 2;
-        rows_cap = (w->out + grid - 1) / grid;
-    }
+    int64_t max_out = 0;
+    for (int j = 0; j < njobs; j++) max_out = std::max(max_out, ws[j]->out);
+    int grid = (int)std::min<int64_t>(max_out, sm_count);
+    // per-CTA partial table [rows of all jobs][S] floats, at most 32 KB
+    auto rows_cap = [&](int gr) {
+        int64_t r = 0;
+        for (int j = 0; j < njobs; j++) r += (ws[j]->out + gr - 1) / gr;
+        return r;
+    };
+    while (rows_cap(grid) * p.S * 4 > 32 * 1024) grid *= 2;
     p.red_off = kBarBytes;
-    p.ring_off = (uint32_t)((kBarBytes + rows_cap * p.S * 4 + 127) & ~(int64_t)127);
+    p.ring_off = (uint32_t)((kBarBytes + rows_cap(grid) * p.S * 4 + 127) & ~(int64_t)127);
     int nstage = (int)((kSmemBudget - p.ring_off) / p.stage_bytes);
     nstage = std::min(nstage, 32);
     if (nstage < 2) return set_error(RQ_ERR_UNSUPPORTED, "matvec pipeline: row of %u bytes too large", rowb);
     p.nstage = nstage;
     const size_t smem = p.ring_off + (size_t)nstage * p.stage_bytes;
     const int threads = 32 * (1 + p.S * p.G);
-    switch (w->type) {
+    switch (w0->type) {
     case RQ_Q4_K: return launch_pipe_type<RQ_Q4_K>(p, rpw, grid, threads, smem, st);
     case RQ_Q3_K: return launch_pipe_type<RQ_Q3_K>(p, rpw, grid, threads, smem, st);
     default: return launch_pipe_type<RQ_Q4_0>(p, rpw, grid, threads, smem, st);

@@ -187,3 +187,40 @@ def test_parallel_q4_linear_mirror(oracle, rq_ctx):
         ParallelQ4Linear.from_qtensor(QTensor(12, (64, 256), oracle.quantize(12, w)))
     with pytest.raises(RqError, match="last dim"):
         lin.forward(np.zeros((1, 128), np.float32))
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+def test_linear_batch_matches_single_calls(oracle, rq_ctx, qtype):
+    """rq_linear_batch (q/k/v-style: shared x, different out) equals
+    separate rq_linear calls and the oracle."""
+    import ctypes
+    import torch
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200._lib import check, lib
+    L = lib()
+    n_in = 4096
+    outs = [512, 128, 128, 300]
+    ws, blocks = [], []
+    for k, out in enumerate(outs):
+        _, b = make_weight(oracle, qtype, out, n_in, seed=100 + k)
+        blocks.append(b)
+        ws.append(QWeight.upload(rq_ctx, qtype, b, out, n_in))
+    rng = np.random.default_rng(3)
+    x_shared = torch.from_numpy(rng.standard_normal((1, n_in)).astype(np.float32)).cuda()
+    x_own = torch.from_numpy(rng.standard_normal((1, n_in)).astype(np.float32)).cuda()
+    xs = [x_shared, x_shared, x_shared, x_own]
+    ys = [torch.full((1, o), float("nan"), device="cuda") for o in outs]
+    arr = lambda vals: (ctypes.c_void_p * len(vals))(*vals)  # noqa: E731
+    check(L.rq_linear_batch(rq_ctx.handle, len(outs), arr([w.handle.value for w in ws]),
+                            arr([x.data_ptr() for x in xs]), arr([y.data_ptr() for y in ys]),
+                            torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    for k, out in enumerate(outs):
+        ref = oracle.matmul_ref(qtype, blocks[k], out, n_in, xs[k].cpu().numpy())
+        assert rel_l2(ys[k].cpu().numpy(), ref) <= REL_L2_TOL
+    # mismatched in_features is rejected
+    _, b2 = make_weight(oracle, qtype, 64, 2048, seed=9)
+    w2 = QWeight.upload(rq_ctx, qtype, b2, 64, 2048)
+    rc = L.rq_linear_batch(rq_ctx.handle, 2, arr([ws[0].handle.value, w2.handle.value]),
+                           arr([x_shared.data_ptr()] * 2), arr([ys[0].data_ptr()] * 2), None)
+    assert rc == 1
