@@ -149,6 +149,52 @@ RQ_API int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const 
 RQ_API int rq_linear_noalloc(const rq_weight* w, const float* x, float* y, int64_t M,
                              void* stream);
 
+/* -------------------------------------------------------- Llama decode loop */
+
+/* The quantized Llama forward of StreamingLlamaQuantized with every layer
+ * resident on the GPU (src/streaming_quantized.rs:611-729, QBlock
+ * :282-318), a per-layer f32 KV cache (QuantStreamCache :93-152) and the
+ * greedy step of generate (:539-593).  Config mirrors candle's llama Config
+ * fields the block uses. */
+typedef struct rq_llama rq_llama;
+typedef struct rq_llama_config {
+    int64_t hidden, intermediate, n_heads, n_kv_heads, head_dim, n_layers, vocab;
+    int64_t max_seq;          /* KV cache capacity in positions */
+    int64_t max_batch_tokens; /* most tokens per rq_llama_forward (prompt chunk) */
+    float rms_eps, rope_theta;
+} rq_llama_config;
+
+RQ_API int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out);
+RQ_API int rq_llama_free(rq_llama* m);
+/* Layer weights q,k,v,o,gate,up,down (borrowed: they must outlive m) and the
+ * two RmsNorm weights (f32 [hidden], host or device, copied).  Replaces
+ * QBlock::load (src/streaming_quantized.rs:290-303). */
+RQ_API int rq_llama_set_layer(rq_llama* m, int64_t layer, const rq_weight* const* w7,
+                              const float* rms1, const float* rms2);
+/* F16 [vocab][hidden] token embedding (model.embed_tokens.weight). */
+RQ_API int rq_llama_set_embedding(rq_llama* m, const uint16_t* embed_f16);
+/* Final RmsNorm weight (f32 [hidden]) and F16 [vocab][hidden] lm_head. */
+RQ_API int rq_llama_set_head(rq_llama* m, const float* ln_f, const uint16_t* lm_head_f16);
+/* forward(input_ids, index_pos) of src/streaming_quantized.rs:622-633 over T
+ * host tokens at positions index_pos..index_pos+T-1: logits (host or device
+ * [vocab], may be NULL) of the last position and the greedy next token (may
+ * be NULL).  Synchronous.  Leaves the next token and position on the device
+ * for rq_llama_decode_step. */
+RQ_API int rq_llama_forward(rq_llama* m, const int32_t* tokens, int64_t T, int64_t index_pos,
+                            float* logits, int32_t* next_token, void* stream);
+/* One greedy decode step entirely on the device (token and position read
+ * from and written to device memory), so it can be captured in a CUDA graph
+ * and replayed; each step appends its token to the device token list. */
+RQ_API int rq_llama_decode_step(rq_llama* m, void* stream);
+/* Tokens appended since the last reset (count may exceed cap), and the
+ * current position.  Synchronous. */
+RQ_API int rq_llama_tokens(rq_llama* m, int32_t* out, int64_t cap, int64_t* count,
+                           int64_t* position);
+RQ_API int rq_llama_reset_tokens(rq_llama* m);
+/* QuantStreamCache::truncate / truncate_caches
+ * (src/streaming_quantized.rs:131-141,603-609): roll the KV length back. */
+RQ_API int rq_llama_truncate(rq_llama* m, int64_t new_len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -188,3 +188,71 @@ def moe_forward(x: np.ndarray, wr: np.ndarray, qtype: int, w1: list, w3: list, w
     if rc != 0:
         raise ValueError(f"rqo_moe_forward failed ({rc})")
     return y, ids, perm, offs
+
+
+class OracleLlama:
+    """CPU restatement of the quantized Llama forward (rqo_llama_*)."""
+
+    def __init__(self, cfg: dict, qtype: int):
+        L = lib()
+        L.rqo_llama_create.restype = ctypes.c_void_p
+        L.rqo_llama_create.argtypes = [ctypes.c_int64] * 8 + [ctypes.c_float, ctypes.c_float, ctypes.c_int]
+        L.rqo_llama_free.argtypes = [ctypes.c_void_p]
+        L.rqo_llama_set_layer.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_void_p]
+        L.rqo_llama_set_embedding.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.rqo_llama_set_head.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        L.rqo_llama_forward.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                        ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        self.cfg = cfg
+        self.h = L.rqo_llama_create(cfg["hidden"], cfg["intermediate"], cfg["n_heads"],
+                                    cfg["n_kv_heads"], cfg["head_dim"], cfg["n_layers"],
+                                    cfg["vocab"], cfg.get("max_seq", 512), cfg.get("rms_eps", 1e-5),
+                                    cfg.get("rope_theta", 10000.0), qtype)
+        self.keep = []
+
+    def set_layer(self, l, blocks7, rms1, rms2):
+        bl = [np.ascontiguousarray(b, dtype=np.uint8) for b in blocks7]
+        r1 = np.ascontiguousarray(rms1, dtype=np.float32)
+        r2 = np.ascontiguousarray(rms2, dtype=np.float32)
+        arr = (ctypes.c_void_p * 7)(*[_p(b) for b in bl])
+        self.keep += [bl, r1, r2, arr]
+        lib().rqo_llama_set_layer(self.h, l, ctypes.cast(arr, ctypes.c_void_p), _p(r1), _p(r2))
+
+    def set_embedding(self, emb_f16):
+        e = np.ascontiguousarray(emb_f16).view(np.uint16)
+        self.keep.append(e)
+        lib().rqo_llama_set_embedding(self.h, _p(e))
+
+    def set_head(self, ln_f, head_f16):
+        n = np.ascontiguousarray(ln_f, dtype=np.float32)
+        h = np.ascontiguousarray(head_f16).view(np.uint16)
+        self.keep += [n, h]
+        lib().rqo_llama_set_head(self.h, _p(n), _p(h))
+
+    def forward(self, tokens, index_pos, nthreads=0):
+        ids = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        logits = np.empty(self.cfg["vocab"], dtype=np.float32)
+        nxt = ctypes.c_int32()
+        rc = lib().rqo_llama_forward(self.h, _p(ids), ids.size, index_pos, _p(logits),
+                                     ctypes.addressof(nxt), nthreads)
+        if rc != 0:
+            raise ValueError(f"rqo_llama_forward failed ({rc})")
+        return logits, int(nxt.value)
+
+    def generate(self, prompt, max_new_tokens, nthreads=0):
+        toks = []
+        _, nxt = self.forward(prompt, 0, nthreads)
+        toks.append(nxt)
+        pos = len(prompt)
+        for _ in range(max_new_tokens - 1):
+            _, nxt = self.forward([nxt], pos, nthreads)
+            pos += 1
+            toks.append(nxt)
+        return toks
+
+    def __del__(self):
+        try:
+            lib().rqo_llama_free(self.h)
+        except Exception:
+            pass

@@ -169,7 +169,8 @@ static void dequantize_q4_k_block(const uint8_t* blk, float* y) {
  * available).  Per sub-block: range [min(mn,0), mx] -> scale=(mx-lo)/15,
  * min=-lo; scales and mins to 6 bits against the super-block maxima; then
  * q = clamp(rint((x + dmin*m)/(d*sc)), 0, 15) with the stored f16 values.
- * The GPU quantizer (rq_quant.cu) performs the same f32 operations. */
+ * The GPU quantizer (rustyllm_b200/csrc/rq_layout.cu) performs the same f32
+ * operations. */
 static void quantize_q4_k_block(const float* x, uint8_t* blk) {
     float scale[8], mins[8];
     float max_scale = 0.0f, max_min = 0.0f;
@@ -606,5 +607,180 @@ int rqo_moe_forward(const float* x, int64_t T, int64_t H, int64_t F, int E, int 
     if (perm_out) memcpy(perm_out, rows, sizeof(int32_t) * (size_t)(T * k));
     if (offsets_out) memcpy(offsets_out, offs, sizeof(int32_t) * (size_t)(E + 1));
     free(logits); free(ids); free(wts); free(rows); free(sw); free(xin); free(g); free(u); free(o);
+    return 0;
+}
+
+/* ------------------------------------------------------------ Llama loop */
+/* The quantized Llama forward of src/streaming_quantized.rs:193-317,611-633
+ * on the CPU, f32 throughout: RmsNorm (candle_nn::ops::rms_norm order:
+ * m = sqrt(sum(x^2)/n + eps), y = x / m * w), q/k/v/o and MLP linears by the
+ * dequantize-then-dot path, non-interleaved RoPE from f32 tables built like
+ * QuantStreamCache::new, causal GQA attention with softmax, silu(g) * u,
+ * residual adds, final norm, F16 lm_head, first-index argmax. */
+
+struct rqo_llama {
+    int64_t H, I, nh, nkv, hd, nl, vocab, max_seq;
+    float eps, theta;
+    int wtype;
+    const uint8_t** w;   /* [nl][7] */
+    const float** rms1;  /* [nl] */
+    const float** rms2;
+    const uint16_t* emb;
+    const float* lnf;
+    const uint16_t* head;
+    float *kc, *vc;      /* [nl][nkv][max_seq][hd] */
+    float *cs, *sn;      /* [max_seq][hd/2] */
+};
+
+rqo_llama* rqo_llama_create(int64_t H, int64_t I, int64_t nh, int64_t nkv, int64_t hd, int64_t nl,
+                            int64_t vocab, int64_t max_seq, float eps, float theta, int wtype) {
+    rqo_llama* m = (rqo_llama*)calloc(1, sizeof(rqo_llama));
+    if (!m) return NULL;
+    m->H = H; m->I = I; m->nh = nh; m->nkv = nkv; m->hd = hd; m->nl = nl; m->vocab = vocab;
+    m->max_seq = max_seq; m->eps = eps; m->theta = theta; m->wtype = wtype;
+    m->w = (const uint8_t**)calloc((size_t)(nl * 7), sizeof(void*));
+    m->rms1 = (const float**)calloc((size_t)nl, sizeof(void*));
+    m->rms2 = (const float**)calloc((size_t)nl, sizeof(void*));
+    m->kc = (float*)calloc((size_t)(nl * nkv * max_seq * hd), sizeof(float));
+    m->vc = (float*)calloc((size_t)(nl * nkv * max_seq * hd), sizeof(float));
+    int64_t half = hd / 2;
+    m->cs = (float*)malloc(sizeof(float) * (size_t)(max_seq * half));
+    m->sn = (float*)malloc(sizeof(float) * (size_t)(max_seq * half));
+    for (int64_t i = 0; i < half; i++) {
+        float inv = 1.0f / powf(theta, (float)(2 * i) / (float)hd);
+        for (int64_t p = 0; p < max_seq; p++) {
+            float a = (float)p * inv;
+            m->cs[p * half + i] = cosf(a);
+            m->sn[p * half + i] = sinf(a);
+        }
+    }
+    return m;
+}
+
+void rqo_llama_free(rqo_llama* m) {
+    if (!m) return;
+    free(m->w); free(m->rms1); free(m->rms2); free(m->kc); free(m->vc); free(m->cs); free(m->sn);
+    free(m);
+}
+
+int rqo_llama_set_layer(rqo_llama* m, int64_t l, const uint8_t* const* w7, const float* rms1,
+                        const float* rms2) {
+    if (l < 0 || l >= m->nl) return -1;
+    for (int i = 0; i < 7; i++) m->w[l * 7 + i] = w7[i];
+    m->rms1[l] = rms1;
+    m->rms2[l] = rms2;
+    return 0;
+}
+
+void rqo_llama_set_embedding(rqo_llama* m, const uint16_t* emb) { m->emb = emb; }
+void rqo_llama_set_head(rqo_llama* m, const float* lnf, const uint16_t* head) { m->lnf = lnf; m->head = head; }
+
+static void rms_norm(const float* x, const float* w, int64_t n, float eps, float* y) {
+    float sum2 = 0.0f;
+    for (int64_t i = 0; i < n; i++) sum2 += x[i] * x[i];
+    float mden = sqrtf(sum2 / (float)n + eps);
+    for (int64_t i = 0; i < n; i++) y[i] = x[i] / mden * w[i];
+}
+
+/* logits_last: [vocab] of the last position (may be NULL); next: argmax. */
+int rqo_llama_forward(rqo_llama* m, const int32_t* tokens, int64_t T, int64_t pos,
+                      float* logits_last, int32_t* next, int nthreads) {
+    const int64_t H = m->H, I = m->I, nh = m->nh, nkv = m->nkv, hd = m->hd, half = hd / 2;
+    const int64_t nq = nh * hd, nk = nkv * hd, rep = nh / nkv;
+    if (pos + T > m->max_seq) return -1;
+    float* x = (float*)malloc(sizeof(float) * (size_t)(T * H));
+    float* h = (float*)malloc(sizeof(float) * (size_t)(T * H));
+    float* q = (float*)malloc(sizeof(float) * (size_t)(T * nq));
+    float* k = (float*)malloc(sizeof(float) * (size_t)(T * nk));
+    float* v = (float*)malloc(sizeof(float) * (size_t)(T * nk));
+    float* a = (float*)malloc(sizeof(float) * (size_t)(T * nq));
+    float* o = (float*)malloc(sizeof(float) * (size_t)(T * H));
+    float* g = (float*)malloc(sizeof(float) * (size_t)(T * I));
+    float* u = (float*)malloc(sizeof(float) * (size_t)(T * I));
+    float* sc = (float*)malloc(sizeof(float) * (size_t)m->max_seq);
+    float* lg = (float*)malloc(sizeof(float) * (size_t)m->vocab);
+    if (!x || !h || !q || !k || !v || !a || !o || !g || !u || !sc || !lg) return -2;
+    for (int64_t t = 0; t < T; t++)
+        for (int64_t i = 0; i < H; i++) x[t * H + i] = rqo_f16_to_f32(m->emb[(int64_t)tokens[t] * H + i]);
+    for (int64_t l = 0; l < m->nl; l++) {
+        const uint8_t* const* W = m->w + l * 7;
+        float* kc = m->kc + l * nkv * m->max_seq * hd;
+        float* vc = m->vc + l * nkv * m->max_seq * hd;
+        for (int64_t t = 0; t < T; t++) rms_norm(x + t * H, m->rms1[l], H, m->eps, h + t * H);
+        rqo_linear_threaded(m->wtype, W[0], nq, H, h, T, q, nthreads);
+        rqo_linear_threaded(m->wtype, W[1], nk, H, h, T, k, nthreads);
+        rqo_linear_threaded(m->wtype, W[2], nk, H, h, T, v, nthreads);
+        for (int64_t t = 0; t < T; t++) {
+            int64_t p = pos + t;
+            const float* c = m->cs + p * half;
+            const float* s = m->sn + p * half;
+            for (int64_t hh = 0; hh < nh; hh++) {
+                float* qh = q + (t * nh + hh) * hd;
+                for (int64_t i = 0; i < half; i++) {
+                    float a0 = qh[i], b0 = qh[i + half];
+                    qh[i] = a0 * c[i] - b0 * s[i];
+                    qh[i + half] = a0 * s[i] + b0 * c[i];
+                }
+            }
+            for (int64_t kh = 0; kh < nkv; kh++) {
+                const float* ks = k + (t * nkv + kh) * hd;
+                const float* vs = v + (t * nkv + kh) * hd;
+                float* kd = kc + (kh * m->max_seq + p) * hd;
+                float* vd = vc + (kh * m->max_seq + p) * hd;
+                for (int64_t i = 0; i < half; i++) {
+                    float a0 = ks[i], b0 = ks[i + half];
+                    kd[i] = a0 * c[i] - b0 * s[i];
+                    kd[i + half] = a0 * s[i] + b0 * c[i];
+                }
+                for (int64_t i = 0; i < hd; i++) vd[i] = vs[i];
+            }
+        }
+        float sq = sqrtf((float)hd);
+        for (int64_t t = 0; t < T; t++) {
+            int64_t L = pos + t + 1;
+            for (int64_t hh = 0; hh < nh; hh++) {
+                const float* qh = q + (t * nh + hh) * hd;
+                int64_t kh = hh / rep;
+                const float* K = kc + kh * m->max_seq * hd;
+                const float* V = vc + kh * m->max_seq * hd;
+                float mx = -INFINITY;
+                for (int64_t j = 0; j < L; j++) {
+                    float acc = 0.0f;
+                    for (int64_t d = 0; d < hd; d++) acc += qh[d] * K[j * hd + d];
+                    sc[j] = acc / sq;
+                    if (sc[j] > mx) mx = sc[j];
+                }
+                float sum = 0.0f;
+                for (int64_t j = 0; j < L; j++) { sc[j] = expf(sc[j] - mx); sum += sc[j]; }
+                for (int64_t j = 0; j < L; j++) sc[j] = sc[j] / sum;
+                float* ah = a + (t * nh + hh) * hd;
+                for (int64_t d = 0; d < hd; d++) {
+                    float acc = 0.0f;
+                    for (int64_t j = 0; j < L; j++) acc += sc[j] * V[j * hd + d];
+                    ah[d] = acc;
+                }
+            }
+        }
+        rqo_linear_threaded(m->wtype, W[3], H, nq, a, T, o, nthreads);
+        for (int64_t i = 0; i < T * H; i++) x[i] = o[i] + x[i];
+        for (int64_t t = 0; t < T; t++) rms_norm(x + t * H, m->rms2[l], H, m->eps, h + t * H);
+        rqo_linear_threaded(m->wtype, W[4], I, H, h, T, g, nthreads);
+        rqo_linear_threaded(m->wtype, W[5], I, H, h, T, u, nthreads);
+        for (int64_t i = 0; i < T * I; i++) g[i] = rqo_silu(g[i]) * u[i];
+        rqo_linear_threaded(m->wtype, W[6], H, I, g, T, o, nthreads);
+        for (int64_t i = 0; i < T * H; i++) x[i] = o[i] + x[i];
+    }
+    rms_norm(x + (T - 1) * H, m->lnf, H, m->eps, h);
+    int32_t best = 0;
+    for (int64_t r = 0; r < m->vocab; r++) {
+        const uint16_t* row = m->head + r * H;
+        float acc = 0.0f;
+        for (int64_t i = 0; i < H; i++) acc += h[i] * rqo_f16_to_f32(row[i]);
+        lg[r] = acc;
+        if (acc > lg[best]) best = (int32_t)r;
+    }
+    if (logits_last) memcpy(logits_last, lg, sizeof(float) * (size_t)m->vocab);
+    if (next) *next = best;
+    free(x); free(h); free(q); free(k); free(v); free(a); free(o); free(g); free(u); free(sc); free(lg);
     return 0;
 }

@@ -84,6 +84,21 @@ int rqo_moe_forward(const float* x, int64_t T, int64_t H, int64_t F, int E, int 
 /* silu in f32: x / (1 + exp(-x)) (candle_nn::ops::silu) */
 float rqo_silu(float x);
 
+/* Quantized Llama forward (src/streaming_quantized.rs:193-317,611-633) with
+ * its own KV cache; weights are borrowed (GGML blocks of type wtype for the
+ * seven linears q,k,v,o,gate,up,down; F16 embedding and lm_head). */
+typedef struct rqo_llama rqo_llama;
+rqo_llama* rqo_llama_create(int64_t hidden, int64_t inter, int64_t n_heads, int64_t n_kv,
+                            int64_t head_dim, int64_t n_layers, int64_t vocab, int64_t max_seq,
+                            float eps, float theta, int wtype);
+void rqo_llama_free(rqo_llama* m);
+int rqo_llama_set_layer(rqo_llama* m, int64_t layer, const uint8_t* const* w7, const float* rms1,
+                        const float* rms2);
+void rqo_llama_set_embedding(rqo_llama* m, const uint16_t* emb);
+void rqo_llama_set_head(rqo_llama* m, const float* ln_f, const uint16_t* lm_head);
+int rqo_llama_forward(rqo_llama* m, const int32_t* tokens, int64_t T, int64_t index_pos,
+                      float* logits_last, int32_t* next, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

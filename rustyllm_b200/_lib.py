@@ -52,6 +52,29 @@ SIGNATURES = {
     "rq_linear_batch": (I, [P, I, PP, PP, PP, P]),
 }
 
+class LlamaConfig(ctypes.Structure):
+    """rq_llama_config of include/rq.h."""
+    _fields_ = [("hidden", ctypes.c_int64), ("intermediate", ctypes.c_int64),
+                ("n_heads", ctypes.c_int64), ("n_kv_heads", ctypes.c_int64),
+                ("head_dim", ctypes.c_int64), ("n_layers", ctypes.c_int64),
+                ("vocab", ctypes.c_int64), ("max_seq", ctypes.c_int64),
+                ("max_batch_tokens", ctypes.c_int64), ("rms_eps", ctypes.c_float),
+                ("rope_theta", ctypes.c_float)]
+
+
+SIGNATURES.update({
+    "rq_llama_create": (I, [P, ctypes.POINTER(LlamaConfig), PP]),
+    "rq_llama_free": (I, [P]),
+    "rq_llama_set_layer": (I, [P, I64, PP, P, P]),
+    "rq_llama_set_embedding": (I, [P, P]),
+    "rq_llama_set_head": (I, [P, P, P]),
+    "rq_llama_forward": (I, [P, P, I64, I64, P, P, P]),
+    "rq_llama_decode_step": (I, [P, P]),
+    "rq_llama_tokens": (I, [P, P, I64, ctypes.POINTER(I64), ctypes.POINTER(I64)]),
+    "rq_llama_reset_tokens": (I, [P]),
+    "rq_llama_truncate": (I, [P, I64]),
+})
+
 _lib = None
 
 

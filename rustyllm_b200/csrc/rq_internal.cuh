@@ -103,19 +103,28 @@ constexpr int kMaxJobs = 8;
 struct PipeJob {
     const uint8_t* qs;
     const uint8_t* hdr;
-    XQ xq;  // the staged activation row of this job
+    XQ xq;             // the staged activation row of this job
     float* y;
+    const float* add;  // optional residual: y = x W^T + add (may alias y)
     int64_t out;
 };
 bool pipe_supported(const rq_weight* w);
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
-                       int sm_count, cudaStream_t st, int* err = nullptr);
+                       int sm_count, cudaStream_t st, int* err = nullptr,
+                       const float* const* adds = nullptr);
 
 // linear kernels (rq_matvec.cu).  launch_linear runs y = x W^T for M staged
 // activation rows (launch_xquant first).  launch_xquant_rows stages up to
 // kMaxJobs separate rows (row j of `in` floats at xs[j]) into consecutive
 // rows of xq in one launch.
 int launch_xquant(const float* x, int64_t M, int64_t in, XQ xq, cudaStream_t st);
+// Staging with a fused producer op (one CTA per row): RMSNorm
+// (x / sqrt(mean(x^2) + eps) * w, candle_nn::ops::rms_norm order) or SwiGLU
+// (silu(x) * up).
+int launch_xquant_rmsnorm(const float* x, const float* w, float eps, int64_t M, int64_t in, XQ xq,
+                          cudaStream_t st);
+int launch_xquant_swiglu(const float* gate, const float* up, int64_t M, int64_t in, XQ xq,
+                         cudaStream_t st);
 int launch_xquant_rows(const float* const* xs, int n, int64_t in, XQ xq, cudaStream_t st);
 int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, cudaStream_t st);
 

@@ -1,0 +1,675 @@
+// rq_llama.cu -- the quantized Llama decode loop on the GPU: the forward of
+// StreamingLlamaQuantized (src/streaming_quantized.rs:622-729) with every
+// QBlock resident (src/streaming_quantized.rs:282-318) and the greedy step of
+// generate (src/streaming_quantized.rs:539-593).
+//
+// Per layer (T tokens):
+//   stage(rmsnorm(x, rms_1))      -> q, k, v  (one batched matvec launch)
+//   rope(q, k); append k, v to the layer's KV cache at pos .. pos+T-1
+//   attention (GQA, causal, softmax in f32)  -> a
+//   stage(a) -> o_proj, + residual x          (epilogue add)
+//   stage(rmsnorm(x, rms_2))      -> gate, up (one batched launch)
+//   stage(silu(gate) * up)        -> down, + residual x
+// then rmsnorm(x[T-1], ln_f), the F16 lm_head matvec fused with a
+// first-index argmax, and the device-side token / position update.  The
+// decode step (T = 1) reads its token and position from device memory, so a
+// whole step can be captured in one CUDA graph.
+//
+// Numerics follow the reference: activations, KV cache and attention in f32;
+// embedding and lm_head weights F16 (exact GGUF F16 values, dequantized to
+// f32 before use); RoPE tables computed on the host in f32 exactly as
+// QuantStreamCache::new does.
+
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "rq_internal.cuh"
+
+struct rq_llama {
+    rq_ctx* ctx;
+    rq_llama_config cfg;
+    struct Layer {
+        const rq_weight* w[7];  // q, k, v, o, gate, up, down (borrowed)
+        float* rms1;
+        float* rms2;
+        float* kc;  // [n_kv][max_seq][head_dim]
+        float* vc;
+    };
+    std::vector<Layer> layers;
+    __half* embed;    // [vocab][hidden]
+    float* ln_f;      // [hidden]
+    __half* lm_head;  // [vocab][hidden]
+    float* rope_cos;  // [max_seq][head_dim/2]
+    float* rope_sin;
+    // activations
+    float* x;     // [Tmax][hidden] residual stream
+    float* q;     // [Tmax][n_heads*head_dim]
+    float* k;     // [Tmax][n_kv*head_dim]
+    float* v;
+    float* att;   // [Tmax][n_heads*head_dim]
+    float* g;     // [Tmax][intermediate]
+    float* u;
+    float* hf;    // [hidden] final normed row
+    float* logits;  // [vocab]
+    rq::XQ xq;      // Tmax rows of max(hidden, intermediate)
+    // device state
+    unsigned long long* best;  // packed (value, -index) of the argmax
+    int32_t* tokens;           // [Tmax] current input tokens
+    int32_t* pos;              // current position (KV length before this step)
+    int32_t* out;              // [max_seq] generated tokens
+    int32_t* nout;
+    std::vector<void*> allocs;
+};
+
+namespace rq {
+namespace {
+
+cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st, cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// x[t][:] = f32(embed[tokens[t]][:])  (Embedding::forward over F16 weights
+// dequantized to f32 by GgufLayer::tensor)
+__global__ void embed_kernel(const __half* __restrict__ emb, const int32_t* __restrict__ tokens,
+                             int64_t T, int64_t hidden, int64_t vocab, float* __restrict__ x) {
+    pdl_enter();
+    const int64_t t = blockIdx.y;
+    if (t >= T) return;
+    int32_t tok = tokens[t];
+    tok = tok < 0 ? 0 : (tok >= vocab ? (int32_t)(vocab - 1) : tok);
+    const __half* row = emb + (int64_t)tok * hidden;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += (int64_t)gridDim.x * blockDim.x)
+        x[t * hidden + i] = __half2float(row[i]);
+}
+
+// RoPE (candle_nn::rotary_emb::rope, non-interleaved halves) on q and k of
+// token t at position pos+t, and the KV-cache append.
+// grid (n_heads + n_kv, T), block head_dim/2.
+__global__ void rope_append_kernel(float* __restrict__ q, const float* __restrict__ k,
+                                   const float* __restrict__ v, float* __restrict__ kc,
+                                   float* __restrict__ vc, const float* __restrict__ cos_t,
+                                   const float* __restrict__ sin_t, const int32_t* __restrict__ pos,
+                                   int n_heads, int n_kv, int hd, int max_seq) {
+    pdl_enter();
+    const int hh = blockIdx.x, t = blockIdx.y, i = threadIdx.x, half = hd / 2;
+    const int p = *pos + t;
+    if (p >= max_seq || i >= half) return;
+    const float c = cos_t[(int64_t)p * half + i], s = sin_t[(int64_t)p * half + i];
+    if (hh < n_heads) {
+        float* qh = q + ((int64_t)t * n_heads + hh) * hd;
+        const float a = qh[i], b = qh[i + half];
+        qh[i] = a * c - b * s;
+        qh[i + half] = a * s + b * c;
+    } else {
+        const int kh = hh - n_heads;
+        const float* kh_src = k + ((int64_t)t * n_kv + kh) * hd;
+        const float* vh_src = v + ((int64_t)t * n_kv + kh) * hd;
+        float* kdst = kc + ((int64_t)kh * max_seq + p) * hd;
+        float* vdst = vc + ((int64_t)kh * max_seq + p) * hd;
+        const float a = kh_src[i], b = kh_src[i + half];
+        kdst[i] = a * c - b * s;
+        kdst[i + half] = a * s + b * c;
+        vdst[i] = vh_src[i];
+        vdst[i + half] = vh_src[i + half];
+    }
+}
+
+// Causal GQA attention for query token t of head h (QAttn::forward,
+// src/streaming_quantized.rs:241-255): scores = q.k / sqrt(hd) over the
+// pos+t+1 cached keys of kv head h / (n_heads / n_kv), softmax, weighted sum
+// of values.  grid (n_heads, T), block 128, dynamic smem max_seq floats.
+__global__ void attention_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                 const float* __restrict__ vc, const int32_t* __restrict__ pos,
+                                 int n_heads, int n_kv, int hd, int max_seq, float* __restrict__ out) {
+    pdl_enter();
+    extern __shared__ float sc[];
+    __shared__ float red[32];
+    const int h = blockIdx.x, t = blockIdx.y;
+    const int L = min(*pos + t + 1, max_seq);
+    const int kh = h / (n_heads / n_kv);
+    const float* qh = q + ((int64_t)t * n_heads + h) * hd;
+    const float* K = kc + (int64_t)kh * max_seq * hd;
+    const float* V = vc + (int64_t)kh * max_seq * hd;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const float inv_sqrt = 1.0f / sqrtf((float)hd);
+    for (int j = warp; j < L; j += nw) {
+        float acc = 0.0f;
+        for (int d = lane; d < hd; d += 32) acc = fmaf(qh[d], K[(int64_t)j * hd + d], acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) sc[j] = acc * inv_sqrt;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < L; j += blockDim.x) mx = fmaxf(mx, sc[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < nw; w++) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int j = threadIdx.x; j < L; j += blockDim.x) {
+        const float e = expf(sc[j] - mx);
+        sc[j] = e;
+        sum += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    sum = 0.0f;
+    for (int w = 0; w < nw; w++) sum += red[w];
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float acc = 0.0f;
+        for (int j = 0; j < L; j++) acc = fmaf(sc[j] / sum, V[(int64_t)j * hd + d], acc);
+        out[((int64_t)t * n_heads + h) * hd + d] = acc;
+    }
+}
+
+// hf = rmsnorm(x[row], w) for one row (the lm_head input).
+__global__ void rmsnorm_row_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                   float eps, int64_t hidden, float* __restrict__ y) {
+    pdl_enter();
+    __shared__ float wsum[32];
+    float s2 = 0.0f;
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) s2 = fmaf(x[i], x[i], s2);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = s2;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int k = 0; k < (int)(blockDim.x >> 5); k++) tot += wsum[k];
+    const float m = sqrtf(tot / (float)hidden + eps);
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) y[i] = x[i] / m * w[i];
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);  // order-preserving
+    return ((unsigned long long)b << 32) | (0xFFFFFFFFu - idx);  // ties: lower index wins
+}
+
+// logits[r] = sum_k hf[k] * f32(W[r][k]) over an F16 [vocab][hidden] matrix,
+// one warp per row, 16-byte streaming loads; the block's best (value, row)
+// is folded into *best with one atomicMax.  hidden % 8 == 0.
+__global__ void __launch_bounds__(256) lm_head_kernel(const __half* __restrict__ W,
+                                                      const float* __restrict__ hf, int64_t vocab,
+                                                      int64_t hidden, float* __restrict__ logits,
+                                                      unsigned long long* __restrict__ best) {
+    extern __shared__ float xs[];
+    pdl_enter();
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) xs[i] = hf[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned long long mykey = 0ull;
+    for (int64_t r = (int64_t)blockIdx.x * 8 + warp; r < vocab; r += (int64_t)gridDim.x * 8) {
+        const uint4* row = reinterpret_cast<const uint4*>(W + r * hidden);
+        float acc = 0.0f;
+        for (int64_t c = lane; c < hidden / 8; c += 32) {
+            uint4 u;
+            asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                         : "l"(row + c));
+            const float4 xa = reinterpret_cast<const float4*>(xs)[2 * c];
+            const float4 xb = reinterpret_cast<const float4*>(xs)[2 * c + 1];
+            const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+            const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+            const float2 w2 = __half22float2(*reinterpret_cast<const __half2*>(&u.z));
+            const float2 w3 = __half22float2(*reinterpret_cast<const __half2*>(&u.w));
+            acc = fmaf(xa.x, w0.x, acc); acc = fmaf(xa.y, w0.y, acc);
+            acc = fmaf(xa.z, w1.x, acc); acc = fmaf(xa.w, w1.y, acc);
+            acc = fmaf(xb.x, w2.x, acc); acc = fmaf(xb.y, w2.y, acc);
+            acc = fmaf(xb.z, w3.x, acc); acc = fmaf(xb.w, w3.y, acc);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            if (logits) logits[r] = acc;
+            const unsigned long long key = argmax_key(acc, (uint32_t)r);
+            mykey = key > mykey ? key : mykey;
+        }
+    }
+    __shared__ unsigned long long kb[8];
+    if (lane == 0) kb[warp] = mykey;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long k = kb[0];
+        for (int w = 1; w < 8; w++) k = kb[w] > k ? kb[w] : k;
+        atomicMax(best, k);
+    }
+}
+
+// Greedy step bookkeeping: next token = argmax, appended to the output list;
+// position advances by T; the argmax slot is cleared for the next step.
+__global__ void finish_step_kernel(unsigned long long* best, int32_t* tokens, int32_t* pos,
+                                   int32_t* out, int32_t* nout, int T, int max_out) {
+    pdl_enter();
+    const unsigned long long k = *best;
+    const int32_t tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    tokens[0] = tok;
+    *pos += T;
+    const int n = *nout;
+    if (n < max_out) out[n] = tok;
+    *nout = n + 1;
+    *best = 0ull;
+}
+
+__global__ void add_rows_kernel(float* __restrict__ y, const float* __restrict__ a, int64_t n) {
+    pdl_enter();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] += a[i];
+}
+
+int launch_simple(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args,
+                  const char* what) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(grid, block, smem, st, attr);
+    return cuda_error(cudaLaunchKernelExC(&cfg, fn, args), what);
+}
+
+// y_i[t] = x[t] W_i^T (+ add_i[t]) for the n weights (same in) and T staged rows.
+int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* const* ys,
+                const float* const* adds, cudaStream_t st) {
+    const int64_t in = ws[0]->in;
+    const int sm = m->ctx->sm_count;
+    if (pipe_supported(ws[0])) {
+        const rq_weight* jw[kMaxJobs];
+        XQ jx[kMaxJobs];
+        float* jy[kMaxJobs];
+        const float* ja[kMaxJobs];
+        int nj = 0;
+        for (int64_t t = 0; t < T; t++)
+            for (int i = 0; i < n; i++) {
+                jw[nj] = ws[i];
+                jx[nj] = XQ{m->xq.planes + t * 3 * in, m->xq.stats + t * (in / 32)};
+                jy[nj] = ys[i] + t * ws[i]->out;
+                ja[nj] = adds && adds[i] ? adds[i] + t * ws[i]->out : nullptr;
+                if (++nj == kMaxJobs) {
+                    int rc = launch_matvec_pipe(jw, jx, jy, nj, sm, st, nullptr, ja);
+                    if (rc) return rc;
+                    nj = 0;
+                }
+            }
+        return nj ? launch_matvec_pipe(jw, jx, jy, nj, sm, st, nullptr, ja) : RQ_OK;
+    }
+    for (int i = 0; i < n; i++) {
+        if (adds && adds[i] && adds[i] != ys[i])
+            return set_error(RQ_ERR_UNSUPPORTED, "llama: residual into a separate buffer needs the pipeline");
+        if (adds && adds[i]) {
+            // y += x W^T: compute into the scratch g, then add
+            int rc = launch_linear(ws[i], m->xq, m->g, T, sm, st);
+            if (rc) return rc;
+            int64_t cnt = T * ws[i]->out;
+            float* y = ys[i];
+            const float* a = m->g;
+            void* args[] = {&y, &a, &cnt};
+            rc = launch_simple((const void*)add_rows_kernel, dim3(256), dim3(256), 0, st, args, "add kernel");
+            if (rc) return rc;
+        } else {
+            int rc = launch_linear(ws[i], m->xq, ys[i], T, sm, st);
+            if (rc) return rc;
+        }
+    }
+    return RQ_OK;
+}
+
+// One forward over the T tokens in m->tokens at device position *m->pos.
+int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
+    const rq_llama_config& c = m->cfg;
+    const int64_t H = c.hidden, I = c.intermediate, nq = c.n_heads * c.head_dim, nk = c.n_kv_heads * c.head_dim;
+    int rc;
+    {
+        const __half* emb = m->embed;
+        const int32_t* tok = m->tokens;
+        int64_t vocab = c.vocab, hidden = H;
+        float* x = m->x;
+        void* args[] = {&emb, &tok, &T, &hidden, &vocab, &x};
+        rc = launch_simple((const void*)embed_kernel, dim3((unsigned)std::min<int64_t>(64, (H + 255) / 256), (unsigned)T),
+                           dim3(256), 0, st, args, "embed kernel");
+        if (rc) return rc;
+    }
+    for (int64_t l = 0; l < c.n_layers; l++) {
+        rq_llama::Layer& L = m->layers[l];
+        rc = launch_xquant_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xq, st);
+        if (rc) return rc;
+        {
+            const rq_weight* w3[3] = {L.w[0], L.w[1], L.w[2]};
+            float* y3[3] = {m->q, m->k, m->v};
+            rc = run_linears(m, 3, w3, T, y3, nullptr, st);
+            if (rc) return rc;
+        }
+        {
+            float* q = m->q;
+            const float* k = m->k;
+            const float* v = m->v;
+            float* kc = L.kc;
+            float* vc = L.vc;
+            const float* cs = m->rope_cos;
+            const float* sn = m->rope_sin;
+            const int32_t* pos = m->pos;
+            int nh = (int)c.n_heads, nkv = (int)c.n_kv_heads, hd = (int)c.head_dim, ms = (int)c.max_seq;
+            void* args[] = {&q, &k, &v, &kc, &vc, &cs, &sn, &pos, &nh, &nkv, &hd, &ms};
+            rc = launch_simple((const void*)rope_append_kernel, dim3((unsigned)(nh + nkv), (unsigned)T),
+                               dim3((unsigned)std::max(32, hd / 2)), 0, st, args, "rope kernel");
+            if (rc) return rc;
+            const float* qc = m->q;
+            float* att = m->att;
+            void* args2[] = {&qc, &kc, &vc, &pos, &nh, &nkv, &hd, &ms, &att};
+            rc = launch_simple((const void*)attention_kernel, dim3((unsigned)nh, (unsigned)T), dim3(128),
+                               (size_t)c.max_seq * sizeof(float), st, args2, "attention kernel");
+            if (rc) return rc;
+        }
+        rc = launch_xquant(m->att, T, nq, m->xq, st);
+        if (rc) return rc;
+        {
+            const rq_weight* w1[1] = {L.w[3]};
+            float* y1[1] = {m->x};
+            const float* a1[1] = {m->x};
+            rc = run_linears(m, 1, w1, T, y1, a1, st);
+            if (rc) return rc;
+        }
+        rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
+        if (rc) return rc;
+        {
+            const rq_weight* w2[2] = {L.w[4], L.w[5]};
+            float* y2[2] = {m->g, m->u};
+            rc = run_linears(m, 2, w2, T, y2, nullptr, st);
+            if (rc) return rc;
+        }
+        rc = launch_xquant_swiglu(m->g, m->u, T, I, m->xq, st);
+        if (rc) return rc;
+        {
+            const rq_weight* w1[1] = {L.w[6]};
+            float* y1[1] = {m->x};
+            const float* a1[1] = {m->x};
+            rc = run_linears(m, 1, w1, T, y1, a1, st);
+            if (rc) return rc;
+        }
+    }
+    (void)nk;
+    {
+        const float* xl = m->x + (T - 1) * H;
+        const float* w = m->ln_f;
+        float eps = c.rms_eps;
+        int64_t hidden = H;
+        float* hf = m->hf;
+        void* args[] = {&xl, &w, &eps, &hidden, &hf};
+        rc = launch_simple((const void*)rmsnorm_row_kernel, dim3(1), dim3(1024), 0, st, args, "final norm kernel");
+        if (rc) return rc;
+    }
+    {
+        const __half* W = m->lm_head;
+        const float* hf = m->hf;
+        int64_t vocab = c.vocab, hidden = H;
+        float* lg = want_logits ? m->logits : nullptr;
+        unsigned long long* best = m->best;
+        void* args[] = {&W, &hf, &vocab, &hidden, &lg, &best};
+        const unsigned grid = (unsigned)std::min<int64_t>((vocab + 7) / 8, (int64_t)m->ctx->sm_count * 8);
+        rc = launch_simple((const void*)lm_head_kernel, dim3(grid), dim3(256), (size_t)H * sizeof(float), st,
+                           args, "lm_head kernel");
+        if (rc) return rc;
+    }
+    {
+        unsigned long long* best = m->best;
+        int32_t* tok = m->tokens;
+        int32_t* pos = m->pos;
+        int32_t* out = m->out;
+        int32_t* nout = m->nout;
+        int Ti = (int)T, mo = (int)c.max_seq;
+        void* args[] = {&best, &tok, &pos, &out, &nout, &Ti, &mo};
+        rc = launch_simple((const void*)finish_step_kernel, dim3(1), dim3(1), 0, st, args, "finish kernel");
+    }
+    return rc;
+}
+
+template <typename T>
+int dalloc(rq_llama* m, T** p, size_t n) {
+    cudaError_t e = cudaMalloc((void**)p, n * sizeof(T));
+    if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(llama)");
+    m->allocs.push_back((void*)*p);
+    return RQ_OK;
+}
+
+int copy_in(void* dst, const void* src, size_t bytes) {
+    cudaPointerAttributes a;
+    cudaMemcpyKind kind = cudaMemcpyHostToDevice;
+    if (cudaPointerGetAttributes(&a, src) == cudaSuccess &&
+        (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged))
+        kind = cudaMemcpyDeviceToDevice;
+    cudaGetLastError();
+    return cuda_error(cudaMemcpy(dst, src, bytes, kind), "llama weight copy");
+}
+
+struct Guard {
+    int prev = -1;
+    explicit Guard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~Guard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+}  // namespace rq
+
+using namespace rq;
+
+extern "C" {
+
+int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
+    if (!ctx || !cfg || !out) return set_error(RQ_ERR_INVALID, "rq_llama_create: NULL argument");
+    *out = nullptr;
+    const rq_llama_config& c = *cfg;
+    if (c.hidden <= 0 || c.intermediate <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 ||
+        c.n_layers <= 0 || c.vocab <= 0 || c.max_seq <= 0 || c.max_batch_tokens <= 0)
+        return set_error(RQ_ERR_INVALID, "rq_llama_create: every size must be positive");
+    if (c.n_heads % c.n_kv_heads || c.head_dim % 2 || c.head_dim > 256 || c.hidden % 256 ||
+        c.intermediate % 256 || (c.n_heads * c.head_dim) % 256)
+        return set_error(RQ_ERR_INVALID,
+                         "rq_llama_create: need n_heads %% n_kv_heads == 0, even head_dim <= 256, and "
+                         "hidden, intermediate, n_heads*head_dim multiples of 256");
+    if (c.max_seq * (int64_t)sizeof(float) > 200 * 1024)
+        return set_error(RQ_ERR_INVALID, "rq_llama_create: max_seq %lld too large for attention", (long long)c.max_seq);
+    Guard g(ctx->device);
+    rq_llama* m = new (std::nothrow) rq_llama();
+    if (!m) return set_error(RQ_ERR_OOM, "host allocation failed");
+    m->ctx = ctx;
+    m->cfg = c;
+    m->layers.resize((size_t)c.n_layers);
+    const int64_t T = c.max_batch_tokens, H = c.hidden, I = c.intermediate;
+    const int64_t nq = c.n_heads * c.head_dim, nk = c.n_kv_heads * c.head_dim, half = c.head_dim / 2;
+    const int64_t maxin = std::max(std::max(H, I), nq);
+    int rc = RQ_OK;
+    for (auto& L : m->layers) {
+        memset(L.w, 0, sizeof L.w);
+        if (!rc) rc = dalloc(m, &L.rms1, (size_t)H);
+        if (!rc) rc = dalloc(m, &L.rms2, (size_t)H);
+        if (!rc) rc = dalloc(m, &L.kc, (size_t)(nk * c.max_seq));
+        if (!rc) rc = dalloc(m, &L.vc, (size_t)(nk * c.max_seq));
+    }
+    if (!rc) rc = dalloc(m, &m->embed, (size_t)(c.vocab * H));
+    if (!rc) rc = dalloc(m, &m->ln_f, (size_t)H);
+    if (!rc) rc = dalloc(m, &m->lm_head, (size_t)(c.vocab * H));
+    if (!rc) rc = dalloc(m, &m->rope_cos, (size_t)(c.max_seq * half));
+    if (!rc) rc = dalloc(m, &m->rope_sin, (size_t)(c.max_seq * half));
+    if (!rc) rc = dalloc(m, &m->x, (size_t)(T * H));
+    if (!rc) rc = dalloc(m, &m->q, (size_t)(T * nq));
+    if (!rc) rc = dalloc(m, &m->k, (size_t)(T * nk));
+    if (!rc) rc = dalloc(m, &m->v, (size_t)(T * nk));
+    if (!rc) rc = dalloc(m, &m->att, (size_t)(T * nq));
+    if (!rc) rc = dalloc(m, &m->g, (size_t)(T * std::max(I, H)));
+    if (!rc) rc = dalloc(m, &m->u, (size_t)(T * I));
+    if (!rc) rc = dalloc(m, &m->hf, (size_t)H);
+    if (!rc) rc = dalloc(m, &m->logits, (size_t)c.vocab);
+    uint8_t* xqbuf = nullptr;
+    if (!rc) rc = dalloc(m, &xqbuf, xq_bytes(T, maxin));
+    if (!rc) rc = dalloc(m, &m->best, 1);
+    if (!rc) rc = dalloc(m, &m->tokens, (size_t)T);
+    if (!rc) rc = dalloc(m, &m->pos, 1);
+    if (!rc) rc = dalloc(m, &m->out, (size_t)c.max_seq);
+    if (!rc) rc = dalloc(m, &m->nout, 1);
+    if (!rc) {
+        m->xq.planes = (int8_t*)xqbuf;
+        m->xq.stats = (float4*)(xqbuf + (((size_t)T * 3 * maxin + 255) & ~(size_t)255));
+        // RoPE tables as QuantStreamCache::new computes them
+        // (src/streaming_quantized.rs:104-118): inv_freq[i] =
+        // 1 / theta^(2i / head_dim), angle = f32(position) * inv_freq[i].
+        std::vector<float> cs((size_t)(c.max_seq * half)), sn(cs.size());
+        for (int64_t i = 0; i < half; i++) {
+            const float inv = 1.0f / powf(c.rope_theta, (float)(2 * i) / (float)c.head_dim);
+            for (int64_t p = 0; p < c.max_seq; p++) {
+                const float a = (float)p * inv;
+                cs[(size_t)(p * half + i)] = cosf(a);
+                sn[(size_t)(p * half + i)] = sinf(a);
+            }
+        }
+        rc = cuda_error(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope copy");
+        if (!rc) rc = cuda_error(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope copy");
+        if (!rc) rc = cuda_error(cudaMemset(m->best, 0, 8), "memset");
+        if (!rc) rc = cuda_error(cudaMemset(m->pos, 0, 4), "memset");
+        if (!rc) rc = cuda_error(cudaMemset(m->nout, 0, 4), "memset");
+        if (!rc) rc = cuda_error(cudaMemset(m->tokens, 0, (size_t)T * 4), "memset");
+    }
+    if (rc) {
+        for (void* p : m->allocs) cudaFree(p);
+        delete m;
+        return rc;
+    }
+    *out = m;
+    return RQ_OK;
+}
+
+int rq_llama_free(rq_llama* m) {
+    if (!m) return RQ_OK;
+    Guard g(m->ctx->device);
+    for (void* p : m->allocs) cudaFree(p);
+    delete m;
+    return RQ_OK;
+}
+
+int rq_llama_set_layer(rq_llama* m, int64_t layer, const rq_weight* const* w7, const float* rms1,
+                       const float* rms2) {
+    if (!m || !w7 || !rms1 || !rms2) return set_error(RQ_ERR_INVALID, "rq_llama_set_layer: NULL argument");
+    const rq_llama_config& c = m->cfg;
+    if (layer < 0 || layer >= c.n_layers) return set_error(RQ_ERR_INVALID, "rq_llama_set_layer: layer %lld", (long long)layer);
+    const int64_t H = c.hidden, I = c.intermediate, nq = c.n_heads * c.head_dim, nk = c.n_kv_heads * c.head_dim;
+    const int64_t shp[7][2] = {{nq, H}, {nk, H}, {nk, H}, {H, nq}, {I, H}, {I, H}, {H, I}};  // (out, in)
+    const char* names[7] = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"};
+    for (int i = 0; i < 7; i++) {
+        if (!w7[i]) return set_error(RQ_ERR_INVALID, "rq_llama_set_layer: %s is NULL", names[i]);
+        if (w7[i]->out != shp[i][0] || w7[i]->in != shp[i][1] || w7[i]->device != m->ctx->device)
+            return set_error(RQ_ERR_INVALID, "rq_llama_set_layer: %s is [%lld, %lld], expected [%lld, %lld]",
+                             names[i], (long long)w7[i]->out, (long long)w7[i]->in, (long long)shp[i][0],
+                             (long long)shp[i][1]);
+    }
+    if (w7[0]->type != w7[1]->type || w7[0]->type != w7[2]->type || w7[4]->type != w7[5]->type)
+        return set_error(RQ_ERR_INVALID, "rq_llama_set_layer: q/k/v and gate/up must share a weight type");
+    Guard g(m->ctx->device);
+    rq_llama::Layer& L = m->layers[(size_t)layer];
+    for (int i = 0; i < 7; i++) L.w[i] = w7[i];
+    int rc = copy_in(L.rms1, rms1, (size_t)H * 4);
+    if (!rc) rc = copy_in(L.rms2, rms2, (size_t)H * 4);
+    return rc;
+}
+
+int rq_llama_set_embedding(rq_llama* m, const uint16_t* embed_f16) {
+    if (!m || !embed_f16) return set_error(RQ_ERR_INVALID, "rq_llama_set_embedding: NULL argument");
+    Guard g(m->ctx->device);
+    return copy_in(m->embed, embed_f16, (size_t)(m->cfg.vocab * m->cfg.hidden) * 2);
+}
+
+int rq_llama_set_head(rq_llama* m, const float* ln_f, const uint16_t* lm_head_f16) {
+    if (!m || !ln_f || !lm_head_f16) return set_error(RQ_ERR_INVALID, "rq_llama_set_head: NULL argument");
+    Guard g(m->ctx->device);
+    int rc = copy_in(m->ln_f, ln_f, (size_t)m->cfg.hidden * 4);
+    if (!rc) rc = copy_in(m->lm_head, lm_head_f16, (size_t)(m->cfg.vocab * m->cfg.hidden) * 2);
+    return rc;
+}
+
+int rq_llama_forward(rq_llama* m, const int32_t* tokens, int64_t T, int64_t index_pos, float* logits,
+                     int32_t* next_token, void* stream) {
+    if (!m || !tokens) return set_error(RQ_ERR_INVALID, "rq_llama_forward: NULL argument");
+    const rq_llama_config& c = m->cfg;
+    if (T < 1 || T > c.max_batch_tokens)
+        return set_error(RQ_ERR_INVALID, "rq_llama_forward: T = %lld (1..%lld)", (long long)T,
+                         (long long)c.max_batch_tokens);
+    if (index_pos < 0 || index_pos + T > c.max_seq)
+        return set_error(RQ_ERR_INVALID, "rq_llama_forward: positions %lld..%lld exceed max_seq %lld",
+                         (long long)index_pos, (long long)(index_pos + T), (long long)c.max_seq);
+    for (auto& L : m->layers)
+        if (!L.w[0]) return set_error(RQ_ERR_INVALID, "rq_llama_forward: a layer was not set");
+    Guard g(m->ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    int32_t p = (int32_t)index_pos;
+    int rc = cuda_error(cudaMemcpyAsync(m->tokens, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, st), "token copy");
+    if (!rc) rc = cuda_error(cudaMemcpyAsync(m->pos, &p, 4, cudaMemcpyHostToDevice, st), "pos copy");
+    if (!rc) rc = forward_device(m, T, logits != nullptr, st);
+    if (!rc && logits)
+        rc = cuda_error(cudaMemcpyAsync(logits, m->logits, (size_t)c.vocab * 4, cudaMemcpyDefault, st), "logits copy");
+    if (!rc && next_token)
+        rc = cuda_error(cudaMemcpyAsync(next_token, m->tokens, 4, cudaMemcpyDeviceToHost, st), "token copy");
+    if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "rq_llama_forward sync");
+    return rc;
+}
+
+int rq_llama_decode_step(rq_llama* m, void* stream) {
+    if (!m) return set_error(RQ_ERR_INVALID, "rq_llama_decode_step: NULL argument");
+    Guard g(m->ctx->device);
+    return forward_device(m, 1, false, (cudaStream_t)stream);
+}
+
+int rq_llama_tokens(rq_llama* m, int32_t* out, int64_t cap, int64_t* count, int64_t* position) {
+    if (!m) return set_error(RQ_ERR_INVALID, "rq_llama_tokens: NULL argument");
+    Guard g(m->ctx->device);
+    int32_t n = 0, p = 0;
+    int rc = cuda_error(cudaMemcpy(&n, m->nout, 4, cudaMemcpyDeviceToHost), "count copy");
+    if (!rc) rc = cuda_error(cudaMemcpy(&p, m->pos, 4, cudaMemcpyDeviceToHost), "pos copy");
+    if (!rc && out && cap > 0) {
+        const int64_t k = std::min<int64_t>(std::min<int64_t>(n, cap), m->cfg.max_seq);
+        if (k > 0) rc = cuda_error(cudaMemcpy(out, m->out, (size_t)k * 4, cudaMemcpyDeviceToHost), "tokens copy");
+    }
+    if (count) *count = n;
+    if (position) *position = p;
+    return rc;
+}
+
+int rq_llama_truncate(rq_llama* m, int64_t new_len) {
+    if (!m) return set_error(RQ_ERR_INVALID, "rq_llama_truncate: NULL argument");
+    if (new_len < 0 || new_len > m->cfg.max_seq)
+        return set_error(RQ_ERR_INVALID, "rq_llama_truncate: %lld", (long long)new_len);
+    Guard g(m->ctx->device);
+    int32_t p = (int32_t)new_len;
+    // positions >= new_len are overwritten by later appends; only the
+    // position moves (QuantStreamCache::truncate narrows the cache to new_len)
+    return cuda_error(cudaMemcpy(m->pos, &p, 4, cudaMemcpyHostToDevice), "truncate");
+}
+
+int rq_llama_reset_tokens(rq_llama* m) {
+    if (!m) return set_error(RQ_ERR_INVALID, "rq_llama_reset_tokens: NULL argument");
+    Guard g(m->ctx->device);
+    return cuda_error(cudaMemset(m->nout, 0, 4), "reset");
+}
+
+}  // extern "C"

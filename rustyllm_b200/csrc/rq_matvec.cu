@@ -33,6 +33,100 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 // programmatic dependent: it first waits for the preceding kernel (which may
 // produce x), then lets the following matvec launch so that its weight
 // streaming overlaps this kernel.
+// Stage the 32 values v (one block of row m, block b) into the planes and
+// stats of xq; the arithmetic of the staged form (see rq_internal.cuh).
+__device__ __forceinline__ void stage_block(const float (&v)[32], int64_t m, int64_t b, int64_t in,
+                                            int8_t* __restrict__ planes, float4* __restrict__ stats) {
+    float amax = 0.0f, sa = 0.0f, sb = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; k++) { amax = fmaxf(amax, fabsf(v[k])); sa += v[k]; }
+#pragma unroll
+    for (int k = 16; k < 32; k++) { amax = fmaxf(amax, fabsf(v[k])); sb += v[k]; }
+    const float inv = amax > 0.0f ? kXQScale / amax : 0.0f;
+    const float sx = amax / kXQScale;
+    uint32_t p1[8], p2[8], p3[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) { p1[k] = 0u; p2[k] = 0u; p3[k] = 0u; }
+#pragma unroll
+    for (int k = 0; k < 32; k++) {
+        const int X = __float2int_rn(v[k] * inv);
+        const int x3 = (X << 24) >> 24;  // balanced base-256 digits
+        const int t1 = (X - x3) >> 8;
+        const int x2 = (t1 << 24) >> 24;
+        const int x1 = (t1 - x2) >> 8;
+        p1[k / 4] |= (uint32_t)(x1 & 255) << (8 * (k % 4));
+        p2[k / 4] |= (uint32_t)(x2 & 255) << (8 * (k % 4));
+        p3[k / 4] |= (uint32_t)(x3 & 255) << (8 * (k % 4));
+    }
+    uint4* d1 = reinterpret_cast<uint4*>(planes + (m * 3 + 0) * in + b * 32);
+    uint4* d2 = reinterpret_cast<uint4*>(planes + (m * 3 + 1) * in + b * 32);
+    uint4* d3 = reinterpret_cast<uint4*>(planes + (m * 3 + 2) * in + b * 32);
+    d1[0] = make_uint4(p1[0], p1[1], p1[2], p1[3]); d1[1] = make_uint4(p1[4], p1[5], p1[6], p1[7]);
+    d2[0] = make_uint4(p2[0], p2[1], p2[2], p2[3]); d2[1] = make_uint4(p2[4], p2[5], p2[6], p2[7]);
+    d3[0] = make_uint4(p3[0], p3[1], p3[2], p3[3]); d3[1] = make_uint4(p3[4], p3[5], p3[6], p3[7]);
+    stats[m * (in / 32) + b] = make_float4(sx, sa, sb, 0.0f);
+}
+
+__device__ __forceinline__ void load_block(const float* src, float (&v)[32]) {
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float4 f = reinterpret_cast<const float4*>(src)[k];
+            v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 32; k++) v[k] = src[k];
+    }
+}
+
+// RMSNorm fused into staging: one CTA per row.  y = (x / m) * w with
+// m = sqrt(sum(x^2) / in + eps), the order of candle_nn::ops::rms_norm.
+__global__ void xquant_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                      float eps, int64_t in, int8_t* __restrict__ planes,
+                                      float4* __restrict__ stats) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    __shared__ float wsum[32];
+    const int64_t m = blockIdx.x;
+    const float* row = x + m * in;
+    float s2 = 0.0f;
+    for (int64_t i = threadIdx.x; i < in; i += blockDim.x) s2 = fmaf(row[i], row[i], s2);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = s2;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int k = 0; k < (int)(blockDim.x >> 5); k++) tot += wsum[k];
+    const float mden = sqrtf(tot / (float)in + eps);
+    const int64_t nb = in / 32;
+    for (int64_t b = threadIdx.x; b < nb; b += blockDim.x) {
+        float v[32];
+        load_block(row + b * 32, v);
+#pragma unroll
+        for (int k = 0; k < 32; k++) v[k] = v[k] / mden * w[b * 32 + k];
+        stage_block(v, m, b, in, planes, stats);
+    }
+}
+
+// SwiGLU fused into staging: v = silu(gate) * up, silu(g) = g / (1 + exp(-g)).
+__global__ void xquant_swiglu_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+                                     int64_t M, int64_t in, int8_t* __restrict__ planes,
+                                     float4* __restrict__ stats) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int64_t nb = in / 32;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= M * nb) return;
+    const int64_t m = t / nb, b = t % nb;
+    float g[32], u[32];
+    load_block(gate + m * in + b * 32, g);
+    load_block(up + m * in + b * 32, u);
+#pragma unroll
+    for (int k = 0; k < 32; k++) g[k] = g[k] / (1.0f + expf(-g[k])) * u[k];
+    stage_block(g, m, b, in, planes, stats);
+}
+
 struct XRows {  // activation rows to stage: row m starts at x[m] (or x[0] + m*in)
     const float* x[kMaxJobs];
     int listed;    // 0: rows are consecutive from x[0]
@@ -48,44 +142,8 @@ __global__ void xquant_kernel(XRows rows, int64_t M, int64_t in, int8_t* __restr
     int64_t m = t / nb, b = t % nb;
     const float* src = (rows.listed ? rows.x[m] : rows.x[0] + m * in) + b * 32;
     float v[32];
-    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            float4 f = reinterpret_cast<const float4*>(src)[k];
-            v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 32; k++) v[k] = src[k];
-    }
-    float amax = 0.0f, sa = 0.0f, sb = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 16; k++) { amax = fmaxf(amax, fabsf(v[k])); sa += v[k]; }
-#pragma unroll
-    for (int k = 16; k < 32; k++) { amax = fmaxf(amax, fabsf(v[k])); sb += v[k]; }
-    float inv = amax > 0.0f ? kXQScale / amax : 0.0f;
-    float sx = amax / kXQScale;
-    uint32_t p1[8], p2[8], p3[8];
-#pragma unroll
-    for (int k = 0; k < 8; k++) { p1[k] = 0u; p2[k] = 0u; p3[k] = 0u; }
-#pragma unroll
-    for (int k = 0; k < 32; k++) {
-        int X = __float2int_rn(v[k] * inv);
-        int x3 = (X << 24) >> 24;  // balanced base-256 digits
-        int t1 = (X - x3) >> 8;
-        int x2 = (t1 << 24) >> 24;
-        int x1 = (t1 - x2) >> 8;
-        p1[k / 4] |= (uint32_t)(x1 & 255) << (8 * (k % 4));
-        p2[k / 4] |= (uint32_t)(x2 & 255) << (8 * (k % 4));
-        p3[k / 4] |= (uint32_t)(x3 & 255) << (8 * (k % 4));
-    }
-    uint4* d1 = reinterpret_cast<uint4*>(planes + (m * 3 + 0) * in + b * 32);
-    uint4* d2 = reinterpret_cast<uint4*>(planes + (m * 3 + 1) * in + b * 32);
-    uint4* d3 = reinterpret_cast<uint4*>(planes + (m * 3 + 2) * in + b * 32);
-    d1[0] = make_uint4(p1[0], p1[1], p1[2], p1[3]); d1[1] = make_uint4(p1[4], p1[5], p1[6], p1[7]);
-    d2[0] = make_uint4(p2[0], p2[1], p2[2], p2[3]); d2[1] = make_uint4(p2[4], p2[5], p2[6], p2[7]);
-    d3[0] = make_uint4(p3[0], p3[1], p3[2], p3[3]); d3[1] = make_uint4(p3[4], p3[5], p3[6], p3[7]);
-    stats[t] = make_float4(sx, sa, sb, 0.0f);
+    load_block(src, v);
+    stage_block(v, m, b, in, planes, stats);
 }
 
 // ------------------------------------------------- register-streaming kernels
@@ -264,6 +322,40 @@ int launch_xquant_impl(const XRows& rows, int64_t M, int64_t in, XQ xq, cudaStre
                       "xquant kernel");
 }
 }  // namespace
+
+namespace {
+cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+}  // namespace
+
+int launch_xquant_rmsnorm(const float* x, const float* w, float eps, int64_t M, int64_t in, XQ xq,
+                          cudaStream_t st) {
+    if (M == 0) return RQ_OK;
+    cudaLaunchAttribute attr[1];
+    const int threads = (int)std::min<int64_t>(1024, std::max<int64_t>(32, ((in / 32) + 31) / 32 * 32));
+    cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)M), dim3((unsigned)threads), st, attr);
+    return cuda_error(cudaLaunchKernelEx(&cfg, xquant_rmsnorm_kernel, x, w, eps, in, xq.planes, xq.stats),
+                      "xquant rmsnorm kernel");
+}
+
+int launch_xquant_swiglu(const float* gate, const float* up, int64_t M, int64_t in, XQ xq,
+                         cudaStream_t st) {
+    const int64_t n = M * (in / 32);
+    if (n == 0) return RQ_OK;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)((n + 127) / 128)), dim3(128), st, attr);
+    return cuda_error(cudaLaunchKernelEx(&cfg, xquant_swiglu_kernel, gate, up, M, in, xq.planes, xq.stats),
+                      "xquant swiglu kernel");
+}
 
 int launch_xquant(const float* x, int64_t M, int64_t in, XQ xq, cudaStream_t st) {
     XRows rows{};

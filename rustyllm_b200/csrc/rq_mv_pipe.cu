@@ -280,10 +280,11 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         int64_t rb;
         int nrows;
         job_rows(p.jobs[j], &rb, &nrows);
+        const float* add = p.jobs[j].add;
         for (int t = threadIdx.x; t < nrows; t += blockDim.x) {
             float acc = 0.0f;
             for (int s = 0; s < p.S; s++) acc += red[(roff + t) * p.S + s];
-            p.jobs[j].y[rb + t] = acc;
+            p.jobs[j].y[rb + t] = add ? acc + add[rb + t] : acc;
         }
         roff += nrows;
     }
@@ -333,7 +334,7 @@ bool pipe_supported(const rq_weight* w) {
 }
 
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
-                       int sm_count, cudaStream_t st, int* err) {
+                       int sm_count, cudaStream_t st, int* err, const float* const* adds) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "matvec pipeline: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     TypeInfo ti = type_info(w0->type);
@@ -344,6 +345,7 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
         p.jobs[j].hdr = ws[j]->hdr;
         p.jobs[j].xq = xqs[j];
         p.jobs[j].y = ys[j];
+        p.jobs[j].add = adds ? adds[j] : nullptr;
         p.jobs[j].out = ws[j]->out;
     }
     p.err = err;
