@@ -197,6 +197,67 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+LLAMA70B = dict(hidden=8192, intermediate=28672, n_heads=64, n_kv_heads=8, head_dim=128,
+                n_layers=80, vocab=32000, max_seq=64, max_batch_tokens=32, rms_eps=1e-5,
+                rope_theta=10000.0)
+
+
+def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20) -> dict:
+    """Config 5: the full 80-layer Llama-2-70B shape (Platypus2-70B), random
+    N(0, 0.02) weights quantized to Q4_K and resident on one GPU, F16
+    embedding / lm_head; 20 seeded uniform prompt ids, greedy decode of 16
+    tokens.  Decode steps are device-side and replayed from one CUDA graph."""
+    import torch
+    from rustyllm_b200._lib import check, lib
+    from rustyllm_b200.llama import random_model
+    cfg = LLAMA70B
+    t0 = time.perf_counter()
+    model, _ = random_model(cfg, Q4_K, seed=7070, device=device)
+    build_s = time.perf_counter() - t0
+    prompt = np.random.default_rng(20).integers(0, cfg["vocab"], size=prompt_len).astype(np.int32)
+    L = lib()
+    stream = torch.cuda.Stream(device=device)
+    # warm-up: one prompt pass and one step (kernel attributes), then capture
+    model.forward(prompt, 0)
+    model.decode_step(stream.cuda_stream)
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        model.decode_step(torch.cuda.current_stream().cuda_stream)
+    # timed generate: prompt forward + (new_tokens - 1) graph-replayed steps
+    check(L.rq_llama_reset_tokens(model.handle))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    model.forward(prompt, 0)
+    prefill_s = time.perf_counter() - t0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(new_tokens - 1):
+            g.replay()
+        e1.record(stream)
+    stream.synchronize()
+    gen_s = time.perf_counter() - t0
+    step_ms = e0.elapsed_time(e1) / (new_tokens - 1)
+    toks, pos = model.tokens()
+    del g
+    model.close()
+    torch.cuda.empty_cache()
+    layer_bytes = sum(Q4K_BYTES(i, o) for (o, i) in [(8192, 8192), (1024, 8192), (1024, 8192),
+                                                        (8192, 8192), (28672, 8192), (28672, 8192),
+                                                        (8192, 28672)])
+    tok_bytes = cfg["n_layers"] * layer_bytes + cfg["vocab"] * cfg["hidden"] * 2
+    return {"config": "Llama-2-70B shape, 80 layers, Q4_K resident, F16 lm_head, 1 GPU",
+            "prompt_tokens": prompt_len, "new_tokens": new_tokens,
+            "decode_tok_s": round(1e3 / step_ms, 2), "ms_per_token": round(step_ms, 3),
+            "prefill_ms": round(prefill_s * 1e3, 2),
+            "generate_tok_s": round(new_tokens / gen_s, 2),
+            "weight_bytes_per_token": tok_bytes,
+            "decode_hbm_gbs": round(tok_bytes / (step_ms / 1e3) / 1e9, 1),
+            "tokens": toks[:new_tokens], "final_position": pos,
+            "model_build_s": round(build_s, 2)}
+
+
 def run_gpu(args) -> None:
     import ctypes
 
@@ -350,6 +411,16 @@ def run_gpu(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host = {n: weights[0][k].download() for k, (n, _, _) in enumerate(SHAPES)}
         cpu = cpu_baseline(host, seconds=args.cpu_seconds)
+    dec = None
+    if world == 1 and not args.no_decode:
+        del graphs, shape_graphs, dom
+        graphs = shape_graphs = dom = None
+        for layer in weights:
+            for w in layer:
+                w.free()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        dec = decode_70b(local)
     if rank == 0:
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic_q4k_gate_up.json")
@@ -384,6 +455,8 @@ def run_gpu(args) -> None:
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if dec is not None:
+            line["decode_70b"] = dec
         print(json.dumps(line), flush=True)
     del graphs, shape_graphs, dom
     if pg is not None:
@@ -399,6 +472,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 80-layer 70B decode run")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
