@@ -149,6 +149,26 @@ RQ_API int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const 
 RQ_API int rq_linear_noalloc(const rq_weight* w, const float* x, float* y, int64_t M,
                              void* stream);
 
+/* ------------------------------------------------------------- sparse MoE */
+
+/* Mixtral SparseMoe (src/streaming_mixtral.rs:259-319) with quantized
+ * experts: router weight f32 [E][hidden] (host or device, copied), expert
+ * weights w1 = gate [ffn][hidden], w3 = up [ffn][hidden], w2 = down
+ * [hidden][ffn] (borrowed: they must outlive the layer).  E <= 32. */
+RQ_API int rq_moe_create(rq_ctx* ctx, int n_experts, int top_k, int64_t hidden, int64_t ffn,
+                         const float* router_w, const rq_weight* const* w1,
+                         const rq_weight* const* w3, const rq_weight* const* w2, rq_moe** out);
+RQ_API int rq_moe_free(rq_moe* m);
+/* y[T][hidden] = SparseMoe::forward(x[T][hidden]) (:280-319): router,
+ * softmax, top-k with renormalised weights (ties to the lower expert index),
+ * per-expert token buckets in ascending token order, SwiGLU experts, combine
+ * in ascending expert order.  x, y host or device.  expert_ids_out [T][k]
+ * (rank order) and perm_out [T*k] (tokens of expert 0, then expert 1, ...)
+ * are optional host outputs.  Reads the routing table back to the host
+ * before the expert products (as the reference does, :284-286). */
+RQ_API int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
+                          int32_t* expert_ids_out, int32_t* perm_out, void* stream);
+
 /* -------------------------------------------------------- Llama decode loop */
 
 /* The quantized Llama forward of StreamingLlamaQuantized with every layer

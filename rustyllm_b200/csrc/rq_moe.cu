@@ -1,0 +1,426 @@
+// rq_moe.cu -- Mixtral sparse-MoE layer (SparseMoe::forward,
+// src/streaming_mixtral.rs:280-319) on the GPU with quantized experts.
+//
+//   route:    logits[t][e] = x[t] . router[e] (warp per (t, e), f32 partials
+//             in a fixed lane order so every run and the CPU oracle produce
+//             the same bits), softmax, top-k by descending score with ties to
+//             the lower expert index (the stable sort of :292-294),
+//             weights p / sum(p over the selected, in rank order) (:295-302)
+//   permute:  per expert, the tokens that chose it in ascending token order
+//             (:292-299), by a block-wide prefix scan over token flags
+//   experts:  w2(silu(w1 x) * (w3 x)) (:250-256) as matvec jobs of the
+//             pipelined kernel; each job reads the staged row of its token, so
+//             no gathered copy of x is made
+//   combine:  y[t] = sum over the token's experts in ascending expert order
+//             of weight * out (the index_add order of :306-316)
+// The host reads the per-expert counts after routing (the reference moves
+// the routing table to the host too, :284-286) to build the job list.
+
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "rq_internal.cuh"
+
+struct rq_moe {
+    rq_ctx* ctx;
+    int E, k;
+    int64_t H, F;
+    float* router;  // [E][H]
+    std::vector<const rq_weight*> w1, w3, w2;
+    // per-forward buffers, grown on demand
+    int64_t cap_t = 0;
+    float* logits = nullptr;     // [T][E]
+    int32_t* ids = nullptr;      // [T][k] expert ids in rank order
+    float* wts = nullptr;        // [T][k]
+    int32_t* offs = nullptr;     // [E+1]
+    int32_t* perm = nullptr;     // [T*k] slot -> token (expert-major)
+    float* slot_w = nullptr;     // [T*k]
+    int32_t* tok_slot = nullptr; // [T][k] token -> its slots in ascending expert order
+    float* g = nullptr;          // [T*k][F]
+    float* u = nullptr;
+    float* o = nullptr;          // [T*k][H]
+    float* xd = nullptr;         // [T][H] device copy of host x
+    float* yd = nullptr;
+    uint8_t* xq_x = nullptr;     // staged x rows
+    uint8_t* xq_h = nullptr;     // staged swiglu rows
+    std::vector<void*> bufs;
+};
+
+namespace rq {
+namespace {
+
+// One CTA per token, one warp per expert (E <= 32).
+__global__ void router_kernel(const float* __restrict__ x, const float* __restrict__ wr, int64_t H,
+                              int E, int k, float* __restrict__ logits, int32_t* __restrict__ ids,
+                              float* __restrict__ wts) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    __shared__ float sl[32];
+    const int64_t t = blockIdx.x;
+    const int e = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (e < E) {
+        const float4* xv = reinterpret_cast<const float4*>(x + t * H);
+        const float4* wv = reinterpret_cast<const float4*>(wr + (int64_t)e * H);
+        float acc = 0.0f;
+        for (int64_t i = lane; i < H / 4; i += 32) {  // chunks l, l+32, ... in component order
+            const float4 a = xv[i], b = wv[i];
+            acc = fmaf(a.x, b.x, acc);
+            acc = fmaf(a.y, b.y, acc);
+            acc = fmaf(a.z, b.z, acc);
+            acc = fmaf(a.w, b.w, acc);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) acc = acc + __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) {
+            sl[e] = acc;
+            logits[t * E + e] = acc;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // softmax_last_dim, then the k best by score (ties -> lower index)
+        float mx = sl[0];
+        for (int j = 1; j < E; j++) mx = fmaxf(mx, sl[j]);
+        float p[32], sum = 0.0f;
+        for (int j = 0; j < E; j++) { p[j] = expf(sl[j] - mx); sum += p[j]; }
+        for (int j = 0; j < E; j++) p[j] = p[j] / sum;
+        int pick[32];
+        unsigned used = 0u;
+        for (int r = 0; r < k; r++) {
+            int best = -1;
+            for (int j = 0; j < E; j++)
+                if (!(used >> j & 1u) && (best < 0 || sl[j] > sl[best])) best = j;
+            pick[r] = best;
+            used |= 1u << best;
+        }
+        float s = 0.0f;
+        for (int r = 0; r < k; r++) s += p[pick[r]];
+        for (int r = 0; r < k; r++) {
+            ids[t * k + r] = pick[r];
+            wts[t * k + r] = p[pick[r]] / s;
+        }
+    }
+}
+
+// Single CTA: expert buckets in ascending token order.  offs[E+1];
+// perm[slot] = token; slot_w[slot]; tok_slot[t][r] = the token's slots sorted
+// by expert id.
+__global__ void permute_kernel(const int32_t* __restrict__ ids, const float* __restrict__ wts,
+                               int64_t T, int E, int k, int32_t* __restrict__ offs,
+                               int32_t* __restrict__ perm, float* __restrict__ slot_w,
+                               int32_t* __restrict__ tok_slot) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    __shared__ int cnt[32];
+    __shared__ int base[33];
+    __shared__ int warp_sum[32][32];  // [warp][expert]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    if (tid < 32) cnt[tid] = 0;
+    __syncthreads();
+    // counts
+    for (int64_t t = tid; t < T; t += blockDim.x)
+        for (int r = 0; r < k; r++) atomicAdd(&cnt[ids[t * k + r]], 1);
+    __syncthreads();
+    if (tid == 0) {
+        base[0] = 0;
+        for (int e = 0; e < E; e++) base[e + 1] = base[e] + cnt[e];
+        for (int e = 0; e <= E; e++) offs[e] = base[e];
+    }
+    __syncthreads();
+    // ordered placement, one chunk of blockDim tokens at a time
+    for (int64_t t0 = 0; t0 < T; t0 += blockDim.x) {
+        const int64_t t = t0 + tid;
+        unsigned mask = 0u;  // experts chosen by token t
+        if (t < T)
+            for (int r = 0; r < k; r++) mask |= 1u << ids[t * k + r];
+        // per expert: rank of token t among chosen tokens of this chunk
+        int rank[32];
+        for (int e = 0; e < E; e++) {
+            const unsigned bal = __ballot_sync(0xffffffffu, (mask >> e) & 1u);
+            rank[e] = __popc(bal & ((1u << lane) - 1u));
+            if (lane == 0) warp_sum[warp][e] = __popc(bal);
+        }
+        __syncthreads();
+        for (int e = 0; e < E; e++) {
+            int before = 0;
+            for (int w = 0; w < warp; w++) before += warp_sum[w][e];
+            rank[e] += before;
+        }
+        if (t < T) {
+            int slots[32];
+            for (int r = 0; r < k; r++) {
+                const int e = ids[t * k + r];
+                const int s = base[e] + rank[e];
+                perm[s] = (int32_t)t;
+                slot_w[s] = wts[t * k + r];
+                slots[r] = s;
+            }
+            // ascending expert order == ascending slot order (buckets are expert-major)
+            for (int a = 1; a < k; a++)
+                for (int b = a; b > 0 && slots[b - 1] > slots[b]; b--) {
+                    const int tmp = slots[b];
+                    slots[b] = slots[b - 1];
+                    slots[b - 1] = tmp;
+                }
+            for (int r = 0; r < k; r++) tok_slot[t * k + r] = slots[r];
+        }
+        __syncthreads();
+        if (tid < 32 && tid < E) {
+            int tot = 0;
+            for (int w = 0; w < nw; w++) tot += warp_sum[w][tid];
+            base[tid] += tot;
+        }
+        __syncthreads();
+    }
+}
+
+// y[t][c] = sum_r slot_w[s_r] * o[s_r][c], slots in ascending expert order,
+// starting from zero (ys.zeros_like then index_add per expert).
+__global__ void combine_kernel(const float* __restrict__ o, const float* __restrict__ slot_w,
+                               const int32_t* __restrict__ tok_slot, int64_t T, int k, int64_t H,
+                               float* __restrict__ y) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int64_t t = blockIdx.y;
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < H; c += (int64_t)gridDim.x * blockDim.x) {
+        float acc = 0.0f;
+        for (int r = 0; r < k; r++) {
+            const int s = tok_slot[t * k + r];
+            acc = acc + o[(int64_t)s * H + c] * slot_w[s];
+        }
+        y[t * H + c] = acc;
+    }
+}
+
+cudaLaunchConfig_t pdl(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+template <typename T>
+int grow(rq_moe* m, T** p, size_t n) {
+    cudaError_t e = cudaMalloc((void**)p, std::max<size_t>(n, 1) * sizeof(T));
+    if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(moe)");
+    m->bufs.push_back((void*)*p);
+    return RQ_OK;
+}
+
+int ensure_cap(rq_moe* m, int64_t T) {
+    if (T <= m->cap_t) return RQ_OK;
+    for (void* p : m->bufs) cudaFree(p);
+    m->bufs.clear();
+    const int64_t S = T * m->k;
+    int rc = RQ_OK;
+    if (!rc) rc = grow(m, &m->logits, (size_t)(T * m->E));
+    if (!rc) rc = grow(m, &m->ids, (size_t)S);
+    if (!rc) rc = grow(m, &m->wts, (size_t)S);
+    if (!rc) rc = grow(m, &m->offs, (size_t)(m->E + 1));
+    if (!rc) rc = grow(m, &m->perm, (size_t)S);
+    if (!rc) rc = grow(m, &m->slot_w, (size_t)S);
+    if (!rc) rc = grow(m, &m->tok_slot, (size_t)S);
+    if (!rc) rc = grow(m, &m->g, (size_t)(S * m->F));
+    if (!rc) rc = grow(m, &m->u, (size_t)(S * m->F));
+    if (!rc) rc = grow(m, &m->o, (size_t)(S * m->H));
+    if (!rc) rc = grow(m, &m->xd, (size_t)(T * m->H));
+    if (!rc) rc = grow(m, &m->yd, (size_t)(T * m->H));
+    if (!rc) rc = grow(m, &m->xq_x, xq_bytes(T, m->H));
+    if (!rc) rc = grow(m, &m->xq_h, xq_bytes(S, m->F));
+    m->cap_t = rc ? 0 : T;
+    return rc;
+}
+
+XQ xq_view(uint8_t* base, int64_t rows, int64_t in) {
+    XQ q;
+    q.planes = (int8_t*)base;
+    q.stats = (float4*)(base + (((size_t)rows * 3 * in + 255) & ~(size_t)255));
+    return q;
+}
+
+// jobs y_j = xq row r_j * W_j^T, batched kMaxJobs per launch (same in)
+struct JobList {
+    std::vector<const rq_weight*> w;
+    std::vector<XQ> x;
+    std::vector<float*> y;
+};
+
+int run_jobs(const JobList& J, int sm, cudaStream_t st) {
+    for (size_t b = 0; b < J.w.size(); b += kMaxJobs) {
+        const int n = (int)std::min<size_t>(kMaxJobs, J.w.size() - b);
+        int rc;
+        if (pipe_supported(J.w[b])) {
+            rc = launch_matvec_pipe(&J.w[b], &J.x[b], &J.y[b], n, sm, st);
+        } else {
+            rc = RQ_OK;
+            for (int j = 0; j < n && !rc; j++) rc = launch_linear(J.w[b + j], J.x[b + j], J.y[b + j], 1, sm, st);
+        }
+        if (rc) return rc;
+    }
+    return RQ_OK;
+}
+
+bool is_device(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+struct Guard {
+    int prev = -1;
+    explicit Guard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~Guard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+}  // namespace rq
+
+using namespace rq;
+
+extern "C" {
+
+int rq_moe_create(rq_ctx* ctx, int n_experts, int top_k, int64_t hidden, int64_t ffn,
+                  const float* router_w, const rq_weight* const* w1, const rq_weight* const* w3,
+                  const rq_weight* const* w2, rq_moe** out) {
+    if (!ctx || !router_w || !w1 || !w3 || !w2 || !out)
+        return set_error(RQ_ERR_INVALID, "rq_moe_create: NULL argument");
+    *out = nullptr;
+    if (n_experts < 1 || n_experts > 32 || top_k < 1 || top_k > n_experts)
+        return set_error(RQ_ERR_INVALID, "rq_moe_create: need 1 <= top_k <= n_experts <= 32");
+    if (hidden <= 0 || ffn <= 0 || hidden % 32 || ffn % 32)
+        return set_error(RQ_ERR_INVALID, "rq_moe_create: hidden and ffn must be positive multiples of 32");
+    for (int e = 0; e < n_experts; e++) {
+        if (!w1[e] || !w3[e] || !w2[e]) return set_error(RQ_ERR_INVALID, "rq_moe_create: expert %d missing", e);
+        if (w1[e]->out != ffn || w1[e]->in != hidden || w3[e]->out != ffn || w3[e]->in != hidden ||
+            w2[e]->out != hidden || w2[e]->in != ffn)
+            return set_error(RQ_ERR_INVALID, "rq_moe_create: expert %d shapes must be w1,w3 [%lld,%lld], w2 [%lld,%lld]",
+                             e, (long long)ffn, (long long)hidden, (long long)hidden, (long long)ffn);
+        if (w1[e]->type != w1[0]->type || w3[e]->type != w1[0]->type || w2[e]->type != w2[0]->type)
+            return set_error(RQ_ERR_INVALID, "rq_moe_create: experts must share weight types");
+    }
+    Guard g(ctx->device);
+    rq_moe* m = new (std::nothrow) rq_moe();
+    if (!m) return set_error(RQ_ERR_OOM, "host allocation failed");
+    m->ctx = ctx;
+    m->E = n_experts;
+    m->k = top_k;
+    m->H = hidden;
+    m->F = ffn;
+    m->w1.assign(w1, w1 + n_experts);
+    m->w3.assign(w3, w3 + n_experts);
+    m->w2.assign(w2, w2 + n_experts);
+    cudaError_t e = cudaMalloc(&m->router, sizeof(float) * (size_t)(n_experts * hidden));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(m->router, router_w, sizeof(float) * (size_t)(n_experts * hidden),
+                       is_device(router_w) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        if (m->router) cudaFree(m->router);
+        delete m;
+        return cuda_error(e, "rq_moe_create router copy");
+    }
+    *out = m;
+    return RQ_OK;
+}
+
+int rq_moe_free(rq_moe* m) {
+    if (!m) return RQ_OK;
+    Guard g(m->ctx->device);
+    for (void* p : m->bufs) cudaFree(p);
+    cudaFree(m->router);
+    delete m;
+    return RQ_OK;
+}
+
+int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
+                   int32_t* expert_ids_out, int32_t* perm_out, void* stream) {
+    if (!ctx || !m || !x || !y) return set_error(RQ_ERR_INVALID, "rq_moe_forward: NULL argument");
+    if (T < 0) return set_error(RQ_ERR_INVALID, "rq_moe_forward: T = %lld", (long long)T);
+    if (T == 0) return RQ_OK;
+    Guard gd(m->ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = ensure_cap(m, T);
+    if (rc) return rc;
+    const int E = m->E, k = m->k;
+    const int64_t H = m->H, F = m->F, S = T * k;
+    const bool x_dev = is_device(x), y_dev = is_device(y);
+    const float* xs = x;
+    if (!x_dev || (reinterpret_cast<uintptr_t>(x) & 15)) {
+        rc = cuda_error(cudaMemcpyAsync(m->xd, x, sizeof(float) * (size_t)(T * H), cudaMemcpyDefault, st), "x copy");
+        if (rc) return rc;
+        xs = m->xd;
+    }
+    float* yd = y_dev ? y : m->yd;
+    const int sm = m->ctx->sm_count;
+    XQ xqx = xq_view(m->xq_x, T, H);
+    rc = launch_xquant(xs, T, H, xqx, st);
+    cudaLaunchAttribute attr[1];
+    if (!rc) {
+        cudaLaunchConfig_t cfg = pdl(dim3((unsigned)T), dim3((unsigned)(32 * E)), st, attr);
+        rc = cuda_error(cudaLaunchKernelEx(&cfg, router_kernel, xs, (const float*)m->router, H, E, k,
+                                           m->logits, m->ids, m->wts), "router kernel");
+    }
+    if (!rc) {
+        cudaLaunchConfig_t cfg = pdl(dim3(1), dim3(1024), st, attr);
+        rc = cuda_error(cudaLaunchKernelEx(&cfg, permute_kernel, (const int32_t*)m->ids, (const float*)m->wts, T,
+                                           E, k, m->offs, m->perm, m->slot_w, m->tok_slot), "permute kernel");
+    }
+    std::vector<int32_t> offs((size_t)E + 1), perm((size_t)S);
+    if (!rc) rc = cuda_error(cudaMemcpyAsync(offs.data(), m->offs, sizeof(int32_t) * (size_t)(E + 1),
+                                             cudaMemcpyDeviceToHost, st), "offsets copy");
+    if (!rc) rc = cuda_error(cudaMemcpyAsync(perm.data(), m->perm, sizeof(int32_t) * (size_t)S,
+                                             cudaMemcpyDeviceToHost, st), "perm copy");
+    if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "routing sync");
+    if (rc) return rc;
+    // gate and up products: one job per (expert, token) slot
+    JobList up;
+    for (int e = 0; e < E; e++)
+        for (int32_t s = offs[(size_t)e]; s < offs[(size_t)e + 1]; s++) {
+            const int64_t t = perm[(size_t)s];
+            const XQ xr{xqx.planes + t * 3 * H, xqx.stats + t * (H / 32)};
+            up.w.push_back(m->w1[(size_t)e]); up.x.push_back(xr); up.y.push_back(m->g + (int64_t)s * F);
+            up.w.push_back(m->w3[(size_t)e]); up.x.push_back(xr); up.y.push_back(m->u + (int64_t)s * F);
+        }
+    rc = run_jobs(up, sm, st);
+    XQ xqh = xq_view(m->xq_h, S, F);
+    if (!rc) rc = launch_xquant_swiglu(m->g, m->u, S, F, xqh, st);
+    if (rc) return rc;
+    JobList down;
+    for (int e = 0; e < E; e++)
+        for (int32_t s = offs[(size_t)e]; s < offs[(size_t)e + 1]; s++) {
+            down.w.push_back(m->w2[(size_t)e]);
+            down.x.push_back(XQ{xqh.planes + (int64_t)s * 3 * F, xqh.stats + (int64_t)s * (F / 32)});
+            down.y.push_back(m->o + (int64_t)s * H);
+        }
+    rc = run_jobs(down, sm, st);
+    if (!rc) {
+        cudaLaunchConfig_t cfg = pdl(dim3((unsigned)std::min<int64_t>(64, (H + 255) / 256), (unsigned)T), dim3(256), st, attr);
+        rc = cuda_error(cudaLaunchKernelEx(&cfg, combine_kernel, (const float*)m->o, (const float*)m->slot_w,
+                                           (const int32_t*)m->tok_slot, T, k, H, yd), "combine kernel");
+    }
+    if (!rc && !y_dev)
+        rc = cuda_error(cudaMemcpyAsync(y, yd, sizeof(float) * (size_t)(T * H), cudaMemcpyDeviceToHost, st), "y copy");
+    if (!rc && expert_ids_out)
+        rc = cuda_error(cudaMemcpyAsync(expert_ids_out, m->ids, sizeof(int32_t) * (size_t)S, cudaMemcpyDefault, st),
+                        "ids copy");
+    if (!rc && perm_out) memcpy(perm_out, perm.data(), sizeof(int32_t) * (size_t)S);
+    if (!rc && (!y_dev || expert_ids_out)) rc = cuda_error(cudaStreamSynchronize(st), "moe sync");
+    return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,74 @@
+"""Host-side mirror of Mixtral's SparseMoe (src/streaming_mixtral.rs:259-319)
+over librq's rq_moe_* entry points, with quantized experts.
+
+``SparseMoe(router_w, experts, top_k).forward(xs)`` takes xs [..., hidden]
+(numpy or torch) and returns the mixed expert outputs of the same shape;
+``forward_with_routing`` also returns the expert ids [T, k] and the
+permutation (tokens of expert 0, expert 1, ...).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import check
+from .linear import Context, QWeight
+
+try:
+    import torch
+except Exception:  # pragma: no cover
+    torch = None
+
+
+class SparseMoe:
+    def __init__(self, router_w, experts: list, top_k: int = 2, device: int = 0):
+        """experts: [(w1 gate, w2 down, w3 up) QWeight triples], as Expert."""
+        self.ctx = Context.get(device)
+        r = np.ascontiguousarray(router_w, dtype=np.float32)
+        E, H = r.shape
+        F = experts[0][0].out
+        arr = lambda ws: (ctypes.c_void_p * E)(*[w.handle.value for w in ws])  # noqa: E731
+        h = ctypes.c_void_p()
+        check(_lib.lib().rq_moe_create(self.ctx.handle, E, top_k, H, F, r.ctypes.data,
+                                       arr([e[0] for e in experts]), arr([e[2] for e in experts]),
+                                       arr([e[1] for e in experts]), ctypes.byref(h)))
+        self.handle, self.E, self.k, self.H, self.F = h, E, top_k, H, F
+        self._keep = experts
+
+    def forward_with_routing(self, xs):
+        torch_in = torch is not None and isinstance(xs, torch.Tensor)
+        shape = tuple(xs.shape)
+        if torch_in:
+            x2 = xs.reshape(-1, self.H).float().contiguous()
+            T = x2.shape[0]
+            y = torch.empty_like(x2)
+            xp, yp = x2.data_ptr(), y.data_ptr()
+            stream = torch.cuda.current_stream(x2.device).cuda_stream if x2.is_cuda else 0
+        else:
+            x2 = np.ascontiguousarray(np.asarray(xs, dtype=np.float32).reshape(-1, self.H))
+            T = x2.shape[0]
+            y = np.empty_like(x2)
+            xp, yp, stream = x2.ctypes.data, y.ctypes.data, 0
+        ids = np.empty((T, self.k), dtype=np.int32)
+        perm = np.empty(T * self.k, dtype=np.int32)
+        check(_lib.lib().rq_moe_forward(self.ctx.handle, self.handle, xp, yp, T, ids.ctypes.data,
+                                        perm.ctypes.data, stream))
+        return y.reshape(shape), ids, perm
+
+    def forward(self, xs):
+        return self.forward_with_routing(xs)[0]
+
+    __call__ = forward
+
+    def close(self):
+        if self.handle:
+            _lib.lib().rq_moe_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
