@@ -202,23 +202,30 @@ LLAMA70B = dict(hidden=8192, intermediate=28672, n_heads=64, n_kv_heads=8, head_
                 rope_theta=10000.0)
 
 
-def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20) -> dict:
+def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None) -> dict:
     """Config 5: the full 80-layer Llama-2-70B shape (Platypus2-70B), random
-    N(0, 0.02) weights quantized to Q4_K and resident on one GPU, F16
+    N(0, 0.02) weights quantized to Q4_K and resident on the GPUs, F16
     embedding / lm_head; 20 seeded uniform prompt ids, greedy decode of 16
-    tokens.  Decode steps are device-side and replayed from one CUDA graph."""
+    tokens.  Decode steps are device-side and replayed from one CUDA graph.
+    Under torch.distributed the model is tensor-parallel over the ranks
+    (column/row-parallel linears joined by NCCL all-reduces over NVLink)."""
     import torch
+    from rustyllm_b200 import Context
     from rustyllm_b200._lib import check, lib
     from rustyllm_b200.llama import random_model
     cfg = LLAMA70B
+    world, rank = 1, 0
+    if pg is not None:
+        from rustyllm_b200 import tp as tpmod
+        world, rank = tpmod.init_from_torch(Context.get(device))
     t0 = time.perf_counter()
-    model, _ = random_model(cfg, Q4_K, seed=7070, device=device)
+    model, _ = random_model(cfg, Q4_K, seed=7070, device=device, tp=(world, rank))
     build_s = time.perf_counter() - t0
     prompt = np.random.default_rng(20).integers(0, cfg["vocab"], size=prompt_len).astype(np.int32)
     L = lib()
     stream = torch.cuda.Stream(device=device)
     # warm-up: one prompt pass and one step (kernel attributes), then capture
-    model.forward(prompt, 0)
+    model.forward(prompt, 0, want_logits=False)
     model.decode_step(stream.cuda_stream)
     stream.synchronize()
     g = torch.cuda.CUDAGraph()
@@ -228,7 +235,7 @@ def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20) -> dict:
     check(L.rq_llama_reset_tokens(model.handle))
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    model.forward(prompt, 0)
+    model.forward(prompt, 0, want_logits=False)
     prefill_s = time.perf_counter() - t0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -239,15 +246,24 @@ def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20) -> dict:
     stream.synchronize()
     gen_s = time.perf_counter() - t0
     step_ms = e0.elapsed_time(e1) / (new_tokens - 1)
+    if pg is not None:  # the slowest rank sets the pace
+        t = torch.tensor([step_ms, gen_s, prefill_s], device=f"cuda:{device}")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        step_ms, gen_s, prefill_s = (float(v) for v in t.tolist())
     toks, pos = model.tokens()
     del g
     model.close()
+    if pg is not None:
+        from rustyllm_b200 import tp as tpmod
+        tpmod.finalize(Context.get(device))
     torch.cuda.empty_cache()
     layer_bytes = sum(Q4K_BYTES(i, o) for (o, i) in [(8192, 8192), (1024, 8192), (1024, 8192),
                                                         (8192, 8192), (28672, 8192), (28672, 8192),
                                                         (8192, 28672)])
     tok_bytes = cfg["n_layers"] * layer_bytes + cfg["vocab"] * cfg["hidden"] * 2
-    return {"config": "Llama-2-70B shape, 80 layers, Q4_K resident, F16 lm_head, 1 GPU",
+    return {"config": f"Llama-2-70B shape, 80 layers, Q4_K resident, F16 lm_head, "
+                      f"tensor-parallel over {world} GPU(s)",
+            "tp": world,
             "prompt_tokens": prompt_len, "new_tokens": new_tokens,
             "decode_tok_s": round(1e3 / step_ms, 2), "ms_per_token": round(step_ms, 3),
             "prefill_ms": round(prefill_s * 1e3, 2),
@@ -412,7 +428,7 @@ def run_gpu(args) -> None:
         host = {n: weights[0][k].download() for k, (n, _, _) in enumerate(SHAPES)}
         cpu = cpu_baseline(host, seconds=args.cpu_seconds)
     dec = None
-    if world == 1 and not args.no_decode:
+    if not args.no_decode:
         del graphs, shape_graphs, dom
         graphs = shape_graphs = dom = None
         for layer in weights:
@@ -420,7 +436,7 @@ def run_gpu(args) -> None:
                 w.free()
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
-        dec = decode_70b(local)
+        dec = decode_70b(local, pg=pg)
     if rank == 0:
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic_q4k_gate_up.json")

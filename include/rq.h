@@ -149,6 +149,23 @@ RQ_API int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const 
 RQ_API int rq_linear_noalloc(const rq_weight* w, const float* x, float* y, int64_t M,
                              void* stream);
 
+/* -------------------------------------------------------- tensor parallel */
+
+/* One process per GPU.  Rank 0 creates an id (rq_tp_unique_id, >= 128
+ * bytes), the host side distributes it (e.g. over torch.distributed), and
+ * every rank calls rq_tp_init on its context.  Initialisation is bounded by
+ * timeout_ms: a rank that never joins yields RQ_ERR_TIMEOUT on the others
+ * (the communicator is aborted), never a hang.  No reference counterpart:
+ * the reference is single-device (the build's TP splits the QAttn / QMlp
+ * linears column- and row-parallel and joins them with all-reduces). */
+RQ_API int rq_tp_unique_id(void* id_out, size_t n);
+RQ_API int rq_tp_init(rq_ctx* ctx, int world, int rank, const void* id, int timeout_ms);
+/* out[n] = sum over ranks of in[n] (f32), asynchronous on stream. */
+RQ_API int rq_tp_allreduce_f32(rq_ctx* ctx, const float* in, float* out, int64_t n, void* stream);
+/* RQ_OK while the communicator is healthy, RQ_ERR_NCCL after an async error. */
+RQ_API int rq_tp_status(rq_ctx* ctx);
+RQ_API int rq_tp_finalize(rq_ctx* ctx);
+
 /* ------------------------------------------------------------- sparse MoE */
 
 /* Mixtral SparseMoe (src/streaming_mixtral.rs:259-319) with quantized
@@ -175,7 +192,11 @@ RQ_API int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int6
  * resident on the GPU (src/streaming_quantized.rs:611-729, QBlock
  * :282-318), a per-layer f32 KV cache (QuantStreamCache :93-152) and the
  * greedy step of generate (:539-593).  Config mirrors candle's llama Config
- * fields the block uses. */
+ * fields the block uses (global sizes).  With a tensor-parallel communicator
+ * on the context (world W, rank r), each rank holds shard r of every layer:
+ * q/k/v/gate/up rows (heads r*n_heads/W.., kv heads r*n_kv_heads/W..,
+ * intermediate rows r*intermediate/W..), the matching o/down columns, and
+ * lm_head rows r*vocab/W..; the embedding and norms are replicated. */
 typedef struct rq_llama rq_llama;
 typedef struct rq_llama_config {
     int64_t hidden, intermediate, n_heads, n_kv_heads, head_dim, n_layers, vocab;
@@ -186,19 +207,20 @@ typedef struct rq_llama_config {
 
 RQ_API int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out);
 RQ_API int rq_llama_free(rq_llama* m);
-/* Layer weights q,k,v,o,gate,up,down (borrowed: they must outlive m) and the
- * two RmsNorm weights (f32 [hidden], host or device, copied).  Replaces
- * QBlock::load (src/streaming_quantized.rs:290-303). */
+/* Layer weights q,k,v,o,gate,up,down (this rank's shards; borrowed: they
+ * must outlive m) and the two RmsNorm weights (f32 [hidden], host or device,
+ * copied).  Replaces QBlock::load (src/streaming_quantized.rs:290-303). */
 RQ_API int rq_llama_set_layer(rq_llama* m, int64_t layer, const rq_weight* const* w7,
                               const float* rms1, const float* rms2);
 /* F16 [vocab][hidden] token embedding (model.embed_tokens.weight). */
 RQ_API int rq_llama_set_embedding(rq_llama* m, const uint16_t* embed_f16);
-/* Final RmsNorm weight (f32 [hidden]) and F16 [vocab][hidden] lm_head. */
+/* Final RmsNorm weight (f32 [hidden]) and F16 lm_head rows of this rank
+ * ([vocab/W][hidden]). */
 RQ_API int rq_llama_set_head(rq_llama* m, const float* ln_f, const uint16_t* lm_head_f16);
 /* forward(input_ids, index_pos) of src/streaming_quantized.rs:622-633 over T
  * host tokens at positions index_pos..index_pos+T-1: logits (host or device
- * [vocab], may be NULL) of the last position and the greedy next token (may
- * be NULL).  Synchronous.  Leaves the next token and position on the device
+ * [vocab], may be NULL; single rank only) of the last position and the
+ * greedy next token (may be NULL).  Synchronous.  Leaves the next token and position on the device
  * for rq_llama_decode_step. */
 RQ_API int rq_llama_forward(rq_llama* m, const int32_t* tokens, int64_t T, int64_t index_pos,
                             float* logits, int32_t* next_token, void* stream);

@@ -73,6 +73,11 @@ SIGNATURES.update({
     "rq_llama_tokens": (I, [P, P, I64, ctypes.POINTER(I64), ctypes.POINTER(I64)]),
     "rq_llama_reset_tokens": (I, [P]),
     "rq_llama_truncate": (I, [P, I64]),
+    "rq_tp_unique_id": (I, [P, SZ]),
+    "rq_tp_init": (I, [P, I, I, P, I]),
+    "rq_tp_allreduce_f32": (I, [P, P, P, I64, P]),
+    "rq_tp_status": (I, [P]),
+    "rq_tp_finalize": (I, [P]),
     "rq_moe_create": (I, [P, I, I, I64, I64, P, PP, PP, PP, PP]),
     "rq_moe_free": (I, [P]),
     "rq_moe_forward": (I, [P, P, P, P, I64, P, P, P]),

@@ -180,6 +180,7 @@ int rq_init(int device, rq_ctx** out) {
                          device, prop.major, prop.minor);
     rq_ctx* c = new (std::nothrow) rq_ctx();
     if (!c) return set_error(RQ_ERR_OOM, "host allocation failed");
+    c->tp = nullptr;
     c->device = device;
     c->own_stream = nullptr;
     c->ws = nullptr;
@@ -192,6 +193,7 @@ int rq_init(int device, rq_ctx** out) {
 int rq_destroy(rq_ctx* ctx) {
     if (!ctx) return RQ_OK;
     DeviceGuard g(ctx->device);
+    tp_destroy(ctx);
     if (ctx->ws) cudaFree(ctx->ws);
     delete ctx;
     return RQ_OK;

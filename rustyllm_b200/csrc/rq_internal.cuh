@@ -74,7 +74,12 @@ struct rq_weight {
     int device;
 };
 
+namespace rq {
+struct TPComm;
+}
+
 struct rq_ctx {
+    rq::TPComm* tp;  // tensor-parallel communicator (rq_tp_init), or NULL
     int device;
     cudaStream_t own_stream;  // used for host-pointer calls when stream == NULL
     void* ws;                 // workspace (activation staging, host-path buffers)
@@ -83,6 +88,13 @@ struct rq_ctx {
 };
 
 namespace rq {
+
+// tensor parallel (rq_tp.cu): world/rank are 1/0 without a communicator;
+// dtype 0 = f32, 1 = u64; op 0 = sum, 1 = max
+int tp_world(const rq_ctx* ctx);
+int tp_rank(const rq_ctx* ctx);
+int tp_allreduce(rq_ctx* ctx, const void* in, void* out, int64_t n, int dtype, int op, cudaStream_t st);
+void tp_destroy(rq_ctx* ctx);
 
 // error handling (rq_api.cu)
 int set_error(int code, const char* fmt, ...);

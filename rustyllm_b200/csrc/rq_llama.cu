@@ -53,7 +53,10 @@ struct rq_llama {
     float* g;     // [Tmax][intermediate]
     float* u;
     float* hf;    // [hidden] final normed row
-    float* logits;  // [vocab]
+    float* logits;  // [vocab / W]
+    float* part;    // [Tmax][hidden] row-parallel partial sums (W > 1)
+    int W, R;       // tensor-parallel world and rank
+    int64_t nh_l, nkv_l, I_l, vocab_l;  // this rank's heads, kv heads, ffn rows, vocab rows
     rq::XQ xq;      // Tmax rows of max(hidden, intermediate)
     // device state
     unsigned long long* best;  // packed (value, -index) of the argmax
@@ -209,11 +212,12 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 }
 
 // logits[r] = sum_k hf[k] * f32(W[r][k]) over an F16 [vocab][hidden] matrix,
-// one warp per row, 16-byte streaming loads; the block's best (value, row)
-// is folded into *best with one atomicMax.  hidden % 8 == 0.
+// one warp per row, 16-byte streaming loads; the block's best (value, row +
+// row_offset) is folded into *best with one atomicMax.  hidden % 8 == 0.
 __global__ void __launch_bounds__(256) lm_head_kernel(const __half* __restrict__ W,
                                                       const float* __restrict__ hf, int64_t vocab,
-                                                      int64_t hidden, float* __restrict__ logits,
+                                                      int64_t hidden, int64_t row_offset,
+                                                      float* __restrict__ logits,
                                                       unsigned long long* __restrict__ best) {
     extern __shared__ float xs[];
     pdl_enter();
@@ -244,7 +248,7 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const __half* __restrict__
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if (lane == 0) {
             if (logits) logits[r] = acc;
-            const unsigned long long key = argmax_key(acc, (uint32_t)r);
+            const unsigned long long key = argmax_key(acc, (uint32_t)(r + row_offset));
             mykey = key > mykey ? key : mykey;
         }
     }
@@ -332,10 +336,29 @@ int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float
     return RQ_OK;
 }
 
+// x = x + x_in W^T for a row-parallel weight (o_proj, down_proj).  One rank:
+// the residual add is fused into the matvec epilogue.  W ranks: each rank's
+// partial product (rank 0 also adds the residual) is summed into x by an
+// all-reduce.
+int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
+    if (m->W == 1) {
+        const rq_weight* w1[1] = {w};
+        float* y1[1] = {m->x};
+        const float* a1[1] = {m->x};
+        return run_linears(m, 1, w1, T, y1, a1, st);
+    }
+    const rq_weight* w1[1] = {w};
+    float* y1[1] = {m->part};
+    const float* a1[1] = {m->R == 0 ? m->x : nullptr};
+    int rc = run_linears(m, 1, w1, T, y1, a1, st);
+    if (!rc) rc = tp_allreduce(m->ctx, m->part, m->x, T * m->cfg.hidden, 0, 0, st);
+    return rc;
+}
+
 // One forward over the T tokens in m->tokens at device position *m->pos.
 int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
     const rq_llama_config& c = m->cfg;
-    const int64_t H = c.hidden, I = c.intermediate, nq = c.n_heads * c.head_dim, nk = c.n_kv_heads * c.head_dim;
+    const int64_t H = c.hidden, I = m->I_l, nq = m->nh_l * c.head_dim, nk = m->nkv_l * c.head_dim;
     int rc;
     {
         const __half* emb = m->embed;
@@ -366,7 +389,7 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
             const float* cs = m->rope_cos;
             const float* sn = m->rope_sin;
             const int32_t* pos = m->pos;
-            int nh = (int)c.n_heads, nkv = (int)c.n_kv_heads, hd = (int)c.head_dim, ms = (int)c.max_seq;
+            int nh = (int)m->nh_l, nkv = (int)m->nkv_l, hd = (int)c.head_dim, ms = (int)c.max_seq;
             void* args[] = {&q, &k, &v, &kc, &vc, &cs, &sn, &pos, &nh, &nkv, &hd, &ms};
             rc = launch_simple((const void*)rope_append_kernel, dim3((unsigned)(nh + nkv), (unsigned)T),
                                dim3((unsigned)std::max(32, hd / 2)), 0, st, args, "rope kernel");
@@ -380,13 +403,8 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
         }
         rc = launch_xquant(m->att, T, nq, m->xq, st);
         if (rc) return rc;
-        {
-            const rq_weight* w1[1] = {L.w[3]};
-            float* y1[1] = {m->x};
-            const float* a1[1] = {m->x};
-            rc = run_linears(m, 1, w1, T, y1, a1, st);
-            if (rc) return rc;
-        }
+        rc = row_parallel(m, L.w[3], T, st);
+        if (rc) return rc;
         rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
         if (rc) return rc;
         {
@@ -397,13 +415,8 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
         }
         rc = launch_xquant_swiglu(m->g, m->u, T, I, m->xq, st);
         if (rc) return rc;
-        {
-            const rq_weight* w1[1] = {L.w[6]};
-            float* y1[1] = {m->x};
-            const float* a1[1] = {m->x};
-            rc = run_linears(m, 1, w1, T, y1, a1, st);
-            if (rc) return rc;
-        }
+        rc = row_parallel(m, L.w[6], T, st);
+        if (rc) return rc;
     }
     (void)nk;
     {
@@ -419,14 +432,18 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
     {
         const __half* W = m->lm_head;
         const float* hf = m->hf;
-        int64_t vocab = c.vocab, hidden = H;
+        int64_t vocab = m->vocab_l, hidden = H, roff = (int64_t)m->R * m->vocab_l;
         float* lg = want_logits ? m->logits : nullptr;
         unsigned long long* best = m->best;
-        void* args[] = {&W, &hf, &vocab, &hidden, &lg, &best};
+        void* args[] = {&W, &hf, &vocab, &hidden, &roff, &lg, &best};
         const unsigned grid = (unsigned)std::min<int64_t>((vocab + 7) / 8, (int64_t)m->ctx->sm_count * 8);
         rc = launch_simple((const void*)lm_head_kernel, dim3(grid), dim3(256), (size_t)H * sizeof(float), st,
                            args, "lm_head kernel");
         if (rc) return rc;
+        if (m->W > 1) {  // global argmax: max of the packed (value, index) keys
+            rc = tp_allreduce(m->ctx, m->best, m->best, 1, 1, 1, st);
+            if (rc) return rc;
+        }
     }
     {
         unsigned long long* best = m->best;
@@ -492,14 +509,25 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
                          "hidden, intermediate, n_heads*head_dim multiples of 256");
     if (c.max_seq * (int64_t)sizeof(float) > 200 * 1024)
         return set_error(RQ_ERR_INVALID, "rq_llama_create: max_seq %lld too large for attention", (long long)c.max_seq);
+    const int W = tp_world(ctx), R = tp_rank(ctx);
+    if (c.n_kv_heads % W || c.intermediate % (256 * W) || (c.n_heads / W * c.head_dim) % 256 || c.vocab % W)
+        return set_error(RQ_ERR_INVALID,
+                         "rq_llama_create: %d-way tensor parallelism needs n_kv_heads %% W == 0, "
+                         "intermediate/W and n_heads/W*head_dim multiples of 256, vocab %% W == 0", W);
     Guard g(ctx->device);
     rq_llama* m = new (std::nothrow) rq_llama();
     if (!m) return set_error(RQ_ERR_OOM, "host allocation failed");
     m->ctx = ctx;
     m->cfg = c;
+    m->W = W;
+    m->R = R;
+    m->nh_l = c.n_heads / W;
+    m->nkv_l = c.n_kv_heads / W;
+    m->I_l = c.intermediate / W;
+    m->vocab_l = c.vocab / W;
     m->layers.resize((size_t)c.n_layers);
-    const int64_t T = c.max_batch_tokens, H = c.hidden, I = c.intermediate;
-    const int64_t nq = c.n_heads * c.head_dim, nk = c.n_kv_heads * c.head_dim, half = c.head_dim / 2;
+    const int64_t T = c.max_batch_tokens, H = c.hidden, I = m->I_l;
+    const int64_t nq = m->nh_l * c.head_dim, nk = m->nkv_l * c.head_dim, half = c.head_dim / 2;
     const int64_t maxin = std::max(std::max(H, I), nq);
     int rc = RQ_OK;
     for (auto& L : m->layers) {
@@ -511,7 +539,7 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     }
     if (!rc) rc = dalloc(m, &m->embed, (size_t)(c.vocab * H));
     if (!rc) rc = dalloc(m, &m->ln_f, (size_t)H);
-    if (!rc) rc = dalloc(m, &m->lm_head, (size_t)(c.vocab * H));
+    if (!rc) rc = dalloc(m, &m->lm_head, (size_t)(m->vocab_l * H));
     if (!rc) rc = dalloc(m, &m->rope_cos, (size_t)(c.max_seq * half));
     if (!rc) rc = dalloc(m, &m->rope_sin, (size_t)(c.max_seq * half));
     if (!rc) rc = dalloc(m, &m->x, (size_t)(T * H));
@@ -522,7 +550,8 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     if (!rc) rc = dalloc(m, &m->g, (size_t)(T * std::max(I, H)));
     if (!rc) rc = dalloc(m, &m->u, (size_t)(T * I));
     if (!rc) rc = dalloc(m, &m->hf, (size_t)H);
-    if (!rc) rc = dalloc(m, &m->logits, (size_t)c.vocab);
+    if (!rc) rc = dalloc(m, &m->logits, (size_t)m->vocab_l);
+    if (!rc) rc = dalloc(m, &m->part, (size_t)(T * H));
     uint8_t* xqbuf = nullptr;
     if (!rc) rc = dalloc(m, &xqbuf, xq_bytes(T, maxin));
     if (!rc) rc = dalloc(m, &m->best, 1);
@@ -574,7 +603,7 @@ int rq_llama_set_layer(rq_llama* m, int64_t layer, const rq_weight* const* w7, c
     if (!m || !w7 || !rms1 || !rms2) return set_error(RQ_ERR_INVALID, "rq_llama_set_layer: NULL argument");
     const rq_llama_config& c = m->cfg;
     if (layer < 0 || layer >= c.n_layers) return set_error(RQ_ERR_INVALID, "rq_llama_set_layer: layer %lld", (long long)layer);
-    const int64_t H = c.hidden, I = c.intermediate, nq = c.n_heads * c.head_dim, nk = c.n_kv_heads * c.head_dim;
+    const int64_t H = c.hidden, I = m->I_l, nq = m->nh_l * c.head_dim, nk = m->nkv_l * c.head_dim;
     const int64_t shp[7][2] = {{nq, H}, {nk, H}, {nk, H}, {H, nq}, {I, H}, {I, H}, {H, I}};  // (out, in)
     const char* names[7] = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"};
     for (int i = 0; i < 7; i++) {
@@ -604,7 +633,7 @@ int rq_llama_set_head(rq_llama* m, const float* ln_f, const uint16_t* lm_head_f1
     if (!m || !ln_f || !lm_head_f16) return set_error(RQ_ERR_INVALID, "rq_llama_set_head: NULL argument");
     Guard g(m->ctx->device);
     int rc = copy_in(m->ln_f, ln_f, (size_t)m->cfg.hidden * 4);
-    if (!rc) rc = copy_in(m->lm_head, lm_head_f16, (size_t)(m->cfg.vocab * m->cfg.hidden) * 2);
+    if (!rc) rc = copy_in(m->lm_head, lm_head_f16, (size_t)(m->vocab_l * m->cfg.hidden) * 2);
     return rc;
 }
 
@@ -620,6 +649,8 @@ int rq_llama_forward(rq_llama* m, const int32_t* tokens, int64_t T, int64_t inde
                          (long long)index_pos, (long long)(index_pos + T), (long long)c.max_seq);
     for (auto& L : m->layers)
         if (!L.w[0]) return set_error(RQ_ERR_INVALID, "rq_llama_forward: a layer was not set");
+    if (logits && m->W > 1)
+        return set_error(RQ_ERR_UNSUPPORTED, "rq_llama_forward: logits are per-rank shards under tensor parallelism");
     Guard g(m->ctx->device);
     cudaStream_t st = (cudaStream_t)stream;
     int32_t p = (int32_t)index_pos;

@@ -61,13 +61,15 @@ class StreamingLlamaQuantized:
         h = np.ascontiguousarray(lm_head_f16).view(np.uint16)
         check(_lib.lib().rq_llama_set_head(self.handle, n.ctypes.data, h.ctypes.data))
 
-    def forward(self, input_ids, index_pos: int):
-        """Logits (f32 [vocab]) of the last position and the greedy token."""
+    def forward(self, input_ids, index_pos: int, want_logits: bool = True):
+        """Logits (f32 [vocab], single rank only; None when not wanted) of the
+        last position and the greedy token."""
         ids = np.ascontiguousarray(input_ids, dtype=np.int32).reshape(-1)
-        logits = np.empty(self.cfg["vocab"], dtype=np.float32)
+        logits = np.empty(self.cfg["vocab"], dtype=np.float32) if want_logits else None
         nxt = ctypes.c_int32()
         check(_lib.lib().rq_llama_forward(self.handle, ids.ctypes.data, ids.size, index_pos,
-                                          logits.ctypes.data, ctypes.byref(nxt), None))
+                                          logits.ctypes.data if want_logits else None,
+                                          ctypes.byref(nxt), None))
         return logits, int(nxt.value)
 
     def decode_step(self, stream: int = 0) -> None:
@@ -88,7 +90,7 @@ class StreamingLlamaQuantized:
         """Greedy generation (generate with temperature 0): the prompt in one
         forward, then device-side decode steps."""
         check(_lib.lib().rq_llama_reset_tokens(self.handle))
-        self.forward(prompt_ids, 0)
+        self.forward(prompt_ids, 0, want_logits=False)
         for _ in range(max_new_tokens - 1):
             self.decode_step()
         if torch is not None:
@@ -108,18 +110,23 @@ class StreamingLlamaQuantized:
             pass
 
 
-def random_model(cfg: dict, qtype: int, seed: int, device: int = 0, host_blocks: bool = False):
+def random_model(cfg: dict, qtype: int, seed: int, device: int = 0, host_blocks: bool = False,
+                 tp: tuple[int, int] = (1, 0)):
     """Random-init weights of the configured architecture, N(0, 0.02), on the
-    device; linears quantized on the GPU.  Returns (model, host dict of the
-    GGML bytes and F16/f32 tensors when host_blocks)."""
+    device; linears quantized on the GPU.  With tp = (world, rank) every rank
+    draws the same full tensors and keeps its shard, so any world size holds
+    the same model.  Returns (model, host dict of the GGML bytes and F16/f32
+    tensors when host_blocks)."""
+    from .tp import LINEAR_SPLIT, shard
+    world, rank = tp
     g = torch.Generator(device=f"cuda:{device}").manual_seed(seed)
     m = StreamingLlamaQuantized(cfg, device)
     host = {"layers": []} if host_blocks else None
     for l in range(cfg["n_layers"]):
         ws = []
-        for (o, i) in layer_shapes(cfg):
+        for k, (o, i) in enumerate(layer_shapes(cfg)):
             wf = torch.randn(o, i, device=f"cuda:{device}", generator=g) * 0.02
-            ws.append(QWeight.quantize(m.ctx, qtype, wf))
+            ws.append(QWeight.quantize(m.ctx, qtype, shard(LINEAR_SPLIT[k], wf, world, rank)))
             del wf
         r1 = (1.0 + 0.1 * torch.randn(cfg["hidden"], device=f"cuda:{device}", generator=g)).cpu().numpy()
         r2 = (1.0 + 0.1 * torch.randn(cfg["hidden"], device=f"cuda:{device}", generator=g)).cpu().numpy()
@@ -130,7 +137,8 @@ def random_model(cfg: dict, qtype: int, seed: int, device: int = 0, host_blocks:
            ).half().cpu().numpy()
     lnf = (1.0 + 0.1 * torch.randn(cfg["hidden"], device=f"cuda:{device}", generator=g)).cpu().numpy()
     head = (torch.randn(cfg["vocab"], cfg["hidden"], device=f"cuda:{device}", generator=g) * 0.02
-            ).half().cpu().numpy()
+            ).half()
+    head = shard("col", head, world, rank).cpu().numpy()
     m.set_embedding(emb)
     m.set_head(lnf, head)
     if host_blocks:
