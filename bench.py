@@ -202,7 +202,8 @@ LLAMA70B = dict(hidden=8192, intermediate=28672, n_heads=64, n_kv_heads=8, head_
                 rope_theta=10000.0)
 
 
-def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None) -> dict:
+def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None,
+               n_layers: int | None = None) -> dict:
     """Config 5: the full 80-layer Llama-2-70B shape (Platypus2-70B), random
     N(0, 0.02) weights quantized to Q4_K and resident on the GPUs, F16
     embedding / lm_head; 20 seeded uniform prompt ids, greedy decode of 16
@@ -213,7 +214,9 @@ def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None)
     from rustyllm_b200 import Context
     from rustyllm_b200._lib import check, lib
     from rustyllm_b200.llama import random_model
-    cfg = LLAMA70B
+    cfg = dict(LLAMA70B)
+    if n_layers:
+        cfg["n_layers"] = n_layers
     world, rank = 1, 0
     if pg is not None:
         from rustyllm_b200 import tp as tpmod
@@ -261,7 +264,7 @@ def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None)
                                                         (8192, 8192), (28672, 8192), (28672, 8192),
                                                         (8192, 28672)])
     tok_bytes = cfg["n_layers"] * layer_bytes + cfg["vocab"] * cfg["hidden"] * 2
-    return {"config": f"Llama-2-70B shape, 80 layers, Q4_K resident, F16 lm_head, "
+    return {"config": f"Llama-2-70B shape, {cfg['n_layers']} layers, Q4_K resident, F16 lm_head, "
                       f"tensor-parallel over {world} GPU(s)",
             "tp": world,
             "prompt_tokens": prompt_len, "new_tokens": new_tokens,
@@ -288,6 +291,15 @@ def run_gpu(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
         pg = dist
+    if args.only_decode:
+        dec = decode_70b(local, pg=pg, n_layers=args.decode_layers)
+        if rank == 0:
+            print(json.dumps({"metric": "70B Q4_K greedy decode tok/s", "value": dec["decode_tok_s"],
+                              "unit": "tok/s", "n_gpus": world, "decode_70b": dec}), flush=True)
+        if pg is not None:
+            pg.barrier()
+            pg.destroy_process_group()
+        return
     from rustyllm_b200 import Context, QWeight
     from rustyllm_b200._lib import check, lib
     L = lib()
@@ -489,6 +501,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 80-layer 70B decode run")
+    ap.add_argument("--only-decode", action="store_true", help="run only the 70B decode")
+    ap.add_argument("--decode-layers", type=int, default=None,
+                    help="layers of the decode model (default 80; fewer for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -26,7 +26,7 @@
 #include <algorithm>
 #include <vector>
 
-#include "rq_internal.cuh"
+#include "rq_mv_common.cuh"
 
 struct rq_llama {
     rq_ctx* ctx;
@@ -188,6 +188,102 @@ __global__ void attention_kernel(const float* __restrict__ q, const float* __res
     }
 }
 
+// Decode (T = 1) attention fused with RoPE, the KV-cache append and the
+// staging of the head's output for o_proj.  One CTA per head h: it ropes its
+// q and its own copy of the new k (position p = *pos), writes k and v to the
+// cache when it is the first head of its kv group, scores the p cached keys
+// plus the new one, softmax, weighted values, and stages the head_dim outputs
+// (head_dim / 32 blocks of row 0) into xq.  No CTA reads a cache slot written
+// in this launch.  block 128 threads, dynamic smem (max_seq + 3*hd) floats.
+__global__ void attn_decode_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                   const float* __restrict__ v, float* __restrict__ kc,
+                                   float* __restrict__ vc, const float* __restrict__ cos_t,
+                                   const float* __restrict__ sin_t, const int32_t* __restrict__ pos,
+                                   int n_heads, int n_kv, int hd, int max_seq, int8_t* __restrict__ planes,
+                                   float4* __restrict__ stats) {
+    pdl_enter();
+    extern __shared__ float sm[];
+    float* sc = sm;                 // [max_seq]
+    float* qs = sm + max_seq;       // [hd] roped q
+    float* kn = qs + hd;            // [hd] roped new k
+    float* vn = kn + hd;            // [hd] new v, later the head output
+    __shared__ float red[32];
+    const int h = blockIdx.x, half = hd / 2;
+    const int p = min(*pos, max_seq - 1);
+    const int L = p + 1;
+    const int rep = n_heads / n_kv, kh = h / rep;
+    const float* qh = q + (int64_t)h * hd;
+    const float* ks = k + (int64_t)kh * hd;
+    const float* vs = v + (int64_t)kh * hd;
+    float* K = kc + (int64_t)kh * max_seq * hd;
+    float* V = vc + (int64_t)kh * max_seq * hd;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float c = cos_t[(int64_t)p * half + i], s = sin_t[(int64_t)p * half + i];
+        const float a = qh[i], b = qh[i + half];
+        qs[i] = a * c - b * s;
+        qs[i + half] = a * s + b * c;
+        const float ka = ks[i], kb = ks[i + half];
+        kn[i] = ka * c - kb * s;
+        kn[i + half] = ka * s + kb * c;
+    }
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) vn[i] = vs[i];
+    __syncthreads();
+    if (h % rep == 0)
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+            K[(int64_t)p * hd + i] = kn[i];
+            V[(int64_t)p * hd + i] = vn[i];
+        }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const float inv_sqrt = 1.0f / sqrtf((float)hd);
+    for (int j = warp; j < L; j += nw) {
+        const float* kj = j == p ? kn : K + (int64_t)j * hd;
+        float acc = 0.0f;
+        for (int d = lane; d < hd; d += 32) acc = fmaf(qs[d], kj[d], acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) sc[j] = acc * inv_sqrt;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < L; j += blockDim.x) mx = fmaxf(mx, sc[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < nw; w++) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int j = threadIdx.x; j < L; j += blockDim.x) {
+        const float e = expf(sc[j] - mx);
+        sc[j] = e;
+        sum += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    sum = 0.0f;
+    for (int w = 0; w < nw; w++) sum += red[w];
+    float outv[2] = {0.0f, 0.0f};
+    for (int d = threadIdx.x, c = 0; d < hd && c < 2; d += blockDim.x, c++) {
+        float acc = 0.0f;
+        for (int j = 0; j < L; j++) acc = fmaf(sc[j] / sum, j == p ? vn[d] : V[(int64_t)j * hd + d], acc);
+        outv[c] = acc;
+    }
+    __syncthreads();  // vn is reused for the output
+    for (int d = threadIdx.x, c = 0; d < hd && c < 2; d += blockDim.x, c++) vn[d] = outv[c];
+    __syncthreads();
+    // stage the head's outputs: blocks (h*hd)/32 .. of row 0 of the o_proj input
+    const int nbh = hd / 32;
+    if (threadIdx.x < nbh) {
+        float blk[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) blk[i] = vn[threadIdx.x * 32 + i];
+        stage_block(blk, 0, (int64_t)h * nbh + threadIdx.x, (int64_t)n_heads * hd, planes, stats);
+    }
+}
+
 // hf = rmsnorm(x[row], w) for one row (the lm_head input).
 __global__ void rmsnorm_row_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                    float eps, int64_t hidden, float* __restrict__ y) {
@@ -285,6 +381,10 @@ __global__ void add_rows_kernel(float* __restrict__ y, const float* __restrict__
 
 int launch_simple(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args,
                   const char* what) {
+    if (smem > 48 * 1024) {
+        int rc = cuda_error(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), what);
+        if (rc) return rc;
+    }
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_cfg(grid, block, smem, st, attr);
     return cuda_error(cudaLaunchKernelExC(&cfg, fn, args), what);
@@ -380,7 +480,23 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
             rc = run_linears(m, 3, w3, T, y3, nullptr, st);
             if (rc) return rc;
         }
-        {
+        if (T == 1 && c.head_dim % 32 == 0) {
+            const float* q = m->q;
+            const float* k = m->k;
+            const float* v = m->v;
+            float* kc = L.kc;
+            float* vc = L.vc;
+            const float* cs = m->rope_cos;
+            const float* sn = m->rope_sin;
+            const int32_t* pos = m->pos;
+            int nh = (int)m->nh_l, nkv = (int)m->nkv_l, hd = (int)c.head_dim, ms = (int)c.max_seq;
+            int8_t* planes = m->xq.planes;
+            float4* stats = m->xq.stats;
+            void* args[] = {&q, &k, &v, &kc, &vc, &cs, &sn, &pos, &nh, &nkv, &hd, &ms, &planes, &stats};
+            rc = launch_simple((const void*)attn_decode_kernel, dim3((unsigned)nh), dim3(128),
+                               (size_t)(c.max_seq + 3 * c.head_dim) * sizeof(float), st, args, "attention kernel");
+            if (rc) return rc;
+        } else {
             float* q = m->q;
             const float* k = m->k;
             const float* v = m->v;
@@ -400,9 +516,9 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
             rc = launch_simple((const void*)attention_kernel, dim3((unsigned)nh, (unsigned)T), dim3(128),
                                (size_t)c.max_seq * sizeof(float), st, args2, "attention kernel");
             if (rc) return rc;
+            rc = launch_xquant(m->att, T, nq, m->xq, st);
+            if (rc) return rc;
         }
-        rc = launch_xquant(m->att, T, nq, m->xq, st);
-        if (rc) return rc;
         rc = row_parallel(m, L.w[3], T, st);
         if (rc) return rc;
         rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);

@@ -33,54 +33,9 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 // programmatic dependent: it first waits for the preceding kernel (which may
 // produce x), then lets the following matvec launch so that its weight
 // streaming overlaps this kernel.
-// Stage the 32 values v (one block of row m, block b) into the planes and
-// stats of xq; the arithmetic of the staged form (see rq_internal.cuh).
-__device__ __forceinline__ void stage_block(const float (&v)[32], int64_t m, int64_t b, int64_t in,
-                                            int8_t* __restrict__ planes, float4* __restrict__ stats) {
-    float amax = 0.0f, sa = 0.0f, sb = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 16; k++) { amax = fmaxf(amax, fabsf(v[k])); sa += v[k]; }
-#pragma unroll
-    for (int k = 16; k < 32; k++) { amax = fmaxf(amax, fabsf(v[k])); sb += v[k]; }
-    const float inv = amax > 0.0f ? kXQScale / amax : 0.0f;
-    const float sx = amax / kXQScale;
-    uint32_t p1[8], p2[8], p3[8];
-#pragma unroll
-    for (int k = 0; k < 8; k++) { p1[k] = 0u; p2[k] = 0u; p3[k] = 0u; }
-#pragma unroll
-    for (int k = 0; k < 32; k++) {
-        const int X = __float2int_rn(v[k] * inv);
-        const int x3 = (X << 24) >> 24;  // balanced base-256 digits
-        const int t1 = (X - x3) >> 8;
-        const int x2 = (t1 << 24) >> 24;
-        const int x1 = (t1 - x2) >> 8;
-        p1[k / 4] |= (uint32_t)(x1 & 255) << (8 * (k % 4));
-        p2[k / 4] |= (uint32_t)(x2 & 255) << (8 * (k % 4));
-        p3[k / 4] |= (uint32_t)(x3 & 255) << (8 * (k % 4));
-    }
-    uint4* d1 = reinterpret_cast<uint4*>(planes + (m * 3 + 0) * in + b * 32);
-    uint4* d2 = reinterpret_cast<uint4*>(planes + (m * 3 + 1) * in + b * 32);
-    uint4* d3 = reinterpret_cast<uint4*>(planes + (m * 3 + 2) * in + b * 32);
-    d1[0] = make_uint4(p1[0], p1[1], p1[2], p1[3]); d1[1] = make_uint4(p1[4], p1[5], p1[6], p1[7]);
-    d2[0] = make_uint4(p2[0], p2[1], p2[2], p2[3]); d2[1] = make_uint4(p2[4], p2[5], p2[6], p2[7]);
-    d3[0] = make_uint4(p3[0], p3[1], p3[2], p3[3]); d3[1] = make_uint4(p3[4], p3[5], p3[6], p3[7]);
-    stats[m * (in / 32) + b] = make_float4(sx, sa, sb, 0.0f);
-}
-
-__device__ __forceinline__ void load_block(const float* src, float (&v)[32]) {
-    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const float4 f = reinterpret_cast<const float4*>(src)[k];
-            v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 32; k++) v[k] = src[k];
-    }
-}
-
-// RMSNorm fused into staging: one CTA per row.  y = (x / m) * w with
+// RMSNorm fused into staging.  Grid (chunks, rows): every CTA reduces the
+// whole row's sum of squares (the row is L2-resident and small), then stages
+// its chunk of 32-element blocks.  y = (x / m) * w with
 // m = sqrt(sum(x^2) / in + eps), the order of candle_nn::ops::rms_norm.
 __global__ void xquant_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                       float eps, int64_t in, int8_t* __restrict__ planes,
@@ -88,10 +43,19 @@ __global__ void xquant_rmsnorm_kernel(const float* __restrict__ x, const float* 
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     __shared__ float wsum[32];
-    const int64_t m = blockIdx.x;
+    const int64_t m = blockIdx.y;
     const float* row = x + m * in;
     float s2 = 0.0f;
-    for (int64_t i = threadIdx.x; i < in; i += blockDim.x) s2 = fmaf(row[i], row[i], s2);
+    if ((in & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        for (int64_t i = threadIdx.x; i < in / 4; i += blockDim.x) {
+            const float4 v = r4[i];
+            s2 = fmaf(v.x, v.x, s2); s2 = fmaf(v.y, v.y, s2);
+            s2 = fmaf(v.z, v.z, s2); s2 = fmaf(v.w, v.w, s2);
+        }
+    } else {
+        for (int64_t i = threadIdx.x; i < in; i += blockDim.x) s2 = fmaf(row[i], row[i], s2);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
     if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = s2;
@@ -100,7 +64,9 @@ __global__ void xquant_rmsnorm_kernel(const float* __restrict__ x, const float* 
     for (int k = 0; k < (int)(blockDim.x >> 5); k++) tot += wsum[k];
     const float mden = sqrtf(tot / (float)in + eps);
     const int64_t nb = in / 32;
-    for (int64_t b = threadIdx.x; b < nb; b += blockDim.x) {
+    const int64_t per = (nb + gridDim.x - 1) / gridDim.x;
+    const int64_t b0 = blockIdx.x * per, b1 = b0 + per < nb ? b0 + per : nb;
+    for (int64_t b = b0 + threadIdx.x; b < b1; b += blockDim.x) {
         float v[32];
         load_block(row + b * 32, v);
 #pragma unroll
@@ -341,8 +307,10 @@ int launch_xquant_rmsnorm(const float* x, const float* w, float eps, int64_t M, 
                           cudaStream_t st) {
     if (M == 0) return RQ_OK;
     cudaLaunchAttribute attr[1];
-    const int threads = (int)std::min<int64_t>(1024, std::max<int64_t>(32, ((in / 32) + 31) / 32 * 32));
-    cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)M), dim3((unsigned)threads), st, attr);
+    // 8 blocks of 32 per CTA: e.g. 32 CTAs of 256 threads for in = 8192
+    const int64_t nb = in / 32;
+    const unsigned chunks = (unsigned)std::max<int64_t>(1, (nb + 7) / 8);
+    cudaLaunchConfig_t cfg = pdl_config(dim3(chunks, (unsigned)M), dim3(256), st, attr);
     return cuda_error(cudaLaunchKernelEx(&cfg, xquant_rmsnorm_kernel, x, w, eps, in, xq.planes, xq.stats),
                       "xquant rmsnorm kernel");
 }

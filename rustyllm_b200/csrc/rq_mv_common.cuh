@@ -73,6 +73,54 @@ __device__ __forceinline__ bool lane_writes(int lane) {
     return (lane & ((1 << (5 - used)) - 1)) == 0;
 }
 
+// --------------------------------------------------------- x staging
+// Stage the 32 values v (one block of row m, block b) into the planes and
+// stats of xq; the arithmetic of the staged form (see rq_internal.cuh).
+__device__ __forceinline__ void stage_block(const float (&v)[32], int64_t m, int64_t b, int64_t in,
+                                            int8_t* __restrict__ planes, float4* __restrict__ stats) {
+    float amax = 0.0f, sa = 0.0f, sb = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; k++) { amax = fmaxf(amax, fabsf(v[k])); sa += v[k]; }
+#pragma unroll
+    for (int k = 16; k < 32; k++) { amax = fmaxf(amax, fabsf(v[k])); sb += v[k]; }
+    const float inv = amax > 0.0f ? kXQScale / amax : 0.0f;
+    const float sx = amax / kXQScale;
+    uint32_t p1[8], p2[8], p3[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) { p1[k] = 0u; p2[k] = 0u; p3[k] = 0u; }
+#pragma unroll
+    for (int k = 0; k < 32; k++) {
+        const int X = __float2int_rn(v[k] * inv);
+        const int x3 = (X << 24) >> 24;  // balanced base-256 digits
+        const int t1 = (X - x3) >> 8;
+        const int x2 = (t1 << 24) >> 24;
+        const int x1 = (t1 - x2) >> 8;
+        p1[k / 4] |= (uint32_t)(x1 & 255) << (8 * (k % 4));
+        p2[k / 4] |= (uint32_t)(x2 & 255) << (8 * (k % 4));
+        p3[k / 4] |= (uint32_t)(x3 & 255) << (8 * (k % 4));
+    }
+    uint4* d1 = reinterpret_cast<uint4*>(planes + (m * 3 + 0) * in + b * 32);
+    uint4* d2 = reinterpret_cast<uint4*>(planes + (m * 3 + 1) * in + b * 32);
+    uint4* d3 = reinterpret_cast<uint4*>(planes + (m * 3 + 2) * in + b * 32);
+    d1[0] = make_uint4(p1[0], p1[1], p1[2], p1[3]); d1[1] = make_uint4(p1[4], p1[5], p1[6], p1[7]);
+    d2[0] = make_uint4(p2[0], p2[1], p2[2], p2[3]); d2[1] = make_uint4(p2[4], p2[5], p2[6], p2[7]);
+    d3[0] = make_uint4(p3[0], p3[1], p3[2], p3[3]); d3[1] = make_uint4(p3[4], p3[5], p3[6], p3[7]);
+    stats[m * (in / 32) + b] = make_float4(sx, sa, sb, 0.0f);
+}
+
+__device__ __forceinline__ void load_block(const float* src, float (&v)[32]) {
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float4 f = reinterpret_cast<const float4*>(src)[k];
+            v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 32; k++) v[k] = src[k];
+    }
+}
+
 // ------------------------------------------------------------------- Q4_K
 
 struct Q4KLane {
