@@ -197,6 +197,46 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+SMALL_M = (2, 3, 4, 8, 16)
+
+
+def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g) -> dict:
+    """Small-M Q4_K matmul at the seven 70B layer shapes (M = 2, 3, 4, 8
+    for speculative verify, 16 for the first prefill tile): one rq_linear
+    call per linear with [M, in] device activations, graph-replayed over the
+    rotating layer copies.  GB/s = (Q4_K weight bytes + 4 M (in + out)) per
+    layer / time, weight bytes counted once."""
+    import torch
+    from rustyllm_b200._lib import check
+    res = {}
+    for M in SMALL_M:
+        xs = [torch.randn(M, i, device=dev, generator=g) for _, i, _ in SHAPES]
+        ys = [torch.empty(M, o, device=dev) for _, _, o in SHAPES]
+
+        def layer(c, st, xs=xs, ys=ys, M=M):
+            for k in range(len(SHAPES)):
+                check(L.rq_linear(ctx.handle, weights[c][k].handle, xs[k].data_ptr(), ys[k].data_ptr(),
+                                  M, st))
+
+        with torch.cuda.stream(stream):
+            for c in range(N_COPIES):
+                layer(c, stream.cuda_stream)
+        stream.synchronize()
+        gr = capture(lambda st: [layer(c, st) for c in range(N_COPIES)])
+        with torch.cuda.stream(stream):
+            gr.replay()
+        reps = 10
+        ms = timed(lambda r: gr.replay(), reps) / (reps * N_COPIES)
+        nbytes = sum(Q4K_BYTES(i, o) + 4 * M * (i + o) for _, i, o in SHAPES)
+        res[str(M)] = {"ms_per_layer": round(ms, 4), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                       "tok_per_s_layer_equiv": round(M / (ms / 1e3), 1)}
+        del gr
+    res["note"] = ("7 rq_linear calls per layer, 4 rotating layer copies. M <= 3: activation staging + "
+                   "one M=1 pipeline pass per row; M >= 4: f16 hi/lo staging + the mma.sync tensor-core "
+                   "kernel, weights read once per 8-row tile")
+    return res
+
+
 LLAMA70B = dict(hidden=8192, intermediate=28672, n_heads=64, n_kv_heads=8, head_dim=128,
                 n_layers=80, vocab=32000, max_seq=64, max_batch_tokens=32, rms_eps=1e-5,
                 rope_theta=10000.0)
@@ -393,6 +433,9 @@ def run_gpu(args) -> None:
     for k, (n, i, o) in enumerate(SHAPES):
         t = timed(lambda r, k=k: shape_graphs[k].replay(), reps) / (reps * N_COPIES)
         per_shape[n] = round((Q4K_BYTES(i, o) + 4 * (i + o)) / (t / 1e3) / 1e9, 1)
+    small_m = None
+    if not args.no_small_m:
+        small_m = small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g)
     clk = clocks.stop()
     barrier()
     torch.cuda.synchronize()
@@ -485,6 +528,8 @@ def run_gpu(args) -> None:
             line["cpu_baseline"] = cpu
         if dec is not None:
             line["decode_70b"] = dec
+        if small_m is not None:
+            line["small_m_q4k"] = small_m
         print(json.dumps(line), flush=True)
     del graphs, shape_graphs, dom
     if pg is not None:
@@ -502,6 +547,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 80-layer 70B decode run")
     ap.add_argument("--only-decode", action="store_true", help="run only the 70B decode")
+    ap.add_argument("--no-small-m", action="store_true", help="skip the small-M Q4_K matmul sweep")
     ap.add_argument("--decode-layers", type=int, default=None,
                     help="layers of the decode model (default 80; fewer for profiling)")
     args = ap.parse_args()

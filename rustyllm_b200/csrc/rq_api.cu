@@ -345,7 +345,10 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
     DeviceGuard g(ctx->device);
     cudaStream_t st = (cudaStream_t)stream;
     const bool x_dev = mem_kind(x) == Mem::Device, y_dev = mem_kind(y) == Mem::Device;
-    const size_t xq_sz = xq_bytes(M, w->in);
+    // M >= 4: one tensor-core pass over the weights per 8 rows; M = 2, 3:
+    // the M=1 pipeline once per row is faster (it streams at ~5 TB/s)
+    const bool small_m = M >= kMinTensorM && mm_small_supported(w);
+    const size_t xq_sz = small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
     const size_t x_sz = x_dev ? 0 : (size_t)(M * w->in) * sizeof(float);
     const size_t y_sz = y_dev ? 0 : (size_t)(M * w->out) * sizeof(float);
     int rc = ensure_workspace(ctx, xq_sz + x_sz + y_sz + 512);
@@ -361,8 +364,14 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
         rc = cuda_error(cudaMemcpyAsync(xd, x, x_sz, cudaMemcpyHostToDevice, st), "x copy");
         if (rc) return rc;
     }
-    rc = launch_xquant(xd, M, w->in, xq, st);
-    if (!rc) rc = launch_linear(w, xq, yd, M, ctx->sm_count, st);
+    if (small_m) {
+        const XH xh = xh_at(ws, M, w->in);
+        rc = launch_xh_stage(xd, M, w->in, xh, st);
+        if (!rc) rc = launch_matmul_small(w, xh, M, yd, nullptr, ctx->sm_count, st);
+    } else {
+        rc = launch_xquant(xd, M, w->in, xq, st);
+        if (!rc) rc = launch_linear(w, xq, yd, M, ctx->sm_count, st);
+    }
     if (rc) return rc;
     if (!y_dev) {
         rc = cuda_error(cudaMemcpyAsync(y, yd, y_sz, cudaMemcpyDeviceToHost, st), "y copy");

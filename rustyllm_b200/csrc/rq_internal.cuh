@@ -125,6 +125,34 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
                        int sm_count, cudaStream_t st, int* err = nullptr,
                        const float* const* adds = nullptr);
 
+// small-M Q4_K matmul on the tensor cores (rq_mm_small.cu).  Activations are
+// staged per row as x / s = hi + lo (two f16 values per element, s a power of
+// two), quad-permuted, with f32 sums per 32-element block:
+struct XH {
+    __half* v;     // [rows][2][in]: hi plane, lo plane
+    float* scale;  // [rows]
+    float* bsum;   // [rows][in/32]
+};
+size_t xh_bytes(int64_t rows, int64_t in);
+XH xh_at(void* base, int64_t rows, int64_t in);
+int launch_xh_stage(const float* x, int64_t M, int64_t in, XH xh, cudaStream_t st);
+// Up to kMaxJobs jobs with the same K, each y_j[M_j][out_j] = x[tok0_j ..
+// tok0_j + M_j) W_j^T (+ add_j), M_j <= 8, all reading one staged matrix of
+// `rows` rows; err may be NULL.
+struct MMJobDesc {
+    const rq_weight* w;
+    int tok0, M;
+    float* y;
+    const float* add;
+};
+bool mm_small_supported(const rq_weight* w);
+constexpr int64_t kMinTensorM = 4;  // smallest M routed to the tensor-core kernel
+int launch_mm_small(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_count, cudaStream_t st,
+                    int* err = nullptr);
+// y[M][out] = x W^T (+ add) for M >= 2 staged rows, in tiles of 8 rows
+int launch_matmul_small(const rq_weight* w, XH xh, int64_t M, float* y, const float* add, int sm_count,
+                        cudaStream_t st);
+
 // linear kernels (rq_matvec.cu).  launch_linear runs y = x W^T for M staged
 // activation rows (launch_xquant first).  launch_xquant_rows stages up to
 // kMaxJobs separate rows (row j of `in` floats at xs[j]) into consecutive

@@ -279,6 +279,34 @@ __device__ __forceinline__ float q4kp_lane_row(const Q4KPLane& L, uint4 qa, uint
     return fmaf(-dd.y, fmaf(m0, L.xsl, m1 * L.xsh), part);
 }
 
+// Selectors that gather the four 6-bit values (scale, min) of the sub-block
+// pair (2g, 2g+1) of a Q4_K header with two byte permutes (GGML packing; the
+// same decode as Q4KPLane, for kernels that keep g per warp).
+struct Q4KScaleSel {
+    uint32_t sel1, sel2, mA, mB, mC;
+    bool hiG;
+};
+
+__device__ __forceinline__ Q4KScaleSel q4k_scale_sel(int g) {
+    Q4KScaleSel S;
+    S.hiG = g >= 2;
+    const uint32_t j = 2u * (uint32_t)(g & 1);
+    const uint32_t yz = j | ((j + 1) << 4) | ((j + 4) << 8) | ((j + 5) << 12);
+    S.sel1 = S.hiG ? (j | ((j + 1) << 4) | (j << 8) | ((j + 1) << 12)) : yz;
+    S.sel2 = yz;
+    S.mA = S.hiG ? 0x00000F0Fu : 0x3F3F3F3Fu;
+    S.mB = S.hiG ? 0x0F0F0000u : 0u;
+    S.mC = S.hiG ? 0x30303030u : 0u;
+    return S;
+}
+
+// bytes [sc(2g), sc(2g+1), m(2g), m(2g+1)] of header h
+__device__ __forceinline__ uint32_t q4k_scales(const Q4KScaleSel& S, uint4 h) {
+    const uint32_t x1 = __byte_perm(S.hiG ? h.w : h.y, h.z, S.sel1);
+    const uint32_t x2 = __byte_perm(h.y, h.z, S.sel2);
+    return (x1 & S.mA) | ((x1 >> 4) & S.mB) | ((x2 >> 2) & S.mC);
+}
+
 // ------------------------------------------------------------------- Q3_K
 
 struct Q3KLane {

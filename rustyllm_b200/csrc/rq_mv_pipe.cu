@@ -26,6 +26,7 @@
 
 #include <algorithm>
 
+#include "rq_async.cuh"
 #include "rq_mv_common.cuh"
 
 namespace rq {
@@ -38,7 +39,6 @@ constexpr int kMaxConsumerWarps = 15;
 constexpr int kThreads = 32 * (1 + kMaxConsumerWarps);
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kBarBytes = 2 * 32 * 8;  // up to 32 stages: full + empty barriers
-constexpr long long kWaitCycles = 1ll << 31;
 
 struct PipeParams {
     PipeJob jobs[kMaxJobs];
@@ -49,46 +49,6 @@ struct PipeParams {
     uint32_t qrow, hrow;  // device bytes per weight row (quant part, header part)
     uint32_t stage_bytes, red_off, ring_off;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t a) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t a, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(a), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Wait for the phase with the given parity to complete; false after ~1 s.
-__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity) {
-    if (mbar_try_wait(a, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try_wait(a, parity))
-        if (clock64() - t0 > kWaitCycles) return false;
-    return true;
-}
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
-                                         uint32_t mbar, uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(mbar), "l"(policy)
-        : "memory");
-}
 
 __device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) {
     const int64_t b = (int64_t)blockIdx.x * j.out / gridDim.x;
@@ -202,8 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
 
     if (warp == 0) {
         if (lane == 0) {
-            uint64_t pol;
-            asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+            const uint64_t pol = policy_evict_first();
             int it = 0;
             bool ok = true;
             for (int j = 0; j < p.njobs && ok; j++) {

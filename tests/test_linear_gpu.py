@@ -73,6 +73,25 @@ def test_small_m_matches_oracle(oracle, rq_ctx, qtype, M):
         assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("out,n_in,M", [(200, 768, 4), (200, 768, 5), (1040, 4096, 8), (16, 256, 6),
+                                         (333, 2048, 67), (4096, 512, 8), (520, 28672, 12)])
+def test_small_m_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
+    """Q4_K M >= 4 runs on the tensor-core kernel: ragged row groups,
+    an odd number of super-blocks (half-empty last stage), more than eight
+    token tiles (two launches), many row blocks per CTA."""
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200.linear import _linear
+    _, blocks = make_weight(oracle, 12, out, n_in, seed=out + M)
+    w = QWeight.upload(rq_ctx, 12, blocks, out, n_in)
+    x = np.random.default_rng(M + 1).standard_normal((M, n_in)).astype(np.float32)
+    y = _linear(w, x)
+    ref = oracle.matmul_ref(12, blocks, out, n_in, x, acc64=True)
+    assert np.isfinite(y).all()
+    assert rel_l2(y, ref) <= REL_L2_TOL
+    for m in range(M):
+        assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
+
+
 @pytest.mark.parametrize("qtype", TYPES)
 def test_gpu_quantizer_matches_oracle_bytes(oracle, rq_ctx, qtype):
     import torch
