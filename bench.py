@@ -237,6 +237,65 @@ def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g) -> dict:
     return res
 
 
+MIXTRAL = dict(E=8, H=4096, F=14336, k=2)
+MOE_T = (1, 16, 512)
+
+
+def moe_sweep(device: int, seed: int = 4321) -> dict:
+    """Mixtral-8x7B sparse-MoE layer: router [8, 4096] f32 N(0, 0.02), 8
+    experts of Q4_K SwiGLU weights (4096 -> 14336 -> 4096) quantized on the
+    device from N(0, 0.02), hidden states N(0, 1) for T = 1, 16, 512 tokens,
+    device-resident.  One forward = route, permute, expert products,
+    combine (with its one host sync after routing).  GB/s counts the Q4_K
+    bytes of the experts the tokens touch, once; T=512 also reports
+    TFLOP/s of the 2*T*k*3*H*F expert flops."""
+    import torch
+    from rustyllm_b200 import Context, QWeight
+    from rustyllm_b200.mixtral import SparseMoe
+    E, H, F, k = MIXTRAL["E"], MIXTRAL["H"], MIXTRAL["F"], MIXTRAL["k"]
+    dev = torch.device("cuda", device)
+    ctx = Context.get(device)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    router = (torch.randn(E, H, device=dev, generator=g) * 0.02).cpu().numpy()
+    experts = []
+    for _ in range(E):
+        trip = []
+        for o, i in ((F, H), (H, F), (F, H)):
+            wf = torch.randn(o, i, device=dev, generator=g) * 0.02
+            trip.append(QWeight.quantize(ctx, Q4_K, wf))
+            del wf
+        experts.append(tuple(trip))
+    moe = SparseMoe(router, experts, top_k=k, device=device)
+    mat_bytes = Q4K_BYTES(H, F)
+    res = {}
+    for T in MOE_T:
+        x = torch.randn(T, H, device=dev, generator=g)
+        _, ids, _ = moe.forward_with_routing(x)
+        touched = len(set(ids.reshape(-1).tolist()))
+        for _ in range(2):
+            moe.forward(x)
+        torch.cuda.synchronize()
+        reps = 20 if T < 512 else 5
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            moe.forward(x)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        r = {"ms": round(ms, 4), "tok_per_s": round(T / (ms / 1e3), 1), "experts_touched": touched,
+             "weight_gbs": round(touched * 3 * mat_bytes / (ms / 1e3) / 1e9, 1)}
+        if T == 512:
+            r["tflops"] = round(2 * T * k * 3 * H * F / (ms / 1e3) / 1e12, 2)
+        res[str(T)] = r
+    res["config"] = "Mixtral-8x7B MoE layer: E=8, top-2, H=4096, F=14336, Q4_K experts, 1 GPU"
+    moe.close()
+    for trip in experts:
+        for w in trip:
+            w.free()
+    return res
+
+
 LLAMA70B = dict(hidden=8192, intermediate=28672, n_heads=64, n_kv_heads=8, head_dim=128,
                 n_layers=80, vocab=32000, max_seq=64, max_batch_tokens=32, rms_eps=1e-5,
                 rope_theta=10000.0)
@@ -482,6 +541,9 @@ def run_gpu(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host = {n: weights[0][k].download() for k, (n, _, _) in enumerate(SHAPES)}
         cpu = cpu_baseline(host, seconds=args.cpu_seconds)
+    moe = None
+    if not args.no_moe and world == 1:
+        moe = moe_sweep(local)
     dec = None
     if not args.no_decode:
         del graphs, shape_graphs, dom
@@ -530,6 +592,8 @@ def run_gpu(args) -> None:
             line["decode_70b"] = dec
         if small_m is not None:
             line["small_m_q4k"] = small_m
+        if moe is not None:
+            line["mixtral_moe"] = moe
         print(json.dumps(line), flush=True)
     del graphs, shape_graphs, dom
     if pg is not None:
@@ -548,6 +612,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the 80-layer 70B decode run")
     ap.add_argument("--only-decode", action="store_true", help="run only the 70B decode")
     ap.add_argument("--no-small-m", action="store_true", help="skip the small-M Q4_K matmul sweep")
+    ap.add_argument("--no-moe", action="store_true", help="skip the Mixtral MoE layer sweep")
     ap.add_argument("--decode-layers", type=int, default=None,
                     help="layers of the decode model (default 80; fewer for profiling)")
     args = ap.parse_args()

@@ -45,6 +45,9 @@ struct rq_moe {
     float* yd = nullptr;
     uint8_t* xq_x = nullptr;     // staged x rows
     uint8_t* xq_h = nullptr;     // staged swiglu rows
+    float* xg = nullptr;         // [T*k][H] x rows gathered in slot order
+    uint8_t* xh_x = nullptr;     // tensor-core staging of xg
+    uint8_t* xh_h = nullptr;     // tensor-core staging of the swiglu rows
     std::vector<void*> bufs;
 };
 
@@ -194,6 +197,26 @@ __global__ void combine_kernel(const float* __restrict__ o, const float* __restr
     }
 }
 
+// xg[s] = x[perm[s]]: the token rows in slot (expert-major) order.
+__global__ void gather_kernel(const float* __restrict__ x, const int32_t* __restrict__ perm, int64_t H,
+                              float* __restrict__ xg) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int64_t s = blockIdx.y, t = perm[s];
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < H; c += (int64_t)gridDim.x * blockDim.x)
+        xg[s * H + c] = x[t * H + c];
+}
+
+// g = silu(g) * up, silu(v) = v / (1 + exp(-v)) (streaming_mixtral.rs:250-256).
+__global__ void swiglu_kernel(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = g[i];
+        g[i] = v / (1.0f + expf(-v)) * u[i];
+    }
+}
+
 cudaLaunchConfig_t pdl(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAttribute* attr) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -234,6 +257,9 @@ int ensure_cap(rq_moe* m, int64_t T) {
     if (!rc) rc = grow(m, &m->yd, (size_t)(T * m->H));
     if (!rc) rc = grow(m, &m->xq_x, xq_bytes(T, m->H));
     if (!rc) rc = grow(m, &m->xq_h, xq_bytes(S, m->F));
+    if (!rc) rc = grow(m, &m->xg, (size_t)(S * m->H));
+    if (!rc) rc = grow(m, &m->xh_x, xh_bytes(S, m->H));
+    if (!rc) rc = grow(m, &m->xh_h, xh_bytes(S, m->F));
     m->cap_t = rc ? 0 : T;
     return rc;
 }
@@ -251,6 +277,15 @@ struct JobList {
     std::vector<XQ> x;
     std::vector<float*> y;
 };
+
+int run_mm_jobs(const std::vector<MMJobDesc>& J, XH xh, int64_t rows, int sm, cudaStream_t st) {
+    for (size_t b = 0; b < J.size(); b += kMaxJobs) {
+        const int n = (int)std::min<size_t>(kMaxJobs, J.size() - b);
+        int rc = launch_mm_small(&J[b], n, xh, rows, sm, st);
+        if (rc) return rc;
+    }
+    return RQ_OK;
+}
 
 int run_jobs(const JobList& J, int sm, cudaStream_t st) {
     for (size_t b = 0; b < J.w.size(); b += kMaxJobs) {
@@ -387,27 +422,71 @@ int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
                                              cudaMemcpyDeviceToHost, st), "perm copy");
     if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "routing sync");
     if (rc) return rc;
-    // gate and up products: one job per (expert, token) slot
+    // Experts with at least kMinTensorM tokens run on the tensor-core kernel
+    // (tiles of up to 8 slots, weights read once per tile); the others run
+    // one M=1 pipeline job per (expert, slot).
+    auto use_mm = [&](int e) {
+        return offs[(size_t)e + 1] - offs[(size_t)e] >= kMinTensorM && mm_small_supported(m->w1[(size_t)e]) &&
+               mm_small_supported(m->w3[(size_t)e]) && mm_small_supported(m->w2[(size_t)e]);
+    };
+    bool any_mm = false, any_pipe = false;
+    for (int e = 0; e < E; e++) {
+        if (offs[(size_t)e + 1] == offs[(size_t)e]) continue;
+        if (use_mm(e)) any_mm = true;
+        else any_pipe = true;
+    }
+    const XH xhx = xh_at(m->xh_x, S, H), xhh = xh_at(m->xh_h, S, F);
+    if (any_mm) {
+        cudaLaunchConfig_t cfg = pdl(dim3((unsigned)std::min<int64_t>(32, (H + 255) / 256), (unsigned)S), dim3(256),
+                                     st, attr);
+        rc = cuda_error(cudaLaunchKernelEx(&cfg, gather_kernel, xs, (const int32_t*)m->perm, H, m->xg), "gather kernel");
+        if (!rc) rc = launch_xh_stage(m->xg, S, H, xhx, st);
+        if (rc) return rc;
+    }
+    // gate and up products
     JobList up;
-    for (int e = 0; e < E; e++)
-        for (int32_t s = offs[(size_t)e]; s < offs[(size_t)e + 1]; s++) {
+    std::vector<MMJobDesc> upm, downm;
+    for (int e = 0; e < E; e++) {
+        const int32_t s0 = offs[(size_t)e], s1 = offs[(size_t)e + 1];
+        if (use_mm(e)) {
+            for (int32_t t0 = s0; t0 < s1; t0 += 8) {
+                const int n = std::min<int32_t>(8, s1 - t0);
+                upm.push_back(MMJobDesc{m->w1[(size_t)e], t0, n, m->g + (int64_t)t0 * F, nullptr});
+                upm.push_back(MMJobDesc{m->w3[(size_t)e], t0, n, m->u + (int64_t)t0 * F, nullptr});
+                downm.push_back(MMJobDesc{m->w2[(size_t)e], t0, n, m->o + (int64_t)t0 * H, nullptr});
+            }
+            continue;
+        }
+        for (int32_t s = s0; s < s1; s++) {
             const int64_t t = perm[(size_t)s];
             const XQ xr{xqx.planes + t * 3 * H, xqx.stats + t * (H / 32)};
             up.w.push_back(m->w1[(size_t)e]); up.x.push_back(xr); up.y.push_back(m->g + (int64_t)s * F);
             up.w.push_back(m->w3[(size_t)e]); up.x.push_back(xr); up.y.push_back(m->u + (int64_t)s * F);
         }
+    }
     rc = run_jobs(up, sm, st);
+    if (!rc) rc = run_mm_jobs(upm, xhx, S, sm, st);
     XQ xqh = xq_view(m->xq_h, S, F);
-    if (!rc) rc = launch_xquant_swiglu(m->g, m->u, S, F, xqh, st);
+    if (!rc && any_mm) {
+        cudaLaunchConfig_t cfg = pdl(dim3(1184), dim3(256), st, attr);
+        rc = cuda_error(cudaLaunchKernelEx(&cfg, swiglu_kernel, m->g, (const float*)m->u, S * F), "swiglu kernel");
+        if (!rc) rc = launch_xh_stage(m->g, S, F, xhh, st);
+        if (!rc && any_pipe) rc = launch_xquant(m->g, S, F, xqh, st);
+    } else if (!rc) {
+        rc = launch_xquant_swiglu(m->g, m->u, S, F, xqh, st);
+    }
     if (rc) return rc;
     JobList down;
-    for (int e = 0; e < E; e++)
+    for (int e = 0; e < E; e++) {
+        if (use_mm(e)) continue;
         for (int32_t s = offs[(size_t)e]; s < offs[(size_t)e + 1]; s++) {
             down.w.push_back(m->w2[(size_t)e]);
             down.x.push_back(XQ{xqh.planes + (int64_t)s * 3 * F, xqh.stats + (int64_t)s * (F / 32)});
             down.y.push_back(m->o + (int64_t)s * H);
         }
+    }
     rc = run_jobs(down, sm, st);
+    if (!rc) rc = run_mm_jobs(downm, xhh, S, sm, st);
     if (!rc) {
         cudaLaunchConfig_t cfg = pdl(dim3((unsigned)std::min<int64_t>(64, (H + 255) / 256), (unsigned)T), dim3(256), st, attr);
         rc = cuda_error(cudaLaunchKernelEx(&cfg, combine_kernel, (const float*)m->o, (const float*)m->slot_w,

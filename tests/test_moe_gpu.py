@@ -31,8 +31,10 @@ def make_layer(oracle, rq_ctx, E, H, F, qtype, seed):
     return wr, blocks, experts
 
 
-@pytest.mark.parametrize("T", [1, 2, 5, 16, 33])
+@pytest.mark.parametrize("T", [1, 2, 5, 16, 33, 130])
 def test_moe_matches_oracle(oracle, rq_ctx, T):
+    """Small T runs per-slot pipeline jobs; experts with >= 4 tokens run the
+    tensor-core kernel in tiles of 8 (T=130: several tiles per expert)."""
     from rustyllm_b200.mixtral import SparseMoe
     E, H, F = 8, 512, 1024
     wr, blocks, experts = make_layer(oracle, rq_ctx, E, H, F, 12, seed=T)
