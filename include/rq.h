@@ -171,7 +171,9 @@ RQ_API int rq_tp_finalize(rq_ctx* ctx);
 /* Mixtral SparseMoe (src/streaming_mixtral.rs:259-319) with quantized
  * experts: router weight f32 [E][hidden] (host or device, copied), expert
  * weights w1 = gate [ffn][hidden], w3 = up [ffn][hidden], w2 = down
- * [hidden][ffn] (borrowed: they must outlive the layer).  E <= 32. */
+ * [hidden][ffn] (borrowed: they must outlive the layer).  E <= 32.  Under a
+ * communicator (rq_tp_init, world W > 1) the experts of other ranks (e % W
+ * != rank) may be NULL: the layer then runs expert-parallel only. */
 RQ_API int rq_moe_create(rq_ctx* ctx, int n_experts, int top_k, int64_t hidden, int64_t ffn,
                          const float* router_w, const rq_weight* const* w1,
                          const rq_weight* const* w3, const rq_weight* const* w2, rq_moe** out);
@@ -185,6 +187,16 @@ RQ_API int rq_moe_free(rq_moe* m);
  * before the expert products (as the reference does, :284-286). */
 RQ_API int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
                           int32_t* expert_ids_out, int32_t* perm_out, void* stream);
+/* Expert-parallel forward over the communicator of ctx: expert e lives on
+ * rank e % W.  Each rank passes its own T tokens (T may differ per rank, 0
+ * included; every rank must call).  Routing is local; the token rows go to
+ * their experts' ranks and the expert outputs come back through NCCL
+ * all-to-alls (ncclSend/ncclRecv), and each rank combines its own tokens in
+ * ascending expert order.  y, expert_ids_out and perm_out as for
+ * rq_moe_forward, for the local tokens; y equals rq_moe_forward on the same
+ * tokens bit for bit. */
+RQ_API int rq_moe_forward_ep(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
+                             int32_t* expert_ids_out, int32_t* perm_out, void* stream);
 
 /* -------------------------------------------------------- Llama decode loop */
 

@@ -81,6 +81,7 @@ SIGNATURES.update({
     "rq_moe_create": (I, [P, I, I, I64, I64, P, PP, PP, PP, PP]),
     "rq_moe_free": (I, [P]),
     "rq_moe_forward": (I, [P, P, P, P, I64, P, P, P]),
+    "rq_moe_forward_ep": (I, [P, P, P, P, I64, P, P, P]),
 })
 
 _lib = None

@@ -95,6 +95,12 @@ int tp_world(const rq_ctx* ctx);
 int tp_rank(const rq_ctx* ctx);
 int tp_allreduce(rq_ctx* ctx, const void* in, void* out, int64_t n, int dtype, int op, cudaStream_t st);
 void tp_destroy(rq_ctx* ctx);
+// all-gather of nbytes from every rank into out[world][nbytes]
+int tp_allgather_bytes(rq_ctx* ctx, const void* in, void* out, int64_t nbytes, cudaStream_t st);
+// all-to-all with per-peer byte counts and offsets (ncclSend/ncclRecv in one
+// group; the rank's own share is a device copy)
+int tp_alltoallv_bytes(rq_ctx* ctx, const void* send, const int64_t* send_bytes, const int64_t* send_off, void* recv,
+                       const int64_t* recv_bytes, const int64_t* recv_off, cudaStream_t st);
 
 // error handling (rq_api.cu)
 int set_error(int code, const char* fmt, ...);

@@ -28,27 +28,35 @@ struct rq_moe {
     int E, k;
     int64_t H, F;
     float* router;  // [E][H]
-    std::vector<const rq_weight*> w1, w3, w2;
-    // per-forward buffers, grown on demand
+    std::vector<const rq_weight*> w1, w3, w2;  // NULL for experts of other ranks (expert parallel)
+    // per-forward routing buffers, T tokens (S = T k slots), grown on demand
     int64_t cap_t = 0;
     float* logits = nullptr;     // [T][E]
     int32_t* ids = nullptr;      // [T][k] expert ids in rank order
     float* wts = nullptr;        // [T][k]
     int32_t* offs = nullptr;     // [E+1]
-    int32_t* perm = nullptr;     // [T*k] slot -> token (expert-major)
-    float* slot_w = nullptr;     // [T*k]
+    int32_t* perm = nullptr;     // [S] slot -> token (expert-major)
+    float* slot_w = nullptr;     // [S]
     int32_t* tok_slot = nullptr; // [T][k] token -> its slots in ascending expert order
-    float* g = nullptr;          // [T*k][F]
-    float* u = nullptr;
-    float* o = nullptr;          // [T*k][H]
     float* xd = nullptr;         // [T][H] device copy of host x
     float* yd = nullptr;
-    uint8_t* xq_x = nullptr;     // staged x rows
-    uint8_t* xq_h = nullptr;     // staged swiglu rows
-    float* xg = nullptr;         // [T*k][H] x rows gathered in slot order
-    uint8_t* xh_x = nullptr;     // tensor-core staging of xg
-    uint8_t* xh_h = nullptr;     // tensor-core staging of the swiglu rows
-    std::vector<void*> bufs;
+    float* xg = nullptr;         // [S][H] token rows in slot order (send order under EP)
+    float* o = nullptr;          // [S][H] expert outputs in slot order
+    float* osend = nullptr;      // [S][H] expert outputs in send order (EP)
+    int32_t* idx = nullptr;      // [S] gather indices
+    int32_t* cnt = nullptr;      // [world][E] slot counts of every rank (EP)
+    std::vector<void*> bufs_t;
+    // expert-product buffers, R rows, grown on demand
+    int64_t cap_r = 0;
+    float* xr = nullptr;         // [R][H] received rows (EP)
+    float* g = nullptr;          // [R][F]
+    float* u = nullptr;
+    float* fo = nullptr;         // [R][H]
+    uint8_t* xq_x = nullptr;     // M=1 pipeline staging of the rows
+    uint8_t* xq_h = nullptr;     // ... of the swiglu rows
+    uint8_t* xh_x = nullptr;     // tensor-core staging of the rows
+    uint8_t* xh_h = nullptr;     // ... of the swiglu rows
+    std::vector<void*> bufs_r;
 };
 
 namespace rq {
@@ -197,14 +205,14 @@ __global__ void combine_kernel(const float* __restrict__ o, const float* __restr
     }
 }
 
-// xg[s] = x[perm[s]]: the token rows in slot (expert-major) order.
-__global__ void gather_kernel(const float* __restrict__ x, const int32_t* __restrict__ perm, int64_t H,
-                              float* __restrict__ xg) {
+// dst[r] = src[idx[r]] for rows of H floats.
+__global__ void gather_kernel(const float* __restrict__ src, const int32_t* __restrict__ idx, int64_t H,
+                              float* __restrict__ dst) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
-    const int64_t s = blockIdx.y, t = perm[s];
+    const int64_t r = blockIdx.y, t = idx[r];
     for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < H; c += (int64_t)gridDim.x * blockDim.x)
-        xg[s * H + c] = x[t * H + c];
+        dst[r * H + c] = src[t * H + c];
 }
 
 // g = silu(g) * up, silu(v) = v / (1 + exp(-v)) (streaming_mixtral.rs:250-256).
@@ -229,38 +237,54 @@ cudaLaunchConfig_t pdl(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAttribu
     return cfg;
 }
 
-template <typename T>
-int grow(rq_moe* m, T** p, size_t n) {
+template <class T>
+int grow(std::vector<void*>& bufs, T** p, size_t n) {
     cudaError_t e = cudaMalloc((void**)p, std::max<size_t>(n, 1) * sizeof(T));
     if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(moe)");
-    m->bufs.push_back((void*)*p);
+    bufs.push_back((void*)*p);
     return RQ_OK;
 }
 
-int ensure_cap(rq_moe* m, int64_t T) {
+int ensure_t(rq_moe* m, int64_t T, int world) {
     if (T <= m->cap_t) return RQ_OK;
-    for (void* p : m->bufs) cudaFree(p);
-    m->bufs.clear();
+    for (void* p : m->bufs_t) cudaFree(p);
+    m->bufs_t.clear();
     const int64_t S = T * m->k;
+    auto& b = m->bufs_t;
     int rc = RQ_OK;
-    if (!rc) rc = grow(m, &m->logits, (size_t)(T * m->E));
-    if (!rc) rc = grow(m, &m->ids, (size_t)S);
-    if (!rc) rc = grow(m, &m->wts, (size_t)S);
-    if (!rc) rc = grow(m, &m->offs, (size_t)(m->E + 1));
-    if (!rc) rc = grow(m, &m->perm, (size_t)S);
-    if (!rc) rc = grow(m, &m->slot_w, (size_t)S);
-    if (!rc) rc = grow(m, &m->tok_slot, (size_t)S);
-    if (!rc) rc = grow(m, &m->g, (size_t)(S * m->F));
-    if (!rc) rc = grow(m, &m->u, (size_t)(S * m->F));
-    if (!rc) rc = grow(m, &m->o, (size_t)(S * m->H));
-    if (!rc) rc = grow(m, &m->xd, (size_t)(T * m->H));
-    if (!rc) rc = grow(m, &m->yd, (size_t)(T * m->H));
-    if (!rc) rc = grow(m, &m->xq_x, xq_bytes(T, m->H));
-    if (!rc) rc = grow(m, &m->xq_h, xq_bytes(S, m->F));
-    if (!rc) rc = grow(m, &m->xg, (size_t)(S * m->H));
-    if (!rc) rc = grow(m, &m->xh_x, xh_bytes(S, m->H));
-    if (!rc) rc = grow(m, &m->xh_h, xh_bytes(S, m->F));
+    if (!rc) rc = grow(b, &m->logits, (size_t)(T * m->E));
+    if (!rc) rc = grow(b, &m->ids, (size_t)S);
+    if (!rc) rc = grow(b, &m->wts, (size_t)S);
+    if (!rc) rc = grow(b, &m->offs, (size_t)(m->E + 1));
+    if (!rc) rc = grow(b, &m->perm, (size_t)S);
+    if (!rc) rc = grow(b, &m->slot_w, (size_t)S);
+    if (!rc) rc = grow(b, &m->tok_slot, (size_t)S);
+    if (!rc) rc = grow(b, &m->xd, (size_t)(T * m->H));
+    if (!rc) rc = grow(b, &m->yd, (size_t)(T * m->H));
+    if (!rc) rc = grow(b, &m->xg, (size_t)(S * m->H));
+    if (!rc) rc = grow(b, &m->o, (size_t)(S * m->H));
+    if (!rc) rc = grow(b, &m->osend, (size_t)(S * m->H));
+    if (!rc) rc = grow(b, &m->idx, (size_t)S);
+    if (!rc) rc = grow(b, &m->cnt, (size_t)(world * m->E));
     m->cap_t = rc ? 0 : T;
+    return rc;
+}
+
+int ensure_r(rq_moe* m, int64_t R) {
+    if (R <= m->cap_r) return RQ_OK;
+    for (void* p : m->bufs_r) cudaFree(p);
+    m->bufs_r.clear();
+    auto& b = m->bufs_r;
+    int rc = RQ_OK;
+    if (!rc) rc = grow(b, &m->xr, (size_t)(R * m->H));
+    if (!rc) rc = grow(b, &m->g, (size_t)(R * m->F));
+    if (!rc) rc = grow(b, &m->u, (size_t)(R * m->F));
+    if (!rc) rc = grow(b, &m->fo, (size_t)(R * m->H));
+    if (!rc) rc = grow(b, &m->xq_x, xq_bytes(R, m->H));
+    if (!rc) rc = grow(b, &m->xq_h, xq_bytes(R, m->F));
+    if (!rc) rc = grow(b, &m->xh_x, xh_bytes(R, m->H));
+    if (!rc) rc = grow(b, &m->xh_h, xh_bytes(R, m->F));
+    m->cap_r = rc ? 0 : R;
     return rc;
 }
 
@@ -323,6 +347,145 @@ struct Guard {
     }
 };
 
+// A run of rows of one expert inside a row buffer.
+struct Seg {
+    int e;
+    int64_t start, n;
+};
+
+int launch_gather(const float* src, const int32_t* idx, int64_t rows, int64_t H, float* dst, cudaStream_t st) {
+    if (rows == 0) return RQ_OK;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl(dim3((unsigned)std::min<int64_t>(32, (H + 255) / 256), (unsigned)rows), dim3(256), st, attr);
+    return cuda_error(cudaLaunchKernelEx(&cfg, gather_kernel, src, idx, H, dst), "gather kernel");
+}
+
+// out[r] = FFN_e(rows[r]) for the R rows of the segments (expert e of each).
+// Segments of at least kMinTensorM rows run on the tensor-core kernel in
+// tiles of 8 rows; the others run one M=1 pipeline job per row.  Every row's
+// result depends only on that row and on its segment's size, so a token gives
+// the same bits in one layer call as in an expert-parallel one.
+int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& segs, float* out, cudaStream_t st) {
+    if (R == 0) return RQ_OK;
+    const int64_t H = m->H, F = m->F;
+    const int sm = m->ctx->sm_count;
+    auto use_mm = [&](const Seg& sg) {
+        const size_t e = (size_t)sg.e;
+        return sg.n >= kMinTensorM && mm_small_supported(m->w1[e]) && mm_small_supported(m->w3[e]) &&
+               mm_small_supported(m->w2[e]);
+    };
+    bool any_mm = false, any_pipe = false;
+    for (const Seg& sg : segs) {
+        if (sg.n == 0) continue;
+        if (use_mm(sg)) any_mm = true;
+        else any_pipe = true;
+    }
+    const XQ xqx = xq_view(m->xq_x, R, H), xqh = xq_view(m->xq_h, R, F);
+    const XH xhx = xh_at(m->xh_x, R, H), xhh = xh_at(m->xh_h, R, F);
+    int rc = RQ_OK;
+    if (any_pipe) rc = launch_xquant(rows, R, H, xqx, st);
+    if (!rc && any_mm) rc = launch_xh_stage(rows, R, H, xhx, st);
+    if (rc) return rc;
+    JobList up, down;
+    std::vector<MMJobDesc> upm, downm;
+    for (const Seg& sg : segs) {
+        const size_t e = (size_t)sg.e;
+        if (use_mm(sg)) {
+            for (int64_t t0 = sg.start; t0 < sg.start + sg.n; t0 += 8) {
+                const int n = (int)std::min<int64_t>(8, sg.start + sg.n - t0);
+                upm.push_back(MMJobDesc{m->w1[e], (int)t0, n, m->g + t0 * F, nullptr});
+                upm.push_back(MMJobDesc{m->w3[e], (int)t0, n, m->u + t0 * F, nullptr});
+                downm.push_back(MMJobDesc{m->w2[e], (int)t0, n, out + t0 * H, nullptr});
+            }
+            continue;
+        }
+        for (int64_t r = sg.start; r < sg.start + sg.n; r++) {
+            const XQ xr{xqx.planes + r * 3 * H, xqx.stats + r * (H / 32)};
+            up.w.push_back(m->w1[e]); up.x.push_back(xr); up.y.push_back(m->g + r * F);
+            up.w.push_back(m->w3[e]); up.x.push_back(xr); up.y.push_back(m->u + r * F);
+            down.w.push_back(m->w2[e]);
+            down.x.push_back(XQ{xqh.planes + r * 3 * F, xqh.stats + r * (F / 32)});
+            down.y.push_back(out + r * H);
+        }
+    }
+    rc = run_jobs(up, sm, st);
+    if (!rc) rc = run_mm_jobs(upm, xhx, R, sm, st);
+    cudaLaunchAttribute attr[1];
+    if (!rc && any_mm) {
+        cudaLaunchConfig_t cfg = pdl(dim3(1184), dim3(256), st, attr);
+        rc = cuda_error(cudaLaunchKernelEx(&cfg, swiglu_kernel, m->g, (const float*)m->u, R * F), "swiglu kernel");
+        if (!rc) rc = launch_xh_stage(m->g, R, F, xhh, st);
+        if (!rc && any_pipe) rc = launch_xquant(m->g, R, F, xqh, st);
+    } else if (!rc) {
+        rc = launch_xquant_swiglu(m->g, m->u, R, F, xqh, st);
+    }
+    if (!rc) rc = run_jobs(down, sm, st);
+    if (!rc) rc = run_mm_jobs(downm, xhh, R, sm, st);
+    return rc;
+}
+
+// Router and permutation of the T local tokens; offs and perm are copied to
+// the host (one stream synchronisation).
+int route(rq_moe* m, const float* xs, int64_t T, std::vector<int32_t>& offs, std::vector<int32_t>& perm,
+          cudaStream_t st) {
+    const int E = m->E, k = m->k;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl(dim3((unsigned)T), dim3((unsigned)(32 * E)), st, attr);
+    int rc = cuda_error(cudaLaunchKernelEx(&cfg, router_kernel, xs, (const float*)m->router, m->H, E, k, m->logits,
+                                           m->ids, m->wts), "router kernel");
+    if (!rc) {
+        cudaLaunchConfig_t cfg2 = pdl(dim3(1), dim3(1024), st, attr);
+        rc = cuda_error(cudaLaunchKernelEx(&cfg2, permute_kernel, (const int32_t*)m->ids, (const float*)m->wts, T, E,
+                                           k, m->offs, m->perm, m->slot_w, m->tok_slot), "permute kernel");
+    }
+    offs.assign((size_t)E + 1, 0);
+    perm.assign((size_t)(T * k), 0);
+    if (!rc) rc = cuda_error(cudaMemcpyAsync(offs.data(), m->offs, sizeof(int32_t) * (size_t)(E + 1),
+                                             cudaMemcpyDeviceToHost, st), "offsets copy");
+    if (!rc) rc = cuda_error(cudaMemcpyAsync(perm.data(), m->perm, sizeof(int32_t) * (size_t)(T * k),
+                                             cudaMemcpyDeviceToHost, st), "perm copy");
+    if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "routing sync");
+    return rc;
+}
+
+int combine(rq_moe* m, int64_t T, float* yd, cudaStream_t st) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl(dim3((unsigned)std::min<int64_t>(64, (m->H + 255) / 256), (unsigned)T), dim3(256),
+                                 st, attr);
+    return cuda_error(cudaLaunchKernelEx(&cfg, combine_kernel, (const float*)m->o, (const float*)m->slot_w,
+                                         (const int32_t*)m->tok_slot, T, m->k, m->H, yd), "combine kernel");
+}
+
+// Shared front and back of both forwards: x to the device (when needed),
+// then after `body` y back to the host and the routing outputs.
+template <class Body>
+int moe_call(rq_moe* m, const float* x, float* y, int64_t T, int32_t* ids_out, int32_t* perm_out, cudaStream_t st,
+             int world, Body&& body) {
+    int rc = ensure_t(m, T, world);
+    if (rc) return rc;
+    const int64_t H = m->H, S = T * m->k;
+    const bool x_dev = is_device(x), y_dev = is_device(y);
+    const float* xs = x;
+    if (!x_dev || (reinterpret_cast<uintptr_t>(x) & 15)) {
+        rc = cuda_error(cudaMemcpyAsync(m->xd, x, sizeof(float) * (size_t)(T * H), cudaMemcpyDefault, st), "x copy");
+        if (rc) return rc;
+        xs = m->xd;
+    }
+    float* yd = y_dev ? y : m->yd;
+    std::vector<int32_t> offs, perm;
+    rc = route(m, xs, T, offs, perm, st);
+    if (!rc) rc = body(xs, offs, perm);
+    if (!rc) rc = combine(m, T, yd, st);
+    if (!rc && !y_dev)
+        rc = cuda_error(cudaMemcpyAsync(y, yd, sizeof(float) * (size_t)(T * H), cudaMemcpyDeviceToHost, st), "y copy");
+    if (!rc && ids_out)
+        rc = cuda_error(cudaMemcpyAsync(ids_out, m->ids, sizeof(int32_t) * (size_t)S, cudaMemcpyDefault, st),
+                        "ids copy");
+    if (!rc && perm_out) memcpy(perm_out, perm.data(), sizeof(int32_t) * (size_t)S);
+    if (!rc && (!y_dev || ids_out)) rc = cuda_error(cudaStreamSynchronize(st), "moe sync");
+    return rc;
+}
+
 }  // namespace
 }  // namespace rq
 
@@ -340,13 +503,17 @@ int rq_moe_create(rq_ctx* ctx, int n_experts, int top_k, int64_t hidden, int64_t
         return set_error(RQ_ERR_INVALID, "rq_moe_create: need 1 <= top_k <= n_experts <= 32");
     if (hidden <= 0 || ffn <= 0 || hidden % 32 || ffn % 32)
         return set_error(RQ_ERR_INVALID, "rq_moe_create: hidden and ffn must be positive multiples of 32");
+    const int W = tp_world(ctx), me = tp_rank(ctx);
+    int present = -1;
     for (int e = 0; e < n_experts; e++) {
+        if (!w1[e] && !w3[e] && !w2[e] && W > 1 && e % W != me) continue;  // another rank's expert
         if (!w1[e] || !w3[e] || !w2[e]) return set_error(RQ_ERR_INVALID, "rq_moe_create: expert %d missing", e);
+        if (present < 0) present = e;
         if (w1[e]->out != ffn || w1[e]->in != hidden || w3[e]->out != ffn || w3[e]->in != hidden ||
             w2[e]->out != hidden || w2[e]->in != ffn)
             return set_error(RQ_ERR_INVALID, "rq_moe_create: expert %d shapes must be w1,w3 [%lld,%lld], w2 [%lld,%lld]",
                              e, (long long)ffn, (long long)hidden, (long long)hidden, (long long)ffn);
-        if (w1[e]->type != w1[0]->type || w3[e]->type != w1[0]->type || w2[e]->type != w2[0]->type)
+        if (w1[e]->type != w1[present]->type || w3[e]->type != w1[present]->type || w2[e]->type != w2[present]->type)
             return set_error(RQ_ERR_INVALID, "rq_moe_create: experts must share weight types");
     }
     Guard g(ctx->device);
@@ -376,7 +543,8 @@ int rq_moe_create(rq_ctx* ctx, int n_experts, int top_k, int64_t hidden, int64_t
 int rq_moe_free(rq_moe* m) {
     if (!m) return RQ_OK;
     Guard g(m->ctx->device);
-    for (void* p : m->bufs) cudaFree(p);
+    for (void* p : m->bufs_t) cudaFree(p);
+    for (void* p : m->bufs_r) cudaFree(p);
     cudaFree(m->router);
     delete m;
     return RQ_OK;
@@ -387,119 +555,100 @@ int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
     if (!ctx || !m || !x || !y) return set_error(RQ_ERR_INVALID, "rq_moe_forward: NULL argument");
     if (T < 0) return set_error(RQ_ERR_INVALID, "rq_moe_forward: T = %lld", (long long)T);
     if (T == 0) return RQ_OK;
+    for (int e = 0; e < m->E; e++)
+        if (!m->w1[(size_t)e])
+            return set_error(RQ_ERR_INVALID, "rq_moe_forward: expert %d is not on this rank (use rq_moe_forward_ep)", e);
     Guard gd(m->ctx->device);
     cudaStream_t st = (cudaStream_t)stream;
-    int rc = ensure_cap(m, T);
-    if (rc) return rc;
-    const int E = m->E, k = m->k;
-    const int64_t H = m->H, F = m->F, S = T * k;
-    const bool x_dev = is_device(x), y_dev = is_device(y);
-    const float* xs = x;
-    if (!x_dev || (reinterpret_cast<uintptr_t>(x) & 15)) {
-        rc = cuda_error(cudaMemcpyAsync(m->xd, x, sizeof(float) * (size_t)(T * H), cudaMemcpyDefault, st), "x copy");
+    const int64_t S = T * m->k;
+    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, 1,
+                    [&](const float* xs, const std::vector<int32_t>& offs, const std::vector<int32_t>&) {
+                        int rc = ensure_r(m, S);
+                        // token rows in slot (expert-major) order
+                        if (!rc) rc = launch_gather(xs, m->perm, S, m->H, m->xg, st);
+                        if (rc) return rc;
+                        std::vector<Seg> segs;
+                        for (int e = 0; e < m->E; e++) {
+                            const int64_t n = offs[(size_t)e + 1] - offs[(size_t)e];
+                            if (n) segs.push_back(Seg{e, offs[(size_t)e], n});
+                        }
+                        return expert_ffn(m, m->xg, S, segs, m->o, st);
+                    });
+}
+
+int rq_moe_forward_ep(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
+                      int32_t* expert_ids_out, int32_t* perm_out, void* stream) {
+    if (!ctx || !m || (T > 0 && (!x || !y))) return set_error(RQ_ERR_INVALID, "rq_moe_forward_ep: NULL argument");
+    if (T < 0) return set_error(RQ_ERR_INVALID, "rq_moe_forward_ep: T = %lld", (long long)T);
+    if (!ctx->tp) return set_error(RQ_ERR_INVALID, "rq_moe_forward_ep: no communicator (rq_tp_init)");
+    const int W = tp_world(ctx), me = tp_rank(ctx), E = m->E;
+    for (int e = me; e < E; e += W)
+        if (!m->w1[(size_t)e])
+            return set_error(RQ_ERR_INVALID, "rq_moe_forward_ep: expert %d belongs to rank %d and is missing", e, me);
+    Guard gd(m->ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    // every rank takes the same collective steps, also for T = 0
+    const int64_t S = T * m->k, H = m->H;
+    auto body = [&](const float* xs, const std::vector<int32_t>& offs, const std::vector<int32_t>& perm) {
+        // slot counts of every rank
+        std::vector<int32_t> mine((size_t)E);
+        for (int e = 0; e < E; e++) mine[(size_t)e] = offs[(size_t)e + 1] - offs[(size_t)e];
+        int rc = cuda_error(cudaMemcpyAsync(m->cnt + (size_t)me * E, mine.data(), sizeof(int32_t) * (size_t)E,
+                                            cudaMemcpyHostToDevice, st), "counts copy");
+        if (!rc) rc = tp_allgather_bytes(ctx, m->cnt + (size_t)me * E, m->cnt, (int64_t)sizeof(int32_t) * E, st);
+        std::vector<int32_t> cnt((size_t)W * E);
+        if (!rc) rc = cuda_error(cudaMemcpyAsync(cnt.data(), m->cnt, sizeof(int32_t) * cnt.size(),
+                                                 cudaMemcpyDeviceToHost, st), "counts copy back");
+        if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "counts sync");
         if (rc) return rc;
-        xs = m->xd;
-    }
-    float* yd = y_dev ? y : m->yd;
-    const int sm = m->ctx->sm_count;
-    XQ xqx = xq_view(m->xq_x, T, H);
-    rc = launch_xquant(xs, T, H, xqx, st);
-    cudaLaunchAttribute attr[1];
-    if (!rc) {
-        cudaLaunchConfig_t cfg = pdl(dim3((unsigned)T), dim3((unsigned)(32 * E)), st, attr);
-        rc = cuda_error(cudaLaunchKernelEx(&cfg, router_kernel, xs, (const float*)m->router, H, E, k,
-                                           m->logits, m->ids, m->wts), "router kernel");
-    }
-    if (!rc) {
-        cudaLaunchConfig_t cfg = pdl(dim3(1), dim3(1024), st, attr);
-        rc = cuda_error(cudaLaunchKernelEx(&cfg, permute_kernel, (const int32_t*)m->ids, (const float*)m->wts, T,
-                                           E, k, m->offs, m->perm, m->slot_w, m->tok_slot), "permute kernel");
-    }
-    std::vector<int32_t> offs((size_t)E + 1), perm((size_t)S);
-    if (!rc) rc = cuda_error(cudaMemcpyAsync(offs.data(), m->offs, sizeof(int32_t) * (size_t)(E + 1),
-                                             cudaMemcpyDeviceToHost, st), "offsets copy");
-    if (!rc) rc = cuda_error(cudaMemcpyAsync(perm.data(), m->perm, sizeof(int32_t) * (size_t)S,
-                                             cudaMemcpyDeviceToHost, st), "perm copy");
-    if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "routing sync");
-    if (rc) return rc;
-    // Experts with at least kMinTensorM tokens run on the tensor-core kernel
-    // (tiles of up to 8 slots, weights read once per tile); the others run
-    // one M=1 pipeline job per (expert, slot).
-    auto use_mm = [&](int e) {
-        return offs[(size_t)e + 1] - offs[(size_t)e] >= kMinTensorM && mm_small_supported(m->w1[(size_t)e]) &&
-               mm_small_supported(m->w3[(size_t)e]) && mm_small_supported(m->w2[(size_t)e]);
-    };
-    bool any_mm = false, any_pipe = false;
-    for (int e = 0; e < E; e++) {
-        if (offs[(size_t)e + 1] == offs[(size_t)e]) continue;
-        if (use_mm(e)) any_mm = true;
-        else any_pipe = true;
-    }
-    const XH xhx = xh_at(m->xh_x, S, H), xhh = xh_at(m->xh_h, S, F);
-    if (any_mm) {
-        cudaLaunchConfig_t cfg = pdl(dim3((unsigned)std::min<int64_t>(32, (H + 255) / 256), (unsigned)S), dim3(256),
-                                     st, attr);
-        rc = cuda_error(cudaLaunchKernelEx(&cfg, gather_kernel, xs, (const int32_t*)m->perm, H, m->xg), "gather kernel");
-        if (!rc) rc = launch_xh_stage(m->xg, S, H, xhx, st);
-        if (rc) return rc;
-    }
-    // gate and up products
-    JobList up;
-    std::vector<MMJobDesc> upm, downm;
-    for (int e = 0; e < E; e++) {
-        const int32_t s0 = offs[(size_t)e], s1 = offs[(size_t)e + 1];
-        if (use_mm(e)) {
-            for (int32_t t0 = s0; t0 < s1; t0 += 8) {
-                const int n = std::min<int32_t>(8, s1 - t0);
-                upm.push_back(MMJobDesc{m->w1[(size_t)e], t0, n, m->g + (int64_t)t0 * F, nullptr});
-                upm.push_back(MMJobDesc{m->w3[(size_t)e], t0, n, m->u + (int64_t)t0 * F, nullptr});
-                downm.push_back(MMJobDesc{m->w2[(size_t)e], t0, n, m->o + (int64_t)t0 * H, nullptr});
+        // send order: destination rank, then its experts ascending, then slots
+        std::vector<int32_t> idx_send((size_t)S), pos_of_slot((size_t)S);
+        std::vector<int64_t> sbytes((size_t)W, 0), soff((size_t)W, 0), rbytes((size_t)W, 0), roff((size_t)W, 0);
+        int64_t p = 0;
+        for (int d = 0; d < W; d++) {
+            soff[(size_t)d] = p * H * 4;
+            for (int e = d; e < E; e += W)
+                for (int32_t sl = offs[(size_t)e]; sl < offs[(size_t)e + 1]; sl++, p++) {
+                    idx_send[(size_t)p] = perm[(size_t)sl];
+                    pos_of_slot[(size_t)sl] = (int32_t)p;
+                }
+            sbytes[(size_t)d] = p * H * 4 - soff[(size_t)d];
+        }
+        // receive layout: source rank, then this rank's experts ascending
+        std::vector<Seg> segs;
+        int64_t R = 0;
+        for (int sr = 0; sr < W; sr++) {
+            roff[(size_t)sr] = R * H * 4;
+            for (int e = me; e < E; e += W) {
+                const int64_t n = cnt[(size_t)sr * E + e];
+                if (n) segs.push_back(Seg{e, R, n});
+                R += n;
             }
-            continue;
+            rbytes[(size_t)sr] = R * H * 4 - roff[(size_t)sr];
         }
-        for (int32_t s = s0; s < s1; s++) {
-            const int64_t t = perm[(size_t)s];
-            const XQ xr{xqx.planes + t * 3 * H, xqx.stats + t * (H / 32)};
-            up.w.push_back(m->w1[(size_t)e]); up.x.push_back(xr); up.y.push_back(m->g + (int64_t)s * F);
-            up.w.push_back(m->w3[(size_t)e]); up.x.push_back(xr); up.y.push_back(m->u + (int64_t)s * F);
-        }
+        rc = ensure_r(m, R);
+        if (!rc && S)
+            rc = cuda_error(cudaMemcpyAsync(m->idx, idx_send.data(), sizeof(int32_t) * (size_t)S,
+                                            cudaMemcpyHostToDevice, st), "send index copy");
+        if (!rc) rc = launch_gather(xs, m->idx, S, H, m->xg, st);
+        if (!rc) rc = tp_alltoallv_bytes(ctx, m->xg, sbytes.data(), soff.data(), m->xr, rbytes.data(), roff.data(), st);
+        if (!rc) rc = expert_ffn(m, m->xr, R, segs, m->fo, st);
+        // results back to their tokens' ranks, then into slot order
+        if (!rc) rc = tp_alltoallv_bytes(ctx, m->fo, rbytes.data(), roff.data(), m->osend, sbytes.data(), soff.data(), st);
+        if (!rc && S)
+            rc = cuda_error(cudaMemcpyAsync(m->idx, pos_of_slot.data(), sizeof(int32_t) * (size_t)S,
+                                            cudaMemcpyHostToDevice, st), "slot index copy");
+        if (!rc) rc = launch_gather(m->osend, m->idx, S, H, m->o, st);
+        return rc;
+    };
+    if (T == 0) {
+        // no local tokens: still take part in the exchange
+        int rc = ensure_t(m, 1, W);
+        if (rc) return rc;
+        std::vector<int32_t> offs((size_t)E + 1, 0), perm;
+        return body(x, offs, perm);
     }
-    rc = run_jobs(up, sm, st);
-    if (!rc) rc = run_mm_jobs(upm, xhx, S, sm, st);
-    XQ xqh = xq_view(m->xq_h, S, F);
-    if (!rc && any_mm) {
-        cudaLaunchConfig_t cfg = pdl(dim3(1184), dim3(256), st, attr);
-        rc = cuda_error(cudaLaunchKernelEx(&cfg, swiglu_kernel, m->g, (const float*)m->u, S * F), "swiglu kernel");
-        if (!rc) rc = launch_xh_stage(m->g, S, F, xhh, st);
-        if (!rc && any_pipe) rc = launch_xquant(m->g, S, F, xqh, st);
-    } else if (!rc) {
-        rc = launch_xquant_swiglu(m->g, m->u, S, F, xqh, st);
-    }
-    if (rc) return rc;
-    JobList down;
-    for (int e = 0; e < E; e++) {
-        if (use_mm(e)) continue;
-        for (int32_t s = offs[(size_t)e]; s < offs[(size_t)e + 1]; s++) {
-            down.w.push_back(m->w2[(size_t)e]);
-            down.x.push_back(XQ{xqh.planes + (int64_t)s * 3 * F, xqh.stats + (int64_t)s * (F / 32)});
-            down.y.push_back(m->o + (int64_t)s * H);
-        }
-    }
-    rc = run_jobs(down, sm, st);
-    if (!rc) rc = run_mm_jobs(downm, xhh, S, sm, st);
-    if (!rc) {
-        cudaLaunchConfig_t cfg = pdl(dim3((unsigned)std::min<int64_t>(64, (H + 255) / 256), (unsigned)T), dim3(256), st, attr);
-        rc = cuda_error(cudaLaunchKernelEx(&cfg, combine_kernel, (const float*)m->o, (const float*)m->slot_w,
-                                           (const int32_t*)m->tok_slot, T, k, H, yd), "combine kernel");
-    }
-    if (!rc && !y_dev)
-        rc = cuda_error(cudaMemcpyAsync(y, yd, sizeof(float) * (size_t)(T * H), cudaMemcpyDeviceToHost, st), "y copy");
-    if (!rc && expert_ids_out)
-        rc = cuda_error(cudaMemcpyAsync(expert_ids_out, m->ids, sizeof(int32_t) * (size_t)S, cudaMemcpyDefault, st),
-                        "ids copy");
-    if (!rc && perm_out) memcpy(perm_out, perm.data(), sizeof(int32_t) * (size_t)S);
-    if (!rc && (!y_dev || expert_ids_out)) rc = cuda_error(cudaStreamSynchronize(st), "moe sync");
-    return rc;
+    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, W, body);
 }
 
 }  // extern "C"

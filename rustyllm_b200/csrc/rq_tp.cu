@@ -73,6 +73,39 @@ int tp_allreduce(rq_ctx* ctx, const void* in, void* out, int64_t n, int dtype, i
     return settle(c, ncclAllReduce(in, out, (size_t)n, dt, ro, c->comm, st), "ncclAllReduce", kOpTimeoutMs);
 }
 
+int tp_allgather_bytes(rq_ctx* ctx, const void* in, void* out, int64_t nbytes, cudaStream_t st) {
+    TPComm* c = ctx->tp;
+    if (!c || !c->comm) return set_error(RQ_ERR_INVALID, "tensor-parallel communicator not initialised");
+    return settle(c, ncclAllGather(in, out, (size_t)nbytes, ncclInt8, c->comm, st), "ncclAllGather", kOpTimeoutMs);
+}
+
+int tp_alltoallv_bytes(rq_ctx* ctx, const void* send, const int64_t* send_bytes, const int64_t* send_off, void* recv,
+                       const int64_t* recv_bytes, const int64_t* recv_off, cudaStream_t st) {
+    TPComm* c = ctx->tp;
+    if (!c || !c->comm) return set_error(RQ_ERR_INVALID, "tensor-parallel communicator not initialised");
+    // this rank's own share is a device copy
+    if (send_bytes[c->rank] != recv_bytes[c->rank])
+        return set_error(RQ_ERR_INVALID, "all-to-all: self send %lld != self receive %lld bytes",
+                         (long long)send_bytes[c->rank], (long long)recv_bytes[c->rank]);
+    if (send_bytes[c->rank] > 0) {
+        int rc = cuda_error(cudaMemcpyAsync((uint8_t*)recv + recv_off[c->rank], (const uint8_t*)send + send_off[c->rank],
+                                            (size_t)send_bytes[c->rank], cudaMemcpyDeviceToDevice, st),
+                            "all-to-all self copy");
+        if (rc) return rc;
+    }
+    ncclResult_t r = ncclGroupStart();
+    for (int peer = 0; peer < c->world && (r == ncclSuccess || r == ncclInProgress); peer++) {
+        if (peer == c->rank) continue;
+        if (send_bytes[peer] > 0)
+            r = ncclSend((const uint8_t*)send + send_off[peer], (size_t)send_bytes[peer], ncclInt8, peer, c->comm, st);
+        if ((r == ncclSuccess || r == ncclInProgress) && recv_bytes[peer] > 0)
+            r = ncclRecv((uint8_t*)recv + recv_off[peer], (size_t)recv_bytes[peer], ncclInt8, peer, c->comm, st);
+    }
+    const ncclResult_t r2 = ncclGroupEnd();
+    if (r == ncclSuccess || r == ncclInProgress) r = r2;
+    return settle(c, r, "all-to-all (ncclSend/ncclRecv)", kOpTimeoutMs);
+}
+
 void tp_destroy(rq_ctx* ctx) {
     if (!ctx->tp) return;
     if (ctx->tp->comm) {

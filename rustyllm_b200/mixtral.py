@@ -23,13 +23,20 @@ except Exception:  # pragma: no cover
 
 
 class SparseMoe:
-    def __init__(self, router_w, experts: list, top_k: int = 2, device: int = 0):
-        """experts: [(w1 gate, w2 down, w3 up) QWeight triples], as Expert."""
+    def __init__(self, router_w, experts: list, top_k: int = 2, device: int = 0,
+                 expert_parallel: bool = False):
+        """experts: [(w1 gate, w2 down, w3 up) QWeight triples], as Expert.
+        With expert_parallel (after rustyllm_b200.tp.init_from_torch), expert
+        e lives on rank e % world and the entries of other ranks are None;
+        forward takes this rank's tokens."""
         self.ctx = Context.get(device)
+        self.expert_parallel = expert_parallel
         r = np.ascontiguousarray(router_w, dtype=np.float32)
         E, H = r.shape
-        F = experts[0][0].out
-        arr = lambda ws: (ctypes.c_void_p * E)(*[w.handle.value for w in ws])  # noqa: E731
+        F = next(e for e in experts if e is not None)[0].out
+        arr = lambda ws: (ctypes.c_void_p * E)(*[w.handle.value if w is not None else None  # noqa: E731
+                                                   for w in ws])
+        experts = [e if e is not None else (None, None, None) for e in experts]
         h = ctypes.c_void_p()
         check(_lib.lib().rq_moe_create(self.ctx.handle, E, top_k, H, F, r.ctypes.data,
                                        arr([e[0] for e in experts]), arr([e[2] for e in experts]),
@@ -53,8 +60,8 @@ class SparseMoe:
             xp, yp, stream = x2.ctypes.data, y.ctypes.data, 0
         ids = np.empty((T, self.k), dtype=np.int32)
         perm = np.empty(T * self.k, dtype=np.int32)
-        check(_lib.lib().rq_moe_forward(self.ctx.handle, self.handle, xp, yp, T, ids.ctypes.data,
-                                        perm.ctypes.data, stream))
+        fwd = _lib.lib().rq_moe_forward_ep if self.expert_parallel else _lib.lib().rq_moe_forward
+        check(fwd(self.ctx.handle, self.handle, xp, yp, T, ids.ctypes.data, perm.ctypes.data, stream))
         return y.reshape(shape), ids, perm
 
     def forward(self, xs):
