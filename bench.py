@@ -296,6 +296,64 @@ def moe_sweep(device: int, seed: int = 4321) -> dict:
     return res
 
 
+def moe_ep_sweep(device: int, pg, seed: int = 4321) -> dict:
+    """The Mixtral layer expert-parallel over the ranks (rq_moe_forward_ep):
+    expert e on rank e % world, every rank with its own T tokens (weak
+    scaling), NCCL all-to-all dispatch and return.  tok/s = world * T / the
+    slowest rank's time per forward."""
+    import torch
+    from rustyllm_b200 import Context, QWeight
+    from rustyllm_b200 import tp as tpmod
+    from rustyllm_b200.mixtral import SparseMoe
+    E, H, F, k = MIXTRAL["E"], MIXTRAL["H"], MIXTRAL["F"], MIXTRAL["k"]
+    dev = torch.device("cuda", device)
+    ctx = Context.get(device)
+    world, rank = tpmod.init_from_torch(ctx)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    router = (torch.randn(E, H, device=dev, generator=g) * 0.02).cpu().numpy()
+    experts = []
+    for e in range(E):
+        ge = torch.Generator(device=dev).manual_seed(seed + 1 + e)
+        if e % world != rank:
+            experts.append(None)
+            continue
+        trip = []
+        for o, i in ((F, H), (H, F), (F, H)):
+            wf = torch.randn(o, i, device=dev, generator=ge) * 0.02
+            trip.append(QWeight.quantize(ctx, Q4_K, wf))
+            del wf
+        experts.append(tuple(trip))
+    moe = SparseMoe(router, experts, top_k=k, device=device, expert_parallel=True)
+    res = {}
+    for T in MOE_T:
+        x = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(99 + rank))
+        for _ in range(2):
+            moe.forward(x)
+        torch.cuda.synchronize()
+        pg.barrier()
+        reps = 20 if T < 512 else 5
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            moe.forward(x)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+        res[str(T)] = {"ms": round(ms, 4), "tokens_per_rank": T, "tok_per_s": round(world * T / (ms / 1e3), 1)}
+    res["config"] = (f"Mixtral-8x7B MoE layer expert-parallel over {world} GPUs (expert e on rank e % {world}), "
+                     "T tokens per rank, NCCL all-to-all")
+    moe.close()
+    for trip in experts:
+        if trip:
+            for w in trip:
+                w.free()
+    tpmod.finalize(ctx)
+    torch.cuda.empty_cache()
+    return res
+
+
 LLAMA70B = dict(hidden=8192, intermediate=28672, n_heads=64, n_kv_heads=8, head_dim=128,
                 n_layers=80, vocab=32000, max_seq=64, max_batch_tokens=32, rms_eps=1e-5,
                 rope_theta=10000.0)
@@ -542,8 +600,8 @@ def run_gpu(args) -> None:
         host = {n: weights[0][k].download() for k, (n, _, _) in enumerate(SHAPES)}
         cpu = cpu_baseline(host, seconds=args.cpu_seconds)
     moe = None
-    if not args.no_moe and world == 1:
-        moe = moe_sweep(local)
+    if not args.no_moe:
+        moe = moe_sweep(local) if world == 1 else moe_ep_sweep(local, pg)
     dec = None
     if not args.no_decode:
         del graphs, shape_graphs, dom
