@@ -197,6 +197,55 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+Q4_0, Q3_K = 2, 11
+Q3K_BYTES = lambda n_in, n_out: n_out * (n_in // 256) * 110  # noqa: E731
+Q40_BYTES = lambda n_in, n_out: n_out * (n_in // 32) * 18  # noqa: E731
+
+
+def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
+    """Config 1: the 4096x4096 Q4_0 matvec (M=1) over 16 rotating copies
+    (151 MB > L2); config 2's Q3_K sweep: the seven 70B shapes in Q3_K, each
+    over 4 rotating copies.  GB/s = GGML weight bytes + 4 (in + out) per call."""
+    import torch
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200._lib import check
+    res = {}
+
+    def sweep(qtype, shapes, copies, nbytes):
+        out = {}
+        for name, i, o in shapes:
+            ws = []
+            for _ in range(copies):
+                wf = torch.randn(o, i, device=dev, generator=g) * 0.02
+                ws.append(QWeight.quantize(ctx, qtype, wf))
+                del wf
+            x = torch.randn(1, i, device=dev, generator=g)
+            y = torch.empty(1, o, device=dev)
+
+            def run(st, ws=ws, x=x, y=y):
+                for w in ws:
+                    check(L.rq_linear(ctx.handle, w.handle, x.data_ptr(), y.data_ptr(), 1, st))
+            with torch.cuda.stream(stream):
+                run(stream.cuda_stream)
+            stream.synchronize()
+            gr = capture(run)
+            with torch.cuda.stream(stream):
+                gr.replay()
+            reps = 10
+            ms = timed(lambda r: gr.replay(), reps) / (reps * copies)
+            out[name] = round((nbytes(i, o) + 4 * (i + o)) / (ms / 1e3) / 1e9, 1)
+            del gr
+            for w in ws:
+                w.free()
+        return out
+
+    res["q4_0_4096x4096_gbs"] = sweep(Q4_0, [("q4_0", 4096, 4096)], 16, Q40_BYTES)["q4_0"]
+    res["q3_k_per_shape_gbs"] = sweep(Q3_K, SHAPES, 4, Q3K_BYTES)
+    res["note"] = ("single rq_linear calls (activation staging + M=1 pipeline), graph-replayed over "
+                   "rotating weight copies larger than L2")
+    return res
+
+
 SMALL_M = (2, 3, 4, 8, 16)
 
 
@@ -553,6 +602,9 @@ def run_gpu(args) -> None:
     small_m = None
     if not args.no_small_m:
         small_m = small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g)
+    formats = None
+    if not args.no_small_m:
+        formats = other_formats(L, ctx, stream, timed, capture, dev, g)
     clk = clocks.stop()
     barrier()
     torch.cuda.synchronize()
@@ -652,11 +704,59 @@ def run_gpu(args) -> None:
             line["small_m_q4k"] = small_m
         if moe is not None:
             line["mixtral_moe"] = moe
+        if formats is not None:
+            line["other_formats"] = formats
         print(json.dumps(line), flush=True)
     del graphs, shape_graphs, dom
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()
+
+
+def run_case(name: str) -> None:
+    """A few launches of one kernel for an ncu capture: 'pipe_gate_up' (the
+    gate+up rq_linear_batch of one 70B layer, M=1) or 'mm_gate_m8' (gate_proj
+    8192 -> 28672 at M=8 on the tensor-core kernel).  Prints the per-call
+    time measured without the profiler."""
+    import ctypes
+
+    import torch
+    from rustyllm_b200 import Context, QWeight
+    from rustyllm_b200._lib import check, lib
+    L = lib()
+    ctx = Context.get(0)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ws = [QWeight.quantize(ctx, Q4_K, torch.randn(28672, 8192, device="cuda", generator=g) * 0.02)
+          for _ in range(2)]
+    s = torch.cuda.current_stream().cuda_stream
+    arr = lambda v: (ctypes.c_void_p * len(v))(*v)  # noqa: E731
+    if name == "pipe_gate_up":
+        x = torch.randn(1, 8192, device="cuda", generator=g)
+        ys = [torch.empty(1, 28672, device="cuda") for _ in range(2)]
+
+        def call():
+            check(L.rq_linear_batch(ctx.handle, 2, arr([w.handle.value for w in ws]), arr([x.data_ptr()] * 2),
+                                    arr([y.data_ptr() for y in ys]), s))
+        nbytes = 2 * Q4K_BYTES(8192, 28672)
+    else:
+        x = torch.randn(8, 8192, device="cuda", generator=g)
+        y = torch.empty(8, 28672, device="cuda")
+
+        def call():
+            check(L.rq_linear(ctx.handle, ws[0].handle, x.data_ptr(), y.data_ptr(), 8, s))
+        nbytes = Q4K_BYTES(8192, 28672)
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 10
+    print(json.dumps({"case": name, "us_per_call": round(ms * 1e3, 2),
+                      "weight_gbs": round(nbytes / (ms / 1e3) / 1e9, 1)}), flush=True)
 
 
 def main():
@@ -673,7 +773,12 @@ def main():
     ap.add_argument("--no-moe", action="store_true", help="skip the Mixtral MoE layer sweep")
     ap.add_argument("--decode-layers", type=int, default=None,
                     help="layers of the decode model (default 80; fewer for profiling)")
+    ap.add_argument("--case", choices=["pipe_gate_up", "mm_gate_m8"], default=None,
+                    help="run a few launches of one kernel (for profiling) and exit")
     args = ap.parse_args()
+    if args.case:
+        run_case(args.case)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
