@@ -238,8 +238,15 @@ RQ_API int rq_llama_forward(rq_llama* m, const int32_t* tokens, int64_t T, int64
                             float* logits, int32_t* next_token, void* stream);
 /* One greedy decode step entirely on the device (token and position read
  * from and written to device memory), so it can be captured in a CUDA graph
- * and replayed; each step appends its token to the device token list. */
+ * and replayed; each step appends its token to the device token list.  By
+ * default a chain of per-layer kernels; rq_llama_set_fused(m, 1) makes the
+ * step (one GPU, one weight type) a single persistent launch that streams the
+ * weights through grid-wide phases and computes the same bits. */
 RQ_API int rq_llama_decode_step(rq_llama* m, void* stream);
+RQ_API int rq_llama_set_fused(rq_llama* m, int enable);
+/* RQ_ERR_TIMEOUT (and clears it) when a wait of a one-launch step timed
+ * out since the last call; synchronous. */
+RQ_API int rq_llama_status(rq_llama* m);
 /* Tokens appended since the last reset (count may exceed cap), and the
  * current position.  Synchronous. */
 RQ_API int rq_llama_tokens(rq_llama* m, int32_t* out, int64_t cap, int64_t* count,

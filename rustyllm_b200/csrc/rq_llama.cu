@@ -26,6 +26,8 @@
 #include <algorithm>
 #include <vector>
 
+#include "rq_attn.cuh"
+#include "rq_decode.cuh"
 #include "rq_mv_common.cuh"
 
 struct rq_llama {
@@ -64,6 +66,13 @@ struct rq_llama {
     int32_t* pos;              // current position (KV length before this step)
     int32_t* out;              // [max_seq] generated tokens
     int32_t* nout;
+    // one-launch decode step (rq_decode.cu)
+    rq::DecLayer* dlayers;              // device copy of the per-layer table
+    std::vector<rq::DecLayer> hlayers;  // host copy
+    std::vector<bool> layer_set;
+    unsigned* bar;                      // grid-barrier arrivals
+    int* derr;                          // error word of the step
+    bool fused = false;                 // rq_llama_set_fused
     std::vector<void*> allocs;
 };
 
@@ -189,99 +198,18 @@ __global__ void attention_kernel(const float* __restrict__ q, const float* __res
 }
 
 // Decode (T = 1) attention fused with RoPE, the KV-cache append and the
-// staging of the head's output for o_proj.  One CTA per head h: it ropes its
-// q and its own copy of the new k (position p = *pos), writes k and v to the
-// cache when it is the first head of its kv group, scores the p cached keys
-// plus the new one, softmax, weighted values, and stages the head_dim outputs
-// (head_dim / 32 blocks of row 0) into xq.  No CTA reads a cache slot written
-// in this launch.  block 128 threads, dynamic smem (max_seq + 3*hd) floats.
-__global__ void attn_decode_kernel(const float* __restrict__ q, const float* __restrict__ k,
-                                   const float* __restrict__ v, float* __restrict__ kc,
-                                   float* __restrict__ vc, const float* __restrict__ cos_t,
-                                   const float* __restrict__ sin_t, const int32_t* __restrict__ pos,
-                                   int n_heads, int n_kv, int hd, int max_seq, int8_t* __restrict__ planes,
-                                   float4* __restrict__ stats) {
+// staging of the head's output for o_proj (attn_decode_head): one CTA of
+// kAttnThreads threads per head, dynamic smem attn_smem_floats floats.
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, float* __restrict__ kc,
+    float* __restrict__ vc, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+    const int32_t* __restrict__ pos, int n_heads, int n_kv, int hd, int max_seq, int8_t* __restrict__ planes,
+    float4* __restrict__ stats) {
     pdl_enter();
     extern __shared__ float sm[];
-    float* sc = sm;                 // [max_seq]
-    float* qs = sm + max_seq;       // [hd] roped q
-    float* kn = qs + hd;            // [hd] roped new k
-    float* vn = kn + hd;            // [hd] new v, later the head output
     __shared__ float red[32];
-    const int h = blockIdx.x, half = hd / 2;
-    const int p = min(*pos, max_seq - 1);
-    const int L = p + 1;
-    const int rep = n_heads / n_kv, kh = h / rep;
-    const float* qh = q + (int64_t)h * hd;
-    const float* ks = k + (int64_t)kh * hd;
-    const float* vs = v + (int64_t)kh * hd;
-    float* K = kc + (int64_t)kh * max_seq * hd;
-    float* V = vc + (int64_t)kh * max_seq * hd;
-    for (int i = threadIdx.x; i < half; i += blockDim.x) {
-        const float c = cos_t[(int64_t)p * half + i], s = sin_t[(int64_t)p * half + i];
-        const float a = qh[i], b = qh[i + half];
-        qs[i] = a * c - b * s;
-        qs[i + half] = a * s + b * c;
-        const float ka = ks[i], kb = ks[i + half];
-        kn[i] = ka * c - kb * s;
-        kn[i + half] = ka * s + kb * c;
-    }
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) vn[i] = vs[i];
-    __syncthreads();
-    if (h % rep == 0)
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-            K[(int64_t)p * hd + i] = kn[i];
-            V[(int64_t)p * hd + i] = vn[i];
-        }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const float inv_sqrt = 1.0f / sqrtf((float)hd);
-    for (int j = warp; j < L; j += nw) {
-        const float* kj = j == p ? kn : K + (int64_t)j * hd;
-        float acc = 0.0f;
-        for (int d = lane; d < hd; d += 32) acc = fmaf(qs[d], kj[d], acc);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) sc[j] = acc * inv_sqrt;
-    }
-    __syncthreads();
-    float mx = -INFINITY;
-    for (int j = threadIdx.x; j < L; j += blockDim.x) mx = fmaxf(mx, sc[j]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    mx = red[0];
-    for (int w = 1; w < nw; w++) mx = fmaxf(mx, red[w]);
-    __syncthreads();
-    float sum = 0.0f;
-    for (int j = threadIdx.x; j < L; j += blockDim.x) {
-        const float e = expf(sc[j] - mx);
-        sc[j] = e;
-        sum += e;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) red[warp] = sum;
-    __syncthreads();
-    sum = 0.0f;
-    for (int w = 0; w < nw; w++) sum += red[w];
-    float outv[2] = {0.0f, 0.0f};
-    for (int d = threadIdx.x, c = 0; d < hd && c < 2; d += blockDim.x, c++) {
-        float acc = 0.0f;
-        for (int j = 0; j < L; j++) acc = fmaf(sc[j] / sum, j == p ? vn[d] : V[(int64_t)j * hd + d], acc);
-        outv[c] = acc;
-    }
-    __syncthreads();  // vn is reused for the output
-    for (int d = threadIdx.x, c = 0; d < hd && c < 2; d += blockDim.x, c++) vn[d] = outv[c];
-    __syncthreads();
-    // stage the head's outputs: blocks (h*hd)/32 .. of row 0 of the o_proj input
-    const int nbh = hd / 32;
-    if (threadIdx.x < nbh) {
-        float blk[32];
-#pragma unroll
-        for (int i = 0; i < 32; i++) blk[i] = vn[threadIdx.x * 32 + i];
-        stage_block(blk, 0, (int64_t)h * nbh + threadIdx.x, (int64_t)n_heads * hd, planes, stats);
-    }
+    attn_decode_head(q, k, v, kc, vc, cos_t, sin_t, pos, n_heads, n_kv, hd, max_seq, planes, stats, (int)blockIdx.x,
+                     (int)threadIdx.x, 0, sm, red);
 }
 
 // hf = rmsnorm(x[row], w) for one row (the lm_head input).
@@ -493,8 +421,9 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
             int8_t* planes = m->xq.planes;
             float4* stats = m->xq.stats;
             void* args[] = {&q, &k, &v, &kc, &vc, &cs, &sn, &pos, &nh, &nkv, &hd, &ms, &planes, &stats};
-            rc = launch_simple((const void*)attn_decode_kernel, dim3((unsigned)nh), dim3(128),
-                               (size_t)(c.max_seq + 3 * c.head_dim) * sizeof(float), st, args, "attention kernel");
+            rc = launch_simple((const void*)attn_decode_kernel, dim3((unsigned)nh), dim3(kAttnThreads),
+                               (size_t)attn_smem_floats(c.max_seq, c.head_dim) * sizeof(float), st, args,
+                               "attention kernel");
             if (rc) return rc;
         } else {
             float* q = m->q;
@@ -604,6 +533,56 @@ struct Guard {
     }
 };
 
+// The one-launch decode step applies with one GPU, every layer set, one
+// weight type throughout and shapes the plan accepts.
+bool fused_plan(rq_llama* m, DecParams& p, size_t* smem) {
+    if (!m->fused || m->W != 1) return false;
+    const rq_llama_config& c = m->cfg;
+    int type = -1;
+    for (int64_t l = 0; l < c.n_layers; l++) {
+        if (!m->layer_set[(size_t)l]) return false;
+        for (int i = 0; i < 7; i++) {
+            const int t = m->layers[(size_t)l].w[i]->type;
+            if (type < 0) type = t;
+            if (t != type) return false;
+        }
+    }
+    p = DecParams{};
+    p.layers = m->dlayers;
+    p.n_layers = (int)c.n_layers;
+    p.type = type;
+    p.H = c.hidden;
+    p.I = m->I_l;
+    p.nq = m->nh_l * c.head_dim;
+    p.nk = m->nkv_l * c.head_dim;
+    p.head_dim = c.head_dim;
+    p.n_heads = m->nh_l;
+    p.n_kv = m->nkv_l;
+    p.max_seq = c.max_seq;
+    p.vocab = m->vocab_l;
+    p.eps = c.rms_eps;
+    p.x = m->x;
+    p.q = m->q;
+    p.k = m->k;
+    p.v = m->v;
+    p.g = m->g;
+    p.u = m->u;
+    p.xq = m->xq;
+    p.rope_cos = m->rope_cos;
+    p.rope_sin = m->rope_sin;
+    p.embed = m->embed;
+    p.ln_f = m->ln_f;
+    p.lm_head = m->lm_head;
+    p.best = m->best;
+    p.tokens = m->tokens;
+    p.pos = m->pos;
+    p.out = m->out;
+    p.nout = m->nout;
+    p.bar = m->bar;
+    p.err = m->derr;
+    return decode_plan(p, m->ctx->sm_count, smem);
+}
+
 }  // namespace
 }  // namespace rq
 
@@ -623,7 +602,7 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
         return set_error(RQ_ERR_INVALID,
                          "rq_llama_create: need n_heads %% n_kv_heads == 0, even head_dim <= 256, and "
                          "hidden, intermediate, n_heads*head_dim multiples of 256");
-    if (c.max_seq * (int64_t)sizeof(float) > 200 * 1024)
+    if (attn_smem_floats(c.max_seq, c.head_dim) * (int64_t)sizeof(float) > 200 * 1024)
         return set_error(RQ_ERR_INVALID, "rq_llama_create: max_seq %lld too large for attention", (long long)c.max_seq);
     const int W = tp_world(ctx), R = tp_rank(ctx);
     if (c.n_kv_heads % W || c.intermediate % (256 * W) || (c.n_heads / W * c.head_dim) % 256 || c.vocab % W)
@@ -675,7 +654,12 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     if (!rc) rc = dalloc(m, &m->pos, 1);
     if (!rc) rc = dalloc(m, &m->out, (size_t)c.max_seq);
     if (!rc) rc = dalloc(m, &m->nout, 1);
+    if (!rc) rc = dalloc(m, &m->dlayers, (size_t)c.n_layers);
+    if (!rc) rc = dalloc(m, &m->bar, 1);
+    if (!rc) rc = dalloc(m, &m->derr, 1);
     if (!rc) {
+        m->hlayers.assign((size_t)c.n_layers, rq::DecLayer{});
+        m->layer_set.assign((size_t)c.n_layers, false);
         m->xq.planes = (int8_t*)xqbuf;
         m->xq.stats = (float4*)(xqbuf + (((size_t)T * 3 * maxin + 255) & ~(size_t)255));
         // RoPE tables as QuantStreamCache::new computes them
@@ -696,6 +680,7 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
         if (!rc) rc = cuda_error(cudaMemset(m->pos, 0, 4), "memset");
         if (!rc) rc = cuda_error(cudaMemset(m->nout, 0, 4), "memset");
         if (!rc) rc = cuda_error(cudaMemset(m->tokens, 0, (size_t)T * 4), "memset");
+        if (!rc) rc = cuda_error(cudaMemset(m->derr, 0, 4), "memset");
     }
     if (rc) {
         for (void* p : m->allocs) cudaFree(p);
@@ -736,7 +721,18 @@ int rq_llama_set_layer(rq_llama* m, int64_t layer, const rq_weight* const* w7, c
     for (int i = 0; i < 7; i++) L.w[i] = w7[i];
     int rc = copy_in(L.rms1, rms1, (size_t)H * 4);
     if (!rc) rc = copy_in(L.rms2, rms2, (size_t)H * 4);
-    return rc;
+    if (rc) return rc;
+    rq::DecLayer& D = m->hlayers[(size_t)layer];
+    for (int i = 0; i < 7; i++) {
+        D.qs[i] = w7[i]->qs;
+        D.hdr[i] = w7[i]->hdr;
+    }
+    D.rms1 = L.rms1;
+    D.rms2 = L.rms2;
+    D.kc = L.kc;
+    D.vc = L.vc;
+    m->layer_set[(size_t)layer] = true;
+    return cuda_error(cudaMemcpy(m->dlayers + layer, &D, sizeof D, cudaMemcpyHostToDevice), "layer table copy");
 }
 
 int rq_llama_set_embedding(rq_llama* m, const uint16_t* embed_f16) {
@@ -784,7 +780,29 @@ int rq_llama_forward(rq_llama* m, const int32_t* tokens, int64_t T, int64_t inde
 int rq_llama_decode_step(rq_llama* m, void* stream) {
     if (!m) return set_error(RQ_ERR_INVALID, "rq_llama_decode_step: NULL argument");
     Guard g(m->ctx->device);
+    DecParams dp;
+    size_t smem = 0;
+    if (fused_plan(m, dp, &smem)) return launch_decode_step(dp, m->ctx->sm_count, smem, (cudaStream_t)stream);
     return forward_device(m, 1, false, (cudaStream_t)stream);
+}
+
+int rq_llama_set_fused(rq_llama* m, int enable) {
+    if (!m) return set_error(RQ_ERR_INVALID, "rq_llama_set_fused: NULL argument");
+    m->fused = enable != 0;
+    return RQ_OK;
+}
+
+int rq_llama_status(rq_llama* m) {
+    if (!m) return set_error(RQ_ERR_INVALID, "rq_llama_status: NULL argument");
+    Guard g(m->ctx->device);
+    int e = 0;
+    int rc = cuda_error(cudaMemcpy(&e, m->derr, 4, cudaMemcpyDeviceToHost), "status copy");
+    if (rc) return rc;
+    if (e) {
+        cudaMemset(m->derr, 0, 4);
+        return set_error(RQ_ERR_TIMEOUT, "decode step: a wait timed out (the step's outputs are invalid)");
+    }
+    return RQ_OK;
 }
 
 int rq_llama_tokens(rq_llama* m, int32_t* out, int64_t cap, int64_t* count, int64_t* position) {

@@ -28,6 +28,7 @@
 
 #include "rq_async.cuh"
 #include "rq_mv_common.cuh"
+#include "rq_pipe_lane.cuh"
 
 namespace rq {
 namespace {
@@ -55,90 +56,6 @@ __device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) 
     const int64_t e = (int64_t)(blockIdx.x + 1) * j.out / gridDim.x;
     *rb = b;
     *n = (int)(e - b);
-}
-
-template <int TYPE>
-struct LaneOf;
-template <>
-struct LaneOf<RQ_Q4_K> { using T = Q4KPLane; };
-template <>
-struct LaneOf<RQ_Q3_K> { using T = Q3KLane; };
-template <>
-struct LaneOf<RQ_Q4_0> { using T = Q40Lane; };
-
-// Per-lane constants of K-slice s: activation planes and the lane's
-// shared-memory byte offsets inside a row.  Lanes past the end of a partial
-// slice get zero activations and read the slice's first block, so the row
-// loop needs no per-lane branch.
-struct LaneOffsets {
-    uint32_t qa, qb, h;
-};
-
-template <int TYPE>
-__device__ __forceinline__ void lane_setup(typename LaneOf<TYPE>::T& L, LaneOffsets& o,
-                                           const PipeParams& p, const XQ& xq, int s, int lane) {
-    if constexpr (TYPE == RQ_Q4_0) {
-        const int64_t b0 = (int64_t)s * 64 + 2 * lane;
-        const bool valid = b0 < p.nblk;
-        if (valid) {
-            q40_lane_setup(L, xq.planes, xq.stats, p.in, p.nblk, b0);
-        } else {
-#pragma unroll
-            for (int q = 0; q < 3; q++)
-#pragma unroll
-                for (int w = 0; w < 16; w++) L.p[q][w] = 0u;
-            L.sx0 = L.sx1 = L.xs0 = L.xs1 = 0.0f;
-            L.has1 = false;
-        }
-        const uint32_t l = valid ? (uint32_t)lane : 0u;
-        o.qa = (uint32_t)(s * 1024) + 32u * l + 16u * ((l >> 2) & 1u);
-        o.qb = o.qa ^ 16u;
-        o.h = (uint32_t)(s * 128) + 4u * l;
-    } else {
-        const int64_t sb = (int64_t)s * 8 + (lane >> 2);
-        const bool valid = sb < p.nblk;
-        const uint32_t sbl = valid ? (uint32_t)(lane >> 2) : 0u;
-        if constexpr (TYPE == RQ_Q4_K) {
-            q4kp_lane_setup(L, xq.planes, xq.stats, p.in, valid ? sb : 0, lane & 3, (lane >> 2) & 1, valid);
-            o.qa = (uint32_t)(s * 1024) + 128u * sbl + 32u * (uint32_t)(lane & 3) + 16u * ((lane >> 2) & 1u);
-            o.qb = o.qa ^ 16u;
-        } else {
-            q3k_lane_setup(L, xq.planes, xq.stats, p.in, valid ? sb : 0, lane & 3);
-            if (!valid) {
-#pragma unroll
-                for (int q = 0; q < 3; q++)
-#pragma unroll
-                    for (int r = 0; r < 4; r++)
-#pragma unroll
-                        for (int c = 0; c < 4; c++) L.p[q][r][c] = 0u;
-#pragma unroll
-                for (int r = 0; r < 4; r++) L.sx[r] = L.xs16[r] = 0.0f;
-            }
-            o.qa = (uint32_t)(s * 768) + 96u * sbl + 16u * (uint32_t)L.u;  // hmask
-            o.qb = (uint32_t)(s * 768) + 96u * sbl + 32u + 32u * (uint32_t)L.h + 16u * (uint32_t)L.u;
-        }
-        o.h = (uint32_t)(s * 128) + 16u * sbl;
-    }
-}
-
-// Lane contribution of one row held in shared memory (q: the row's quant
-// bytes, h: its header bytes).
-template <int TYPE>
-__device__ __forceinline__ float lane_row(const typename LaneOf<TYPE>::T& L, const LaneOffsets& o,
-                                          const uint8_t* q, const uint8_t* h) {
-    const uint4 a = *reinterpret_cast<const uint4*>(q + o.qa);
-    const uint4 b = *reinterpret_cast<const uint4*>(q + o.qb);
-    if constexpr (TYPE == RQ_Q4_K) {
-        return q4kp_lane_row(L, a, b, *reinterpret_cast<const uint4*>(h + o.h), 0.0f);
-    } else if constexpr (TYPE == RQ_Q3_K) {
-        return q3k_lane_row(L, a, b, *reinterpret_cast<const uint4*>(h + o.h));
-    } else {
-        // a is the half selected by lane bit 2; swap back to blocks (b0, b0+1)
-        const bool swap = (o.qa & 16u) != 0u;
-        const uint32_t dd = *reinterpret_cast<const uint32_t*>(h + o.h);
-        return q40_lane_row(L, swap ? b : a, swap ? a : b, (uint16_t)(dd & 0xFFFFu),
-                            L.has1 ? (uint16_t)(dd >> 16) : (uint16_t)0);
-    }
 }
 
 template <int TYPE, int RPW>
@@ -202,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
             int nrows;
             job_rows(jb, &rb, &nrows);
             if (jb.xq.planes != cur_x) {  // jobs that share x keep the planes
-                lane_setup<TYPE>(L, o, p, jb.xq, s, lane);
+                lane_setup<TYPE>(L, o, p.nblk, p.in, jb.xq, s, lane);
                 cur_x = jb.xq.planes;
             }
             for (int r0 = 0; r0 < nrows; r0 += p.RS, it++) {

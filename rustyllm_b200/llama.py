@@ -75,6 +75,15 @@ class StreamingLlamaQuantized:
     def decode_step(self, stream: int = 0) -> None:
         check(_lib.lib().rq_llama_decode_step(self.handle, stream))
 
+    def set_fused(self, enable: bool) -> None:
+        """One persistent launch per decode step (one GPU) or the chain of
+        per-layer kernels (default); both compute the same bits."""
+        check(_lib.lib().rq_llama_set_fused(self.handle, 1 if enable else 0))
+
+    def status(self) -> None:
+        """Raises RqError if a wait inside a one-launch decode step timed out."""
+        check(_lib.lib().rq_llama_status(self.handle))
+
     def tokens(self) -> tuple[list, int]:
         cap = self.cfg.get("max_seq", 512)
         buf = np.empty(cap, dtype=np.int32)
@@ -95,6 +104,7 @@ class StreamingLlamaQuantized:
             self.decode_step()
         if torch is not None:
             torch.cuda.synchronize(self.ctx.device)
+        self.status()
         toks, _ = self.tokens()
         return toks[:max_new_tokens]
 

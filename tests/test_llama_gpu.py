@@ -73,6 +73,21 @@ def test_decode_step_graph_and_truncate(oracle, rq_ctx):
     del g
 
 
+@pytest.mark.parametrize("qtype", [12, 11, 2])
+def test_one_launch_step_matches_launch_chain(oracle, rq_ctx, qtype):
+    """The persistent one-launch decode step computes the same tokens as the
+    per-layer launch chain and the oracle, for every weight type."""
+    cfg = dict(CFG, n_layers=3)
+    model, ref = build(oracle, qtype, seed=30 + qtype, cfg=cfg)
+    prompt = np.random.default_rng(8).integers(0, cfg["vocab"], size=9).astype(np.int32)
+    model.set_fused(True)
+    fused = model.generate(prompt, 12)
+    model.set_fused(False)
+    chain = model.generate(prompt, 12)
+    assert fused == chain
+    assert fused == ref.generate(prompt, 12)
+
+
 def test_llama_rejects_bad_config(rq_ctx):
     from rustyllm_b200 import RqError
     from rustyllm_b200.llama import StreamingLlamaQuantized
