@@ -246,15 +246,16 @@ def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
     return res
 
 
-SMALL_M = (2, 3, 4, 8, 16)
+SMALL_M = (2, 3, 4, 8, 16, 24, 128, 512)
 
 
 def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g) -> dict:
     """Small-M Q4_K matmul at the seven 70B layer shapes (M = 2, 3, 4, 8
-    for speculative verify, 16 for the first prefill tile): one rq_linear
+    for speculative verify; 16, 24, 128, 512 for prefill): one rq_linear
     call per linear with [M, in] device activations, graph-replayed over the
     rotating layer copies.  GB/s = (Q4_K weight bytes + 4 M (in + out)) per
-    layer / time, weight bytes counted once."""
+    layer / time, weight bytes counted once; TFLOP/s = 2 M sum(in * out) /
+    time."""
     import torch
     from rustyllm_b200._lib import check
     res = {}
@@ -277,12 +278,15 @@ def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g) -> dict:
         reps = 10
         ms = timed(lambda r: gr.replay(), reps) / (reps * N_COPIES)
         nbytes = sum(Q4K_BYTES(i, o) + 4 * M * (i + o) for _, i, o in SHAPES)
+        flops = 2 * M * sum(i * o for _, i, o in SHAPES)
         res[str(M)] = {"ms_per_layer": round(ms, 4), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                       "tflops": round(flops / (ms / 1e3) / 1e12, 1),
                        "tok_per_s_layer_equiv": round(M / (ms / 1e3), 1)}
         del gr
     res["note"] = ("7 rq_linear calls per layer, 4 rotating layer copies. M <= 3: activation staging + "
-                   "one M=1 pipeline pass per row; M >= 4: f16 hi/lo staging + the mma.sync tensor-core "
-                   "kernel, weights read once per 8-row tile")
+                   "one M=1 pipeline pass per row; M = 4..23: f16 hi/lo staging + the mma.sync "
+                   "tensor-core kernel, weights read once per 8-row tile; M >= 24: the tcgen05 kernel "
+                   "(exact sc*q weights in TMEM, 128 rows x up to 112 tokens per tile)")
     return res
 
 
@@ -715,9 +719,10 @@ def run_gpu(args) -> None:
 
 def run_case(name: str) -> None:
     """A few launches of one kernel for an ncu capture: 'pipe_gate_up' (the
-    gate+up rq_linear_batch of one 70B layer, M=1) or 'mm_gate_m8' (gate_proj
-    8192 -> 28672 at M=8 on the tensor-core kernel).  Prints the per-call
-    time measured without the profiler."""
+    gate+up rq_linear_batch of one 70B layer, M=1), 'mm_gate_m8' (gate_proj
+    8192 -> 28672 at M=8 on the mma.sync kernel) or 'tc_gate_m128' (the same
+    at M=128 on the tcgen05 kernel).  Prints the per-call time measured
+    without the profiler."""
     import ctypes
 
     import torch
@@ -739,11 +744,12 @@ def run_case(name: str) -> None:
                                     arr([y.data_ptr() for y in ys]), s))
         nbytes = 2 * Q4K_BYTES(8192, 28672)
     else:
-        x = torch.randn(8, 8192, device="cuda", generator=g)
-        y = torch.empty(8, 28672, device="cuda")
+        M = 8 if name == "mm_gate_m8" else 128
+        x = torch.randn(M, 8192, device="cuda", generator=g)
+        y = torch.empty(M, 28672, device="cuda")
 
         def call():
-            check(L.rq_linear(ctx.handle, ws[0].handle, x.data_ptr(), y.data_ptr(), 8, s))
+            check(L.rq_linear(ctx.handle, ws[0].handle, x.data_ptr(), y.data_ptr(), M, s))
         nbytes = Q4K_BYTES(8192, 28672)
     for _ in range(3):
         call()
@@ -755,8 +761,10 @@ def run_case(name: str) -> None:
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / 10
-    print(json.dumps({"case": name, "us_per_call": round(ms * 1e3, 2),
-                      "weight_gbs": round(nbytes / (ms / 1e3) / 1e9, 1)}), flush=True)
+    out = {"case": name, "us_per_call": round(ms * 1e3, 2), "weight_gbs": round(nbytes / (ms / 1e3) / 1e9, 1)}
+    if name == "tc_gate_m128":
+        out["tflops"] = round(2 * 128 * 8192 * 28672 / (ms / 1e3) / 1e12, 1)
+    print(json.dumps(out), flush=True)
 
 
 def main():
@@ -773,7 +781,7 @@ def main():
     ap.add_argument("--no-moe", action="store_true", help="skip the Mixtral MoE layer sweep")
     ap.add_argument("--decode-layers", type=int, default=None,
                     help="layers of the decode model (default 80; fewer for profiling)")
-    ap.add_argument("--case", choices=["pipe_gate_up", "mm_gate_m8"], default=None,
+    ap.add_argument("--case", choices=["pipe_gate_up", "mm_gate_m8", "tc_gate_m128"], default=None,
                     help="run a few launches of one kernel (for profiling) and exit")
     args = ap.parse_args()
     if args.case:

@@ -345,8 +345,9 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
     DeviceGuard g(ctx->device);
     cudaStream_t st = (cudaStream_t)stream;
     const bool x_dev = mem_kind(x) == Mem::Device, y_dev = mem_kind(y) == Mem::Device;
-    // M >= 4: one tensor-core pass over the weights per 8 rows; M = 2, 3:
-    // the M=1 pipeline once per row is faster (it streams at ~5 TB/s)
+    // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 4..23:
+    // one mma.sync pass over the weights per 8 rows; M = 2, 3: the M=1
+    // pipeline once per row is faster (it streams at ~5 TB/s)
     const bool small_m = M >= kMinTensorM && mm_small_supported(w);
     const size_t xq_sz = small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
     const size_t x_sz = x_dev ? 0 : (size_t)(M * w->in) * sizeof(float);
@@ -367,7 +368,12 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
     if (small_m) {
         const XH xh = xh_at(ws, M, w->in);
         rc = launch_xh_stage(xd, M, w->in, xh, st);
-        if (!rc) rc = launch_matmul_small(w, xh, M, yd, nullptr, ctx->sm_count, st);
+        if (!rc && M >= kMinTcgenM && mm_tc_supported(w)) {
+            const MMJobDesc job{w, 0, (int)M, yd, nullptr};
+            rc = launch_mm_tc(&job, 1, xh, M, ctx->sm_count, st);
+        } else if (!rc) {
+            rc = launch_matmul_small(w, xh, M, yd, nullptr, ctx->sm_count, st);
+        }
     } else {
         rc = launch_xquant(xd, M, w->in, xq, st);
         if (!rc) rc = launch_linear(w, xq, yd, M, ctx->sm_count, st);

@@ -138,6 +138,7 @@ struct XH {
     __half* v;     // [rows][2][in]: hi plane, lo plane
     float* scale;  // [rows]
     float* bsum;   // [rows][in/32]
+    __half* bs16;  // [rows][in/256][16]: the 8 block sums of a super-block as f16 hi, then f16 lo
 };
 size_t xh_bytes(int64_t rows, int64_t in);
 XH xh_at(void* base, int64_t rows, int64_t in);
@@ -158,6 +159,13 @@ int launch_mm_small(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int s
 // y[M][out] = x W^T (+ add) for M >= 2 staged rows, in tiles of 8 rows
 int launch_matmul_small(const rq_weight* w, XH xh, int64_t M, float* y, const float* add, int sm_count,
                         cudaStream_t st);
+// Q4_K matmul on tcgen05 (rq_mm_tc.cu) for jobs of any M: 128 weight rows x
+// up to 128 tokens per tile, f32 accumulators in TMEM; same staged matrix and
+// job descriptors as launch_mm_small (no limit on M_j); err may be NULL.
+constexpr int64_t kMinTcgenM = 24;  // smallest M routed to the tcgen05 kernel (measured crossover)
+bool mm_tc_supported(const rq_weight* w);
+int launch_mm_tc(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_count, cudaStream_t st,
+                 int* err = nullptr);
 
 // linear kernels (rq_matvec.cu).  launch_linear runs y = x W^T for M staged
 // activation rows (launch_xquant first).  launch_xquant_rows stages up to

@@ -57,7 +57,8 @@ namespace rq {
 size_t xh_bytes(int64_t rows, int64_t in) {
     size_t b = ((size_t)rows * 4 * (size_t)in + 255) & ~(size_t)255;  // f16 hi + lo
     b += ((size_t)rows * 4 + 255) & ~(size_t)255;                     // row scales
-    b += (size_t)rows * (size_t)(in / 32) * 4;                        // block sums
+    b += ((size_t)rows * (size_t)(in / 32) * 4 + 255) & ~(size_t)255;  // block sums
+    b += (size_t)rows * (size_t)(in / 256) * 32;                        // block sums, f16 hi / lo
     return b;
 }
 
@@ -69,6 +70,8 @@ XH xh_at(void* base, int64_t rows, int64_t in) {
     x.scale = (float*)p;
     p += ((size_t)rows * 4 + 255) & ~(size_t)255;
     x.bsum = (float*)p;
+    p += ((size_t)rows * (size_t)(in / 32) * 4 + 255) & ~(size_t)255;
+    x.bs16 = (__half*)p;
     return x;
 }
 
@@ -77,10 +80,11 @@ namespace {
 // ------------------------------------------------------------------ staging
 // One CTA per row: s = 2^e with amax < s <= 2 amax (1 for a zero row),
 // v = x / s, hi = f16(v), lo = f16(v - hi), stored quad-permuted; block sums
-// of v in element order.
+// of v in element order, in f32 and as f16 hi / lo pairs grouped per
+// super-block (the K = 16 operand of the tcgen05 kernel's min term).
 __global__ void __launch_bounds__(256) xh_stage_kernel(const float* __restrict__ x, int64_t in,
                                                        __half* __restrict__ xh, float* __restrict__ scale,
-                                                       float* __restrict__ bsum) {
+                                                       float* __restrict__ bsum, __half* __restrict__ bs16) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     __shared__ float red[8];
@@ -129,6 +133,10 @@ __global__ void __launch_bounds__(256) xh_stage_kernel(const float* __restrict__
             dl[k] = make_uint4(pl[4 * k], pl[4 * k + 1], pl[4 * k + 2], pl[4 * k + 3]);
         }
         bsum[m * (in / 32) + b] = s;
+        const __half sh = __float2half_rn(s);
+        __half* b16 = bs16 + m * (in / 32) * 2 + (b >> 3) * 16 + (b & 7);
+        b16[0] = sh;
+        b16[8] = __float2half_rn(s - __half2float(sh));
     }
 }
 
@@ -602,7 +610,7 @@ int launch_xh_stage(const float* x, int64_t M, int64_t in, XH xh, cudaStream_t s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_error(cudaLaunchKernelEx(&cfg, xh_stage_kernel, x, in, xh.v, xh.scale, xh.bsum), "x staging (f16)");
+    return cuda_error(cudaLaunchKernelEx(&cfg, xh_stage_kernel, x, in, xh.v, xh.scale, xh.bsum, xh.bs16), "x staging (f16)");
 }
 
 bool mm_small_supported(const rq_weight* w) { return w->type == RQ_Q4_K; }

@@ -302,10 +302,18 @@ struct JobList {
     std::vector<float*> y;
 };
 
+// jobs with M_j <= 8 on the mma.sync kernel, larger ones on tcgen05
 int run_mm_jobs(const std::vector<MMJobDesc>& J, XH xh, int64_t rows, int sm, cudaStream_t st) {
-    for (size_t b = 0; b < J.size(); b += kMaxJobs) {
-        const int n = (int)std::min<size_t>(kMaxJobs, J.size() - b);
-        int rc = launch_mm_small(&J[b], n, xh, rows, sm, st);
+    std::vector<MMJobDesc> sm_jobs, tc_jobs;
+    for (const MMJobDesc& j : J) (j.M >= kMinTcgenM ? tc_jobs : sm_jobs).push_back(j);
+    for (size_t b = 0; b < sm_jobs.size(); b += kMaxJobs) {
+        const int n = (int)std::min<size_t>(kMaxJobs, sm_jobs.size() - b);
+        int rc = launch_mm_small(&sm_jobs[b], n, xh, rows, sm, st);
+        if (rc) return rc;
+    }
+    for (size_t b = 0; b < tc_jobs.size(); b += kMaxJobs) {
+        const int n = (int)std::min<size_t>(kMaxJobs, tc_jobs.size() - b);
+        int rc = launch_mm_tc(&tc_jobs[b], n, xh, rows, sm, st);
         if (rc) return rc;
     }
     return RQ_OK;
@@ -390,6 +398,12 @@ int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& 
     std::vector<MMJobDesc> upm, downm;
     for (const Seg& sg : segs) {
         const size_t e = (size_t)sg.e;
+        if (use_mm(sg) && sg.n >= kMinTcgenM) {
+            upm.push_back(MMJobDesc{m->w1[e], (int)sg.start, (int)sg.n, m->g + sg.start * F, nullptr});
+            upm.push_back(MMJobDesc{m->w3[e], (int)sg.start, (int)sg.n, m->u + sg.start * F, nullptr});
+            downm.push_back(MMJobDesc{m->w2[e], (int)sg.start, (int)sg.n, out + sg.start * H, nullptr});
+            continue;
+        }
         if (use_mm(sg)) {
             for (int64_t t0 = sg.start; t0 < sg.start + sg.n; t0 += 8) {
                 const int n = (int)std::min<int64_t>(8, sg.start + sg.n - t0);

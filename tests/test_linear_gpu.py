@@ -92,6 +92,32 @@ def test_small_m_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
         assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("out,n_in,M", [(200, 768, 24), (128, 256, 25), (333, 2048, 67), (1040, 4096, 128),
+                                         (520, 4096, 129), (256, 8192, 300), (4096, 1024, 512),
+                                         (130, 28672, 40), (300, 1024, 33), (200, 2048, 90)])
+def test_tcgen05_matmul_shapes(oracle, rq_ctx, out, n_in, M):
+    """Q4_K M >= 24 runs on the tcgen05 kernel: a partial last 128-row tile,
+    the shortest K (one super-block), token tiles split evenly (128 -> 2 x
+    64, 129 -> 2 x 80, 300 -> 3 x 112), every TMEM plan (16..112 tokens per
+    tile: 4, 2 or 1 K chains, one or two accumulator buffers), several tiles
+    per CTA, and a long K."""
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200.linear import _linear
+    _, blocks = make_weight(oracle, 12, out, n_in, seed=3 * out + M)
+    w = QWeight.upload(rq_ctx, 12, blocks, out, n_in)
+    x = np.random.default_rng(M + 7).standard_normal((M, n_in)).astype(np.float32)
+    x[M // 2] = 0.0                      # an all-zero activation row
+    x[M - 1] *= 1e-3                     # a row far from unit scale
+    y = _linear(w, x)
+    ref = oracle.matmul_ref(12, blocks, out, n_in, x, acc64=True)
+    assert np.isfinite(y).all()
+    assert rel_l2(y, ref) <= REL_L2_TOL
+    assert np.all(y[M // 2] == 0.0)
+    for m in range(M):
+        if m != M // 2:
+            assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
+
+
 @pytest.mark.parametrize("qtype", TYPES)
 def test_gpu_quantizer_matches_oracle_bytes(oracle, rq_ctx, qtype):
     import torch

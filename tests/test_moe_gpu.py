@@ -31,10 +31,11 @@ def make_layer(oracle, rq_ctx, E, H, F, qtype, seed):
     return wr, blocks, experts
 
 
-@pytest.mark.parametrize("T", [1, 2, 5, 16, 33, 130])
+@pytest.mark.parametrize("T", [1, 2, 5, 16, 33, 130, 600])
 def test_moe_matches_oracle(oracle, rq_ctx, T):
-    """Small T runs per-slot pipeline jobs; experts with >= 4 tokens run the
-    tensor-core kernel in tiles of 8 (T=130: several tiles per expert)."""
+    """Small T runs per-slot pipeline jobs; experts with 4..15 tokens run the
+    mma.sync kernel in tiles of 8, experts with >= 16 tokens the tcgen05
+    kernel (T=130: about 32 per expert; T=600: about 150, two token tiles)."""
     from rustyllm_b200.mixtral import SparseMoe
     E, H, F = 8, 512, 1024
     wr, blocks, experts = make_layer(oracle, rq_ctx, E, H, F, 12, seed=T)
