@@ -143,6 +143,10 @@ struct XH {
 size_t xh_bytes(int64_t rows, int64_t in);
 XH xh_at(void* base, int64_t rows, int64_t in);
 int launch_xh_stage(const float* x, int64_t M, int64_t in, XH xh, cudaStream_t st);
+// the same staging of RMSNorm(x) * w, and of silu(gate) * up
+int launch_xh_stage_rmsnorm(const float* x, const float* w, float eps, int64_t M, int64_t in, XH xh,
+                            cudaStream_t st);
+int launch_xh_stage_swiglu(const float* gate, const float* up, int64_t M, int64_t in, XH xh, cudaStream_t st);
 // Up to kMaxJobs jobs with the same K, each y_j[M_j][out_j] = x[tok0_j ..
 // tok0_j + M_j) W_j^T (+ add_j), M_j <= 8, all reading one staged matrix of
 // `rows` rows; err may be NULL.

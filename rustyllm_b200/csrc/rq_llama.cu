@@ -60,6 +60,7 @@ struct rq_llama {
     int W, R;       // tensor-parallel world and rank
     int64_t nh_l, nkv_l, I_l, vocab_l;  // this rank's heads, kv heads, ffn rows, vocab rows
     rq::XQ xq;      // Tmax rows of max(hidden, intermediate)
+    rq::XH xh;      // the same rows staged as f16 hi / lo (tensor-core prefill)
     // device state
     unsigned long long* best;  // packed (value, -index) of the argmax
     int32_t* tokens;           // [Tmax] current input tokens
@@ -383,6 +384,52 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
     return rc;
 }
 
+// y_i = x W_i^T (+ add_i) for the n Q4_K weights (same in) over the T rows
+// staged in m->xh: one tcgen05 launch for T >= kMinTcgenM, else mma.sync
+// tiles of 8 rows, up to kMaxJobs tiles per launch.
+int run_mm(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* const* ys, const float* const* adds,
+           cudaStream_t st) {
+    const int sm = m->ctx->sm_count;
+    std::vector<MMJobDesc> jobs;
+    if (T >= kMinTcgenM) {
+        for (int i = 0; i < n; i++) jobs.push_back(MMJobDesc{ws[i], 0, (int)T, ys[i], adds ? adds[i] : nullptr});
+        return launch_mm_tc(jobs.data(), (int)jobs.size(), m->xh, T, sm, st);
+    }
+    for (int64_t t0 = 0; t0 < T; t0 += 8)
+        for (int i = 0; i < n; i++) {
+            const int64_t o = ws[i]->out;
+            jobs.push_back(MMJobDesc{ws[i], (int)t0, (int)std::min<int64_t>(8, T - t0), ys[i] + t0 * o,
+                                     adds && adds[i] ? adds[i] + t0 * o : nullptr});
+        }
+    for (size_t b = 0; b < jobs.size(); b += kMaxJobs) {
+        const int nj = (int)std::min<size_t>(kMaxJobs, jobs.size() - b);
+        int rc = launch_mm_small(&jobs[b], nj, m->xh, T, sm, st);
+        if (rc) return rc;
+    }
+    return RQ_OK;
+}
+
+// row_parallel on the tensor-core path: x = x + x_in W^T with x_in staged in
+// m->xh (the residual add in the epilogue; under tensor parallelism rank 0
+// adds it to its partial before the all-reduce).
+int row_parallel_mm(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
+    const rq_weight* w1[1] = {w};
+    float* y1[1] = {m->W == 1 ? m->x : m->part};
+    const float* a1[1] = {m->R == 0 ? m->x : nullptr};
+    int rc = run_mm(m, 1, w1, T, y1, a1, st);
+    if (!rc && m->W > 1) rc = tp_allreduce(m->ctx, m->part, m->x, T * m->cfg.hidden, 0, 0, st);
+    return rc;
+}
+
+// Prompt chunks of T >= kMinTensorM tokens with Q4_K weights run every
+// linear on the tensor cores, one pass over the weights per chunk.
+bool tensor_prefill(const rq_llama* m, int64_t T, int64_t l) {
+    if (T < kMinTensorM || !m->xh.v) return false;
+    for (int i = 0; i < 7; i++)
+        if (!mm_small_supported(m->layers[(size_t)l].w[i])) return false;
+    return true;
+}
+
 // One forward over the T tokens in m->tokens at device position *m->pos.
 int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
     const rq_llama_config& c = m->cfg;
@@ -400,12 +447,17 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
     }
     for (int64_t l = 0; l < c.n_layers; l++) {
         rq_llama::Layer& L = m->layers[l];
-        rc = launch_xquant_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xq, st);
-        if (rc) return rc;
+        const bool tc = tensor_prefill(m, T, l);
         {
             const rq_weight* w3[3] = {L.w[0], L.w[1], L.w[2]};
             float* y3[3] = {m->q, m->k, m->v};
-            rc = run_linears(m, 3, w3, T, y3, nullptr, st);
+            if (tc) {
+                rc = launch_xh_stage_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xh, st);
+                if (!rc) rc = run_mm(m, 3, w3, T, y3, nullptr, st);
+            } else {
+                rc = launch_xquant_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xq, st);
+                if (!rc) rc = run_linears(m, 3, w3, T, y3, nullptr, st);
+            }
             if (rc) return rc;
         }
         if (T == 1 && c.head_dim % 32 == 0) {
@@ -445,22 +497,30 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
             rc = launch_simple((const void*)attention_kernel, dim3((unsigned)nh, (unsigned)T), dim3(128),
                                (size_t)c.max_seq * sizeof(float), st, args2, "attention kernel");
             if (rc) return rc;
-            rc = launch_xquant(m->att, T, nq, m->xq, st);
+            rc = tc ? launch_xh_stage(m->att, T, nq, m->xh, st) : launch_xquant(m->att, T, nq, m->xq, st);
             if (rc) return rc;
         }
-        rc = row_parallel(m, L.w[3], T, st);
-        if (rc) return rc;
-        rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
+        rc = tc ? row_parallel_mm(m, L.w[3], T, st) : row_parallel(m, L.w[3], T, st);
         if (rc) return rc;
         {
             const rq_weight* w2[2] = {L.w[4], L.w[5]};
             float* y2[2] = {m->g, m->u};
-            rc = run_linears(m, 2, w2, T, y2, nullptr, st);
+            if (tc) {
+                rc = launch_xh_stage_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xh, st);
+                if (!rc) rc = run_mm(m, 2, w2, T, y2, nullptr, st);
+            } else {
+                rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
+                if (!rc) rc = run_linears(m, 2, w2, T, y2, nullptr, st);
+            }
             if (rc) return rc;
         }
-        rc = launch_xquant_swiglu(m->g, m->u, T, I, m->xq, st);
-        if (rc) return rc;
-        rc = row_parallel(m, L.w[6], T, st);
+        if (tc) {
+            rc = launch_xh_stage_swiglu(m->g, m->u, T, I, m->xh, st);
+            if (!rc) rc = row_parallel_mm(m, L.w[6], T, st);
+        } else {
+            rc = launch_xquant_swiglu(m->g, m->u, T, I, m->xq, st);
+            if (!rc) rc = row_parallel(m, L.w[6], T, st);
+        }
         if (rc) return rc;
     }
     (void)nk;
@@ -648,7 +708,9 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     if (!rc) rc = dalloc(m, &m->logits, (size_t)m->vocab_l);
     if (!rc) rc = dalloc(m, &m->part, (size_t)(T * H));
     uint8_t* xqbuf = nullptr;
+    uint8_t* xhbuf = nullptr;
     if (!rc) rc = dalloc(m, &xqbuf, xq_bytes(T, maxin));
+    if (!rc && T >= kMinTensorM) rc = dalloc(m, &xhbuf, xh_bytes(T, maxin));
     if (!rc) rc = dalloc(m, &m->best, 1);
     if (!rc) rc = dalloc(m, &m->tokens, (size_t)T);
     if (!rc) rc = dalloc(m, &m->pos, 1);
@@ -662,6 +724,7 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
         m->layer_set.assign((size_t)c.n_layers, false);
         m->xq.planes = (int8_t*)xqbuf;
         m->xq.stats = (float4*)(xqbuf + (((size_t)T * 3 * maxin + 255) & ~(size_t)255));
+        m->xh = xhbuf ? xh_at(xhbuf, T, maxin) : XH{};
         // RoPE tables as QuantStreamCache::new computes them
         // (src/streaming_quantized.rs:104-118): inv_freq[i] =
         // 1 / theta^(2i / head_dim), angle = f32(position) * inv_freq[i].

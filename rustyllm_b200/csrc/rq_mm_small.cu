@@ -81,17 +81,65 @@ namespace {
 // One CTA per row: s = 2^e with amax < s <= 2 amax (1 for a zero row),
 // v = x / s, hi = f16(v), lo = f16(v - hi), stored quad-permuted; block sums
 // of v in element order, in f32 and as f16 hi / lo pairs grouped per
-// super-block (the K = 16 operand of the tcgen05 kernel's min term).
-__global__ void __launch_bounds__(256) xh_stage_kernel(const float* __restrict__ x, int64_t in,
-                                                       __half* __restrict__ xh, float* __restrict__ scale,
-                                                       float* __restrict__ bsum, __half* __restrict__ bs16) {
+// super-block (the K = 16 operand of the tcgen05 kernel's min term).  The
+// staged row is Op's value of each element: the input itself, its RMSNorm
+// (x / sqrt(mean(x^2) + eps) * w, the order of xquant_rmsnorm_kernel) or
+// SwiGLU (silu(gate) * up, silu(g) = g / (1 + exp(-g))).
+struct OpPlain {
+    const float* x;
+    __device__ void setup(int64_t, int64_t, float*) {}
+    __device__ float at(int64_t m, int64_t in, int64_t k) const { return x[m * in + k]; }
+};
+struct OpRms {
+    const float* x;
+    const float* w;
+    float eps;
+    float mden;
+    __device__ void setup(int64_t m, int64_t in, float* red) {
+        const float* row = x + m * in;
+        float s2 = 0.0f;
+        if ((in & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+            const float4* r4 = reinterpret_cast<const float4*>(row);
+            for (int64_t i = threadIdx.x; i < in / 4; i += blockDim.x) {
+                const float4 v = r4[i];
+                s2 = fmaf(v.x, v.x, s2); s2 = fmaf(v.y, v.y, s2);
+                s2 = fmaf(v.z, v.z, s2); s2 = fmaf(v.w, v.w, s2);
+            }
+        } else {
+            for (int64_t i = threadIdx.x; i < in; i += blockDim.x) s2 = fmaf(row[i], row[i], s2);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s2;
+        __syncthreads();
+        float tot = 0.0f;
+        for (int k = 0; k < (int)(blockDim.x >> 5); k++) tot += red[k];
+        mden = sqrtf(tot / (float)in + eps);
+        __syncthreads();
+    }
+    __device__ float at(int64_t m, int64_t in, int64_t k) const { return x[m * in + k] / mden * w[k]; }
+};
+struct OpSwiglu {
+    const float* g;
+    const float* u;
+    __device__ void setup(int64_t, int64_t, float*) {}
+    __device__ float at(int64_t m, int64_t in, int64_t k) const {
+        const float v = g[m * in + k];
+        return v / (1.0f + expf(-v)) * u[m * in + k];
+    }
+};
+
+template <class Op>
+__global__ void __launch_bounds__(256) xh_stage_kernel(Op op, int64_t in, __half* __restrict__ xh,
+                                                       float* __restrict__ scale, float* __restrict__ bsum,
+                                                       __half* __restrict__ bs16) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     __shared__ float red[8];
     const int64_t m = blockIdx.x;
-    const float* xr = x + m * in;
+    op.setup(m, in, red);
     float a = 0.0f;
-    for (int64_t k = threadIdx.x; k < in; k += blockDim.x) a = fmaxf(a, fabsf(xr[k]));
+    for (int64_t k = threadIdx.x; k < in; k += blockDim.x) a = fmaxf(a, fabsf(op.at(m, in, k)));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
@@ -105,13 +153,11 @@ __global__ void __launch_bounds__(256) xh_stage_kernel(const float* __restrict__
     __half* hi = xh + m * 2 * in;
     __half* lo = hi + in;
     for (int64_t b = threadIdx.x; b < in / 32; b += blockDim.x) {
-        float v[32];
-        load_block(xr + 32 * b, v);
         float s = 0.0f;
         __half h[32], l[32];
 #pragma unroll
         for (int k = 0; k < 32; k++) {
-            const float t = v[k] * inv;
+            const float t = op.at(m, in, 32 * b + k) * inv;
             s += t;
             h[k] = __float2half_rn(t);
             l[k] = __float2half_rn(t - __half2float(h[k]));
@@ -138,6 +184,22 @@ __global__ void __launch_bounds__(256) xh_stage_kernel(const float* __restrict__
         b16[0] = sh;
         b16[8] = __float2half_rn(s - __half2float(sh));
     }
+}
+
+template <class Op>
+int launch_stage(Op op, int64_t M, int64_t in, XH xh, cudaStream_t st) {
+    if (M <= 0) return RQ_OK;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_error(cudaLaunchKernelEx(&cfg, xh_stage_kernel<Op>, op, in, xh.v, xh.scale, xh.bsum, xh.bs16),
+                      "x staging (f16)");
 }
 
 // ------------------------------------------------------------------- matmul
@@ -600,17 +662,16 @@ int encode_2d(CUtensorMap* m, const void* base, uint64_t dim0, uint64_t dim1, ui
 }  // namespace
 
 int launch_xh_stage(const float* x, int64_t M, int64_t in, XH xh, cudaStream_t st) {
-    if (M <= 0) return RQ_OK;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)M);
-    cfg.blockDim = dim3(256);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cuda_error(cudaLaunchKernelEx(&cfg, xh_stage_kernel, x, in, xh.v, xh.scale, xh.bsum, xh.bs16), "x staging (f16)");
+    return launch_stage(OpPlain{x}, M, in, xh, st);
+}
+
+int launch_xh_stage_rmsnorm(const float* x, const float* w, float eps, int64_t M, int64_t in, XH xh,
+                            cudaStream_t st) {
+    return launch_stage(OpRms{x, w, eps, 0.0f}, M, in, xh, st);
+}
+
+int launch_xh_stage_swiglu(const float* gate, const float* up, int64_t M, int64_t in, XH xh, cudaStream_t st) {
+    return launch_stage(OpSwiglu{gate, up}, M, in, xh, st);
 }
 
 bool mm_small_supported(const rq_weight* w) { return w->type == RQ_Q4_K; }

@@ -31,11 +31,13 @@ def build(oracle, qtype, seed, cfg=CFG):
     return model, ref
 
 
-@pytest.mark.parametrize("qtype", [12, 11])
-def test_prompt_logits_and_greedy_tokens_match_oracle(oracle, rq_ctx, qtype):
-    model, ref = build(oracle, qtype, seed=qtype)
+@pytest.mark.parametrize("qtype,n_prompt", [(12, 20), (12, 28), (11, 20), (12, 3)])
+def test_prompt_logits_and_greedy_tokens_match_oracle(oracle, rq_ctx, qtype, n_prompt):
+    """Q4_K prompts of 4..23 tokens run their linears on the mma.sync
+    kernel, 24 and more on tcgen05; 3 tokens and Q3_K run M=1 jobs."""
+    model, ref = build(oracle, qtype, seed=qtype + n_prompt)
     rng = np.random.default_rng(20)
-    prompt = rng.integers(0, CFG["vocab"], size=20).astype(np.int32)
+    prompt = rng.integers(0, CFG["vocab"], size=n_prompt).astype(np.int32)
     lg, nxt = model.forward(prompt, 0)
     lr, nr = ref.forward(prompt, 0)
     assert rel_l2(lg, lr) <= LOGIT_TOL
@@ -43,6 +45,18 @@ def test_prompt_logits_and_greedy_tokens_match_oracle(oracle, rq_ctx, qtype):
     gen = model.generate(prompt, 16)
     want = ref.generate(prompt, 16)
     assert gen == want
+
+
+def test_chunked_prompt_matches_one_pass(oracle, rq_ctx):
+    """A prompt fed as chunks of 6 and 25 tokens (the second at position 6,
+    attention over the cached keys) gives the one-pass logits and tokens."""
+    model, ref = build(oracle, 12, seed=44)
+    prompt = np.random.default_rng(9).integers(0, CFG["vocab"], size=31).astype(np.int32)
+    model.forward(prompt[:6], 0)
+    lg, nxt = model.forward(prompt[6:], 6)
+    lr, nr = ref.forward(prompt, 0)
+    assert rel_l2(lg, lr) <= LOGIT_TOL
+    assert nxt == nr
 
 
 def test_decode_step_graph_and_truncate(oracle, rq_ctx):
