@@ -256,6 +256,48 @@ RQ_API int rq_llama_reset_tokens(rq_llama* m);
  * (src/streaming_quantized.rs:131-141,603-609): roll the KV length back. */
 RQ_API int rq_llama_truncate(rq_llama* m, int64_t new_len);
 
+/* ------------------------------------------------------------------- GGUF */
+
+/* A GGUF file read into host memory once (one sequential read, as
+ * GgufLayer::open does, src/streaming_quantized.rs:42-61) and parsed:
+ * versions 2 and 3, metadata skipped except general.alignment, tensor infos
+ * bounds-checked against the file.  The format candle's gguf_file::write
+ * emits for the reference's shards (src/quantize.rs:146-150). */
+typedef struct rq_gguf rq_gguf;
+RQ_API int rq_gguf_open(const char* path, rq_gguf** out);
+/* the same from a caller-held buffer (copied), e.g. GgufLayer.buffer */
+RQ_API int rq_gguf_open_memory(const void* data, size_t nbytes, rq_gguf** out);
+RQ_API int rq_gguf_free(rq_gguf* f);
+RQ_API int rq_gguf_tensor_count(const rq_gguf* f, int64_t* count);
+/* index of a tensor by name (RQ_ERR_INVALID and index -1 when absent) */
+RQ_API int rq_gguf_find(const rq_gguf* f, const char* name, int64_t* index);
+/* name (NUL-terminated, truncated to name_cap), ggml type, n_dims, dims[4]
+ * innermost first (a [out, in] matrix is {in, out, 1, 1}), offset of the
+ * data in the file and its size (0 for an unknown type); NULL outputs are
+ * skipped */
+RQ_API int rq_gguf_tensor_info(const rq_gguf* f, int64_t index, char* name, size_t name_cap, int* ggml_type,
+                               int* n_dims, int64_t* dims, uint64_t* file_offset, uint64_t* nbytes);
+/* pointer to a tensor's bytes inside the file buffer (valid until free) */
+RQ_API int rq_gguf_tensor_data(const rq_gguf* f, int64_t index, const void** data, uint64_t* nbytes);
+/* the first `count` elements of an F32 / F16 / BF16 tensor as f32 (norms,
+ * GgufLayer::tensor's dequantize, src/streaming_quantized.rs:74-83) */
+RQ_API int rq_gguf_read_f32(const rq_gguf* f, const char* name, float* out, int64_t count);
+/* Upload rows [row0, row0+rows) x columns [col0, col0+cols) of a 2-D Q4_0 /
+ * Q4_K / Q3_K tensor (rows or cols < 0: to the end; columns on block
+ * boundaries): GgufLayer::qmatmul (src/streaming_quantized.rs:63-70) with
+ * the tensor-parallel shard taken on the host. */
+RQ_API int rq_weight_upload_gguf(rq_ctx* ctx, const rq_gguf* f, const char* name, int64_t row0, int64_t rows,
+                                 int64_t col0, int64_t cols, rq_weight** out);
+/* Load a shard directory as StreamingLlamaQuantized::from_pretrained reads
+ * it (src/streaming_quantized.rs:451-501): model.layers.<l>.gguf for every
+ * layer (model.layers.<l>.self_attn.{q,k,v,o}_proj.weight,
+ * .mlp.{gate,up,down}_proj.weight, .input_layernorm.weight,
+ * .post_attention_layernorm.weight), model.embed_tokens.gguf,
+ * model.norm.gguf and lm_head.gguf (absent: the head is the embedding).
+ * Under tensor parallelism each rank uploads its own shards.  The model
+ * owns the weights it uploads. */
+RQ_API int rq_llama_load_gguf_dir(rq_llama* m, const char* dir);
+
 #ifdef __cplusplus
 }
 #endif

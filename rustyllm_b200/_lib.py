@@ -84,6 +84,18 @@ SIGNATURES.update({
     "rq_moe_free": (I, [P]),
     "rq_moe_forward": (I, [P, P, P, P, I64, P, P, P]),
     "rq_moe_forward_ep": (I, [P, P, P, P, I64, P, P, P]),
+    "rq_gguf_open": (I, [ctypes.c_char_p, PP]),
+    "rq_gguf_open_memory": (I, [P, SZ, PP]),
+    "rq_gguf_free": (I, [P]),
+    "rq_gguf_tensor_count": (I, [P, ctypes.POINTER(I64)]),
+    "rq_gguf_find": (I, [P, ctypes.c_char_p, ctypes.POINTER(I64)]),
+    "rq_gguf_tensor_info": (I, [P, I64, ctypes.c_char_p, SZ, ctypes.POINTER(I), ctypes.POINTER(I),
+                                ctypes.POINTER(I64), ctypes.POINTER(ctypes.c_uint64),
+                                ctypes.POINTER(ctypes.c_uint64)]),
+    "rq_gguf_tensor_data": (I, [P, I64, PP, ctypes.POINTER(ctypes.c_uint64)]),
+    "rq_gguf_read_f32": (I, [P, ctypes.c_char_p, P, I64]),
+    "rq_weight_upload_gguf": (I, [P, P, ctypes.c_char_p, I64, I64, I64, I64, PP]),
+    "rq_llama_load_gguf_dir": (I, [P, ctypes.c_char_p]),
 })
 
 _lib = None

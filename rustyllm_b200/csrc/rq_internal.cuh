@@ -1,6 +1,8 @@
 // rq_internal.cuh -- shared definitions of librq (not part of the ABI).
 #pragma once
 
+#include <vector>
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -101,6 +103,14 @@ int tp_allgather_bytes(rq_ctx* ctx, const void* in, void* out, int64_t nbytes, c
 // group; the rank's own share is a device copy)
 int tp_alltoallv_bytes(rq_ctx* ctx, const void* send, const int64_t* send_bytes, const int64_t* send_off, void* recv,
                        const int64_t* recv_bytes, const int64_t* recv_off, cudaStream_t st);
+
+// GGUF shard directory -> a Llama model (rq_gguf.cu): per layer the 7
+// linears (out x in of this rank's shard in dims7_out / dims7_in, q, k, v,
+// o, gate, up, down) and the two norms, then embedding, final norm, head.
+// The uploaded weights are appended to `owned`.
+int llama_load_gguf_dir(rq_ctx* ctx, rq_llama* m, const char* dir, int64_t n_layers, int64_t vocab, int64_t hidden,
+                        int world, int rank, const int64_t* dims7_out, const int64_t* dims7_in,
+                        std::vector<rq_weight*>& owned);
 
 // error handling (rq_api.cu)
 int set_error(int code, const char* fmt, ...);

@@ -75,6 +75,7 @@ struct rq_llama {
     int* derr;                          // error word of the step
     bool fused = false;                 // rq_llama_set_fused
     std::vector<void*> allocs;
+    std::vector<rq_weight*> owned;  // weights uploaded by rq_llama_load_gguf_dir
 };
 
 namespace rq {
@@ -758,6 +759,7 @@ int rq_llama_free(rq_llama* m) {
     if (!m) return RQ_OK;
     Guard g(m->ctx->device);
     for (void* p : m->allocs) cudaFree(p);
+    for (rq_weight* w : m->owned) rq_weight_free(m->ctx, w);
     delete m;
     return RQ_OK;
 }
@@ -796,6 +798,16 @@ int rq_llama_set_layer(rq_llama* m, int64_t layer, const rq_weight* const* w7, c
     D.vc = L.vc;
     m->layer_set[(size_t)layer] = true;
     return cuda_error(cudaMemcpy(m->dlayers + layer, &D, sizeof D, cudaMemcpyHostToDevice), "layer table copy");
+}
+
+int rq_llama_load_gguf_dir(rq_llama* m, const char* dir) {
+    if (!m || !dir) return set_error(RQ_ERR_INVALID, "rq_llama_load_gguf_dir: NULL argument");
+    Guard g(m->ctx->device);
+    const rq_llama_config& c = m->cfg;
+    const int64_t H = c.hidden, nq = m->nh_l * c.head_dim, nk = m->nkv_l * c.head_dim, I = m->I_l;
+    const int64_t out7[7] = {nq, nk, nk, H, I, I, H};
+    const int64_t in7[7] = {H, H, H, nq, H, H, I};
+    return llama_load_gguf_dir(m->ctx, m, dir, c.n_layers, c.vocab, H, m->W, m->R, out7, in7, m->owned);
 }
 
 int rq_llama_set_embedding(rq_llama* m, const uint16_t* embed_f16) {

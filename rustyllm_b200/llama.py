@@ -52,6 +52,16 @@ class StreamingLlamaQuantized:
         check(_lib.lib().rq_llama_set_layer(self.handle, layer, arr, r1.ctypes.data, r2.ctypes.data))
         self._keep.append(weights)
 
+    @classmethod
+    def from_gguf_dir(cls, cfg: dict, shard_dir, device: int = 0) -> "StreamingLlamaQuantized":
+        """The model from a directory of per-layer GGUF shards, laid out as
+        StreamingLlamaQuantized::from_pretrained reads them
+        (src/streaming_quantized.rs:451-501).  Under tensor parallelism (a
+        communicator on the device's context) each rank loads its shards."""
+        m = cls(cfg, device)
+        check(_lib.lib().rq_llama_load_gguf_dir(m.handle, str(shard_dir).encode()))
+        return m
+
     def set_embedding(self, embed_f16) -> None:
         e = np.ascontiguousarray(embed_f16).view(np.uint16)
         check(_lib.lib().rq_llama_set_embedding(self.handle, e.ctypes.data))
