@@ -464,6 +464,26 @@ def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None,
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         step_ms, gen_s, prefill_s = (float(v) for v in t.tolist())
     toks, pos = model.tokens()
+    # speculative-decoding verify forwards (forward_all over K+1 tokens at
+    # the current position, cache rolled back after each): their cost next
+    # to one decode step sets the acceptance a draft model must reach
+    verify_ms = {}
+    for kp1 in (2, 5, 9):
+        ids = np.array(toks[:kp1] + [0] * max(0, kp1 - len(toks)), dtype=np.int32)[:kp1]
+        model.forward_all(ids, pos)
+        model.truncate_caches(pos)
+        torch.cuda.synchronize()
+        reps = 5
+        t1 = time.perf_counter()
+        for _ in range(reps):
+            model.forward_all(ids, pos)
+            model.truncate_caches(pos)
+        ms = (time.perf_counter() - t1) * 1e3 / reps
+        if pg is not None:
+            t = torch.tensor([ms], device=f"cuda:{device}")
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            ms = float(t.item())
+        verify_ms[str(kp1)] = round(ms, 3)
     del g
     model.close()
     if pg is not None:
@@ -484,6 +504,10 @@ def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None,
             "weight_bytes_per_token": tok_bytes,
             "decode_hbm_gbs": round(tok_bytes / (step_ms / 1e3) / 1e9, 1),
             "tokens": toks[:new_tokens], "final_position": pos,
+            "verify_forward_ms": verify_ms,
+            "verify_note": "rq_llama_forward_all over K+1 tokens (host call incl. argmax copy), "
+                           "keys = K+1; a draft that gets accepted tokens cheaper than "
+                           "decode ms_per_token * (accepted+1) - verify pays off",
             "model_build_s": round(build_s, 2)}
 
 

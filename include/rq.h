@@ -242,6 +242,15 @@ RQ_API int rq_llama_forward(rq_llama* m, const int32_t* tokens, int64_t T, int64
  * default a chain of per-layer kernels; rq_llama_set_fused(m, 1) makes the
  * step (one GPU, one weight type) a single persistent launch that streams the
  * weights through grid-wide phases and computes the same bits. */
+/* The verify forward of speculative decoding (forward_all,
+ * src/streaming_quantized.rs:611-620): T tokens at index_pos through every
+ * layer, then the final norm and lm_head at EVERY position; argmax[T] (host
+ * or device) receives each position's greedy token and logits[T][vocab]
+ * (optional, one GPU only) the logits.  Like rq_llama_forward it leaves the
+ * KV cache at index_pos + T and the last position's token as the next
+ * input; rq_llama_truncate rolls back rejected positions. */
+RQ_API int rq_llama_forward_all(rq_llama* m, const int32_t* tokens, int64_t T, int64_t index_pos, float* logits,
+                                int32_t* argmax, void* stream);
 RQ_API int rq_llama_decode_step(rq_llama* m, void* stream);
 RQ_API int rq_llama_set_fused(rq_llama* m, int enable);
 /* RQ_ERR_TIMEOUT (and clears it) when a wait of a one-launch step timed

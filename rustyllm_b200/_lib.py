@@ -70,6 +70,7 @@ SIGNATURES.update({
     "rq_llama_set_head": (I, [P, P, P]),
     "rq_llama_forward": (I, [P, P, I64, I64, P, P, P]),
     "rq_llama_decode_step": (I, [P, P]),
+    "rq_llama_forward_all": (I, [P, P, I64, I64, P, P, P]),
     "rq_llama_set_fused": (I, [P, I]),
     "rq_llama_status": (I, [P]),
     "rq_llama_tokens": (I, [P, P, I64, ctypes.POINTER(I64), ctypes.POINTER(I64)]),

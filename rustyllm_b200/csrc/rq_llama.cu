@@ -56,6 +56,9 @@ struct rq_llama {
     float* u;
     float* hf;    // [hidden] final normed row
     float* logits;  // [vocab / W]
+    float* logits_all;  // [Tmax][vocab / W] (forward_all)
+    unsigned long long* keys;  // [Tmax] per-position argmax keys (forward_all)
+    int32_t* amax;             // [Tmax] per-position argmax tokens
     float* part;    // [Tmax][hidden] row-parallel partial sums (W > 1)
     int W, R;       // tensor-parallel world and rank
     int64_t nh_l, nkv_l, I_l, vocab_l;  // this rank's heads, kv heads, ffn rows, vocab rows
@@ -288,6 +291,102 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const __half* __restrict__
     }
 }
 
+// lm_head_kernel for NT rows of hf at once (the verify forward): the F16
+// matrix is read once; every row's accumulation has the single-row order.
+template <int NT>
+__global__ void __launch_bounds__(256) lm_head_rows_kernel(const __half* __restrict__ W,
+                                                           const float* __restrict__ hf, int64_t vocab,
+                                                           int64_t hidden, int64_t row_offset,
+                                                           float* __restrict__ logits,
+                                                           unsigned long long* __restrict__ best) {
+    extern __shared__ float xs[];  // [NT][hidden]
+    pdl_enter();
+    for (int64_t i = threadIdx.x; i < NT * hidden; i += blockDim.x) xs[i] = hf[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned long long mykey[NT];
+#pragma unroll
+    for (int t = 0; t < NT; t++) mykey[t] = 0ull;
+    for (int64_t r = (int64_t)blockIdx.x * 8 + warp; r < vocab; r += (int64_t)gridDim.x * 8) {
+        const uint4* row = reinterpret_cast<const uint4*>(W + r * hidden);
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.0f;
+        for (int64_t c = lane; c < hidden / 8; c += 32) {
+            uint4 u;
+            asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                         : "l"(row + c));
+            const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+            const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+            const float2 w2 = __half22float2(*reinterpret_cast<const __half2*>(&u.z));
+            const float2 w3 = __half22float2(*reinterpret_cast<const __half2*>(&u.w));
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                const float4 xa = reinterpret_cast<const float4*>(xs + t * hidden)[2 * c];
+                const float4 xb = reinterpret_cast<const float4*>(xs + t * hidden)[2 * c + 1];
+                float a = acc[t];
+                a = fmaf(xa.x, w0.x, a); a = fmaf(xa.y, w0.y, a);
+                a = fmaf(xa.z, w1.x, a); a = fmaf(xa.w, w1.y, a);
+                a = fmaf(xb.x, w2.x, a); a = fmaf(xb.y, w2.y, a);
+                a = fmaf(xb.z, w3.x, a); a = fmaf(xb.w, w3.y, a);
+                acc[t] = a;
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (logits) logits[t * vocab + r] = acc[t];
+                const unsigned long long key = argmax_key(acc[t], (uint32_t)(r + row_offset));
+                mykey[t] = key > mykey[t] ? key : mykey[t];
+            }
+        }
+    }
+    __shared__ unsigned long long kb[NT][8];
+    if (lane == 0)
+#pragma unroll
+        for (int t = 0; t < NT; t++) kb[t][warp] = mykey[t];
+    __syncthreads();
+    if (threadIdx.x < NT) {
+        unsigned long long k = kb[threadIdx.x][0];
+        for (int w = 1; w < 8; w++) k = kb[threadIdx.x][w] > k ? kb[threadIdx.x][w] : k;
+        atomicMax(best + threadIdx.x, k);
+    }
+}
+
+// y[row] = rmsnorm(x[row], w) for every row (blockIdx.x), the math of
+// rmsnorm_row_kernel.
+__global__ void rmsnorm_rows_kernel(const float* __restrict__ x, const float* __restrict__ w, float eps,
+                                    int64_t hidden, float* __restrict__ y) {
+    pdl_enter();
+    __shared__ float wsum[32];
+    const float* xr = x + (int64_t)blockIdx.x * hidden;
+    float* yr = y + (int64_t)blockIdx.x * hidden;
+    float s2 = 0.0f;
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) s2 = fmaf(xr[i], xr[i], s2);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = s2;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int k = 0; k < (int)(blockDim.x >> 5); k++) tot += wsum[k];
+    const float m = sqrtf(tot / (float)hidden + eps);
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) yr[i] = xr[i] / m * w[i];
+}
+
+// argmax tokens of T packed keys; the keys are cleared for the next call
+__global__ void unpack_argmax_kernel(unsigned long long* keys, int T, int32_t* out) {
+    pdl_enter();
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        out[t] = (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[t] & 0xFFFFFFFFull));
+    }
+}
+
 // Greedy step bookkeeping: next token = argmax, appended to the output list;
 // position advances by T; the argmax slot is cleared for the next step.
 __global__ void finish_step_kernel(unsigned long long* best, int32_t* tokens, int32_t* pos,
@@ -432,7 +531,9 @@ bool tensor_prefill(const rq_llama* m, int64_t T, int64_t l) {
 }
 
 // One forward over the T tokens in m->tokens at device position *m->pos.
-int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
+int head_all(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st);
+
+int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bool all_positions = false) {
     const rq_llama_config& c = m->cfg;
     const int64_t H = c.hidden, I = m->I_l, nq = m->nh_l * c.head_dim, nk = m->nkv_l * c.head_dim;
     int rc;
@@ -525,17 +626,23 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
         if (rc) return rc;
     }
     (void)nk;
-    {
-        const float* xl = m->x + (T - 1) * H;
-        const float* w = m->ln_f;
-        float eps = c.rms_eps;
-        int64_t hidden = H;
-        float* hf = m->hf;
-        void* args[] = {&xl, &w, &eps, &hidden, &hf};
-        rc = launch_simple((const void*)rmsnorm_row_kernel, dim3(1), dim3(1024), 0, st, args, "final norm kernel");
+    unsigned long long* last_key = m->best;
+    if (all_positions) {
+        rc = head_all(m, T, want_logits, st);
         if (rc) return rc;
-    }
-    {
+        last_key = m->keys + (T - 1);
+    } else {
+        {
+            const float* xl = m->x + (T - 1) * H;
+            const float* w = m->ln_f;
+            float eps = c.rms_eps;
+            int64_t hidden = H;
+            float* hf = m->hf;
+            void* args[] = {&xl, &w, &eps, &hidden, &hf};
+            rc = launch_simple((const void*)rmsnorm_row_kernel, dim3(1), dim3(1024), 0, st, args,
+                               "final norm kernel");
+            if (rc) return rc;
+        }
         const __half* W = m->lm_head;
         const float* hf = m->hf;
         int64_t vocab = m->vocab_l, hidden = H, roff = (int64_t)m->R * m->vocab_l;
@@ -552,7 +659,7 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
         }
     }
     {
-        unsigned long long* best = m->best;
+        unsigned long long* best = last_key;
         int32_t* tok = m->tokens;
         int32_t* pos = m->pos;
         int32_t* out = m->out;
@@ -562,6 +669,57 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
         rc = launch_simple((const void*)finish_step_kernel, dim3(1), dim3(1), 0, st, args, "finish kernel");
     }
     return rc;
+}
+
+// Final norm and lm_head at every one of the T positions (the verify
+// forward, forward_all of src/streaming_quantized.rs:611-620): per-position
+// argmax tokens into m->amax (a MAX all-reduce of the keys under tensor
+// parallelism) and, if wanted, logits into m->logits_all.  The lm_head
+// matrix is read once per 6 positions.
+int head_all(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st) {
+    const rq_llama_config& c = m->cfg;
+    const int64_t H = c.hidden;
+    int rc = cuda_error(cudaMemsetAsync(m->keys, 0, (size_t)T * 8, st), "memset");
+    if (rc) return rc;
+    {
+        const float* x = m->x;
+        const float* w = m->ln_f;
+        float eps = c.rms_eps;
+        int64_t hidden = H;
+        float* y = m->part;  // [T][H], free at this point
+        void* args[] = {&x, &w, &eps, &hidden, &y};
+        rc = launch_simple((const void*)rmsnorm_rows_kernel, dim3((unsigned)T), dim3(1024), 0, st, args,
+                           "final norm kernel");
+        if (rc) return rc;
+    }
+    for (int64_t t0 = 0; t0 < T; t0 += 6) {
+        const int nt = (int)std::min<int64_t>(6, T - t0);
+        const __half* W = m->lm_head;
+        const float* hf = m->part + t0 * H;
+        int64_t vocab = m->vocab_l, hidden = H, roff = (int64_t)m->R * m->vocab_l;
+        float* lg = want_logits ? m->logits_all + t0 * m->vocab_l : nullptr;
+        unsigned long long* keys = m->keys + t0;
+        void* args[] = {&W, &hf, &vocab, &hidden, &roff, &lg, &keys};
+        const unsigned grid = (unsigned)std::min<int64_t>((vocab + 7) / 8, (int64_t)m->ctx->sm_count * 8);
+        const size_t smem = (size_t)nt * H * sizeof(float);
+        const void* fn = nt == 1   ? (const void*)lm_head_rows_kernel<1>
+                         : nt == 2 ? (const void*)lm_head_rows_kernel<2>
+                         : nt == 3 ? (const void*)lm_head_rows_kernel<3>
+                         : nt == 4 ? (const void*)lm_head_rows_kernel<4>
+                         : nt == 5 ? (const void*)lm_head_rows_kernel<5>
+                                   : (const void*)lm_head_rows_kernel<6>;
+        rc = launch_simple(fn, dim3(grid), dim3(256), smem, st, args, "lm_head kernel");
+        if (rc) return rc;
+    }
+    if (m->W > 1) {
+        rc = tp_allreduce(m->ctx, m->keys, m->keys, T, 1, 1, st);
+        if (rc) return rc;
+    }
+    unsigned long long* keys = m->keys;
+    int Ti = (int)T;
+    int32_t* out = m->amax;
+    void* args[] = {&keys, &Ti, &out};
+    return launch_simple((const void*)unpack_argmax_kernel, dim3(1), dim3(256), 0, st, args, "argmax kernel");
 }
 
 template <typename T>
@@ -713,6 +871,9 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     if (!rc) rc = dalloc(m, &xqbuf, xq_bytes(T, maxin));
     if (!rc && T >= kMinTensorM) rc = dalloc(m, &xhbuf, xh_bytes(T, maxin));
     if (!rc) rc = dalloc(m, &m->best, 1);
+    if (!rc) rc = dalloc(m, &m->keys, (size_t)T);
+    if (!rc) rc = dalloc(m, &m->amax, (size_t)T);
+    if (!rc) rc = dalloc(m, &m->logits_all, (size_t)(T * m->vocab_l));
     if (!rc) rc = dalloc(m, &m->tokens, (size_t)T);
     if (!rc) rc = dalloc(m, &m->pos, 1);
     if (!rc) rc = dalloc(m, &m->out, (size_t)c.max_seq);
@@ -849,6 +1010,34 @@ int rq_llama_forward(rq_llama* m, const int32_t* tokens, int64_t T, int64_t inde
     if (!rc && next_token)
         rc = cuda_error(cudaMemcpyAsync(next_token, m->tokens, 4, cudaMemcpyDeviceToHost, st), "token copy");
     if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "rq_llama_forward sync");
+    return rc;
+}
+
+int rq_llama_forward_all(rq_llama* m, const int32_t* tokens, int64_t T, int64_t index_pos, float* logits,
+                         int32_t* argmax, void* stream) {
+    if (!m || !tokens || !argmax) return set_error(RQ_ERR_INVALID, "rq_llama_forward_all: NULL argument");
+    const rq_llama_config& c = m->cfg;
+    if (T < 1 || T > c.max_batch_tokens)
+        return set_error(RQ_ERR_INVALID, "rq_llama_forward_all: T = %lld (1..%lld)", (long long)T,
+                         (long long)c.max_batch_tokens);
+    if (index_pos < 0 || index_pos + T > c.max_seq)
+        return set_error(RQ_ERR_INVALID, "rq_llama_forward_all: positions %lld..%lld exceed max_seq %lld",
+                         (long long)index_pos, (long long)(index_pos + T), (long long)c.max_seq);
+    for (auto& L : m->layers)
+        if (!L.w[0]) return set_error(RQ_ERR_INVALID, "rq_llama_forward_all: a layer was not set");
+    if (logits && m->W > 1)
+        return set_error(RQ_ERR_UNSUPPORTED, "rq_llama_forward_all: logits are per-rank shards under tensor parallelism");
+    Guard g(m->ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    int32_t p = (int32_t)index_pos;
+    int rc = cuda_error(cudaMemcpyAsync(m->tokens, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, st), "token copy");
+    if (!rc) rc = cuda_error(cudaMemcpyAsync(m->pos, &p, 4, cudaMemcpyHostToDevice, st), "pos copy");
+    if (!rc) rc = forward_device(m, T, logits != nullptr, st, true);
+    if (!rc && logits)
+        rc = cuda_error(cudaMemcpyAsync(logits, m->logits_all, (size_t)(T * c.vocab) * 4, cudaMemcpyDefault, st),
+                        "logits copy");
+    if (!rc) rc = cuda_error(cudaMemcpyAsync(argmax, m->amax, (size_t)T * 4, cudaMemcpyDefault, st), "argmax copy");
+    if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "rq_llama_forward_all sync");
     return rc;
 }
 

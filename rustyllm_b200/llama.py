@@ -102,6 +102,17 @@ class StreamingLlamaQuantized:
                                          ctypes.byref(p)))
         return buf[:min(n.value, cap)].tolist(), p.value
 
+    def forward_all(self, input_ids, index_pos: int, want_logits: bool = False):
+        """The verify forward (forward_all, src/streaming_quantized.rs:611-620):
+        greedy token at every position, and [T, vocab] logits when wanted."""
+        ids = np.ascontiguousarray(input_ids, dtype=np.int32).reshape(-1)
+        logits = np.empty((ids.size, self.cfg["vocab"]), dtype=np.float32) if want_logits else None
+        amax = np.empty(ids.size, dtype=np.int32)
+        check(_lib.lib().rq_llama_forward_all(self.handle, ids.ctypes.data, ids.size, index_pos,
+                                              logits.ctypes.data if want_logits else None,
+                                              amax.ctypes.data, None))
+        return logits, amax.tolist()
+
     def truncate_caches(self, new_len: int) -> None:
         check(_lib.lib().rq_llama_truncate(self.handle, new_len))
 
