@@ -204,8 +204,9 @@ Q40_BYTES = lambda n_in, n_out: n_out * (n_in // 32) * 18  # noqa: E731
 
 def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
     """Config 1: the 4096x4096 Q4_0 matvec (M=1) over 16 rotating copies
-    (151 MB > L2); config 2's Q3_K sweep: the seven 70B shapes in Q3_K, each
-    over 4 rotating copies.  GB/s = GGML weight bytes + 4 (in + out) per call."""
+    (151 MB > L2); config 2's Q3_K sweep and the same sweep in Q8_0 and Q6_K:
+    the seven 70B shapes, each over 4 rotating copies.  GB/s = GGML weight
+    bytes + 4 (in + out) per call."""
     import torch
     from rustyllm_b200 import QWeight
     from rustyllm_b200._lib import check
@@ -241,6 +242,9 @@ def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
 
     res["q4_0_4096x4096_gbs"] = sweep(Q4_0, [("q4_0", 4096, 4096)], 16, Q40_BYTES)["q4_0"]
     res["q3_k_per_shape_gbs"] = sweep(Q3_K, SHAPES, 4, Q3K_BYTES)
+    # the other formats of the reference's quantizer (src/quantize.rs:29-37)
+    res["q8_0_per_shape_gbs"] = sweep(8, SHAPES, 4, lambda i, o: o * (i // 32) * 34)
+    res["q6_k_per_shape_gbs"] = sweep(14, SHAPES, 4, lambda i, o: o * (i // 256) * 210)
     res["note"] = ("single rq_linear calls (activation staging + M=1 pipeline), graph-replayed over "
                    "rotating weight copies larger than L2")
     return res

@@ -52,7 +52,7 @@ enum rq_status {
 };
 
 /* GGML type ids (ggml_type / candle GgmlDType numbering). */
-enum rq_ggml_type { RQ_Q4_0 = 2, RQ_Q3_K = 11, RQ_Q4_K = 12 };
+enum rq_ggml_type { RQ_Q4_0 = 2, RQ_Q8_0 = 8, RQ_Q3_K = 11, RQ_Q4_K = 12, RQ_Q6_K = 14 };
 
 /* ---------------------------------------------------------------- context */
 

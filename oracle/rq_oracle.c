@@ -18,6 +18,9 @@
 #define QK_K 256
 #define BS_Q4_K 144
 #define BS_Q3_K 110
+#define QK8_0 32
+#define BS_Q8_0 34
+#define BS_Q6_K 210
 
 /* ------------------------------------------------------------------ f16 */
 
@@ -83,13 +86,16 @@ int64_t rqo_block_bytes(int type) {
     case RQO_Q4_0: return BS_Q4_0;
     case RQO_Q4_K: return BS_Q4_K;
     case RQO_Q3_K: return BS_Q3_K;
+    case RQO_Q8_0: return BS_Q8_0;
+    case RQO_Q6_K: return BS_Q6_K;
     default: return 0;
     }
 }
 int64_t rqo_block_elems(int type) {
     switch (type) {
     case RQO_Q4_0: return QK4_0;
-    case RQO_Q4_K: case RQO_Q3_K: return QK_K;
+    case RQO_Q8_0: return QK8_0;
+    case RQO_Q4_K: case RQO_Q3_K: case RQO_Q6_K: return QK_K;
     default: return 0;
     }
 }
@@ -127,6 +133,90 @@ static void dequantize_q4_0_block(const uint8_t* blk, float* y) {
     for (int i = 0; i < QK4_0 / 2; i++) {
         y[i] = d * (float)((int)(blk[2 + i] & 0x0f) - 8);
         y[i + QK4_0 / 2] = d * (float)((int)(blk[2 + i] >> 4) - 8);
+    }
+}
+
+/* ------------------------------------------------------------- Q8_0 */
+/* Block of 32: f16 d, 32 int8.  Quantizer of GGML's quantize_row_q8_0_ref /
+ * candle's BlockQ8_0::from_float: d = amax / 127, id = 1/d (0 for a zero
+ * block), q = round(x * id) with ties away from zero (roundf / f32::round).
+ * Dequantization: w = d * q. */
+static void quantize_q8_0_block(const float* x, uint8_t* blk) {
+    float amax = 0.0f;
+    for (int i = 0; i < QK8_0; i++) amax = fmaxf(amax, fabsf(x[i]));
+    const float d = amax / 127.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    wr16(blk, rqo_f32_to_f16(d));
+    for (int i = 0; i < QK8_0; i++) blk[2 + i] = (uint8_t)(int8_t)roundf(x[i] * id);
+}
+
+static void dequantize_q8_0_block(const uint8_t* blk, float* y) {
+    const float d = rqo_f16_to_f32(rd16(blk));
+    for (int i = 0; i < QK8_0; i++) y[i] = d * (float)(int8_t)blk[2 + i];
+}
+
+/* ------------------------------------------------------------- Q6_K */
+/* Super-block of 256 (GGML block_q6_K): ql[128] low 4 bits, qh[64] high 2
+ * bits, scales[16] int8 (one per 16 elements), f16 d.  Half n (128 elements)
+ * uses ql[64n..], qh[32n..], scales[8n..]; for l < 32:
+ *   element 128n+l    = (ql[l]    & 15) | ((qh[l] >> 0) & 3) << 4, scale is+0
+ *   element 128n+l+32 = (ql[l+32] & 15) | ((qh[l] >> 2) & 3) << 4, scale is+2
+ *   element 128n+l+64 = (ql[l]    >> 4) | ((qh[l] >> 4) & 3) << 4, scale is+4
+ *   element 128n+l+96 = (ql[l+32] >> 4) | ((qh[l] >> 6) & 3) << 4, scale is+6
+ * with is = l / 16; w = (d * sc) * (q - 32) (GGML dequantize_row_q6_K and
+ * gguf-py's order).  The quantizer is this project's own deterministic rule
+ * (one int8 scale per 16 elements from the sub-block's largest magnitude). */
+static int q6k_index(int i, int* lb, int* hb, int* hshift, int* hi_nib, int* sidx) {
+    const int n = i / 128, r = i % 128, quarter = r / 32, l = r % 32;
+    *lb = 64 * n + l + ((quarter & 1) ? 32 : 0);
+    *hb = 128 + 32 * n + l;
+    *hshift = 2 * quarter;
+    *hi_nib = quarter >= 2;
+    *sidx = 8 * n + l / 16 + 2 * quarter;
+    return 0;
+}
+
+static void dequantize_q6_k_block(const uint8_t* blk, float* y) {
+    const float d = rqo_f16_to_f32(rd16(blk + 208));
+    for (int i = 0; i < QK_K; i++) {
+        int lb, hb, hs, hn, si;
+        q6k_index(i, &lb, &hb, &hs, &hn, &si);
+        const int lo = hn ? (blk[lb] >> 4) : (blk[lb] & 15);
+        const int q = (lo | (((blk[hb] >> hs) & 3) << 4)) - 32;
+        const float sc = (float)(int8_t)blk[192 + si];
+        y[i] = (d * sc) * (float)q;
+    }
+}
+
+static void quantize_q6_k_block(const float* x, uint8_t* blk) {
+    memset(blk, 0, BS_Q6_K);
+    float scale[16], amax_all = 0.0f;
+    for (int j = 0; j < 16; j++) {
+        float amax = 0.0f;
+        for (int k = 0; k < 16; k++) amax = fmaxf(amax, fabsf(x[16 * j + k]));
+        scale[j] = amax / 31.0f;  /* q - 32 in [-31, 31] */
+        amax_all = fmaxf(amax_all, scale[j]);
+    }
+    const float d = amax_all / 127.0f;
+    const uint16_t dh = rqo_f32_to_f16(d);
+    const float df = rqo_f16_to_f32(dh);
+    wr16(blk + 208, dh);
+    int sc[16];
+    for (int j = 0; j < 16; j++) {
+        int v = df != 0.0f ? nearest_int(scale[j] / df) : 0;
+        sc[j] = v > 127 ? 127 : (v < -128 ? -128 : v);
+        blk[192 + j] = (uint8_t)(int8_t)sc[j];
+    }
+    for (int i = 0; i < QK_K; i++) {
+        const int j = i / 16;
+        const float dl = df * (float)sc[j];
+        int q = dl != 0.0f ? nearest_int(x[i] / dl) : 0;
+        q = q < -32 ? -32 : (q > 31 ? 31 : q);
+        const int u = q + 32;  /* 0..63 */
+        int lb, hb, hs, hn, si;
+        q6k_index(i, &lb, &hb, &hs, &hn, &si);
+        blk[lb] |= (uint8_t)(hn ? ((u & 15) << 4) : (u & 15));
+        blk[hb] |= (uint8_t)((u >> 4) << hs);
     }
 }
 
@@ -320,7 +410,9 @@ int rqo_quantize(int type, const float* x, int64_t rows, int64_t in, uint8_t* ou
             const float* src = x + r * in + b * be;
             uint8_t* dst = out + (r * nb + b) * bb;
             if (type == RQO_Q4_0) quantize_q4_0_block(src, dst);
+            else if (type == RQO_Q8_0) quantize_q8_0_block(src, dst);
             else if (type == RQO_Q4_K) quantize_q4_k_block(src, dst);
+            else if (type == RQO_Q6_K) quantize_q6_k_block(src, dst);
             else quantize_q3_k_block(src, dst);
         }
     return 0;
@@ -335,7 +427,9 @@ int rqo_dequantize(int type, const uint8_t* blocks, int64_t rows, int64_t in, fl
             const uint8_t* src = blocks + (r * nb + b) * bb;
             float* dst = out + r * in + b * be;
             if (type == RQO_Q4_0) dequantize_q4_0_block(src, dst);
+            else if (type == RQO_Q8_0) dequantize_q8_0_block(src, dst);
             else if (type == RQO_Q4_K) dequantize_q4_k_block(src, dst);
+            else if (type == RQO_Q6_K) dequantize_q6_k_block(src, dst);
             else dequantize_q3_k_block(src, dst);
         }
     return 0;
@@ -424,11 +518,14 @@ float rqo_dot_q4_0_avx2order(const uint8_t* w_row, const float* x_row, int64_t b
 static float dot_kquant_f32(int type, const uint8_t* w_row, const float* x, int64_t nb) {
     float acc[8] = {0};
     float w[256];
+    const int be = (int)rqo_block_elems(type);
     for (int64_t b = 0; b < nb; b++) {
         if (type == RQO_Q4_K) dequantize_q4_k_block(w_row + b * BS_Q4_K, w);
+        else if (type == RQO_Q6_K) dequantize_q6_k_block(w_row + b * BS_Q6_K, w);
+        else if (type == RQO_Q8_0) dequantize_q8_0_block(w_row + b * BS_Q8_0, w);
         else dequantize_q3_k_block(w_row + b * BS_Q3_K, w);
-        const float* xb = x + b * QK_K;
-        for (int i = 0; i < 256; i += 8)
+        const float* xb = x + b * be;
+        for (int i = 0; i < be; i += 8)
             for (int c = 0; c < 8; c++) acc[c] = fmaf(w[i + c], xb[i + c], acc[c]);
     }
     float s = 0.0f;

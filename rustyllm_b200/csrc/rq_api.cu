@@ -56,20 +56,23 @@ Mem mem_kind(const void* p) {
                                                                                 : Mem::Host;
 }
 
-bool valid_type(int t) { return t == RQ_Q4_0 || t == RQ_Q4_K || t == RQ_Q3_K; }
+bool valid_type(int t) { return t == RQ_Q4_0 || t == RQ_Q4_K || t == RQ_Q3_K || t == RQ_Q8_0 || t == RQ_Q6_K; }
 
 const char* type_name(int t) {
     switch (t) {
     case RQ_Q4_0: return "Q4_0";
     case RQ_Q4_K: return "Q4_K";
     case RQ_Q3_K: return "Q3_K";
+    case RQ_Q8_0: return "Q8_0";
+    case RQ_Q6_K: return "Q6_K";
     default: return "?";
     }
 }
 
 int check_shape(int type, int64_t out, int64_t in) {
     if (!valid_type(type))
-        return set_error(RQ_ERR_UNSUPPORTED, "unsupported ggml type %d (Q4_0=2, Q3_K=11, Q4_K=12)", type);
+        return set_error(RQ_ERR_UNSUPPORTED, "unsupported ggml type %d (Q4_0=2, Q8_0=8, Q3_K=11, Q4_K=12, Q6_K=14)",
+                         type);
     TypeInfo ti = type_info(type);
     if (out <= 0 || in <= 0)
         return set_error(RQ_ERR_INVALID, "weight shape [%lld, %lld] must be positive", (long long)out,
@@ -110,7 +113,7 @@ int alloc_weight(rq_ctx* ctx, int type, int64_t out, int64_t in, rq_weight** res
     }
     w->qs = (uint8_t*)w->base;
     w->hdr = (uint8_t*)w->base + qpad;
-    if (type == RQ_Q3_K) {  // pad bytes of the Q3_K headers stay zero
+    if (type == RQ_Q3_K || type == RQ_Q6_K) {  // pad bytes of the headers stay zero
         e = cudaMemset(w->hdr, 0, hsz);
         if (e != cudaSuccess) {
             cudaFree(w->base);

@@ -38,6 +38,10 @@ __host__ __device__ inline TypeInfo type_info(int t) {
     case RQ_Q4_K: return TypeInfo{RQ_Q4_K, 256, 144, 128, 16};
     case RQ_Q3_K: return TypeInfo{RQ_Q3_K, 256, 110, 96, 16};
     case RQ_Q4_0: return TypeInfo{RQ_Q4_0, 32, 18, 16, 2};
+    case RQ_Q8_0: return TypeInfo{RQ_Q8_0, 32, 34, 32, 2};
+    // Q6_K: quant part ql[128] qh[64]; header scales[16] d[2] + 2 bytes of
+    // padding (4-byte aligned headers)
+    case RQ_Q6_K: return TypeInfo{RQ_Q6_K, 256, 210, 192, 20};
     default: return TypeInfo{0, 0, 0, 0, 0};
     }
 }

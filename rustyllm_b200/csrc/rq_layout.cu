@@ -23,7 +23,11 @@ __device__ __forceinline__ bool ggml_byte_slot(int type, int b, int* off) {
         if (b < 96) { *off = b; return false; }
         *off = b - 96; return true;  // scales 0..11, d 12..13
     }
-    // Q4_0: [d 2][qs 16]
+    if (type == RQ_Q6_K) {  // [ql 128][qh 64][scales 16][d 2]
+        if (b < 192) { *off = b; return false; }
+        *off = b - 192; return true;  // scales 0..15, d 16..17
+    }
+    // Q4_0: [d 2][qs 16]; Q8_0: [d 2][qs 32]
     if (b < 2) { *off = b; return true; }
     *off = b - 2; return false;
 }
@@ -111,6 +115,27 @@ __global__ void dequant_kernel(int type, const uint8_t* __restrict__ qs,
                 int hb = (hm[j] >> c) & 1;
                 v[j] = __fmul_rn(dl, (float)(low - (hb ? 0 : 4)));
             }
+        }
+    } else if (type == RQ_Q8_0) {  // w = d * q
+        const int8_t* q = reinterpret_cast<const int8_t*>(qs + t * 32);
+        float d = h2f((uint16_t)(hdr[2 * t] | (hdr[2 * t + 1] << 8)));
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = __fmul_rn(d, (float)q[j]);
+    } else if (type == RQ_Q6_K) {  // w = (d * sc) * (q - 32), GGML dequantize_row_q6_K
+        int64_t sbi = t / 8;
+        int c = (int)(t % 8);  // 32-element chunk: half n = c / 4, quarter = c % 4
+        const uint8_t* ql = qs + sbi * 192;
+        const uint8_t* qh = ql + 128;
+        const uint8_t* h = hdr + sbi * 20;
+        float d = h2f((uint16_t)(h[16] | (h[17] << 8)));
+        const int n = c / 4, quarter = c % 4;
+#pragma unroll
+        for (int l = 0; l < 32; l++) {
+            const uint8_t lb = ql[64 * n + l + ((quarter & 1) ? 32 : 0)];
+            const int lo = quarter >= 2 ? (lb >> 4) : (lb & 15);
+            const int q = (lo | (((qh[32 * n + l] >> (2 * quarter)) & 3) << 4)) - 32;
+            const float sc = (float)(int8_t)h[8 * n + l / 16 + 2 * quarter];
+            v[l] = __fmul_rn(__fmul_rn(d, sc), (float)q);
         }
     } else {  // Q4_0
         const uint8_t* q = qs + t * 16;
@@ -329,6 +354,67 @@ __global__ void quant_q40_kernel(const float* __restrict__ x, int64_t nblk_total
     }
 }
 
+// Q8_0: one thread per 32-element block (GGML quantize_row_q8_0_ref /
+// candle BlockQ8_0::from_float): d = amax / 127, q = round(x / d) with ties
+// away from zero.
+__global__ void quant_q80_kernel(const float* __restrict__ x, int64_t nblk_total, uint8_t* __restrict__ qs,
+                                 uint8_t* __restrict__ hdr) {
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= nblk_total) return;
+    const float* c = x + t * 32;
+    float amax = 0.0f;
+    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(c[i]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    reinterpret_cast<__half*>(hdr)[t] = __float2half_rn(d);
+    int8_t* q = reinterpret_cast<int8_t*>(qs + t * 32);
+    for (int i = 0; i < 32; i++) q[i] = (int8_t)(int)roundf(__fmul_rn(c[i], id));
+}
+
+// Q6_K: one thread per super-block, the oracle's rule: per 16 elements
+// scale = amax / 31, d = max scale / 127 (as f16), sc = rint(scale / d)
+// (int8), q = rint(x / (d sc)) in [-32, 31] stored as q + 32.
+__global__ void quant_q6k_kernel(const float* __restrict__ x, int64_t nsb, uint8_t* __restrict__ qs,
+                                 uint8_t* __restrict__ hdr) {
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= nsb) return;
+    const float* c = x + t * 256;
+    float scale[16], amax_all = 0.0f;
+    for (int j = 0; j < 16; j++) {
+        float amax = 0.0f;
+        for (int k = 0; k < 16; k++) amax = fmaxf(amax, fabsf(c[16 * j + k]));
+        scale[j] = __fdiv_rn(amax, 31.0f);
+        amax_all = fmaxf(amax_all, scale[j]);
+    }
+    const __half dh = __float2half_rn(__fdiv_rn(amax_all, 127.0f));
+    const float df = __half2float(dh);
+    uint8_t* h = hdr + t * 20;
+    int sc[16];
+    for (int j = 0; j < 16; j++) {
+        int v = df != 0.0f ? __float2int_rn(__fdiv_rn(scale[j], df)) : 0;
+        sc[j] = v > 127 ? 127 : (v < -128 ? -128 : v);
+        h[j] = (uint8_t)(int8_t)sc[j];
+    }
+    const uint16_t db = __half_as_ushort(dh);
+    h[16] = (uint8_t)(db & 255u);
+    h[17] = (uint8_t)(db >> 8);
+    h[18] = h[19] = 0;
+    uint8_t* ql = qs + t * 192;
+    uint8_t* qh = ql + 128;
+    for (int i = 0; i < 192; i++) ql[i] = 0;
+    for (int i = 0; i < 256; i++) {
+        const int j = i / 16;
+        const float dl = __fmul_rn(df, (float)sc[j]);
+        int q = dl != 0.0f ? __float2int_rn(__fdiv_rn(c[i], dl)) : 0;
+        q = q < -32 ? -32 : (q > 31 ? 31 : q);
+        const int u = q + 32;
+        const int n = i / 128, r = i % 128, quarter = r / 32, l = r % 32;
+        const int lb = 64 * n + l + ((quarter & 1) ? 32 : 0);
+        ql[lb] |= (uint8_t)(quarter >= 2 ? ((u & 15) << 4) : (u & 15));
+        qh[32 * n + l] |= (uint8_t)((u >> 4) << (2 * quarter));
+    }
+}
+
 int grid_for(int64_t n, int threads) {
     int64_t g = (n + threads - 1) / threads;
     return (int)(g > (1 << 30) ? (1 << 30) : g);
@@ -369,7 +455,13 @@ int launch_dequant(const rq_weight* w, float* y, cudaStream_t st) {
 
 int launch_quantize(const rq_weight* w, const float* x, cudaStream_t st) {
     if (w->out * w->in == 0) return RQ_OK;
-    if (w->type == RQ_Q4_K || w->type == RQ_Q3_K) {
+    if (w->type == RQ_Q8_0) {
+        int64_t nb = w->out * w->nblk;
+        quant_q80_kernel<<<grid_for(nb, 128), 128, 0, st>>>(x, nb, w->qs, w->hdr);
+    } else if (w->type == RQ_Q6_K) {
+        int64_t nsb = w->out * w->nblk;
+        quant_q6k_kernel<<<grid_for(nsb, 128), 128, 0, st>>>(x, nsb, w->qs, w->hdr);
+    } else if (w->type == RQ_Q4_K || w->type == RQ_Q3_K) {
         int64_t nsb = w->out * w->nblk;
         int64_t threads = nsb * 32;
         if (w->type == RQ_Q4_K)

@@ -426,4 +426,131 @@ __device__ __forceinline__ float q40_lane_row(const Q40Lane& L, uint4 qa, uint4 
     return fmaf(d0, v0, d1 * v1);
 }
 
+// ------------------------------------------------------------------- Q8_0
+// Lane of blocks b0, b0+1 (64 weights): signed int8 weights times the three
+// signed activation planes by dp4a; w = d * q.  Lanes with bit 1 set take
+// the two blocks in swapped order (first = b0+1) so a quarter-warp's
+// 128-bit shared loads spread over twice as many banks.
+struct Q80Lane {
+    uint32_t p[3][16];  // [plane][first block 0..7, second block 8..15]
+    float sx0, sx1;     // plane scales of the first / second block
+    bool swp, has1;
+};
+
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ void q80_lane_setup(Q80Lane& L, const int8_t* planes, const float4* stats, int64_t in,
+                                               int64_t nblk, int64_t b0, bool valid, bool swp) {
+    L.has1 = valid && b0 + 1 < nblk;
+    L.swp = swp && L.has1;
+    const int64_t fb = L.swp ? b0 + 1 : b0, sb = L.swp ? b0 : b0 + 1;
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+        const uint4* f = reinterpret_cast<const uint4*>(planes + p * in + fb * 32);
+        const uint4* s = reinterpret_cast<const uint4*>(planes + p * in + sb * 32);
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const uint4 a = valid ? f[k] : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 b = L.has1 ? s[k] : make_uint4(0u, 0u, 0u, 0u);
+            L.p[p][4 * k] = a.x; L.p[p][4 * k + 1] = a.y; L.p[p][4 * k + 2] = a.z; L.p[p][4 * k + 3] = a.w;
+            L.p[p][8 + 4 * k] = b.x; L.p[p][8 + 4 * k + 1] = b.y; L.p[p][8 + 4 * k + 2] = b.z;
+            L.p[p][8 + 4 * k + 3] = b.w;
+        }
+    }
+    L.sx0 = valid ? stats[fb].x : 0.0f;
+    L.sx1 = L.has1 ? stats[sb].x : 0.0f;
+}
+
+// w0..w3: the first block's 32 quant bytes (w0, w1) then the second's
+// (w2, w3); dd: the pair's f16 scales (b0 low, b0+1 high).
+__device__ __forceinline__ float q80_lane_row(const Q80Lane& L, uint4 w0, uint4 w1, uint4 w2, uint4 w3,
+                                              uint32_t dd) {
+    const uint32_t a[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const uint32_t b[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
+    int e1 = 0, e2 = 0, e3 = 0, f1 = 0, f2 = 0, f3 = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        e1 = dp4a_ss(a[k], L.p[0][k], e1);
+        e2 = dp4a_ss(a[k], L.p[1][k], e2);
+        e3 = dp4a_ss(a[k], L.p[2][k], e3);
+        f1 = dp4a_ss(b[k], L.p[0][8 + k], f1);
+        f2 = dp4a_ss(b[k], L.p[1][8 + k], f2);
+        f3 = dp4a_ss(b[k], L.p[2][8 + k], f3);
+    }
+    const uint16_t lo = (uint16_t)(dd & 0xFFFFu), hi = (uint16_t)(dd >> 16);
+    const float d0 = __half2float(__ushort_as_half(L.swp ? hi : lo));
+    const float d1 = L.has1 ? __half2float(__ushort_as_half(L.swp ? lo : hi)) : 0.0f;
+    return fmaf(d0, fix24(e1, e2, e3) * L.sx0, d1 * (fix24(f1, f2, f3) * L.sx1));
+}
+
+// ------------------------------------------------------------------- Q6_K
+// Lane g (0..3) of super-block sb: half n = g / 2, offset l0 = 16 (g & 1);
+// its 64 weights are the four groups of 16 at 128n + 32j + l0 (j = 0..3,
+// sub-block scale 8n + (g & 1) + 2j).  The 6-bit q of group j is the low
+// (j < 2) or high nibble of ql[64n + 32 (j & 1) + l0 ..] with bits 2j, 2j+1
+// of qh[32n + l0 ..] on top; w = (d * sc) * (q - 32), so per group
+// d * sc * (sx * sum(q X) - 32 * sum(x)) with the group's x sum from the
+// block stats.
+struct Q6KLane {
+    uint32_t p[3][16];  // [plane][group j words 4j .. 4j+3]
+    float sx[4], s32[4];  // per group: plane scale, 32 * sum(x)
+};
+
+__device__ __forceinline__ void q6k_lane_setup(Q6KLane& L, const int8_t* planes, const float4* stats, int64_t in,
+                                               int64_t sb, int g, bool valid) {
+    const int n = g >> 1, l0 = 16 * (g & 1);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int64_t blk = sb * 8 + 4 * n + j;  // 32-element block of group j
+#pragma unroll
+        for (int p = 0; p < 3; p++) {
+            const uint4 v = valid ? *reinterpret_cast<const uint4*>(planes + p * in + blk * 32 + l0)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+            L.p[p][4 * j] = v.x; L.p[p][4 * j + 1] = v.y; L.p[p][4 * j + 2] = v.z; L.p[p][4 * j + 3] = v.w;
+        }
+        const float4 st = valid ? stats[blk] : make_float4(0.f, 0.f, 0.f, 0.f);
+        L.sx[j] = st.x;
+        L.s32[j] = 32.0f * (l0 ? st.z : st.y);
+    }
+}
+
+// a: ql bytes of groups 0 / 2 (low / high nibbles), b: of groups 1 / 3,
+// h: the qh bytes; sc01 / sc23: the header words holding scales 8n .. 8n+3,
+// 8n+4 .. 8n+7; dw: the word holding d; gs = g & 1.
+__device__ __forceinline__ float q6k_lane_row(const Q6KLane& L, uint4 a, uint4 b, uint4 h, uint32_t sc01,
+                                              uint32_t sc23, uint32_t dw, int gs) {
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w}, hw[4] = {h.x, h.y, h.z, h.w};
+    int acc[4][3];
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const uint32_t q0 = (aw[k] & 0x0F0F0F0Fu) | ((hw[k] << 4) & 0x30303030u);
+        const uint32_t q1 = (bw[k] & 0x0F0F0F0Fu) | ((hw[k] << 2) & 0x30303030u);
+        const uint32_t q2 = ((aw[k] >> 4) & 0x0F0F0F0Fu) | (hw[k] & 0x30303030u);
+        const uint32_t q3 = ((bw[k] >> 4) & 0x0F0F0F0Fu) | ((hw[k] >> 2) & 0x30303030u);
+        const uint32_t qv[4] = {q0, q1, q2, q3};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            acc[j][0] = dp4a_us(qv[j], L.p[0][4 * j + k], acc[j][0]);
+            acc[j][1] = dp4a_us(qv[j], L.p[1][4 * j + k], acc[j][1]);
+            acc[j][2] = dp4a_us(qv[j], L.p[2][4 * j + k], acc[j][2]);
+        }
+    }
+    // scales of groups j = 0..3: bytes gs, gs + 2 of sc01, then of sc23
+    const int sh = 8 * gs;
+    const float s0 = (float)(int8_t)(sc01 >> sh), s1 = (float)(int8_t)(sc01 >> (sh + 16));
+    const float s2 = (float)(int8_t)(sc23 >> sh), s3 = (float)(int8_t)(sc23 >> (sh + 16));
+    const float v0 = fmaf(fix24(acc[0][0], acc[0][1], acc[0][2]), L.sx[0], -L.s32[0]);
+    const float v1 = fmaf(fix24(acc[1][0], acc[1][1], acc[1][2]), L.sx[1], -L.s32[1]);
+    const float v2 = fmaf(fix24(acc[2][0], acc[2][1], acc[2][2]), L.sx[2], -L.s32[2]);
+    const float v3 = fmaf(fix24(acc[3][0], acc[3][1], acc[3][2]), L.sx[3], -L.s32[3]);
+    const float d = __half2float(__ushort_as_half((uint16_t)(dw & 0xFFFFu)));
+    return d * fmaf(s0, v0, fmaf(s1, v1, fmaf(s2, v2, s3 * v3)));
+}
+
 }  // namespace rq

@@ -80,15 +80,15 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
     if (warp == 0) {
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
-            int it = 0;
+            int it = 0, slot = 0, use = 0;  // stage count, ring slot, uses of the slot
             bool ok = true;
             for (int j = 0; j < p.njobs && ok; j++) {
                 const PipeJob& jb = p.jobs[j];
                 int64_t rb;
                 int nrows;
                 job_rows(jb, &rb, &nrows);
-                for (int r0 = 0; r0 < nrows; r0 += p.RS, it++) {
-                    const int slot = it % p.nstage, use = it / p.nstage;
+                for (int r0 = 0; r0 < nrows; r0 += p.RS, it++, slot = slot + 1 == p.nstage ? 0 : slot + 1,
+                         use += slot == 0) {
                     if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
                     const int rows = min(p.RS, nrows - r0);
                     const int64_t row = rb + r0;
@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         LaneOffsets o;
         asm volatile("griddepcontrol.wait;" ::: "memory");
         const int8_t* cur_x = nullptr;
-        int it = 0, roff = 0;
+        int slot = 0, use = 0, roff = 0;
         bool ok = true;
         for (int j = 0; j < p.njobs && ok; j++) {
             const PipeJob& jb = p.jobs[j];
@@ -122,8 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
                 lane_setup<TYPE>(L, o, p.nblk, p.in, jb.xq, s, lane);
                 cur_x = jb.xq.planes;
             }
-            for (int r0 = 0; r0 < nrows; r0 += p.RS, it++) {
-                const int slot = it % p.nstage, use = it / p.nstage;
+            for (int r0 = 0; r0 < nrows; r0 += p.RS, slot = slot + 1 == p.nstage ? 0 : slot + 1, use += slot == 0) {
                 if (!mbar_wait(full0 + 8 * slot, use & 1)) {
                     if (lane == 0 && p.err) atomicExch(p.err, 1);
                     ok = false;
@@ -259,6 +258,8 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
     switch (w0->type) {
     case RQ_Q4_K: return launch_pipe_type<RQ_Q4_K>(p, rpw, grid, threads, smem, st);
     case RQ_Q3_K: return launch_pipe_type<RQ_Q3_K>(p, rpw, grid, threads, smem, st);
+    case RQ_Q8_0: return launch_pipe_type<RQ_Q8_0>(p, rpw, grid, threads, smem, st);
+    case RQ_Q6_K: return launch_pipe_type<RQ_Q6_K>(p, rpw, grid, threads, smem, st);
     default: return launch_pipe_type<RQ_Q4_0>(p, rpw, grid, threads, smem, st);
     }
 }

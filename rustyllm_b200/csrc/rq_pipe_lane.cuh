@@ -15,6 +15,10 @@ template <>
 struct LaneOf<RQ_Q3_K> { using T = Q3KLane; };
 template <>
 struct LaneOf<RQ_Q4_0> { using T = Q40Lane; };
+template <>
+struct LaneOf<RQ_Q8_0> { using T = Q80Lane; };
+template <>
+struct LaneOf<RQ_Q6_K> { using T = Q6KLane; };
 
 // Per-lane constants of K-slice s: activation planes and the lane's
 // shared-memory byte offsets inside a row.  Lanes past the end of a partial
@@ -22,12 +26,39 @@ struct LaneOf<RQ_Q4_0> { using T = Q40Lane; };
 // loop needs no per-lane branch.
 struct LaneOffsets {
     uint32_t qa, qb, h;
+    uint32_t q3;  // Q6_K: offset of the lane's qh bytes
+    uint32_t hd;  // Q6_K: offset of the super-block's d
+    int gs;       // Q6_K: g & 1
 };
 
 template <int TYPE>
 __device__ __forceinline__ void lane_setup(typename LaneOf<TYPE>::T& L, LaneOffsets& o, int64_t nblk, int64_t in,
                                            const XQ& xq, int s, int lane) {
-    if constexpr (TYPE == RQ_Q4_0) {
+    if constexpr (TYPE == RQ_Q8_0) {
+        // blocks b0, b0+1 of slice s (64 blocks of 32 per slice)
+        const int64_t b0 = (int64_t)s * 64 + 2 * lane;
+        const bool valid = b0 < nblk;
+        const uint32_t l = valid ? (uint32_t)lane : 0u;
+        const bool swp = (l >> 1) & 1u;
+        q80_lane_setup(L, xq.planes, xq.stats, in, nblk, valid ? b0 : (int64_t)s * 64, valid, swp);
+        o.qa = (uint32_t)(s * 2048) + 64u * l + (L.swp ? 32u : 0u);  // the first block's 32 bytes
+        o.qb = o.qa ^ 32u;                                             // the second block's
+        o.h = (uint32_t)(s * 128) + 4u * l;
+    } else if constexpr (TYPE == RQ_Q6_K) {
+        // super-block 8s + lane / 4, lane g = lane % 4 (192 quant + 20 header bytes each)
+        const int64_t sb = (int64_t)s * 8 + (lane >> 2);
+        const bool valid = sb < nblk;
+        const uint32_t sbl = valid ? (uint32_t)(lane >> 2) : 0u;
+        const int g = lane & 3, n = g >> 1, l0 = 16 * (g & 1);
+        q6k_lane_setup(L, xq.planes, xq.stats, in, valid ? sb : (int64_t)s * 8, g, valid);
+        const uint32_t base = (uint32_t)(s * 8 * 192) + 192u * sbl;
+        o.qa = base + 64u * (uint32_t)n + (uint32_t)l0;
+        o.qb = o.qa + 32u;
+        o.q3 = base + 128u + 32u * (uint32_t)n + (uint32_t)l0;
+        o.h = (uint32_t)(s * 8 * 20) + 20u * sbl + 8u * (uint32_t)n;
+        o.hd = (uint32_t)(s * 8 * 20) + 20u * sbl + 16u;
+        o.gs = g & 1;
+    } else if constexpr (TYPE == RQ_Q4_0) {
         const int64_t b0 = (int64_t)s * 64 + 2 * lane;
         const bool valid = b0 < nblk;
         if (valid) {
@@ -78,7 +109,16 @@ __device__ __forceinline__ float lane_row(const typename LaneOf<TYPE>::T& L, con
                                           const uint8_t* q, const uint8_t* h) {
     const uint4 a = *reinterpret_cast<const uint4*>(q + o.qa);
     const uint4 b = *reinterpret_cast<const uint4*>(q + o.qb);
-    if constexpr (TYPE == RQ_Q4_K) {
+    if constexpr (TYPE == RQ_Q8_0) {
+        const uint4 a1 = *reinterpret_cast<const uint4*>(q + o.qa + 16);
+        const uint4 b1 = *reinterpret_cast<const uint4*>(q + o.qb + 16);
+        return q80_lane_row(L, a, a1, b, b1, *reinterpret_cast<const uint32_t*>(h + o.h));
+    } else if constexpr (TYPE == RQ_Q6_K) {
+        const uint4 hh = *reinterpret_cast<const uint4*>(q + o.q3);
+        const uint32_t* hw = reinterpret_cast<const uint32_t*>(h + o.h);
+        const uint32_t dw = *reinterpret_cast<const uint32_t*>(h + o.hd);
+        return q6k_lane_row(L, a, b, hh, hw[0], hw[1], dw, o.gs);
+    } else if constexpr (TYPE == RQ_Q4_K) {
         return q4kp_lane_row(L, a, b, *reinterpret_cast<const uint4*>(h + o.h), 0.0f);
     } else if constexpr (TYPE == RQ_Q3_K) {
         return q3k_lane_row(L, a, b, *reinterpret_cast<const uint4*>(h + o.h));

@@ -27,7 +27,8 @@ def main():
     rng = np.random.default_rng(20261201)
     out = {}
     specs = {"q4_0": (GT.Q4_0, 18, [0]), "q4_k": (GT.Q4_K, 144, [0, 2]),
-             "q3_k": (GT.Q3_K, 110, [108])}
+             "q3_k": (GT.Q3_K, 110, [108]), "q8_0": (GT.Q8_0, 34, [0]),
+             "q6_k": (GT.Q6_K, 210, [208])}
     for name, (gt, bb, offs) in specs.items():
         raw = finite_blocks(rng, 96, bb, offs)
         out[f"{name}_blocks"] = raw
@@ -38,6 +39,12 @@ def main():
     w[1, 5] = -3.0                                   # negative max
     out["q4_0_quant_in"] = w
     out["q4_0_quant_out"] = quants.quantize(w, GT.Q4_0).reshape(8, -1)
+    # Q8_0 quantizer (GGML quantize_row_q8_0_ref; random data has no rounding
+    # ties, where gguf-py's half-to-even and candle's half-away would differ)
+    w8 = (rng.standard_normal((8, 256)) * 0.1).astype(np.float32)
+    w8[0, :32] = 0.0
+    out["q8_0_quant_in"] = w8
+    out["q8_0_quant_out"] = quants.quantize(w8, GT.Q8_0).reshape(8, -1)
     np.savez_compressed(os.path.join(HERE, "golden_gguf.npz"), **out)
     print({k: v.shape for k, v in out.items()})
 

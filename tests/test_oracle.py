@@ -29,12 +29,31 @@ def test_f16_conversion_matches_numpy(oracle):
     assert ok.all()
 
 
-@pytest.mark.parametrize("name,qtype", [("q4_0", 2), ("q4_k", 12), ("q3_k", 11)])
+@pytest.mark.parametrize("name,qtype", [("q4_0", 2), ("q4_k", 12), ("q3_k", 11), ("q8_0", 8), ("q6_k", 14)])
 def test_dequant_matches_gguf_golden(oracle, golden, name, qtype):
     blocks = golden[f"{name}_blocks"]
     want = golden[f"{name}_dequant"]
     got = oracle.dequantize(qtype, blocks, blocks.shape[0], want.shape[1])
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_q8_0_quantizer_matches_gguf_golden(oracle, golden):
+    got = oracle.quantize(oracle.Q8_0, golden["q8_0_quant_in"])
+    assert np.array_equal(got, golden["q8_0_quant_out"])
+
+
+def test_q6_k_quantizer_roundtrip(oracle):
+    """The Q6_K quantizer is this project's own rule (unpinned, like Q4_K /
+    Q3_K): its blocks dequantize close to the input and re-quantize to the
+    same bytes."""
+    rng = np.random.default_rng(9)
+    w = (rng.standard_normal((6, 512)) * 0.02).astype(np.float32)
+    w[0, :256] = 0.0
+    b = oracle.quantize(oracle.Q6_K, w)
+    d = oracle.dequantize(oracle.Q6_K, b, 6, 512)
+    assert np.all(d[0, :256] == 0.0)
+    assert np.linalg.norm(d - w) / np.linalg.norm(w) < 0.03
+    assert np.array_equal(oracle.quantize(oracle.Q6_K, d), b)
 
 
 def test_q4_0_quantizer_matches_gguf_golden(oracle, golden):
