@@ -89,6 +89,7 @@ struct OpPlain {
     const float* x;
     __device__ void setup(int64_t, int64_t, float*) {}
     __device__ float at(int64_t m, int64_t in, int64_t k) const { return x[m * in + k]; }
+    __device__ void block(int64_t m, int64_t in, int64_t b, float (&v)[32]) const { load_block(x + m * in + 32 * b, v); }
 };
 struct OpRms {
     const float* x;
@@ -118,6 +119,13 @@ struct OpRms {
         __syncthreads();
     }
     __device__ float at(int64_t m, int64_t in, int64_t k) const { return x[m * in + k] / mden * w[k]; }
+    __device__ void block(int64_t m, int64_t in, int64_t b, float (&v)[32]) const {
+        float ww[32];
+        load_block(x + m * in + 32 * b, v);
+        load_block(w + 32 * b, ww);
+#pragma unroll
+        for (int k = 0; k < 32; k++) v[k] = v[k] / mden * ww[k];
+    }
 };
 struct OpSwiglu {
     const float* g;
@@ -126,6 +134,13 @@ struct OpSwiglu {
     __device__ float at(int64_t m, int64_t in, int64_t k) const {
         const float v = g[m * in + k];
         return v / (1.0f + expf(-v)) * u[m * in + k];
+    }
+    __device__ void block(int64_t m, int64_t in, int64_t b, float (&v)[32]) const {
+        float uu[32];
+        load_block(g + m * in + 32 * b, v);
+        load_block(u + m * in + 32 * b, uu);
+#pragma unroll
+        for (int k = 0; k < 32; k++) v[k] = v[k] / (1.0f + expf(-v[k])) * uu[k];
     }
 };
 
@@ -155,9 +170,11 @@ __global__ void __launch_bounds__(256) xh_stage_kernel(Op op, int64_t in, __half
     for (int64_t b = threadIdx.x; b < in / 32; b += blockDim.x) {
         float s = 0.0f;
         __half h[32], l[32];
+        float vb[32];
+        op.block(m, in, b, vb);  // the values of at(), loaded as 16-byte vectors
 #pragma unroll
         for (int k = 0; k < 32; k++) {
-            const float t = op.at(m, in, 32 * b + k) * inv;
+            const float t = vb[k] * inv;
             s += t;
             h[k] = __float2half_rn(t);
             l[k] = __float2half_rn(t - __half2float(h[k]));
