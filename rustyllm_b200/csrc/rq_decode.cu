@@ -107,11 +107,24 @@ __device__ __forceinline__ bool grid_sync(const DecParams& p, unsigned& nbar, in
     return *flag != 0;
 }
 
+// Position in the ring of weight stages: slot, and how often the ring has
+// wrapped (the slot's use count, whose parity is the mbarrier phase).
+struct RingPos {
+    int slot = 0, use = 0;
+    __device__ __forceinline__ void next(int n) {
+        if (++slot == n) {
+            slot = 0;
+            use++;
+        }
+    }
+};
+
 // ---------------------------------------------------------------- producer
 template <int TYPE>
 __device__ __noinline__ void produce(const DecParams& p, uint32_t full0, uint32_t empty0, uint32_t ring) {
     const uint64_t pol = policy_evict_first();
     int it = 0;
+    RingPos rp;
     bool ok = true;
     for (int l = 0; l < p.n_layers && ok; l++) {
         const DecLayer& Ly = p.layers[l];
@@ -122,8 +135,8 @@ __device__ __noinline__ void produce(const DecParams& p, uint32_t full0, uint32_
             int64_t rb;
             int n;
             rows_of(job_out(p, j), &rb, &n);
-            for (int r0 = 0; r0 < n; r0 += RS, it++) {
-                const int slot = it % p.nslot, use = it / p.nslot;
+            for (int r0 = 0; r0 < n; r0 += RS, it++, rp.next(p.nslot)) {
+                const int slot = rp.slot, use = rp.use;
                 if (use > 0 && !mbar_wait_err(empty0 + 8 * slot, (use - 1) & 1, p.err)) {
                     ok = false;
                     break;
@@ -150,7 +163,7 @@ __device__ __noinline__ void produce(const DecParams& p, uint32_t full0, uint32_
 // c / S + G, ...).  Epilogue: y = sum over slices in slice order (+ x for o
 // and down).
 template <int TYPE>
-__device__ __noinline__ void matvec_phase(const DecParams& p, const XQ xsrc, int j0, int nj, int& it, float* red,
+__device__ __noinline__ void matvec_phase(const DecParams& p, const XQ xsrc, int j0, int nj, RingPos& it, float* red,
                              const uint8_t* ring_p, uint32_t full0, uint32_t empty0, int cw, int lane, int ct,
                              bool& ok) {
     const int cls = job_cls(j0);
@@ -167,8 +180,8 @@ __device__ __noinline__ void matvec_phase(const DecParams& p, const XQ xsrc, int
         int64_t rb;
         int n;
         rows_of(job_out(p, j), &rb, &n);
-        for (int r0 = 0; r0 < n; r0 += RS, it++) {
-            const int slot = it % p.nslot, use = it / p.nslot;
+        for (int r0 = 0; r0 < n; r0 += RS, it.next(p.nslot)) {
+            const int slot = it.slot, use = it.use;
             if (ok && !mbar_wait_err(full0 + 8 * slot, use & 1, p.err)) {
                 ok = false;
                 if (lane == 0) atomicExch(p.err, 1);
@@ -356,7 +369,7 @@ __global__ void __launch_bounds__(kThreadsD, 1) decode_step_kernel(const __grid_
     const int cw = warp - 1, ct = threadIdx.x - 32;
     unsigned nbar = 0;
     bool ok = true;
-    int it = 0;
+    RingPos it;
     // embedding row of the current token into x (this CTA's rows of x)
     {
         int32_t tok = p.tokens[0];
