@@ -204,7 +204,8 @@ Q40_BYTES = lambda n_in, n_out: n_out * (n_in // 32) * 18  # noqa: E731
 
 def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
     """Config 1: the 4096x4096 Q4_0 matvec (M=1) over 16 rotating copies
-    (151 MB > L2); config 2's Q3_K sweep and the same sweep in Q8_0 and Q6_K:
+    (151 MB > L2); config 2's Q3_K sweep and the same sweep in Q8_0, Q6_K,
+    Q5_K and Q2_K:
     the seven 70B shapes, each over 4 rotating copies.  GB/s = GGML weight
     bytes + 4 (in + out) per call."""
     import torch
@@ -245,6 +246,8 @@ def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
     # the other formats of the reference's quantizer (src/quantize.rs:29-37)
     res["q8_0_per_shape_gbs"] = sweep(8, SHAPES, 4, lambda i, o: o * (i // 32) * 34)
     res["q6_k_per_shape_gbs"] = sweep(14, SHAPES, 4, lambda i, o: o * (i // 256) * 210)
+    res["q5_k_per_shape_gbs"] = sweep(13, SHAPES, 4, lambda i, o: o * (i // 256) * 176)
+    res["q2_k_per_shape_gbs"] = sweep(10, SHAPES, 4, lambda i, o: o * (i // 256) * 84)
     res["note"] = ("single rq_linear calls (activation staging + M=1 pipeline), graph-replayed over "
                    "rotating weight copies larger than L2")
     return res

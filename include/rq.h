@@ -10,7 +10,8 @@
  *     the way q4_kernel.rs:90-107 builds its messages.  Nothing aborts.
  *   - Weights are GGML block bytes exactly as they sit in a GGUF tensor
  *     (Q4_0 = 18-byte blocks of 32, Q4_K = 144-byte super-blocks of 256,
- *     Q3_K = 110-byte super-blocks of 256), row-major [out][in/block].
+ *     Q3_K = 110-byte super-blocks of 256; also Q8_0 = 34 / 32, Q6_K = 210,
+ *     Q5_K = 176 and Q2_K = 84 bytes per 256), row-major [out][in/block].
  *     The library copies them to the GPU and owns the device copy.
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
  *   - Activation pointers (x, y) may be host or device memory; host pointers
@@ -52,7 +53,7 @@ enum rq_status {
 };
 
 /* GGML type ids (ggml_type / candle GgmlDType numbering). */
-enum rq_ggml_type { RQ_Q4_0 = 2, RQ_Q8_0 = 8, RQ_Q3_K = 11, RQ_Q4_K = 12, RQ_Q6_K = 14 };
+enum rq_ggml_type { RQ_Q4_0 = 2, RQ_Q8_0 = 8, RQ_Q2_K = 10, RQ_Q3_K = 11, RQ_Q4_K = 12, RQ_Q5_K = 13, RQ_Q6_K = 14 };
 
 /* ---------------------------------------------------------------- context */
 
@@ -85,7 +86,8 @@ RQ_API int rq_weight_upload(rq_ctx* ctx, int ggml_type, const void* blocks, size
 /* Quantize an f32 matrix [out][in] that is already on this device straight
  * into a device weight (no host round trip); the call returns once the
  * weight is written.  Q4_0 follows the rule of
- * src/q4_kernel.rs:137-163; Q4_K/Q3_K use librq's deterministic quantizer
+ * src/q4_kernel.rs:137-163, Q8_0 GGML's rounding rule; the K-types use
+ * librq's deterministic quantizers
  * (the counterpart of candle's QTensor::quantize, src/quantize.rs:131). */
 RQ_API int rq_weight_quantize(rq_ctx* ctx, int ggml_type, const float* w_dev, int64_t out, int64_t in,
                        rq_weight** w, void* stream);
@@ -96,8 +98,8 @@ RQ_API int rq_weight_download(rq_ctx* ctx, const rq_weight* w, void* blocks_host
 RQ_API int rq_weight_free(rq_ctx* ctx, rq_weight* w);
 
 /* Any of the out-pointers may be NULL.  device_bytes counts the library's
- * device copy (equal to the GGML byte count, plus 2 pad bytes per Q3_K
- * super-block). */
+ * device copy (equal to the GGML byte count, plus 2 pad bytes per Q3_K or
+ * Q6_K super-block). */
 RQ_API int rq_weight_info(const rq_weight* w, int* ggml_type, int64_t* out, int64_t* in,
                    size_t* device_bytes);
 

@@ -21,6 +21,8 @@
 #define QK8_0 32
 #define BS_Q8_0 34
 #define BS_Q6_K 210
+#define BS_Q5_K 176
+#define BS_Q2_K 84
 
 /* ------------------------------------------------------------------ f16 */
 
@@ -88,6 +90,8 @@ int64_t rqo_block_bytes(int type) {
     case RQO_Q3_K: return BS_Q3_K;
     case RQO_Q8_0: return BS_Q8_0;
     case RQO_Q6_K: return BS_Q6_K;
+    case RQO_Q5_K: return BS_Q5_K;
+    case RQO_Q2_K: return BS_Q2_K;
     default: return 0;
     }
 }
@@ -95,7 +99,7 @@ int64_t rqo_block_elems(int type) {
     switch (type) {
     case RQO_Q4_0: return QK4_0;
     case RQO_Q8_0: return QK8_0;
-    case RQO_Q4_K: case RQO_Q3_K: case RQO_Q6_K: return QK_K;
+    case RQO_Q4_K: case RQO_Q3_K: case RQO_Q6_K: case RQO_Q5_K: case RQO_Q2_K: return QK_K;
     default: return 0;
     }
 }
@@ -316,6 +320,155 @@ static void quantize_q4_k_block(const float* x, uint8_t* blk) {
             qs[32 * g + j] = (uint8_t)(L[64 * g + j] | (L[64 * g + 32 + j] << 4));
 }
 
+/* ------------------------------------------------------------- Q5_K */
+/* Super-block of 256: f16 d, f16 dmin, the 12 bytes of 6-bit (scale, min)
+ * of Q4_K, qh[32], qs[128].  Element 64g+j (sub-block 2g) = low nibble of
+ * qs[32g+j] | bit 2g of qh[j] << 4; element 64g+32+j (sub-block 2g+1) = high
+ * nibble | bit 2g+1 of qh[j] << 4.  w = (d*sc)*q - (dmin*m) (gguf-py's
+ * Q5_K.dequantize_blocks).  The quantizer is this project's Q4_K rule with
+ * 5-bit q (unpinned). */
+static void dequantize_q5_k_block(const uint8_t* blk, float* y) {
+    float d = rqo_f16_to_f32(rd16(blk));
+    float dmin = rqo_f16_to_f32(rd16(blk + 2));
+    const uint8_t* sc = blk + 4;
+    const uint8_t* qh = blk + 16;
+    const uint8_t* qs = blk + 48;
+    for (int g = 0; g < 4; g++) {
+        int s0, m0, s1, m1;
+        q4k_get_scale_min(2 * g, sc, &s0, &m0);
+        q4k_get_scale_min(2 * g + 1, sc, &s1, &m1);
+        float d0 = d * (float)s0, mm0 = dmin * (float)m0;
+        float d1 = d * (float)s1, mm1 = dmin * (float)m1;
+        for (int j = 0; j < 32; j++) {
+            int q0 = (qs[32 * g + j] & 0x0f) | (((qh[j] >> (2 * g)) & 1) << 4);
+            int q1 = (qs[32 * g + j] >> 4) | (((qh[j] >> (2 * g + 1)) & 1) << 4);
+            y[64 * g + j] = d0 * (float)q0 - mm0;
+            y[64 * g + 32 + j] = d1 * (float)q1 - mm1;
+        }
+    }
+}
+
+static void quantize_q5_k_block(const float* x, uint8_t* blk) {
+    memset(blk, 0, BS_Q5_K);
+    float scale[8], mins[8];
+    float max_scale = 0.0f, max_min = 0.0f;
+    for (int s = 0; s < 8; s++) {
+        float mn = x[32 * s], mx = x[32 * s];
+        for (int i = 1; i < 32; i++) {
+            float v = x[32 * s + i];
+            if (v < mn) mn = v;
+            if (v > mx) mx = v;
+        }
+        if (mn > 0.0f) mn = 0.0f;
+        scale[s] = (mx - mn) / 31.0f;
+        mins[s] = -mn;
+        if (scale[s] > max_scale) max_scale = scale[s];
+        if (mins[s] > max_min) max_min = mins[s];
+    }
+    float inv_scale = max_scale > 0.0f ? 63.0f / max_scale : 0.0f;
+    float inv_min = max_min > 0.0f ? 63.0f / max_min : 0.0f;
+    int ls[8], lm[8];
+    for (int s = 0; s < 8; s++) {
+        int a = nearest_int(inv_scale * scale[s]);
+        int b = nearest_int(inv_min * mins[s]);
+        ls[s] = a > 63 ? 63 : a;
+        lm[s] = b > 63 ? 63 : b;
+    }
+    uint16_t dh = rqo_f32_to_f16(max_scale / 63.0f);
+    uint16_t mh = rqo_f32_to_f16(max_min / 63.0f);
+    wr16(blk, dh);
+    wr16(blk + 2, mh);
+    uint8_t* sc = blk + 4;
+    for (int j = 0; j < 4; j++) {
+        sc[j] = (uint8_t)(ls[j] | ((ls[j + 4] >> 4) << 6));
+        sc[j + 4] = (uint8_t)(lm[j] | ((lm[j + 4] >> 4) << 6));
+        sc[j + 8] = (uint8_t)((ls[j + 4] & 0x0f) | ((lm[j + 4] & 0x0f) << 4));
+    }
+    float d = rqo_f16_to_f32(dh), dmin = rqo_f16_to_f32(mh);
+    uint8_t* qh = blk + 16;
+    uint8_t* qs = blk + 48;
+    for (int s = 0; s < 8; s++) {
+        float dl = d * (float)ls[s];
+        float ml = dmin * (float)lm[s];
+        for (int i = 0; i < 32; i++) {
+            int q = 0;
+            if (dl != 0.0f) {
+                q = nearest_int((x[32 * s + i] + ml) / dl);
+                q = q < 0 ? 0 : (q > 31 ? 31 : q);
+            }
+            const int g = s / 2;
+            qs[32 * g + i] |= (uint8_t)((s & 1) ? ((q & 15) << 4) : (q & 15));
+            qh[i] |= (uint8_t)((q >> 4) << s);
+        }
+    }
+}
+
+/* ------------------------------------------------------------- Q2_K */
+/* Super-block of 256: scales[16] (low nibble: scale, high nibble: min of a
+ * 16-element sub-block), qs[64] (2-bit), f16 d, f16 dmin.  Element
+ * 128n+32j+l = (qs[32n+l] >> 2j) & 3 of sub-block (128n+32j+l)/16;
+ * w = (d*sc)*q - (dmin*m) (gguf-py's Q2_K.dequantize_blocks).  The
+ * quantizer is this project's own rule (unpinned). */
+static void dequantize_q2_k_block(const uint8_t* blk, float* y) {
+    const uint8_t* sc = blk;
+    const uint8_t* qs = blk + 16;
+    float d = rqo_f16_to_f32(rd16(blk + 80));
+    float dmin = rqo_f16_to_f32(rd16(blk + 82));
+    for (int n = 0; n < 2; n++)
+        for (int j = 0; j < 4; j++)
+            for (int l = 0; l < 32; l++) {
+                const int e = 128 * n + 32 * j + l, s = e / 16;
+                const float dl = d * (float)(sc[s] & 15), ml = dmin * (float)(sc[s] >> 4);
+                y[e] = dl * (float)((qs[32 * n + l] >> (2 * j)) & 3) - ml;
+            }
+}
+
+static void quantize_q2_k_block(const float* x, uint8_t* blk) {
+    memset(blk, 0, BS_Q2_K);
+    float scale[16], mins[16];
+    float max_scale = 0.0f, max_min = 0.0f;
+    for (int s = 0; s < 16; s++) {
+        float mn = x[16 * s], mx = x[16 * s];
+        for (int i = 1; i < 16; i++) {
+            float v = x[16 * s + i];
+            if (v < mn) mn = v;
+            if (v > mx) mx = v;
+        }
+        if (mn > 0.0f) mn = 0.0f;
+        scale[s] = (mx - mn) / 3.0f;
+        mins[s] = -mn;
+        if (scale[s] > max_scale) max_scale = scale[s];
+        if (mins[s] > max_min) max_min = mins[s];
+    }
+    float inv_scale = max_scale > 0.0f ? 15.0f / max_scale : 0.0f;
+    float inv_min = max_min > 0.0f ? 15.0f / max_min : 0.0f;
+    int ls[16], lm[16];
+    for (int s = 0; s < 16; s++) {
+        int a = nearest_int(inv_scale * scale[s]);
+        int b = nearest_int(inv_min * mins[s]);
+        ls[s] = a > 15 ? 15 : a;
+        lm[s] = b > 15 ? 15 : b;
+        blk[s] = (uint8_t)(ls[s] | (lm[s] << 4));
+    }
+    uint16_t dh = rqo_f32_to_f16(max_scale / 15.0f);
+    uint16_t mh = rqo_f32_to_f16(max_min / 15.0f);
+    wr16(blk + 80, dh);
+    wr16(blk + 82, mh);
+    float d = rqo_f16_to_f32(dh), dmin = rqo_f16_to_f32(mh);
+    uint8_t* qs = blk + 16;
+    for (int e = 0; e < 256; e++) {
+        const int s = e / 16;
+        const float dl = d * (float)ls[s], ml = dmin * (float)lm[s];
+        int q = 0;
+        if (dl != 0.0f) {
+            q = nearest_int((x[e] + ml) / dl);
+            q = q < 0 ? 0 : (q > 3 ? 3 : q);
+        }
+        const int n = e / 128, j = (e % 128) / 32, l = e % 32;
+        qs[32 * n + l] |= (uint8_t)(q << (2 * j));
+    }
+}
+
 /* ------------------------------------------------------------- Q3_K */
 /* Super-block of 256: hmask[32], qs[64], scales[12], f16 d (110 bytes).
  * Element i: h=i/128, s=(i%128)/32, j=i%32; low 2 bits (qs[32h+j] >> 2s)&3;
@@ -413,6 +566,8 @@ int rqo_quantize(int type, const float* x, int64_t rows, int64_t in, uint8_t* ou
             else if (type == RQO_Q8_0) quantize_q8_0_block(src, dst);
             else if (type == RQO_Q4_K) quantize_q4_k_block(src, dst);
             else if (type == RQO_Q6_K) quantize_q6_k_block(src, dst);
+            else if (type == RQO_Q5_K) quantize_q5_k_block(src, dst);
+            else if (type == RQO_Q2_K) quantize_q2_k_block(src, dst);
             else quantize_q3_k_block(src, dst);
         }
     return 0;
@@ -430,6 +585,8 @@ int rqo_dequantize(int type, const uint8_t* blocks, int64_t rows, int64_t in, fl
             else if (type == RQO_Q8_0) dequantize_q8_0_block(src, dst);
             else if (type == RQO_Q4_K) dequantize_q4_k_block(src, dst);
             else if (type == RQO_Q6_K) dequantize_q6_k_block(src, dst);
+            else if (type == RQO_Q5_K) dequantize_q5_k_block(src, dst);
+            else if (type == RQO_Q2_K) dequantize_q2_k_block(src, dst);
             else dequantize_q3_k_block(src, dst);
         }
     return 0;
@@ -523,6 +680,8 @@ static float dot_kquant_f32(int type, const uint8_t* w_row, const float* x, int6
         if (type == RQO_Q4_K) dequantize_q4_k_block(w_row + b * BS_Q4_K, w);
         else if (type == RQO_Q6_K) dequantize_q6_k_block(w_row + b * BS_Q6_K, w);
         else if (type == RQO_Q8_0) dequantize_q8_0_block(w_row + b * BS_Q8_0, w);
+        else if (type == RQO_Q5_K) dequantize_q5_k_block(w_row + b * BS_Q5_K, w);
+        else if (type == RQO_Q2_K) dequantize_q2_k_block(w_row + b * BS_Q2_K, w);
         else dequantize_q3_k_block(w_row + b * BS_Q3_K, w);
         const float* xb = x + b * be;
         for (int i = 0; i < be; i += 8)

@@ -13,9 +13,10 @@
  *   - GGML Q4_K / Q3_K dequantization  (candle-core 0.10.2 k-quants, reached
  *     through QMatMul at src/streaming_quantized.rs:63-70); pinned bit-for-bit
  *     against gguf-py 0.19.0 golden vectors in tests/golden/
- *   - GGML Q8_0 (quantizer and dequantization) and Q6_K dequantization, the
- *     other formats of src/quantize.rs:29-37; pinned against gguf-py 0.19.0
- *     (Q8_0 quantize + dequantize, Q6_K dequantize) by tests/test_oracle.py
+ *   - GGML Q8_0 (quantizer and dequantization) and Q6_K / Q5_K / Q2_K
+ *     dequantization, the other formats of src/quantize.rs:29-37; pinned
+ *     against gguf-py 0.19.0 (Q8_0 quantize + dequantize, the K-types'
+ *     dequantize) by tests/test_oracle.py
  *   - SparseMoe routing/permute/combine src/streaming_mixtral.rs:280-319
  *
  * Parity pins: Q4_0 follows the in-repo rule exactly.  Q4_K/Q3_K dequant is
@@ -33,7 +34,7 @@
 extern "C" {
 #endif
 
-enum { RQO_Q4_0 = 2, RQO_Q8_0 = 8, RQO_Q3_K = 11, RQO_Q4_K = 12, RQO_Q6_K = 14 };
+enum { RQO_Q4_0 = 2, RQO_Q8_0 = 8, RQO_Q2_K = 10, RQO_Q3_K = 11, RQO_Q4_K = 12, RQO_Q5_K = 13, RQO_Q6_K = 14 };
 
 uint16_t rqo_f32_to_f16(float f);
 float rqo_f16_to_f32(uint16_t h);

@@ -3,8 +3,8 @@
 The compute lives in librq.so (hand-written CUDA behind the C ABI of
 include/rq.h); this package is the host-side mirror of the reference's API.
 """
-from ._lib import Q3_K, Q4_0, Q4_K, Q6_K, Q8_0, RqError, lib
+from ._lib import Q2_K, Q3_K, Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, RqError, lib
 from .linear import Context, ParallelQ4Linear, QMatMul, QTensor, QWeight
 
-__all__ = ["Q3_K", "Q4_0", "Q4_K", "Q6_K", "Q8_0", "RqError", "lib", "Context", "ParallelQ4Linear", "QMatMul",
+__all__ = ["Q2_K", "Q3_K", "Q4_0", "Q4_K", "Q5_K", "Q6_K", "Q8_0", "RqError", "lib", "Context", "ParallelQ4Linear", "QMatMul",
            "QTensor", "QWeight"]

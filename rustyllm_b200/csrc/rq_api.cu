@@ -56,7 +56,10 @@ Mem mem_kind(const void* p) {
                                                                                 : Mem::Host;
 }
 
-bool valid_type(int t) { return t == RQ_Q4_0 || t == RQ_Q4_K || t == RQ_Q3_K || t == RQ_Q8_0 || t == RQ_Q6_K; }
+bool valid_type(int t) {
+    return t == RQ_Q4_0 || t == RQ_Q4_K || t == RQ_Q3_K || t == RQ_Q8_0 || t == RQ_Q6_K || t == RQ_Q5_K ||
+           t == RQ_Q2_K;
+}
 
 const char* type_name(int t) {
     switch (t) {
@@ -65,13 +68,15 @@ const char* type_name(int t) {
     case RQ_Q3_K: return "Q3_K";
     case RQ_Q8_0: return "Q8_0";
     case RQ_Q6_K: return "Q6_K";
+    case RQ_Q5_K: return "Q5_K";
+    case RQ_Q2_K: return "Q2_K";
     default: return "?";
     }
 }
 
 int check_shape(int type, int64_t out, int64_t in) {
     if (!valid_type(type))
-        return set_error(RQ_ERR_UNSUPPORTED, "unsupported ggml type %d (Q4_0=2, Q8_0=8, Q3_K=11, Q4_K=12, Q6_K=14)",
+        return set_error(RQ_ERR_UNSUPPORTED, "unsupported ggml type %d (Q4_0=2, Q8_0=8, Q2_K=10, Q3_K=11, Q4_K=12, Q5_K=13, Q6_K=14)",
                          type);
     TypeInfo ti = type_info(type);
     if (out <= 0 || in <= 0)

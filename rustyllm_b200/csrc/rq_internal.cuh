@@ -42,6 +42,10 @@ __host__ __device__ inline TypeInfo type_info(int t) {
     // Q6_K: quant part ql[128] qh[64]; header scales[16] d[2] + 2 bytes of
     // padding (4-byte aligned headers)
     case RQ_Q6_K: return TypeInfo{RQ_Q6_K, 256, 210, 192, 20};
+    // Q5_K: quant part qh[32] qs[128]; header d dmin scales[12] (as Q4_K)
+    case RQ_Q5_K: return TypeInfo{RQ_Q5_K, 256, 176, 160, 16};
+    // Q2_K: quant part qs[64]; header scales[16] d[2] dmin[2]
+    case RQ_Q2_K: return TypeInfo{RQ_Q2_K, 256, 84, 64, 20};
     default: return TypeInfo{0, 0, 0, 0, 0};
     }
 }

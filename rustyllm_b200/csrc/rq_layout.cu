@@ -15,7 +15,7 @@ namespace {
 
 // Map byte b of a GGML block to (is_header, offset) in the device layout.
 __device__ __forceinline__ bool ggml_byte_slot(int type, int b, int* off) {
-    if (type == RQ_Q4_K) {  // [d dmin scales(12)] [qs 128]
+    if (type == RQ_Q4_K || type == RQ_Q5_K) {  // [d dmin scales(12)] [qs 128] / [qh 32][qs 128]
         if (b < 16) { *off = b; return true; }
         *off = b - 16; return false;
     }
@@ -26,6 +26,11 @@ __device__ __forceinline__ bool ggml_byte_slot(int type, int b, int* off) {
     if (type == RQ_Q6_K) {  // [ql 128][qh 64][scales 16][d 2]
         if (b < 192) { *off = b; return false; }
         *off = b - 192; return true;  // scales 0..15, d 16..17
+    }
+    if (type == RQ_Q2_K) {  // [scales 16][qs 64][d 2][dmin 2]
+        if (b < 16) { *off = b; return true; }
+        if (b < 80) { *off = b - 16; return false; }
+        *off = b - 64; return true;  // d 16..17, dmin 18..19
     }
     // Q4_0: [d 2][qs 16]; Q8_0: [d 2][qs 32]
     if (b < 2) { *off = b; return true; }
@@ -114,6 +119,41 @@ __global__ void dequant_kernel(int type, const uint8_t* __restrict__ qs,
                 int low = (q[32 * hh + j] >> (2 * s)) & 3;
                 int hb = (hm[j] >> c) & 1;
                 v[j] = __fmul_rn(dl, (float)(low - (hb ? 0 : 4)));
+            }
+        }
+    } else if (type == RQ_Q5_K) {  // w = (d * sc) * q - (dmin * m), q = nibble | qh bit << 4
+        int64_t sbi = t / 8;
+        int s = (int)(t % 8);
+        const uint8_t* qh = qs + sbi * 160;
+        const uint8_t* q = qh + 32 + 32 * (s / 2);
+        const uint8_t* h = hdr + sbi * 16;
+        float d = h2f((uint16_t)(h[0] | (h[1] << 8)));
+        float dmin = h2f((uint16_t)(h[2] | (h[3] << 8)));
+        int sc, m;
+        q4k_scale_min(s, h + 4, &sc, &m);
+        float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+        int shift = (s & 1) * 4;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int qv = ((q[j] >> shift) & 15) | (((qh[j] >> s) & 1) << 4);
+            v[j] = __fsub_rn(__fmul_rn(d1, (float)qv), m1);
+        }
+    } else if (type == RQ_Q2_K) {  // w = (d * (sc & 15)) * q - (dmin * (sc >> 4))
+        int64_t sbi = t / 8;
+        int c = (int)(t % 8);  // 32-element chunk: half n = c / 4, shift 2 (c % 4)
+        const uint8_t* q = qs + sbi * 64 + 32 * (c / 4);
+        const uint8_t* h = hdr + sbi * 20;
+        float d = h2f((uint16_t)(h[16] | (h[17] << 8)));
+        float dmin = h2f((uint16_t)(h[18] | (h[19] << 8)));
+        const int shift = 2 * (c % 4);
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            const int sc = h[2 * c + half];
+            const float dl = __fmul_rn(d, (float)(sc & 15)), ml = __fmul_rn(dmin, (float)(sc >> 4));
+#pragma unroll
+            for (int jj = 0; jj < 16; jj++) {
+                const int j = 16 * half + jj;
+                v[j] = __fsub_rn(__fmul_rn(dl, (float)((q[j] >> shift) & 3)), ml);
             }
         }
     } else if (type == RQ_Q8_0) {  // w = d * q
@@ -415,6 +455,145 @@ __global__ void quant_q6k_kernel(const float* __restrict__ x, int64_t nsb, uint8
     }
 }
 
+// Q5_K: one warp per super-block, the Q4_K rule with 5-bit q (scale =
+// (max - min) / 31); lane l holds elements 8l..8l+7 (sub-block l/4).
+__global__ void quant_q5k_kernel(const float* __restrict__ x, int64_t nsb_total,
+                                 uint8_t* __restrict__ qs, uint8_t* __restrict__ hdr) {
+    int64_t sbi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    int lane = threadIdx.x & 31;
+    if (sbi >= nsb_total) return;  // warp-uniform
+    const float4* src = reinterpret_cast<const float4*>(x + sbi * 256 + 8 * lane);
+    float4 a = src[0], b = src[1];
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float mn = v[0], mx = v[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) { mn = fminf(mn, v[i]); mx = fmaxf(mx, v[i]); }
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (mn > 0.0f) mn = 0.0f;
+    float scale = __fdiv_rn(__fsub_rn(mx, mn), 31.0f);
+    float mins = -mn;
+    float max_scale = scale, max_min = mins;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        max_scale = fmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, o));
+        max_min = fmaxf(max_min, __shfl_xor_sync(0xffffffffu, max_min, o));
+    }
+    if (!(max_scale > 0.0f)) max_scale = 0.0f;
+    if (!(max_min > 0.0f)) max_min = 0.0f;
+    float inv_scale = max_scale > 0.0f ? __fdiv_rn(63.0f, max_scale) : 0.0f;
+    float inv_min = max_min > 0.0f ? __fdiv_rn(63.0f, max_min) : 0.0f;
+    int ls = min(63, __float2int_rn(__fmul_rn(inv_scale, scale)));
+    int lm = min(63, __float2int_rn(__fmul_rn(inv_min, mins)));
+    __half dh = __float2half_rn(__fdiv_rn(max_scale, 63.0f));
+    __half mh = __float2half_rn(__fdiv_rn(max_min, 63.0f));
+    float d = __half2float(dh), dmin = __half2float(mh);
+    float dl = __fmul_rn(d, (float)ls), ml = __fmul_rn(dmin, (float)lm);
+    const int s = lane / 4;
+    uint32_t pk[2] = {0u, 0u};
+    unsigned long long hp = 0ull;  // bit s of qh bytes 8 (l % 4) .. +7
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        int q = 0;
+        if (dl != 0.0f) q = min(31, max(0, __float2int_rn(__fdiv_rn(__fadd_rn(v[i], ml), dl))));
+        pk[i / 4] |= (uint32_t)(q & 15) << (8 * (i % 4));
+        hp |= (unsigned long long)((q >> 4) << s) << (8 * i);
+    }
+    uint32_t p0 = __shfl_xor_sync(0xffffffffu, pk[0], 4);
+    uint32_t p1 = __shfl_xor_sync(0xffffffffu, pk[1], 4);
+    // the 8 sub-blocks' bits of one qh byte sit on lanes differing in bits 2..4
+    hp |= __shfl_xor_sync(0xffffffffu, hp, 4);
+    hp |= __shfl_xor_sync(0xffffffffu, hp, 8);
+    hp |= __shfl_xor_sync(0xffffffffu, hp, 16);
+    uint8_t* base = qs + sbi * 160;
+    if (lane < 4) *reinterpret_cast<unsigned long long*>(base + 8 * lane) = hp;
+    if ((lane & 7) < 4) {
+        uint2 outv = make_uint2(pk[0] | (p0 << 4), pk[1] | (p1 << 4));
+        *reinterpret_cast<uint2*>(base + 32 + 32 * (lane / 8) + 8 * (lane & 7)) = outv;
+    }
+    int all_ls[8], all_lm[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        all_ls[k] = __shfl_sync(0xffffffffu, ls, 4 * k);
+        all_lm[k] = __shfl_sync(0xffffffffu, lm, 4 * k);
+    }
+    if (lane == 0) {
+        uint8_t hb[16];
+        uint16_t dbits = __half_as_ushort(dh), mbits = __half_as_ushort(mh);
+        hb[0] = (uint8_t)dbits; hb[1] = (uint8_t)(dbits >> 8);
+        hb[2] = (uint8_t)mbits; hb[3] = (uint8_t)(mbits >> 8);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            hb[4 + j] = (uint8_t)(all_ls[j] | ((all_ls[j + 4] >> 4) << 6));
+            hb[8 + j] = (uint8_t)(all_lm[j] | ((all_lm[j + 4] >> 4) << 6));
+            hb[12 + j] = (uint8_t)((all_ls[j + 4] & 15) | ((all_lm[j + 4] & 15) << 4));
+        }
+        uint4 hv;
+        hv.x = hb[0] | (hb[1] << 8) | (hb[2] << 16) | ((uint32_t)hb[3] << 24);
+        hv.y = hb[4] | (hb[5] << 8) | (hb[6] << 16) | ((uint32_t)hb[7] << 24);
+        hv.z = hb[8] | (hb[9] << 8) | (hb[10] << 16) | ((uint32_t)hb[11] << 24);
+        hv.w = hb[12] | (hb[13] << 8) | (hb[14] << 16) | ((uint32_t)hb[15] << 24);
+        *reinterpret_cast<uint4*>(hdr + sbi * 16) = hv;
+    }
+}
+
+// Q2_K: one thread per super-block, the oracle's rule: per 16 elements
+// scale = (max - min) / 3 and min = -min(0, smallest), 4-bit ls / lm
+// against the super-block maxima, q = rint((x + dmin lm) / (d ls)) in 0..3.
+__global__ void quant_q2k_kernel(const float* __restrict__ x, int64_t nsb, uint8_t* __restrict__ qs,
+                                 uint8_t* __restrict__ hdr) {
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= nsb) return;
+    const float* c = x + t * 256;
+    float scale[16], mins[16], max_scale = 0.0f, max_min = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        float mn = c[16 * j], mx = c[16 * j];
+#pragma unroll
+        for (int k = 1; k < 16; k++) { mn = fminf(mn, c[16 * j + k]); mx = fmaxf(mx, c[16 * j + k]); }
+        if (mn > 0.0f) mn = 0.0f;
+        scale[j] = __fdiv_rn(__fsub_rn(mx, mn), 3.0f);
+        mins[j] = -mn;
+        if (scale[j] > max_scale) max_scale = scale[j];
+        if (mins[j] > max_min) max_min = mins[j];
+    }
+    const float inv_scale = max_scale > 0.0f ? __fdiv_rn(15.0f, max_scale) : 0.0f;
+    const float inv_min = max_min > 0.0f ? __fdiv_rn(15.0f, max_min) : 0.0f;
+    const __half dh = __float2half_rn(__fdiv_rn(max_scale, 15.0f));
+    const __half mh = __float2half_rn(__fdiv_rn(max_min, 15.0f));
+    const float d = __half2float(dh), dmin = __half2float(mh);
+    // header words: scales 0..15, then (d, dmin); quant words: 64 bytes, byte
+    // 32n + l holds the 2-bit q of elements 128n + 32 sh + l at bits 2 sh
+    uint32_t hw[5] = {0u, 0u, 0u, 0u, 0u}, qw[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) qw[k] = 0u;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const int ls = min(15, __float2int_rn(__fmul_rn(inv_scale, scale[j])));
+        const int lm = min(15, __float2int_rn(__fmul_rn(inv_min, mins[j])));
+        hw[j / 4] |= (uint32_t)(ls | (lm << 4)) << (8 * (j % 4));
+        const float dl = __fmul_rn(d, (float)ls), ml = __fmul_rn(dmin, (float)lm);
+        const int n = j / 8, sh = (j % 8) / 2, l0 = 16 * (j % 2);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            int v = 0;
+            if (dl != 0.0f) v = min(3, max(0, __float2int_rn(__fdiv_rn(__fadd_rn(c[16 * j + k], ml), dl))));
+            const int byte = 32 * n + l0 + k;
+            qw[byte / 4] |= (uint32_t)v << (8 * (byte % 4) + 2 * sh);
+        }
+    }
+    hw[4] = (uint32_t)__half_as_ushort(dh) | ((uint32_t)__half_as_ushort(mh) << 16);
+    // 20 t is a multiple of 4 and the header array is 256-byte aligned
+    uint32_t* hp = reinterpret_cast<uint32_t*>(hdr + t * 20);
+#pragma unroll
+    for (int k = 0; k < 5; k++) hp[k] = hw[k];
+    uint4* qp = reinterpret_cast<uint4*>(qs + t * 64);
+#pragma unroll
+    for (int k = 0; k < 4; k++) qp[k] = make_uint4(qw[4 * k], qw[4 * k + 1], qw[4 * k + 2], qw[4 * k + 3]);
+}
+
 int grid_for(int64_t n, int threads) {
     int64_t g = (n + threads - 1) / threads;
     return (int)(g > (1 << 30) ? (1 << 30) : g);
@@ -461,6 +640,12 @@ int launch_quantize(const rq_weight* w, const float* x, cudaStream_t st) {
     } else if (w->type == RQ_Q6_K) {
         int64_t nsb = w->out * w->nblk;
         quant_q6k_kernel<<<grid_for(nsb, 128), 128, 0, st>>>(x, nsb, w->qs, w->hdr);
+    } else if (w->type == RQ_Q2_K) {
+        int64_t nsb = w->out * w->nblk;
+        quant_q2k_kernel<<<grid_for(nsb, 128), 128, 0, st>>>(x, nsb, w->qs, w->hdr);
+    } else if (w->type == RQ_Q5_K) {
+        int64_t threads = w->out * w->nblk * 32;
+        quant_q5k_kernel<<<grid_for(threads, 256), 256, 0, st>>>(x, w->out * w->nblk, w->qs, w->hdr);
     } else if (w->type == RQ_Q4_K || w->type == RQ_Q3_K) {
         int64_t nsb = w->out * w->nblk;
         int64_t threads = nsb * 32;

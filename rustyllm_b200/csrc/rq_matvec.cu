@@ -358,10 +358,12 @@ int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, 
         }
         return RQ_OK;
     }
-    if (w->type == RQ_Q8_0 || w->type == RQ_Q6_K)
+    if (w->type == RQ_Q8_0 || w->type == RQ_Q6_K || w->type == RQ_Q5_K || w->type == RQ_Q2_K)
         return set_error(RQ_ERR_UNSUPPORTED,
-                         "%s matvec needs the pipelined kernel: in %lld must be a multiple of %d", 
-                         w->type == RQ_Q8_0 ? "Q8_0" : "Q6_K", (long long)w->in, w->type == RQ_Q8_0 ? 256 : 1024);
+                         "%s matvec needs the pipelined kernel: in %lld must be a multiple of %d",
+                         w->type == RQ_Q8_0 ? "Q8_0" : w->type == RQ_Q6_K ? "Q6_K" : w->type == RQ_Q5_K ? "Q5_K" : "Q2_K",
+                         (long long)w->in,
+                         w->type == RQ_Q8_0 || w->type == RQ_Q5_K ? 256 : 1024);
     for (int64_t m = 0; m < M; m++) {
         XQ row{xq.planes + m * 3 * w->in, xq.stats + m * (w->in / 32)};
         int rc = launch_matvec_regs(w, row, y + m * w->out, sm_count, st);

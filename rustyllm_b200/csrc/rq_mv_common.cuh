@@ -500,8 +500,9 @@ struct Q6KLane {
     float sx[4], s32[4];  // per group: plane scale, 32 * sum(x)
 };
 
+// xmul: factor on the group sums (32 for Q6_K's q - 32, 1 for Q2_K's min)
 __device__ __forceinline__ void q6k_lane_setup(Q6KLane& L, const int8_t* planes, const float4* stats, int64_t in,
-                                               int64_t sb, int g, bool valid) {
+                                               int64_t sb, int g, bool valid, float xmul = 32.0f) {
     const int n = g >> 1, l0 = 16 * (g & 1);
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -514,7 +515,7 @@ __device__ __forceinline__ void q6k_lane_setup(Q6KLane& L, const int8_t* planes,
         }
         const float4 st = valid ? stats[blk] : make_float4(0.f, 0.f, 0.f, 0.f);
         L.sx[j] = st.x;
-        L.s32[j] = 32.0f * (l0 ? st.z : st.y);
+        L.s32[j] = xmul * (l0 ? st.z : st.y);
     }
 }
 
@@ -551,6 +552,105 @@ __device__ __forceinline__ float q6k_lane_row(const Q6KLane& L, uint4 a, uint4 b
     const float v3 = fmaf(fix24(acc[3][0], acc[3][1], acc[3][2]), L.sx[3], -L.s32[3]);
     const float d = __half2float(__ushort_as_half((uint16_t)(dw & 0xFFFFu)));
     return d * fmaf(s0, v0, fmaf(s1, v1, fmaf(s2, v2, s3 * v3)));
+}
+
+// ------------------------------------------------------------------- Q5_K
+// The Q4_K pipeline lane with a fifth bit: q = nibble | (bit 2g or 2g+1 of
+// qh[j]) << 4 for the low / high nibble of qs[32g + j].  The lane reads the
+// qh bytes j of its two 16-byte halves in the same half order as its qs
+// bytes; a lane-constant rotation brings bit 2g (2g+1) of every qh byte to
+// bit 4, so each 5-bit word costs one more shift and a 3-input logic op.
+// High nibbles are shifted down (16 q would not fit a byte), so both
+// sub-blocks use the plain plane scale.
+struct Q5KLane {
+    Q4KPLane b;
+    uint32_t rl, rh;  // rotate-right amounts for the low / high sub-block's bit
+};
+
+__device__ __forceinline__ void q5k_lane_setup(Q5KLane& L, const int8_t* planes, const float4* stats, int64_t in,
+                                               int64_t sb, int g, int h1, bool valid) {
+    q4kp_lane_setup(L.b, planes, stats, in, sb, g, h1, valid);
+    L.b.sxh = valid ? stats[sb * 8 + 2 * g + 1].x : 0.0f;
+    L.rl = (uint32_t)(2 * g - 4) & 31u;
+    L.rh = (uint32_t)(2 * g - 3) & 31u;
+}
+
+__device__ __forceinline__ float q5k_lane_row(const Q5KLane& L, uint4 qa, uint4 qb, uint4 ha, uint4 hb, uint4 h) {
+    const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
+    const uint32_t xa[4] = {ha.x, ha.y, ha.z, ha.w}, xb[4] = {hb.x, hb.y, hb.z, hb.w};
+    int l1 = 0, l2 = 0, l3 = 0, h1 = 0, h2 = 0, h3 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const uint32_t lo = (wa[k] & 0x0F0F0F0Fu) | (__funnelshift_r(xa[k], xa[k], L.rl) & 0x10101010u);
+        const uint32_t hi = ((wa[k] >> 4) & 0x0F0F0F0Fu) | (__funnelshift_r(xa[k], xa[k], L.rh) & 0x10101010u);
+        l1 = dp4a_us(lo, L.b.xa[0][k], l1);
+        l2 = dp4a_us(lo, L.b.xa[1][k], l2);
+        l3 = dp4a_us(lo, L.b.xa[2][k], l3);
+        h1 = dp4a_us(hi, L.b.xa[0][4 + k], h1);
+        h2 = dp4a_us(hi, L.b.xa[1][4 + k], h2);
+        h3 = dp4a_us(hi, L.b.xa[2][4 + k], h3);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const uint32_t lo = (wb[k] & 0x0F0F0F0Fu) | (__funnelshift_r(xb[k], xb[k], L.rl) & 0x10101010u);
+        const uint32_t hi = ((wb[k] >> 4) & 0x0F0F0F0Fu) | (__funnelshift_r(xb[k], xb[k], L.rh) & 0x10101010u);
+        l1 = dp4a_us(lo, L.b.xb[0][k], l1);
+        l2 = dp4a_us(lo, L.b.xb[1][k], l2);
+        l3 = dp4a_us(lo, L.b.xb[2][k], l3);
+        h1 = dp4a_us(hi, L.b.xb[0][4 + k], h1);
+        h2 = dp4a_us(hi, L.b.xb[1][4 + k], h2);
+        h3 = dp4a_us(hi, L.b.xb[2][4 + k], h3);
+    }
+    const float fl = fix24(l1, l2, l3) * L.b.sxl;
+    const float fh = fix24(h1, h2, h3) * L.b.sxh;
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+    const uint32_t x1 = __byte_perm(L.b.hiG ? h.w : h.y, h.z, L.b.sel1);
+    const uint32_t x2 = __byte_perm(h.y, h.z, L.b.sel2);
+    const uint32_t w = (x1 & L.b.mA) | ((x1 >> 4) & L.b.mB) | ((x2 >> 2) & L.b.mC);  // [sc0, sc1, m0, m1]
+    const float sc0 = (float)(w & 0xFFu), sc1 = (float)((w >> 8) & 0xFFu);
+    const float m0 = (float)((w >> 16) & 0xFFu), m1 = (float)(w >> 24);
+    return dd.x * fmaf(sc0, fl, sc1 * fh) - dd.y * fmaf(m0, L.b.xsl, m1 * L.b.xsh);
+}
+
+// ------------------------------------------------------------------- Q2_K
+// Lane g (0..3) of super-block sb owns the same four 16-weight groups as a
+// Q6_K lane: 128n + 32j + l0 + (0..15), n = g / 2, l0 = 16 (g & 1), sub-block
+// 8n + 2j + (g & 1).  Group j's 2-bit q are bits 2j, 2j+1 of the 16 bytes
+// qs[32n + l0 ..]; w = (d * (sc & 15)) * q - dmin * (sc >> 4), so per group
+// d * sc * sx * sum(q X) - dmin * m * sum(x).
+using Q2KLane = Q6KLane;
+
+// q: the lane's 16 qs bytes; sc01 / sc23: header words holding the scale
+// bytes 8n .. 8n+3 and 8n+4 .. 8n+7; dw: the word holding (d, dmin).
+__device__ __forceinline__ float q2k_lane_row(const Q2KLane& L, uint4 q, uint32_t sc01, uint32_t sc23, uint32_t dw,
+                                              int gs) {
+    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+    int acc[4][3];
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t qv = (qw[k] >> (2 * j)) & 0x03030303u;
+            acc[j][0] = dp4a_us(qv, L.p[0][4 * j + k], acc[j][0]);
+            acc[j][1] = dp4a_us(qv, L.p[1][4 * j + k], acc[j][1]);
+            acc[j][2] = dp4a_us(qv, L.p[2][4 * j + k], acc[j][2]);
+        }
+    }
+    // scale bytes of groups j = 0..3: bytes gs, gs + 2 of sc01, then of sc23
+    const int sh = 8 * gs;
+    const uint32_t b0 = sc01 >> sh, b1 = sc01 >> (sh + 16), b2 = sc23 >> sh, b3 = sc23 >> (sh + 16);
+    const float v0 = fix24(acc[0][0], acc[0][1], acc[0][2]) * L.sx[0];
+    const float v1 = fix24(acc[1][0], acc[1][1], acc[1][2]) * L.sx[1];
+    const float v2 = fix24(acc[2][0], acc[2][1], acc[2][2]) * L.sx[2];
+    const float v3 = fix24(acc[3][0], acc[3][1], acc[3][2]) * L.sx[3];
+    const float dot = fmaf((float)(b0 & 15u), v0, fmaf((float)(b1 & 15u), v1,
+                      fmaf((float)(b2 & 15u), v2, (float)(b3 & 15u) * v3)));
+    const float mins = fmaf((float)((b0 >> 4) & 15u), L.s32[0], fmaf((float)((b1 >> 4) & 15u), L.s32[1],
+                       fmaf((float)((b2 >> 4) & 15u), L.s32[2], (float)((b3 >> 4) & 15u) * L.s32[3])));
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&dw));
+    return fmaf(dd.x, dot, -dd.y * mins);
 }
 
 }  // namespace rq

@@ -260,6 +260,8 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
     case RQ_Q3_K: return launch_pipe_type<RQ_Q3_K>(p, rpw, grid, threads, smem, st);
     case RQ_Q8_0: return launch_pipe_type<RQ_Q8_0>(p, rpw, grid, threads, smem, st);
     case RQ_Q6_K: return launch_pipe_type<RQ_Q6_K>(p, rpw, grid, threads, smem, st);
+    case RQ_Q5_K: return launch_pipe_type<RQ_Q5_K>(p, rpw, grid, threads, smem, st);
+    case RQ_Q2_K: return launch_pipe_type<RQ_Q2_K>(p, rpw, grid, threads, smem, st);
     default: return launch_pipe_type<RQ_Q4_0>(p, rpw, grid, threads, smem, st);
     }
 }

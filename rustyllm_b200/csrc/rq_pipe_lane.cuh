@@ -19,6 +19,10 @@ template <>
 struct LaneOf<RQ_Q8_0> { using T = Q80Lane; };
 template <>
 struct LaneOf<RQ_Q6_K> { using T = Q6KLane; };
+template <>
+struct LaneOf<RQ_Q5_K> { using T = Q5KLane; };
+template <>
+struct LaneOf<RQ_Q2_K> { using T = Q2KLane; };
 
 // Per-lane constants of K-slice s: activation planes and the lane's
 // shared-memory byte offsets inside a row.  Lanes past the end of a partial
@@ -26,9 +30,9 @@ struct LaneOf<RQ_Q6_K> { using T = Q6KLane; };
 // loop needs no per-lane branch.
 struct LaneOffsets {
     uint32_t qa, qb, h;
-    uint32_t q3;  // Q6_K: offset of the lane's qh bytes
-    uint32_t hd;  // Q6_K: offset of the super-block's d
-    int gs;       // Q6_K: g & 1
+    uint32_t q3;  // Q6_K / Q5_K: offset of the lane's (first) qh bytes
+    uint32_t hd;  // Q6_K / Q2_K: offset of the super-block's d
+    int gs;       // Q6_K / Q2_K: g & 1
 };
 
 template <int TYPE>
@@ -58,6 +62,31 @@ __device__ __forceinline__ void lane_setup(typename LaneOf<TYPE>::T& L, LaneOffs
         o.h = (uint32_t)(s * 8 * 20) + 20u * sbl + 8u * (uint32_t)n;
         o.hd = (uint32_t)(s * 8 * 20) + 20u * sbl + 16u;
         o.gs = g & 1;
+    } else if constexpr (TYPE == RQ_Q2_K) {
+        // super-block 8s + lane / 4, lane g = lane % 4 (64 quant + 20 header bytes each)
+        const int64_t sb = (int64_t)s * 8 + (lane >> 2);
+        const bool valid = sb < nblk;
+        const uint32_t sbl = valid ? (uint32_t)(lane >> 2) : 0u;
+        const int g = lane & 3, n = g >> 1, l0 = 16 * (g & 1);
+        q6k_lane_setup(L, xq.planes, xq.stats, in, valid ? sb : (int64_t)s * 8, g, valid, 1.0f);
+        o.qa = (uint32_t)(s * 8 * 64) + 64u * sbl + 32u * (uint32_t)n + (uint32_t)l0;
+        o.qb = o.qa;
+        o.h = (uint32_t)(s * 8 * 20) + 20u * sbl + 8u * (uint32_t)n;
+        o.hd = (uint32_t)(s * 8 * 20) + 20u * sbl + 16u;
+        o.gs = g & 1;
+    } else if constexpr (TYPE == RQ_Q5_K) {
+        // super-block 8s + lane / 4, group g = lane % 4, half order h1 = bit 2
+        // of the lane (160 quant bytes: qh[32] then qs[128]; 16 header bytes)
+        const int64_t sb = (int64_t)s * 8 + (lane >> 2);
+        const bool valid = sb < nblk;
+        const uint32_t sbl = valid ? (uint32_t)(lane >> 2) : 0u;
+        const int g = lane & 3, h1 = (lane >> 2) & 1;
+        q5k_lane_setup(L, xq.planes, xq.stats, in, valid ? sb : 0, g, h1, valid);
+        const uint32_t base = (uint32_t)(s * 8 * 160) + 160u * sbl;
+        o.qa = base + 32u + 32u * (uint32_t)g + 16u * (uint32_t)h1;
+        o.qb = o.qa ^ 16u;
+        o.q3 = base + 16u * (uint32_t)h1;
+        o.h = (uint32_t)(s * 128) + 16u * sbl;
     } else if constexpr (TYPE == RQ_Q4_0) {
         const int64_t b0 = (int64_t)s * 64 + 2 * lane;
         const bool valid = b0 < nblk;
@@ -107,9 +136,20 @@ __device__ __forceinline__ void lane_setup(typename LaneOf<TYPE>::T& L, LaneOffs
 template <int TYPE>
 __device__ __forceinline__ float lane_row(const typename LaneOf<TYPE>::T& L, const LaneOffsets& o,
                                           const uint8_t* q, const uint8_t* h) {
+    if constexpr (TYPE == RQ_Q2_K) {
+        const uint32_t* hw = reinterpret_cast<const uint32_t*>(h + o.h);
+        return q2k_lane_row(L, *reinterpret_cast<const uint4*>(q + o.qa), hw[0], hw[1],
+                            *reinterpret_cast<const uint32_t*>(h + o.hd), o.gs);
+    }
     const uint4 a = *reinterpret_cast<const uint4*>(q + o.qa);
     const uint4 b = *reinterpret_cast<const uint4*>(q + o.qb);
-    if constexpr (TYPE == RQ_Q8_0) {
+    if constexpr (TYPE == RQ_Q2_K) {
+        return 0.0f;  // handled above
+    } else if constexpr (TYPE == RQ_Q5_K) {
+        const uint4 ha = *reinterpret_cast<const uint4*>(q + o.q3);
+        const uint4 hb = *reinterpret_cast<const uint4*>(q + (o.q3 ^ 16u));
+        return q5k_lane_row(L, a, b, ha, hb, *reinterpret_cast<const uint4*>(h + o.h));
+    } else if constexpr (TYPE == RQ_Q8_0) {
         const uint4 a1 = *reinterpret_cast<const uint4*>(q + o.qa + 16);
         const uint4 b1 = *reinterpret_cast<const uint4*>(q + o.qb + 16);
         return q80_lane_row(L, a, a1, b, b1, *reinterpret_cast<const uint32_t*>(h + o.h));

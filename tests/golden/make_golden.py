@@ -45,6 +45,13 @@ def main():
     w8[0, :32] = 0.0
     out["q8_0_quant_in"] = w8
     out["q8_0_quant_out"] = quants.quantize(w8, GT.Q8_0).reshape(8, -1)
+    # Q5_K and Q2_K blocks (a separate stream, so the vectors above keep
+    # their values)
+    rng2 = np.random.default_rng(20261202)
+    for name, (gt, bb, offs) in {"q5_k": (GT.Q5_K, 176, [0, 2]), "q2_k": (GT.Q2_K, 84, [80, 82])}.items():
+        raw = finite_blocks(rng2, 96, bb, offs)
+        out[f"{name}_blocks"] = raw
+        out[f"{name}_dequant"] = quants.dequantize(raw.reshape(-1), gt).reshape(96, -1).astype(np.float32)
     np.savez_compressed(os.path.join(HERE, "golden_gguf.npz"), **out)
     print({k: v.shape for k, v in out.items()})
 

@@ -181,7 +181,7 @@ def test_errors_are_reported(oracle, rq_ctx):
     with pytest.raises(RqError, match="bytes"):
         QWeight.upload(rq_ctx, 12, blocks[:2], 4, 256)
     with pytest.raises(RqError, match="unsupported"):
-        QWeight.upload(rq_ctx, 13, blocks, 4, 256)     # Q5_K: not implemented
+        QWeight.upload(rq_ctx, 15, blocks, 4, 256)     # Q8_K: not a weight format here
     w = QWeight.upload(rq_ctx, 12, blocks, 4, 256)
     assert _linear(w, np.zeros((0, 256), np.float32)).shape == (0, 4)
 

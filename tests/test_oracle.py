@@ -29,7 +29,8 @@ def test_f16_conversion_matches_numpy(oracle):
     assert ok.all()
 
 
-@pytest.mark.parametrize("name,qtype", [("q4_0", 2), ("q4_k", 12), ("q3_k", 11), ("q8_0", 8), ("q6_k", 14)])
+@pytest.mark.parametrize("name,qtype", [("q4_0", 2), ("q4_k", 12), ("q3_k", 11), ("q8_0", 8), ("q6_k", 14),
+                                        ("q5_k", 13), ("q2_k", 10)])
 def test_dequant_matches_gguf_golden(oracle, golden, name, qtype):
     blocks = golden[f"{name}_blocks"]
     want = golden[f"{name}_dequant"]
@@ -54,6 +55,22 @@ def test_q6_k_quantizer_roundtrip(oracle):
     assert np.all(d[0, :256] == 0.0)
     assert np.linalg.norm(d - w) / np.linalg.norm(w) < 0.03
     assert np.array_equal(oracle.quantize(oracle.Q6_K, d), b)
+
+
+@pytest.mark.parametrize("qtype,tol", [(13, 0.05), (10, 0.4)])
+def test_k_quantizers_roundtrip(oracle, qtype, tol):
+    """The Q5_K / Q2_K quantizers are this project's own rules (unpinned):
+    an all-zero super-block stays zero, blocks dequantize within the
+    format's expected error (5-bit vs 2-bit levels), and the packed fields
+    decode back to the levels the quantizer chose."""
+    rng = np.random.default_rng(qtype)
+    w = (rng.standard_normal((6, 512)) * 0.02).astype(np.float32)
+    w[0, :256] = 0.0
+    b = oracle.quantize(qtype, w)
+    assert b.shape == (6, 2 * oracle.BLOCK_BYTES[qtype])
+    d = oracle.dequantize(qtype, b, 6, 512)
+    assert np.all(d[0, :256] == 0.0)
+    assert np.linalg.norm(d - w) / np.linalg.norm(w) < tol
 
 
 def test_q4_0_quantizer_matches_gguf_golden(oracle, golden):
