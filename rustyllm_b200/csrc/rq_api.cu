@@ -149,6 +149,33 @@ int ensure_workspace(rq_ctx* ctx, size_t bytes) {
     return RQ_OK;
 }
 
+int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles) {
+    if (floats <= ctx->sk_ws_floats && tiles <= ctx->sk_cnt_n) return RQ_OK;
+    // first use (or a larger launch): one allocation, outside any graph
+    // capture (cudaMalloc fails inside one and the error is reported)
+    if (floats > ctx->sk_ws_floats) {
+        if (ctx->sk_ws) cudaFree(ctx->sk_ws);  // implicit device sync: no kernel still uses it
+        ctx->sk_ws = nullptr;
+        ctx->sk_ws_floats = 0;
+        const size_t nf = std::max(floats, (size_t)4 << 20);
+        cudaError_t e = cudaMalloc(&ctx->sk_ws, nf * sizeof(float));
+        if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(skinny matmul pieces)");
+        ctx->sk_ws_floats = nf;
+    }
+    if (tiles > ctx->sk_cnt_n) {
+        if (ctx->sk_cnt) cudaFree(ctx->sk_cnt);
+        ctx->sk_cnt = nullptr;
+        ctx->sk_cnt_n = 0;
+        const int n = std::max(tiles, 16384);
+        cudaError_t e = cudaMalloc(&ctx->sk_cnt, (size_t)n * sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(ctx->sk_cnt, 0, (size_t)n * sizeof(int));
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_error(e, "skinny matmul counters");
+        ctx->sk_cnt_n = n;
+    }
+    return RQ_OK;
+}
+
 }  // namespace rq
 
 using namespace rq;
@@ -203,6 +230,8 @@ int rq_destroy(rq_ctx* ctx) {
     DeviceGuard g(ctx->device);
     tp_destroy(ctx);
     if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->sk_ws) cudaFree(ctx->sk_ws);
+    if (ctx->sk_cnt) cudaFree(ctx->sk_cnt);
     delete ctx;
     return RQ_OK;
 }
@@ -353,9 +382,9 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
     DeviceGuard g(ctx->device);
     cudaStream_t st = (cudaStream_t)stream;
     const bool x_dev = mem_kind(x) == Mem::Device, y_dev = mem_kind(y) == Mem::Device;
-    // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 4..23:
-    // one mma.sync pass over the weights per 8 rows; M = 2, 3: the M=1
-    // pipeline once per row is faster (it streams at ~5 TB/s)
+    // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 2..16:
+    // the split-K tcgen05 kernel, one pass over the weights; M = 17..23: one
+    // mma.sync pass per 8 rows
     const bool small_m = M >= kMinTensorM && mm_small_supported(w);
     const size_t xq_sz = small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
     const size_t x_sz = x_dev ? 0 : (size_t)(M * w->in) * sizeof(float);
@@ -379,6 +408,9 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
         if (!rc && M >= kMinTcgenM && mm_tc_supported(w)) {
             const MMJobDesc job{w, 0, (int)M, yd, nullptr};
             rc = launch_mm_tc(&job, 1, xh, M, ctx->sm_count, st);
+        } else if (!rc && M <= kSkinnyMaxM) {
+            const MMJobDesc job{w, 0, (int)M, yd, nullptr};
+            rc = launch_mm_skinny(ctx, &job, 1, xh, M, st);
         } else if (!rc) {
             rc = launch_matmul_small(w, xh, M, yd, nullptr, ctx->sm_count, st);
         }

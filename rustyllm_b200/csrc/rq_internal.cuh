@@ -95,6 +95,10 @@ struct rq_ctx {
     void* ws;                 // workspace (activation staging, host-path buffers)
     size_t ws_bytes;
     int sm_count;
+    float* sk_ws = nullptr;  // skinny matmul: split-K tile pieces
+    size_t sk_ws_floats = 0;
+    int* sk_cnt = nullptr;   // skinny matmul: arrivals per tile (kept at zero between launches)
+    int sk_cnt_n = 0;
 };
 
 namespace rq {
@@ -175,7 +179,7 @@ struct MMJobDesc {
     const float* add;
 };
 bool mm_small_supported(const rq_weight* w);
-constexpr int64_t kMinTensorM = 4;  // smallest M routed to the tensor-core kernel
+constexpr int64_t kMinTensorM = 2;  // smallest M routed to the tensor-core kernels
 int launch_mm_small(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_count, cudaStream_t st,
                     int* err = nullptr);
 // y[M][out] = x W^T (+ add) for M >= 2 staged rows, in tiles of 8 rows
@@ -185,6 +189,14 @@ int launch_matmul_small(const rq_weight* w, XH xh, int64_t M, float* y, const fl
 // up to 128 tokens per tile, f32 accumulators in TMEM; same staged matrix and
 // job descriptors as launch_mm_small (no limit on M_j); err may be NULL.
 constexpr int64_t kMinTcgenM = 24;  // smallest M routed to the tcgen05 kernel (measured crossover)
+// M = 2..16 per job: tcgen05 with the raw quants as operands, per-sub-block
+// accumulators and split-K over all SMs (rq_mm_skinny.cu); same job
+// descriptors, every job M_j <= kSkinnyMaxM.
+constexpr int kSkinnyMaxM = 16;
+int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, cudaStream_t st,
+                     int* err = nullptr);
+// grow ctx's split-K scratch to floats / tiles (never during stream capture)
+int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles);
 bool mm_tc_supported(const rq_weight* w);
 int launch_mm_tc(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_count, cudaStream_t st,
                  int* err = nullptr);

@@ -1,0 +1,576 @@
+// rq_mm_skinny.cu -- Q4_K matmul for 2..16 activation rows (speculative
+// verify batches, short prompt chunks) on the 5th-gen tensor cores.
+//
+// At this width the work is HBM-bound: every weight byte must be read once
+// and at ~40 weights per clock per SM, so the kernel is built around the
+// cost per weight, not per MMA.
+//   * The 4-bit quants enter the MMA as they are: a nibble's bit pattern
+//     in a 16-bit lane is the f16 subnormal q * 2^-24, a high nibble masked
+//     in place is 16 q * 2^-24; one shift and four masks turn a word of 8
+//     weights into four f16x2 operand words (no multiply, no conversion).
+//   * Each of the 8 sub-blocks of a super-block accumulates into its own
+//     TMEM accumulator (K = 32: two MMAs), so 8 independent MMA chains hide
+//     the tensor core's latency, and the sub-block scales sc_j (6-bit) are
+//     applied in the epilogue: y += d * sum_j sc_j P1_j - dmin * P2 with
+//     P2 = [m_0..7, m_0..7] . [bsum_hi ; bsum_lo] (one K = 16 MMA) exactly
+//     as in rq_mm_tc.cu.  Every operand is exact; the activations arrive as
+//     x / s = hi + lo in f16 (stacked along N: the MMA's N is 2 nt).
+//   * Persistent CTAs take equal ranges of (128-row tile, super-block)
+//     units over all jobs, so 1024-row and 28672-row weights alike fill the
+//     148 SMs.  A tile cut between CTAs is finished by the last CTA to
+//     arrive (an atomic count per tile), which sums the pieces from a
+//     workspace in CTA order: the result does not depend on timing.
+//
+// Warp roles (18 warps, one CTA per SM):
+//   0      TMA producer: ring R (one super-block of 128 rows: quant bytes,
+//          headers, the block-sum operand B2), ring C (one 64-element chunk
+//          of x_hi / x_lo: B1).
+//   1      TMEM allocation, all MMAs (one elected lane), commits.
+//   2..9   expand: warp w writes TMEM lanes 32 (w % 4) .. +31 (rows), the
+//          low (h = 0) or high (h = 1) nibbles of a chunk: 16 columns of the
+//          chunk's A slot; the h = 0 warps also write A2 (the m values).
+//   10..17 epilogue: two warps per lane quarter, each reads 4 of the 8
+//          sub-block accumulators; running totals stay in registers and the
+//          two halves are added once per tile piece.
+// TMEM columns: nb buffers of [8 chains x 2 nt | P2 16], then na A slots
+// of 32 (64 f16 of K per row).  Every mbarrier wait is bounded; on expiry
+// the CTA records the error and skips work, and TMEM is always released.
+
+#include <string.h>
+
+#include <algorithm>
+
+#include "rq_async.cuh"
+#include "rq_mv_common.cuh"
+#include "rq_tcgen05.cuh"
+
+namespace rq {
+namespace {
+
+using namespace tc;
+
+constexpr int kWarpsSK = 18;
+constexpr int kThreadsSK = 32 * kWarpsSK;
+constexpr int kExpWarp0 = 2, kEpiWarp0 = 10;
+constexpr int kChains = 8;  // one accumulator per sub-block
+constexpr int kMaxR = 8, kMaxC = 8, kMaxA = 6;
+constexpr int kSmemSK = 227 * 1024;
+constexpr float kSub = 16777216.0f;  // 2^24: f16 subnormal n * 2^-24 -> n
+
+struct SKJob {
+    float* y;
+    const float* add;
+    const uint8_t* hdr;  // [out][nblk][16]
+    int64_t out;
+    int tok0, M;
+    int t0;  // first tile of the job in the global tile order
+};
+
+struct alignas(64) SKParams {
+    CUtensorMap wq[kMaxJobs];  // quant bytes [out][nblk*128], box 128 x 128, 128-byte swizzle
+    CUtensorMap wh[kMaxJobs];  // headers [out][nblk*16], box 16 x 128
+    CUtensorMap xhi, xlo;      // staged x planes [rows][in] f16, box 64 x nt, 128-byte swizzle
+    CUtensorMap bs;            // block sums [rows][nblk*16] f16, box 16 x 16, 32-byte swizzle
+    SKJob jobs[kMaxJobs];
+    const float* xscale;
+    int* err;
+    float* ws;  // tile pieces: slot (tile + cta) of [nt][128] floats
+    int* cnt;   // arrivals per tile (reset by the last arrival)
+    long long units;
+    int njobs, nblk, nb, na, nr, nc;
+    uint32_t buf_cols, acol0, tmem_cols;
+    uint32_t r_bytes, r_hdr, r_b2, r_a2, c_bytes, ring_off, c_off;
+};
+
+// A CTA's share: units [U b / G, U (b+1) / G) of the (tile, super-block)
+// order, walked as segments of consecutive super-blocks of one tile.
+struct Seg {
+    int t, sb0, sb1;
+};
+struct Segs {
+    long long u, u1;
+    __device__ __forceinline__ void start(const SKParams& p) {
+        u = p.units * (long long)blockIdx.x / gridDim.x;
+        u1 = p.units * (long long)(blockIdx.x + 1) / gridDim.x;
+    }
+    __device__ __forceinline__ bool next(const SKParams& p, Seg& s) {
+        if (u >= u1) return false;
+        s.t = (int)(u / p.nblk);
+        s.sb0 = (int)(u - (long long)s.t * p.nblk);
+        const long long e = min(u1, (long long)(s.t + 1) * p.nblk);
+        s.sb1 = s.sb0 + (int)(e - u);
+        u = e;
+        return true;
+    }
+};
+
+__device__ __forceinline__ int job_of(const SKParams& p, int t) {
+    int j = 0;
+    while (j + 1 < p.njobs && t >= p.jobs[j + 1].t0) j++;
+    return j;
+}
+
+// the CTA whose share holds unit x
+__device__ __forceinline__ long long cta_of(const SKParams& p, long long x) {
+    return ((x + 1) * (long long)gridDim.x + p.units - 1) / p.units - 1;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_constant__ SKParams p) {
+    constexpr uint32_t N1 = 2 * NT;  // P1 columns per chain: x_hi tokens, then x_lo tokens
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+    uint8_t* smem = smem_raw + pad;
+    const uint32_t sbase = raw + pad;
+    // first 1 KB: rfull, rempty [kMaxR]; cfull, cempty [kMaxC]; aready,
+    // aempty [kMaxA]; accfull, accempty [2]; the TMEM address; a flag
+    const uint32_t rfull0 = sbase, rempty0 = rfull0 + 8 * kMaxR;
+    const uint32_t cfull0 = rempty0 + 8 * kMaxR, cempty0 = cfull0 + 8 * kMaxC;
+    const uint32_t aready0 = cempty0 + 8 * kMaxC, aempty0 = aready0 + 8 * kMaxA;
+    const uint32_t accfull0 = aempty0 + 8 * kMaxA, accempty0 = accfull0 + 16;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (accempty0 + 16 - sbase));
+    volatile int* last_flag = reinterpret_cast<volatile int*>(smem + (accempty0 + 20 - sbase));
+    float* ered = reinterpret_cast<float*>(smem + 1024);  // [128 rows][NT]: the high half's totals
+    const uint32_t ringr = sbase + p.ring_off, ringc = ringr + p.c_off;
+    const uint8_t* ringr_p = smem + p.ring_off;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nblk = p.nblk;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.nr; i++) {
+            mbar_init(rfull0 + 8 * i, 1);
+            mbar_init(rempty0 + 8 * i, 1);
+        }
+        for (int i = 0; i < p.nc; i++) {
+            mbar_init(cfull0 + 8 * i, 1);
+            mbar_init(cempty0 + 8 * i, 1);
+        }
+        for (int i = 0; i < p.na; i++) {
+            mbar_init(aready0 + 8 * i, 8);
+            mbar_init(aempty0 + 8 * i, 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(accfull0 + 8 * b, 1);
+            mbar_init(accempty0 + 8 * b, 8);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(p.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // the staged activations are written by the preceding kernel in the stream
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    Segs sg;
+    sg.start(p);
+    Seg s;
+    if (warp == 0) {
+        // -------------------------------------------------------------- TMA
+        if (lane == 0) {
+            const uint64_t pol_w = policy_evict_first(), pol_h = policy_evict_normal();
+            const uint64_t pol_x = policy_evict_last();
+            const uint32_t rtx = kRowsTC * 128 + kRowsTC * 16 + 16 * 32;
+            const uint32_t ctx = 2u * 128u * NT;
+            Ring rr, cr;
+            int ri = 0, ci = 0;
+            bool ok = true;
+            while (ok && sg.next(p, s)) {
+                const int j = job_of(p, s.t);
+                const int row0 = (s.t - p.jobs[j].t0) * kRowsTC, tok = p.jobs[j].tok0;
+                for (int sb = s.sb0; sb < s.sb1 && ok; sb++, ri++, rr.next(p.nr)) {
+                    if (rr.u > 0 && !wait_err(rempty0 + 8 * rr.i, (rr.u - 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t st = ringr + (uint32_t)rr.i * p.r_bytes;
+                    const uint32_t fb = rfull0 + 8 * rr.i;
+                    mbar_expect_tx(fb, rtx);
+                    tma_load_2d(st, &p.wq[j], sb * 128, row0, fb, pol_w);
+                    tma_load_2d(st + p.r_hdr, &p.wh[j], sb * 16, row0, fb, pol_h);
+                    tma_load_2d(st + p.r_b2, &p.bs, sb * 16, tok, fb, pol_x);
+                    for (int cq = 0; cq < 4; cq++, ci++, cr.next(p.nc)) {
+                        if (cr.u > 0 && !wait_err(cempty0 + 8 * cr.i, (cr.u - 1) & 1, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t sc = ringc + (uint32_t)cr.i * p.c_bytes;
+                        const uint32_t cb = cfull0 + 8 * cr.i;
+                        mbar_expect_tx(cb, ctx);
+                        tma_load_2d(sc, &p.xhi, (4 * sb + cq) * 64, tok, cb, pol_x);
+                        tma_load_2d(sc + 128u * NT, &p.xlo, (4 * sb + cq) * 64, tok, cb, pol_x);
+                    }
+                }
+            }
+            // no copy may still be in flight when the CTA exits
+            for (int k = max(0, ri - p.nr); k < ri; k++)
+                if (!mbar_wait(rfull0 + 8 * (k % p.nr), (k / p.nr) & 1)) ok = false;
+            for (int k = max(0, ci - p.nc); k < ci; k++)
+                if (!mbar_wait(cfull0 + 8 * (k % p.nc), (k / p.nc) & 1)) ok = false;
+            if (!ok && p.err) atomicExch(p.err, 1);
+        }
+    } else if (warp == 1) {
+        // -------------------------------------------------------------- MMA
+        const uint32_t idesc1 = umma_idesc(N1), idesc2 = umma_idesc(16);
+        Ring rr, cr, ar, br;
+        bool ok = true;
+        while (sg.next(p, s)) {
+            for (int sb = s.sb0; sb < s.sb1; sb++, rr.next(p.nr), br.next(p.nb)) {
+                const int b = br.i;
+                // buffer b is free once the epilogue has read its previous super-block
+                if (ok && br.u > 0 && !wait_err(accempty0 + 8 * b, (br.u - 1) & 1, p.err)) ok = false;
+                ok = __all_sync(0xffffffffu, ok);
+                tmem_fence_after();
+                const uint32_t bcol = tmem + (uint32_t)b * p.buf_cols;
+                for (int cq = 0; cq < 4; cq++, cr.next(p.nc), ar.next(p.na)) {
+                    if (ok && !wait_err(cfull0 + 8 * cr.i, cr.u & 1, p.err)) ok = false;
+                    if (ok && !wait_err(aready0 + 8 * ar.i, ar.u & 1, p.err)) ok = false;
+                    ok = __all_sync(0xffffffffu, ok);
+                    tmem_fence_after();
+                    const uint32_t sc = ringc + (uint32_t)cr.i * p.c_bytes;
+                    const uint32_t acol = tmem + p.acol0 + 32u * (uint32_t)ar.i;
+                    if (elect_one()) {
+                        if (ok) {
+                            // K steps 0, 2 start sub-blocks 2cq, 2cq+1; 1, 3 finish them
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                const int kk = (i >> 1) | ((i & 1) << 1);
+                                const uint32_t d = bcol + (uint32_t)(2 * cq + (kk >> 1)) * N1;
+                                umma_f16_ts(d, acol + 8u * kk, desc_sw128(sc + 32u * kk), idesc1, (uint32_t)(kk & 1));
+                            }
+                        }
+                        umma_commit(cempty0 + 8 * cr.i);
+                        umma_commit(aempty0 + 8 * ar.i);
+                    }
+                    __syncwarp();
+                }
+                const uint32_t st = ringr + (uint32_t)rr.i * p.r_bytes;
+                if (elect_one()) {
+                    if (ok)
+                        umma_f16(bcol + kChains * N1, desc_sw32(st + p.r_a2), desc_sw32(st + p.r_b2), idesc2, 0u);
+                    umma_commit(rempty0 + 8 * rr.i);
+                    umma_commit(accfull0 + 8 * b);
+                }
+                __syncwarp();
+            }
+        }
+        if (!ok && lane == 0 && p.err) atomicExch(p.err, 1);
+    } else if (warp < kEpiWarp0) {
+        // ----------------------------------------------------------- expand
+        const int q = warp & 3, h = (warp - kExpWarp0) >> 2;
+        const int r = 32 * q + lane;
+        const uint32_t swz = (uint32_t)(r & 7);
+        const uint32_t lane_a = tmem + ((uint32_t)(32 * q) << 16) + p.acol0 + 16u * (uint32_t)h;
+        const uint32_t mask = h ? 0x00F000F0u : 0x000F000Fu;
+        Ring rr, ar;
+        bool ok = true;
+        while (sg.next(p, s)) {
+            for (int sb = s.sb0; sb < s.sb1; sb++, rr.next(p.nr)) {
+                if (ok && !wait_err(rfull0 + 8 * rr.i, rr.u & 1, p.err)) ok = false;
+                const uint8_t* rst = ringr_p + (size_t)rr.i * p.r_bytes;
+                if (ok && h == 0) {
+                    // A2 row r: [m_0..7, m_0..7] as f16 subnormals (32-byte
+                    // swizzle; both 16-byte halves are equal)
+                    const uint4 hd = *reinterpret_cast<const uint4*>(rst + p.r_hdr + r * 16);
+                    uint32_t m[4];
+#pragma unroll
+                    for (int g = 0; g < 4; g++) {
+                        const uint32_t w = q4k_scales(q4k_scale_sel(g), hd);
+                        m[g] = ((w >> 16) & 0xFFu) | ((w >> 24) << 16);
+                    }
+                    const uint4 mv = make_uint4(m[0], m[1], m[2], m[3]);
+                    uint8_t* a2 = const_cast<uint8_t*>(rst) + p.r_a2 + (r >> 3) * 256 + (r & 7) * 32;
+                    *reinterpret_cast<uint4*>(a2) = mv;
+                    *reinterpret_cast<uint4*>(a2 + 16) = mv;
+                    // generic-proxy writes become visible to the tensor core
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                }
+                for (int cq = 0; cq < 4; cq++, ar.next(p.na)) {
+                    if (ok && ar.u > 0 && !wait_err(aempty0 + 8 * ar.i, (ar.u - 1) & 1, p.err)) ok = false;
+                    ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-wide
+                    tmem_fence_after();
+                    if (ok) {
+                        // the chunk's 32 quant bytes of row r: 16-byte chunks
+                        // 2cq, 2cq+1 of the row's 128-byte-swizzled line
+                        const uint8_t* qrow = rst + r * 128;
+                        const uint4 qa = *reinterpret_cast<const uint4*>(qrow + (((2 * cq) ^ swz) << 4));
+                        const uint4 qb = *reinterpret_cast<const uint4*>(qrow + (((2 * cq + 1) ^ swz) << 4));
+                        const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                        uint32_t o[16];
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            // bytes b0..b3: (b0, b2) and (b1, b3) in 16-bit
+                            // lanes, i.e. elements (e0, e2), (e1, e3)
+                            o[2 * i] = qw[i] & mask;
+                            o[2 * i + 1] = (qw[i] >> 8) & mask;
+                        }
+                        // TMEM column c of the slot holds K positions 2c, 2c+1
+                        tmem_st16u(lane_a + 32u * (uint32_t)ar.i, o);
+                        tmem_wait_st();
+                    }
+                    tmem_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(aready0 + 8 * ar.i);
+                }
+            }
+        }
+        if (!ok && lane == 0 && p.err) atomicExch(p.err, 1);
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3, half = (warp - kEpiWarp0) >> 2;
+        const int r = 32 * q + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+        const Q4KScaleSel sel0 = q4k_scale_sel(2 * half), sel1 = q4k_scale_sel(2 * half + 1);
+        Ring br;
+        bool ok = true;
+        while (sg.next(p, s)) {
+            const int j = job_of(p, s.t);
+            const SKJob& jb = p.jobs[j];
+            const int64_t row = (int64_t)(s.t - jb.t0) * kRowsTC + r;
+            const bool live = row < jb.out;
+            const uint8_t* hrow = jb.hdr + (live ? row : 0) * (int64_t)nblk * 16;
+            float tot[NT];
+#pragma unroll
+            for (int i = 0; i < NT; i++) tot[i] = 0.0f;
+            uint4 hd = live ? __ldg(reinterpret_cast<const uint4*>(hrow + s.sb0 * 16)) : make_uint4(0u, 0u, 0u, 0u);
+            for (int sb = s.sb0; sb < s.sb1; sb++, br.next(p.nb)) {
+                const int b = br.i;
+                const uint4 hn = (live && sb + 1 < s.sb1) ? __ldg(reinterpret_cast<const uint4*>(hrow + (sb + 1) * 16))
+                                                          : make_uint4(0u, 0u, 0u, 0u);
+                const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hd.x));
+                const float fd = dm.x * kSub, fm = -dm.y * kSub;
+                const uint32_t w0 = q4k_scales(sel0, hd), w1 = q4k_scales(sel1, hd);
+                // chains 4 half + i: sub-blocks 4 half, +1 (high nibbles: 16 q), +2, +3 (16 q)
+                const float k0 = fd * (float)(w0 & 0xFFu), k1 = fd * 0.0625f * (float)((w0 >> 8) & 0xFFu);
+                const float k2 = fd * (float)(w1 & 0xFFu), k3 = fd * 0.0625f * (float)((w1 >> 8) & 0xFFu);
+                if (ok && !wait_err(accfull0 + 8 * b, br.u & 1, p.err)) ok = false;
+                ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-wide
+                tmem_fence_after();
+                const uint32_t bcol = lane_base + (uint32_t)b * p.buf_cols + (uint32_t)(4 * half) * N1;
+                if (ok) {
+                    if constexpr (NT == 8) {
+                        uint32_t u0[16], u1[16];
+                        tmem_ld16(bcol, u0);
+                        tmem_ld16(bcol + N1, u1);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const float v = fmaf(k0, __uint_as_float(u0[i]) + __uint_as_float(u0[8 + i]), tot[i]);
+                            tot[i] = fmaf(k1, __uint_as_float(u1[i]) + __uint_as_float(u1[8 + i]), v);
+                        }
+                        tmem_ld16(bcol + 2 * N1, u0);
+                        tmem_ld16(bcol + 3 * N1, u1);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const float v = fmaf(k2, __uint_as_float(u0[i]) + __uint_as_float(u0[8 + i]), tot[i]);
+                            tot[i] = fmaf(k3, __uint_as_float(u1[i]) + __uint_as_float(u1[8 + i]), v);
+                        }
+                        if (half == 0) {
+                            tmem_ld16(lane_base + (uint32_t)b * p.buf_cols + kChains * N1, u0);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 8; i++) tot[i] = fmaf(fm, __uint_as_float(u0[i]), tot[i]);
+                        }
+                    } else {
+                        const float kc[4] = {k0, k1, k2, k3};
+#pragma unroll
+                        for (int c = 0; c < 4; c += 2) {
+                            uint32_t ua[32], ub[32];
+                            tmem_ld32(bcol + (uint32_t)c * N1, ua);
+                            tmem_ld32(bcol + (uint32_t)(c + 1) * N1, ub);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 16; i++) {
+                                float v = fmaf(kc[c], __uint_as_float(ua[i]) + __uint_as_float(ua[16 + i]), tot[i]);
+                                tot[i] = fmaf(kc[c + 1], __uint_as_float(ub[i]) + __uint_as_float(ub[16 + i]), v);
+                            }
+                        }
+                        if (half == 0) {
+                            uint32_t p2[16];
+                            tmem_ld16(lane_base + (uint32_t)b * p.buf_cols + kChains * N1, p2);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 16; i++) tot[i] = fmaf(fm, __uint_as_float(p2[i]), tot[i]);
+                        }
+                    }
+                }
+                tmem_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(accempty0 + 8 * b);
+                hd = hn;
+            }
+            // ---- end of the tile piece: add the halves (low + high), then
+            // write y, or the piece and count it
+            if (half == 1) {
+#pragma unroll
+                for (int i = 0; i < NT; i++) ered[r * NT + i] = tot[i];
+            }
+            named_bar_sync(1, 256);
+            if (half == 0) {
+#pragma unroll
+                for (int i = 0; i < NT; i++) tot[i] += ered[r * NT + i];
+                const long long x0 = (long long)s.t * nblk;
+                const long long bf = cta_of(p, x0), bl = cta_of(p, x0 + nblk - 1);
+                const int P = (int)(bl - bf + 1);
+                const float* xs = p.xscale + jb.tok0;
+                if (P == 1) {
+                    if (ok && live) {
+#pragma unroll
+                        for (int i = 0; i < NT; i++) {
+                            if (i < jb.M) {
+                                const int64_t o = (int64_t)i * jb.out + row;
+                                const float v = tot[i] * xs[i];
+                                jb.y[o] = jb.add ? v + jb.add[o] : v;
+                            }
+                        }
+                    }
+                } else {
+                    float* wsl = p.ws + ((size_t)s.t + blockIdx.x) * (NT * 128);
+#pragma unroll
+                    for (int i = 0; i < NT; i++) wsl[i * 128 + r] = tot[i];
+                    __threadfence();
+                    named_bar_sync(2, 128);
+                    if (warp == kEpiWarp0 && lane == 0) {
+                        const int old = atomicAdd(p.cnt + s.t, 1);
+                        *last_flag = old == P - 1;
+                    }
+                    named_bar_sync(2, 128);
+                    if (*last_flag) {
+                        __threadfence();
+                        if (ok && live) {
+                            for (int i = 0; i < NT && i < jb.M; i++) {
+                                float v = 0.0f;
+                                for (int pc = 0; pc < P; pc++)
+                                    v += __ldcg(p.ws + ((size_t)s.t + bf + pc) * (NT * 128) + i * 128 + r);
+                                const int64_t o = (int64_t)i * jb.out + row;
+                                v *= xs[i];
+                                jb.y[o] = jb.add ? v + jb.add[o] : v;
+                            }
+                        }
+                        if (warp == kEpiWarp0 && lane == 0) p.cnt[s.t] = 0;
+                    }
+                }
+            }
+            // the combine buffer and the flag are reused by the next piece
+            named_bar_sync(1, 256);
+        }
+        if (!ok && lane == 0 && p.err) atomicExch(p.err, 1);
+    }
+    // every MMA has completed (the epilogue waited for the last commit)
+    // before the columns are released
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    __syncwarp();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols)
+                     : "memory");
+}
+
+}  // namespace
+
+int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, cudaStream_t st, int* err) {
+    if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "skinny matmul: %d jobs", njobs);
+    const int64_t in = jobs[0].w->in, nblk = jobs[0].w->nblk;
+    SKParams p;
+    memset(&p, 0, sizeof p);
+    int tiles = 0, mmax = 1;
+    for (int j = 0; j < njobs; j++) {
+        const rq_weight* w = jobs[j].w;
+        if (w->type != RQ_Q4_K || w->in != in)
+            return set_error(RQ_ERR_INVALID, "skinny matmul: jobs need Q4_K weights with the same K");
+        if (jobs[j].M < 1 || jobs[j].M > kSkinnyMaxM || jobs[j].tok0 < 0 || jobs[j].tok0 + jobs[j].M > rows)
+            return set_error(RQ_ERR_INVALID, "skinny matmul: token rows [%d, %d) of %lld (at most %d per job)",
+                             jobs[j].tok0, jobs[j].tok0 + jobs[j].M, (long long)rows, kSkinnyMaxM);
+        int rc = encode(&p.wq[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, (uint64_t)(nblk * 128), (uint64_t)w->out,
+                        (uint64_t)(nblk * 128), 128, kRowsTC, CU_TENSOR_MAP_SWIZZLE_128B, "quant bytes");
+        if (!rc)
+            rc = encode(&p.wh[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, w->hdr, (uint64_t)(nblk * 16), (uint64_t)w->out,
+                        (uint64_t)(nblk * 16), 16, kRowsTC, CU_TENSOR_MAP_SWIZZLE_NONE, "headers");
+        if (rc) return rc;
+        SKJob& t = p.jobs[j];
+        t.y = jobs[j].y;
+        t.add = jobs[j].add;
+        t.hdr = w->hdr;
+        t.out = w->out;
+        t.tok0 = jobs[j].tok0;
+        t.M = jobs[j].M;
+        t.t0 = tiles;
+        tiles += (int)((w->out + kRowsTC - 1) / kRowsTC);
+        mmax = std::max(mmax, jobs[j].M);
+    }
+    const int nt = mmax <= 8 ? 8 : 16;
+    int rc = encode(&p.xhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh.v, (uint64_t)in, (uint64_t)rows, (uint64_t)(4 * in),
+                    64, (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B, "activations (hi)");
+    if (!rc)
+        rc = encode(&p.xlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh.v + in, (uint64_t)in, (uint64_t)rows,
+                    (uint64_t)(4 * in), 64, (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B, "activations (lo)");
+    if (!rc)
+        rc = encode(&p.bs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh.bs16, (uint64_t)(nblk * 16), (uint64_t)rows,
+                    (uint64_t)(nblk * 32), 16, 16, CU_TENSOR_MAP_SWIZZLE_32B, "block sums");
+    if (rc) return rc;
+    p.units = (long long)tiles * nblk;
+    const int grid = (int)std::min<long long>(ctx->sm_count, p.units);
+    // split-K scratch: slot (tile + cta) of [nt][128] floats, a count per tile
+    rc = ensure_skinny_scratch(ctx, (size_t)(tiles + grid) * nt * kRowsTC, tiles);
+    if (rc) return rc;
+    p.ws = ctx->sk_ws;
+    p.cnt = ctx->sk_cnt;
+    p.xscale = xh.scale;
+    p.err = err;
+    p.njobs = njobs;
+    p.nblk = (int)nblk;
+    // TMEM: nb buffers of [8 chains x 2 nt | P2 16] and na A slots of 32
+    p.buf_cols = (uint32_t)(kChains * 2 * nt + 16);
+    p.nb = nt == 8 ? 2 : 1;
+    p.acol0 = (uint32_t)p.nb * p.buf_cols;
+    p.na = std::min(kMaxA, (int)((512 - p.acol0) / 32));
+    p.tmem_cols = 512;
+    // R stage: quant 16 KB | headers 2 KB | B2 16 x 32 B | A2 4 KB; C stage:
+    // x_hi, x_lo nt x 128 B each; every tile 1024-aligned
+    auto al = [](uint32_t v) { return (v + 1023u) & ~1023u; };
+    p.r_hdr = kRowsTC * 128;
+    p.r_b2 = al(p.r_hdr + kRowsTC * 16);
+    p.r_a2 = al(p.r_b2 + 16 * 32);
+    p.r_bytes = al(p.r_a2 + kRowsTC * 32);
+    p.c_bytes = al(2 * 128u * (uint32_t)nt);
+    p.ring_off = 1024 + al(kRowsTC * 4u * (uint32_t)nt);
+    p.nc = kMaxC;
+    const int avail = kSmemSK - 1024 - (int)p.ring_off - p.nc * (int)p.c_bytes;
+    p.nr = std::min(kMaxR, avail / (int)p.r_bytes);
+    if (p.nr < 2) return set_error(RQ_ERR_UNSUPPORTED, "skinny matmul: stages too large");
+    p.c_off = (uint32_t)p.nr * p.r_bytes;
+    const size_t smem = 1024 + (size_t)p.ring_off + p.c_off + (size_t)p.nc * p.c_bytes;
+
+    static bool attr_set[2][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int ki = nt == 8 ? 0 : 1;
+    auto kern = nt == 8 ? mm_skinny_kernel<8> : mm_skinny_kernel<16>;
+    if (dev < 0 || dev >= 64 || !attr_set[ki][dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemSK);
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(skinny matmul)");
+        if (dev >= 0 && dev < 64) attr_set[ki][dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreadsSK);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_error(cudaLaunchKernelEx(&cfg, kern, p), "skinny matmul kernel");
+}
+
+}  // namespace rq

@@ -92,6 +92,27 @@ def test_small_m_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
         assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("out,n_in,M", [(128, 8192, 2), (200, 768, 3), (1024, 8192, 5), (256, 28672, 8),
+                                         (72, 256, 9), (1040, 4096, 16), (8192, 1024, 4), (300, 1280, 11)])
+def test_split_k_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
+    """Q4_K M = 2..16 run on the split-K tcgen05 kernel: one 128-row tile cut
+    into single-super-block pieces on 32 SMs, ragged last tiles, 8- and
+    16-token tiles, more tiles than SMs, odd super-block counts.  The pieces
+    are summed in a fixed order, so two calls give the same bits."""
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200.linear import _linear
+    _, blocks = make_weight(oracle, 12, out, n_in, seed=out + 7 * M)
+    w = QWeight.upload(rq_ctx, 12, blocks, out, n_in)
+    x = np.random.default_rng(M + 3).standard_normal((M, n_in)).astype(np.float32)
+    y = _linear(w, x)
+    ref = oracle.matmul_ref(12, blocks, out, n_in, x, acc64=True)
+    assert np.isfinite(y).all()
+    assert rel_l2(y, ref) <= REL_L2_TOL
+    for m in range(M):
+        assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
+    assert np.array_equal(_linear(w, x).view(np.uint32), y.view(np.uint32))
+
+
 @pytest.mark.parametrize("out,n_in,M", [(200, 768, 24), (128, 256, 25), (333, 2048, 67), (1040, 4096, 128),
                                          (520, 4096, 129), (256, 8192, 300), (4096, 1024, 512),
                                          (130, 28672, 40), (300, 1024, 33), (200, 2048, 90)])
