@@ -382,9 +382,10 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
     DeviceGuard g(ctx->device);
     cudaStream_t st = (cudaStream_t)stream;
     const bool x_dev = mem_kind(x) == Mem::Device, y_dev = mem_kind(y) == Mem::Device;
-    // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 2..16:
-    // the split-K tcgen05 kernel, one pass over the weights; M = 17..23: one
-    // mma.sync pass per 8 rows
+    // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 9..16:
+    // the split-K tcgen05 kernel, one pass over the weights; M = 4..8 and
+    // 17..23: one mma.sync pass per 8 rows; M = 2, 3: the M=1 pipeline once
+    // per row is faster (it streams at ~5 TB/s)
     const bool small_m = M >= kMinTensorM && mm_small_supported(w);
     const size_t xq_sz = small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
     const size_t x_sz = x_dev ? 0 : (size_t)(M * w->in) * sizeof(float);
@@ -408,7 +409,7 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
         if (!rc && M >= kMinTcgenM && mm_tc_supported(w)) {
             const MMJobDesc job{w, 0, (int)M, yd, nullptr};
             rc = launch_mm_tc(&job, 1, xh, M, ctx->sm_count, st);
-        } else if (!rc && M <= kSkinnyMaxM) {
+        } else if (!rc && M >= kSkinnyMinM && M <= kSkinnyMaxM) {
             const MMJobDesc job{w, 0, (int)M, yd, nullptr};
             rc = launch_mm_skinny(ctx, &job, 1, xh, M, st);
         } else if (!rc) {

@@ -179,7 +179,7 @@ struct MMJobDesc {
     const float* add;
 };
 bool mm_small_supported(const rq_weight* w);
-constexpr int64_t kMinTensorM = 2;  // smallest M routed to the tensor-core kernels
+constexpr int64_t kMinTensorM = 4;  // smallest M routed to the tensor-core kernels
 int launch_mm_small(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_count, cudaStream_t st,
                     int* err = nullptr);
 // y[M][out] = x W^T (+ add) for M >= 2 staged rows, in tiles of 8 rows
@@ -189,9 +189,13 @@ int launch_matmul_small(const rq_weight* w, XH xh, int64_t M, float* y, const fl
 // up to 128 tokens per tile, f32 accumulators in TMEM; same staged matrix and
 // job descriptors as launch_mm_small (no limit on M_j); err may be NULL.
 constexpr int64_t kMinTcgenM = 24;  // smallest M routed to the tcgen05 kernel (measured crossover)
-// M = 2..16 per job: tcgen05 with the raw quants as operands, per-sub-block
+// M = 9..16 per job: tcgen05 with the raw quants as operands, per-sub-block
 // accumulators and split-K over all SMs (rq_mm_skinny.cu); same job
-// descriptors, every job M_j <= kSkinnyMaxM.
+// descriptors, every job M_j <= kSkinnyMaxM.  Below kSkinnyMinM the
+// mma.sync kernel is faster (one tcgen05.mma of 128 x 16 x 16 issues only
+// every ~60-100 cycles, which caps this kernel near 1.3 TB/s of weights at
+// any M; mma.sync's 8-row tiles cost the same and M <= 8 needs one tile).
+constexpr int kSkinnyMinM = 9;
 constexpr int kSkinnyMaxM = 16;
 int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, cudaStream_t st,
                      int* err = nullptr);

@@ -485,9 +485,9 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
 }
 
 // y_i = x W_i^T (+ add_i) for the n Q4_K weights (same in) over the T rows
-// staged in m->xh: one tcgen05 launch for T >= kMinTcgenM or T <= 16 (the
-// split-K kernel), else mma.sync tiles of 8 rows, up to kMaxJobs tiles per
-// launch.
+// staged in m->xh: one tcgen05 launch for T >= kMinTcgenM or 9 <= T <= 16
+// (the split-K kernel), else mma.sync tiles of 8 rows, up to kMaxJobs tiles
+// per launch.
 int run_mm(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* const* ys, const float* const* adds,
            cudaStream_t st) {
     const int sm = m->ctx->sm_count;
@@ -496,7 +496,7 @@ int run_mm(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* con
         for (int i = 0; i < n; i++) jobs.push_back(MMJobDesc{ws[i], 0, (int)T, ys[i], adds ? adds[i] : nullptr});
         return launch_mm_tc(jobs.data(), (int)jobs.size(), m->xh, T, sm, st);
     }
-    if (T <= kSkinnyMaxM) {
+    if (T >= kSkinnyMinM && T <= kSkinnyMaxM) {
         for (int i = 0; i < n; i++) jobs.push_back(MMJobDesc{ws[i], 0, (int)T, ys[i], adds ? adds[i] : nullptr});
         return launch_mm_skinny(m->ctx, jobs.data(), (int)jobs.size(), m->xh, T, st);
     }

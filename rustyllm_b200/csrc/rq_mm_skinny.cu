@@ -1,20 +1,27 @@
-// rq_mm_skinny.cu -- Q4_K matmul for 2..16 activation rows (speculative
-// verify batches, short prompt chunks) on the 5th-gen tensor cores.
+// rq_mm_skinny.cu -- Q4_K matmul for 9..16 activation rows (speculative
+// verify batches, short prompt chunks) on the 5th-gen tensor cores, in one
+// pass over the weights.
 //
-// At this width the work is HBM-bound: every weight byte must be read once
-// and at ~40 weights per clock per SM, so the kernel is built around the
-// cost per weight, not per MMA.
+// The kernel is built around the cost per weight, not per MMA, and around
+// one measured limit: a CTA issues a tcgen05.mma of 128 x N x 16 only every
+// ~60-100 cycles at small N, whatever the operand source (TMEM or shared
+// memory), the spacing of dependent MMAs or the number of issuing warps, so
+// the ~2048 weights per MMA cap the kernel near 20 weights per clock per SM
+// (~1.3 TB/s of Q4_K) at any M.  Below 9 rows the mma.sync kernel, whose
+// 8-row tiles cost the same, is faster; from 9 to 16 rows this one is (one
+// pass instead of two).
 //   * The 4-bit quants enter the MMA as they are: a nibble's bit pattern
 //     in a 16-bit lane is the f16 subnormal q * 2^-24, a high nibble masked
 //     in place is 16 q * 2^-24; one shift and four masks turn a word of 8
 //     weights into four f16x2 operand words (no multiply, no conversion).
 //   * Each of the 8 sub-blocks of a super-block accumulates into its own
-//     TMEM accumulator (K = 32: two MMAs), so 8 independent MMA chains hide
-//     the tensor core's latency, and the sub-block scales sc_j (6-bit) are
+//     TMEM accumulator (K = 32: two MMAs), so the MMAs never wait on one
+//     another, and the sub-block scales sc_j (6-bit) are
 //     applied in the epilogue: y += d * sum_j sc_j P1_j - dmin * P2 with
 //     P2 = [m_0..7, m_0..7] . [bsum_hi ; bsum_lo] (one K = 16 MMA) exactly
 //     as in rq_mm_tc.cu.  Every operand is exact; the activations arrive as
-//     x / s = hi + lo in f16 (stacked along N: the MMA's N is 2 nt).
+//     x / s = hi + lo in f16 (stacked along N: the MMA's N is 32 for the
+//     16 token columns).
 //   * Persistent CTAs take equal ranges of (128-row tile, super-block)
 //     units over all jobs, so 1024-row and 28672-row weights alike fill the
 //     148 SMs.  A tile cut between CTAs is finished by the last CTA to
@@ -26,14 +33,15 @@
 //          headers, the block-sum operand B2), ring C (one 64-element chunk
 //          of x_hi / x_lo: B1).
 //   1      TMEM allocation, all MMAs (one elected lane), commits.
-//   2..9   expand: warp w writes TMEM lanes 32 (w % 4) .. +31 (rows), the
-//          low (h = 0) or high (h = 1) nibbles of a chunk: 16 columns of the
-//          chunk's A slot; the h = 0 warps also write A2 (the m values).
+//   2..9   expand: warp w writes TMEM lanes 32 (w % 4) .. +31 (rows); the
+//          two warps of a lane quarter take alternate 64-element chunks
+//          (both nibbles: the chunk's 32-column A slot); the first also
+//          writes A2 (the m values).
 //   10..17 epilogue: two warps per lane quarter, each reads 4 of the 8
 //          sub-block accumulators; running totals stay in registers and the
 //          two halves are added once per tile piece.
-// TMEM columns: nb buffers of [8 chains x 2 nt | P2 16], then na A slots
-// of 32 (64 f16 of K per row).  Every mbarrier wait is bounded; on expiry
+// TMEM columns: one buffer of [8 chains x 32 | P2 16], then na A slots of
+// 32 (64 f16 of K per row).  Every mbarrier wait is bounded; on expiry
 // the CTA records the error and skips work, and TMEM is always released.
 
 #include <string.h>
@@ -56,6 +64,7 @@ constexpr int kChains = 8;  // one accumulator per sub-block
 constexpr int kMaxR = 8, kMaxC = 8, kMaxA = 6;
 constexpr int kSmemSK = 227 * 1024;
 constexpr float kSub = 16777216.0f;  // 2^24: f16 subnormal n * 2^-24 -> n
+constexpr int kNT = 16;              // token columns per tile (x_hi and x_lo: MMA N = 32)
 
 struct SKJob {
     float* y;
@@ -115,9 +124,10 @@ __device__ __forceinline__ long long cta_of(const SKParams& p, long long x) {
     return ((x + 1) * (long long)gridDim.x + p.units - 1) / p.units - 1;
 }
 
-template <int NT>
 __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_constant__ SKParams p) {
-    constexpr uint32_t N1 = 2 * NT;  // P1 columns per chain: x_hi tokens, then x_lo tokens
+    constexpr int NT = kNT;
+    constexpr uint32_t N1 = 2 * NT;   // P1 columns per chain: x_hi tokens, then x_lo tokens
+    constexpr uint32_t kEpiPerSB = 8;  // epilogue warps that read one super-block
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
@@ -138,21 +148,23 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
     const int nblk = p.nblk;
 
     if (threadIdx.x == 0) {
+        // an R stage is free once the MMAs have read it (one commit) and
+        // the epilogue warps of its super-block have read the header
         for (int i = 0; i < p.nr; i++) {
             mbar_init(rfull0 + 8 * i, 1);
-            mbar_init(rempty0 + 8 * i, 1);
+            mbar_init(rempty0 + 8 * i, 1 + kEpiPerSB);
         }
         for (int i = 0; i < p.nc; i++) {
             mbar_init(cfull0 + 8 * i, 1);
             mbar_init(cempty0 + 8 * i, 1);
         }
         for (int i = 0; i < p.na; i++) {
-            mbar_init(aready0 + 8 * i, 8);
+            mbar_init(aready0 + 8 * i, 4);
             mbar_init(aempty0 + 8 * i, 1);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(accfull0 + 8 * b, 1);
-            mbar_init(accempty0 + 8 * b, 8);
+            mbar_init(accempty0 + 8 * b, kEpiPerSB);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -264,18 +276,21 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
         if (!ok && lane == 0 && p.err) atomicExch(p.err, 1);
     } else if (warp < kEpiWarp0) {
         // ----------------------------------------------------------- expand
-        const int q = warp & 3, h = (warp - kExpWarp0) >> 2;
+        // Warp w writes TMEM lanes 32 (w % 4) .. +31 (rows r); the two warps
+        // of a lane quarter take alternate chunks (par 0: chunks 0, 2 of every
+        // super-block, par 1: chunks 1, 3), both nibbles of each (32
+        // columns), and store both chunks before waiting for the stores.
+        const int q = warp & 3, par = (warp - kExpWarp0) >> 2;
         const int r = 32 * q + lane;
         const uint32_t swz = (uint32_t)(r & 7);
-        const uint32_t lane_a = tmem + ((uint32_t)(32 * q) << 16) + p.acol0 + 16u * (uint32_t)h;
-        const uint32_t mask = h ? 0x00F000F0u : 0x000F000Fu;
-        Ring rr, ar;
+        const uint32_t lane_a = tmem + ((uint32_t)(32 * q) << 16) + p.acol0;
+        Ring rr, ar;  // ar: the A slot of the super-block's chunk 0
         bool ok = true;
         while (sg.next(p, s)) {
             for (int sb = s.sb0; sb < s.sb1; sb++, rr.next(p.nr)) {
                 if (ok && !wait_err(rfull0 + 8 * rr.i, rr.u & 1, p.err)) ok = false;
                 const uint8_t* rst = ringr_p + (size_t)rr.i * p.r_bytes;
-                if (ok && h == 0) {
+                if (ok && par == 0) {
                     // A2 row r: [m_0..7, m_0..7] as f16 subnormals (32-byte
                     // swizzle; both 16-byte halves are equal)
                     const uint4 hd = *reinterpret_cast<const uint4*>(rst + p.r_hdr + r * 16);
@@ -292,120 +307,117 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
                     // generic-proxy writes become visible to the tensor core
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
-                for (int cq = 0; cq < 4; cq++, ar.next(p.na)) {
-                    if (ok && ar.u > 0 && !wait_err(aempty0 + 8 * ar.i, (ar.u - 1) & 1, p.err)) ok = false;
+                Ring a = ar;
+                if (par) a.next(p.na);
+                int slot[2];
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    if (c) {
+                        a.next(p.na);
+                        a.next(p.na);
+                    }
+                    slot[c] = a.i;
+                    if (ok && a.u > 0 && !wait_err(aempty0 + 8 * a.i, (a.u - 1) & 1, p.err)) ok = false;
                     ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-wide
                     tmem_fence_after();
                     if (ok) {
                         // the chunk's 32 quant bytes of row r: 16-byte chunks
                         // 2cq, 2cq+1 of the row's 128-byte-swizzled line
+                        const int cq = par + 2 * c;
                         const uint8_t* qrow = rst + r * 128;
                         const uint4 qa = *reinterpret_cast<const uint4*>(qrow + (((2 * cq) ^ swz) << 4));
                         const uint4 qb = *reinterpret_cast<const uint4*>(qrow + (((2 * cq + 1) ^ swz) << 4));
                         const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                        uint32_t o[16];
+                        uint32_t o[32];
 #pragma unroll
                         for (int i = 0; i < 8; i++) {
                             // bytes b0..b3: (b0, b2) and (b1, b3) in 16-bit
-                            // lanes, i.e. elements (e0, e2), (e1, e3)
-                            o[2 * i] = qw[i] & mask;
-                            o[2 * i + 1] = (qw[i] >> 8) & mask;
+                            // lanes, i.e. elements (e0, e2), (e1, e3); low
+                            // nibbles are K 0..31 of the chunk, high 32..63
+                            const uint32_t v = qw[i] >> 8;
+                            o[2 * i] = qw[i] & 0x000F000Fu;
+                            o[2 * i + 1] = v & 0x000F000Fu;
+                            o[16 + 2 * i] = qw[i] & 0x00F000F0u;
+                            o[17 + 2 * i] = v & 0x00F000F0u;
                         }
                         // TMEM column c of the slot holds K positions 2c, 2c+1
-                        tmem_st16u(lane_a + 32u * (uint32_t)ar.i, o);
-                        tmem_wait_st();
+                        tmem_st32u(lane_a + 32u * (uint32_t)a.i, o);
                     }
-                    tmem_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(aready0 + 8 * ar.i);
                 }
+                if (ok) tmem_wait_st();
+                tmem_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(aready0 + 8 * slot[0]);
+                    mbar_arrive(aready0 + 8 * slot[1]);
+                }
+#pragma unroll
+                for (int c = 0; c < 4; c++) ar.next(p.na);
             }
         }
         if (!ok && lane == 0 && p.err) atomicExch(p.err, 1);
     } else {
         // ------------------------------------------------------------ epilogue
+        // Each warp reads 4 of the 8 chains of every super-block, the low
+        // half also P2.  The header comes from the R stage, which the
+        // epilogue releases together with the MMA.
         const int q = warp & 3, half = (warp - kEpiWarp0) >> 2;
         const int r = 32 * q + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-        const Q4KScaleSel sel0 = q4k_scale_sel(2 * half), sel1 = q4k_scale_sel(2 * half + 1);
-        Ring br;
+        Ring br, rr;
         bool ok = true;
         while (sg.next(p, s)) {
             const int j = job_of(p, s.t);
             const SKJob& jb = p.jobs[j];
             const int64_t row = (int64_t)(s.t - jb.t0) * kRowsTC + r;
             const bool live = row < jb.out;
-            const uint8_t* hrow = jb.hdr + (live ? row : 0) * (int64_t)nblk * 16;
             float tot[NT];
 #pragma unroll
             for (int i = 0; i < NT; i++) tot[i] = 0.0f;
-            uint4 hd = live ? __ldg(reinterpret_cast<const uint4*>(hrow + s.sb0 * 16)) : make_uint4(0u, 0u, 0u, 0u);
-            for (int sb = s.sb0; sb < s.sb1; sb++, br.next(p.nb)) {
+            for (int sb = s.sb0; sb < s.sb1; sb++, br.next(p.nb), rr.next(p.nr)) {
                 const int b = br.i;
-                const uint4 hn = (live && sb + 1 < s.sb1) ? __ldg(reinterpret_cast<const uint4*>(hrow + (sb + 1) * 16))
-                                                          : make_uint4(0u, 0u, 0u, 0u);
-                const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hd.x));
-                const float fd = dm.x * kSub, fm = -dm.y * kSub;
-                const uint32_t w0 = q4k_scales(sel0, hd), w1 = q4k_scales(sel1, hd);
-                // chains 4 half + i: sub-blocks 4 half, +1 (high nibbles: 16 q), +2, +3 (16 q)
-                const float k0 = fd * (float)(w0 & 0xFFu), k1 = fd * 0.0625f * (float)((w0 >> 8) & 0xFFu);
-                const float k2 = fd * (float)(w1 & 0xFFu), k3 = fd * 0.0625f * (float)((w1 >> 8) & 0xFFu);
                 if (ok && !wait_err(accfull0 + 8 * b, br.u & 1, p.err)) ok = false;
                 ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-wide
                 tmem_fence_after();
-                const uint32_t bcol = lane_base + (uint32_t)b * p.buf_cols + (uint32_t)(4 * half) * N1;
+                // sub-block scales: chain c = sub-block c, its coefficient
+                // d 2^24 sc_c (1/16 more for odd c: high nibbles are 16 q)
+                const uint4 hd = *reinterpret_cast<const uint4*>(ringr_p + (size_t)rr.i * p.r_bytes + p.r_hdr + r * 16);
+                const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hd.x));
+                const float fd = dm.x * kSub, fm = -dm.y * kSub;
+                // chains 4 half .. 4 half + 3
+                float kc[4];
+#pragma unroll
+                for (int g = 0; g < 2; g++) {
+                    const uint32_t w = q4k_scales(q4k_scale_sel(2 * half + g), hd);
+                    kc[2 * g] = fd * (float)(w & 0xFFu);
+                    kc[2 * g + 1] = fd * 0.0625f * (float)((w >> 8) & 0xFFu);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(rempty0 + 8 * rr.i);  // the header is read
+                const uint32_t bbase = lane_base + (uint32_t)b * p.buf_cols;
                 if (ok) {
-                    if constexpr (NT == 8) {
-                        uint32_t u0[16], u1[16];
-                        tmem_ld16(bcol, u0);
-                        tmem_ld16(bcol + N1, u1);
-                        tmem_wait_ld();
+                        // one 32-column chain per load: 18 warps leave 96
+                        // registers per thread
 #pragma unroll
-                        for (int i = 0; i < 8; i++) {
-                            const float v = fmaf(k0, __uint_as_float(u0[i]) + __uint_as_float(u0[8 + i]), tot[i]);
-                            tot[i] = fmaf(k1, __uint_as_float(u1[i]) + __uint_as_float(u1[8 + i]), v);
-                        }
-                        tmem_ld16(bcol + 2 * N1, u0);
-                        tmem_ld16(bcol + 3 * N1, u1);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 8; i++) {
-                            const float v = fmaf(k2, __uint_as_float(u0[i]) + __uint_as_float(u0[8 + i]), tot[i]);
-                            tot[i] = fmaf(k3, __uint_as_float(u1[i]) + __uint_as_float(u1[8 + i]), v);
-                        }
-                        if (half == 0) {
-                            tmem_ld16(lane_base + (uint32_t)b * p.buf_cols + kChains * N1, u0);
+                        for (int c = 0; c < 4; c++) {
+                            uint32_t ua[32];
+                            tmem_ld32(bbase + (uint32_t)(4 * half + c) * N1, ua);
                             tmem_wait_ld();
 #pragma unroll
-                            for (int i = 0; i < 8; i++) tot[i] = fmaf(fm, __uint_as_float(u0[i]), tot[i]);
-                        }
-                    } else {
-                        const float kc[4] = {k0, k1, k2, k3};
-#pragma unroll
-                        for (int c = 0; c < 4; c += 2) {
-                            uint32_t ua[32], ub[32];
-                            tmem_ld32(bcol + (uint32_t)c * N1, ua);
-                            tmem_ld32(bcol + (uint32_t)(c + 1) * N1, ub);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int i = 0; i < 16; i++) {
-                                float v = fmaf(kc[c], __uint_as_float(ua[i]) + __uint_as_float(ua[16 + i]), tot[i]);
-                                tot[i] = fmaf(kc[c + 1], __uint_as_float(ub[i]) + __uint_as_float(ub[16 + i]), v);
-                            }
+                            for (int i = 0; i < 16; i++)
+                                tot[i] = fmaf(kc[c], __uint_as_float(ua[i]) + __uint_as_float(ua[16 + i]), tot[i]);
                         }
                         if (half == 0) {
                             uint32_t p2[16];
-                            tmem_ld16(lane_base + (uint32_t)b * p.buf_cols + kChains * N1, p2);
+                            tmem_ld16(bbase + kChains * N1, p2);
                             tmem_wait_ld();
 #pragma unroll
                             for (int i = 0; i < 16; i++) tot[i] = fmaf(fm, __uint_as_float(p2[i]), tot[i]);
                         }
-                    }
                 }
                 tmem_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(accempty0 + 8 * b);
-                hd = hn;
             }
             // ---- end of the tile piece: add the halves (low + high), then
             // write y, or the piece and count it
@@ -507,7 +519,8 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
         tiles += (int)((w->out + kRowsTC - 1) / kRowsTC);
         mmax = std::max(mmax, jobs[j].M);
     }
-    const int nt = mmax <= 8 ? 8 : 16;
+    const int nt = kNT;
+    (void)mmax;
     int rc = encode(&p.xhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh.v, (uint64_t)in, (uint64_t)rows, (uint64_t)(4 * in),
                     64, (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B, "activations (hi)");
     if (!rc)
@@ -530,7 +543,7 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
     p.nblk = (int)nblk;
     // TMEM: nb buffers of [8 chains x 2 nt | P2 16] and na A slots of 32
     p.buf_cols = (uint32_t)(kChains * 2 * nt + 16);
-    p.nb = nt == 8 ? 2 : 1;
+    p.nb = 1;
     p.acol0 = (uint32_t)p.nb * p.buf_cols;
     p.na = std::min(kMaxA, (int)((512 - p.acol0) / 32));
     p.tmem_cols = 512;
@@ -550,15 +563,13 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
     p.c_off = (uint32_t)p.nr * p.r_bytes;
     const size_t smem = 1024 + (size_t)p.ring_off + p.c_off + (size_t)p.nc * p.c_bytes;
 
-    static bool attr_set[2][64] = {};
+    static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    const int ki = nt == 8 ? 0 : 1;
-    auto kern = nt == 8 ? mm_skinny_kernel<8> : mm_skinny_kernel<16>;
-    if (dev < 0 || dev >= 64 || !attr_set[ki][dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemSK);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(mm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemSK);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(skinny matmul)");
-        if (dev >= 0 && dev < 64) attr_set[ki][dev] = true;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
@@ -570,7 +581,7 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_error(cudaLaunchKernelEx(&cfg, kern, p), "skinny matmul kernel");
+    return cuda_error(cudaLaunchKernelEx(&cfg, mm_skinny_kernel, p), "skinny matmul kernel");
 }
 
 }  // namespace rq

@@ -31,7 +31,7 @@ def build(oracle, qtype, seed, cfg=CFG):
     return model, ref
 
 
-@pytest.mark.parametrize("qtype,n_prompt", [(12, 20), (12, 28), (11, 20), (12, 3)])
+@pytest.mark.parametrize("qtype,n_prompt", [(12, 20), (12, 28), (11, 20), (12, 3), (12, 13)])
 def test_prompt_logits_and_greedy_tokens_match_oracle(oracle, rq_ctx, qtype, n_prompt):
     """Q4_K prompts of 4..23 tokens run their linears on the mma.sync
     kernel, 24 and more on tcgen05; 3 tokens and Q3_K run M=1 jobs."""
