@@ -302,17 +302,13 @@ struct JobList {
     std::vector<float*> y;
 };
 
-// jobs with 9 <= M_j <= 16 on the split-K tcgen05 kernel, M_j >= 24 on the
-// tiled tcgen05 kernel, the rest (8-row tiles) on mma.sync
-int run_mm_jobs(rq_ctx* ctx, const std::vector<MMJobDesc>& J, XH xh, int64_t rows, int sm, cudaStream_t st) {
-    std::vector<MMJobDesc> sm_jobs, tc_jobs, sk_jobs;
-    for (const MMJobDesc& j : J)
-        (j.M >= kMinTcgenM ? tc_jobs : (j.M >= kSkinnyMinM && j.M <= kSkinnyMaxM) ? sk_jobs : sm_jobs).push_back(j);
-    for (size_t b = 0; b < sk_jobs.size(); b += kMaxJobs) {
-        const int n = (int)std::min<size_t>(kMaxJobs, sk_jobs.size() - b);
-        int rc = launch_mm_skinny(ctx, &sk_jobs[b], n, xh, rows, st);
-        if (rc) return rc;
-    }
+// jobs with M_j <= 8 on the mma.sync kernel, larger ones on tcgen05 (not
+// the split-K kernel: its piece boundaries depend on the other jobs of a
+// launch, and a token must give the same bits in a layer call as in an
+// expert-parallel one)
+int run_mm_jobs(const std::vector<MMJobDesc>& J, XH xh, int64_t rows, int sm, cudaStream_t st) {
+    std::vector<MMJobDesc> sm_jobs, tc_jobs;
+    for (const MMJobDesc& j : J) (j.M >= kMinTcgenM ? tc_jobs : sm_jobs).push_back(j);
     for (size_t b = 0; b < sm_jobs.size(); b += kMaxJobs) {
         const int n = (int)std::min<size_t>(kMaxJobs, sm_jobs.size() - b);
         int rc = launch_mm_small(&sm_jobs[b], n, xh, rows, sm, st);
@@ -376,14 +372,10 @@ int launch_gather(const float* src, const int32_t* idx, int64_t rows, int64_t H,
 }
 
 // out[r] = FFN_e(rows[r]) for the R rows of the segments (expert e of each).
-// Segments of at least kMinTensorM rows run on the tensor cores (9..16 rows
-// as one split-K job, 4..8 and 17..23 in tiles of 8 rows, more as one tiled
-// job); the others run one M=1 pipeline job per row.  On the pipeline and
-// the tiled kernels a row's result depends only on that row and on its
-// segment's size; the split-K kernel also sums a tile's K pieces at
-// boundaries set by the launch's total work, so there a token's bits can
-// differ between a layer call and an expert-parallel one (both stay within
-// the tolerance of the f32 reference).
+// Segments of at least kMinTensorM rows run on the tensor-core kernel in
+// tiles of 8 rows; the others run one M=1 pipeline job per row.  Every row's
+// result depends only on that row and on its segment's size, so a token gives
+// the same bits in one layer call as in an expert-parallel one.
 int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& segs, float* out, cudaStream_t st) {
     if (R == 0) return RQ_OK;
     const int64_t H = m->H, F = m->F;
@@ -409,7 +401,7 @@ int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& 
     std::vector<MMJobDesc> upm, downm;
     for (const Seg& sg : segs) {
         const size_t e = (size_t)sg.e;
-        if (use_mm(sg) && (sg.n >= kMinTcgenM || (sg.n >= kSkinnyMinM && sg.n <= kSkinnyMaxM))) {
+        if (use_mm(sg) && sg.n >= kMinTcgenM) {
             upm.push_back(MMJobDesc{m->w1[e], (int)sg.start, (int)sg.n, m->g + sg.start * F, nullptr});
             upm.push_back(MMJobDesc{m->w3[e], (int)sg.start, (int)sg.n, m->u + sg.start * F, nullptr});
             downm.push_back(MMJobDesc{m->w2[e], (int)sg.start, (int)sg.n, out + sg.start * H, nullptr});
@@ -434,7 +426,7 @@ int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& 
         }
     }
     rc = run_jobs(up, sm, st);
-    if (!rc) rc = run_mm_jobs(m->ctx, upm, xhx, R, sm, st);
+    if (!rc) rc = run_mm_jobs(upm, xhx, R, sm, st);
     cudaLaunchAttribute attr[1];
     if (!rc && any_mm) {
         cudaLaunchConfig_t cfg = pdl(dim3(1184), dim3(256), st, attr);
@@ -445,7 +437,7 @@ int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& 
         rc = launch_xquant_swiglu(m->g, m->u, R, F, xqh, st);
     }
     if (!rc) rc = run_jobs(down, sm, st);
-    if (!rc) rc = run_mm_jobs(m->ctx, downm, xhh, R, sm, st);
+    if (!rc) rc = run_mm_jobs(downm, xhh, R, sm, st);
     return rc;
 }
 
