@@ -108,6 +108,9 @@ namespace rq {
 int tp_world(const rq_ctx* ctx);
 int tp_rank(const rq_ctx* ctx);
 int tp_allreduce(rq_ctx* ctx, const void* in, void* out, int64_t n, int dtype, int op, cudaStream_t st);
+// the peer-memory exchange regions of the communicator, if it has them
+struct P2PArgs;
+bool tp_p2p_args(const rq_ctx* ctx, P2PArgs* a);
 void tp_destroy(rq_ctx* ctx);
 // all-gather of nbytes from every rank into out[world][nbytes]
 int tp_allgather_bytes(rq_ctx* ctx, const void* in, void* out, int64_t nbytes, cudaStream_t st);
@@ -149,9 +152,15 @@ struct PipeJob {
     int64_t out;
 };
 bool pipe_supported(const rq_weight* w);
+// With ar (one job, row-parallel under tensor parallelism): the partial y is
+// all-reduced over the ranks' NVLink exchange regions inside the kernel and
+// y receives the sum; returns kPipeNotFusable (no error set) when the launch
+// cannot be fused.
+struct P2PArgs;
+constexpr int kPipeNotFusable = -1;
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err = nullptr,
-                       const float* const* adds = nullptr);
+                       const float* const* adds = nullptr, const P2PArgs* ar = nullptr);
 
 // small-M Q4_K matmul on the tensor cores (rq_mm_small.cu).  Activations are
 // staged per row as x / s = hi + lo (two f16 values per element, s a power of

@@ -28,6 +28,7 @@
 
 #include "rq_attn.cuh"
 #include "rq_decode.cuh"
+#include "rq_p2p.cuh"
 #include "rq_mv_common.cuh"
 
 struct rq_llama {
@@ -465,10 +466,21 @@ int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float
     return RQ_OK;
 }
 
+// RQ_TP_FUSED=0 in the environment keeps the decode all-reduce a separate
+// kernel (the fused and separate forms give the same bits)
+bool tp_fused_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("RQ_TP_FUSED");
+        return !(e && strcmp(e, "0") == 0);
+    }();
+    return on;
+}
+
 // x = x + x_in W^T for a row-parallel weight (o_proj, down_proj).  One rank:
 // the residual add is fused into the matvec epilogue.  W ranks: each rank's
 // partial product (rank 0 also adds the residual) is summed into x by an
-// all-reduce.
+// all-reduce -- at T = 1 on the pipeline inside the matvec kernel itself,
+// over the ranks' NVLink exchange regions.
 int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
     if (m->W == 1) {
         const rq_weight* w1[1] = {w};
@@ -477,6 +489,14 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
         return run_linears(m, 1, w1, T, y1, a1, st);
     }
     const rq_weight* w1[1] = {w};
+    P2PArgs ar;
+    if (T == 1 && tp_fused_enabled() && pipe_supported(w) && tp_p2p_args(m->ctx, &ar)) {
+        const XQ xq = m->xq;
+        float* y = m->x;
+        const float* add = m->R == 0 ? m->x : nullptr;
+        const int rc = launch_matvec_pipe(w1, &xq, &y, 1, m->ctx->sm_count, st, nullptr, &add, &ar);
+        if (rc != kPipeNotFusable) return rc;
+    }
     float* y1[1] = {m->part};
     const float* a1[1] = {m->R == 0 ? m->x : nullptr};
     int rc = run_linears(m, 1, w1, T, y1, a1, st);

@@ -23,11 +23,21 @@
 // wait (griddepcontrol.wait) for the staging kernel before reading planes.
 // Every mbarrier wait is bounded (~1 s); on expiry the kernel sets the error
 // word, drains its in-flight copies and exits.
+//
+// Fused all-reduce (row-parallel linears under tensor parallelism, one job):
+// instead of writing its rows of y, a CTA stores its partial rows into slot
+// [its rank] of every rank's NVLink exchange buffer (posted stores, no round
+// trip), release-flags every peer, waits (acquire, bounded) for the peers'
+// flags of the same CTA index -- every rank runs the same grid over the same
+// rows -- and sums the W slots of its own buffer in rank order into y: the
+// bits of the standalone one-shot all-reduce (rq_tp.cu), without its launch
+// and with only local reads after the wait.
 
 #include <algorithm>
 
 #include "rq_async.cuh"
 #include "rq_mv_common.cuh"
+#include "rq_p2p.cuh"
 #include "rq_pipe_lane.cuh"
 
 namespace rq {
@@ -49,6 +59,8 @@ struct PipeParams {
     int S, G, RS, nstage;
     uint32_t qrow, hrow;  // device bytes per weight row (quant part, header part)
     uint32_t stage_bytes, red_off, ring_off;
+    int fuse;             // 1: all-reduce y over the ranks of ar (one job)
+    P2PArgs ar;
 };
 
 __device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) {
@@ -56,6 +68,68 @@ __device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) 
     const int64_t e = (int64_t)(blockIdx.x + 1) * j.out / gridDim.x;
     *rb = b;
     *n = (int)(e - b);
+}
+
+// The fused all-reduce epilogue of one job (see the file comment); red holds
+// this CTA's [row][slice] partials.
+__device__ __forceinline__ void allreduce_rows(const PipeParams& p, const float* red) {
+    // every thread orders its reads (the epoch word) after the previous grids
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const PipeJob& jb = p.jobs[0];
+    int64_t rb;
+    int nrows;
+    job_rows(jb, &rb, &nrows);
+    uint8_t* own = p.ar.base[p.ar.rank];
+    uint32_t* ctl = reinterpret_cast<uint32_t*>(own + kP2PCtlOff);  // epoch, done, err
+    const uint32_t e = *reinterpret_cast<volatile uint32_t*>(ctl);
+    const int par = (int)(e & 1u);
+    const int t = threadIdx.x, W = p.ar.world, me = p.ar.rank;
+    const int64_t slot = (int64_t)me * jb.out;  // this rank's slot in every buffer
+    for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
+        float acc = 0.0f;
+        for (int s = 0; s < p.S; s++) acc += red[i * p.S + s];
+        const float v = jb.add ? acc + jb.add[rb + i] : acc;
+#pragma unroll
+        for (int r = 0; r < kP2PMaxWorld; r++)
+            if (r < W) reinterpret_cast<float*>(p.ar.base[r] + par * kP2PCap)[slot + rb + i] = v;
+    }
+    __syncthreads();
+    const size_t fslot = ((size_t)par * kP2PFlagCTAs + blockIdx.x) * kP2PMaxWorld;
+    if (t < W && t != me) {
+        // this CTA's rows are in place: tell rank t
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<uint32_t*>(p.ar.base[t] + kP2PFlagsOff) + fslot + me, e + 1u);
+    }
+    bool ok = true;
+    if (t < W && t != me) {
+        const uint32_t* f = reinterpret_cast<const uint32_t*>(own + kP2PFlagsOff) + fslot + t;
+        const long long t0 = clock64();
+        while ((int)(ld_acquire_sys(f) - (e + 1u)) < 0)
+            if (clock64() - t0 > kWaitCycles) {
+                ok = false;
+                atomicExch(ctl + 2, 1u);
+                break;
+            }
+    }
+    ok = __syncthreads_and(ok);
+    if (ok) {
+        const float* mine = reinterpret_cast<const float*>(own + par * kP2PCap);
+        for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
+            float acc = mine[rb + i];
+#pragma unroll
+            for (int r = 1; r < kP2PMaxWorld; r++)
+                if (r < W) acc = acc + mine[(int64_t)r * jb.out + rb + i];
+            jb.y[rb + i] = acc;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(ctl + 1, 1u) == gridDim.x - 1u) {
+            atomicExch(ctl + 1, 0u);
+            atomicAdd(ctl, 1u);
+        }
+    }
 }
 
 template <int TYPE, int RPW>
@@ -150,6 +224,10 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         }
     }
     __syncthreads();
+    if (p.fuse) {
+        allreduce_rows(p, red);
+        return;
+    }
     int roff = 0;
     for (int j = 0; j < p.njobs; j++) {
         int64_t rb;
@@ -209,7 +287,7 @@ bool pipe_supported(const rq_weight* w) {
 }
 
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
-                       int sm_count, cudaStream_t st, int* err, const float* const* adds) {
+                       int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "matvec pipeline: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     TypeInfo ti = type_info(w0->type);
@@ -247,6 +325,16 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
         return r;
     };
     while (rows_cap(grid) * p.S * 4 > 32 * 1024) grid *= 2;
+    p.fuse = 0;
+    if (ar) {
+        // every CTA must be resident at once (it waits for its peers), and
+        // the flags and the exchange buffer must hold the grid and the rows
+        if (njobs != 1 || grid > sm_count || grid > kP2PFlagCTAs || ar->world > kP2PMaxWorld ||
+            (size_t)ar->world * w0->out * 4 > kP2PCap)
+            return kPipeNotFusable;
+        p.fuse = 1;
+        p.ar = *ar;
+    }
     p.red_off = kBarBytes;
     p.ring_off = (uint32_t)((kBarBytes + rows_cap(grid) * p.S * 4 + 127) & ~(int64_t)127);
     int nstage = (int)((kSmemBudget - p.ring_off) / p.stage_bytes);

@@ -25,21 +25,11 @@
 
 #include "rq_async.cuh"
 #include "rq_internal.cuh"
+#include "rq_p2p.cuh"
 
 namespace rq {
 
-constexpr int kP2PMaxWorld = 8;
-constexpr int kP2PMaxCTA = 32;
-constexpr size_t kP2PCap = 4u << 20;  // bytes per buffer parity
-// own exchange region: data [2][kP2PCap] | flags [2][kP2PMaxCTA][kP2PMaxWorld] u32 | epoch, done, err
-constexpr size_t kP2PFlagsOff = 2 * kP2PCap;
-constexpr size_t kP2PCtlOff = kP2PFlagsOff + 2 * kP2PMaxCTA * kP2PMaxWorld * 4;
-constexpr size_t kP2PBytes = kP2PCtlOff + 256;
-
-struct P2PArgs {
-    uint8_t* base[kP2PMaxWorld];  // every rank's exchange region (own included), in this process
-    int world, rank;
-};
+constexpr int kP2PMaxCTA = 32;  // CTAs of the standalone all-reduce kernel
 
 struct TPComm {
     ncclComm_t comm = nullptr;
@@ -91,15 +81,6 @@ int settle(TPComm* c, ncclResult_t r, const char* what, double timeout_ms) {
 
 constexpr double kOpTimeoutMs = 60000.0;  // enqueue bound for collectives
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 template <typename T>
 __device__ __forceinline__ T reduce_op(T a, T b) {
     return a + b;
@@ -135,7 +116,7 @@ __global__ void __launch_bounds__(512) p2p_allreduce_kernel(const T* in, T* out,
     for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) mine[i] = src[i];
     __syncthreads();
     const int t = threadIdx.x;
-    const size_t fslot = ((size_t)par * kP2PMaxCTA + (size_t)c) * kP2PMaxWorld;
+    const size_t fslot = ((size_t)par * kP2PFlagCTAs + (size_t)c) * kP2PMaxWorld;
     if (t < a.world && t != a.rank) {
         // this CTA's slice is in place: tell rank t
         __threadfence_system();
@@ -277,6 +258,13 @@ int p2p_setup(TPComm* c) {
 
 int tp_world(const rq_ctx* ctx) { return ctx->tp ? ctx->tp->world : 1; }
 int tp_rank(const rq_ctx* ctx) { return ctx->tp ? ctx->tp->rank : 0; }
+
+bool tp_p2p_args(const rq_ctx* ctx, P2PArgs* a) {
+    const TPComm* c = ctx->tp;
+    if (!c || !c->comm || !c->p2p) return false;
+    *a = c->args;
+    return true;
+}
 
 int tp_allreduce(rq_ctx* ctx, const void* in, void* out, int64_t n, int dtype, int op, cudaStream_t st) {
     TPComm* c = ctx->tp;

@@ -1,6 +1,8 @@
 """Two-GPU tensor parallelism of the Llama decode loop: greedy tokens of the
 TP=2 model (column/row-parallel shards, all-reduces, vocab-parallel argmax)
-equal the single-GPU model's, with the peer-memory all-reduce and with NCCL.
+equal the single-GPU model's with the all-reduce fused into the row-parallel
+matvec kernel (the decode default), as a separate peer-memory kernel
+(RQ_TP_FUSED=0) and with NCCL.
 The peer-memory all-reduce itself: every rank gets the same bits, the sum
 in rank order, over both buffer parities, in place and out of place, at
 sizes below and above its NCCL cut-over.  Skipped with fewer than two
@@ -33,6 +35,8 @@ def _tp_rank(rank, world, port, out_dir, mode="p2p"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     if mode == "nccl":
         os.environ["RQ_TP_ALLREDUCE"] = "nccl"
+    if mode == "unfused":
+        os.environ["RQ_TP_FUSED"] = "0"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60),
@@ -47,6 +51,8 @@ def _tp_rank(rank, world, port, out_dir, mode="p2p"):
     toks = model.generate(prompt, 12)
     np.save(os.path.join(out_dir, f"tp{mode}{rank}.npy"), np.array(toks))
     model.close()
+    from rustyllm_b200 import _lib
+    _lib.check(_lib.lib().rq_tp_status(ctx.handle))   # no peer wait timed out
     tpmod.finalize(ctx)
     dist.destroy_process_group()
 
@@ -61,7 +67,7 @@ def test_tp2_decode_matches_single_gpu(tmp_path):
     prompt = np.random.default_rng(4).integers(0, CFG["vocab"], size=16).astype(np.int32)
     want = model.generate(prompt, 12)
     model.close()
-    for mode in ("p2p", "nccl"):
+    for mode in ("p2p", "unfused", "nccl"):
         mp.spawn(_tp_rank, args=(2, _free_port(), str(tmp_path), mode), nprocs=2, join=True)
         for r in range(2):
             assert np.load(tmp_path / f"tp{mode}{r}.npy").tolist() == want
