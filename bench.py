@@ -751,8 +751,9 @@ def run_gpu(args) -> None:
 def run_case(name: str) -> None:
     """A few launches of one kernel for an ncu capture: 'pipe_gate_up' (the
     gate+up rq_linear_batch of one 70B layer, M=1), 'mm_gate_m8' (gate_proj
-    8192 -> 28672 at M=8 on the mma.sync kernel) or 'tc_gate_m128' (the same
-    at M=128 on the tcgen05 kernel).  Prints the per-call time measured
+    8192 -> 28672 at M=8 on the mma.sync kernel), 'sk_gate_m16' (the same at
+    M=16 on the split-K tcgen05 kernel) or 'tc_gate_m128' (M=128 on the tiled
+    tcgen05 kernel).  Prints the per-call time measured
     without the profiler."""
     import ctypes
 
@@ -775,7 +776,7 @@ def run_case(name: str) -> None:
                                     arr([y.data_ptr() for y in ys]), s))
         nbytes = 2 * Q4K_BYTES(8192, 28672)
     else:
-        M = 8 if name == "mm_gate_m8" else 128
+        M = {"mm_gate_m8": 8, "sk_gate_m16": 16}.get(name, 128)
         x = torch.randn(M, 8192, device="cuda", generator=g)
         y = torch.empty(M, 28672, device="cuda")
 
@@ -793,8 +794,8 @@ def run_case(name: str) -> None:
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / 10
     out = {"case": name, "us_per_call": round(ms * 1e3, 2), "weight_gbs": round(nbytes / (ms / 1e3) / 1e9, 1)}
-    if name == "tc_gate_m128":
-        out["tflops"] = round(2 * 128 * 8192 * 28672 / (ms / 1e3) / 1e12, 1)
+    if name in ("tc_gate_m128", "sk_gate_m16"):
+        out["tflops"] = round(2 * M * 8192 * 28672 / (ms / 1e3) / 1e12, 1)
     print(json.dumps(out), flush=True)
 
 
@@ -812,7 +813,7 @@ def main():
     ap.add_argument("--no-moe", action="store_true", help="skip the Mixtral MoE layer sweep")
     ap.add_argument("--decode-layers", type=int, default=None,
                     help="layers of the decode model (default 80; fewer for profiling)")
-    ap.add_argument("--case", choices=["pipe_gate_up", "mm_gate_m8", "tc_gate_m128"], default=None,
+    ap.add_argument("--case", choices=["pipe_gate_up", "mm_gate_m8", "sk_gate_m16", "tc_gate_m128"], default=None,
                     help="run a few launches of one kernel (for profiling) and exit")
     args = ap.parse_args()
     if args.case:
