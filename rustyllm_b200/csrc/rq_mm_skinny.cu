@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
             mbar_init(cempty0 + 8 * i, 1);
         }
         for (int i = 0; i < p.na; i++) {
-            mbar_init(aready0 + 8 * i, 4);
+            mbar_init(aready0 + 8 * i, 8);
             mbar_init(aempty0 + 8 * i, 1);
         }
         for (int b = 0; b < 2; b++) {
@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
             const uint64_t pol_w = policy_evict_first(), pol_h = policy_evict_normal();
             const uint64_t pol_x = policy_evict_last();
             const uint32_t rtx = kRowsTC * 128 + kRowsTC * 16 + 16 * 32;
-            const uint32_t ctx = 2u * 128u * NT;
+            const uint32_t ctx = 4u * 128u * NT;  // two chunks of x_hi and x_lo
             Ring rr, cr;
             int ri = 0, ci = 0;
             bool ok = true;
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
                     tma_load_2d(st, &p.wq[j], sb * 128, row0, fb, pol_w);
                     tma_load_2d(st + p.r_hdr, &p.wh[j], sb * 16, row0, fb, pol_h);
                     tma_load_2d(st + p.r_b2, &p.bs, sb * 16, tok, fb, pol_x);
-                    for (int cq = 0; cq < 4; cq++, ci++, cr.next(p.nc)) {
+                    for (int h = 0; h < 2; h++, ci++, cr.next(p.nc)) {
                         if (cr.u > 0 && !wait_err(cempty0 + 8 * cr.i, (cr.u - 1) & 1, p.err)) {
                             ok = false;
                             break;
@@ -216,8 +216,12 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
                         const uint32_t sc = ringc + (uint32_t)cr.i * p.c_bytes;
                         const uint32_t cb = cfull0 + 8 * cr.i;
                         mbar_expect_tx(cb, ctx);
-                        tma_load_2d(sc, &p.xhi, (4 * sb + cq) * 64, tok, cb, pol_x);
-                        tma_load_2d(sc + 128u * NT, &p.xlo, (4 * sb + cq) * 64, tok, cb, pol_x);
+#pragma unroll
+                        for (int c = 0; c < 2; c++) {
+                            const int x = (4 * sb + 2 * h + c) * 64;
+                            tma_load_2d(sc + 256u * NT * c, &p.xhi, x, tok, cb, pol_x);
+                            tma_load_2d(sc + 256u * NT * c + 128u * NT, &p.xlo, x, tok, cb, pol_x);
+                        }
                     }
                 }
             }
@@ -230,47 +234,52 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
         }
     } else if (warp == 1) {
         // -------------------------------------------------------------- MMA
+        // Per half super-block h (chunks 2h, 2h+1, sub-blocks 4h .. 4h+3):
+        // wait for its accumulator half, activation stage and A slot, issue
+        // the first K step of the four sub-blocks, then the second, and
+        // commit each ring once.  Every tcgen05 instruction costs tens of
+        // cycles to issue, so the kernel issues as few as it can.
         const uint32_t idesc1 = umma_idesc(N1), idesc2 = umma_idesc(16);
-        Ring rr, cr, ar, br;
+        Ring rr, cr, ar;
+        int ksb = 0;  // super-blocks done: the parity of the accumulator halves
         bool ok = true;
         while (sg.next(p, s)) {
-            for (int sb = s.sb0; sb < s.sb1; sb++, rr.next(p.nr), br.next(p.nb)) {
-                const int b = br.i;
-                // buffer b is free once the epilogue has read its previous super-block
-                if (ok && br.u > 0 && !wait_err(accempty0 + 8 * b, (br.u - 1) & 1, p.err)) ok = false;
-                ok = __all_sync(0xffffffffu, ok);
-                tmem_fence_after();
-                const uint32_t bcol = tmem + (uint32_t)b * p.buf_cols;
-                for (int cq = 0; cq < 4; cq++, cr.next(p.nc), ar.next(p.na)) {
+            for (int sb = s.sb0; sb < s.sb1; sb++, rr.next(p.nr), ksb++) {
+                for (int h = 0; h < 2; h++, cr.next(p.nc), ar.next(p.na)) {
+                    // half h of the accumulators is free once the epilogue has read it
+                    if (ok && ksb > 0 && !wait_err(accempty0 + 8 * h, (ksb - 1) & 1, p.err)) ok = false;
                     if (ok && !wait_err(cfull0 + 8 * cr.i, cr.u & 1, p.err)) ok = false;
                     if (ok && !wait_err(aready0 + 8 * ar.i, ar.u & 1, p.err)) ok = false;
                     ok = __all_sync(0xffffffffu, ok);
                     tmem_fence_after();
                     const uint32_t sc = ringc + (uint32_t)cr.i * p.c_bytes;
-                    const uint32_t acol = tmem + p.acol0 + 32u * (uint32_t)ar.i;
+                    const uint32_t acol = tmem + p.acol0 + 64u * (uint32_t)ar.i;
                     if (elect_one()) {
                         if (ok) {
-                            // K steps 0, 2 start sub-blocks 2cq, 2cq+1; 1, 3 finish them
 #pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                const int kk = (i >> 1) | ((i & 1) << 1);
-                                const uint32_t d = bcol + (uint32_t)(2 * cq + (kk >> 1)) * N1;
-                                umma_f16_ts(d, acol + 8u * kk, desc_sw128(sc + 32u * kk), idesc1, (uint32_t)(kk & 1));
+                            for (int k2 = 0; k2 < 2; k2++)
+#pragma unroll
+                                for (int i = 0; i < 4; i++) {
+                                    // sub-block 4h + i: chunk c = i / 2, nibble half i % 2
+                                    const int c = i >> 1, nh = i & 1, kk = 2 * nh + k2;
+                                    const uint32_t d = tmem + (uint32_t)(4 * h + i) * N1;
+                                    umma_f16_ts(d, acol + 32u * (uint32_t)c + 8u * kk,
+                                                desc_sw128(sc + 256u * NT * (uint32_t)c + 32u * kk), idesc1,
+                                                (uint32_t)k2);
+                                }
+                            if (h == 1) {
+                                const uint32_t st = ringr + (uint32_t)rr.i * p.r_bytes;
+                                umma_f16(tmem + kChains * N1, desc_sw32(st + p.r_a2), desc_sw32(st + p.r_b2), idesc2,
+                                         0u);
                             }
                         }
                         umma_commit(cempty0 + 8 * cr.i);
                         umma_commit(aempty0 + 8 * ar.i);
+                        if (h == 1) umma_commit(rempty0 + 8 * rr.i);
+                        umma_commit(accfull0 + 8 * h);
                     }
                     __syncwarp();
                 }
-                const uint32_t st = ringr + (uint32_t)rr.i * p.r_bytes;
-                if (elect_one()) {
-                    if (ok)
-                        umma_f16(bcol + kChains * N1, desc_sw32(st + p.r_a2), desc_sw32(st + p.r_b2), idesc2, 0u);
-                    umma_commit(rempty0 + 8 * rr.i);
-                    umma_commit(accfull0 + 8 * b);
-                }
-                __syncwarp();
             }
         }
         if (!ok && lane == 0 && p.err) atomicExch(p.err, 1);
@@ -280,11 +289,11 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
         // of a lane quarter take alternate chunks (par 0: chunks 0, 2 of every
         // super-block, par 1: chunks 1, 3), both nibbles of each (32
         // columns), and store both chunks before waiting for the stores.
-        const int q = warp & 3, par = (warp - kExpWarp0) >> 2;
+        const int q = warp & 3, par = (warp - kExpWarp0) >> 2;  // par: chunk 2h + par of half h
         const int r = 32 * q + lane;
         const uint32_t swz = (uint32_t)(r & 7);
         const uint32_t lane_a = tmem + ((uint32_t)(32 * q) << 16) + p.acol0;
-        Ring rr, ar;  // ar: the A slot of the super-block's chunk 0
+        Ring rr, ar;  // ar: the A slot of the current half super-block
         bool ok = true;
         while (sg.next(p, s)) {
             for (int sb = s.sb0; sb < s.sb1; sb++, rr.next(p.nr)) {
@@ -307,23 +316,14 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
                     // generic-proxy writes become visible to the tensor core
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
-                Ring a = ar;
-                if (par) a.next(p.na);
-                int slot[2];
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    if (c) {
-                        a.next(p.na);
-                        a.next(p.na);
-                    }
-                    slot[c] = a.i;
-                    if (ok && a.u > 0 && !wait_err(aempty0 + 8 * a.i, (a.u - 1) & 1, p.err)) ok = false;
+                for (int h = 0; h < 2; h++, ar.next(p.na)) {
+                    if (ok && ar.u > 0 && !wait_err(aempty0 + 8 * ar.i, (ar.u - 1) & 1, p.err)) ok = false;
                     ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-wide
                     tmem_fence_after();
                     if (ok) {
                         // the chunk's 32 quant bytes of row r: 16-byte chunks
                         // 2cq, 2cq+1 of the row's 128-byte-swizzled line
-                        const int cq = par + 2 * c;
+                        const int cq = 2 * h + par;
                         const uint8_t* qrow = rst + r * 128;
                         const uint4 qa = *reinterpret_cast<const uint4*>(qrow + (((2 * cq) ^ swz) << 4));
                         const uint4 qb = *reinterpret_cast<const uint4*>(qrow + (((2 * cq + 1) ^ swz) << 4));
@@ -340,19 +340,14 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
                             o[16 + 2 * i] = qw[i] & 0x00F000F0u;
                             o[17 + 2 * i] = v & 0x00F000F0u;
                         }
-                        // TMEM column c of the slot holds K positions 2c, 2c+1
-                        tmem_st32u(lane_a + 32u * (uint32_t)a.i, o);
+                        // TMEM column c of the chunk holds K positions 2c, 2c+1
+                        tmem_st32u(lane_a + 64u * (uint32_t)ar.i + 32u * (uint32_t)par, o);
+                        tmem_wait_st();
                     }
+                    tmem_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(aready0 + 8 * ar.i);
                 }
-                if (ok) tmem_wait_st();
-                tmem_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(aready0 + 8 * slot[0]);
-                    mbar_arrive(aready0 + 8 * slot[1]);
-                }
-#pragma unroll
-                for (int c = 0; c < 4; c++) ar.next(p.na);
             }
         }
         if (!ok && lane == 0 && p.err) atomicExch(p.err, 1);
@@ -364,7 +359,8 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
         const int q = warp & 3, half = (warp - kEpiWarp0) >> 2;
         const int r = 32 * q + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-        Ring br, rr;
+        Ring rr;
+        int ksb = 0;  // super-blocks done: the parity of the accumulator halves
         bool ok = true;
         while (sg.next(p, s)) {
             const int j = job_of(p, s.t);
@@ -374,50 +370,56 @@ __global__ void __launch_bounds__(kThreadsSK, 1) mm_skinny_kernel(const __grid_c
             float tot[NT];
 #pragma unroll
             for (int i = 0; i < NT; i++) tot[i] = 0.0f;
-            for (int sb = s.sb0; sb < s.sb1; sb++, br.next(p.nb), rr.next(p.nr)) {
-                const int b = br.i;
-                if (ok && !wait_err(accfull0 + 8 * b, br.u & 1, p.err)) ok = false;
-                ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-wide
-                tmem_fence_after();
+            for (int sb = s.sb0; sb < s.sb1; sb++, rr.next(p.nr), ksb++) {
                 // sub-block scales: chain c = sub-block c, its coefficient
-                // d 2^24 sc_c (1/16 more for odd c: high nibbles are 16 q)
-                const uint4 hd = *reinterpret_cast<const uint4*>(ringr_p + (size_t)rr.i * p.r_bytes + p.r_hdr + r * 16);
-                const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hd.x));
-                const float fd = dm.x * kSub, fm = -dm.y * kSub;
-                // chains 4 half .. 4 half + 3
-                float kc[4];
+                // d 2^24 sc_c (1/16 more for odd c: high nibbles are 16 q);
+                // this warp reads chains 2e, 2e + 1 and 4 + 2e, 5 + 2e
+                float kc[4], fm = 0.0f;
+                for (int h = 0; h < 2; h++) {
+                    if (ok && !wait_err(accfull0 + 8 * h, ksb & 1, p.err)) ok = false;
+                    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-wide
+                    tmem_fence_after();
+                    if (h == 0) {
+                        const uint4 hd =
+                            *reinterpret_cast<const uint4*>(ringr_p + (size_t)rr.i * p.r_bytes + p.r_hdr + r * 16);
+                        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hd.x));
+                        const float fd = dm.x * kSub;
+                        fm = -dm.y * kSub;
 #pragma unroll
-                for (int g = 0; g < 2; g++) {
-                    const uint32_t w = q4k_scales(q4k_scale_sel(2 * half + g), hd);
-                    kc[2 * g] = fd * (float)(w & 0xFFu);
-                    kc[2 * g + 1] = fd * 0.0625f * (float)((w >> 8) & 0xFFu);
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(rempty0 + 8 * rr.i);  // the header is read
-                const uint32_t bbase = lane_base + (uint32_t)b * p.buf_cols;
-                if (ok) {
-                        // one 32-column chain per load: 18 warps leave 96
-                        // registers per thread
+                        for (int g = 0; g < 2; g++) {
+                            const uint32_t w = q4k_scales(q4k_scale_sel(2 * g + half), hd);
+                            kc[2 * g] = fd * (float)(w & 0xFFu);
+                            kc[2 * g + 1] = fd * 0.0625f * (float)((w >> 8) & 0xFFu);
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(rempty0 + 8 * rr.i);  // the header is read
+                    }
+                    if (ok) {
+                        // one 32-column chain at a time (96 registers per
+                        // thread with 18 warps)
 #pragma unroll
-                        for (int c = 0; c < 4; c++) {
+                        for (int c = 0; c < 2; c++) {
                             uint32_t ua[32];
-                            tmem_ld32(bbase + (uint32_t)(4 * half + c) * N1, ua);
+                            tmem_ld32(lane_base + (uint32_t)(4 * h + 2 * half + c) * N1, ua);
                             tmem_wait_ld();
 #pragma unroll
                             for (int i = 0; i < 16; i++)
-                                tot[i] = fmaf(kc[c], __uint_as_float(ua[i]) + __uint_as_float(ua[16 + i]), tot[i]);
+                                tot[i] = fmaf(kc[2 * h + c], __uint_as_float(ua[i]) + __uint_as_float(ua[16 + i]), tot[i]);
                         }
-                        if (half == 0) {
+                        if (h == 1 && half == 0) {
                             uint32_t p2[16];
-                            tmem_ld16(bbase + kChains * N1, p2);
+                            tmem_ld16(lane_base + kChains * N1, p2);
                             tmem_wait_ld();
 #pragma unroll
                             for (int i = 0; i < 16; i++) tot[i] = fmaf(fm, __uint_as_float(p2[i]), tot[i]);
                         }
+                    }
+                    // this half of the accumulators is read: the next MMAs
+                    // may overwrite it
+                    tmem_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(accempty0 + 8 * h);
                 }
-                tmem_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(accempty0 + 8 * b);
             }
             // ---- end of the tile piece: add the halves (low + high), then
             // write y, or the piece and count it
@@ -545,7 +547,7 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
     p.buf_cols = (uint32_t)(kChains * 2 * nt + 16);
     p.nb = 1;
     p.acol0 = (uint32_t)p.nb * p.buf_cols;
-    p.na = std::min(kMaxA, (int)((512 - p.acol0) / 32));
+    p.na = std::min(kMaxA, (int)((512 - p.acol0) / 64));
     p.tmem_cols = 512;
     // R stage: quant 16 KB | headers 2 KB | B2 16 x 32 B | A2 4 KB; C stage:
     // x_hi, x_lo nt x 128 B each; every tile 1024-aligned
@@ -554,9 +556,9 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
     p.r_b2 = al(p.r_hdr + kRowsTC * 16);
     p.r_a2 = al(p.r_b2 + 16 * 32);
     p.r_bytes = al(p.r_a2 + kRowsTC * 32);
-    p.c_bytes = al(2 * 128u * (uint32_t)nt);
+    p.c_bytes = al(4 * 128u * (uint32_t)nt);
     p.ring_off = 1024 + al(kRowsTC * 4u * (uint32_t)nt);
-    p.nc = kMaxC;
+    p.nc = 4;
     const int avail = kSmemSK - 1024 - (int)p.ring_off - p.nc * (int)p.c_bytes;
     p.nr = std::min(kMaxR, avail / (int)p.r_bytes);
     if (p.nr < 2) return set_error(RQ_ERR_UNSUPPORTED, "skinny matmul: stages too large");
