@@ -56,6 +56,25 @@ Mem mem_kind(const void* p) {
                                                                                 : Mem::Host;
 }
 
+// The address a kernel on this device can use for p: p itself in device
+// memory, the mapped address of page-locked host memory (kernels then read
+// and write it over the bus), or NULL for pageable host memory.
+// *host tells whether p is host memory (page-locked or not).
+void* device_alias(const void* p, bool* host) {
+    cudaPointerAttributes a;
+    *host = true;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+        *host = false;
+        return const_cast<void*>(p);
+    }
+    if (a.type == cudaMemoryTypeHost && a.devicePointer) return a.devicePointer;
+    return nullptr;
+}
+
 bool valid_type(int t) {
     return t == RQ_Q4_0 || t == RQ_Q4_K || t == RQ_Q3_K || t == RQ_Q8_0 || t == RQ_Q6_K || t == RQ_Q5_K ||
            t == RQ_Q2_K;
@@ -381,7 +400,13 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
     if (M == 0) return RQ_OK;
     DeviceGuard g(ctx->device);
     cudaStream_t st = (cudaStream_t)stream;
-    const bool x_dev = mem_kind(x) == Mem::Device, y_dev = mem_kind(y) == Mem::Device;
+    // device or page-locked host buffers are used in place (the kernels read
+    // x and write y over the bus for the latter); pageable host buffers go
+    // through the workspace with copies
+    bool x_host = true, y_host = true;
+    float* const x_alias = static_cast<float*>(device_alias(x, &x_host));
+    float* const y_alias = static_cast<float*>(device_alias(y, &y_host));
+    const bool x_dev = x_alias != nullptr, y_dev = y_alias != nullptr;
     // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 9..16:
     // the split-K tcgen05 kernel, one pass over the weights; M = 4..8 and
     // 17..23: one mma.sync pass per 8 rows; M = 2, 3: the M=1 pipeline once
@@ -396,8 +421,8 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
     XQ xq;
     xq.planes = (int8_t*)ws;
     xq.stats = (float4*)(ws + (((size_t)M * 3 * w->in + 255) & ~(size_t)255));
-    float* xd = x_dev ? const_cast<float*>(x) : (float*)(ws + ((xq_sz + 255) & ~(size_t)255));
-    float* yd = y_dev ? y : (float*)((uint8_t*)xd + (x_dev ? 0 : ((x_sz + 255) & ~(size_t)255)));
+    float* xd = x_dev ? x_alias : (float*)(ws + ((xq_sz + 255) & ~(size_t)255));
+    float* yd = y_dev ? y_alias : (float*)((uint8_t*)xd + (x_dev ? 0 : ((x_sz + 255) & ~(size_t)255)));
     if (!y_dev && x_dev) yd = (float*)(ws + ((xq_sz + 255) & ~(size_t)255));
     if (!x_dev) {
         rc = cuda_error(cudaMemcpyAsync(xd, x, x_sz, cudaMemcpyHostToDevice, st), "x copy");
@@ -420,10 +445,9 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
         if (!rc) rc = launch_linear(w, xq, yd, M, ctx->sm_count, st);
     }
     if (rc) return rc;
-    if (!y_dev) {
-        rc = cuda_error(cudaMemcpyAsync(y, yd, y_sz, cudaMemcpyDeviceToHost, st), "y copy");
-        if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "rq_linear sync");
-    }
+    if (!y_dev) rc = cuda_error(cudaMemcpyAsync(y, yd, y_sz, cudaMemcpyDeviceToHost, st), "y copy");
+    // host buffers: y is complete and x no longer read when the call returns
+    if (!rc && (x_host || y_host)) rc = cuda_error(cudaStreamSynchronize(st), "rq_linear sync");
     return rc;
 }
 

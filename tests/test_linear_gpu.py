@@ -173,6 +173,31 @@ def test_device_pointers_and_streams(oracle, rq_ctx):
     assert rel_l2(_linear(w, x), ref) <= REL_L2_TOL   # host path
 
 
+@pytest.mark.parametrize("M", [1, 4, 12])
+def test_pinned_host_buffers(oracle, rq_ctx, M):
+    """Page-locked host x and y are used in place: the staging kernel reads x
+    and the matvec / matmul kernels write y over the bus (M = 1 pipeline,
+    M = 4 mma.sync, M = 12 split-K tcgen05); the call returns with y complete,
+    and a pageable y next to a page-locked x still works."""
+    import ctypes
+
+    import torch
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200._lib import check, lib
+    out, n_in = 520, 4096
+    _, blocks = make_weight(oracle, 12, out, n_in, seed=17 + M)
+    w = QWeight.upload(rq_ctx, 12, blocks, out, n_in)
+    x = np.random.default_rng(M).standard_normal((M, n_in)).astype(np.float32)
+    ref = oracle.matmul_ref(12, blocks, out, n_in, x, acc64=True)
+    xp = torch.from_numpy(x).pin_memory()
+    yp = torch.full((M, out), float("nan")).pin_memory()
+    check(lib().rq_linear(rq_ctx.handle, w.handle, xp.data_ptr(), yp.data_ptr(), M, None))
+    assert rel_l2(yp.numpy(), ref) <= REL_L2_TOL
+    ypage = np.full((M, out), np.nan, np.float32)
+    check(lib().rq_linear(rq_ctx.handle, w.handle, xp.data_ptr(), ypage.ctypes.data_as(ctypes.c_void_p), M, None))
+    assert np.array_equal(ypage.view(np.uint32), yp.numpy().view(np.uint32))
+
+
 def test_scaled_activations(oracle, rq_ctx):
     """Large and tiny activation scales, and a zero block: the fixed-point
     staging is per 32-element block, so scale must not matter."""
