@@ -3,13 +3,14 @@
 // pass over the weights.
 //
 // The kernel is built around the cost per weight, not per MMA, and around
-// one measured limit: a CTA issues a tcgen05.mma of 128 x N x 16 only every
-// ~60-100 cycles at small N, whatever the operand source (TMEM or shared
-// memory), the spacing of dependent MMAs or the number of issuing warps, so
-// the ~2048 weights per MMA cap the kernel near 20 weights per clock per SM
-// (~1.3 TB/s of Q4_K) at any M.  Below 9 rows the mma.sync kernel, whose
-// 8-row tiles cost the same, is faster; from 9 to 16 rows this one is (one
-// pass instead of two).
+// one measured limit: the single warp that issues the MMAs pays ~30-130
+// cycles for every tcgen05 instruction (MMA or commit) and every mbarrier
+// wait, whatever the operand source (TMEM or shared memory), the spacing of
+// dependent MMAs or the number of issuing warps, so a 128-row super-block
+// (17 MMAs of 2048 weights) costs ~2100 cycles, ~1.7 TB/s of Q4_K at any M.
+// The kernel therefore waits and commits once per half super-block.  Below
+// 9 rows the mma.sync kernel, whose 8-row tiles cost the same, is faster;
+// from 9 to 16 rows this one is (one pass instead of two).
 //   * The 4-bit quants enter the MMA as they are: a nibble's bit pattern
 //     in a 16-bit lane is the f16 subnormal q * 2^-24, a high nibble masked
 //     in place is 16 q * 2^-24; one shift and four masks turn a word of 8
@@ -30,18 +31,19 @@
 //
 // Warp roles (18 warps, one CTA per SM):
 //   0      TMA producer: ring R (one super-block of 128 rows: quant bytes,
-//          headers, the block-sum operand B2), ring C (one 64-element chunk
-//          of x_hi / x_lo: B1).
+//          headers, the block-sum operand B2), ring C (two 64-element chunks
+//          of x_hi / x_lo: B1, half a super-block).
 //   1      TMEM allocation, all MMAs (one elected lane), commits.
 //   2..9   expand: warp w writes TMEM lanes 32 (w % 4) .. +31 (rows); the
-//          two warps of a lane quarter take alternate 64-element chunks
-//          (both nibbles: the chunk's 32-column A slot); the first also
-//          writes A2 (the m values).
-//   10..17 epilogue: two warps per lane quarter, each reads 4 of the 8
-//          sub-block accumulators; running totals stay in registers and the
-//          two halves are added once per tile piece.
-// TMEM columns: one buffer of [8 chains x 32 | P2 16], then na A slots of
-// 32 (64 f16 of K per row).  Every mbarrier wait is bounded; on expiry
+//          two warps of a lane quarter take the two 64-element chunks of a
+//          half super-block (both nibbles: 32 of the half's 64 A-slot
+//          columns each); the first also writes A2 (the m values).
+//   10..17 epilogue: two warps per lane quarter, each reads 2 of the 4
+//          sub-block accumulators of each half and releases the half as soon
+//          as it has read it; running totals stay in registers and the two
+//          warps' totals are added once per tile piece.
+// TMEM columns: [8 chains x 32 | P2 16] (two halves of 4 chains), then na A
+// slots of 64 (128 f16 of K per row).  Every mbarrier wait is bounded; on expiry
 // the CTA records the error and skips work, and TMEM is always released.
 
 #include <string.h>
@@ -496,7 +498,7 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
     const int64_t in = jobs[0].w->in, nblk = jobs[0].w->nblk;
     SKParams p;
     memset(&p, 0, sizeof p);
-    int tiles = 0, mmax = 1;
+    int tiles = 0;
     for (int j = 0; j < njobs; j++) {
         const rq_weight* w = jobs[j].w;
         if (w->type != RQ_Q4_K || w->in != in)
@@ -519,10 +521,8 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
         t.M = jobs[j].M;
         t.t0 = tiles;
         tiles += (int)((w->out + kRowsTC - 1) / kRowsTC);
-        mmax = std::max(mmax, jobs[j].M);
     }
     const int nt = kNT;
-    (void)mmax;
     int rc = encode(&p.xhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh.v, (uint64_t)in, (uint64_t)rows, (uint64_t)(4 * in),
                     64, (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B, "activations (hi)");
     if (!rc)
@@ -543,14 +543,16 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
     p.err = err;
     p.njobs = njobs;
     p.nblk = (int)nblk;
-    // TMEM: nb buffers of [8 chains x 2 nt | P2 16] and na A slots of 32
+    // TMEM: [8 chains x 2 nt | P2 16] and na A slots of 64 (one per half
+    // super-block)
     p.buf_cols = (uint32_t)(kChains * 2 * nt + 16);
     p.nb = 1;
     p.acol0 = (uint32_t)p.nb * p.buf_cols;
     p.na = std::min(kMaxA, (int)((512 - p.acol0) / 64));
     p.tmem_cols = 512;
-    // R stage: quant 16 KB | headers 2 KB | B2 16 x 32 B | A2 4 KB; C stage:
-    // x_hi, x_lo nt x 128 B each; every tile 1024-aligned
+    // R stage: quant 16 KB | headers 2 KB | B2 16 x 32 B | A2 4 KB; C stage
+    // (half a super-block): two chunks of x_hi, x_lo nt x 128 B each; every
+    // tile 1024-aligned
     auto al = [](uint32_t v) { return (v + 1023u) & ~1023u; };
     p.r_hdr = kRowsTC * 128;
     p.r_b2 = al(p.r_hdr + kRowsTC * 16);
