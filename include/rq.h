@@ -14,9 +14,12 @@
  *     Q5_K = 176 and Q2_K = 84 bytes per 256), row-major [out][in/block].
  *     The library copies them to the GPU and owns the device copy.
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
- *   - Activation pointers (x, y) may be host or device memory; host pointers
- *     are staged through device memory and the call returns with y filled.
- *     Device pointers: the call is asynchronous on `stream`.
+ *   - Activation pointers (x, y) may be host or device memory.  Page-locked
+ *     host memory (cudaHostAlloc / cudaHostRegister) is used in place: the
+ *     kernels read x and write y over the bus.  Pageable host memory is
+ *     staged through device memory.  With any host pointer the call returns
+ *     with y filled and x no longer read; with device pointers only it is
+ *     asynchronous on `stream`.
  *   - One rq_ctx per device; calls on one ctx are serialised by the caller
  *     (the reference's single-writer generate loop,
  *     src/streaming_quantized.rs:345-351).  Weight handles are read-only
