@@ -466,14 +466,18 @@ int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float
     return RQ_OK;
 }
 
-// RQ_TP_FUSED=0 in the environment keeps the decode all-reduce a separate
-// kernel (the fused and separate forms give the same bits)
-bool tp_fused_enabled() {
-    static const bool on = [] {
+// Whether the decode all-reduce runs inside the row-parallel matvec over
+// `world` ranks (the fused and separate forms give the same bits).  By
+// default at two ranks, the configuration it has been validated on;
+// RQ_TP_FUSED=1 in the environment enables it at any world size, =0 never.
+bool tp_fused_enabled(int world) {
+    static const int mode = [] {
         const char* e = getenv("RQ_TP_FUSED");
-        return !(e && strcmp(e, "0") == 0);
+        if (e && strcmp(e, "0") == 0) return 0;
+        if (e && strcmp(e, "1") == 0) return 1;
+        return 2;  // default
     }();
-    return on;
+    return mode == 1 || (mode == 2 && world == 2);
 }
 
 // x = x + x_in W^T for a row-parallel weight (o_proj, down_proj).  One rank:
@@ -490,7 +494,7 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
     }
     const rq_weight* w1[1] = {w};
     P2PArgs ar;
-    if (T == 1 && tp_fused_enabled() && pipe_supported(w) && tp_p2p_args(m->ctx, &ar)) {
+    if (T == 1 && tp_fused_enabled(m->W) && pipe_supported(w) && tp_p2p_args(m->ctx, &ar)) {
         const XQ xq = m->xq;
         float* y = m->x;
         const float* add = m->R == 0 ? m->x : nullptr;
