@@ -5,16 +5,25 @@ A step is one pass of the decode hot path over one 70B layer's seven
 quantized linears (q, k, v, o: 8192->8192/1024/1024/8192; gate, up:
 8192->28672; down: 28672->8192) through librq's public entry points with
 device-resident activations, grouped as a decoder issues them: q/k/v in one
-rq_linear_batch call on their shared x, o, gate/up in one batch call, down.  Weights are random
-N(0, 0.02) f32 quantized to Q4_K on the device; x ~ N(0, 1).  Steps rotate
-over 4 distinct layer copies (1.93 GB > 126 MB L2), so every weight byte
-comes from HBM.  value = algorithmic bytes (weights + x + y) per step / time.
+rq_linear_batch call on their shared x, o, gate/up in one batch call, down.
+Weights are random N(0, 0.02) f32 quantized to Q4_K on the device; x ~
+N(0, 1).  Steps rotate over 4 distinct layer copies (1.93 GB > 126 MB L2), so
+every weight byte comes from HBM.  value = algorithmic bytes (weights + x +
+y) of the full layer per step / time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-With --gpus N > 1 (under torchrun) every rank runs the same workload on its
-own GPU (independent replicas, weak scaling): the layer matvecs have no
-cross-GPU exchange when each GPU decodes its own stream.
+With --gpus N > 1 (under torchrun) the same layer runs tensor-parallel over
+the N GPUs (strong scaling): q/k/v/gate/up are split by output rows, o/down
+by input columns, and o/down end in an all-reduce over NVLink that runs
+inside the matvec kernel (rq_linear_allreduce).  value = the full layer's
+bytes / the slowest rank's time per step.  The line also carries the
+tensor-parallel 80-layer 70B decode (config 5) and the expert-parallel
+Mixtral layer at that N.
+
+Beside each GPU figure at N = 1 sits the reference's CPU path, restated in
+the oracle and timed on the host's cores (`cpu_baseline`), and the roofline
+of the kernel that dominates it (`roofline`).
 """
 from __future__ import annotations
 
@@ -36,8 +45,11 @@ sys.path.insert(0, ROOT)
 SHAPES = [("q_proj", 8192, 8192), ("k_proj", 8192, 1024), ("v_proj", 8192, 1024),
           ("o_proj", 8192, 8192), ("gate_proj", 8192, 28672), ("up_proj", 8192, 28672),
           ("down_proj", 28672, 8192)]
-Q4_K = 12
+SPLIT = ("col", "col", "col", "row", "col", "col", "row")  # tensor-parallel split per linear
+Q4_K, Q4_0, Q3_K = 12, 2, 11
 Q4K_BYTES = lambda n_in, n_out: n_out * (n_in // 256) * 144  # noqa: E731
+Q3K_BYTES = lambda n_in, n_out: n_out * (n_in // 256) * 110  # noqa: E731
+Q40_BYTES = lambda n_in, n_out: n_out * (n_in // 32) * 18  # noqa: E731
 N_COPIES = 4
 METRIC = "Q4_K matvec HBM GB/s at Llama-2-70B layer shapes (M=1)"
 WORKLOAD = ("Q4_K matvec M=1 over one Llama-2-70B layer's 7 linears "
@@ -48,13 +60,42 @@ def step_bytes() -> int:
     return sum(Q4K_BYTES(i, o) + 4 * (i + o) for _, i, o in SHAPES)
 
 
+def layer_weight_bytes() -> int:
+    return sum(Q4K_BYTES(i, o) for _, i, o in SHAPES)
+
+
 def peaks() -> dict:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def traffic(name: str):
+    """Per-launch DRAM bytes of an ncu capture summarised under profiles/."""
+    p = os.path.join(ROOT, "profiles", f"traffic_{name}.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get("bytes_per_launch")
+    return None
+
+
+def roofline_hbm(nbytes: float, ms: float, pk: dict, kernel: str, traffic_name: str | None = None) -> dict:
+    a = nbytes / (ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": round(a, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(a / pk["hbm_gbs"], 4), "traffic": traffic(traffic_name) if traffic_name else None,
+            "kernel": kernel, "peak_source": pk["source"]}
+
+
+def roofline_tensor(flops: float, ms: float, pk: dict, kernel: str, traffic_name: str | None = None) -> dict:
+    a = flops / (ms / 1e3) / 1e12
+    return {"bound": "tensor", "achieved": round(a, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(a / pk["bf16_tflops"], 4), "traffic": traffic(traffic_name) if traffic_name else None,
+            "kernel": kernel, "peak_source": pk["source"] + " (bf16 dense, burst)"}
 
 
 class ClockSampler:
@@ -122,27 +163,169 @@ def dist_env():
     return world, rank, local
 
 
-def cpu_baseline(blocks: dict, seconds: float = 6.0) -> dict:
-    """The oracle's threaded CPU restatement over the same seven shapes
-    (one layer), all host cores; bounded to ~`seconds` of work."""
+def nthreads_host() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_desc() -> str:
+    """Host CPU model and NUMA layout, for the baselines' record."""
+    model, nodes = "unknown", None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except Exception:
+        pass
+    try:
+        nodes = len([d for d in os.listdir("/sys/devices/system/node") if d.startswith("node")])
+    except Exception:
+        pass
+    return f"{model}; {nthreads_host()} usable threads; {nodes} NUMA node(s); threads not pinned"
+
+
+def _timed_loop(fn, seconds: float, max_iters: int = 1000, warm: bool = True) -> tuple[float, int]:
+    if warm:
+        fn()  # page faults, thread start-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= max_iters:
+            return el / n, n
+
+
+def cpu_layer_q4k(blocks: dict, seconds: float = 6.0) -> dict:
+    """Config 2 on the CPU: the oracle's threaded restatement of the
+    reference's path (q4_kernel.rs:207-243 chunking over a dequant-fused f32
+    dot) over the seven shapes of one layer, all host cores."""
     from oracle import oracle as O
-    nthreads = os.cpu_count() or 1
+    nt = nthreads_host()
     rng = np.random.default_rng(1)
     xs = {n: rng.standard_normal((1, i)).astype(np.float32) for n, i, _ in SHAPES}
     ys = {n: np.empty((1, o), np.float32) for n, _, o in SHAPES}
-    O.lib()
-    passes, t0 = 0, time.perf_counter()
-    while True:
+
+    def one():
         for n, i, o in SHAPES:
-            O.linear_threaded(Q4_K, blocks[n], o, i, xs[n], nthreads=nthreads, y=ys[n])
-        passes += 1
-        el = time.perf_counter() - t0
-        if el >= seconds or passes >= 200:
-            break
-    gbs = step_bytes() * passes / el / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
-            "sample": f"{passes} passes over the 7 Q4_K layer shapes (one layer copy), "
-                      f"{el:.1f} s, oracle rqo_linear_threaded"}
+            O.linear_threaded(Q4_K, blocks[n], o, i, xs[n], nthreads=nt, y=ys[n])
+
+    t, n = _timed_loop(one, seconds, 200)
+    return {"value": round(step_bytes() / t / 1e9, 3), "unit": "GB/s", "cores": nt, "kind": "port",
+            "sample": f"{n} passes over the 7 Q4_K layer shapes (one layer copy), oracle rqo_linear_threaded "
+                      f"(dequant-fused f32, q4_kernel.rs:207-243 chunking); {cpu_desc()}"}
+
+
+def cpu_q4_0(blocks: np.ndarray, seconds: float = 2.0) -> dict:
+    """Config 1 on the CPU: ParallelQ4Linear::forward (q4_kernel.rs:183-256)
+    with the AVX2-order dot (:300-360), restated in the oracle."""
+    from oracle import oracle as O
+    nt = nthreads_host()
+    x = np.random.default_rng(2).standard_normal((1, 4096)).astype(np.float32)
+    y = np.empty((1, 4096), np.float32)
+    t, n = _timed_loop(lambda: O.linear_threaded(Q4_0, blocks, 4096, 4096, x, nthreads=nt, y=y), seconds)
+    nbytes = Q40_BYTES(4096, 4096) + 4 * (4096 + 4096)
+    return {"value": round(nbytes / t / 1e9, 3), "unit": "GB/s", "cores": nt, "kind": "port",
+            "sample": f"{n} calls of the 4096x4096 Q4_0 forward, oracle rqo_linear_threaded "
+                      "(AVX2-order dot q4_kernel.rs:300-360, chunking :207-243)"}
+
+
+def cpu_small_m(blocks: dict, ms_list=None) -> dict:
+    """Config 3 on the CPU: the threaded restatement at each M over the
+    seven shapes; at large M over a leading fraction f = min(1, 8/M) of each
+    weight's rows, scaled by 1/f (the work per row is the same)."""
+    from oracle import oracle as O
+    nt = nthreads_host()
+    rng = np.random.default_rng(3)
+    out = {}
+    for M in (ms_list or SMALL_M):
+        f = min(1.0, 8.0 / M)
+        xs = {n: rng.standard_normal((M, i)).astype(np.float32) for n, i, _ in SHAPES}
+        rows = {n: max(1, int(o * f)) for n, _, o in SHAPES}
+
+        def one():
+            for n, i, o in SHAPES:
+                O.linear_threaded(Q4_K, blocks[n][:rows[n]], rows[n], i, xs[n], nthreads=nt)
+
+        t, _ = _timed_loop(one, 0.5, 3)
+        frac = sum(rows[n] * i for n, i, _ in SHAPES) / sum(o * i for _, i, o in SHAPES)
+        ms = t / frac * 1e3
+        nbytes = sum(Q4K_BYTES(i, o) + 4 * M * (i + o) for _, i, o in SHAPES)
+        out[str(M)] = {"ms_per_layer": round(ms, 2), "gbs": round(nbytes / (ms / 1e3) / 1e9, 3),
+                       "tok_per_s_layer_equiv": round(M / (ms / 1e3), 2)}
+    return {"value_by_M": out, "unit": "ms per layer", "cores": nt, "kind": "port",
+            "sample": "oracle rqo_linear_threaded over the 7 shapes at each M; rows scaled by "
+                      "f = min(1, 8/M) (M=512: 1/64 of each weight's rows), time / f"}
+
+
+def cpu_moe_f16(router: np.ndarray, xs: dict, seconds_cap: float = 30.0) -> dict:
+    """Config 4 on the CPU: the reference's own Mixtral layer
+    (SparseMoe::forward, streaming_mixtral.rs:280-319, with ParallelLinear
+    F16 gate and experts, parallel_linear.rs:191-295), restated in the
+    oracle.  One expert's F16 weights (352 MB, far above the host caches)
+    serve all eight experts; T = 512 is timed on its first 32 tokens."""
+    from oracle import oracle as O
+    nt = nthreads_host()
+    H, F, E = MIXTRAL["H"], MIXTRAL["F"], MIXTRAL["E"]
+    rng = np.random.default_rng(8)
+    w1 = (rng.standard_normal((F, H), dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+    w3 = (rng.standard_normal((F, H), dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+    w2 = (rng.standard_normal((H, F), dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+    res = {}
+    for T, x in xs.items():
+        xt = x if T < 512 else x[:32]
+        t, n = _timed_loop(lambda: O.moe_forward(xt, router, O.F16, [w1] * E, [w3] * E, [w2] * E, F,
+                                                 k=MIXTRAL["k"], nthreads=nt), 1.0, 5, warm=T == 1)
+        res[str(T)] = {"ms": round(t * 1e3 * (T / xt.shape[0]), 2),
+                       "tok_per_s": round(xt.shape[0] / t, 2),
+                       "sample": f"T={xt.shape[0]}" + (" of 512, ms scaled by 16" if T == 512 else "")}
+    return {"value_by_T": res, "unit": "tok/s", "cores": nt, "kind": "port",
+            "sample": "oracle rqo_moe_forward with F16 experts (ParallelLinear restatement, AVX2 lane order) and "
+                      "the F16 gate; 8 experts share one F16 weight set"}
+
+
+def cpu_decode(blocks7: list, head_f16: np.ndarray, n_layers: int, seconds: float = 3.0) -> dict:
+    """Config 5 on the CPU, extrapolated: one layer's seven Q4_K linears at
+    M = 1 (the threaded restatement) times the layer count, plus the F16
+    lm_head through the ParallelLinear restatement (the reference's
+    parallel-cpu F16 path).  Attention over <= 36 positions is negligible."""
+    from oracle import oracle as O
+    nt = nthreads_host()
+    rng = np.random.default_rng(9)
+    xs = [rng.standard_normal((1, i)).astype(np.float32) for _, i, _ in SHAPES]
+
+    def layer():
+        for k, (_, i, o) in enumerate(SHAPES):
+            O.linear_threaded(Q4_K, blocks7[k], o, i, xs[k], nthreads=nt)
+
+    tl, _ = _timed_loop(layer, seconds, 50)
+    xh = rng.standard_normal((1, head_f16.shape[1])).astype(np.float32)
+    th, _ = _timed_loop(lambda: O.parallel_linear_f16(head_f16, xh, nthreads=nt), 1.0, 20)
+    ms = (n_layers * tl + th) * 1e3
+    return {"value": round(1e3 / ms, 4), "unit": "tok/s", "cores": nt, "kind": "port",
+            "ms_per_token": round(ms, 1),
+            "sample": f"one 70B layer's 7 linears at M=1 ({tl * 1e3:.1f} ms, oracle rqo_linear_threaded) x "
+                      f"{n_layers} + the 32000x8192 F16 lm_head ({th * 1e3:.1f} ms, ParallelLinear "
+                      "restatement); extrapolated per token"}
+
+
+def headline_config(world: int) -> dict:
+    """The config of the headline line, shared by both arms (the reference
+    arm replaces only the l2 field)."""
+    par = "single GPU" if world == 1 else (
+        f"tensor parallel x{world}: q/k/v/gate/up split by rows, o/down by columns + all-reduce "
+        "(rq_linear_allreduce)")
+    return {"workload": WORKLOAD, "batch_m": 1, "weight_format": "GGML Q4_K",
+            "bytes_per_step": step_bytes(),
+            "launch_grouping": "q/k/v batched on their shared x, o, gate/up batched on their shared x, down "
+                               "(4 rq_linear[_batch|_allreduce] calls)",
+            "l2": f"inputs larger than L2: {N_COPIES} rotating layer copies, "
+                  f"{N_COPIES * step_bytes() / 1e9:.2f} GB per rotation vs 126 MB L2",
+            "parallelism": par}
 
 
 def host_blocks_for_cpu(seed: int = 1234) -> dict:
@@ -158,19 +341,22 @@ def host_blocks_for_cpu(seed: int = 1234) -> dict:
 
 
 def run_reference(args) -> None:
+    """The reference arm: the reference's CPU path for this workload (the
+    oracle's threaded restatement, all host cores), same metric and config.
+    Under torchrun only rank 0 runs."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
     blocks = host_blocks_for_cpu()
     from oracle import oracle as O
-    nthreads = os.cpu_count() or 1
+    nt = nthreads_host()
     rng = np.random.default_rng(1)
     xs = {n: rng.standard_normal((1, i)).astype(np.float32) for n, i, _ in SHAPES}
     ys = {n: np.empty((1, o), np.float32) for n, _, o in SHAPES}
 
     def one_step():
         for n, i, o in SHAPES:
-            O.linear_threaded(Q4_K, blocks[n], o, i, xs[n], nthreads=nthreads, y=ys[n])
+            O.linear_threaded(Q4_K, blocks[n], o, i, xs[n], nthreads=nt, y=ys[n])
 
     for _ in range(args.warmup):
         one_step()
@@ -180,16 +366,19 @@ def run_reference(args) -> None:
     el = time.perf_counter() - t0
     ms = el / args.steps * 1e3
     gbs = step_bytes() / (ms / 1e3) / 1e9
+    cfg = headline_config(world)
+    cfg["l2"] = "CPU path: one layer copy (481 MB, far above the host caches)"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak" if world == 1 else "strong", "vs_baseline": None,
+        "dtype": "f32",
         "data": "synthetic: W ~ N(0,0.02) f32 quantized to Q4_K (seeded), x ~ N(0,1)",
-        "config": {"workload": WORKLOAD, "l2": "CPU path", "batch_m": 1},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
+        "config": cfg,
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": nt, "kind": "port",
                          "sample": f"{args.steps} timed passes over the 7 shapes, "
                                    "oracle rqo_linear_threaded (dequant-fused f32, "
-                                   "q4_kernel.rs:207-243 chunking)"},
+                                   f"q4_kernel.rs:207-243 chunking); {cpu_desc()}"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
@@ -197,23 +386,19 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-Q4_0, Q3_K = 2, 11
-Q3K_BYTES = lambda n_in, n_out: n_out * (n_in // 256) * 110  # noqa: E731
-Q40_BYTES = lambda n_in, n_out: n_out * (n_in // 32) * 18  # noqa: E731
-
-
-def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
+def other_formats(L, ctx, stream, timed, capture, dev, g, pk, with_cpu: bool) -> dict:
     """Config 1: the 4096x4096 Q4_0 matvec (M=1) over 16 rotating copies
     (151 MB > L2); config 2's Q3_K sweep and the same sweep in Q8_0, Q6_K,
-    Q5_K and Q2_K:
-    the seven 70B shapes, each over 4 rotating copies.  GB/s = GGML weight
-    bytes + 4 (in + out) per call."""
+    Q5_K and Q2_K: the seven 70B shapes, each over 4 rotating copies.  GB/s =
+    GGML weight bytes + 4 (in + out) per call; each format's roofline is its
+    gate_proj call (the M=1 pipeline kernel)."""
     import torch
     from rustyllm_b200 import QWeight
     from rustyllm_b200._lib import check
     res = {}
+    host0 = {}
 
-    def sweep(qtype, shapes, copies, nbytes):
+    def sweep(qtype, shapes, copies, nbytes, keep_host=False):
         out = {}
         for name, i, o in shapes:
             ws = []
@@ -221,6 +406,8 @@ def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
                 wf = torch.randn(o, i, device=dev, generator=g) * 0.02
                 ws.append(QWeight.quantize(ctx, qtype, wf))
                 del wf
+            if keep_host:
+                host0[name] = ws[0].download()
             x = torch.randn(1, i, device=dev, generator=g)
             y = torch.empty(1, o, device=dev)
 
@@ -235,19 +422,32 @@ def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
                 gr.replay()
             reps = 10
             ms = timed(lambda r: gr.replay(), reps) / (reps * copies)
-            out[name] = round((nbytes(i, o) + 4 * (i + o)) / (ms / 1e3) / 1e9, 1)
+            out[name] = {"gbs": round((nbytes(i, o) + 4 * (i + o)) / (ms / 1e3) / 1e9, 1), "ms": ms}
             del gr
             for w in ws:
                 w.free()
         return out
 
-    res["q4_0_4096x4096_gbs"] = sweep(Q4_0, [("q4_0", 4096, 4096)], 16, Q40_BYTES)["q4_0"]
-    res["q3_k_per_shape_gbs"] = sweep(Q3_K, SHAPES, 4, Q3K_BYTES)
+    def fmt(qtype, name, nb):
+        r = sweep(qtype, SHAPES, 4, nb)
+        gate = r["gate_proj"]
+        res[f"{name}_per_shape_gbs"] = {k: v["gbs"] for k, v in r.items()}
+        res[f"{name}_roofline"] = roofline_hbm(nb(8192, 28672) + 4 * (8192 + 28672), gate["ms"], pk,
+                                               f"xquant + mv_pipe_kernel<{name.upper()}> gate_proj 8192->28672",
+                                               f"{name}_gate" if name == "q3_k" else None)
+
+    q40 = sweep(Q4_0, [("q4_0", 4096, 4096)], 16, Q40_BYTES, keep_host=with_cpu)["q4_0"]
+    res["q4_0_4096x4096_gbs"] = q40["gbs"]
+    res["q4_0_roofline"] = roofline_hbm(Q40_BYTES(4096, 4096) + 4 * 8192, q40["ms"], pk,
+                                        "xquant + mv_pipe_kernel<Q4_0> 4096x4096 (9.4 MB: launch-latency bound)")
+    if with_cpu:
+        res["q4_0_cpu_baseline"] = cpu_q4_0(host0["q4_0"])
+    fmt(Q3_K, "q3_k", Q3K_BYTES)
     # the other formats of the reference's quantizer (src/quantize.rs:29-37)
-    res["q8_0_per_shape_gbs"] = sweep(8, SHAPES, 4, lambda i, o: o * (i // 32) * 34)
-    res["q6_k_per_shape_gbs"] = sweep(14, SHAPES, 4, lambda i, o: o * (i // 256) * 210)
-    res["q5_k_per_shape_gbs"] = sweep(13, SHAPES, 4, lambda i, o: o * (i // 256) * 176)
-    res["q2_k_per_shape_gbs"] = sweep(10, SHAPES, 4, lambda i, o: o * (i // 256) * 84)
+    fmt(8, "q8_0", lambda i, o: o * (i // 32) * 34)
+    fmt(14, "q6_k", lambda i, o: o * (i // 256) * 210)
+    fmt(13, "q5_k", lambda i, o: o * (i // 256) * 176)
+    fmt(10, "q2_k", lambda i, o: o * (i // 256) * 84)
     res["note"] = ("single rq_linear calls (activation staging + M=1 pipeline), graph-replayed over "
                    "rotating weight copies larger than L2")
     return res
@@ -256,13 +456,13 @@ def other_formats(L, ctx, stream, timed, capture, dev, g) -> dict:
 SMALL_M = (2, 3, 4, 8, 16, 24, 128, 512)
 
 
-def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g) -> dict:
+def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g, pk, host_blocks) -> dict:
     """Small-M Q4_K matmul at the seven 70B layer shapes (M = 2, 3, 4, 8
     for speculative verify; 16, 24, 128, 512 for prefill): one rq_linear
     call per linear with [M, in] device activations, graph-replayed over the
     rotating layer copies.  GB/s = (Q4_K weight bytes + 4 M (in + out)) per
     layer / time, weight bytes counted once; TFLOP/s = 2 M sum(in * out) /
-    time."""
+    time.  Roofline per M: HBM up to M = 8, the tensor cores from 16."""
     import torch
     from rustyllm_b200._lib import check
     res = {}
@@ -286,14 +486,23 @@ def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g) -> dict:
         ms = timed(lambda r: gr.replay(), reps) / (reps * N_COPIES)
         nbytes = sum(Q4K_BYTES(i, o) + 4 * M * (i + o) for _, i, o in SHAPES)
         flops = 2 * M * sum(i * o for _, i, o in SHAPES)
-        res[str(M)] = {"ms_per_layer": round(ms, 4), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
-                       "tflops": round(flops / (ms / 1e3) / 1e12, 1),
-                       "tok_per_s_layer_equiv": round(M / (ms / 1e3), 1)}
+        kern = ("xquant + mv_pipe_kernel, one pass per row" if M <= 3 else
+                "xh_stage + mm_q4k_kernel (mma.sync)" if M <= 8 else
+                "xh_stage + mm_skinny_kernel (split-K tcgen05)" if M <= 16 else
+                "xh_stage + mm_q4k_kernel (mma.sync)" if M < 24 else "xh_stage + mm_tc_kernel (tcgen05)")
+        r = {"ms_per_layer": round(ms, 4), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+             "tflops": round(flops / (ms / 1e3) / 1e12, 1),
+             "tok_per_s_layer_equiv": round(M / (ms / 1e3), 1)}
+        r["roofline"] = (roofline_hbm(nbytes, ms, pk, kern + ", 7 linears of a layer") if M <= 8 else
+                         roofline_tensor(flops, ms, pk, kern + ", 7 linears of a layer"))
+        res[str(M)] = r
         del gr
     res["note"] = ("7 rq_linear calls per layer, 4 rotating layer copies. M <= 3: activation staging + "
-                   "one M=1 pipeline pass per row; M = 4..23: f16 hi/lo staging + the mma.sync "
-                   "tensor-core kernel, weights read once per 8-row tile; M >= 24: the tcgen05 kernel "
-                   "(exact sc*q weights in TMEM, 128 rows x up to 112 tokens per tile)")
+                   "one M=1 pipeline pass per row; M = 4..8, 17..23: f16 hi/lo staging + the mma.sync "
+                   "tensor-core kernel, weights read once per 8-row tile; M = 9..16: split-K tcgen05; "
+                   "M >= 24: the tiled tcgen05 kernel (exact sc*q weights in TMEM)")
+    if host_blocks is not None:
+        res["cpu_baseline"] = cpu_small_m(host_blocks)
     return res
 
 
@@ -301,7 +510,7 @@ MIXTRAL = dict(E=8, H=4096, F=14336, k=2)
 MOE_T = (1, 16, 512)
 
 
-def moe_sweep(device: int, seed: int = 4321) -> dict:
+def moe_sweep(device: int, pk, with_cpu: bool, seed: int = 4321) -> dict:
     """Mixtral-8x7B sparse-MoE layer: router [8, 4096] f32 N(0, 0.02), 8
     experts of Q4_K SwiGLU weights (4096 -> 14336 -> 4096) quantized on the
     device from N(0, 0.02), hidden states N(0, 1) for T = 1, 16, 512 tokens,
@@ -328,8 +537,10 @@ def moe_sweep(device: int, seed: int = 4321) -> dict:
     moe = SparseMoe(router, experts, top_k=k, device=device)
     mat_bytes = Q4K_BYTES(H, F)
     res = {}
+    xs_host = {}
     for T in MOE_T:
         x = torch.randn(T, H, device=dev, generator=g)
+        xs_host[T] = x.cpu().numpy()
         _, ids, _ = moe.forward_with_routing(x)
         touched = len(set(ids.reshape(-1).tolist()))
         for _ in range(2):
@@ -343,16 +554,25 @@ def moe_sweep(device: int, seed: int = 4321) -> dict:
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / reps
+        wb = touched * 3 * mat_bytes
         r = {"ms": round(ms, 4), "tok_per_s": round(T / (ms / 1e3), 1), "experts_touched": touched,
-             "weight_gbs": round(touched * 3 * mat_bytes / (ms / 1e3) / 1e9, 1)}
+             "weight_gbs": round(wb / (ms / 1e3) / 1e9, 1)}
+        flops = 2 * T * k * 3 * H * F
         if T == 512:
-            r["tflops"] = round(2 * T * k * 3 * H * F / (ms / 1e3) / 1e12, 2)
+            r["tflops"] = round(flops / (ms / 1e3) / 1e12, 2)
+            r["roofline"] = roofline_tensor(flops, ms, pk, "route + permute + expert tiles (mm_tc_kernel) + combine")
+        else:
+            r["roofline"] = roofline_hbm(wb + 4 * T * H * 2, ms, pk,
+                                         "route + permute + expert products (M=1 pipeline / mma.sync) + combine",
+                                         f"moe_t{T}")
         res[str(T)] = r
     res["config"] = "Mixtral-8x7B MoE layer: E=8, top-2, H=4096, F=14336, Q4_K experts, 1 GPU"
     moe.close()
     for trip in experts:
         for w in trip:
             w.free()
+    if with_cpu:
+        res["cpu_baseline"] = cpu_moe_f16(router, xs_host)
     return res
 
 
@@ -368,7 +588,7 @@ def moe_ep_sweep(device: int, pg, seed: int = 4321) -> dict:
     E, H, F, k = MIXTRAL["E"], MIXTRAL["H"], MIXTRAL["F"], MIXTRAL["k"]
     dev = torch.device("cuda", device)
     ctx = Context.get(device)
-    world, rank = tpmod.init_from_torch(ctx)
+    world, rank = tpmod.world_rank(ctx)
     g = torch.Generator(device=dev).manual_seed(seed)
     router = (torch.randn(E, H, device=dev, generator=g) * 0.02).cpu().numpy()
     experts = []
@@ -409,7 +629,6 @@ def moe_ep_sweep(device: int, pg, seed: int = 4321) -> dict:
         if trip:
             for w in trip:
                 w.free()
-    tpmod.finalize(ctx)
     torch.cuda.empty_cache()
     return res
 
@@ -419,27 +638,61 @@ LLAMA70B = dict(hidden=8192, intermediate=28672, n_heads=64, n_kv_heads=8, head_
                 rope_theta=10000.0)
 
 
-def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None,
-               n_layers: int | None = None) -> dict:
+def verify_decode(model, host: dict, cfg: dict, prompt: np.ndarray, toks: list) -> dict:
+    """Replay the decode through the oracle, one layer at a time (the
+    layer's Q4_K blocks downloaded from the device, run, dropped): the
+    prompt plus the first 15 generated tokens teacher-forced, so position p's
+    greedy token is the one decode step p emitted, with the arithmetic of
+    the incremental step.  Also the top-1 / top-2 logit margin per step."""
+    from oracle import oracle as O
+    t0 = time.perf_counter()
+    ref = O.OracleLlama(cfg, Q4_K)
+    ref.set_embedding(host["embed"])
+    ref.set_head(host["ln_f"], host["lm_head"])
+    seq = np.concatenate([prompt, np.array(toks[:-1], np.int32)]).astype(np.int32)
+    x = ref.embed(seq)
+    layer0 = None
+    for l in range(cfg["n_layers"]):
+        blocks = [w.download() for w in model.layer_weights(l)]
+        _, r1, r2 = host["layers"][l]
+        ref.stream_layer(l, blocks, r1, r2, x, 0)
+        if l == 0:
+            layer0 = blocks
+    logits, amax = ref.head(x)
+    p0 = len(prompt) - 1
+    want = amax[p0:].tolist()
+    top2 = np.sort(logits[p0:], axis=1)[:, -2:]
+    margins = (top2[:, 1] - top2[:, 0]).tolist()
+    return {"tokens_match_oracle": want == list(toks), "oracle_tokens": want,
+            "top1_top2_margins": [round(float(m), 5) for m in margins],
+            "min_margin": round(float(min(margins)), 5),
+            "logit_std": round(float(logits[p0:].std()), 4),
+            "verify_s": round(time.perf_counter() - t0, 1),
+            "verify_note": "oracle rqo_llama_layer per layer on the downloaded blocks, prompt + generated "
+                           "tokens teacher-forced (positions 19..34); logits of the F16 lm_head"}, layer0
+
+
+def decode_70b(device: int, pk, new_tokens: int = 16, prompt_len: int = 20, pg=None,
+               n_layers: int | None = None, verify: bool = True, with_cpu: bool = True) -> dict:
     """Config 5: the full 80-layer Llama-2-70B shape (Platypus2-70B), random
     N(0, 0.02) weights quantized to Q4_K and resident on the GPUs, F16
     embedding / lm_head; 20 seeded uniform prompt ids, greedy decode of 16
     tokens.  Decode steps are device-side and replayed from one CUDA graph.
     Under torch.distributed the model is tensor-parallel over the ranks
-    (column/row-parallel linears joined by NCCL all-reduces over NVLink)."""
+    (column/row-parallel linears joined by all-reduces over NVLink).  On one
+    GPU the tokens are checked against the oracle."""
     import torch
     from rustyllm_b200 import Context
+    from rustyllm_b200 import tp as tpmod
     from rustyllm_b200._lib import check, lib
     from rustyllm_b200.llama import random_model
     cfg = dict(LLAMA70B)
     if n_layers:
         cfg["n_layers"] = n_layers
-    world, rank = 1, 0
-    if pg is not None:
-        from rustyllm_b200 import tp as tpmod
-        world, rank = tpmod.init_from_torch(Context.get(device))
+    world, rank = tpmod.world_rank(Context.get(device))
+    verify = verify and world == 1
     t0 = time.perf_counter()
-    model, _ = random_model(cfg, Q4_K, seed=7070, device=device, tp=(world, rank))
+    model, host = random_model(cfg, Q4_K, seed=7070, device=device, tp=(world, rank), host_tensors=verify)
     build_s = time.perf_counter() - t0
     prompt = np.random.default_rng(20).integers(0, cfg["vocab"], size=prompt_len).astype(np.int32)
     L = lib()
@@ -465,12 +718,14 @@ def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None,
         e1.record(stream)
     stream.synchronize()
     gen_s = time.perf_counter() - t0
+    model.status()
     step_ms = e0.elapsed_time(e1) / (new_tokens - 1)
     if pg is not None:  # the slowest rank sets the pace
         t = torch.tensor([step_ms, gen_s, prefill_s], device=f"cuda:{device}")
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         step_ms, gen_s, prefill_s = (float(v) for v in t.tolist())
     toks, pos = model.tokens()
+    toks = toks[:new_tokens]
     # speculative-decoding verify forwards (forward_all over K+1 tokens at
     # the current position, cache rolled back after each): their cost next
     # to one decode step sets the acceptance a draft model must reach
@@ -492,30 +747,33 @@ def decode_70b(device: int, new_tokens: int = 16, prompt_len: int = 20, pg=None,
             ms = float(t.item())
         verify_ms[str(kp1)] = round(ms, 3)
     del g
+    tok_bytes = cfg["n_layers"] * layer_weight_bytes() + cfg["vocab"] * cfg["hidden"] * 2
+    out = {"config": f"Llama-2-70B shape, {cfg['n_layers']} layers, Q4_K resident, F16 lm_head, "
+                     f"tensor-parallel over {world} GPU(s)",
+           "tp": world,
+           "prompt_tokens": prompt_len, "new_tokens": new_tokens,
+           "decode_tok_s": round(1e3 / step_ms, 2), "ms_per_token": round(step_ms, 3),
+           "prefill_ms": round(prefill_s * 1e3, 2),
+           "generate_tok_s": round(new_tokens / gen_s, 2),
+           "weight_bytes_per_token": tok_bytes,
+           "decode_hbm_gbs": round(tok_bytes / (step_ms / 1e3) / 1e9, 1),
+           "roofline": roofline_hbm(tok_bytes / world, step_ms, pk,
+                                    "one graph-replayed decode step (per layer: rmsnorm staging, q/k/v, attention, "
+                                    "o, staging, gate/up, swiglu staging, down; lm_head + argmax); bytes per rank"),
+           "tokens": toks, "final_position": pos,
+           "verify_forward_ms": verify_ms,
+           "verify_note": "rq_llama_forward_all over K+1 tokens (host call incl. argmax copy), keys = K+1; a draft "
+                          "that gets accepted tokens cheaper than decode ms_per_token * (accepted+1) - verify pays "
+                          "off",
+           "model_build_s": round(build_s, 2)}
+    if verify:
+        chk, layer0 = verify_decode(model, host, cfg, prompt, toks)
+        out.update(chk)
+        if with_cpu:
+            out["cpu_baseline"] = cpu_decode(layer0, host["lm_head"], cfg["n_layers"])
     model.close()
-    if pg is not None:
-        from rustyllm_b200 import tp as tpmod
-        tpmod.finalize(Context.get(device))
     torch.cuda.empty_cache()
-    layer_bytes = sum(Q4K_BYTES(i, o) for (o, i) in [(8192, 8192), (1024, 8192), (1024, 8192),
-                                                        (8192, 8192), (28672, 8192), (28672, 8192),
-                                                        (8192, 28672)])
-    tok_bytes = cfg["n_layers"] * layer_bytes + cfg["vocab"] * cfg["hidden"] * 2
-    return {"config": f"Llama-2-70B shape, {cfg['n_layers']} layers, Q4_K resident, F16 lm_head, "
-                      f"tensor-parallel over {world} GPU(s)",
-            "tp": world,
-            "prompt_tokens": prompt_len, "new_tokens": new_tokens,
-            "decode_tok_s": round(1e3 / step_ms, 2), "ms_per_token": round(step_ms, 3),
-            "prefill_ms": round(prefill_s * 1e3, 2),
-            "generate_tok_s": round(new_tokens / gen_s, 2),
-            "weight_bytes_per_token": tok_bytes,
-            "decode_hbm_gbs": round(tok_bytes / (step_ms / 1e3) / 1e9, 1),
-            "tokens": toks[:new_tokens], "final_position": pos,
-            "verify_forward_ms": verify_ms,
-            "verify_note": "rq_llama_forward_all over K+1 tokens (host call incl. argmax copy), "
-                           "keys = K+1; a draft that gets accepted tokens cheaper than "
-                           "decode ms_per_token * (accepted+1) - verify pays off",
-            "model_build_s": round(build_s, 2)}
+    return out
 
 
 def run_gpu(args) -> None:
@@ -526,42 +784,50 @@ def run_gpu(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     pg = None
+    from rustyllm_b200 import Context, QWeight
+    from rustyllm_b200 import tp as tpmod
+    from rustyllm_b200._lib import check, lib
+    L = lib()
+    ctx = Context.get(local)
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = dist
+        tpmod.init_from_torch(ctx)
+    pk = peaks()
     if args.only_decode:
-        dec = decode_70b(local, pg=pg, n_layers=args.decode_layers)
+        dec = decode_70b(local, pk, pg=pg, n_layers=args.decode_layers, verify=not args.no_verify,
+                         with_cpu=False)
         if rank == 0:
             print(json.dumps({"metric": "70B Q4_K greedy decode tok/s", "value": dec["decode_tok_s"],
                               "unit": "tok/s", "n_gpus": world, "decode_70b": dec}), flush=True)
         if pg is not None:
             pg.barrier()
+            tpmod.finalize(ctx)
             pg.destroy_process_group()
         return
-    from rustyllm_b200 import Context, QWeight
-    from rustyllm_b200._lib import check, lib
-    L = lib()
-    ctx = Context.get(local)
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    # every rank draws the same full tensors and keeps its shard (the whole
+    # layer at one GPU)
+    from rustyllm_b200.tp import shard
+    g = torch.Generator(device=dev).manual_seed(1234)
     weights = []  # [copy][shape] -> QWeight
     for c in range(N_COPIES):
         layer = []
-        for n, i, o in SHAPES:
+        for k, (n, i, o) in enumerate(SHAPES):
             wf = torch.randn(o, i, device=dev, generator=g) * 0.02
-            layer.append(QWeight.quantize(ctx, Q4_K, wf))
+            layer.append(QWeight.quantize(ctx, Q4_K, shard(SPLIT[k], wf, world, rank).contiguous()))
             del wf
         weights.append(layer)
     torch.cuda.synchronize()
-    # activations: q/k/v share one x, gate/up share one x (as QAttn / QMlp do)
+    # activations: q/k/v share one x, gate/up share one x (as QAttn / QMlp do);
+    # o and down take this rank's slice of their input
     x_attn = torch.randn(1, 8192, device=dev, generator=g)
-    x_o = torch.randn(1, 8192, device=dev, generator=g)
+    x_o = torch.randn(1, 8192 // world, device=dev, generator=g)
     x_mlp = torch.randn(1, 8192, device=dev, generator=g)
-    x_down = torch.randn(1, 28672, device=dev, generator=g)
+    x_down = torch.randn(1, 28672 // world, device=dev, generator=g)
     xs = [x_attn, x_attn, x_attn, x_o, x_mlp, x_mlp, x_down]
-    ys = [torch.empty(1, o, device=dev) for _, _, o in SHAPES]
+    ys = [torch.empty(1, w.out, device=dev) for w in weights[0]]
     stream = torch.cuda.Stream(device=dev)
     arr = lambda vals: (ctypes.c_void_p * len(vals))(*vals)  # noqa: E731
     groups = [(0, 1, 2), (3,), (4, 5), (6,)]  # q/k/v batched, o, gate/up batched, down
@@ -569,8 +835,12 @@ def run_gpu(args) -> None:
     def launch_group(c, grp, st):
         if len(grp) == 1:
             k = grp[0]
-            check(L.rq_linear(ctx.handle, weights[c][k].handle, xs[k].data_ptr(),
-                              ys[k].data_ptr(), 1, st))
+            if world > 1 and SPLIT[k] == "row":
+                check(L.rq_linear_allreduce(ctx.handle, weights[c][k].handle, xs[k].data_ptr(),
+                                            ys[k].data_ptr(), 1, st))
+            else:
+                check(L.rq_linear(ctx.handle, weights[c][k].handle, xs[k].data_ptr(),
+                                  ys[k].data_ptr(), 1, st))
         else:
             check(L.rq_linear_batch(ctx.handle, len(grp),
                                     arr([weights[c][k].handle.value for k in grp]),
@@ -622,113 +892,107 @@ def run_gpu(args) -> None:
         if pg is not None:
             pg.barrier()
 
+    def max_over_ranks(v: float) -> float:
+        if pg is None:
+            return v
+        t = torch.tensor([v], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
     clocks = ClockSampler(local)
     barrier()
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
     ms_total = timed(lambda s: graphs[s % N_COPIES].replay(), args.steps)
+    clk = clocks.stop()
     reps = max(10, args.steps // 4)
-    dom_ms = timed(lambda r: dom.replay(), reps) / (reps * N_COPIES)
+    barrier()
+    dom_ms = max_over_ranks(timed(lambda r: dom.replay(), reps) / (reps * N_COPIES))
     per_shape = {}
     for k, (n, i, o) in enumerate(SHAPES):
-        t = timed(lambda r, k=k: shape_graphs[k].replay(), reps) / (reps * N_COPIES)
-        per_shape[n] = round((Q4K_BYTES(i, o) + 4 * (i + o)) / (t / 1e3) / 1e9, 1)
-    small_m = None
-    if not args.no_small_m:
-        small_m = small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g)
-    formats = None
-    if not args.no_small_m:
-        formats = other_formats(L, ctx, stream, timed, capture, dev, g)
-    clk = clocks.stop()
-    barrier()
-    torch.cuda.synchronize()
+        barrier()
+        t = max_over_ranks(timed(lambda r, k=k: shape_graphs[k].replay(), reps) / (reps * N_COPIES))
+        per_shape[n] = round((Q4K_BYTES(i, o) + 4 * (i + o)) / world / (t / 1e3) / 1e9, 1)
+    ms_step = max_over_ranks(ms_total / args.steps)
 
-    ms_step = ms_total / args.steps
-    if pg is not None:
-        t = torch.tensor([ms_step], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms_step = float(t.item())
-
-    # e2e: the seven linears through the public call with HOST buffers
-    # (pinned), host->device of x and device->host of y inside the timed region
-    xh = [torch.randn(1, i, generator=torch.Generator().manual_seed(7)).pin_memory()
-          for _, i, _ in SHAPES]
-    yh = [torch.empty(1, o).pin_memory() for _, _, o in SHAPES]
+    # e2e: the public calls with host buffers -- every step copies its four
+    # activation rows from page-locked host memory to the device, runs the
+    # four calls, copies the seven outputs back and synchronises once
+    hx = [t.cpu().pin_memory() for t in (x_attn, x_o, x_mlp, x_down)]
+    dx = [x_attn, x_o, x_mlp, x_down]
+    hy = [torch.empty(y.shape).pin_memory() for y in ys]
+    h2d = sum(t.numel() * 4 for t in hx)
+    d2h = sum(t.numel() * 4 for t in hy)
 
     def e2e_step(c):
-        for k in range(len(SHAPES)):
-            check(L.rq_linear(ctx.handle, weights[c][k].handle, xh[k].data_ptr(), yh[k].data_ptr(),
-                              1, stream.cuda_stream))
+        with torch.cuda.stream(stream):
+            for h, d in zip(hx, dx):
+                d.copy_(h, non_blocking=True)
+            launch_layer(c, stream.cuda_stream)
+            for h, d in zip(hy, ys):
+                h.copy_(d, non_blocking=True)
+        stream.synchronize()
 
     for c in range(3):
         e2e_step(c % N_COPIES)
     barrier()
     torch.cuda.synchronize()
-    e2e_steps = max(5, min(args.steps, 50))
+    e2e_steps = max(5, min(args.steps, 100))
     t0 = time.perf_counter()
     for s in range(e2e_steps):
         e2e_step(s % N_COPIES)
-    torch.cuda.synchronize()
-    e2e_ms = (time.perf_counter() - t0) / e2e_steps * 1e3
-    if pg is not None:
-        t = torch.tensor([e2e_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) / e2e_steps * 1e3)
 
     sb = step_bytes()
-    value = sb * world / (ms_step / 1e3) / 1e9
-    e2e_val = sb * world / (e2e_ms / 1e3) / 1e9
-    pk = peaks()
-    dom_bytes = 2 * Q4K_BYTES(8192, 28672) + 4 * (8192 + 2 * 28672)
-    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    value = sb / (ms_step / 1e3) / 1e9
+    e2e_val = sb / (e2e_ms / 1e3) / 1e9
+    dom_bytes = (2 * Q4K_BYTES(8192, 28672)) // world + 4 * (8192 + 2 * 28672 // world)
     cpu = None
+    host_layer = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        host = {n: weights[0][k].download() for k, (n, _, _) in enumerate(SHAPES)}
-        cpu = cpu_baseline(host, seconds=args.cpu_seconds)
+        host_layer = {n: weights[0][k].download() for k, (n, _, _) in enumerate(SHAPES)}
+        cpu = cpu_layer_q4k(host_layer, seconds=args.cpu_seconds)
+    small_m = formats = None
+    if world == 1 and not args.no_small_m:
+        small_m = small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g, pk, host_layer)
+        formats = other_formats(L, ctx, stream, timed, capture, dev, g, pk, host_layer is not None)
+    del graphs, shape_graphs, dom
+    graphs = shape_graphs = dom = None
+    for layer in weights:
+        for w in layer:
+            w.free()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
     moe = None
     if not args.no_moe:
-        moe = moe_sweep(local) if world == 1 else moe_ep_sweep(local, pg)
+        moe = (moe_sweep(local, pk, with_cpu=host_layer is not None) if world == 1
+               else moe_ep_sweep(local, pg))
     dec = None
     if not args.no_decode:
-        del graphs, shape_graphs, dom
-        graphs = shape_graphs = dom = None
-        for layer in weights:
-            for w in layer:
-                w.free()
-        torch.cuda.synchronize()
-        torch.cuda.empty_cache()
-        dec = decode_70b(local, pg=pg)
+        dec = decode_70b(local, pk, pg=pg, verify=not args.no_verify, with_cpu=host_layer is not None)
     if rank == 0:
-        traffic = None
-        tp = os.path.join(ROOT, "profiles", "traffic_q4k_gate_up.json")
-        if os.path.exists(tp):
-            with open(tp) as f:
-                traffic = json.load(f).get("bytes_per_launch")
+        launches = 2 * len(groups)  # staging + matvec per call (the all-reduce runs inside the matvec)
+        if world > 1 and not fused_allreduce_default(world):
+            launches += 2           # a separate all-reduce kernel after o and down
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "weak" if world == 1 else "strong", "vs_baseline": None,
             "dtype": "int8x3 dp4a + f32 (4-bit weights)",
             "data": "synthetic: W ~ N(0,0.02) f32 quantized to Q4_K on device (seeded), x ~ N(0,1)",
-            "config": {"workload": WORKLOAD, "batch_m": 1, "weight_format": "GGML Q4_K",
-                       "bytes_per_step": sb,
-                       "launch_grouping": "q/k/v batched on their shared x, o, gate/up batched "
-                                          "on their shared x, down (4 rq_linear[_batch] calls)",
-                       "l2": f"inputs larger than L2: {N_COPIES} rotating layer copies, "
-                             f"{N_COPIES * sb / 1e9:.2f} GB per rotation vs 126 MB L2",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "pct_of_hbm_peak": round(100 * value / world / pk["hbm_gbs"], 1),
-                       "per_shape_single_call_gbs": per_shape},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
-                         "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                         "traffic": traffic,
-                         "kernel": "rq_linear_batch gate+up 2x(8192->28672): xquant + mv_pipe, "
-                                   f"peak {pk['source']}"},
-            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": sum(4 * i for _, i, _ in SHAPES),
-                    "d2h_bytes_per_step": sum(4 * o for _, _, o in SHAPES)},
-            "gpu_launches": args.steps * 2 * len(groups),
+            "config": headline_config(world),
+            "pct_of_hbm_peak_per_gpu": round(100 * value / world / pk["hbm_gbs"], 1),
+            "per_shape_single_call_gbs": per_shape,
+            "roofline": roofline_hbm(dom_bytes, dom_ms, pk,
+                                     "rq_linear_batch gate+up 2x(8192->28672" +
+                                     (f"/{world}" if world > 1 else "") + "): xquant + mv_pipe_kernel<Q4_K>",
+                                     "q4k_gate_up" if world == 1 else None),
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "how": "per step: 4 pinned-host -> device activation copies, the 4 public calls, 7 outputs "
+                           "back to pinned host memory, one stream synchronisation"},
+            "gpu_launches": args.steps * launches,
             "clocks": clk,
         }
         if cpu is not None:
@@ -742,19 +1006,35 @@ def run_gpu(args) -> None:
         if formats is not None:
             line["other_formats"] = formats
         print(json.dumps(line), flush=True)
-    del graphs, shape_graphs, dom
     if pg is not None:
         pg.barrier()
+        tpmod.finalize(ctx)
         pg.destroy_process_group()
 
 
+def fused_allreduce_default(world: int) -> bool:
+    """Mirrors librq's rule for the in-kernel all-reduce (RQ_TP_FUSED)."""
+    e = os.environ.get("RQ_TP_FUSED")
+    if e == "0":
+        return False
+    if e == "1":
+        return True
+    return world == 2
+
+
+CASES = ("pipe_gate_up", "mm_gate_m8", "sk_gate_m16", "tc_gate_m128", "q3k_gate", "moe_t1", "moe_t16",
+         "attn_decode")
+
+
 def run_case(name: str) -> None:
-    """A few launches of one kernel for an ncu capture: 'pipe_gate_up' (the
-    gate+up rq_linear_batch of one 70B layer, M=1), 'mm_gate_m8' (gate_proj
-    8192 -> 28672 at M=8 on the mma.sync kernel), 'sk_gate_m16' (the same at
-    M=16 on the split-K tcgen05 kernel) or 'tc_gate_m128' (M=128 on the tiled
-    tcgen05 kernel).  Prints the per-call time measured
-    without the profiler."""
+    """A few launches of one kernel or layer for an ncu capture, at the
+    bench's shapes: 'pipe_gate_up' (the gate+up rq_linear_batch of one 70B
+    layer, M=1), 'mm_gate_m8' (gate_proj 8192 -> 28672 at M=8, mma.sync),
+    'sk_gate_m16' (M=16, split-K tcgen05), 'tc_gate_m128' (M=128, tiled
+    tcgen05), 'q3k_gate' (the Q3_K gate_proj matvec), 'moe_t1' / 'moe_t16'
+    (the Mixtral layer at T = 1 / 16), 'attn_decode' (a 4-layer 70B-shape
+    model's decode steps: attention at head_dim 128).  Prints the per-call
+    time measured without the profiler."""
     import ctypes
 
     import torch
@@ -763,26 +1043,50 @@ def run_case(name: str) -> None:
     L = lib()
     ctx = Context.get(0)
     g = torch.Generator(device="cuda").manual_seed(5)
-    ws = [QWeight.quantize(ctx, Q4_K, torch.randn(28672, 8192, device="cuda", generator=g) * 0.02)
-          for _ in range(2)]
     s = torch.cuda.current_stream().cuda_stream
-    arr = lambda v: (ctypes.c_void_p * len(v))(*v)  # noqa: E731
-    if name == "pipe_gate_up":
-        x = torch.randn(1, 8192, device="cuda", generator=g)
-        ys = [torch.empty(1, 28672, device="cuda") for _ in range(2)]
+    if name in ("moe_t1", "moe_t16"):
+        from rustyllm_b200.mixtral import SparseMoe
+        E, H, F = MIXTRAL["E"], MIXTRAL["H"], MIXTRAL["F"]
+        router = (torch.randn(E, H, device="cuda", generator=g) * 0.02).cpu().numpy()
+        experts = [tuple(QWeight.quantize(ctx, Q4_K, torch.randn(o, i, device="cuda", generator=g) * 0.02)
+                         for o, i in ((F, H), (H, F), (F, H))) for _ in range(E)]
+        moe = SparseMoe(router, experts, top_k=2)
+        T = 1 if name == "moe_t1" else 16
+        x = torch.randn(T, H, device="cuda", generator=g)
 
         def call():
-            check(L.rq_linear_batch(ctx.handle, 2, arr([w.handle.value for w in ws]), arr([x.data_ptr()] * 2),
-                                    arr([y.data_ptr() for y in ys]), s))
-        nbytes = 2 * Q4K_BYTES(8192, 28672)
+            moe.forward(x)
+        nbytes = 0
+    elif name == "attn_decode":
+        from rustyllm_b200.llama import random_model
+        cfg = dict(LLAMA70B, n_layers=4)
+        model, _ = random_model(cfg, Q4_K, seed=3)
+        model.forward(np.arange(20, dtype=np.int32), 0, want_logits=False)
+
+        def call():
+            model.decode_step(s)
+        nbytes = 0
     else:
-        M = {"mm_gate_m8": 8, "sk_gate_m16": 16}.get(name, 128)
-        x = torch.randn(M, 8192, device="cuda", generator=g)
-        y = torch.empty(M, 28672, device="cuda")
+        qt = Q3_K if name == "q3k_gate" else Q4_K
+        ws = [QWeight.quantize(ctx, qt, torch.randn(28672, 8192, device="cuda", generator=g) * 0.02)
+              for _ in range(2)]
+        arr = lambda v: (ctypes.c_void_p * len(v))(*v)  # noqa: E731
+        if name == "pipe_gate_up":
+            x = torch.randn(1, 8192, device="cuda", generator=g)
+            ys = [torch.empty(1, 28672, device="cuda") for _ in range(2)]
 
-        def call():
-            check(L.rq_linear(ctx.handle, ws[0].handle, x.data_ptr(), y.data_ptr(), M, s))
-        nbytes = Q4K_BYTES(8192, 28672)
+            def call():
+                check(L.rq_linear_batch(ctx.handle, 2, arr([w.handle.value for w in ws]),
+                                        arr([x.data_ptr()] * 2), arr([y.data_ptr() for y in ys]), s))
+            nbytes = 2 * Q4K_BYTES(8192, 28672)
+        else:
+            M = {"mm_gate_m8": 8, "sk_gate_m16": 16, "q3k_gate": 1}.get(name, 128)
+            x = torch.randn(M, 8192, device="cuda", generator=g)
+            y = torch.empty(M, 28672, device="cuda")
+
+            def call():
+                check(L.rq_linear(ctx.handle, ws[0].handle, x.data_ptr(), y.data_ptr(), M, s))
+            nbytes = (Q3K_BYTES if qt == Q3_K else Q4K_BYTES)(8192, 28672)
     for _ in range(3):
         call()
     torch.cuda.synchronize()
@@ -793,8 +1097,11 @@ def run_case(name: str) -> None:
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / 10
-    out = {"case": name, "us_per_call": round(ms * 1e3, 2), "weight_gbs": round(nbytes / (ms / 1e3) / 1e9, 1)}
+    out = {"case": name, "us_per_call": round(ms * 1e3, 2)}
+    if nbytes:
+        out["weight_gbs"] = round(nbytes / (ms / 1e3) / 1e9, 1)
     if name in ("tc_gate_m128", "sk_gate_m16"):
+        M = 16 if name == "sk_gate_m16" else 128
         out["tflops"] = round(2 * M * 8192 * 28672 / (ms / 1e3) / 1e12, 1)
     print(json.dumps(out), flush=True)
 
@@ -808,12 +1115,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 80-layer 70B decode run")
+    ap.add_argument("--no-verify", action="store_true", help="skip the oracle replay of the decode tokens")
     ap.add_argument("--only-decode", action="store_true", help="run only the 70B decode")
-    ap.add_argument("--no-small-m", action="store_true", help="skip the small-M Q4_K matmul sweep")
+    ap.add_argument("--no-small-m", action="store_true", help="skip the small-M and other-format sweeps")
     ap.add_argument("--no-moe", action="store_true", help="skip the Mixtral MoE layer sweep")
     ap.add_argument("--decode-layers", type=int, default=None,
                     help="layers of the decode model (default 80; fewer for profiling)")
-    ap.add_argument("--case", choices=["pipe_gate_up", "mm_gate_m8", "sk_gate_m16", "tc_gate_m128"], default=None,
+    ap.add_argument("--case", choices=CASES, default=None,
                     help="run a few launches of one kernel (for profiling) and exit")
     args = ap.parse_args()
     if args.case:

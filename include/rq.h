@@ -69,6 +69,15 @@ RQ_API int rq_destroy(rq_ctx* ctx);
  * truncated to n).  Returns the full message length. */
 RQ_API int rq_last_error(char* buf, size_t n);
 
+/* Synchronise the context's device and report whether a bounded wait
+ * (mbarrier or peer flag, ~1 s) inside a kernel of an asynchronous call on
+ * this context -- or of rq_linear_noalloc on this device -- gave up since the
+ * last check: RQ_ERR_TIMEOUT (record cleared; the outputs of those calls are
+ * incomplete), else RQ_OK.  Calls with host buffers check this themselves
+ * before they return.  No reference counterpart (candle's CPU kernels cannot
+ * time out). */
+RQ_API int rq_ctx_status(rq_ctx* ctx);
+
 /* "rq <version> sm_100a" */
 RQ_API const char* rq_version(void);
 
@@ -130,6 +139,20 @@ RQ_API int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, 
 RQ_API int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const float* const* x,
                            float* const* y, void* stream);
 
+/* Row-parallel linear under tensor parallelism: y[M][out] = the sum over
+ * the ranks of x_r[M][in] * W_r^T, where W_r is this rank's column slice of
+ * the weight (the o_proj / down_proj shard) and x_r its slice of the input;
+ * every rank calls with the same M and gets the same y bits.  At M = 1 the
+ * all-reduce runs inside the matvec kernel: each CTA stores its rows of the
+ * partial product straight into every peer's NVLink exchange buffer and sums
+ * the W slots in rank order once the peers have flagged theirs; otherwise
+ * (or with RQ_TP_FUSED=0) the partial product is all-reduced by a separate
+ * kernel (NCCL above 512 K elements).  x and y are device memory;
+ * asynchronous on `stream`; needs rq_tp_init.  No reference counterpart (the
+ * reference runs on one device). */
+RQ_API int rq_linear_allreduce(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t M,
+                               void* stream);
+
 /* rq_linear for callers that cannot allocate device memory.  No counterpart
  * in the reference.
  *
@@ -143,14 +166,22 @@ RQ_API int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const 
  *
  *   - x [M][in] and y [M][out] must be device memory on w's device;
  *   - M * in is limited by the 2 MiB array at 3.5 bytes per element (plus
- *     alignment); larger requests fail with RQ_ERR_INVALID and a message;
+ *     alignment; e.g. M <= 20 at in = 28672, M <= 73 at in = 8192); larger
+ *     requests fail with RQ_ERR_INVALID and a message;
+ *   - every row runs the M=1 matvec kernels, so results match rq_linear's
+ *     within the linear parity tolerance (relative L2 <= 1e-4; for M <= 3
+ *     they are the same kernels); weights with no M=1 pipeline shape --
+ *     Q8_0 / Q5_K with in not a multiple of 256, Q6_K / Q2_K with in not a
+ *     multiple of 1024, any type with in > 30720 other than Q4_0 / Q4_K /
+ *     Q3_K -- return RQ_ERR_UNSUPPORTED;
  *   - the first call on a device resolves the array's device address
  *     (cudaGetSymbolAddress): make that first call before any stream
  *     capture;
  *   - all calls on a device share the one array, which keeps the last
  *     call's contents: calls that overlap on the GPU (other streams,
- *     threads) race on it, so serialise them.
- * Results equal rq_linear's (same kernels). */
+ *     threads) race on it, so serialise them;
+ *   - the call is asynchronous on `stream`; a bounded kernel wait that gave
+ *     up inside it is reported by rq_ctx_status on a context of that device. */
 RQ_API int rq_linear_noalloc(const rq_weight* w, const float* x, float* y, int64_t M,
                              void* stream);
 
@@ -174,7 +205,8 @@ RQ_API int rq_tp_finalize(rq_ctx* ctx);
 /* ------------------------------------------------------------- sparse MoE */
 
 /* Mixtral SparseMoe (src/streaming_mixtral.rs:259-319) with quantized
- * experts: router weight f32 [E][hidden] (host or device, copied), expert
+ * experts: router weight f32 [E][hidden] (host or device; copied and rounded
+ * to F16 as ParallelLinear::new does, src/parallel_linear.rs:128-131), expert
  * weights w1 = gate [ffn][hidden], w3 = up [ffn][hidden], w2 = down
  * [hidden][ffn] (borrowed: they must outlive the layer).  E <= 32.  Under a
  * communicator (rq_tp_init, world W > 1) the experts of other ranks (e % W
@@ -258,8 +290,10 @@ RQ_API int rq_llama_forward_all(rq_llama* m, const int32_t* tokens, int64_t T, i
                                 int32_t* argmax, void* stream);
 RQ_API int rq_llama_decode_step(rq_llama* m, void* stream);
 RQ_API int rq_llama_set_fused(rq_llama* m, int enable);
-/* RQ_ERR_TIMEOUT (and clears it) when a wait of a one-launch step timed
- * out since the last call; synchronous. */
+/* RQ_ERR_TIMEOUT (and clears it) when a bounded wait inside a kernel of the
+ * model (a decode step, the one-launch step, a forward) gave up since the
+ * last call; synchronous.  rq_llama_forward / _forward_all check it before
+ * they return. */
 RQ_API int rq_llama_status(rq_llama* m);
 /* Tokens appended since the last reset (count may exceed cap), and the
  * current position.  Synchronous. */

@@ -15,7 +15,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
-Q4_0, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 2, 8, 10, 11, 12, 13, 14
+F16, Q4_0, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 1, 2, 8, 10, 11, 12, 13, 14
 BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q2_K: 84, Q3_K: 110, Q4_K: 144, Q5_K: 176, Q6_K: 210}
 BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q2_K: 256, Q3_K: 256, Q4_K: 256, Q5_K: 256, Q6_K: 256}
 
@@ -39,6 +39,8 @@ def lib() -> ctypes.CDLL:
         L.rqo_dequantize.argtypes = [I, P, I64, I64, P]
         L.rqo_matmul_ref.argtypes = [I, P, I64, I64, P, I64, P, I]
         L.rqo_linear_threaded.argtypes = [I, P, I64, I64, P, I64, P, I]
+        L.rqo_linear_rows.argtypes = [I, P, I64, I64, P, I64, P, I]
+        L.rqo_parallel_linear_f16.argtypes = [P, I64, I64, P, I64, P, I, I]
         L.rqo_dot_q4_0_scalar.argtypes = [P, P, I64]
         L.rqo_dot_q4_0_scalar.restype = F
         L.rqo_dot_q4_0_avx2order.argtypes = [P, P, I64]
@@ -52,7 +54,7 @@ def lib() -> ctypes.CDLL:
         L.rqo_silu.argtypes = [F]
         L.rqo_silu.restype = F
         for fn in ("rqo_quantize", "rqo_dequantize", "rqo_matmul_ref", "rqo_linear_threaded",
-                   "rqo_moe_forward"):
+                   "rqo_linear_rows", "rqo_parallel_linear_f16", "rqo_moe_forward"):
             getattr(L, fn).restype = I
         _lib = L
     return _lib
@@ -112,6 +114,43 @@ def linear_threaded(qtype: int, blocks: np.ndarray, n_out: int, n_in: int, x: np
     return y
 
 
+def linear_rows(qtype: int, blocks: np.ndarray, n_out: int, n_in: int, x: np.ndarray,
+                nthreads: int = 0) -> np.ndarray:
+    """rqo_linear_threaded's products, each weight row dequantized once."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, n_in)
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    y = np.empty((x.shape[0], n_out), dtype=np.float32)
+    rc = lib().rqo_linear_rows(qtype, _p(blocks), n_out, n_in, _p(x), x.shape[0], _p(y), nthreads)
+    if rc != 0:
+        raise ValueError(f"rqo_linear_rows failed ({rc})")
+    return y
+
+
+def parallel_linear_f16(w16: np.ndarray, x: np.ndarray, avx2: bool = True, nthreads: int = 0,
+                        y: np.ndarray | None = None) -> np.ndarray:
+    """ParallelLinear::forward (parallel_linear.rs:191-295): w16 [out, in]
+    float16 (or its uint16 bits), x f32 [n, in]."""
+    w = np.ascontiguousarray(w16).view(np.uint16)
+    out, n_in = w.shape
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, n_in)
+    if y is None:
+        y = np.empty((x.shape[0], out), dtype=np.float32)
+    rc = lib().rqo_parallel_linear_f16(_p(w), out, n_in, _p(x), x.shape[0], _p(y), int(avx2), nthreads)
+    if rc != 0:
+        raise ValueError(f"rqo_parallel_linear_f16 failed ({rc})")
+    return y
+
+
+def router_f16(wr: np.ndarray) -> np.ndarray:
+    """The router weight as the reference holds it: ParallelLinear::new
+    converts it to F16 (round to nearest even), as uint16 bits."""
+    if wr.dtype == np.float16:
+        return np.ascontiguousarray(wr).view(np.uint16)
+    if wr.dtype == np.uint16:
+        return np.ascontiguousarray(wr)
+    return f32_to_f16_bits(np.ascontiguousarray(wr, dtype=np.float32))
+
+
 def dot_q4_0_scalar(w_row: np.ndarray, x_row: np.ndarray) -> float:
     nb = x_row.size // 32
     return float(lib().rqo_dot_q4_0_scalar(_p(w_row), _p(x_row), nb))
@@ -137,8 +176,10 @@ def f16_bits_to_f32(h: np.ndarray) -> np.ndarray:
 
 
 def router_logits(x: np.ndarray, wr: np.ndarray) -> np.ndarray:
+    """Gate logits: ParallelLinear over the F16 router weight (wr f32, f16
+    or f16 bits)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    wr = np.ascontiguousarray(wr, dtype=np.float32)
+    wr = router_f16(wr)
     T, H = x.shape
     E = wr.shape[0]
     out = np.empty((T, E), dtype=np.float32)
@@ -168,13 +209,18 @@ def permute(ids: np.ndarray, weights: np.ndarray, E: int):
 
 def moe_forward(x: np.ndarray, wr: np.ndarray, qtype: int, w1: list, w3: list, w2: list,
                 F: int, k: int = 2, nthreads: int = 0):
-    """Full SparseMoe layer on the CPU; returns (y, ids, perm, offsets)."""
+    """Full SparseMoe layer on the CPU; returns (y, ids, perm, offsets).
+    qtype F16: w1/w3/w2 are float16 [out, in] arrays (the reference's
+    ParallelLinear experts); otherwise GGML block bytes."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    wr = np.ascontiguousarray(wr, dtype=np.float32)
+    wr = router_f16(wr)
     T, H = x.shape
     E = wr.shape[0]
     arr_t = ctypes.c_void_p * E
-    keep = [np.ascontiguousarray(a, dtype=np.uint8) for a in (*w1, *w3, *w2)]
+    if qtype == F16:
+        keep = [np.ascontiguousarray(a).view(np.uint16) for a in (*w1, *w3, *w2)]
+    else:
+        keep = [np.ascontiguousarray(a, dtype=np.uint8) for a in (*w1, *w3, *w2)]
     p1 = arr_t(*[_p(a) for a in keep[:E]])
     p3 = arr_t(*[_p(a) for a in keep[E:2 * E]])
     p2 = arr_t(*[_p(a) for a in keep[2 * E:]])
@@ -204,6 +250,11 @@ class OracleLlama:
         L.rqo_llama_set_head.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         L.rqo_llama_forward.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                         ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        L.rqo_llama_embed.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+        L.rqo_llama_layer.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                                      ctypes.c_int64, ctypes.c_int]
+        L.rqo_llama_head.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                     ctypes.c_void_p, ctypes.c_int]
         self.cfg = cfg
         self.h = L.rqo_llama_create(cfg["hidden"], cfg["intermediate"], cfg["n_heads"],
                                     cfg["n_kv_heads"], cfg["head_dim"], cfg["n_layers"],
@@ -218,6 +269,20 @@ class OracleLlama:
         arr = (ctypes.c_void_p * 7)(*[_p(b) for b in bl])
         self.keep += [bl, r1, r2, arr]
         lib().rqo_llama_set_layer(self.h, l, ctypes.cast(arr, ctypes.c_void_p), _p(r1), _p(r2))
+
+    def stream_layer(self, l, blocks7, rms1, rms2, x: np.ndarray, index_pos: int, nthreads=0) -> None:
+        """Run layer l over x in place with weights given for this call only
+        (not kept: a model larger than host memory runs a layer at a time)."""
+        bl = [np.ascontiguousarray(b, dtype=np.uint8) for b in blocks7]
+        r1 = np.ascontiguousarray(rms1, dtype=np.float32)
+        r2 = np.ascontiguousarray(rms2, dtype=np.float32)
+        arr = (ctypes.c_void_p * 7)(*[_p(b) for b in bl])
+        lib().rqo_llama_set_layer(self.h, l, ctypes.cast(arr, ctypes.c_void_p), _p(r1), _p(r2))
+        try:
+            self.layer(l, x, index_pos, nthreads)
+        finally:
+            null = (ctypes.c_void_p * 7)()
+            lib().rqo_llama_set_layer(self.h, l, ctypes.cast(null, ctypes.c_void_p), _p(r1), _p(r2))
 
     def set_embedding(self, emb_f16):
         e = np.ascontiguousarray(emb_f16).view(np.uint16)
@@ -239,6 +304,41 @@ class OracleLlama:
         if rc != 0:
             raise ValueError(f"rqo_llama_forward failed ({rc})")
         return logits, int(nxt.value)
+
+    def embed(self, tokens) -> np.ndarray:
+        ids = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        x = np.empty((ids.size, self.cfg["hidden"]), dtype=np.float32)
+        lib().rqo_llama_embed(self.h, _p(ids), ids.size, _p(x))
+        return x
+
+    def layer(self, l, x: np.ndarray, index_pos: int, nthreads=0) -> None:
+        """QBlock l over the hidden rows x [T, hidden] in place."""
+        assert x.dtype == np.float32 and x.flags["C_CONTIGUOUS"]
+        rc = lib().rqo_llama_layer(self.h, l, _p(x), x.shape[0], index_pos, nthreads)
+        if rc != 0:
+            raise ValueError(f"rqo_llama_layer failed ({rc})")
+
+    def head(self, x: np.ndarray, nthreads=0):
+        """(logits [T, vocab], argmax [T]) of every row of x."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T = x.shape[0]
+        logits = np.empty((T, self.cfg["vocab"]), dtype=np.float32)
+        amax = np.empty(T, dtype=np.int32)
+        rc = lib().rqo_llama_head(self.h, _p(x), T, _p(logits), _p(amax), nthreads)
+        if rc != 0:
+            raise ValueError(f"rqo_llama_head failed ({rc})")
+        return logits, amax
+
+    def forward_all(self, tokens, index_pos, nthreads=0):
+        """forward_all (src/streaming_quantized.rs:611-620): logits and the
+        greedy token of every position.  Fed the prompt plus the tokens a
+        greedy decode produced, position p's argmax is the token that decode
+        step p emitted (every position's arithmetic is that of the
+        incremental step)."""
+        x = self.embed(tokens)
+        for l in range(self.cfg["n_layers"]):
+            self.layer(l, x, index_pos, nthreads)
+        return self.head(x, nthreads)
 
     def generate(self, prompt, max_new_tokens, nthreads=0):
         toks = []

@@ -748,35 +748,161 @@ int rqo_linear_threaded(int type, const uint8_t* blocks, int64_t out, int64_t in
     return 0;
 }
 
+/* The same products as rqo_linear_threaded, computed faster for M > 1:
+ * each weight row is dequantized once and dotted with every activation row.
+ * The dot is the 8-lane fmaf order of dot_kquant_f32 / the AVX2-order Q4_0
+ * dot (element i into lane i % 8, lanes summed in order), and the dequant is
+ * exact, so every output has the bits rqo_linear_threaded gives it.  Used by
+ * the layer and model oracles, where M is a prompt or a batch of tokens. */
+static float dot_lanes8_fma(const float* w, const float* x, int64_t n) {
+    float acc[8] = {0};
+    for (int64_t i = 0; i < n; i += 8)
+        for (int c = 0; c < 8; c++) acc[c] = fmaf(w[i + c], x[i + c], acc[c]);
+    float s = 0.0f;
+    for (int c = 0; c < 8; c++) s += acc[c];
+    return s;
+}
+
+typedef struct {
+    int type;
+    const uint8_t* blocks;
+    int64_t out, in, M, row_bytes;
+    const float* x;
+    float* y;
+    int64_t next; /* atomic row-chunk counter */
+} rows_job;
+
+static void* rows_worker(void* arg) {
+    rows_job* j = (rows_job*)arg;
+    float* w = (float*)malloc(sizeof(float) * (size_t)j->in);
+    if (!w) return NULL;
+    const int64_t chunk = 16;
+    for (;;) {
+        int64_t c = __atomic_fetch_add(&j->next, 1, __ATOMIC_RELAXED);
+        int64_t o0 = c * chunk;
+        if (o0 >= j->out) break;
+        int64_t o1 = o0 + chunk < j->out ? o0 + chunk : j->out;
+        for (int64_t o = o0; o < o1; o++) {
+            dequantize_row(j->type, j->blocks + o * j->row_bytes, j->in, w);
+            for (int64_t m = 0; m < j->M; m++) j->y[m * j->out + o] = dot_lanes8_fma(w, j->x + m * j->in, j->in);
+        }
+    }
+    free(w);
+    return NULL;
+}
+
+int rqo_linear_rows(int type, const uint8_t* blocks, int64_t out, int64_t in, const float* x, int64_t M,
+                    float* y, int nthreads) {
+    int64_t be = rqo_block_elems(type), bb = rqo_block_bytes(type);
+    if (!be || in % be || M <= 0 || out <= 0) return -1;
+    if (nthreads <= 0) nthreads = (int)sysconf(_SC_NPROCESSORS_ONLN);
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    rows_job j;
+    j.type = type; j.blocks = blocks; j.out = out; j.in = in; j.M = M;
+    j.row_bytes = in / be * bb; j.x = x; j.y = y; j.next = 0;
+    pthread_t th[256];
+    int started = 0;
+    for (int t = 1; t < nthreads; t++)
+        if (pthread_create(&th[started], NULL, rows_worker, &j) == 0) started++;
+    rows_worker(&j);
+    for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
+    return 0;
+}
+
 /* ------------------------------------------------------------------ MoE */
 
 float rqo_silu(float x) { return x / (1.0f + expf(-x)); }
 
-/* Canonical router dot: 32 partial sums p[l] over float4 chunks l, l+32, ...
- * (each chunk folded with fmaf in component order), then the butterfly
- * p[l] + p[l^off] for off = 16, 8, 4, 2, 1 -- the order a warp computes with
- * shuffles.  Both the GPU router kernel and this oracle use it, so router
- * logits agree bit for bit.  H must be a multiple of 4. */
-static float router_dot(const float* x, const float* w, int64_t H) {
-    float p[32];
-    int64_t n4 = H / 4;
-    for (int l = 0; l < 32; l++) {
-        float acc = 0.0f;
-        for (int64_t i = l; i < n4; i += 32)
-            for (int c = 0; c < 4; c++) acc = fmaf(x[4 * i + c], w[4 * i + c], acc);
-        p[l] = acc;
-    }
-    for (int off = 16; off >= 1; off >>= 1) {
-        float q[32];
-        for (int l = 0; l < 32; l++) q[l] = p[l] + p[l ^ off];
-        memcpy(p, q, sizeof p);
-    }
-    return p[0];
+/* ------------------------------------------- ParallelLinear (F16 weights) */
+
+/* parallel_linear.rs:33-94: the f16 row is converted to an f32 scratch row
+ * (half's convert_to_f32_slice, exact), then the dot product.  A build with
+ * the avx2 and fma target features (the configuration the AVX2 figures of
+ * q4_kernel.rs:31-39 come from) runs dot_f32_avx2_fma: eight f32 lanes
+ * accumulate element 8i+c into lane c with a fused multiply-add
+ * (_mm256_fmadd_ps, :80-84), the lanes are summed left to right
+ * (buf.iter().sum(), :87-89) and a scalar tail adds a[i]*b[i] (two
+ * roundings, :91-94).  Without those features the scalar loop of :48-55 runs:
+ * sum += x[k]*w[k] in ascending k, two roundings each. */
+static float dot_f16_scalar(const float* x, const float* w, int64_t n) {
+    float sum = 0.0f;
+    for (int64_t k = 0; k < n; k++) sum += x[k] * w[k];
+    return sum;
 }
 
-void rqo_router_logits(const float* x, int64_t T, int64_t H, const float* wr, int E, float* logits) {
-    for (int64_t t = 0; t < T; t++)
-        for (int e = 0; e < E; e++) logits[t * E + e] = router_dot(x + t * H, wr + (int64_t)e * H, H);
+static float dot_f16_lanes8(const float* x, const float* w, int64_t n) {
+    float acc[8] = {0};
+    const int64_t chunks = n / 8;
+    for (int64_t i = 0; i < chunks; i++)
+        for (int c = 0; c < 8; c++) acc[c] = fmaf(x[8 * i + c], w[8 * i + c], acc[c]);
+    float sum = -0.0f;
+    for (int c = 0; c < 8; c++) sum += acc[c];
+    for (int64_t i = chunks * 8; i < n; i++) sum += x[i] * w[i];
+    return sum;
+}
+
+typedef struct {
+    const uint16_t* w;
+    int64_t out, in, n, chunk, nchunks;
+    const float* x;
+    float* y;
+    int avx2;
+    int64_t next; /* atomic chunk counter */
+} pl_job;
+
+static void* pl_worker(void* arg) {
+    pl_job* j = (pl_job*)arg;
+    float* scratch = (float*)malloc(sizeof(float) * (size_t)j->in);
+    if (!scratch) return NULL;
+    for (;;) {
+        int64_t c = __atomic_fetch_add(&j->next, 1, __ATOMIC_RELAXED);
+        if (c >= j->nchunks) break;
+        int64_t start = c * j->chunk, end = start + j->chunk;
+        if (end > j->n * j->out) end = j->n * j->out;
+        for (int64_t pos = start; pos < end; pos++) {
+            int64_t b = pos / j->out, o = pos % j->out;
+            rqo_f16_to_f32_n(j->w + o * j->in, scratch, j->in);
+            j->y[pos] = j->avx2 ? dot_f16_lanes8(j->x + b * j->in, scratch, j->in)
+                                : dot_f16_scalar(j->x + b * j->in, scratch, j->in);
+        }
+    }
+    free(scratch);
+    return NULL;
+}
+
+/* parallel_linear.rs:191-295: y[b][j] = dot_f16_f32(W[j], x[b]) over the
+ * flattened n*out outputs in chunks of max(total / (4 workers), 8) (:223-225);
+ * the n == 1 fast path (:239-259) computes the same values. */
+int rqo_parallel_linear_f16(const uint16_t* w, int64_t out, int64_t in, const float* x, int64_t n,
+                            float* y, int avx2, int nthreads) {
+    if (out <= 0 || in <= 0 || n <= 0) return -1;
+    if (nthreads <= 0) nthreads = (int)sysconf(_SC_NPROCESSORS_ONLN);
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    pl_job j;
+    j.w = w; j.out = out; j.in = in; j.n = n; j.x = x; j.y = y; j.avx2 = avx2; j.next = 0;
+    int64_t total = n * out;
+    int64_t chunk = total / ((int64_t)nthreads * 4);
+    if (chunk < 8) chunk = 8;
+    if (chunk > total) chunk = total;
+    if (chunk < 1) chunk = 1;
+    j.chunk = chunk;
+    j.nchunks = (total + chunk - 1) / chunk;
+    pthread_t th[256];
+    int started = 0;
+    for (int t = 1; t < nthreads; t++)
+        if (pthread_create(&th[started], NULL, pl_worker, &j) == 0) started++;
+    pl_worker(&j);
+    for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
+    return 0;
+}
+
+/* Router logits: the gate of SparseMoe is a ParallelLinear (F16 weight,
+ * streaming_mixtral.rs:265,283), so logits[t][e] = dot_f16_f32(wr[e], x[t])
+ * in the AVX2 lane order. */
+void rqo_router_logits(const float* x, int64_t T, int64_t H, const uint16_t* wr16, int E, float* logits) {
+    rqo_parallel_linear_f16(wr16, E, H, x, T, logits, 1, 1);
 }
 
 /* streaming_mixtral.rs:284-303: softmax_last_dim, then per token a stable
@@ -824,7 +950,7 @@ void rqo_permute(const int32_t* ids, const float* weights, int64_t T, int E, int
 }
 
 int rqo_moe_forward(const float* x, int64_t T, int64_t H, int64_t F, int E, int k,
-                    const float* wr, int wtype, const uint8_t* const* w1,
+                    const uint16_t* wr, int wtype, const uint8_t* const* w1,
                     const uint8_t* const* w3, const uint8_t* const* w2, float* y,
                     int32_t* ids_out, int32_t* perm_out, int32_t* offsets_out,
                     int nthreads) {
@@ -849,10 +975,16 @@ int rqo_moe_forward(const float* x, int64_t T, int64_t H, int64_t F, int E, int 
         if (n == 0) continue;
         for (int64_t i = 0; i < n; i++)
             memcpy(xin + i * H, x + (int64_t)rows[offs[e] + i] * H, sizeof(float) * (size_t)H);
-        rqo_linear_threaded(wtype, w1[e], F, H, xin, n, g, nthreads);
-        rqo_linear_threaded(wtype, w3[e], F, H, xin, n, u, nthreads);
+        if (wtype == RQO_F16) {  /* the reference's experts: ParallelLinear (streaming_mixtral.rs:231-257) */
+            rqo_parallel_linear_f16((const uint16_t*)w1[e], F, H, xin, n, g, 1, nthreads);
+            rqo_parallel_linear_f16((const uint16_t*)w3[e], F, H, xin, n, u, 1, nthreads);
+        } else {
+            rqo_linear_rows(wtype, w1[e], F, H, xin, n, g, nthreads);
+            rqo_linear_rows(wtype, w3[e], F, H, xin, n, u, nthreads);
+        }
         for (int64_t i = 0; i < n * F; i++) g[i] = rqo_silu(g[i]) * u[i];
-        rqo_linear_threaded(wtype, w2[e], H, F, g, n, o, nthreads);
+        if (wtype == RQO_F16) rqo_parallel_linear_f16((const uint16_t*)w2[e], H, F, g, n, o, 1, nthreads);
+        else rqo_linear_rows(wtype, w2[e], H, F, g, n, o, nthreads);
         for (int64_t i = 0; i < n; i++) {
             float wv = sw[offs[e] + i];
             float* yr = y + (int64_t)rows[offs[e] + i] * H;
@@ -938,14 +1070,22 @@ static void rms_norm(const float* x, const float* w, int64_t n, float eps, float
     for (int64_t i = 0; i < n; i++) y[i] = x[i] / mden * w[i];
 }
 
-/* logits_last: [vocab] of the last position (may be NULL); next: argmax. */
-int rqo_llama_forward(rqo_llama* m, const int32_t* tokens, int64_t T, int64_t pos,
-                      float* logits_last, int32_t* next, int nthreads) {
+void rqo_llama_embed(const rqo_llama* m, const int32_t* tokens, int64_t T, float* x) {
+    for (int64_t t = 0; t < T; t++)
+        for (int64_t i = 0; i < m->H; i++) x[t * m->H + i] = rqo_f16_to_f32(m->emb[(int64_t)tokens[t] * m->H + i]);
+}
+
+/* QBlock::forward (src/streaming_quantized.rs:305-317) of layer l over the
+ * hidden rows x[T][H] at positions pos..pos+T-1, in place; the layer's keys
+ * and values are written into its cache at those positions. */
+int rqo_llama_layer(rqo_llama* m, int64_t l, float* x, int64_t T, int64_t pos, int nthreads) {
     const int64_t H = m->H, I = m->I, nh = m->nh, nkv = m->nkv, hd = m->hd, half = hd / 2;
     const int64_t nq = nh * hd, nk = nkv * hd, rep = nh / nkv;
-    if (pos + T > m->max_seq) return -1;
-    float* x = (float*)malloc(sizeof(float) * (size_t)(T * H));
-    float* h = (float*)malloc(sizeof(float) * (size_t)(T * H));
+    if (l < 0 || l >= m->nl || pos < 0 || pos + T > m->max_seq) return -1;
+    const uint8_t* const* W = m->w + l * 7;
+    for (int i = 0; i < 7; i++)
+        if (!W[i]) return -1;
+    float* h = (float*)calloc((size_t)(T * H), sizeof(float));
     float* q = (float*)malloc(sizeof(float) * (size_t)(T * nq));
     float* k = (float*)malloc(sizeof(float) * (size_t)(T * nk));
     float* v = (float*)malloc(sizeof(float) * (size_t)(T * nk));
@@ -954,89 +1094,156 @@ int rqo_llama_forward(rqo_llama* m, const int32_t* tokens, int64_t T, int64_t po
     float* g = (float*)malloc(sizeof(float) * (size_t)(T * I));
     float* u = (float*)malloc(sizeof(float) * (size_t)(T * I));
     float* sc = (float*)malloc(sizeof(float) * (size_t)m->max_seq);
-    float* lg = (float*)malloc(sizeof(float) * (size_t)m->vocab);
-    if (!x || !h || !q || !k || !v || !a || !o || !g || !u || !sc || !lg) return -2;
-    for (int64_t t = 0; t < T; t++)
-        for (int64_t i = 0; i < H; i++) x[t * H + i] = rqo_f16_to_f32(m->emb[(int64_t)tokens[t] * H + i]);
-    for (int64_t l = 0; l < m->nl; l++) {
-        const uint8_t* const* W = m->w + l * 7;
-        float* kc = m->kc + l * nkv * m->max_seq * hd;
-        float* vc = m->vc + l * nkv * m->max_seq * hd;
-        for (int64_t t = 0; t < T; t++) rms_norm(x + t * H, m->rms1[l], H, m->eps, h + t * H);
-        rqo_linear_threaded(m->wtype, W[0], nq, H, h, T, q, nthreads);
-        rqo_linear_threaded(m->wtype, W[1], nk, H, h, T, k, nthreads);
-        rqo_linear_threaded(m->wtype, W[2], nk, H, h, T, v, nthreads);
-        for (int64_t t = 0; t < T; t++) {
-            int64_t p = pos + t;
-            const float* c = m->cs + p * half;
-            const float* s = m->sn + p * half;
-            for (int64_t hh = 0; hh < nh; hh++) {
-                float* qh = q + (t * nh + hh) * hd;
-                for (int64_t i = 0; i < half; i++) {
-                    float a0 = qh[i], b0 = qh[i + half];
-                    qh[i] = a0 * c[i] - b0 * s[i];
-                    qh[i + half] = a0 * s[i] + b0 * c[i];
-                }
-            }
-            for (int64_t kh = 0; kh < nkv; kh++) {
-                const float* ks = k + (t * nkv + kh) * hd;
-                const float* vs = v + (t * nkv + kh) * hd;
-                float* kd = kc + (kh * m->max_seq + p) * hd;
-                float* vd = vc + (kh * m->max_seq + p) * hd;
-                for (int64_t i = 0; i < half; i++) {
-                    float a0 = ks[i], b0 = ks[i + half];
-                    kd[i] = a0 * c[i] - b0 * s[i];
-                    kd[i + half] = a0 * s[i] + b0 * c[i];
-                }
-                for (int64_t i = 0; i < hd; i++) vd[i] = vs[i];
+    if (!h || !q || !k || !v || !a || !o || !g || !u || !sc) return -2;
+    float* kc = m->kc + l * nkv * m->max_seq * hd;
+    float* vc = m->vc + l * nkv * m->max_seq * hd;
+    for (int64_t t = 0; t < T; t++) rms_norm(x + t * H, m->rms1[l], H, m->eps, h + t * H);
+    rqo_linear_rows(m->wtype, W[0], nq, H, h, T, q, nthreads);
+    rqo_linear_rows(m->wtype, W[1], nk, H, h, T, k, nthreads);
+    rqo_linear_rows(m->wtype, W[2], nk, H, h, T, v, nthreads);
+    for (int64_t t = 0; t < T; t++) {
+        int64_t p = pos + t;
+        const float* c = m->cs + p * half;
+        const float* s = m->sn + p * half;
+        for (int64_t hh = 0; hh < nh; hh++) {
+            float* qh = q + (t * nh + hh) * hd;
+            for (int64_t i = 0; i < half; i++) {
+                float a0 = qh[i], b0 = qh[i + half];
+                qh[i] = a0 * c[i] - b0 * s[i];
+                qh[i + half] = a0 * s[i] + b0 * c[i];
             }
         }
-        float sq = sqrtf((float)hd);
-        for (int64_t t = 0; t < T; t++) {
-            int64_t L = pos + t + 1;
-            for (int64_t hh = 0; hh < nh; hh++) {
-                const float* qh = q + (t * nh + hh) * hd;
-                int64_t kh = hh / rep;
-                const float* K = kc + kh * m->max_seq * hd;
-                const float* V = vc + kh * m->max_seq * hd;
-                float mx = -INFINITY;
-                for (int64_t j = 0; j < L; j++) {
-                    float acc = 0.0f;
-                    for (int64_t d = 0; d < hd; d++) acc += qh[d] * K[j * hd + d];
-                    sc[j] = acc / sq;
-                    if (sc[j] > mx) mx = sc[j];
-                }
-                float sum = 0.0f;
-                for (int64_t j = 0; j < L; j++) { sc[j] = expf(sc[j] - mx); sum += sc[j]; }
-                for (int64_t j = 0; j < L; j++) sc[j] = sc[j] / sum;
-                float* ah = a + (t * nh + hh) * hd;
-                for (int64_t d = 0; d < hd; d++) {
-                    float acc = 0.0f;
-                    for (int64_t j = 0; j < L; j++) acc += sc[j] * V[j * hd + d];
-                    ah[d] = acc;
-                }
+        for (int64_t kh = 0; kh < nkv; kh++) {
+            const float* ks = k + (t * nkv + kh) * hd;
+            const float* vs = v + (t * nkv + kh) * hd;
+            float* kd = kc + (kh * m->max_seq + p) * hd;
+            float* vd = vc + (kh * m->max_seq + p) * hd;
+            for (int64_t i = 0; i < half; i++) {
+                float a0 = ks[i], b0 = ks[i + half];
+                kd[i] = a0 * c[i] - b0 * s[i];
+                kd[i + half] = a0 * s[i] + b0 * c[i];
+            }
+            for (int64_t i = 0; i < hd; i++) vd[i] = vs[i];
+        }
+    }
+    float sq = sqrtf((float)hd);
+    for (int64_t t = 0; t < T; t++) {
+        int64_t L = pos + t + 1;
+        for (int64_t hh = 0; hh < nh; hh++) {
+            const float* qh = q + (t * nh + hh) * hd;
+            int64_t kh = hh / rep;
+            const float* K = kc + kh * m->max_seq * hd;
+            const float* V = vc + kh * m->max_seq * hd;
+            float mx = -INFINITY;
+            for (int64_t j = 0; j < L; j++) {
+                float acc = 0.0f;
+                for (int64_t d = 0; d < hd; d++) acc += qh[d] * K[j * hd + d];
+                sc[j] = acc / sq;
+                if (sc[j] > mx) mx = sc[j];
+            }
+            float sum = 0.0f;
+            for (int64_t j = 0; j < L; j++) { sc[j] = expf(sc[j] - mx); sum += sc[j]; }
+            for (int64_t j = 0; j < L; j++) sc[j] = sc[j] / sum;
+            float* ah = a + (t * nh + hh) * hd;
+            for (int64_t d = 0; d < hd; d++) {
+                float acc = 0.0f;
+                for (int64_t j = 0; j < L; j++) acc += sc[j] * V[j * hd + d];
+                ah[d] = acc;
             }
         }
-        rqo_linear_threaded(m->wtype, W[3], H, nq, a, T, o, nthreads);
-        for (int64_t i = 0; i < T * H; i++) x[i] = o[i] + x[i];
-        for (int64_t t = 0; t < T; t++) rms_norm(x + t * H, m->rms2[l], H, m->eps, h + t * H);
-        rqo_linear_threaded(m->wtype, W[4], I, H, h, T, g, nthreads);
-        rqo_linear_threaded(m->wtype, W[5], I, H, h, T, u, nthreads);
-        for (int64_t i = 0; i < T * I; i++) g[i] = rqo_silu(g[i]) * u[i];
-        rqo_linear_threaded(m->wtype, W[6], H, I, g, T, o, nthreads);
-        for (int64_t i = 0; i < T * H; i++) x[i] = o[i] + x[i];
     }
-    rms_norm(x + (T - 1) * H, m->lnf, H, m->eps, h);
-    int32_t best = 0;
-    for (int64_t r = 0; r < m->vocab; r++) {
-        const uint16_t* row = m->head + r * H;
-        float acc = 0.0f;
-        for (int64_t i = 0; i < H; i++) acc += h[i] * rqo_f16_to_f32(row[i]);
-        lg[r] = acc;
-        if (acc > lg[best]) best = (int32_t)r;
-    }
-    if (logits_last) memcpy(logits_last, lg, sizeof(float) * (size_t)m->vocab);
-    if (next) *next = best;
-    free(x); free(h); free(q); free(k); free(v); free(a); free(o); free(g); free(u); free(sc); free(lg);
+    rqo_linear_rows(m->wtype, W[3], H, nq, a, T, o, nthreads);
+    for (int64_t i = 0; i < T * H; i++) x[i] = o[i] + x[i];
+    for (int64_t t = 0; t < T; t++) rms_norm(x + t * H, m->rms2[l], H, m->eps, h + t * H);
+    rqo_linear_rows(m->wtype, W[4], I, H, h, T, g, nthreads);
+    rqo_linear_rows(m->wtype, W[5], I, H, h, T, u, nthreads);
+    for (int64_t i = 0; i < T * I; i++) g[i] = rqo_silu(g[i]) * u[i];
+    rqo_linear_rows(m->wtype, W[6], H, I, g, T, o, nthreads);
+    for (int64_t i = 0; i < T * H; i++) x[i] = o[i] + x[i];
+    free(h); free(q); free(k); free(v); free(a); free(o); free(g); free(u); free(sc);
     return 0;
+}
+
+/* f16 -> f32 of every half, for the lm_head rows (same values as rqo_f16_to_f32) */
+static float g_f16_table[65536];
+static pthread_once_t g_f16_once = PTHREAD_ONCE_INIT;
+static void f16_table_init(void) {
+    for (uint32_t i = 0; i < 65536u; i++) g_f16_table[i] = rqo_f16_to_f32((uint16_t)i);
+}
+
+typedef struct {
+    const rqo_llama* m;
+    const float* hn;  /* [T][H] normed rows */
+    int64_t T;
+    float* lg;        /* [T][vocab] */
+    int64_t next;
+} head_job;
+
+static void* head_worker(void* arg) {
+    head_job* j = (head_job*)arg;
+    const int64_t H = j->m->H, V = j->m->vocab, chunk = 64;
+    for (;;) {
+        int64_t r0 = __atomic_fetch_add(&j->next, 1, __ATOMIC_RELAXED) * chunk;
+        if (r0 >= V) break;
+        int64_t r1 = r0 + chunk < V ? r0 + chunk : V;
+        for (int64_t r = r0; r < r1; r++) {
+            const uint16_t* row = j->m->head + r * H;
+            for (int64_t t = 0; t < j->T; t++) {
+                const float* h = j->hn + t * H;
+                float acc = 0.0f;
+                for (int64_t i = 0; i < H; i++) acc += h[i] * g_f16_table[row[i]];
+                j->lg[t * V + r] = acc;
+            }
+        }
+    }
+    return NULL;
+}
+
+/* ln_f and the F16 lm_head (src/streaming_quantized.rs:630-632) of every row
+ * of x[T][H]: logits[T][vocab] (may be NULL) and the first-index argmax of
+ * each row. */
+int rqo_llama_head(const rqo_llama* m, const float* x, int64_t T, float* logits, int32_t* argmax, int nthreads) {
+    const int64_t H = m->H, V = m->vocab;
+    pthread_once(&g_f16_once, f16_table_init);
+    float* hn = (float*)malloc(sizeof(float) * (size_t)(T * H));
+    float* lg = logits ? logits : (float*)malloc(sizeof(float) * (size_t)(T * V));
+    if (!hn || !lg) return -2;
+    for (int64_t t = 0; t < T; t++) rms_norm(x + t * H, m->lnf, H, m->eps, hn + t * H);
+    if (nthreads <= 0) nthreads = (int)sysconf(_SC_NPROCESSORS_ONLN);
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    head_job j = {m, hn, T, lg, 0};
+    pthread_t th[256];
+    int started = 0;
+    for (int t = 1; t < nthreads; t++)
+        if (pthread_create(&th[started], NULL, head_worker, &j) == 0) started++;
+    head_worker(&j);
+    for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
+    for (int64_t t = 0; t < T; t++) {
+        const float* r = lg + t * V;
+        int32_t best = 0;
+        for (int64_t v = 1; v < V; v++)
+            if (r[v] > r[best]) best = (int32_t)v;
+        argmax[t] = best;
+    }
+    free(hn);
+    if (!logits) free(lg);
+    return 0;
+}
+
+/* forward(input_ids, index_pos) (src/streaming_quantized.rs:622-633):
+ * logits_last [vocab] of the last position (may be NULL); next: argmax. */
+int rqo_llama_forward(rqo_llama* m, const int32_t* tokens, int64_t T, int64_t pos,
+                      float* logits_last, int32_t* next, int nthreads) {
+    if (pos + T > m->max_seq || T < 1) return -1;
+    float* x = (float*)malloc(sizeof(float) * (size_t)(T * m->H));
+    if (!x) return -2;
+    rqo_llama_embed(m, tokens, T, x);
+    int rc = 0;
+    for (int64_t l = 0; l < m->nl && !rc; l++) rc = rqo_llama_layer(m, l, x, T, pos, nthreads);
+    int32_t best = 0;
+    if (!rc) rc = rqo_llama_head(m, x + (T - 1) * m->H, 1, logits_last, &best, nthreads);
+    if (!rc && next) *next = best;
+    free(x);
+    return rc;
 }

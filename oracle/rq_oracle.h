@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-enum { RQO_Q4_0 = 2, RQO_Q8_0 = 8, RQO_Q2_K = 10, RQO_Q3_K = 11, RQO_Q4_K = 12, RQO_Q5_K = 13, RQO_Q6_K = 14 };
+enum { RQO_F16 = 1, RQO_Q4_0 = 2, RQO_Q8_0 = 8, RQO_Q2_K = 10, RQO_Q3_K = 11, RQO_Q4_K = 12, RQO_Q5_K = 13, RQO_Q6_K = 14 };
 
 uint16_t rqo_f32_to_f16(float f);
 float rqo_f16_to_f32(uint16_t h);
@@ -65,10 +65,22 @@ float rqo_dot_q4_0_avx2order(const uint8_t* w_row, const float* x_row, int64_t b
 int rqo_linear_threaded(int type, const uint8_t* blocks, int64_t out, int64_t in,
                         const float* x, int64_t M, float* y, int nthreads);
 
+/* The same products as rqo_linear_threaded (bit for bit), each weight row
+ * dequantized once for all M activation rows (the oracle's fast path). */
+int rqo_linear_rows(int type, const uint8_t* blocks, int64_t out, int64_t in, const float* x, int64_t M,
+                    float* y, int nthreads);
+
+/* ParallelLinear::forward (parallel_linear.rs:191-295): F16 weight w
+ * [out][in] (IEEE half bits) times f32 x [n][in], chunked as :223-225.
+ * avx2 = 1: the dot_f32_avx2_fma lane order (:64-94); 0: the scalar loop
+ * (:48-55).  nthreads <= 0 -> all cores. */
+int rqo_parallel_linear_f16(const uint16_t* w, int64_t out, int64_t in, const float* x, int64_t n,
+                            float* y, int avx2, int nthreads);
+
 /* ---- sparse MoE (streaming_mixtral.rs:280-319) ---- */
-/* Router logits in the canonical order the GPU router kernel uses
- * (32 strided f32 partials with fmaf, butterfly combine); see rq_oracle.c. */
-void rqo_router_logits(const float* x, int64_t T, int64_t H, const float* wr, int E, float* logits);
+/* Router logits: the gate is a ParallelLinear with F16 weights wr16 [E][H]
+ * (streaming_mixtral.rs:265,283), AVX2 lane order. */
+void rqo_router_logits(const float* x, int64_t T, int64_t H, const uint16_t* wr16, int E, float* logits);
 /* softmax + stable descending top-k with renormalised weights.
  * ids[T][k] in rank order, weights[T][k]. */
 void rqo_route_topk(const float* logits, int64_t T, int E, int k, int32_t* ids, float* weights);
@@ -76,11 +88,14 @@ void rqo_route_topk(const float* logits, int64_t T, int E, int k, int32_t* ids, 
  * holds token ids; slot_w[T*k] the matching routing weights. */
 void rqo_permute(const int32_t* ids, const float* weights, int64_t T, int E, int k,
                  int32_t* offsets, int32_t* rows, float* slot_w);
-/* Full layer: route -> permute -> SwiGLU experts (w1=gate, w3=up, w2=down,
- * all Q4_K) -> weighted combine in ascending expert order.
- * w1/w3 blocks: [E] pointers to [F][H] weights; w2: [E] pointers to [H][F]. */
+/* Full layer: route -> permute -> SwiGLU experts (w1=gate, w3=up, w2=down)
+ * -> weighted combine in ascending expert order.  w1/w3: [E] pointers to
+ * [F][H] weights; w2: [E] pointers to [H][F].  wtype = a GGML block type
+ * (quantized experts) or RQO_F16 (F16 half bits: the reference's own
+ * ParallelLinear experts, streaming_mixtral.rs:231-257).  wr16: F16 router
+ * weight [E][H]. */
 int rqo_moe_forward(const float* x, int64_t T, int64_t H, int64_t F, int E, int k,
-                    const float* wr, int wtype, const uint8_t* const* w1,
+                    const uint16_t* wr16, int wtype, const uint8_t* const* w1,
                     const uint8_t* const* w3, const uint8_t* const* w2, float* y,
                     int32_t* ids_out, int32_t* perm_out, int32_t* offsets_out,
                     int nthreads);
@@ -102,6 +117,13 @@ void rqo_llama_set_embedding(rqo_llama* m, const uint16_t* emb);
 void rqo_llama_set_head(rqo_llama* m, const float* ln_f, const uint16_t* lm_head);
 int rqo_llama_forward(rqo_llama* m, const int32_t* tokens, int64_t T, int64_t index_pos,
                       float* logits_last, int32_t* next, int nthreads);
+/* The forward in pieces, so a model too large for host memory can be run a
+ * layer at a time (set_layer, layer, drop the blocks): x[T][H] = embedding
+ * rows; one QBlock over x in place at positions pos..pos+T-1; final norm
+ * and lm_head of every row of x (logits [T][vocab] may be NULL). */
+void rqo_llama_embed(const rqo_llama* m, const int32_t* tokens, int64_t T, float* x);
+int rqo_llama_layer(rqo_llama* m, int64_t layer, float* x, int64_t T, int64_t pos, int nthreads);
+int rqo_llama_head(const rqo_llama* m, const float* x, int64_t T, float* logits, int32_t* argmax, int nthreads);
 
 #ifdef __cplusplus
 }

@@ -49,6 +49,8 @@ SIGNATURES = {
     "rq_dequantize": (I, [P, P, P, P]),
     "rq_linear": (I, [P, P, P, P, I64, P]),
     "rq_linear_noalloc": (I, [P, P, P, I64, P]),
+    "rq_ctx_status": (I, [P]),
+    "rq_linear_allreduce": (I, [P, P, P, P, I64, P]),
     "rq_linear_batch": (I, [P, I, PP, PP, PP, P]),
 }
 

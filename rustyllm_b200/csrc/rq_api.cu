@@ -8,6 +8,7 @@
 #include <algorithm>
 
 #include "rq_internal.cuh"
+#include "rq_p2p.cuh"
 
 namespace rq {
 
@@ -195,6 +196,59 @@ int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles) {
     return RQ_OK;
 }
 
+// Bytes of activation staging at the start of ctx->ws for rq_linear's
+// kernel choice at M rows.
+size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
+    const bool small_m = M >= kMinTensorM && mm_small_supported(w);
+    return small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
+}
+
+// y = x W^T for device-resident x, y (M rows): stages x at the start of
+// ctx->ws (small_m_staging_bytes) and runs the kernel rq_linear routes M to.
+// M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 9..16:
+// the split-K tcgen05 kernel, one pass over the weights; M = 4..8 and
+// 17..23: one mma.sync pass per 8 rows; M = 2, 3: the M=1 pipeline once per
+// row is faster (it streams at ~5 TB/s).
+int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, int64_t M, cudaStream_t st) {
+    uint8_t* ws = (uint8_t*)ctx->ws;
+    int rc;
+    if (M >= kMinTensorM && mm_small_supported(w)) {
+        const XH xh = xh_at(ws, M, w->in);
+        rc = launch_xh_stage(xd, M, w->in, xh, st);
+        if (!rc && M >= kMinTcgenM && mm_tc_supported(w)) {
+            const MMJobDesc job{w, 0, (int)M, yd, nullptr};
+            rc = launch_mm_tc(&job, 1, xh, M, ctx->sm_count, st, ctx->derr);
+        } else if (!rc && M >= kSkinnyMinM && M <= kSkinnyMaxM) {
+            const MMJobDesc job{w, 0, (int)M, yd, nullptr};
+            rc = launch_mm_skinny(ctx, &job, 1, xh, M, st, ctx->derr);
+        } else if (!rc) {
+            rc = launch_matmul_small(w, xh, M, yd, nullptr, ctx->sm_count, st, ctx->derr);
+        }
+        return rc;
+    }
+    XQ xq;
+    xq.planes = (int8_t*)ws;
+    xq.stats = (float4*)(ws + (((size_t)M * 3 * w->in + 255) & ~(size_t)255));
+    rc = launch_xquant(xd, M, w->in, xq, st);
+    if (!rc) rc = launch_linear(w, xq, yd, M, ctx->sm_count, st, ctx->derr);
+    return rc;
+}
+
+int queue_error_readback(rq_ctx* ctx, cudaStream_t st) {
+    return cuda_error(cudaMemcpyAsync(ctx->err_host, ctx->derr, sizeof(int), cudaMemcpyDeviceToHost, st),
+                      "error word copy");
+}
+
+int take_kernel_error(rq_ctx* ctx, cudaStream_t st, const char* what) {
+    if (*(volatile int*)ctx->err_host == 0) return RQ_OK;
+    *(volatile int*)ctx->err_host = 0;
+    int rc = cuda_error(cudaMemsetAsync(ctx->derr, 0, sizeof(int), st), "error word reset");
+    if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "error word reset");
+    if (rc) return rc;
+    return set_error(RQ_ERR_TIMEOUT, "%s: a kernel's bounded wait gave up after ~1 s (its outputs are incomplete)",
+                     what);
+}
+
 }  // namespace rq
 
 using namespace rq;
@@ -240,7 +294,33 @@ int rq_init(int device, rq_ctx** out) {
     c->ws = nullptr;
     c->ws_bytes = 0;
     c->sm_count = prop.multiProcessorCount;
+    e = cudaMalloc(&c->derr, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->derr, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaHostAlloc(&c->err_host, sizeof(int), cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+        if (c->derr) cudaFree(c->derr);
+        delete c;
+        return cuda_error(e, "rq_init: error word");
+    }
+    *c->err_host = 0;
     *out = c;
+    return RQ_OK;
+}
+
+int rq_ctx_status(rq_ctx* ctx) {
+    if (!ctx) return set_error(RQ_ERR_INVALID, "rq_ctx_status: NULL context");
+    DeviceGuard g(ctx->device);
+    int rc = cuda_error(cudaDeviceSynchronize(), "rq_ctx_status sync");
+    if (!rc) rc = cuda_error(cudaMemcpy(ctx->err_host, ctx->derr, sizeof(int), cudaMemcpyDeviceToHost),
+                             "error word copy");
+    if (!rc) rc = take_kernel_error(ctx, nullptr, "rq_ctx_status");
+    if (rc) return rc;
+    const int s = static_error_take(ctx->device);
+    if (s < 0) return s == -RQ_ERR_INVALID ? RQ_ERR_INVALID : RQ_ERR_CUDA;
+    if (s > 0)
+        return set_error(RQ_ERR_TIMEOUT,
+                         "rq_ctx_status: a bounded wait inside an rq_linear_noalloc kernel on device %d gave up "
+                         "after ~1 s (that call's y is incomplete)", ctx->device);
     return RQ_OK;
 }
 
@@ -251,6 +331,8 @@ int rq_destroy(rq_ctx* ctx) {
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->sk_ws) cudaFree(ctx->sk_ws);
     if (ctx->sk_cnt) cudaFree(ctx->sk_cnt);
+    if (ctx->derr) cudaFree(ctx->derr);
+    if (ctx->err_host) cudaFreeHost(ctx->err_host);
     delete ctx;
     return RQ_OK;
 }
@@ -407,20 +489,12 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
     float* const x_alias = static_cast<float*>(device_alias(x, &x_host));
     float* const y_alias = static_cast<float*>(device_alias(y, &y_host));
     const bool x_dev = x_alias != nullptr, y_dev = y_alias != nullptr;
-    // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 9..16:
-    // the split-K tcgen05 kernel, one pass over the weights; M = 4..8 and
-    // 17..23: one mma.sync pass per 8 rows; M = 2, 3: the M=1 pipeline once
-    // per row is faster (it streams at ~5 TB/s)
-    const bool small_m = M >= kMinTensorM && mm_small_supported(w);
-    const size_t xq_sz = small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
+    const size_t xq_sz = small_m_staging_bytes(w, M);
     const size_t x_sz = x_dev ? 0 : (size_t)(M * w->in) * sizeof(float);
     const size_t y_sz = y_dev ? 0 : (size_t)(M * w->out) * sizeof(float);
     int rc = ensure_workspace(ctx, xq_sz + x_sz + y_sz + 512);
     if (rc) return rc;
     uint8_t* ws = (uint8_t*)ctx->ws;
-    XQ xq;
-    xq.planes = (int8_t*)ws;
-    xq.stats = (float4*)(ws + (((size_t)M * 3 * w->in + 255) & ~(size_t)255));
     float* xd = x_dev ? x_alias : (float*)(ws + ((xq_sz + 255) & ~(size_t)255));
     float* yd = y_dev ? y_alias : (float*)((uint8_t*)xd + (x_dev ? 0 : ((x_sz + 255) & ~(size_t)255)));
     if (!y_dev && x_dev) yd = (float*)(ws + ((xq_sz + 255) & ~(size_t)255));
@@ -428,26 +502,52 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
         rc = cuda_error(cudaMemcpyAsync(xd, x, x_sz, cudaMemcpyHostToDevice, st), "x copy");
         if (rc) return rc;
     }
-    if (small_m) {
-        const XH xh = xh_at(ws, M, w->in);
-        rc = launch_xh_stage(xd, M, w->in, xh, st);
-        if (!rc && M >= kMinTcgenM && mm_tc_supported(w)) {
-            const MMJobDesc job{w, 0, (int)M, yd, nullptr};
-            rc = launch_mm_tc(&job, 1, xh, M, ctx->sm_count, st);
-        } else if (!rc && M >= kSkinnyMinM && M <= kSkinnyMaxM) {
-            const MMJobDesc job{w, 0, (int)M, yd, nullptr};
-            rc = launch_mm_skinny(ctx, &job, 1, xh, M, st);
-        } else if (!rc) {
-            rc = launch_matmul_small(w, xh, M, yd, nullptr, ctx->sm_count, st);
-        }
-    } else {
-        rc = launch_xquant(xd, M, w->in, xq, st);
-        if (!rc) rc = launch_linear(w, xq, yd, M, ctx->sm_count, st);
-    }
+    rc = linear_device(ctx, w, xd, yd, M, st);
     if (rc) return rc;
     if (!y_dev) rc = cuda_error(cudaMemcpyAsync(y, yd, y_sz, cudaMemcpyDeviceToHost, st), "y copy");
-    // host buffers: y is complete and x no longer read when the call returns
-    if (!rc && (x_host || y_host)) rc = cuda_error(cudaStreamSynchronize(st), "rq_linear sync");
+    // host buffers: y is complete and x no longer read when the call returns,
+    // and a kernel wait that gave up is reported here (device-only calls are
+    // asynchronous: rq_ctx_status reports it)
+    if (!rc && (x_host || y_host)) {
+        rc = queue_error_readback(ctx, st);
+        if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "rq_linear sync");
+        if (!rc) rc = take_kernel_error(ctx, st, "rq_linear");
+    }
+    return rc;
+}
+
+/* Row-parallel linear under tensor parallelism (no reference counterpart:
+ * the reference runs on one device): y = sum over ranks of x_r W_r^T. */
+int rq_linear_allreduce(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t M, void* stream) {
+    if (!ctx || !w || !x || !y) return set_error(RQ_ERR_INVALID, "rq_linear_allreduce: NULL argument");
+    if (M < 0) return set_error(RQ_ERR_INVALID, "rq_linear_allreduce: M = %lld", (long long)M);
+    if (!ctx->tp) return set_error(RQ_ERR_INVALID, "rq_linear_allreduce: no communicator (rq_tp_init)");
+    if (M == 0) return RQ_OK;
+    if (mem_kind(x) != Mem::Device || mem_kind(y) != Mem::Device)
+        return set_error(RQ_ERR_INVALID, "rq_linear_allreduce: x and y must be device memory");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    P2PArgs ar;
+    if (M == 1 && pipe_supported(w) && tp_fused_enabled(tp_world(ctx)) && tp_p2p_args(ctx, &ar)) {
+        int rc = ensure_workspace(ctx, xq_bytes(1, w->in));
+        if (rc) return rc;
+        XQ xq;
+        xq.planes = (int8_t*)ctx->ws;
+        xq.stats = (float4*)((uint8_t*)ctx->ws + (((size_t)3 * w->in + 255) & ~(size_t)255));
+        rc = launch_xquant(x, 1, w->in, xq, st);
+        if (rc) return rc;
+        const float* add = nullptr;
+        rc = launch_matvec_pipe(&w, &xq, &y, 1, ctx->sm_count, st, ctx->derr, &add, &ar);
+        if (rc != kPipeNotFusable) return rc;
+    }
+    // the partial product into the workspace's tail, then the all-reduce
+    const size_t stage = small_m_staging_bytes(w, M);
+    const size_t part_off = (stage + 255) & ~(size_t)255;
+    int rc = ensure_workspace(ctx, part_off + (size_t)(M * w->out) * sizeof(float));
+    if (rc) return rc;
+    float* part = (float*)((uint8_t*)ctx->ws + part_off);
+    rc = linear_device(ctx, w, x, part, M, st);
+    if (!rc) rc = tp_allreduce(ctx, part, y, M * w->out, 0, 0, st);
     return rc;
 }
 
@@ -493,7 +593,7 @@ int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const float* 
     XQ xqs[kMaxJobs];
     for (int j = 0; j < n; j++)
         xqs[j] = XQ{xq.planes + (int64_t)row_of[j] * 3 * in, xq.stats + (int64_t)row_of[j] * (in / 32)};
-    return launch_matvec_pipe(w, xqs, y, n, ctx->sm_count, st);
+    return launch_matvec_pipe(w, xqs, y, n, ctx->sm_count, st, ctx->derr);
 }
 
 }  // extern "C"

@@ -99,6 +99,12 @@ struct rq_ctx {
     size_t sk_ws_floats = 0;
     int* sk_cnt = nullptr;   // skinny matmul: arrivals per tile (kept at zero between launches)
     int sk_cnt_n = 0;
+    // Error word of the context's kernels: a bounded wait (mbarrier, peer
+    // flag) that gives up sets it to 1 and the kernel returns.  Synchronous
+    // calls read it back (err_host, page-locked) before returning;
+    // rq_ctx_status reads it for asynchronous ones.
+    int* derr = nullptr;
+    int* err_host = nullptr;
 };
 
 namespace rq {
@@ -111,6 +117,10 @@ int tp_allreduce(rq_ctx* ctx, const void* in, void* out, int64_t n, int dtype, i
 // the peer-memory exchange regions of the communicator, if it has them
 struct P2PArgs;
 bool tp_p2p_args(const rq_ctx* ctx, P2PArgs* a);
+// Whether a row-parallel M=1 matvec does its all-reduce inside the matvec
+// kernel (the fused epilogue; same bits as the separate kernel) at `world`
+// ranks.  RQ_TP_FUSED=1 / =0 in the environment forces it on / off.
+bool tp_fused_enabled(int world);
 void tp_destroy(rq_ctx* ctx);
 // all-gather of nbytes from every rank into out[world][nbytes]
 int tp_allgather_bytes(rq_ctx* ctx, const void* in, void* out, int64_t nbytes, cudaStream_t st);
@@ -131,6 +141,15 @@ int llama_load_gguf_dir(rq_ctx* ctx, rq_llama* m, const char* dir, int64_t n_lay
 int set_error(int code, const char* fmt, ...);
 int cuda_error(cudaError_t e, const char* what);
 int ensure_workspace(rq_ctx* ctx, size_t bytes);
+// Queue the copy of ctx's kernel error word to the host on st (before the
+// call's final synchronisation) ...
+int queue_error_readback(rq_ctx* ctx, cudaStream_t st);
+// ... and after that synchronisation: RQ_ERR_TIMEOUT (word cleared) when a
+// kernel's bounded wait gave up, else RQ_OK.
+int take_kernel_error(rq_ctx* ctx, cudaStream_t st, const char* what);
+// the error word of rq_linear_noalloc's kernels on device dev (rq_static.cu):
+// 1 if set since the last call (and cleared), 0 if not, < 0 on a CUDA error
+int static_error_take(int dev);
 
 // layout kernels (rq_layout.cu)
 int launch_repack(const rq_weight* w, const uint8_t* raw_dev, int64_t row0, int64_t rows,
@@ -193,7 +212,7 @@ int launch_mm_small(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int s
                     int* err = nullptr);
 // y[M][out] = x W^T (+ add) for M >= 2 staged rows, in tiles of 8 rows
 int launch_matmul_small(const rq_weight* w, XH xh, int64_t M, float* y, const float* add, int sm_count,
-                        cudaStream_t st);
+                        cudaStream_t st, int* err = nullptr);
 // Q4_K matmul on tcgen05 (rq_mm_tc.cu) for jobs of any M: 128 weight rows x
 // up to 128 tokens per tile, f32 accumulators in TMEM; same staged matrix and
 // job descriptors as launch_mm_small (no limit on M_j); err may be NULL.
@@ -227,6 +246,7 @@ int launch_xquant_rmsnorm(const float* x, const float* w, float eps, int64_t M, 
 int launch_xquant_swiglu(const float* gate, const float* up, int64_t M, int64_t in, XQ xq,
                          cudaStream_t st);
 int launch_xquant_rows(const float* const* xs, int n, int64_t in, XQ xq, cudaStream_t st);
-int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, cudaStream_t st);
+int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, cudaStream_t st,
+                  int* err = nullptr);
 
 }  // namespace rq

@@ -438,19 +438,19 @@ int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float
                 jy[nj] = ys[i] + t * ws[i]->out;
                 ja[nj] = adds && adds[i] ? adds[i] + t * ws[i]->out : nullptr;
                 if (++nj == kMaxJobs) {
-                    int rc = launch_matvec_pipe(jw, jx, jy, nj, sm, st, nullptr, ja);
+                    int rc = launch_matvec_pipe(jw, jx, jy, nj, sm, st, m->derr, ja);
                     if (rc) return rc;
                     nj = 0;
                 }
             }
-        return nj ? launch_matvec_pipe(jw, jx, jy, nj, sm, st, nullptr, ja) : RQ_OK;
+        return nj ? launch_matvec_pipe(jw, jx, jy, nj, sm, st, m->derr, ja) : RQ_OK;
     }
     for (int i = 0; i < n; i++) {
         if (adds && adds[i] && adds[i] != ys[i])
             return set_error(RQ_ERR_UNSUPPORTED, "llama: residual into a separate buffer needs the pipeline");
         if (adds && adds[i]) {
             // y += x W^T: compute into the scratch g, then add
-            int rc = launch_linear(ws[i], m->xq, m->g, T, sm, st);
+            int rc = launch_linear(ws[i], m->xq, m->g, T, sm, st, m->derr);
             if (rc) return rc;
             int64_t cnt = T * ws[i]->out;
             float* y = ys[i];
@@ -459,25 +459,11 @@ int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float
             rc = launch_simple((const void*)add_rows_kernel, dim3(256), dim3(256), 0, st, args, "add kernel");
             if (rc) return rc;
         } else {
-            int rc = launch_linear(ws[i], m->xq, ys[i], T, sm, st);
+            int rc = launch_linear(ws[i], m->xq, ys[i], T, sm, st, m->derr);
             if (rc) return rc;
         }
     }
     return RQ_OK;
-}
-
-// Whether the decode all-reduce runs inside the row-parallel matvec over
-// `world` ranks (the fused and separate forms give the same bits).  By
-// default at two ranks, the configuration it has been validated on;
-// RQ_TP_FUSED=1 in the environment enables it at any world size, =0 never.
-bool tp_fused_enabled(int world) {
-    static const int mode = [] {
-        const char* e = getenv("RQ_TP_FUSED");
-        if (e && strcmp(e, "0") == 0) return 0;
-        if (e && strcmp(e, "1") == 0) return 1;
-        return 2;  // default
-    }();
-    return mode == 1 || (mode == 2 && world == 2);
 }
 
 // x = x + x_in W^T for a row-parallel weight (o_proj, down_proj).  One rank:
@@ -498,7 +484,7 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
         const XQ xq = m->xq;
         float* y = m->x;
         const float* add = m->R == 0 ? m->x : nullptr;
-        const int rc = launch_matvec_pipe(w1, &xq, &y, 1, m->ctx->sm_count, st, nullptr, &add, &ar);
+        const int rc = launch_matvec_pipe(w1, &xq, &y, 1, m->ctx->sm_count, st, m->derr, &add, &ar);
         if (rc != kPipeNotFusable) return rc;
     }
     float* y1[1] = {m->part};
@@ -518,11 +504,11 @@ int run_mm(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* con
     std::vector<MMJobDesc> jobs;
     if (T >= kMinTcgenM) {
         for (int i = 0; i < n; i++) jobs.push_back(MMJobDesc{ws[i], 0, (int)T, ys[i], adds ? adds[i] : nullptr});
-        return launch_mm_tc(jobs.data(), (int)jobs.size(), m->xh, T, sm, st);
+        return launch_mm_tc(jobs.data(), (int)jobs.size(), m->xh, T, sm, st, m->derr);
     }
     if (T >= kSkinnyMinM && T <= kSkinnyMaxM) {
         for (int i = 0; i < n; i++) jobs.push_back(MMJobDesc{ws[i], 0, (int)T, ys[i], adds ? adds[i] : nullptr});
-        return launch_mm_skinny(m->ctx, jobs.data(), (int)jobs.size(), m->xh, T, st);
+        return launch_mm_skinny(m->ctx, jobs.data(), (int)jobs.size(), m->xh, T, st, m->derr);
     }
     for (int64_t t0 = 0; t0 < T; t0 += 8)
         for (int i = 0; i < n; i++) {
@@ -532,7 +518,7 @@ int run_mm(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* con
         }
     for (size_t b = 0; b < jobs.size(); b += kMaxJobs) {
         const int nj = (int)std::min<size_t>(kMaxJobs, jobs.size() - b);
-        int rc = launch_mm_small(&jobs[b], nj, m->xh, T, sm, st);
+        int rc = launch_mm_small(&jobs[b], nj, m->xh, T, sm, st, m->derr);
         if (rc) return rc;
     }
     return RQ_OK;
@@ -1039,6 +1025,7 @@ int rq_llama_forward(rq_llama* m, const int32_t* tokens, int64_t T, int64_t inde
     if (!rc && next_token)
         rc = cuda_error(cudaMemcpyAsync(next_token, m->tokens, 4, cudaMemcpyDeviceToHost, st), "token copy");
     if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "rq_llama_forward sync");
+    if (!rc) rc = rq_llama_status(m);  // a kernel wait that gave up
     return rc;
 }
 
@@ -1067,6 +1054,7 @@ int rq_llama_forward_all(rq_llama* m, const int32_t* tokens, int64_t T, int64_t 
                         "logits copy");
     if (!rc) rc = cuda_error(cudaMemcpyAsync(argmax, m->amax, (size_t)T * 4, cudaMemcpyDefault, st), "argmax copy");
     if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "rq_llama_forward_all sync");
+    if (!rc) rc = rq_llama_status(m);
     return rc;
 }
 
@@ -1093,7 +1081,8 @@ int rq_llama_status(rq_llama* m) {
     if (rc) return rc;
     if (e) {
         cudaMemset(m->derr, 0, 4);
-        return set_error(RQ_ERR_TIMEOUT, "decode step: a wait timed out (the step's outputs are invalid)");
+        return set_error(RQ_ERR_TIMEOUT, "llama: a kernel's bounded wait gave up after ~1 s (the outputs since the "
+                                         "last check are invalid)");
     }
     return RQ_OK;
 }

@@ -694,7 +694,7 @@ int launch_xh_stage_swiglu(const float* gate, const float* up, int64_t M, int64_
 bool mm_small_supported(const rq_weight* w) { return w->type == RQ_Q4_K; }
 
 int launch_matmul_small(const rq_weight* w, XH xh, int64_t M, float* y, const float* add, int sm_count,
-                        cudaStream_t st) {
+                        cudaStream_t st, int* err) {
     // tiles of kMP activation rows, up to kMaxJobs tiles per launch: each
     // launch reads the weights once per tile
     for (int64_t m0 = 0; m0 < M; m0 += (int64_t)kMP * kMaxJobs) {
@@ -703,7 +703,7 @@ int launch_matmul_small(const rq_weight* w, XH xh, int64_t M, float* y, const fl
         for (int64_t t0 = m0; t0 < M && n < kMaxJobs; t0 += kMP, n++)
             jobs[n] = MMJobDesc{w, (int)t0, (int)std::min<int64_t>(kMP, M - t0), y + t0 * w->out,
                                 add ? add + t0 * w->out : nullptr};
-        int rc = launch_mm_small(jobs, n, xh, M, sm_count, st);
+        int rc = launch_mm_small(jobs, n, xh, M, sm_count, st, err);
         if (rc) return rc;
     }
     return RQ_OK;

@@ -1,9 +1,9 @@
 // rq_moe.cu -- Mixtral sparse-MoE layer (SparseMoe::forward,
 // src/streaming_mixtral.rs:280-319) on the GPU with quantized experts.
 //
-//   route:    logits[t][e] = x[t] . router[e] (warp per (t, e), f32 partials
-//             in a fixed lane order so every run and the CPU oracle produce
-//             the same bits), softmax, top-k by descending score with ties to
+//   route:    logits[t][e] = x[t] . router[e] (warp per (t, e), the F16
+//             ParallelLinear gate of the reference in its exact lane order,
+//             so the logits carry its bits), softmax, top-k by descending score with ties to
 //             the lower expert index (the stable sort of :292-294),
 //             weights p / sum(p over the selected, in rank order) (:295-302)
 //   permute:  per expert, the tokens that chose it in ascending token order
@@ -27,7 +27,7 @@ struct rq_moe {
     rq_ctx* ctx;
     int E, k;
     int64_t H, F;
-    float* router;  // [E][H]
+    __half* router;  // [E][H], F16 as ParallelLinear::new stores it
     std::vector<const rq_weight*> w1, w3, w2;  // NULL for experts of other ranks (expert parallel)
     // per-forward routing buffers, T tokens (S = T k slots), grown on demand
     int64_t cap_t = 0;
@@ -62,8 +62,14 @@ struct rq_moe {
 namespace rq {
 namespace {
 
-// One CTA per token, one warp per expert (E <= 32).
-__global__ void router_kernel(const float* __restrict__ x, const float* __restrict__ wr, int64_t H,
+// One CTA per token, one warp per expert (E <= 32).  The gate is the
+// reference's ParallelLinear (streaming_mixtral.rs:265,283): F16 weights, and
+// dot_f32_avx2_fma's arithmetic (parallel_linear.rs:64-94), restated exactly:
+// lane c (c < 8) accumulates x[8i+c] * w[8i+c] with a fused multiply-add in
+// ascending i, the eight lane sums are added left to right, and a tail of
+// H % 8 elements adds x*w with two roundings.  So the logits carry the bits
+// of the reference's CPU gate.
+__global__ void router_kernel(const float* __restrict__ x, const __half* __restrict__ wr, int64_t H,
                               int E, int k, float* __restrict__ logits, int32_t* __restrict__ ids,
                               float* __restrict__ wts) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -72,21 +78,22 @@ __global__ void router_kernel(const float* __restrict__ x, const float* __restri
     const int64_t t = blockIdx.x;
     const int e = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (e < E) {
-        const float4* xv = reinterpret_cast<const float4*>(x + t * H);
-        const float4* wv = reinterpret_cast<const float4*>(wr + (int64_t)e * H);
+        const float* xr = x + t * H;
+        const __half* wrow = wr + (int64_t)e * H;
+        const int64_t chunks = H / 8;
         float acc = 0.0f;
-        for (int64_t i = lane; i < H / 4; i += 32) {  // chunks l, l+32, ... in component order
-            const float4 a = xv[i], b = wv[i];
-            acc = fmaf(a.x, b.x, acc);
-            acc = fmaf(a.y, b.y, acc);
-            acc = fmaf(a.z, b.z, acc);
-            acc = fmaf(a.w, b.w, acc);
+        if (lane < 8) {
+#pragma unroll 8
+            for (int64_t i = 0; i < chunks; i++)
+                acc = __fmaf_rn(xr[8 * i + lane], __half2float(wrow[8 * i + lane]), acc);
         }
+        float sum = -0.0f;
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) acc = acc + __shfl_xor_sync(0xffffffffu, acc, off);
+        for (int c = 0; c < 8; c++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, c));
+        for (int64_t i = chunks * 8; i < H; i++) sum = __fadd_rn(sum, __fmul_rn(xr[i], __half2float(wrow[i])));
         if (lane == 0) {
-            sl[e] = acc;
-            logits[t * E + e] = acc;
+            sl[e] = sum;
+            logits[t * E + e] = sum;
         }
     }
     __syncthreads();
@@ -199,7 +206,8 @@ __global__ void combine_kernel(const float* __restrict__ o, const float* __restr
         float acc = 0.0f;
         for (int r = 0; r < k; r++) {
             const int s = tok_slot[t * k + r];
-            acc = acc + o[(int64_t)s * H + c] * slot_w[s];
+            // index_add of outputs * weight (:313-315): two roundings
+            acc = __fadd_rn(acc, __fmul_rn(o[(int64_t)s * H + c], slot_w[s]));
         }
         y[t * H + c] = acc;
     }
@@ -306,31 +314,31 @@ struct JobList {
 // the split-K kernel: its piece boundaries depend on the other jobs of a
 // launch, and a token must give the same bits in a layer call as in an
 // expert-parallel one)
-int run_mm_jobs(const std::vector<MMJobDesc>& J, XH xh, int64_t rows, int sm, cudaStream_t st) {
+int run_mm_jobs(const std::vector<MMJobDesc>& J, XH xh, int64_t rows, int sm, cudaStream_t st, int* err) {
     std::vector<MMJobDesc> sm_jobs, tc_jobs;
     for (const MMJobDesc& j : J) (j.M >= kMinTcgenM ? tc_jobs : sm_jobs).push_back(j);
     for (size_t b = 0; b < sm_jobs.size(); b += kMaxJobs) {
         const int n = (int)std::min<size_t>(kMaxJobs, sm_jobs.size() - b);
-        int rc = launch_mm_small(&sm_jobs[b], n, xh, rows, sm, st);
+        int rc = launch_mm_small(&sm_jobs[b], n, xh, rows, sm, st, err);
         if (rc) return rc;
     }
     for (size_t b = 0; b < tc_jobs.size(); b += kMaxJobs) {
         const int n = (int)std::min<size_t>(kMaxJobs, tc_jobs.size() - b);
-        int rc = launch_mm_tc(&tc_jobs[b], n, xh, rows, sm, st);
+        int rc = launch_mm_tc(&tc_jobs[b], n, xh, rows, sm, st, err);
         if (rc) return rc;
     }
     return RQ_OK;
 }
 
-int run_jobs(const JobList& J, int sm, cudaStream_t st) {
+int run_jobs(const JobList& J, int sm, cudaStream_t st, int* err) {
     for (size_t b = 0; b < J.w.size(); b += kMaxJobs) {
         const int n = (int)std::min<size_t>(kMaxJobs, J.w.size() - b);
         int rc;
         if (pipe_supported(J.w[b])) {
-            rc = launch_matvec_pipe(&J.w[b], &J.x[b], &J.y[b], n, sm, st);
+            rc = launch_matvec_pipe(&J.w[b], &J.x[b], &J.y[b], n, sm, st, err);
         } else {
             rc = RQ_OK;
-            for (int j = 0; j < n && !rc; j++) rc = launch_linear(J.w[b + j], J.x[b + j], J.y[b + j], 1, sm, st);
+            for (int j = 0; j < n && !rc; j++) rc = launch_linear(J.w[b + j], J.x[b + j], J.y[b + j], 1, sm, st, err);
         }
         if (rc) return rc;
     }
@@ -425,8 +433,9 @@ int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& 
             down.y.push_back(out + r * H);
         }
     }
-    rc = run_jobs(up, sm, st);
-    if (!rc) rc = run_mm_jobs(upm, xhx, R, sm, st);
+    int* err = m->ctx->derr;
+    rc = run_jobs(up, sm, st, err);
+    if (!rc) rc = run_mm_jobs(upm, xhx, R, sm, st, err);
     cudaLaunchAttribute attr[1];
     if (!rc && any_mm) {
         cudaLaunchConfig_t cfg = pdl(dim3(1184), dim3(256), st, attr);
@@ -436,8 +445,8 @@ int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& 
     } else if (!rc) {
         rc = launch_xquant_swiglu(m->g, m->u, R, F, xqh, st);
     }
-    if (!rc) rc = run_jobs(down, sm, st);
-    if (!rc) rc = run_mm_jobs(downm, xhh, R, sm, st);
+    if (!rc) rc = run_jobs(down, sm, st, err);
+    if (!rc) rc = run_mm_jobs(downm, xhh, R, sm, st, err);
     return rc;
 }
 
@@ -448,7 +457,7 @@ int route(rq_moe* m, const float* xs, int64_t T, std::vector<int32_t>& offs, std
     const int E = m->E, k = m->k;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl(dim3((unsigned)T), dim3((unsigned)(32 * E)), st, attr);
-    int rc = cuda_error(cudaLaunchKernelEx(&cfg, router_kernel, xs, (const float*)m->router, m->H, E, k, m->logits,
+    int rc = cuda_error(cudaLaunchKernelEx(&cfg, router_kernel, xs, (const __half*)m->router, m->H, E, k, m->logits,
                                            m->ids, m->wts), "router kernel");
     if (!rc) {
         cudaLaunchConfig_t cfg2 = pdl(dim3(1), dim3(1024), st, attr);
@@ -499,7 +508,11 @@ int moe_call(rq_moe* m, const float* x, float* y, int64_t T, int32_t* ids_out, i
         rc = cuda_error(cudaMemcpyAsync(ids_out, m->ids, sizeof(int32_t) * (size_t)S, cudaMemcpyDefault, st),
                         "ids copy");
     if (!rc && perm_out) memcpy(perm_out, perm.data(), sizeof(int32_t) * (size_t)S);
-    if (!rc && (!y_dev || ids_out)) rc = cuda_error(cudaStreamSynchronize(st), "moe sync");
+    if (!rc && (!y_dev || ids_out)) {
+        rc = queue_error_readback(m->ctx, st);
+        if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "moe sync");
+        if (!rc) rc = take_kernel_error(m->ctx, st, "rq_moe_forward");
+    }
     return rc;
 }
 
@@ -544,10 +557,15 @@ int rq_moe_create(rq_ctx* ctx, int n_experts, int top_k, int64_t hidden, int64_t
     m->w1.assign(w1, w1 + n_experts);
     m->w3.assign(w3, w3 + n_experts);
     m->w2.assign(w2, w2 + n_experts);
-    cudaError_t e = cudaMalloc(&m->router, sizeof(float) * (size_t)(n_experts * hidden));
-    if (e == cudaSuccess)
-        e = cudaMemcpy(m->router, router_w, sizeof(float) * (size_t)(n_experts * hidden),
-                       is_device(router_w) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+    // ParallelLinear::new converts the gate weight to F16
+    // (parallel_linear.rs:128-131): round to nearest even
+    const size_t nr = (size_t)n_experts * (size_t)hidden;
+    std::vector<float> rf(nr);
+    std::vector<__half> rh(nr);
+    cudaError_t e = cudaMemcpy(rf.data(), router_w, sizeof(float) * nr, cudaMemcpyDefault);
+    for (size_t i = 0; e == cudaSuccess && i < nr; i++) rh[i] = __float2half_rn(rf[i]);
+    if (e == cudaSuccess) e = cudaMalloc(&m->router, sizeof(__half) * nr);
+    if (e == cudaSuccess) e = cudaMemcpy(m->router, rh.data(), sizeof(__half) * nr, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         if (m->router) cudaFree(m->router);
         delete m;

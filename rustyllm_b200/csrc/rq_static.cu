@@ -8,8 +8,10 @@
 // fragment its reservation), a host framework whose allocator owns every
 // device buffer (candle's CUDA device in rustyllm), or a latency-critical
 // decode loop where cudaMalloc/cudaFree may synchronise the device.  This
-// entry point runs the same kernels with the staging area in a file-scope
-// static __device__ array instead, and allocates nothing.
+// entry point stages the activations the same way in a file-scope static
+// __device__ array instead and runs the M=1 matvec kernels on every row
+// (rq_linear moves to the tensor-core kernels from M = 4 on), and allocates
+// nothing.
 //
 // The array is kStaticScratchBytes (2 MiB) on every GPU that loads librq,
 // held until the process exits.
@@ -27,12 +29,17 @@ constexpr size_t kStaticScratchBytes = (size_t)2 << 20;
 // `g_static_scratch` itself to a kernel: on the host that name is only a
 // stand-in; the device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+// The error word of rq_linear_noalloc's kernels (a bounded wait that gave up
+// sets it); rq_ctx_status on a context of the same device reads and clears it.
+// Resolved like the scratch array.
+static __device__ int g_static_err;
 
 constexpr int kMaxDevices = 64;
 
 struct StaticDeviceState {
     bool ready = false;
     void* scratch = nullptr;  // device address of g_static_scratch on this device
+    int* err = nullptr;       // device address of g_static_err on this device
     int sm_count = 0;
 };
 
@@ -50,10 +57,14 @@ int static_setup(int dev, StaticDeviceState** out) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
         if (e != cudaSuccess) return cuda_error(e, "rq_linear_noalloc: cudaGetSymbolAddress(scratch)");
+        void* pe = nullptr;
+        e = cudaGetSymbolAddress(&pe, g_static_err);
+        if (e != cudaSuccess) return cuda_error(e, "rq_linear_noalloc: cudaGetSymbolAddress(error word)");
         int sms = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return cuda_error(e, "rq_linear_noalloc: cudaDeviceGetAttribute");
         s.scratch = p;
+        s.err = (int*)pe;
         s.sm_count = sms;
         s.ready = true;
     }
@@ -71,6 +82,24 @@ bool on_device(const void* p, int dev) {
 }
 
 }  // namespace
+
+// rq_ctx_status's view of the error word of device dev (the device is current):
+// 1 = set since the last look (now cleared), 0 = not set or never used.
+int static_error_take(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) return -RQ_ERR_INVALID;
+    StaticDeviceState* s = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_states_mu);
+        if (!g_states[dev].ready) return 0;
+        s = &g_states[dev];
+    }
+    int v = 0;
+    if (cuda_error(cudaMemcpy(&v, s->err, sizeof(int), cudaMemcpyDeviceToHost), "noalloc error word copy"))
+        return -RQ_ERR_CUDA;
+    if (v && cuda_error(cudaMemset(s->err, 0, sizeof(int)), "noalloc error word reset")) return -RQ_ERR_CUDA;
+    return v ? 1 : 0;
+}
+
 }  // namespace rq
 
 using namespace rq;
@@ -107,7 +136,7 @@ extern "C" int rq_linear_noalloc(const rq_weight* w, const float* x, float* y, i
         xq.stats = (float4*)(base + (((size_t)M * 3 * w->in + 255) & ~(size_t)255));
         cudaStream_t st = (cudaStream_t)stream;
         rc = launch_xquant(x, M, w->in, xq, st);
-        if (!rc) rc = launch_linear(w, xq, y, M, s->sm_count, st);
+        if (!rc) rc = launch_linear(w, xq, y, M, s->sm_count, st, s->err);
     }
     if (prev >= 0 && prev != w->device) cudaSetDevice(prev);
     return rc;

@@ -259,6 +259,16 @@ int p2p_setup(TPComm* c) {
 int tp_world(const rq_ctx* ctx) { return ctx->tp ? ctx->tp->world : 1; }
 int tp_rank(const rq_ctx* ctx) { return ctx->tp ? ctx->tp->rank : 0; }
 
+bool tp_fused_enabled(int world) {
+    static const int mode = [] {
+        const char* e = getenv("RQ_TP_FUSED");
+        if (e && strcmp(e, "0") == 0) return 0;
+        if (e && strcmp(e, "1") == 0) return 1;
+        return 2;  // default
+    }();
+    return mode == 1 || (mode == 2 && world == 2);
+}
+
 bool tp_p2p_args(const rq_ctx* ctx, P2PArgs* a) {
     const TPComm* c = ctx->tp;
     if (!c || !c->comm || !c->p2p) return false;

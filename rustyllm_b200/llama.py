@@ -62,6 +62,10 @@ class StreamingLlamaQuantized:
         check(_lib.lib().rq_llama_load_gguf_dir(m.handle, str(shard_dir).encode()))
         return m
 
+    def layer_weights(self, layer: int) -> list:
+        """The QWeights (q, k, v, o, gate, up, down) set for a layer."""
+        return self._keep[layer]
+
     def set_embedding(self, embed_f16) -> None:
         e = np.ascontiguousarray(embed_f16).view(np.uint16)
         check(_lib.lib().rq_llama_set_embedding(self.handle, e.ctypes.data))
@@ -142,17 +146,19 @@ class StreamingLlamaQuantized:
 
 
 def random_model(cfg: dict, qtype: int, seed: int, device: int = 0, host_blocks: bool = False,
-                 tp: tuple[int, int] = (1, 0)):
+                 tp: tuple[int, int] = (1, 0), host_tensors: bool = False):
     """Random-init weights of the configured architecture, N(0, 0.02), on the
     device; linears quantized on the GPU.  With tp = (world, rank) every rank
     draws the same full tensors and keeps its shard, so any world size holds
     the same model.  Returns (model, host dict of the GGML bytes and F16/f32
-    tensors when host_blocks)."""
+    tensors when host_blocks; with host_tensors the same dict without the
+    block bytes -- layers hold (None, rms1, rms2) and the device weights of
+    layer l stay reachable as model.layer_weights(l))."""
     from .tp import LINEAR_SPLIT, shard
     world, rank = tp
     g = torch.Generator(device=f"cuda:{device}").manual_seed(seed)
     m = StreamingLlamaQuantized(cfg, device)
-    host = {"layers": []} if host_blocks else None
+    host = {"layers": []} if (host_blocks or host_tensors) else None
     for l in range(cfg["n_layers"]):
         ws = []
         for k, (o, i) in enumerate(layer_shapes(cfg)):
@@ -164,6 +170,8 @@ def random_model(cfg: dict, qtype: int, seed: int, device: int = 0, host_blocks:
         m.set_layer(l, ws, r1, r2)
         if host_blocks:
             host["layers"].append(([w.download() for w in ws], r1, r2))
+        elif host_tensors:
+            host["layers"].append((None, r1, r2))
     emb = (torch.randn(cfg["vocab"], cfg["hidden"], device=f"cuda:{device}", generator=g) * 0.02
            ).half().cpu().numpy()
     lnf = (1.0 + 0.1 * torch.randn(cfg["hidden"], device=f"cuda:{device}", generator=g)).cpu().numpy()
@@ -172,6 +180,6 @@ def random_model(cfg: dict, qtype: int, seed: int, device: int = 0, host_blocks:
     head = shard("col", head, world, rank).cpu().numpy()
     m.set_embedding(emb)
     m.set_head(lnf, head)
-    if host_blocks:
+    if host is not None:
         host.update(embed=emb, ln_f=lnf, lm_head=head)
     return m, host

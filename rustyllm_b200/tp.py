@@ -27,6 +27,18 @@ def init_from_torch(ctx, timeout_ms: int = 60000) -> tuple[int, int]:
     return world, rank
 
 
+def world_rank(ctx=None) -> tuple[int, int]:
+    """(world, rank) of the current torch.distributed group, (1, 0) without
+    one; the context's communicator (init_from_torch) spans that group."""
+    try:
+        import torch.distributed as dist
+        if dist.is_available() and dist.is_initialized():
+            return dist.get_world_size(), dist.get_rank()
+    except Exception:
+        pass
+    return 1, 0
+
+
 def finalize(ctx) -> None:
     _lib.lib().rq_tp_finalize(ctx.handle)
 

@@ -67,3 +67,47 @@ def test_moe_device_tensors_and_ties(oracle, rq_ctx):
     assert ids.tolist() == ids_ref.tolist() == [[2, 3]] * 6
     assert np.array_equal(perm, perm_ref)
     assert rel_l2(y.cpu().numpy(), y_ref) <= REL_L2_TOL
+
+
+@pytest.fixture(scope="module")
+def mixtral_layer(oracle, rq_ctx):
+    """The Mixtral-8x7B MoE layer of the bench: E=8, top-2, H=4096,
+    F=14336, Q4_K experts quantized on the device from N(0, 0.02) (the GPU
+    quantizer writes the oracle quantizer's bytes) and downloaded for the
+    oracle; router f32 N(0, 0.02)."""
+    import torch
+    from rustyllm_b200 import QWeight
+    E, H, F = 8, 4096, 14336
+    g = torch.Generator(device="cuda").manual_seed(4321)
+    wr = (torch.randn(E, H, device="cuda", generator=g) * 0.02).cpu().numpy()
+    experts, blocks = [], {"w1": [], "w2": [], "w3": []}
+    for _ in range(E):
+        trip = []
+        for name, (o, i) in (("w1", (F, H)), ("w2", (H, F)), ("w3", (F, H))):
+            w = QWeight.quantize(rq_ctx, 12, torch.randn(o, i, device="cuda", generator=g) * 0.02)
+            trip.append(w)
+            blocks[name].append(w.download())
+        experts.append(tuple(trip))
+    yield wr, blocks, experts
+    for trip in experts:
+        for w in trip:
+            w.free()
+
+
+@pytest.mark.parametrize("T", [1, 16, 512])
+def test_mixtral_geometry_matches_oracle(oracle, mixtral_layer, T):
+    """Routing ids and permutation bit-exact and outputs within 1e-4 at the
+    configured Mixtral shapes: T=1 (two M=1 experts), T=16 (about 4 tokens
+    per expert: mma.sync tiles and M=1 jobs), T=512 (about 128 per expert:
+    tcgen05 tiles)."""
+    from rustyllm_b200.mixtral import SparseMoe
+    wr, blocks, experts = mixtral_layer
+    moe = SparseMoe(wr, experts, top_k=2)
+    x = np.random.default_rng(900 + T).standard_normal((T, 4096)).astype(np.float32)
+    y, ids, perm = moe.forward_with_routing(x)
+    y_ref, ids_ref, perm_ref, _ = oracle.moe_forward(x, wr, 12, blocks["w1"], blocks["w3"], blocks["w2"],
+                                                    14336, k=2)
+    moe.close()
+    assert np.array_equal(ids, ids_ref)
+    assert np.array_equal(perm, perm_ref)
+    assert rel_l2(y, y_ref) <= REL_L2_TOL

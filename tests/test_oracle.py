@@ -140,9 +140,148 @@ def test_route_topk_semantics(oracle):
 
 
 def test_router_logits_close_to_f64(oracle):
+    """The gate holds its weight in F16 (ParallelLinear::new,
+    parallel_linear.rs:128-131)."""
     rng = np.random.default_rng(6)
     x = rng.standard_normal((5, 4096)).astype(np.float32)
     wr = (rng.standard_normal((8, 4096)) * 0.02).astype(np.float32)
     got = oracle.router_logits(x, wr)
-    ref = x.astype(np.float64) @ wr.astype(np.float64).T
+    ref = x.astype(np.float64) @ wr.astype(np.float16).astype(np.float64).T
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5)
+
+
+def _f32_nearest(v):
+    """The float32 nearest to the rational v, ties to even."""
+    from fractions import Fraction
+    f = np.float32(float(v))
+    best = None
+    for c in (np.nextafter(f, np.float32(-np.inf)), f, np.nextafter(f, np.float32(np.inf))):
+        d = abs(Fraction(float(c)) - v)
+        key = (d, int(np.array(c, np.float32).view(np.uint32)) & 1)
+        if best is None or key < best[0]:
+            best = (key, c)
+    return np.float32(best[1])
+
+
+def _parallel_linear_exact(w16, x, avx2):
+    """parallel_linear.rs:33-94 with every rounding done exactly: fused
+    multiply-adds round once, the scalar and tail products twice."""
+    from fractions import Fraction
+    w = w16.astype(np.float32)
+    out, n_in = w.shape
+    y = np.empty((x.shape[0], out), np.float32)
+    for b in range(x.shape[0]):
+        for j in range(out):
+            if avx2:
+                acc = [np.float32(0.0)] * 8
+                for i in range(n_in // 8):
+                    for c in range(8):
+                        k = 8 * i + c
+                        acc[c] = _f32_nearest(Fraction(float(x[b, k])) * Fraction(float(w[j, k]))
+                                              + Fraction(float(acc[c])))
+                s = np.float32(-0.0)
+                for c in range(8):
+                    s = np.float32(s + acc[c])
+                for k in range(n_in // 8 * 8, n_in):
+                    s = np.float32(s + np.float32(x[b, k] * w[j, k]))
+            else:
+                s = np.float32(0.0)
+                for k in range(n_in):
+                    s = np.float32(s + np.float32(x[b, k] * w[j, k]))
+            y[b, j] = s
+    return y
+
+
+@pytest.mark.parametrize("avx2", [True, False])
+def test_parallel_linear_restates_reference_exactly(oracle, avx2):
+    """The ParallelLinear restatement (a row of F16 weights converted to f32,
+    then dot_f32_avx2_fma or the scalar loop) against an exact-rounding
+    Python model of parallel_linear.rs:33-94, bit for bit; in = 44 exercises
+    the scalar tail."""
+    rng = np.random.default_rng(11)
+    for n_in in (40, 44):
+        w16 = (rng.standard_normal((5, n_in)) * 0.1).astype(np.float16)
+        x = rng.standard_normal((3, n_in)).astype(np.float32)
+        got = oracle.parallel_linear_f16(w16, x, avx2=avx2, nthreads=2)
+        want = _parallel_linear_exact(w16, x, avx2)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_parallel_linear_matches_f32_linear(oracle):
+    """parallel_linear.rs:304-328 matches_candle_linear_on_random_input:
+    within 1e-2 of the plain f32 linear on the F16 weight; and the bias-free
+    ones test of :330-343 (64 x 32 ones -> 32)."""
+    rng = np.random.default_rng(12)
+    w16 = (rng.standard_normal((128, 256)) * 0.1).astype(np.float16)
+    x = rng.standard_normal((3, 256)).astype(np.float32)
+    ref = x.astype(np.float64) @ w16.astype(np.float64).T
+    for avx2 in (True, False):
+        for nt in (1, 5):
+            got = oracle.parallel_linear_f16(w16, x, avx2=avx2, nthreads=nt)
+            assert np.abs(got - ref).max() < 1e-2
+    ones = oracle.parallel_linear_f16(np.ones((64, 32), np.float16), np.ones((1, 32), np.float32))
+    assert np.all(ones == 32.0)
+
+
+@pytest.mark.parametrize("qtype", [2, 8, 10, 11, 12, 13, 14])
+def test_linear_rows_bits_equal_threaded(oracle, qtype):
+    """The oracle's dequantize-once fast path gives rqo_linear_threaded's
+    bits for every type and several M."""
+    rng = np.random.default_rng(13 + qtype)
+    out, n_in = 41, 1024
+    b = oracle.quantize(qtype, (rng.standard_normal((out, n_in)) * 0.02).astype(np.float32))
+    for M in (1, 3, 8):
+        x = rng.standard_normal((M, n_in)).astype(np.float32)
+        a = oracle.linear_threaded(qtype, b, out, n_in, x, nthreads=3)
+        r = oracle.linear_rows(qtype, b, out, n_in, x, nthreads=4)
+        assert np.array_equal(a.view(np.uint32), r.view(np.uint32))
+
+
+def test_moe_f16_experts_close_to_f64(oracle):
+    """The reference's own Mixtral layer (ParallelLinear F16 experts and
+    gate) against a float64 restatement of SparseMoe::forward."""
+    rng = np.random.default_rng(14)
+    E, H, F, T, k = 4, 64, 96, 7, 2
+    wr = (rng.standard_normal((E, H)) * 0.3).astype(np.float32)
+    w1 = [(rng.standard_normal((F, H)) * 0.1).astype(np.float16) for _ in range(E)]
+    w3 = [(rng.standard_normal((F, H)) * 0.1).astype(np.float16) for _ in range(E)]
+    w2 = [(rng.standard_normal((H, F)) * 0.1).astype(np.float16) for _ in range(E)]
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    y, ids, perm, offs = oracle.moe_forward(x, wr, oracle.F16, w1, w3, w2, F, k=k)
+    lg = x.astype(np.float64) @ wr.astype(np.float16).astype(np.float64).T
+    p = np.exp(lg - lg.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    want = np.zeros((T, H))
+    for t in range(T):
+        top = sorted(range(E), key=lambda e: -p[t, e])[:k]
+        assert list(ids[t]) == top
+        for e in sorted(top):
+            g = w1[e].astype(np.float64) @ x[t]
+            u = w3[e].astype(np.float64) @ x[t]
+            want[t] += (p[t, e] / p[t, top].sum()) * (w2[e].astype(np.float64) @ (g / (1 + np.exp(-g)) * u))
+    assert np.abs(y - want).max() < 1e-4 * np.abs(want).max() + 1e-6
+
+
+def test_llama_teacher_forced_equals_incremental(oracle):
+    """forward_all over prompt + generated tokens reproduces, position by
+    position, the tokens and logits of the incremental greedy decode (the
+    check the 70B bench applies to its tokens)."""
+    rng = np.random.default_rng(15)
+    cfg = dict(hidden=256, intermediate=512, n_heads=4, n_kv_heads=2, head_dim=64, n_layers=2,
+               vocab=300, max_seq=40)
+    ref = oracle.OracleLlama(cfg, 12)
+    H, I = cfg["hidden"], cfg["intermediate"]
+    shapes = [(256, H), (128, H), (128, H), (H, 256), (I, H), (I, H), (H, I)]
+    for l in range(2):
+        bl = [oracle.quantize(12, (rng.standard_normal(s) * 0.05).astype(np.float32)) for s in shapes]
+        ref.set_layer(l, bl, (1 + 0.1 * rng.standard_normal(H)).astype(np.float32),
+                      (1 + 0.1 * rng.standard_normal(H)).astype(np.float32))
+    ref.set_embedding((rng.standard_normal((cfg["vocab"], H)) * 0.5).astype(np.float16))
+    ref.set_head((1 + 0.1 * rng.standard_normal(H)).astype(np.float32),
+                 (rng.standard_normal((cfg["vocab"], H)) * 0.1).astype(np.float16))
+    prompt = rng.integers(0, cfg["vocab"], 9).astype(np.int32)
+    gen = ref.generate(prompt, 6)
+    last_logits, _ = ref.forward(np.array([gen[-1]], np.int32), len(prompt) + 5)
+    logits, amax = ref.forward_all(np.concatenate([prompt, gen]).astype(np.int32), 0)
+    assert amax[len(prompt) - 1:len(prompt) + 5].tolist() == gen
+    assert np.array_equal(logits[-1].view(np.uint32), last_logits.view(np.uint32))
