@@ -220,8 +220,14 @@ RQ_API int rq_moe_free(rq_moe* m);
  * per-expert token buckets in ascending token order, SwiGLU experts, combine
  * in ascending expert order.  x, y host or device.  expert_ids_out [T][k]
  * (rank order) and perm_out [T*k] (tokens of expert 0, then expert 1, ...)
- * are optional host outputs.  Reads the routing table back to the host
- * before the expert products (as the reference does, :284-286). */
+ * are optional host outputs.  With T < 4 (decode and speculative-verify
+ * batches) no expert segment reaches the tensor-core kernels, so routing,
+ * permutation and the expert products stay on the device: with device x /
+ * y and no routing outputs the call is asynchronous on `stream` and can be
+ * captured in a CUDA graph (after one call at that T outside capture, which
+ * sizes the layer's buffers).  From T = 4 on, the per-expert token counts
+ * are read back to the host once (the reference reads its whole routing
+ * table there, :284-286) to pick each segment's kernel. */
 RQ_API int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
                           int32_t* expert_ids_out, int32_t* perm_out, void* stream);
 /* Expert-parallel forward over the communicator of ctx: expert e lives on

@@ -170,6 +170,19 @@ struct PipeJob {
     const float* add;  // optional residual: y = x W^T + add (may alias y)
     int64_t out;
 };
+// Jobs whose weight is chosen on the device (the sparse-MoE expert of a
+// routing slot): job j's weight is (qs[kind[j]][e], hdr[kind[j]][e]) with e =
+// slot_e[slot[j]] -- slot_e written by an earlier kernel in the stream, the
+// tables device arrays of per-expert pointers (kind: gate, up, down).  The
+// jobs' qs / hdr fields are then ignored; every table entry has the shape
+// and type of the launch's representative weights.
+struct PipeDevWeights {
+    const int32_t* slot_e;        // [slots] expert of each routing slot (device)
+    const uint8_t* const* qs[3];  // [kind] -> [E] (device)
+    const uint8_t* const* hdr[3];
+    int slot[kMaxJobs];           // routing slot of each job
+    int kind[kMaxJobs];
+};
 bool pipe_supported(const rq_weight* w);
 // With ar (one job, row-parallel under tensor parallelism): the partial y is
 // all-reduced over the ranks' NVLink exchange regions inside the kernel and
@@ -179,7 +192,8 @@ struct P2PArgs;
 constexpr int kPipeNotFusable = -1;
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err = nullptr,
-                       const float* const* adds = nullptr, const P2PArgs* ar = nullptr);
+                       const float* const* adds = nullptr, const P2PArgs* ar = nullptr,
+                       const PipeDevWeights* dw = nullptr);
 
 // small-M Q4_K matmul on the tensor cores (rq_mm_small.cu).  Activations are
 // staged per row as x / s = hi + lo (two f16 values per element, s a power of

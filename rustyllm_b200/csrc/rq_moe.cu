@@ -28,6 +28,7 @@ struct rq_moe {
     int E, k;
     int64_t H, F;
     __half* router;  // [E][H], F16 as ParallelLinear::new stores it
+    const uint8_t** wtab = nullptr;  // device [kind gate/up/down][qs/hdr][E] expert weight pointers
     std::vector<const rq_weight*> w1, w3, w2;  // NULL for experts of other ranks (expert parallel)
     // per-forward routing buffers, T tokens (S = T k slots), grown on demand
     int64_t cap_t = 0;
@@ -38,6 +39,7 @@ struct rq_moe {
     int32_t* perm = nullptr;     // [S] slot -> token (expert-major)
     float* slot_w = nullptr;     // [S]
     int32_t* tok_slot = nullptr; // [T][k] token -> its slots in ascending expert order
+    int32_t* slot_e = nullptr;   // [S] expert of each slot
     float* xd = nullptr;         // [T][H] device copy of host x
     float* yd = nullptr;
     float* xg = nullptr;         // [S][H] token rows in slot order (send order under EP)
@@ -123,12 +125,12 @@ __global__ void router_kernel(const float* __restrict__ x, const __half* __restr
 }
 
 // Single CTA: expert buckets in ascending token order.  offs[E+1];
-// perm[slot] = token; slot_w[slot]; tok_slot[t][r] = the token's slots sorted
-// by expert id.
+// perm[slot] = token; slot_w[slot]; slot_e[slot] = its expert; tok_slot[t][r]
+// = the token's slots sorted by expert id.
 __global__ void permute_kernel(const int32_t* __restrict__ ids, const float* __restrict__ wts,
                                int64_t T, int E, int k, int32_t* __restrict__ offs,
                                int32_t* __restrict__ perm, float* __restrict__ slot_w,
-                               int32_t* __restrict__ tok_slot) {
+                               int32_t* __restrict__ tok_slot, int32_t* __restrict__ slot_e) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     __shared__ int cnt[32];
@@ -173,6 +175,7 @@ __global__ void permute_kernel(const int32_t* __restrict__ ids, const float* __r
                 const int s = base[e] + rank[e];
                 perm[s] = (int32_t)t;
                 slot_w[s] = wts[t * k + r];
+                slot_e[s] = e;
                 slots[r] = s;
             }
             // ascending expert order == ascending slot order (buckets are expert-major)
@@ -267,6 +270,7 @@ int ensure_t(rq_moe* m, int64_t T, int world) {
     if (!rc) rc = grow(b, &m->perm, (size_t)S);
     if (!rc) rc = grow(b, &m->slot_w, (size_t)S);
     if (!rc) rc = grow(b, &m->tok_slot, (size_t)S);
+    if (!rc) rc = grow(b, &m->slot_e, (size_t)S);
     if (!rc) rc = grow(b, &m->xd, (size_t)(T * m->H));
     if (!rc) rc = grow(b, &m->yd, (size_t)(T * m->H));
     if (!rc) rc = grow(b, &m->xg, (size_t)(S * m->H));
@@ -450,9 +454,68 @@ int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& 
     return rc;
 }
 
-// Router and permutation of the T local tokens; offs and perm are copied to
-// the host (one stream synchronisation).
-int route(rq_moe* m, const float* xs, int64_t T, std::vector<int32_t>& offs, std::vector<int32_t>& perm,
+// out[s] = FFN_{expert of slot s}(rows[s]) for the S slots of a batch whose
+// every expert segment is shorter than kMinTensorM rows (T < kMinTensorM):
+// one M=1 pipeline job per slot, as expert_ffn would run them, but the
+// expert of each job is read by the matvec kernel from the routing table on
+// the device -- no host synchronisation, so the layer can be captured in a
+// CUDA graph.  Same jobs, same kernels, same bits as the host plan.
+int expert_ffn_slots(rq_moe* m, const float* rows, int64_t S, float* out, cudaStream_t st) {
+    const int64_t H = m->H, F = m->F;
+    const int sm = m->ctx->sm_count;
+    int* err = m->ctx->derr;
+    const XQ xqx = xq_view(m->xq_x, S, H), xqh = xq_view(m->xq_h, S, F);
+    PipeDevWeights dw;
+    memset(&dw, 0, sizeof dw);
+    dw.slot_e = m->slot_e;
+    for (int kind = 0; kind < 3; kind++) {
+        dw.qs[kind] = m->wtab + (size_t)(2 * kind) * m->E;
+        dw.hdr[kind] = m->wtab + (size_t)(2 * kind + 1) * m->E;
+    }
+    int rc = launch_xquant(rows, S, H, xqx, st);
+    // gate and up of each slot, kMaxJobs / 2 slots per launch
+    for (int64_t s0 = 0; !rc && s0 < S; s0 += kMaxJobs / 2) {
+        const int n = (int)std::min<int64_t>(kMaxJobs / 2, S - s0);
+        const rq_weight* ws[kMaxJobs];
+        XQ xs[kMaxJobs];
+        float* ys[kMaxJobs];
+        for (int i = 0; i < n; i++) {
+            const int64_t s = s0 + i;
+            const XQ xr{xqx.planes + s * 3 * H, xqx.stats + s * (H / 32)};
+            ws[2 * i] = m->w1[0];
+            ws[2 * i + 1] = m->w3[0];
+            xs[2 * i] = xs[2 * i + 1] = xr;
+            ys[2 * i] = m->g + s * F;
+            ys[2 * i + 1] = m->u + s * F;
+            dw.slot[2 * i] = dw.slot[2 * i + 1] = (int)s;
+            dw.kind[2 * i] = 0;
+            dw.kind[2 * i + 1] = 1;
+        }
+        rc = launch_matvec_pipe(ws, xs, ys, 2 * n, sm, st, err, nullptr, nullptr, &dw);
+    }
+    if (!rc) rc = launch_xquant_swiglu(m->g, m->u, S, F, xqh, st);
+    for (int64_t s0 = 0; !rc && s0 < S; s0 += kMaxJobs) {
+        const int n = (int)std::min<int64_t>(kMaxJobs, S - s0);
+        const rq_weight* ws[kMaxJobs];
+        XQ xs[kMaxJobs];
+        float* ys[kMaxJobs];
+        for (int i = 0; i < n; i++) {
+            const int64_t s = s0 + i;
+            ws[i] = m->w2[0];
+            xs[i] = XQ{xqh.planes + s * 3 * F, xqh.stats + s * (F / 32)};
+            ys[i] = out + s * H;
+            dw.slot[i] = (int)s;
+            dw.kind[i] = 2;
+        }
+        rc = launch_matvec_pipe(ws, xs, ys, n, sm, st, err, nullptr, nullptr, &dw);
+    }
+    return rc;
+}
+
+// Router and permutation of the T local tokens; with offs / perm given they
+// are copied to the host (one stream synchronisation), else everything
+// stays on the device.
+int route(rq_moe* m, const float* xs, int64_t T, std::vector<int32_t>* offs, std::vector<int32_t>* perm,
           cudaStream_t st) {
     const int E = m->E, k = m->k;
     cudaLaunchAttribute attr[1];
@@ -462,13 +525,14 @@ int route(rq_moe* m, const float* xs, int64_t T, std::vector<int32_t>& offs, std
     if (!rc) {
         cudaLaunchConfig_t cfg2 = pdl(dim3(1), dim3(1024), st, attr);
         rc = cuda_error(cudaLaunchKernelEx(&cfg2, permute_kernel, (const int32_t*)m->ids, (const float*)m->wts, T, E,
-                                           k, m->offs, m->perm, m->slot_w, m->tok_slot), "permute kernel");
+                                           k, m->offs, m->perm, m->slot_w, m->tok_slot, m->slot_e), "permute kernel");
     }
-    offs.assign((size_t)E + 1, 0);
-    perm.assign((size_t)(T * k), 0);
-    if (!rc) rc = cuda_error(cudaMemcpyAsync(offs.data(), m->offs, sizeof(int32_t) * (size_t)(E + 1),
+    if (!offs) return rc;
+    offs->assign((size_t)E + 1, 0);
+    perm->assign((size_t)(T * k), 0);
+    if (!rc) rc = cuda_error(cudaMemcpyAsync(offs->data(), m->offs, sizeof(int32_t) * (size_t)(E + 1),
                                              cudaMemcpyDeviceToHost, st), "offsets copy");
-    if (!rc) rc = cuda_error(cudaMemcpyAsync(perm.data(), m->perm, sizeof(int32_t) * (size_t)(T * k),
+    if (!rc) rc = cuda_error(cudaMemcpyAsync(perm->data(), m->perm, sizeof(int32_t) * (size_t)(T * k),
                                              cudaMemcpyDeviceToHost, st), "perm copy");
     if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "routing sync");
     return rc;
@@ -486,7 +550,7 @@ int combine(rq_moe* m, int64_t T, float* yd, cudaStream_t st) {
 // then after `body` y back to the host and the routing outputs.
 template <class Body>
 int moe_call(rq_moe* m, const float* x, float* y, int64_t T, int32_t* ids_out, int32_t* perm_out, cudaStream_t st,
-             int world, Body&& body) {
+             int world, bool host_plan, Body&& body) {
     int rc = ensure_t(m, T, world);
     if (rc) return rc;
     const int64_t H = m->H, S = T * m->k;
@@ -499,7 +563,7 @@ int moe_call(rq_moe* m, const float* x, float* y, int64_t T, int32_t* ids_out, i
     }
     float* yd = y_dev ? y : m->yd;
     std::vector<int32_t> offs, perm;
-    rc = route(m, xs, T, offs, perm, st);
+    rc = route(m, xs, T, host_plan ? &offs : nullptr, host_plan ? &perm : nullptr, st);
     if (!rc) rc = body(xs, offs, perm);
     if (!rc) rc = combine(m, T, yd, st);
     if (!rc && !y_dev)
@@ -507,8 +571,14 @@ int moe_call(rq_moe* m, const float* x, float* y, int64_t T, int32_t* ids_out, i
     if (!rc && ids_out)
         rc = cuda_error(cudaMemcpyAsync(ids_out, m->ids, sizeof(int32_t) * (size_t)S, cudaMemcpyDefault, st),
                         "ids copy");
-    if (!rc && perm_out) memcpy(perm_out, perm.data(), sizeof(int32_t) * (size_t)S);
-    if (!rc && (!y_dev || ids_out)) {
+    if (!rc && perm_out) {
+        if (host_plan)
+            memcpy(perm_out, perm.data(), sizeof(int32_t) * (size_t)S);
+        else
+            rc = cuda_error(cudaMemcpyAsync(perm_out, m->perm, sizeof(int32_t) * (size_t)S, cudaMemcpyDefault, st),
+                            "perm copy");
+    }
+    if (!rc && (!y_dev || ids_out || (perm_out && !host_plan))) {
         rc = queue_error_readback(m->ctx, st);
         if (!rc) rc = cuda_error(cudaStreamSynchronize(st), "moe sync");
         if (!rc) rc = take_kernel_error(m->ctx, st, "rq_moe_forward");
@@ -566,8 +636,22 @@ int rq_moe_create(rq_ctx* ctx, int n_experts, int top_k, int64_t hidden, int64_t
     for (size_t i = 0; e == cudaSuccess && i < nr; i++) rh[i] = __float2half_rn(rf[i]);
     if (e == cudaSuccess) e = cudaMalloc(&m->router, sizeof(__half) * nr);
     if (e == cudaSuccess) e = cudaMemcpy(m->router, rh.data(), sizeof(__half) * nr, cudaMemcpyHostToDevice);
+    // per-expert weight pointers for the device-planned path:
+    // [kind gate, up, down][qs, hdr][E]
+    std::vector<const uint8_t*> tab((size_t)6 * n_experts, nullptr);
+    for (int x = 0; x < n_experts; x++) {
+        const rq_weight* trip[3] = {w1[x], w3[x], w2[x]};
+        for (int kind = 0; kind < 3; kind++)
+            if (trip[kind]) {
+                tab[(size_t)(2 * kind) * n_experts + x] = trip[kind]->qs;
+                tab[(size_t)(2 * kind + 1) * n_experts + x] = trip[kind]->hdr;
+            }
+    }
+    if (e == cudaSuccess) e = cudaMalloc((void**)&m->wtab, sizeof(void*) * tab.size());
+    if (e == cudaSuccess) e = cudaMemcpy(m->wtab, tab.data(), sizeof(void*) * tab.size(), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         if (m->router) cudaFree(m->router);
+        if (m->wtab) cudaFree(m->wtab);
         delete m;
         return cuda_error(e, "rq_moe_create router copy");
     }
@@ -581,6 +665,7 @@ int rq_moe_free(rq_moe* m) {
     for (void* p : m->bufs_t) cudaFree(p);
     for (void* p : m->bufs_r) cudaFree(p);
     cudaFree(m->router);
+    if (m->wtab) cudaFree(m->wtab);
     delete m;
     return RQ_OK;
 }
@@ -596,12 +681,19 @@ int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
     Guard gd(m->ctx->device);
     cudaStream_t st = (cudaStream_t)stream;
     const int64_t S = T * m->k;
-    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, 1,
+    // below kMinTensorM tokens no expert gets a tensor-core segment, so the
+    // kernel of every slot is known without the routing: plan on the device
+    bool dev_plan = T < kMinTensorM;
+    for (int e = 0; e < m->E && dev_plan; e++)
+        dev_plan = pipe_supported(m->w1[(size_t)e]) && pipe_supported(m->w3[(size_t)e]) &&
+                   pipe_supported(m->w2[(size_t)e]);
+    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, 1, !dev_plan,
                     [&](const float* xs, const std::vector<int32_t>& offs, const std::vector<int32_t>&) {
                         int rc = ensure_r(m, S);
                         // token rows in slot (expert-major) order
                         if (!rc) rc = launch_gather(xs, m->perm, S, m->H, m->xg, st);
                         if (rc) return rc;
+                        if (dev_plan) return expert_ffn_slots(m, m->xg, S, m->o, st);
                         std::vector<Seg> segs;
                         for (int e = 0; e < m->E; e++) {
                             const int64_t n = offs[(size_t)e + 1] - offs[(size_t)e];
@@ -683,7 +775,7 @@ int rq_moe_forward_ep(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t 
         std::vector<int32_t> offs((size_t)E + 1, 0), perm;
         return body(x, offs, perm);
     }
-    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, W, body);
+    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, W, true, body);
 }
 
 }  // extern "C"

@@ -61,6 +61,8 @@ struct PipeParams {
     uint32_t stage_bytes, red_off, ring_off;
     int fuse;             // 1: all-reduce y over the ranks of ar (one job)
     P2PArgs ar;
+    int dev_w;            // 1: weights resolved on the device (dw)
+    PipeDevWeights dw;
 };
 
 __device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) {
@@ -156,11 +158,21 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
             const uint64_t pol = policy_evict_first();
             int it = 0, slot = 0, use = 0;  // stage count, ring slot, uses of the slot
             bool ok = true;
+            // weights chosen on the device: the routing table comes from an
+            // earlier kernel, so wait for it before the first copy
+            if (p.dev_w) asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int j = 0; j < p.njobs && ok; j++) {
                 const PipeJob& jb = p.jobs[j];
                 int64_t rb;
                 int nrows;
                 job_rows(jb, &rb, &nrows);
+                const uint8_t* jqs = jb.qs;
+                const uint8_t* jhdr = jb.hdr;
+                if (p.dev_w) {
+                    const int e = p.dw.slot_e[p.dw.slot[j]];
+                    jqs = p.dw.qs[p.dw.kind[j]][e];
+                    jhdr = p.dw.hdr[p.dw.kind[j]][e];
+                }
                 for (int r0 = 0; r0 < nrows; r0 += p.RS, it++, slot = slot + 1 == p.nstage ? 0 : slot + 1,
                          use += slot == 0) {
                     if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
@@ -169,8 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
                     const uint32_t qb = (uint32_t)rows * p.qrow, hb = (uint32_t)rows * p.hrow;
                     const uint32_t dst = smem_u32(ring) + (uint32_t)slot * p.stage_bytes;
                     mbar_expect_tx(full0 + 8 * slot, qb + hb);
-                    bulk_g2s(dst, jb.qs + row * p.qrow, qb, full0 + 8 * slot, pol);
-                    bulk_g2s(dst + (uint32_t)p.RS * p.qrow, jb.hdr + row * p.hrow, hb, full0 + 8 * slot, pol);
+                    bulk_g2s(dst, jqs + row * p.qrow, qb, full0 + 8 * slot, pol);
+                    bulk_g2s(dst + (uint32_t)p.RS * p.qrow, jhdr + row * p.hrow, hb, full0 + 8 * slot, pol);
                 }
             }
             // no bulk copy may still be landing when the CTA exits
@@ -287,7 +299,8 @@ bool pipe_supported(const rq_weight* w) {
 }
 
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
-                       int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar) {
+                       int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar,
+                       const PipeDevWeights* dw) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "matvec pipeline: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     TypeInfo ti = type_info(w0->type);
@@ -302,6 +315,8 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
         p.jobs[j].out = ws[j]->out;
     }
     p.err = err;
+    p.dev_w = dw ? 1 : 0;
+    if (dw) p.dw = *dw;
     p.nblk = w0->nblk;
     p.in = w0->in;
     p.S = (int)((w0->in + 2047) / 2048);

@@ -44,7 +44,7 @@ class SparseMoe:
         self.handle, self.E, self.k, self.H, self.F = h, E, top_k, H, F
         self._keep = experts
 
-    def forward_with_routing(self, xs):
+    def forward_with_routing(self, xs, routing: bool = True):
         torch_in = torch is not None and isinstance(xs, torch.Tensor)
         shape = tuple(xs.shape)
         if torch_in:
@@ -58,14 +58,18 @@ class SparseMoe:
             T = x2.shape[0]
             y = np.empty_like(x2)
             xp, yp, stream = x2.ctypes.data, y.ctypes.data, 0
-        ids = np.empty((T, self.k), dtype=np.int32)
-        perm = np.empty(T * self.k, dtype=np.int32)
+        ids = np.empty((T, self.k), dtype=np.int32) if routing else None
+        perm = np.empty(T * self.k, dtype=np.int32) if routing else None
         fwd = _lib.lib().rq_moe_forward_ep if self.expert_parallel else _lib.lib().rq_moe_forward
-        check(fwd(self.ctx.handle, self.handle, xp, yp, T, ids.ctypes.data, perm.ctypes.data, stream))
+        check(fwd(self.ctx.handle, self.handle, xp, yp, T, ids.ctypes.data if routing else None,
+                  perm.ctypes.data if routing else None, stream))
         return y.reshape(shape), ids, perm
 
     def forward(self, xs):
-        return self.forward_with_routing(xs)[0]
+        """The layer output.  With CUDA tensors and fewer than four tokens the
+        call stays on the device (no host synchronisation) and can be captured
+        in a CUDA graph once a first call at that token count has run."""
+        return self.forward_with_routing(xs, routing=False)[0]
 
     __call__ = forward
 
