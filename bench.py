@@ -667,9 +667,9 @@ def verify_decode(model, host: dict, cfg: dict, prompt: np.ndarray, toks: list) 
             "top1_top2_margins": [round(float(m), 5) for m in margins],
             "min_margin": round(float(min(margins)), 5),
             "logit_std": round(float(logits[p0:].std()), 4),
-            "verify_s": round(time.perf_counter() - t0, 1),
-            "verify_note": "oracle rqo_llama_layer per layer on the downloaded blocks, prompt + generated "
-                           "tokens teacher-forced (positions 19..34); logits of the F16 lm_head"}, layer0
+            "oracle_check_s": round(time.perf_counter() - t0, 1),
+            "oracle_check_note": "oracle rqo_llama_layer per layer on the downloaded blocks, prompt + generated "
+                                 "tokens teacher-forced (positions 19..34); logits of the F16 lm_head"}, layer0
 
 
 def decode_70b(device: int, pk, new_tokens: int = 16, prompt_len: int = 20, pg=None,
