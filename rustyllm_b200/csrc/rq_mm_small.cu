@@ -368,6 +368,10 @@ struct MMLane {
     const float* bs1;
 };
 
+// PAIR (jobs of at most 4 rows): MMA column 2t + h is half h (hi, lo) of
+// token t, so one MMA serves both halves; thread (g, t) loads half g & 1 of
+// token g >> 1 (L.xrow points at that plane) and the block sums of token t.
+template <bool PAIR>
 __device__ __forceinline__ BFrag load_b(const MMLane& L, int64_t in, int c) {
     const int64_t e0 = (int64_t)c * (kCS * 256) + 256 * L.sbl + 64 * L.gq;
     BFrag b;
@@ -376,12 +380,20 @@ __device__ __forceinline__ BFrag load_b(const MMLane& L, int64_t in, int c) {
         b.s0 = b.s1 = make_float2(0.f, 0.f);
         return b;
     }
-    b.lh = ldg128(L.xrow + e0);
-    b.ll = ldg128(L.xrow + in + e0);
-    b.hh = ldg128(L.xrow + e0 + 32);
-    b.hl = ldg128(L.xrow + in + e0 + 32);
-    b.s0 = ldg64f(L.bs0 + e0 / 32);
-    b.s1 = ldg64f(L.bs1 + e0 / 32);
+    if constexpr (PAIR) {
+        b.lh = ldg128(L.xrow + e0);
+        b.hh = ldg128(L.xrow + e0 + 32);
+        b.ll = b.hl = make_uint4(0u, 0u, 0u, 0u);
+        b.s0 = ldg64f(L.bs0 + e0 / 32);
+        b.s1 = make_float2(0.f, 0.f);
+    } else {
+        b.lh = ldg128(L.xrow + e0);
+        b.ll = ldg128(L.xrow + in + e0);
+        b.hh = ldg128(L.xrow + e0 + 32);
+        b.hl = ldg128(L.xrow + in + e0 + 32);
+        b.s0 = ldg64f(L.bs0 + e0 / 32);
+        b.s1 = ldg64f(L.bs1 + e0 / 32);
+    }
     return b;
 }
 
@@ -405,7 +417,9 @@ __device__ __forceinline__ void load_pair(PairOps& o, int rg0, uint32_t st, uint
 }
 
 // Row groups rg0 and rg0+1 (the second may lie past the block's ng: it reads
-// stale shared memory and its sums are discarded).
+// stale shared memory and its sums are discarded).  acc[rg][i]: weight row
+// 2g + (i >> 1) of the group; token 2t + (i & 1), or with PAIR token t (i < 2).
+template <bool PAIR>
 __device__ __forceinline__ void compute_pair(float (&acc)[kRG][4], int rg0, const PairOps& o, const BFrag& b) {
     float dl[2][4], dh[2][4];
 #pragma unroll
@@ -430,22 +444,40 @@ __device__ __forceinline__ void compute_pair(float (&acc)[kRG][4], int rg0, cons
             const uint32_t ha2 = v0 & 0x00F000F0u, ha3 = v1 & 0x00F000F0u;
             hmma(dl[k], la0, la1, la2, la3, bh0, bh1);
             hmma(dh[k], ha0, ha1, ha2, ha3, ch0, ch1);
-            hmma(dl[k], la0, la1, la2, la3, bl0, bl1);
-            hmma(dh[k], ha0, ha1, ha2, ha3, cl0, cl1);
+            if constexpr (!PAIR) {
+                hmma(dl[k], la0, la1, la2, la3, bl0, bl1);
+                hmma(dh[k], ha0, ha1, ha2, ha3, cl0, cl1);
+            }
         }
     }
 #pragma unroll
     for (int k = 0; k < 2; k++) {
+        if constexpr (PAIR) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint4 q = (i >> 1) ? o.q1[k] : o.q0[k];
-            const float bsl = (i & 1) ? b.s1.x : b.s0.x, bsh = (i & 1) ? b.s1.y : b.s0.y;
-            float a = acc[rg0 + k][i];
-            a = fmaf(__uint_as_float(q.x), dl[k][i], a);
-            a = fmaf(__uint_as_float(q.y), dh[k][i], a);
-            a = fmaf(-__uint_as_float(q.z), bsl, a);
-            a = fmaf(-__uint_as_float(q.w), bsh, a);
-            acc[rg0 + k][i] = a;
+            for (int j = 0; j < 2; j++) {
+                const uint4 q = j ? o.q1[k] : o.q0[k];
+                // columns 2t, 2t+1 are the hi and lo halves of token t
+                const float vl = dl[k][2 * j] + dl[k][2 * j + 1];
+                const float vh = dh[k][2 * j] + dh[k][2 * j + 1];
+                float a = acc[rg0 + k][j];
+                a = fmaf(__uint_as_float(q.x), vl, a);
+                a = fmaf(__uint_as_float(q.y), vh, a);
+                a = fmaf(-__uint_as_float(q.z), b.s0.x, a);
+                a = fmaf(-__uint_as_float(q.w), b.s0.y, a);
+                acc[rg0 + k][j] = a;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint4 q = (i >> 1) ? o.q1[k] : o.q0[k];
+                const float bsl = (i & 1) ? b.s1.x : b.s0.x, bsh = (i & 1) ? b.s1.y : b.s0.y;
+                float a = acc[rg0 + k][i];
+                a = fmaf(__uint_as_float(q.x), dl[k][i], a);
+                a = fmaf(__uint_as_float(q.y), dh[k][i], a);
+                a = fmaf(-__uint_as_float(q.z), bsl, a);
+                a = fmaf(-__uint_as_float(q.w), bsh, a);
+                acc[rg0 + k][i] = a;
+            }
         }
     }
 }
@@ -475,6 +507,7 @@ __device__ __forceinline__ void issue_stage(const MMParams& p, const Sched& s, u
 
 // Warp 0 streams the stages; warps 1..8 consume them.  9 warps: one
 // scheduler holds 3 of them, so 168 registers per thread at most.
+template <bool PAIR>
 __global__ void __launch_bounds__(kThreadsMM, 1) mm_q4k_kernel(const __grid_constant__ MMParams p) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled boxes
@@ -556,19 +589,26 @@ __global__ void __launch_bounds__(kThreadsMM, 1) mm_q4k_kernel(const __grid_cons
     while (cs.valid) {
         const MMJob& jb = p.jobs[cs.j];
         if (cs.c == 0) {  // a new row block
-            const int tb = jb.tok0 + min(L.g, jb.M - 1);
-            L.xrow = p.xh + (int64_t)tb * 2 * p.in + 8 * L.t;
-            L.bs0 = p.xbsum + (int64_t)(jb.tok0 + min(2 * L.t, jb.M - 1)) * (p.in / 32);
-            L.bs1 = p.xbsum + (int64_t)(jb.tok0 + min(2 * L.t + 1, jb.M - 1)) * (p.in / 32);
+            if constexpr (PAIR) {
+                const int tb = jb.tok0 + min(L.g >> 1, jb.M - 1);
+                L.xrow = p.xh + (int64_t)tb * 2 * p.in + (L.g & 1) * p.in + 8 * L.t;
+                L.bs0 = p.xbsum + (int64_t)(jb.tok0 + min(L.t, jb.M - 1)) * (p.in / 32);
+                L.bs1 = L.bs0;
+            } else {
+                const int tb = jb.tok0 + min(L.g, jb.M - 1);
+                L.xrow = p.xh + (int64_t)tb * 2 * p.in + 8 * L.t;
+                L.bs0 = p.xbsum + (int64_t)(jb.tok0 + min(2 * L.t, jb.M - 1)) * (p.in / 32);
+                L.bs1 = p.xbsum + (int64_t)(jb.tok0 + min(2 * L.t + 1, jb.M - 1)) * (p.in / 32);
+            }
 #pragma unroll
             for (int rg = 0; rg < kRG; rg++)
 #pragma unroll
                 for (int i = 0; i < 4; i++) acc[rg][i] = 0.0f;
-            bcur = load_b(L, p.in, 0);
+            bcur = load_b<PAIR>(L, p.in, 0);
         }
         const int ng = cs.ng;
         BFrag bnext = bcur;
-        if (cs.c + 1 < p.nchunk) bnext = load_b(L, p.in, cs.c + 1);
+        if (cs.c + 1 < p.nchunk) bnext = load_b<PAIR>(L, p.in, cs.c + 1);
         if (ok && !mbar_wait(full0 + 8 * slot, phase)) {
             ok = false;
             if (lane == 0 && p.err) atomicExch(p.err, 1);
@@ -598,7 +638,7 @@ __global__ void __launch_bounds__(kThreadsMM, 1) mm_q4k_kernel(const __grid_cons
                 if (rg < ng) {
                     PairOps ops;
                     load_pair(ops, rg, st, dec, L);
-                    compute_pair(acc, rg, ops, bcur);
+                    compute_pair<PAIR>(acc, rg, ops, bcur);
                 }
             }
         }
@@ -614,10 +654,18 @@ __global__ void __launch_bounds__(kThreadsMM, 1) mm_q4k_kernel(const __grid_cons
 #pragma unroll
             for (int rg = 0; rg < kRG; rg++) {
                 if (rg < ng) {
+                    if constexpr (PAIR) {
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const int row = rg * 16 + 2 * L.g + (i >> 1);
-                        red[(cw * kRG * 16 + row) * kMP + 2 * L.t + (i & 1)] = acc[rg][i];
+                        for (int j = 0; j < 2; j++) {
+                            const int row = rg * 16 + 2 * L.g + j;
+                            red[(cw * kRG * 16 + row) * kMP + L.t] = acc[rg][j];
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int row = rg * 16 + 2 * L.g + (i >> 1);
+                            red[(cw * kRG * 16 + row) * kMP + 2 * L.t + (i & 1)] = acc[rg][i];
+                        }
                     }
                 }
             }
@@ -753,11 +801,17 @@ int launch_mm_small(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int s
     const size_t smem = 1024 + kBarRegion + 2 * kDecBytes + (size_t)p.nstage * kStageBytes;
     const int grid = (int)std::min<int64_t>(gtot, sm_count);
 
+    // jobs of at most kMP / 2 rows put both activation halves in one MMA
+    bool pair = true;
+    for (int j = 0; j < njobs; j++) pair = pair && jobs[j].M <= kMP / 2;
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(mm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudgetMM);
+        cudaError_t e = cudaFuncSetAttribute(mm_q4k_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemBudgetMM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(mm_q4k_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudgetMM);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(small-M matmul)");
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -771,7 +825,9 @@ int launch_mm_small(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_error(cudaLaunchKernelEx(&cfg, mm_q4k_kernel, p), "small-M matmul kernel");
+    return cuda_error(pair ? cudaLaunchKernelEx(&cfg, mm_q4k_kernel<true>, p)
+                           : cudaLaunchKernelEx(&cfg, mm_q4k_kernel<false>, p),
+                      "small-M matmul kernel");
 }
 
 }  // namespace rq
