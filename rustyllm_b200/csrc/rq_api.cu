@@ -205,28 +205,13 @@ size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
 
 // y = x W^T for device-resident x, y (M rows): stages x at the start of
 // ctx->ws (small_m_staging_bytes) and runs the kernel rq_linear routes M to.
-// x_local: x is in device memory (not page-locked host memory read over the
-// bus), so the matvec may stage it itself -- every CTA reads the row.
 // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 9..16:
 // the split-K tcgen05 kernel, one pass over the weights; M = 4..8 and
 // 17..23: one mma.sync pass per 8 rows; M = 2, 3: the M=1 pipeline once per
 // row is faster (it streams at ~5 TB/s).
-int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, int64_t M, cudaStream_t st,
-                  bool x_local = true) {
+int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, int64_t M, cudaStream_t st) {
     uint8_t* ws = (uint8_t*)ctx->ws;
     int rc;
-    if (x_local && M < kMinTensorM && M <= kMaxJobs && pipe_fused_staging(w)) {
-        // one pipeline job per row, each staging its row in the matvec
-        const rq_weight* wj[kMaxJobs];
-        XSrc src[kMaxJobs];
-        float* yj[kMaxJobs];
-        for (int64_t m = 0; m < M; m++) {
-            wj[m] = w;
-            src[m] = XSrc{kXPlain, xd + m * w->in, nullptr, 0.0f};
-            yj[m] = yd + m * w->out;
-        }
-        return launch_matvec_pipe_src(wj, src, yj, (int)M, ctx->sm_count, st, ctx->derr);
-    }
     if (M >= kMinTensorM && mm_small_supported(w)) {
         const XH xh = xh_at(ws, M, w->in);
         rc = launch_xh_stage(xd, M, w->in, xh, st);
@@ -517,8 +502,7 @@ int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, int64_t
         rc = cuda_error(cudaMemcpyAsync(xd, x, x_sz, cudaMemcpyHostToDevice, st), "x copy");
         if (rc) return rc;
     }
-    // page-locked host x is read once by the staging kernel, not by every CTA
-    rc = linear_device(ctx, w, xd, yd, M, st, !(x_host && x_dev));
+    rc = linear_device(ctx, w, xd, yd, M, st);
     if (rc) return rc;
     if (!y_dev) rc = cuda_error(cudaMemcpyAsync(y, yd, y_sz, cudaMemcpyDeviceToHost, st), "y copy");
     // host buffers: y is complete and x no longer read when the call returns,
@@ -545,21 +529,15 @@ int rq_linear_allreduce(rq_ctx* ctx, const rq_weight* w, const float* x, float* 
     cudaStream_t st = (cudaStream_t)stream;
     P2PArgs ar;
     if (M == 1 && pipe_supported(w) && tp_fused_enabled(tp_world(ctx)) && tp_p2p_args(ctx, &ar)) {
+        int rc = ensure_workspace(ctx, xq_bytes(1, w->in));
+        if (rc) return rc;
+        XQ xq;
+        xq.planes = (int8_t*)ctx->ws;
+        xq.stats = (float4*)((uint8_t*)ctx->ws + (((size_t)3 * w->in + 255) & ~(size_t)255));
+        rc = launch_xquant(x, 1, w->in, xq, st);
+        if (rc) return rc;
         const float* add = nullptr;
-        int rc;
-        if (pipe_fused_staging(w)) {
-            const XSrc src{kXPlain, x, nullptr, 0.0f};
-            rc = launch_matvec_pipe_src(&w, &src, &y, 1, ctx->sm_count, st, ctx->derr, &add, &ar);
-        } else {
-            rc = ensure_workspace(ctx, xq_bytes(1, w->in));
-            if (rc) return rc;
-            XQ xq;
-            xq.planes = (int8_t*)ctx->ws;
-            xq.stats = (float4*)((uint8_t*)ctx->ws + (((size_t)3 * w->in + 255) & ~(size_t)255));
-            rc = launch_xquant(x, 1, w->in, xq, st);
-            if (rc) return rc;
-            rc = launch_matvec_pipe(&w, &xq, &y, 1, ctx->sm_count, st, ctx->derr, &add, &ar);
-        }
+        rc = launch_matvec_pipe(&w, &xq, &y, 1, ctx->sm_count, st, ctx->derr, &add, &ar);
         if (rc != kPipeNotFusable) return rc;
     }
     // the partial product into the workspace's tail, then the all-reduce
@@ -594,11 +572,6 @@ int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const float* 
             if (rc) return rc;
         }
         return RQ_OK;
-    }
-    if (pipe_fused_staging(w[0])) {  // every job stages its row in the matvec
-        XSrc src[kMaxJobs];
-        for (int j = 0; j < n; j++) src[j] = XSrc{kXPlain, x[j], nullptr, 0.0f};
-        return launch_matvec_pipe_src(w, src, y, n, ctx->sm_count, st, ctx->derr);
     }
     // stage each distinct activation row once
     const float* rows[kMaxJobs];

@@ -162,27 +162,14 @@ int launch_quantize(const rq_weight* w, const float* x, cudaStream_t st);
 // bulk-copy pipelined matvec (rq_mv_pipe.cu): up to kMaxJobs independent
 // M=1 matvecs with the same type and K in one launch; err may be NULL
 constexpr int kMaxJobs = 8;
-// Where a pipeline job's activation row comes from.  kXStaged: planes and
-// stats written by a staging kernel (xq).  The others (Q4_K weights only) let
-// the matvec kernel stage the row itself, in registers, with the staging
-// kernels' arithmetic (same bits): kXPlain x; kXRms RMSNorm(x) * x2 (x2 the
-// norm weight, eps); kXSwiglu silu(x) * x2.  That takes the staging kernel,
-// and its wait between two matvecs, off the critical path.
-enum XMode { kXStaged = 0, kXPlain = 1, kXRms = 2, kXSwiglu = 3 };
 struct PipeJob {
     const uint8_t* qs;
     const uint8_t* hdr;
-    XQ xq;             // the staged activation row of this job (kXStaged)
+    XQ xq;             // the staged activation row of this job
     float* y;
     const float* add;  // optional residual: y = x W^T + add (may alias y)
     int64_t out;
-    int xmode;         // XMode
-    const float* x;    // f32 activation row (kXPlain / kXRms / kXSwiglu)
-    const float* x2;   // RMSNorm weight (kXRms) or up (kXSwiglu)
-    float eps;
 };
-// Whether a weight can take an activation row staged inside the matvec.
-bool pipe_fused_staging(const rq_weight* w);
 // Jobs whose weight is chosen on the device (the sparse-MoE expert of a
 // routing slot): job j's weight is (qs[kind[j]][e], hdr[kind[j]][e]) with e =
 // slot_e[slot[j]] -- slot_e written by an earlier kernel in the stream, the
@@ -207,17 +194,6 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
                        int sm_count, cudaStream_t st, int* err = nullptr,
                        const float* const* adds = nullptr, const P2PArgs* ar = nullptr,
                        const PipeDevWeights* dw = nullptr);
-// The same with each job's activation staged by the matvec itself: job j
-// reads srcs[j] (xmode, x, x2, eps; xq ignored).  Needs pipe_fused_staging.
-struct XSrc {
-    int xmode;
-    const float* x;
-    const float* x2;
-    float eps;
-};
-int launch_matvec_pipe_src(const rq_weight* const* ws, const XSrc* srcs, float* const* ys, int njobs,
-                           int sm_count, cudaStream_t st, int* err = nullptr,
-                           const float* const* adds = nullptr, const P2PArgs* ar = nullptr);
 
 // small-M Q4_K matmul on the tensor cores (rq_mm_small.cu).  Activations are
 // staged per row as x / s = hi + lo (two f16 values per element, s a power of

@@ -470,41 +470,28 @@ int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float
 // the residual add is fused into the matvec epilogue.  W ranks: each rank's
 // partial product (rank 0 also adds the residual) is summed into x by an
 // all-reduce -- at T = 1 on the pipeline inside the matvec kernel itself,
-// over the ranks' NVLink exchange regions.  With src (T = 1, Q4_K) the
-// matvec stages x_in itself from src instead of reading m->xq.
-int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st, const XSrc* src = nullptr) {
-    const rq_weight* w1[1] = {w};
+// over the ranks' NVLink exchange regions.
+int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
     if (m->W == 1) {
+        const rq_weight* w1[1] = {w};
         float* y1[1] = {m->x};
         const float* a1[1] = {m->x};
-        if (src) return launch_matvec_pipe_src(w1, src, y1, 1, m->ctx->sm_count, st, m->derr, a1);
         return run_linears(m, 1, w1, T, y1, a1, st);
     }
+    const rq_weight* w1[1] = {w};
     P2PArgs ar;
     if (T == 1 && tp_fused_enabled(m->W) && pipe_supported(w) && tp_p2p_args(m->ctx, &ar)) {
         const XQ xq = m->xq;
         float* y = m->x;
         const float* add = m->R == 0 ? m->x : nullptr;
-        const int rc = src ? launch_matvec_pipe_src(w1, src, &y, 1, m->ctx->sm_count, st, m->derr, &add, &ar)
-                           : launch_matvec_pipe(w1, &xq, &y, 1, m->ctx->sm_count, st, m->derr, &add, &ar);
+        const int rc = launch_matvec_pipe(w1, &xq, &y, 1, m->ctx->sm_count, st, m->derr, &add, &ar);
         if (rc != kPipeNotFusable) return rc;
     }
     float* y1[1] = {m->part};
     const float* a1[1] = {m->R == 0 ? m->x : nullptr};
-    int rc = src ? launch_matvec_pipe_src(w1, src, y1, 1, m->ctx->sm_count, st, m->derr, a1)
-                 : run_linears(m, 1, w1, T, y1, a1, st);
+    int rc = run_linears(m, 1, w1, T, y1, a1, st);
     if (!rc) rc = tp_allreduce(m->ctx, m->part, m->x, T * m->cfg.hidden, 0, 0, st);
     return rc;
-}
-
-// Decode (T = 1) with Q4_K weights: the matvecs stage their own activation
-// rows (RMSNorm of the residual, SwiGLU of gate and up) in registers, so no
-// staging kernel sits between two matvecs.
-bool decode_fused_staging(const rq_llama* m, const rq_weight* const* ws, int n, int64_t T) {
-    if (T != 1) return false;
-    for (int i = 0; i < n; i++)
-        if (!pipe_fused_staging(ws[i])) return false;
-    return true;
 }
 
 // y_i = x W_i^T (+ add_i) for the n Q4_K weights (same in) over the T rows
@@ -584,10 +571,6 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
             if (tc) {
                 rc = launch_xh_stage_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xh, st);
                 if (!rc) rc = run_mm(m, 3, w3, T, y3, nullptr, st);
-            } else if (decode_fused_staging(m, w3, 3, T)) {
-                const XSrc src{kXRms, m->x, L.rms1, c.rms_eps};
-                const XSrc s3[3] = {src, src, src};
-                rc = launch_matvec_pipe_src(w3, s3, y3, 3, m->ctx->sm_count, st, m->derr);
             } else {
                 rc = launch_xquant_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xq, st);
                 if (!rc) rc = run_linears(m, 3, w3, T, y3, nullptr, st);
@@ -642,10 +625,6 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
             if (tc) {
                 rc = launch_xh_stage_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xh, st);
                 if (!rc) rc = run_mm(m, 2, w2, T, y2, nullptr, st);
-            } else if (decode_fused_staging(m, w2, 2, T)) {
-                const XSrc src{kXRms, m->x, L.rms2, c.rms_eps};
-                const XSrc s2[2] = {src, src};
-                rc = launch_matvec_pipe_src(w2, s2, y2, 2, m->ctx->sm_count, st, m->derr);
             } else {
                 rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
                 if (!rc) rc = run_linears(m, 2, w2, T, y2, nullptr, st);
@@ -655,9 +634,6 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
         if (tc) {
             rc = launch_xh_stage_swiglu(m->g, m->u, T, I, m->xh, st);
             if (!rc) rc = row_parallel_mm(m, L.w[6], T, st);
-        } else if (decode_fused_staging(m, &L.w[6], 1, T)) {
-            const XSrc src{kXSwiglu, m->g, m->u, 0.0f};
-            rc = row_parallel(m, L.w[6], T, st, &src);
         } else {
             rc = launch_xquant_swiglu(m->g, m->u, T, I, m->xq, st);
             if (!rc) rc = row_parallel(m, L.w[6], T, st);

@@ -74,11 +74,10 @@ __device__ __forceinline__ bool lane_writes(int lane) {
 }
 
 // --------------------------------------------------------- x staging
-// The arithmetic of the staged form (see rq_internal.cuh) for the 32 values
-// v of one block: the three plane words p1/p2/p3 (element 4w + i in byte i
-// of word w) and the block's (sx, sum of the first 16, sum of the last 16).
-__device__ __forceinline__ void stage_block_regs(const float (&v)[32], uint32_t (&p1)[8], uint32_t (&p2)[8],
-                                                 uint32_t (&p3)[8], float4& st) {
+// Stage the 32 values v (one block of row m, block b) into the planes and
+// stats of xq; the arithmetic of the staged form (see rq_internal.cuh).
+__device__ __forceinline__ void stage_block(const float (&v)[32], int64_t m, int64_t b, int64_t in,
+                                            int8_t* __restrict__ planes, float4* __restrict__ stats) {
     float amax = 0.0f, sa = 0.0f, sb = 0.0f;
 #pragma unroll
     for (int k = 0; k < 16; k++) { amax = fmaxf(amax, fabsf(v[k])); sa += v[k]; }
@@ -86,6 +85,7 @@ __device__ __forceinline__ void stage_block_regs(const float (&v)[32], uint32_t 
     for (int k = 16; k < 32; k++) { amax = fmaxf(amax, fabsf(v[k])); sb += v[k]; }
     const float inv = amax > 0.0f ? kXQScale / amax : 0.0f;
     const float sx = amax / kXQScale;
+    uint32_t p1[8], p2[8], p3[8];
 #pragma unroll
     for (int k = 0; k < 8; k++) { p1[k] = 0u; p2[k] = 0u; p3[k] = 0u; }
 #pragma unroll
@@ -99,23 +99,13 @@ __device__ __forceinline__ void stage_block_regs(const float (&v)[32], uint32_t 
         p2[k / 4] |= (uint32_t)(x2 & 255) << (8 * (k % 4));
         p3[k / 4] |= (uint32_t)(x3 & 255) << (8 * (k % 4));
     }
-    st = make_float4(sx, sa, sb, 0.0f);
-}
-
-// Stage the 32 values v (one block of row m, block b) into the planes and
-// stats of xq.
-__device__ __forceinline__ void stage_block(const float (&v)[32], int64_t m, int64_t b, int64_t in,
-                                            int8_t* __restrict__ planes, float4* __restrict__ stats) {
-    uint32_t p1[8], p2[8], p3[8];
-    float4 st;
-    stage_block_regs(v, p1, p2, p3, st);
     uint4* d1 = reinterpret_cast<uint4*>(planes + (m * 3 + 0) * in + b * 32);
     uint4* d2 = reinterpret_cast<uint4*>(planes + (m * 3 + 1) * in + b * 32);
     uint4* d3 = reinterpret_cast<uint4*>(planes + (m * 3 + 2) * in + b * 32);
     d1[0] = make_uint4(p1[0], p1[1], p1[2], p1[3]); d1[1] = make_uint4(p1[4], p1[5], p1[6], p1[7]);
     d2[0] = make_uint4(p2[0], p2[1], p2[2], p2[3]); d2[1] = make_uint4(p2[4], p2[5], p2[6], p2[7]);
     d3[0] = make_uint4(p3[0], p3[1], p3[2], p3[3]); d3[1] = make_uint4(p3[4], p3[5], p3[6], p3[7]);
-    stats[m * (in / 32) + b] = st;
+    stats[m * (in / 32) + b] = make_float4(sx, sa, sb, 0.0f);
 }
 
 __device__ __forceinline__ void load_block(const float* src, float (&v)[32]) {
@@ -244,70 +234,6 @@ __device__ __forceinline__ void q4kp_lane_setup(Q4KPLane& L, const int8_t* plane
     // g < 2:  bytes [s[j], s[j+1], s[j+4], s[j+5]] of (h.y, h.z)
     // g >= 2: bytes [s[j+8], s[j+9], s[j+8], s[j+9]] of h.w (j relative), and
     //         top bits from [s[j], s[j+1], s[j+4], s[j+5]] of (h.y, h.z)
-    const uint32_t yz = j | ((j + 1) << 4) | ((j + 4) << 8) | ((j + 5) << 12);
-    L.sel1 = L.hiG ? (j | ((j + 1) << 4) | (j << 8) | ((j + 1) << 12)) : yz;
-    L.sel2 = yz;
-    L.mA = L.hiG ? 0x00000F0Fu : 0x3F3F3F3Fu;
-    L.mB = L.hiG ? 0x0F0F0000u : 0u;
-    L.mC = L.hiG ? 0x30303030u : 0u;
-}
-
-// The 32 activation values of elements pos..pos+31 of a job's row for the
-// in-kernel staging modes (XMode in rq_internal.cuh), computed as the
-// staging kernels compute them: x; x / mden * w (xquant_rmsnorm_kernel);
-// silu(g) * u with silu(g) = g / (1 + exp(-g)) (xquant_swiglu_kernel).
-__device__ __forceinline__ void src_block(int xmode, const float* x, const float* x2, float mden, int64_t pos,
-                                          float (&v)[32]) {
-    load_block(x + pos, v);
-    if (xmode == kXRms) {
-        float w[32];
-        load_block(x2 + pos, w);
-#pragma unroll
-        for (int k = 0; k < 32; k++) v[k] = v[k] / mden * w[k];
-    } else if (xmode == kXSwiglu) {
-        float u[32];
-        load_block(x2 + pos, u);
-#pragma unroll
-        for (int k = 0; k < 32; k++) v[k] = v[k] / (1.0f + expf(-v[k])) * u[k];
-    }
-}
-
-// q4kp_lane_setup with the lane staging its own 64 activation values
-// (blocks 2g and 2g+1 of super-block sb) in registers instead of reading the
-// planes of a staging kernel: the same words in the same order.
-__device__ __forceinline__ void q4kp_lane_setup_src(Q4KPLane& L, int xmode, const float* x, const float* x2,
-                                                    float mden, int64_t sb, int g, int h1, bool valid) {
-    uint32_t pa[3][8], pb[3][8];
-    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
-    if (valid) {
-        const int64_t pos = sb * 256 + 64 * g;
-        float v[32];
-        src_block(xmode, x, x2, mden, pos, v);
-        stage_block_regs(v, pa[0], pa[1], pa[2], lo);
-        src_block(xmode, x, x2, mden, pos + 32, v);
-        stage_block_regs(v, pb[0], pb[1], pb[2], hi);
-    } else {
-#pragma unroll
-        for (int p = 0; p < 3; p++)
-#pragma unroll
-            for (int k = 0; k < 8; k++) pa[p][k] = pb[p][k] = 0u;
-    }
-    // half A holds words [4 h1, 4 h1 + 4) of both blocks, half B the others
-#pragma unroll
-    for (int p = 0; p < 3; p++)
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            L.xa[p][k] = h1 ? pa[p][4 + k] : pa[p][k];
-            L.xa[p][4 + k] = h1 ? pb[p][4 + k] : pb[p][k];
-            L.xb[p][k] = h1 ? pa[p][k] : pa[p][4 + k];
-            L.xb[p][4 + k] = h1 ? pb[p][k] : pb[p][4 + k];
-        }
-    L.sxl = lo.x;
-    L.xsl = lo.y + lo.z;
-    L.sxh = hi.x * 0.0625f;  // high nibbles are masked in place: 16*q
-    L.xsh = hi.y + hi.z;
-    L.hiG = g >= 2;
-    const uint32_t j = 2u * (uint32_t)(g & 1);
     const uint32_t yz = j | ((j + 1) << 4) | ((j + 4) << 8) | ((j + 5) << 12);
     L.sel1 = L.hiG ? (j | ((j + 1) << 4) | (j << 8) | ((j + 1) << 12)) : yz;
     L.sel2 = yz;

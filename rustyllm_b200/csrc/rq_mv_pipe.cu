@@ -33,8 +33,6 @@
 // bits of the standalone one-shot all-reduce (rq_tp.cu), without its launch
 // and with only local reads after the wait.
 
-#include <string.h>
-
 #include <algorithm>
 
 #include "rq_async.cuh"
@@ -65,46 +63,7 @@ struct PipeParams {
     P2PArgs ar;
     int dev_w;            // 1: weights resolved on the device (dw)
     PipeDevWeights dw;
-    int rms;              // 1: the jobs' (shared) x is RMSNorm-staged: the CTA reduces its sum of squares
-    uint32_t rms_off;     // shared memory: 8 warp partials (and the mbarrier at rms_off + 32)
 };
-
-// The RMSNorm denominator m = sqrt(sum(x^2) / in + eps) of the row x, with
-// the reduction of xquant_rmsnorm_kernel (256 threads, float4 strides, a warp
-// butterfly, warp partials summed in order) so the staged values carry its
-// bits.  Consumer warps 0..7 reduce and arrive on the mbarrier; every
-// consumer waits for it (bounded) and sums the partials.
-__device__ __forceinline__ bool rms_denominator(const PipeParams& p, const PipeJob& jb, uint8_t* smem, int cw,
-                                                int lane, float* mden) {
-    float* wsum = reinterpret_cast<float*>(smem + p.rms_off);
-    const uint32_t bar = smem_u32(smem + p.rms_off + 32);
-    if (cw < 8) {
-        const int t = cw * 32 + lane;
-        const float* row = jb.x;
-        float s2 = 0.0f;
-        if ((p.in & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
-            const float4* r4 = reinterpret_cast<const float4*>(row);
-            for (int64_t i = t; i < p.in / 4; i += 256) {
-                const float4 v = r4[i];
-                s2 = fmaf(v.x, v.x, s2); s2 = fmaf(v.y, v.y, s2);
-                s2 = fmaf(v.z, v.z, s2); s2 = fmaf(v.w, v.w, s2);
-            }
-        } else {
-            for (int64_t i = t; i < p.in; i += 256) s2 = fmaf(row[i], row[i], s2);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-        if (lane == 0) {
-            wsum[cw] = s2;
-            mbar_arrive(bar);
-        }
-    }
-    if (!mbar_wait(bar, 0)) return false;
-    float tot = 0.0f;
-    for (int k = 0; k < 8; k++) tot += wsum[k];
-    *mden = sqrtf(tot / (float)p.in + jb.eps);
-    return true;
-}
 
 __device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) {
     const int64_t b = (int64_t)blockIdx.x * j.out / gridDim.x;
@@ -190,7 +149,6 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
             mbar_init(full0 + 8 * i, 1);
             mbar_init(empty0 + 8 * i, p.S * p.G);
         }
-        if (p.rms) mbar_init(smem_u32(smem + p.rms_off + 32), 8);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -238,31 +196,17 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         typename LaneOf<TYPE>::T L;
         LaneOffsets o;
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        const void* cur_x = nullptr;
+        const int8_t* cur_x = nullptr;
         int slot = 0, use = 0, roff = 0;
         bool ok = true;
-        float mden = 1.0f;
-        if (p.rms && !rms_denominator(p, p.jobs[0], smem, c, lane, &mden)) {
-            if (lane == 0 && p.err) atomicExch(p.err, 1);
-            ok = false;
-        }
         for (int j = 0; j < p.njobs && ok; j++) {
             const PipeJob& jb = p.jobs[j];
             int64_t rb;
             int nrows;
             job_rows(jb, &rb, &nrows);
-            // jobs that share x keep the planes
-            const void* key = jb.xmode == kXStaged ? (const void*)jb.xq.planes : (const void*)jb.x;
-            if (key != cur_x) {
-                if constexpr (TYPE == RQ_Q4_K) {
-                    if (jb.xmode != kXStaged)
-                        lane_setup_src(L, o, p.nblk, jb.xmode, jb.x, jb.x2, mden, s, lane);
-                    else
-                        lane_setup<TYPE>(L, o, p.nblk, p.in, jb.xq, s, lane);
-                } else {
-                    lane_setup<TYPE>(L, o, p.nblk, p.in, jb.xq, s, lane);
-                }
-                cur_x = key;
+            if (jb.xq.planes != cur_x) {  // jobs that share x keep the planes
+                lane_setup<TYPE>(L, o, p.nblk, p.in, jb.xq, s, lane);
+                cur_x = jb.xq.planes;
             }
             for (int r0 = 0; r0 < nrows; r0 += p.RS, slot = slot + 1 == p.nstage ? 0 : slot + 1, use += slot == 0) {
                 if (!mbar_wait(full0 + 8 * slot, use & 1)) {
@@ -354,47 +298,21 @@ bool pipe_supported(const rq_weight* w) {
     return true;
 }
 
-bool pipe_fused_staging(const rq_weight* w) { return w->type == RQ_Q4_K && pipe_supported(w); }
-
-namespace {
-int launch_pipe_impl(const rq_weight* const* ws, const XQ* xqs, const XSrc* srcs, float* const* ys, int njobs,
-                     int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar,
-                     const PipeDevWeights* dw) {
+int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
+                       int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar,
+                       const PipeDevWeights* dw) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "matvec pipeline: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     TypeInfo ti = type_info(w0->type);
     PipeParams p;
-    memset(&p, 0, sizeof p);
     p.njobs = njobs;
     for (int j = 0; j < njobs; j++) {
         p.jobs[j].qs = ws[j]->qs;
         p.jobs[j].hdr = ws[j]->hdr;
-        if (srcs) {
-            p.jobs[j].xmode = srcs[j].xmode;
-            p.jobs[j].x = srcs[j].x;
-            p.jobs[j].x2 = srcs[j].x2;
-            p.jobs[j].eps = srcs[j].eps;
-        } else {
-            p.jobs[j].xq = xqs[j];
-            p.jobs[j].xmode = kXStaged;
-        }
+        p.jobs[j].xq = xqs[j];
         p.jobs[j].y = ys[j];
         p.jobs[j].add = adds ? adds[j] : nullptr;
         p.jobs[j].out = ws[j]->out;
-    }
-    if (srcs) {
-        if (!pipe_fused_staging(w0))
-            return set_error(RQ_ERR_UNSUPPORTED, "matvec pipeline: in-kernel staging needs Q4_K weights");
-        for (int j = 0; j < njobs; j++) {
-            if (srcs[j].xmode == kXRms) p.rms = 1;
-            if (srcs[j].xmode == kXStaged || !srcs[j].x || (srcs[j].xmode != kXPlain && !srcs[j].x2))
-                return set_error(RQ_ERR_INVALID, "matvec pipeline: job %d has no activation source", j);
-        }
-        // the RMSNorm denominator is reduced once per launch: one shared row
-        for (int j = 0; p.rms && j < njobs; j++)
-            if (srcs[j].xmode != kXRms || srcs[j].x != srcs[0].x || srcs[j].x2 != srcs[0].x2 ||
-                srcs[j].eps != srcs[0].eps)
-                return set_error(RQ_ERR_INVALID, "matvec pipeline: RMSNorm staging needs one shared row per launch");
     }
     p.err = err;
     p.dev_w = dw ? 1 : 0;
@@ -432,17 +350,14 @@ int launch_pipe_impl(const rq_weight* const* ws, const XQ* xqs, const XSrc* srcs
         p.fuse = 1;
         p.ar = *ar;
     }
-    p.rms_off = kBarBytes;
-    p.red_off = kBarBytes + 64;
-    p.ring_off = (uint32_t)((p.red_off + rows_cap(grid) * p.S * 4 + 127) & ~(int64_t)127);
+    p.red_off = kBarBytes;
+    p.ring_off = (uint32_t)((kBarBytes + rows_cap(grid) * p.S * 4 + 127) & ~(int64_t)127);
     int nstage = (int)((kSmemBudget - p.ring_off) / p.stage_bytes);
     nstage = std::min(nstage, 32);
     if (nstage < 2) return set_error(RQ_ERR_UNSUPPORTED, "matvec pipeline: row of %u bytes too large", rowb);
     p.nstage = nstage;
     const size_t smem = p.ring_off + (size_t)nstage * p.stage_bytes;
     const int threads = 32 * (1 + p.S * p.G);
-    if (p.rms && p.S * p.G < 8)
-        return set_error(RQ_ERR_UNSUPPORTED, "matvec pipeline: RMSNorm staging needs 8 consumer warps");
     switch (w0->type) {
     case RQ_Q4_K: return launch_pipe_type<RQ_Q4_K>(p, rpw, grid, threads, smem, st);
     case RQ_Q3_K: return launch_pipe_type<RQ_Q3_K>(p, rpw, grid, threads, smem, st);
@@ -452,18 +367,6 @@ int launch_pipe_impl(const rq_weight* const* ws, const XQ* xqs, const XSrc* srcs
     case RQ_Q2_K: return launch_pipe_type<RQ_Q2_K>(p, rpw, grid, threads, smem, st);
     default: return launch_pipe_type<RQ_Q4_0>(p, rpw, grid, threads, smem, st);
     }
-}
-}  // namespace
-
-int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
-                       int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar,
-                       const PipeDevWeights* dw) {
-    return launch_pipe_impl(ws, xqs, nullptr, ys, njobs, sm_count, st, err, adds, ar, dw);
-}
-
-int launch_matvec_pipe_src(const rq_weight* const* ws, const XSrc* srcs, float* const* ys, int njobs,
-                           int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar) {
-    return launch_pipe_impl(ws, nullptr, srcs, ys, njobs, sm_count, st, err, adds, ar, nullptr);
 }
 
 }  // namespace rq

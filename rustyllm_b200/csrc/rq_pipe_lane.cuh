@@ -131,19 +131,6 @@ __device__ __forceinline__ void lane_setup(typename LaneOf<TYPE>::T& L, LaneOffs
     }
 }
 
-// Q4_K lane set-up with the lane staging its activation values itself (an
-// in-kernel staging mode); the offsets are those of lane_setup<RQ_Q4_K>.
-__device__ __forceinline__ void lane_setup_src(Q4KPLane& L, LaneOffsets& o, int64_t nblk, int xmode,
-                                               const float* x, const float* x2, float mden, int s, int lane) {
-    const int64_t sb = (int64_t)s * 8 + (lane >> 2);
-    const bool valid = sb < nblk;
-    const uint32_t sbl = valid ? (uint32_t)(lane >> 2) : 0u;
-    q4kp_lane_setup_src(L, xmode, x, x2, mden, valid ? sb : 0, lane & 3, (lane >> 2) & 1, valid);
-    o.qa = (uint32_t)(s * 1024) + 128u * sbl + 32u * (uint32_t)(lane & 3) + 16u * ((lane >> 2) & 1u);
-    o.qb = o.qa ^ 16u;
-    o.h = (uint32_t)(s * 128) + 16u * sbl;
-}
-
 // Lane contribution of one row held in shared memory (q: the row's quant
 // bytes, h: its header bytes).
 template <int TYPE>
