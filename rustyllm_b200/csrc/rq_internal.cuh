@@ -190,10 +190,15 @@ bool pipe_supported(const rq_weight* w);
 // cannot be fused.
 struct P2PArgs;
 constexpr int kPipeNotFusable = -1;
+// With swiglu_to (two jobs, gate then up, of the same shape, out a multiple
+// of 32): instead of writing y, the kernel stages silu(gate) * up straight
+// into swiglu_to (one activation row of `out` elements), with the
+// arithmetic of launch_xquant_swiglu, for the down projection -- one launch
+// fewer per decode layer.  CTAs then own whole 32-row blocks.
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err = nullptr,
                        const float* const* adds = nullptr, const P2PArgs* ar = nullptr,
-                       const PipeDevWeights* dw = nullptr);
+                       const PipeDevWeights* dw = nullptr, const XQ* swiglu_to = nullptr);
 
 // small-M Q4_K matmul on the tensor cores (rq_mm_small.cu).  Activations are
 // staged per row as x / s = hi + lo (two f16 values per element, s a power of

@@ -64,6 +64,7 @@ struct rq_llama {
     int W, R;       // tensor-parallel world and rank
     int64_t nh_l, nkv_l, I_l, vocab_l;  // this rank's heads, kv heads, ffn rows, vocab rows
     rq::XQ xq;      // Tmax rows of max(hidden, intermediate)
+    rq::XQ xqd;     // one row of the local intermediate: the down projection's input at decode
     rq::XH xh;      // the same rows staged as f16 hi / lo (tensor-core prefill)
     // device state
     unsigned long long* best;  // packed (value, -index) of the argmax
@@ -471,17 +472,19 @@ int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float
 // partial product (rank 0 also adds the residual) is summed into x by an
 // all-reduce -- at T = 1 on the pipeline inside the matvec kernel itself,
 // over the ranks' NVLink exchange regions.
-int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
+int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st, const XQ* staged = nullptr) {
+    const XQ xin = staged ? *staged : m->xq;
     if (m->W == 1) {
         const rq_weight* w1[1] = {w};
         float* y1[1] = {m->x};
         const float* a1[1] = {m->x};
+        if (staged) return launch_matvec_pipe(w1, &xin, y1, 1, m->ctx->sm_count, st, m->derr, a1);
         return run_linears(m, 1, w1, T, y1, a1, st);
     }
     const rq_weight* w1[1] = {w};
     P2PArgs ar;
     if (T == 1 && tp_fused_enabled(m->W) && pipe_supported(w) && tp_p2p_args(m->ctx, &ar)) {
-        const XQ xq = m->xq;
+        const XQ xq = xin;
         float* y = m->x;
         const float* add = m->R == 0 ? m->x : nullptr;
         const int rc = launch_matvec_pipe(w1, &xq, &y, 1, m->ctx->sm_count, st, m->derr, &add, &ar);
@@ -489,9 +492,18 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st) {
     }
     float* y1[1] = {m->part};
     const float* a1[1] = {m->R == 0 ? m->x : nullptr};
-    int rc = run_linears(m, 1, w1, T, y1, a1, st);
+    int rc = staged ? launch_matvec_pipe(w1, &xin, y1, 1, m->ctx->sm_count, st, m->derr, a1)
+                    : run_linears(m, 1, w1, T, y1, a1, st);
     if (!rc) rc = tp_allreduce(m->ctx, m->part, m->x, T * m->cfg.hidden, 0, 0, st);
     return rc;
+}
+
+// Decode (T = 1): the gate/up matvec stages silu(gate) * up for the down
+// projection in its own epilogue (no separate staging launch) when both
+// weights run on the pipeline and the local intermediate size is a multiple
+// of 32.
+bool swiglu_in_epilogue(const rq_llama* m, const rq_weight* gate, const rq_weight* up, int64_t T) {
+    return T == 1 && pipe_supported(gate) && pipe_supported(up) && gate->out == up->out && m->I_l % 32 == 0;
 }
 
 // y_i = x W_i^T (+ add_i) for the n Q4_K weights (same in) over the T rows
@@ -625,6 +637,14 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
             if (tc) {
                 rc = launch_xh_stage_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xh, st);
                 if (!rc) rc = run_mm(m, 2, w2, T, y2, nullptr, st);
+            } else if (swiglu_in_epilogue(m, L.w[4], L.w[5], T)) {
+                rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
+                const XQ in2[2] = {m->xq, m->xq};
+                if (!rc) rc = launch_matvec_pipe(w2, in2, y2, 2, m->ctx->sm_count, st, m->derr, nullptr, nullptr,
+                                                 nullptr, &m->xqd);
+                if (!rc) rc = row_parallel(m, L.w[6], T, st, &m->xqd);
+                if (rc) return rc;
+                continue;
             } else {
                 rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
                 if (!rc) rc = run_linears(m, 2, w2, T, y2, nullptr, st);
@@ -883,7 +903,9 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     if (!rc) rc = dalloc(m, &m->part, (size_t)(T * H));
     uint8_t* xqbuf = nullptr;
     uint8_t* xhbuf = nullptr;
+    uint8_t* xqdbuf = nullptr;
     if (!rc) rc = dalloc(m, &xqbuf, xq_bytes(T, maxin));
+    if (!rc) rc = dalloc(m, &xqdbuf, xq_bytes(1, I));
     if (!rc && T >= kMinTensorM) rc = dalloc(m, &xhbuf, xh_bytes(T, maxin));
     if (!rc) rc = dalloc(m, &m->best, 1);
     if (!rc) rc = dalloc(m, &m->keys, (size_t)T);
@@ -901,6 +923,8 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
         m->layer_set.assign((size_t)c.n_layers, false);
         m->xq.planes = (int8_t*)xqbuf;
         m->xq.stats = (float4*)(xqbuf + (((size_t)T * 3 * maxin + 255) & ~(size_t)255));
+        m->xqd.planes = (int8_t*)xqdbuf;
+        m->xqd.stats = (float4*)(xqdbuf + (((size_t)3 * I + 255) & ~(size_t)255));
         m->xh = xhbuf ? xh_at(xhbuf, T, maxin) : XH{};
         // RoPE tables as QuantStreamCache::new computes them
         // (src/streaming_quantized.rs:104-118): inv_freq[i] =

@@ -63,11 +63,16 @@ struct PipeParams {
     P2PArgs ar;
     int dev_w;            // 1: weights resolved on the device (dw)
     PipeDevWeights dw;
+    int sw;               // 1: stage silu(y_0) * y_1 into swq instead of writing y
+    XQ swq;
 };
 
-__device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) {
-    const int64_t b = (int64_t)blockIdx.x * j.out / gridDim.x;
-    const int64_t e = (int64_t)(blockIdx.x + 1) * j.out / gridDim.x;
+// This CTA's rows of a job; in whole 32-row blocks when the epilogue stages
+// SwiGLU blocks (sw).
+__device__ __forceinline__ void job_rows(const PipeJob& j, int sw, int64_t* rb, int* n) {
+    const int64_t unit = sw ? 32 : 1, units = j.out / unit;
+    const int64_t b = (int64_t)blockIdx.x * units / gridDim.x * unit;
+    const int64_t e = (int64_t)(blockIdx.x + 1) * units / gridDim.x * unit;
     *rb = b;
     *n = (int)(e - b);
 }
@@ -80,7 +85,7 @@ __device__ __forceinline__ void allreduce_rows(const PipeParams& p, const float*
     const PipeJob& jb = p.jobs[0];
     int64_t rb;
     int nrows;
-    job_rows(jb, &rb, &nrows);
+    job_rows(jb, p.sw, &rb, &nrows);
     uint8_t* own = p.ar.base[p.ar.rank];
     uint32_t* ctl = reinterpret_cast<uint32_t*>(own + kP2PCtlOff);  // epoch, done, err
     const uint32_t e = *reinterpret_cast<volatile uint32_t*>(ctl);
@@ -165,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
                 const PipeJob& jb = p.jobs[j];
                 int64_t rb;
                 int nrows;
-                job_rows(jb, &rb, &nrows);
+                job_rows(jb, p.sw, &rb, &nrows);
                 const uint8_t* jqs = jb.qs;
                 const uint8_t* jhdr = jb.hdr;
                 if (p.dev_w) {
@@ -203,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
             const PipeJob& jb = p.jobs[j];
             int64_t rb;
             int nrows;
-            job_rows(jb, &rb, &nrows);
+            job_rows(jb, p.sw, &rb, &nrows);
             if (jb.xq.planes != cur_x) {  // jobs that share x keep the planes
                 lane_setup<TYPE>(L, o, p.nblk, p.in, jb.xq, s, lane);
                 cur_x = jb.xq.planes;
@@ -240,11 +245,33 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         allreduce_rows(p, red);
         return;
     }
+    if (p.sw) {
+        // gate rows at red[0 ..), up rows after them: one thread per 32-row
+        // block computes both sums in slice order (the bits of y), then
+        // silu(g) * u and its staged form (xquant_swiglu_kernel's arithmetic)
+        int64_t rb;
+        int nrows;
+        job_rows(p.jobs[0], 1, &rb, &nrows);
+        for (int b = threadIdx.x; b < nrows / 32; b += blockDim.x) {
+            float v[32];
+#pragma unroll 4
+            for (int k = 0; k < 32; k++) {
+                float g = 0.0f, u = 0.0f;
+                for (int s = 0; s < p.S; s++) {
+                    g += red[(32 * b + k) * p.S + s];
+                    u += red[(nrows + 32 * b + k) * p.S + s];
+                }
+                v[k] = g / (1.0f + expf(-g)) * u;
+            }
+            stage_block(v, 0, rb / 32 + b, p.jobs[0].out, p.swq.planes, p.swq.stats);
+        }
+        return;
+    }
     int roff = 0;
     for (int j = 0; j < p.njobs; j++) {
         int64_t rb;
         int nrows;
-        job_rows(p.jobs[j], &rb, &nrows);
+        job_rows(p.jobs[j], p.sw, &rb, &nrows);
         const float* add = p.jobs[j].add;
         for (int t = threadIdx.x; t < nrows; t += blockDim.x) {
             float acc = 0.0f;
@@ -300,7 +327,7 @@ bool pipe_supported(const rq_weight* w) {
 
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar,
-                       const PipeDevWeights* dw) {
+                       const PipeDevWeights* dw, const XQ* swiglu_to) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "matvec pipeline: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     TypeInfo ti = type_info(w0->type);
@@ -317,6 +344,13 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
     p.err = err;
     p.dev_w = dw ? 1 : 0;
     if (dw) p.dw = *dw;
+    p.sw = 0;
+    if (swiglu_to) {
+        if (njobs != 2 || ar || ws[0]->out != ws[1]->out || ws[0]->out % 32 || (adds && (adds[0] || adds[1])))
+            return set_error(RQ_ERR_INVALID, "matvec pipeline: SwiGLU staging needs gate and up of one shape");
+        p.sw = 1;
+        p.swq = *swiglu_to;
+    }
     p.nblk = w0->nblk;
     p.in = w0->in;
     p.S = (int)((w0->in + 2047) / 2048);
@@ -336,7 +370,8 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
     // per-CTA partial table [rows of all jobs][S] floats, at most 32 KB
     auto rows_cap = [&](int gr) {
         int64_t r = 0;
-        for (int j = 0; j < njobs; j++) r += (ws[j]->out + gr - 1) / gr;
+        for (int j = 0; j < njobs; j++)
+            r += swiglu_to ? (ws[j]->out / 32 + gr - 1) / gr * 32 : (ws[j]->out + gr - 1) / gr;
         return r;
     };
     while (rows_cap(grid) * p.S * 4 > 32 * 1024) grid *= 2;
