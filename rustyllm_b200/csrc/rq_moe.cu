@@ -70,29 +70,56 @@ namespace {
 // lane c (c < 8) accumulates x[8i+c] * w[8i+c] with a fused multiply-add in
 // ascending i, the eight lane sums are added left to right, and a tail of
 // H % 8 elements adds x*w with two roundings.  So the logits carry the bits
-// of the reference's CPU gate.
+// of the reference's CPU gate.  The chains are sequential by definition, so
+// the CTA first copies a chunk of x and of every expert's row into shared
+// memory with all its threads (coalesced 16-byte loads) and the eight chain
+// lanes of each warp then run from shared memory.
+constexpr int kRouterSmem = 40 * 1024;
+
+__host__ __device__ inline int router_chunk(int E) {
+    int ch = kRouterSmem / (4 + 2 * E);
+    return ch - ch % 8;
+}
+
 __global__ void router_kernel(const float* __restrict__ x, const __half* __restrict__ wr, int64_t H,
                               int E, int k, float* __restrict__ logits, int32_t* __restrict__ ids,
                               float* __restrict__ wts) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
+    extern __shared__ __align__(16) uint8_t rsm[];
     __shared__ float sl[32];
     const int64_t t = blockIdx.x;
     const int e = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (e < E) {
-        const float* xr = x + t * H;
-        const __half* wrow = wr + (int64_t)e * H;
-        const int64_t chunks = H / 8;
-        float acc = 0.0f;
-        if (lane < 8) {
-#pragma unroll 8
-            for (int64_t i = 0; i < chunks; i++)
-                acc = __fmaf_rn(xr[8 * i + lane], __half2float(wrow[8 * i + lane]), acc);
+    const int ch = router_chunk(E);
+    float* xs = reinterpret_cast<float*>(rsm);
+    __half* ws = reinterpret_cast<__half*>(rsm + (size_t)ch * 4);
+    const float* xr = x + t * H;
+    const int64_t chunks8 = H / 8;  // elements covered by the eight chains
+    float acc = 0.0f;
+    for (int64_t c0 = 0; c0 < chunks8 * 8; c0 += ch) {
+        const int64_t left = chunks8 * 8 - c0;
+        const int n = (int)(left < ch ? left : ch);  // a multiple of 8
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = xr[c0 + i];
+        for (int r = 0; r < E; r++) {
+            const uint4* src = reinterpret_cast<const uint4*>(wr + (int64_t)r * H + c0);
+            uint4* dst = reinterpret_cast<uint4*>(ws + (size_t)r * ch);
+            for (int i = threadIdx.x; i < n / 8; i += blockDim.x) dst[i] = src[i];
         }
+        __syncthreads();
+        if (e < E && lane < 8) {
+            const __half* wrow = ws + (size_t)e * ch;
+#pragma unroll 8
+            for (int i = 0; i < n / 8; i++)
+                acc = __fmaf_rn(xs[8 * i + lane], __half2float(wrow[8 * i + lane]), acc);
+        }
+    }
+    if (e < E) {
+        const __half* wrow = wr + (int64_t)e * H;
         float sum = -0.0f;
 #pragma unroll
         for (int c = 0; c < 8; c++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, c));
-        for (int64_t i = chunks * 8; i < H; i++) sum = __fadd_rn(sum, __fmul_rn(xr[i], __half2float(wrow[i])));
+        for (int64_t i = chunks8 * 8; i < H; i++) sum = __fadd_rn(sum, __fmul_rn(xr[i], __half2float(wrow[i])));
         if (lane == 0) {
             sl[e] = sum;
             logits[t * E + e] = sum;
@@ -520,6 +547,8 @@ int route(rq_moe* m, const float* xs, int64_t T, std::vector<int32_t>* offs, std
     const int E = m->E, k = m->k;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl(dim3((unsigned)T), dim3((unsigned)(32 * E)), st, attr);
+    const int ch = router_chunk(E);
+    cfg.dynamicSmemBytes = (size_t)ch * 4 + (size_t)E * ch * 2;
     int rc = cuda_error(cudaLaunchKernelEx(&cfg, router_kernel, xs, (const __half*)m->router, m->H, E, k, m->logits,
                                            m->ids, m->wts), "router kernel");
     if (!rc) {
