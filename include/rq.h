@@ -110,8 +110,9 @@ RQ_API int rq_weight_download(rq_ctx* ctx, const rq_weight* w, void* blocks_host
 RQ_API int rq_weight_free(rq_ctx* ctx, rq_weight* w);
 
 /* Any of the out-pointers may be NULL.  device_bytes counts the library's
- * device copy (equal to the GGML byte count, plus 2 pad bytes per Q3_K or
- * Q6_K super-block). */
+ * device copy: the GGML byte count, plus 2 pad bytes per Q6_K super-block;
+ * Q3_K is held expanded (4-bit values and int8 scales, 148 bytes per
+ * 110-byte super-block) so that its matvec is not bound by unpacking. */
 RQ_API int rq_weight_info(const rq_weight* w, int* ggml_type, int64_t* out, int64_t* in,
                    size_t* device_bytes);
 

@@ -21,10 +21,15 @@ namespace rq {
 //         128-bit loads are aligned and coalesced;
 //   hdr : the per-block scale bytes.
 //   Q4_K  qs 128 B (GGML bytes 16..143)     hdr 16 B (d, dmin, 12 scale bytes)
-//   Q3_K  qs  96 B (hmask 32 + qs 64)       hdr 16 B (12 scale bytes, d, 2 pad)
+//   Q3_K  qs 128 B (q + 4 as nibbles)       hdr 20 B (16 int8 scales, d, 2 pad)
 //   Q4_0  qs  16 B (GGML bytes 2..17)       hdr  2 B (d)
 // Bytes keep their GGML order inside each part, so the total equals the GGML
-// size (Q3_K adds 2 pad bytes per super-block).
+// size -- except Q3_K, which is expanded at upload: its 3-bit values (2 low
+// bits + hmask bit) become nibbles in Q4_K's arrangement (byte j of 64-element
+// group c: element 64c + j low, 64c + 32 + j high) and its packed 6-bit
+// scales become int8, so its matvec lane is a Q4_K lane (the 3-bit unpacking
+// made it ALU-bound); 148 device bytes per 110 GGML bytes, and the layout
+// kernels convert both ways exactly.
 struct TypeInfo {
     int type;
     int block_elems;  // 32 or 256
@@ -36,7 +41,7 @@ struct TypeInfo {
 __host__ __device__ inline TypeInfo type_info(int t) {
     switch (t) {
     case RQ_Q4_K: return TypeInfo{RQ_Q4_K, 256, 144, 128, 16};
-    case RQ_Q3_K: return TypeInfo{RQ_Q3_K, 256, 110, 96, 16};
+    case RQ_Q3_K: return TypeInfo{RQ_Q3_K, 256, 110, 128, 20};
     case RQ_Q4_0: return TypeInfo{RQ_Q4_0, 32, 18, 16, 2};
     case RQ_Q8_0: return TypeInfo{RQ_Q8_0, 32, 34, 32, 2};
     // Q6_K: quant part ql[128] qh[64]; header scales[16] d[2] + 2 bytes of
@@ -119,7 +124,8 @@ struct P2PArgs;
 bool tp_p2p_args(const rq_ctx* ctx, P2PArgs* a);
 // Whether a row-parallel M=1 matvec does its all-reduce inside the matvec
 // kernel (the fused epilogue; same bits as the separate kernel) at `world`
-// ranks.  RQ_TP_FUSED=1 / =0 in the environment forces it on / off.
+// ranks: the default at every world size; RQ_TP_FUSED=0 in the environment
+// turns it off (the separate peer-memory kernel then runs).
 bool tp_fused_enabled(int world);
 void tp_destroy(rq_ctx* ctx);
 // all-gather of nbytes from every rank into out[world][nbytes]
@@ -190,15 +196,35 @@ bool pipe_supported(const rq_weight* w);
 // cannot be fused.
 struct P2PArgs;
 constexpr int kPipeNotFusable = -1;
-// With swiglu_to (two jobs, gate then up, of the same shape, out a multiple
-// of 32): instead of writing y, the kernel stages silu(gate) * up straight
-// into swiglu_to (one activation row of `out` elements), with the
-// arithmetic of launch_xquant_swiglu, for the down projection -- one launch
-// fewer per decode layer.  CTAs then own whole 32-row blocks.
+// SwiGLU staging epilogue: jobs come in pairs (2i gate, 2i+1 up) of one
+// shape, out a multiple of 32.  Besides writing y, the kernel stages
+// silu(gate) * up of pair i into row row0 + i of xq, with the arithmetic of
+// launch_xquant_swiglu, for the down projection.  A 32-row block spans CTAs:
+// each CTA adds the rows it wrote to the block's arrival counter
+// cnt[(row0 + i) * out / 32 + block] and the CTA that completes the block
+// (64 rows) stages it and zeroes the counter.  cnt starts zeroed.
+struct PipeSwiglu {
+    XQ xq;
+    int* cnt;
+    int row0;
+};
+// Sparse-MoE combine epilogue: the jobs are the down projections of routing
+// slots slot0 .. slot0 + njobs - 1 in token-major order (slot t * k + r is
+// the r-th pick of token t, njobs and slot0 multiples of k), so the k slots of
+// a token share a CTA's rows.  Instead of writing y the kernel writes
+// out[t][c] = sum over the token's slots in ascending expert order of
+// wts[s] * o_s[c] (combine_kernel's arithmetic).
+struct PipeCombine {
+    const int32_t* ids;  // [slots] expert of each slot (device)
+    const float* wts;    // [slots] routing weight of each slot (device)
+    float* out;          // [tokens][out]
+    int k, slot0;
+};
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err = nullptr,
                        const float* const* adds = nullptr, const P2PArgs* ar = nullptr,
-                       const PipeDevWeights* dw = nullptr, const XQ* swiglu_to = nullptr);
+                       const PipeDevWeights* dw = nullptr, const PipeSwiglu* sw = nullptr,
+                       const PipeCombine* cmb = nullptr);
 
 // small-M Q4_K matmul on the tensor cores (rq_mm_small.cu).  Activations are
 // staged per row as x / s = hi + lo (two f16 values per element, s a power of

@@ -6,6 +6,8 @@
 // to GGML's (w = (d*sc)*q - (dmin*m), two roundings), and the quantizers must
 // produce the same bytes as the CPU quantizer on the same f32 input.
 
+#include <algorithm>
+
 #include "rq_internal.cuh"
 
 namespace rq {
@@ -18,10 +20,6 @@ __device__ __forceinline__ bool ggml_byte_slot(int type, int b, int* off) {
     if (type == RQ_Q4_K || type == RQ_Q5_K) {  // [d dmin scales(12)] [qs 128] / [qh 32][qs 128]
         if (b < 16) { *off = b; return true; }
         *off = b - 16; return false;
-    }
-    if (type == RQ_Q3_K) {  // [hmask 32][qs 64][scales 12][d 2]
-        if (b < 96) { *off = b; return false; }
-        *off = b - 96; return true;  // scales 0..11, d 12..13
     }
     if (type == RQ_Q6_K) {  // [ql 128][qh 64][scales 16][d 2]
         if (b < 192) { *off = b; return false; }
@@ -64,6 +62,87 @@ __global__ void unpack_kernel(int type, int bb, int qsb, int hb, uint8_t* __rest
     }
 }
 
+// Q3_K expanded layout (rq_internal.cuh): per super-block 128 nibble bytes
+// of q + 4 in Q4_K's arrangement and 20 header bytes (16 int8 scales, d).
+
+// q + 4 (0..7) of element e of a GGML Q3_K block: 2 low bits from qs
+// (byte 32 (c / 4) + e % 32, shift 2 (c % 4)), bit 2 from hmask (byte e % 32,
+// bit c), c = e / 32 -- GGML's dequantize_row_q3_K order.
+__device__ __forceinline__ int q3k_raw_q4(const uint8_t* blk, int e) {
+    const int c = e / 32, j = e % 32;
+    const int low = (blk[32 + 32 * (c / 4) + j] >> (2 * (c % 4))) & 3;
+    const int hb = (blk[j] >> c) & 1;
+    return low | (hb << 2);
+}
+
+// The 6-bit scale (0..63) of 16-element sub-block i of a GGML Q3_K block.
+__device__ __forceinline__ int q3k_raw_scale(const uint8_t* blk, int i) {
+    const uint8_t* sc = blk + 96;
+    const int lo = i < 8 ? (sc[i] & 15) : (sc[i - 8] >> 4);
+    const int hi = (sc[8 + i % 4] >> (2 * (i / 4))) & 3;
+    return lo | (hi << 4);
+}
+
+// q + 4 of element e of an expanded super-block (qs part).
+__device__ __forceinline__ int q3k_exp_q4(const uint8_t* q, int e) {
+    const int c4 = e / 64, w = e % 64;
+    const uint8_t b = q[32 * c4 + (w % 32)];
+    return w < 32 ? (b & 15) : (b >> 4);
+}
+
+// GGML Q3_K blocks -> expanded layout; one thread per output byte (128 qs
+// bytes + 20 header bytes per super-block).
+__global__ void q3k_expand_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ qs,
+                                  uint8_t* __restrict__ hdr, int64_t blk0, int64_t nsb) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (; i < nsb * 148; i += stride) {
+        const int64_t sb = i / 148;
+        const int b = (int)(i % 148);
+        const uint8_t* blk = raw + sb * 110;
+        if (b < 128) {
+            const int e0 = 64 * (b / 32) + b % 32;
+            qs[(blk0 + sb) * 128 + b] = (uint8_t)(q3k_raw_q4(blk, e0) | (q3k_raw_q4(blk, e0 + 32) << 4));
+        } else {
+            const int h = b - 128;
+            uint8_t v = 0;
+            if (h < 16) v = (uint8_t)(int8_t)(q3k_raw_scale(blk, h) - 32);
+            else if (h < 18) v = blk[108 + h - 16];
+            hdr[(blk0 + sb) * 20 + h] = v;
+        }
+    }
+}
+
+// Expanded layout -> GGML Q3_K blocks; one thread per GGML byte.
+__global__ void q3k_contract_kernel(uint8_t* __restrict__ raw, const uint8_t* __restrict__ qs,
+                                    const uint8_t* __restrict__ hdr, int64_t blk0, int64_t nsb) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (; i < nsb * 110; i += stride) {
+        const int64_t sb = i / 110;
+        const int b = (int)(i % 110);
+        const uint8_t* q = qs + (blk0 + sb) * 128;
+        const uint8_t* h = hdr + (blk0 + sb) * 20;
+        int v = 0;
+        if (b < 32) {  // hmask byte b: bit c = bit 2 of element 32 c + b
+            for (int c = 0; c < 8; c++) v |= ((q3k_exp_q4(q, 32 * c + b) >> 2) & 1) << c;
+        } else if (b < 96) {  // qs byte: half hh, column j, four 2-bit fields
+            const int hh = (b - 32) / 32, j = (b - 32) % 32;
+            for (int s = 0; s < 4; s++) v |= (q3k_exp_q4(q, 32 * (4 * hh + s) + j) & 3) << (2 * s);
+        } else if (b < 108) {  // packed 6-bit scales
+            const int k = b - 96;
+            if (k < 8) {
+                v = ((((int)(int8_t)h[k]) + 32) & 15) | (((((int)(int8_t)h[k + 8]) + 32) & 15) << 4);
+            } else {
+                for (int qd = 0; qd < 4; qd++) v |= (((((int)(int8_t)h[4 * qd + k - 8]) + 32) >> 4) & 3) << (2 * qd);
+            }
+        } else {
+            v = h[16 + b - 108];
+        }
+        raw[sb * 110 + b] = (uint8_t)v;
+    }
+}
+
 // ----------------------------------------------------------- dequantization
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
@@ -99,26 +178,20 @@ __global__ void dequant_kernel(int type, const uint8_t* __restrict__ qs,
         int shift = (s & 1) * 4;
 #pragma unroll
         for (int j = 0; j < 32; j++) v[j] = __fsub_rn(__fmul_rn(d1, (float)((q[j] >> shift) & 15)), m1);
-    } else if (type == RQ_Q3_K) {
+    } else if (type == RQ_Q3_K) {  // w = (d * sc) * (q - 4), expanded layout
         int64_t sbi = t / 8;
-        int c = (int)(t % 8);  // 32-element chunk: h = c/4, s = c%4
-        const uint8_t* hm = qs + sbi * 96;
-        const uint8_t* q = hm + 32;
-        const uint8_t* h = hdr + sbi * 16;
-        float d = h2f((uint16_t)(h[12] | (h[13] << 8)));
-        int hh = c / 4, s = c % 4;
+        int c = (int)(t % 8);  // 32-element chunk
+        const uint8_t* q = qs + sbi * 128;
+        const uint8_t* h = hdr + sbi * 20;
+        float d = h2f((uint16_t)(h[16] | (h[17] << 8)));
 #pragma unroll
         for (int half = 0; half < 2; half++) {
-            int sub = 2 * c + half;  // 16-element sub-block
-            int lo = sub < 8 ? (h[sub] & 15) : (h[sub - 8] >> 4);
-            int hi = (h[8 + (sub % 4)] >> (2 * (sub / 4))) & 3;
-            float dl = __fmul_rn(d, (float)((lo | (hi << 4)) - 32));
+            const int sub = 2 * c + half;  // 16-element sub-block
+            float dl = __fmul_rn(d, (float)(int8_t)h[sub]);
 #pragma unroll
             for (int jj = 0; jj < 16; jj++) {
-                int j = 16 * half + jj;
-                int low = (q[32 * hh + j] >> (2 * s)) & 3;
-                int hb = (hm[j] >> c) & 1;
-                v[j] = __fmul_rn(dl, (float)(low - (hb ? 0 : 4)));
+                const int j = 16 * half + jj;
+                v[j] = __fmul_rn(dl, (float)(q3k_exp_q4(q, 32 * c + j) - 4));
             }
         }
     } else if (type == RQ_Q5_K) {  // w = (d * sc) * q - (dmin * m), q = nibble | qh bit << 4
@@ -320,51 +393,33 @@ __global__ void quant_q3k_kernel(const float* __restrict__ x, int64_t nsb_total,
     __half dh = __float2half_rn(iscale != 0.0f ? __fdiv_rn(1.0f, iscale) : 0.0f);
     float d = __half2float(dh);
     float dl = __fmul_rn(d, (float)l);
-    int c = lane / 4, s = c % 4, hh = c / 4;
-    unsigned long long qpart = 0ull, hpart = 0ull;
+    // expanded layout: element 8 lane + i is nibble (q + 4) of byte
+    // 32 (lane / 8) + 8 (lane % 4) + i, the low nibble for lane % 8 < 4
+    unsigned long long part = 0ull;
+    const int nshift = (lane & 4) ? 4 : 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         int q = 0;
         if (dl != 0.0f) q = max(-4, min(3, __float2int_rn(__fdiv_rn(v[i], dl))));
-        int u = q + 4;
-        qpart |= (unsigned long long)((u & 3) << (2 * s)) << (8 * i);
-        hpart |= (unsigned long long)((u >> 2) << c) << (8 * i);
+        part |= (unsigned long long)((q + 4) << nshift) << (8 * i);
     }
-    // OR the 2-bit fields of the 4 shift groups (lanes differing in bits 2,3)
-    qpart |= __shfl_xor_sync(0xffffffffu, qpart, 4);
-    qpart |= __shfl_xor_sync(0xffffffffu, qpart, 8);
-    // OR the high bits of all 8 chunks (lanes differing in bits 2,3,4)
-    hpart |= __shfl_xor_sync(0xffffffffu, hpart, 4);
-    hpart |= __shfl_xor_sync(0xffffffffu, hpart, 8);
-    hpart |= __shfl_xor_sync(0xffffffffu, hpart, 16);
-    uint8_t* base = qs + sbi * 96;
-    if (s == 0) *reinterpret_cast<unsigned long long*>(base + 32 + 32 * hh + 8 * (lane & 3)) = qpart;
-    if (c == 0) *reinterpret_cast<unsigned long long*>(base + 8 * (lane & 3)) = hpart;
+    part |= __shfl_xor_sync(0xffffffffu, part, 4);
+    if (!(lane & 4))
+        *reinterpret_cast<unsigned long long*>(qs + sbi * 128 + 32 * (lane / 8) + 8 * (lane & 3)) = part;
     int all_l[16];
 #pragma unroll
-    for (int k = 0; k < 16; k++) all_l[k] = __shfl_sync(0xffffffffu, l, 2 * k) + 32;
+    for (int k = 0; k < 16; k++) all_l[k] = __shfl_sync(0xffffffffu, l, 2 * k);
     if (lane == 0) {
-        uint8_t sb[16];
+        uint32_t w[5];
 #pragma unroll
-        for (int k = 0; k < 16; k++) sb[k] = 0;
+        for (int k = 0; k < 4; k++)
+            w[k] = (uint32_t)(uint8_t)(int8_t)all_l[4 * k] | ((uint32_t)(uint8_t)(int8_t)all_l[4 * k + 1] << 8) |
+                   ((uint32_t)(uint8_t)(int8_t)all_l[4 * k + 2] << 16) |
+                   ((uint32_t)(uint8_t)(int8_t)all_l[4 * k + 3] << 24);
+        w[4] = (uint32_t)__half_as_ushort(dh);
+        uint32_t* hp = reinterpret_cast<uint32_t*>(hdr + sbi * 20);
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-            int vv = all_l[k];
-            if (k < 8) sb[k] |= (uint8_t)(vv & 15);
-            else sb[k - 8] |= (uint8_t)((vv & 15) << 4);
-            sb[8 + (k % 4)] |= (uint8_t)((vv >> 4) << (2 * (k / 4)));
-        }
-        uint16_t dbits = __half_as_ushort(dh);
-        sb[12] = (uint8_t)dbits;
-        sb[13] = (uint8_t)(dbits >> 8);
-        sb[14] = 0;
-        sb[15] = 0;
-        uint4 hv;
-        hv.x = sb[0] | (sb[1] << 8) | (sb[2] << 16) | ((uint32_t)sb[3] << 24);
-        hv.y = sb[4] | (sb[5] << 8) | (sb[6] << 16) | ((uint32_t)sb[7] << 24);
-        hv.z = sb[8] | (sb[9] << 8) | (sb[10] << 16) | ((uint32_t)sb[11] << 24);
-        hv.w = sb[12] | (sb[13] << 8) | (sb[14] << 16) | ((uint32_t)sb[15] << 24);
-        *reinterpret_cast<uint4*>(hdr + sbi * 16) = hv;
+        for (int k = 0; k < 5; k++) hp[k] = w[k];
     }
 }
 
@@ -606,6 +661,12 @@ int launch_repack(const rq_weight* w, const uint8_t* raw_dev, int64_t row0, int6
     TypeInfo ti = type_info(w->type);
     int64_t nbytes = rows * w->nblk * ti.block_bytes;
     if (nbytes == 0) return RQ_OK;
+    if (w->type == RQ_Q3_K) {
+        const int64_t nsb = rows * w->nblk;
+        const int64_t grid = std::min<int64_t>((nsb * 148 + 255) / 256, 148 * 64);
+        q3k_expand_kernel<<<(unsigned)grid, 256, 0, st>>>(raw_dev, w->qs, w->hdr, row0 * w->nblk, nsb);
+        return cuda_error(cudaGetLastError(), "Q3_K expand kernel");
+    }
     int64_t grid = (nbytes + 255) / 256;
     if (grid > 148 * 64) grid = 148 * 64;
     repack_kernel<<<(unsigned)grid, 256, 0, st>>>(w->type, ti.block_bytes, ti.qs_bytes, ti.hdr_bytes,
@@ -618,6 +679,12 @@ int launch_unpack(const rq_weight* w, uint8_t* raw_dev, int64_t row0, int64_t ro
     TypeInfo ti = type_info(w->type);
     int64_t nbytes = rows * w->nblk * ti.block_bytes;
     if (nbytes == 0) return RQ_OK;
+    if (w->type == RQ_Q3_K) {
+        const int64_t nsb = rows * w->nblk;
+        const int64_t grid = std::min<int64_t>((nsb * 110 + 255) / 256, 148 * 64);
+        q3k_contract_kernel<<<(unsigned)grid, 256, 0, st>>>(raw_dev, w->qs, w->hdr, row0 * w->nblk, nsb);
+        return cuda_error(cudaGetLastError(), "Q3_K contract kernel");
+    }
     int64_t grid = (nbytes + 255) / 256;
     if (grid > 148 * 64) grid = 148 * 64;
     unpack_kernel<<<(unsigned)grid, 256, 0, st>>>(w->type, ti.block_bytes, ti.qs_bytes, ti.hdr_bytes,

@@ -65,6 +65,7 @@ struct rq_llama {
     int64_t nh_l, nkv_l, I_l, vocab_l;  // this rank's heads, kv heads, ffn rows, vocab rows
     rq::XQ xq;      // Tmax rows of max(hidden, intermediate)
     rq::XQ xqd;     // one row of the local intermediate: the down projection's input at decode
+    int* swcnt;     // [I / 32] arrival counters of the decode SwiGLU staging (zero between launches)
     rq::XH xh;      // the same rows staged as f16 hi / lo (tensor-core prefill)
     // device state
     unsigned long long* best;  // packed (value, -index) of the argmax
@@ -640,8 +641,9 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
             } else if (swiglu_in_epilogue(m, L.w[4], L.w[5], T)) {
                 rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
                 const XQ in2[2] = {m->xq, m->xq};
+                const PipeSwiglu sw{m->xqd, m->swcnt, 0};
                 if (!rc) rc = launch_matvec_pipe(w2, in2, y2, 2, m->ctx->sm_count, st, m->derr, nullptr, nullptr,
-                                                 nullptr, &m->xqd);
+                                                 nullptr, &sw);
                 if (!rc) rc = row_parallel(m, L.w[6], T, st, &m->xqd);
                 if (rc) return rc;
                 continue;
@@ -906,6 +908,9 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     uint8_t* xqdbuf = nullptr;
     if (!rc) rc = dalloc(m, &xqbuf, xq_bytes(T, maxin));
     if (!rc) rc = dalloc(m, &xqdbuf, xq_bytes(1, I));
+    if (!rc) rc = dalloc(m, &m->swcnt, (size_t)(I / 32 + 1));
+    if (!rc) rc = cuda_error(cudaMemset(m->swcnt, 0, sizeof(int) * (size_t)(I / 32 + 1)), "counter reset");
+    if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "counter reset");
     if (!rc && T >= kMinTensorM) rc = dalloc(m, &xhbuf, xh_bytes(T, maxin));
     if (!rc) rc = dalloc(m, &m->best, 1);
     if (!rc) rc = dalloc(m, &m->keys, (size_t)T);

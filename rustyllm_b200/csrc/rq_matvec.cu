@@ -179,17 +179,19 @@ mv_q3k_kernel(const uint8_t* __restrict__ qs, const uint8_t* __restrict__ hdr,
         const int64_t gidx = s0 * 32 + lane;
         const int64_t sb = gidx >> 2;
         if (sb < nsb) {
+            // expanded layout: 128 nibble bytes and a 20-byte header per super-block
+            const int g = (int)(gidx & 3), h1 = (lane >> 2) & 1;
             Q3KLane L;
-            q3k_lane_setup(L, planes, stats, in, sb, (int)(gidx & 3));
+            q3k_lane_setup(L, planes, stats, in, sb, g, h1, true);
 #pragma unroll
             for (int r = 0; r < R; r++) {
                 const int64_t row = row0 + r;
                 if (row < out) {
                     const int64_t bi = row * nsb + sb;
-                    const uint8_t* base = qs + bi * 96;
-                    part[r] += q3k_lane_row(L, ldg_stream(base + 16 * L.u),
-                                            ldg_stream(base + 32 + 32 * L.h + 16 * L.u),
-                                            ldg_stream(hdr + bi * 16));
+                    const uint8_t* base = qs + bi * 128 + 32 * g;
+                    const uint32_t* hw = reinterpret_cast<const uint32_t*>(hdr + bi * 20);
+                    part[r] += q3k_lane_row(L, ldg_stream(base + 16 * h1), ldg_stream(base + 16 * (1 - h1)),
+                                            hw[g], hw[4]);
                 }
             }
         }

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "rq_internal.cuh"
+#include "rq_mv_common.cuh"
 
 struct rq_moe {
     rq_ctx* ctx;
@@ -58,6 +59,7 @@ struct rq_moe {
     uint8_t* xq_h = nullptr;     // ... of the swiglu rows
     uint8_t* xh_x = nullptr;     // tensor-core staging of the rows
     uint8_t* xh_h = nullptr;     // ... of the swiglu rows
+    int* swcnt = nullptr;        // [R][F/32] SwiGLU staging arrival counters (zero between launches)
     std::vector<void*> bufs_r;
 };
 
@@ -81,9 +83,11 @@ __host__ __device__ inline int router_chunk(int E) {
     return ch - ch % 8;
 }
 
+// With planes given, the CTA also stages its token's row of x for the
+// pipeline matvec (xquant_kernel's arithmetic) into row t of (planes, stats).
 __global__ void router_kernel(const float* __restrict__ x, const __half* __restrict__ wr, int64_t H,
                               int E, int k, float* __restrict__ logits, int32_t* __restrict__ ids,
-                              float* __restrict__ wts) {
+                              float* __restrict__ wts, int8_t* __restrict__ planes, float4* __restrict__ stats) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     extern __shared__ __align__(16) uint8_t rsm[];
@@ -149,6 +153,12 @@ __global__ void router_kernel(const float* __restrict__ x, const __half* __restr
             wts[t * k + r] = p[pick[r]] / s;
         }
     }
+    if (planes)
+        for (int64_t b = threadIdx.x; b < H / 32; b += blockDim.x) {
+            float v[32];
+            load_block(xr + b * 32, v);
+            stage_block(v, t, b, H, planes, stats);
+        }
 }
 
 // Single CTA: expert buckets in ascending token order.  offs[E+1];
@@ -323,6 +333,10 @@ int ensure_r(rq_moe* m, int64_t R) {
     if (!rc) rc = grow(b, &m->xq_h, xq_bytes(R, m->F));
     if (!rc) rc = grow(b, &m->xh_x, xh_bytes(R, m->H));
     if (!rc) rc = grow(b, &m->xh_h, xh_bytes(R, m->F));
+    if (!rc) rc = grow(b, &m->swcnt, (size_t)(R * (m->F / 32)));
+    // zeroed before any stream of the caller can use them
+    if (!rc) rc = cuda_error(cudaMemset(m->swcnt, 0, sizeof(int) * (size_t)(R * (m->F / 32))), "counter reset");
+    if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "counter reset");
     m->cap_r = rc ? 0 : R;
     return rc;
 }
@@ -481,34 +495,36 @@ int expert_ffn(rq_moe* m, const float* rows, int64_t R, const std::vector<Seg>& 
     return rc;
 }
 
-// out[s] = FFN_{expert of slot s}(rows[s]) for the S slots of a batch whose
-// every expert segment is shorter than kMinTensorM rows (T < kMinTensorM):
-// one M=1 pipeline job per slot, as expert_ffn would run them, but the
-// expert of each job is read by the matvec kernel from the routing table on
-// the device -- no host synchronisation, so the layer can be captured in a
-// CUDA graph.  Same jobs, same kernels, same bits as the host plan.
-int expert_ffn_slots(rq_moe* m, const float* rows, int64_t S, float* out, cudaStream_t st) {
-    const int64_t H = m->H, F = m->F;
+// The T < kMinTensorM forward with the plan on the device: routing slots in
+// token-major order (slot t k + r is the r-th pick of token t, its expert
+// ids[slot]), token t's row staged by the router kernel into row t of xq_x.
+// Gate and up of kMaxJobs / 2 slots per launch, silu(gate) * up staged in
+// their epilogue into row `slot` of xq_h; then the down projections of
+// kMaxJobs / k whole tokens per launch, the weighted combine in their
+// epilogue, straight into y.  Three launches for T k <= kMaxJobs / 2 with the
+// router: every slot's product has the bits of the host-planned path (the
+// same kernels on the same rows), and combine sums in ascending expert order.
+int expert_ffn_tokens(rq_moe* m, int64_t T, float* yd, cudaStream_t st) {
+    const int64_t H = m->H, F = m->F, k = m->k, S = T * k;
     const int sm = m->ctx->sm_count;
     int* err = m->ctx->derr;
-    const XQ xqx = xq_view(m->xq_x, S, H), xqh = xq_view(m->xq_h, S, F);
+    const XQ xqx = xq_view(m->xq_x, T, H), xqh = xq_view(m->xq_h, S, F);
     PipeDevWeights dw;
     memset(&dw, 0, sizeof dw);
-    dw.slot_e = m->slot_e;
+    dw.slot_e = m->ids;
     for (int kind = 0; kind < 3; kind++) {
         dw.qs[kind] = m->wtab + (size_t)(2 * kind) * m->E;
         dw.hdr[kind] = m->wtab + (size_t)(2 * kind + 1) * m->E;
     }
-    int rc = launch_xquant(rows, S, H, xqx, st);
-    // gate and up of each slot, kMaxJobs / 2 slots per launch
+    const rq_weight* ws[kMaxJobs];
+    XQ xs[kMaxJobs];
+    float* ys[kMaxJobs];
+    int rc = RQ_OK;
     for (int64_t s0 = 0; !rc && s0 < S; s0 += kMaxJobs / 2) {
         const int n = (int)std::min<int64_t>(kMaxJobs / 2, S - s0);
-        const rq_weight* ws[kMaxJobs];
-        XQ xs[kMaxJobs];
-        float* ys[kMaxJobs];
         for (int i = 0; i < n; i++) {
-            const int64_t s = s0 + i;
-            const XQ xr{xqx.planes + s * 3 * H, xqx.stats + s * (H / 32)};
+            const int64_t s = s0 + i, t = s / k;
+            const XQ xr{xqx.planes + t * 3 * H, xqx.stats + t * (H / 32)};
             ws[2 * i] = m->w1[0];
             ws[2 * i + 1] = m->w3[0];
             xs[2 * i] = xs[2 * i + 1] = xr;
@@ -518,25 +534,49 @@ int expert_ffn_slots(rq_moe* m, const float* rows, int64_t S, float* out, cudaSt
             dw.kind[2 * i] = 0;
             dw.kind[2 * i + 1] = 1;
         }
-        rc = launch_matvec_pipe(ws, xs, ys, 2 * n, sm, st, err, nullptr, nullptr, &dw);
+        const PipeSwiglu sw{xqh, m->swcnt, (int)s0};
+        rc = launch_matvec_pipe(ws, xs, ys, 2 * n, sm, st, err, nullptr, nullptr, &dw, &sw);
     }
-    if (!rc) rc = launch_xquant_swiglu(m->g, m->u, S, F, xqh, st);
-    for (int64_t s0 = 0; !rc && s0 < S; s0 += kMaxJobs) {
-        const int n = (int)std::min<int64_t>(kMaxJobs, S - s0);
-        const rq_weight* ws[kMaxJobs];
-        XQ xs[kMaxJobs];
-        float* ys[kMaxJobs];
+    const int64_t per = kMaxJobs / k;  // whole tokens per down launch
+    for (int64_t t0 = 0; !rc && t0 < T; t0 += per) {
+        const int n = (int)(std::min<int64_t>(per, T - t0) * k);
+        const int64_t s0 = t0 * k;
         for (int i = 0; i < n; i++) {
             const int64_t s = s0 + i;
             ws[i] = m->w2[0];
             xs[i] = XQ{xqh.planes + s * 3 * F, xqh.stats + s * (F / 32)};
-            ys[i] = out + s * H;
+            ys[i] = m->o + s * H;
             dw.slot[i] = (int)s;
             dw.kind[i] = 2;
         }
-        rc = launch_matvec_pipe(ws, xs, ys, n, sm, st, err, nullptr, nullptr, &dw);
+        const PipeCombine cb{m->ids, m->wts, yd, (int)k, (int)s0};
+        rc = launch_matvec_pipe(ws, xs, ys, n, sm, st, err, nullptr, nullptr, &dw, nullptr, &cb);
     }
     return rc;
+}
+
+// Router of the T local tokens (logits, ids, wts), staging their rows into
+// `stage` when given.
+int launch_router(rq_moe* m, const float* xs, int64_t T, const XQ* stage, cudaStream_t st) {
+    const int E = m->E, k = m->k;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl(dim3((unsigned)T), dim3((unsigned)(32 * E)), st, attr);
+    const int ch = router_chunk(E);
+    cfg.dynamicSmemBytes = (size_t)ch * 4 + (size_t)E * ch * 2;
+    return cuda_error(cudaLaunchKernelEx(&cfg, router_kernel, xs, (const __half*)m->router, m->H, E, k, m->logits,
+                                         m->ids, m->wts, stage ? stage->planes : (int8_t*)nullptr,
+                                         stage ? stage->stats : (float4*)nullptr),
+                      "router kernel");
+}
+
+// Expert-major permutation of the routed slots (offs, perm, slot_w, tok_slot,
+// slot_e).
+int launch_permute(rq_moe* m, int64_t T, cudaStream_t st) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl(dim3(1), dim3(1024), st, attr);
+    return cuda_error(cudaLaunchKernelEx(&cfg, permute_kernel, (const int32_t*)m->ids, (const float*)m->wts, T, m->E,
+                                         m->k, m->offs, m->perm, m->slot_w, m->tok_slot, m->slot_e),
+                      "permute kernel");
 }
 
 // Router and permutation of the T local tokens; with offs / perm given they
@@ -545,17 +585,8 @@ int expert_ffn_slots(rq_moe* m, const float* rows, int64_t S, float* out, cudaSt
 int route(rq_moe* m, const float* xs, int64_t T, std::vector<int32_t>* offs, std::vector<int32_t>* perm,
           cudaStream_t st) {
     const int E = m->E, k = m->k;
-    cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = pdl(dim3((unsigned)T), dim3((unsigned)(32 * E)), st, attr);
-    const int ch = router_chunk(E);
-    cfg.dynamicSmemBytes = (size_t)ch * 4 + (size_t)E * ch * 2;
-    int rc = cuda_error(cudaLaunchKernelEx(&cfg, router_kernel, xs, (const __half*)m->router, m->H, E, k, m->logits,
-                                           m->ids, m->wts), "router kernel");
-    if (!rc) {
-        cudaLaunchConfig_t cfg2 = pdl(dim3(1), dim3(1024), st, attr);
-        rc = cuda_error(cudaLaunchKernelEx(&cfg2, permute_kernel, (const int32_t*)m->ids, (const float*)m->wts, T, E,
-                                           k, m->offs, m->perm, m->slot_w, m->tok_slot, m->slot_e), "permute kernel");
-    }
+    int rc = launch_router(m, xs, T, nullptr, st);
+    if (!rc) rc = launch_permute(m, T, st);
     if (!offs) return rc;
     offs->assign((size_t)E + 1, 0);
     perm->assign((size_t)(T * k), 0);
@@ -577,9 +608,12 @@ int combine(rq_moe* m, int64_t T, float* yd, cudaStream_t st) {
 
 // Shared front and back of both forwards: x to the device (when needed),
 // then after `body` y back to the host and the routing outputs.
+// With `fused` (the device-planned path of expert_ffn_tokens) the router
+// stages the rows, the experts write y and the permutation runs only for
+// perm_out; `body` is not called.
 template <class Body>
 int moe_call(rq_moe* m, const float* x, float* y, int64_t T, int32_t* ids_out, int32_t* perm_out, cudaStream_t st,
-             int world, bool host_plan, Body&& body) {
+             int world, bool host_plan, bool fused, Body&& body) {
     int rc = ensure_t(m, T, world);
     if (rc) return rc;
     const int64_t H = m->H, S = T * m->k;
@@ -592,9 +626,17 @@ int moe_call(rq_moe* m, const float* x, float* y, int64_t T, int32_t* ids_out, i
     }
     float* yd = y_dev ? y : m->yd;
     std::vector<int32_t> offs, perm;
-    rc = route(m, xs, T, host_plan ? &offs : nullptr, host_plan ? &perm : nullptr, st);
-    if (!rc) rc = body(xs, offs, perm);
-    if (!rc) rc = combine(m, T, yd, st);
+    if (fused) {
+        rc = ensure_r(m, S);
+        const XQ xqx = xq_view(m->xq_x, T, H);
+        if (!rc) rc = launch_router(m, xs, T, &xqx, st);
+        if (!rc) rc = expert_ffn_tokens(m, T, yd, st);
+        if (!rc && perm_out) rc = launch_permute(m, T, st);
+    } else {
+        rc = route(m, xs, T, host_plan ? &offs : nullptr, host_plan ? &perm : nullptr, st);
+        if (!rc) rc = body(xs, offs, perm);
+        if (!rc) rc = combine(m, T, yd, st);
+    }
     if (!rc && !y_dev)
         rc = cuda_error(cudaMemcpyAsync(y, yd, sizeof(float) * (size_t)(T * H), cudaMemcpyDeviceToHost, st), "y copy");
     if (!rc && ids_out)
@@ -712,17 +754,16 @@ int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
     const int64_t S = T * m->k;
     // below kMinTensorM tokens no expert gets a tensor-core segment, so the
     // kernel of every slot is known without the routing: plan on the device
-    bool dev_plan = T < kMinTensorM;
+    bool dev_plan = T < kMinTensorM && m->k <= kMaxJobs && m->F % 32 == 0;
     for (int e = 0; e < m->E && dev_plan; e++)
         dev_plan = pipe_supported(m->w1[(size_t)e]) && pipe_supported(m->w3[(size_t)e]) &&
                    pipe_supported(m->w2[(size_t)e]);
-    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, 1, !dev_plan,
+    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, 1, !dev_plan, dev_plan,
                     [&](const float* xs, const std::vector<int32_t>& offs, const std::vector<int32_t>&) {
                         int rc = ensure_r(m, S);
                         // token rows in slot (expert-major) order
                         if (!rc) rc = launch_gather(xs, m->perm, S, m->H, m->xg, st);
                         if (rc) return rc;
-                        if (dev_plan) return expert_ffn_slots(m, m->xg, S, m->o, st);
                         std::vector<Seg> segs;
                         for (int e = 0; e < m->E; e++) {
                             const int64_t n = offs[(size_t)e + 1] - offs[(size_t)e];
@@ -804,7 +845,7 @@ int rq_moe_forward_ep(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t 
         std::vector<int32_t> offs((size_t)E + 1, 0), perm;
         return body(x, offs, perm);
     }
-    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, W, true, body);
+    return moe_call(m, x, y, T, expert_ids_out, perm_out, st, W, true, false, body);
 }
 
 }  // extern "C"

@@ -309,61 +309,86 @@ __device__ __forceinline__ uint32_t q4k_scales(const Q4KScaleSel& S, uint4 h) {
 
 // ------------------------------------------------------------------- Q3_K
 
+// Q3_K on the expanded device layout (rq_internal.cuh): q + 4 as nibbles in
+// Q4_K's arrangement, 16 int8 scales and d per super-block.  The lane is the
+// Q4_K pipeline lane's data path (group g = lane % 4 of the super-block,
+// halves in order h1) with one accumulator chain per 16-element sub-block:
+// A lo = sub-block 4g + h1, B lo = 4g + 1 - h1, A hi = 4g + 2 + h1,
+// B hi = 4g + 3 - h1, each scaled by its int8 scale, and the -4 offset of
+// q + 4 taken from the 16-element sums of the staged activations.
 struct Q3KLane {
-    uint32_t p[3][4][4];  // [plane][run s][word]
-    float sx[4], xs16[4];
-    int h, u;
+    uint32_t xa[3][8];  // half A: [plane][0..3 low-nibble words, 4..7 high-nibble words]
+    uint32_t xb[3][8];  // half B
+    float sxl, sxh;     // block scales of the low / high 32 elements (sxh / 16: nibbles in place)
+    float xs[4];        // 4 * sum of x over the sub-blocks A lo, B lo, A hi, B hi
+    uint32_t sel;       // byte permute putting the four scales in that order
 };
 
-__device__ __forceinline__ void q3k_lane_setup(Q3KLane& L, const int8_t* planes,
-                                               const float4* stats, int64_t in, int64_t sb,
-                                               int qq) {
-    L.h = qq >> 1;
-    L.u = qq & 1;
+__device__ __forceinline__ void q3k_lane_setup(Q3KLane& L, const int8_t* planes, const float4* stats, int64_t in,
+                                               int64_t sb, int g, int h1, bool valid) {
+    const int64_t pos = sb * 256 + 64 * g;
 #pragma unroll
-    for (int s = 0; s < 4; s++) {
-        const int64_t pos = sb * 256 + 128 * L.h + 32 * s + 16 * L.u;
+    for (int p = 0; p < 3; p++) {
+        const int8_t* base = planes + p * in + pos;
 #pragma unroll
-        for (int p = 0; p < 3; p++) {
-            const uint4 v = *reinterpret_cast<const uint4*>(planes + p * in + pos);
-            L.p[p][s][0] = v.x; L.p[p][s][1] = v.y; L.p[p][s][2] = v.z; L.p[p][s][3] = v.w;
+        for (int half = 0; half < 2; half++) {
+            const int hsel = half == 0 ? h1 : 1 - h1;
+            uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = make_uint4(0u, 0u, 0u, 0u);
+            if (valid) {
+                lo = *reinterpret_cast<const uint4*>(base + 16 * hsel);
+                hi = *reinterpret_cast<const uint4*>(base + 32 + 16 * hsel);
+            }
+            uint32_t* dst = half == 0 ? L.xa[p] : L.xb[p];
+            dst[0] = lo.x; dst[1] = lo.y; dst[2] = lo.z; dst[3] = lo.w;
+            dst[4] = hi.x; dst[5] = hi.y; dst[6] = hi.z; dst[7] = hi.w;
         }
-        const float4 st = stats[sb * 8 + 4 * L.h + s];
-        L.sx[s] = st.x;
-        L.xs16[s] = L.u ? st.z : st.y;
     }
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+    if (valid) {
+        lo = stats[sb * 8 + 2 * g];
+        hi = stats[sb * 8 + 2 * g + 1];
+    }
+    L.sxl = lo.x;
+    L.sxh = hi.x * 0.0625f;
+    L.xs[0] = 4.0f * (h1 ? lo.z : lo.y);
+    L.xs[1] = 4.0f * (h1 ? lo.y : lo.z);
+    L.xs[2] = 4.0f * (h1 ? hi.z : hi.y);
+    L.xs[3] = 4.0f * (h1 ? hi.y : hi.z);
+    L.sel = h1 ? 0x2301u : 0x3210u;
 }
 
-// hm: hmask bytes [16u, +16); qv: 2-bit quant bytes [32h+16u, +16);
-// hd: header (scales 0..11, d at 12..13).
-__device__ __forceinline__ float q3k_lane_row(const Q3KLane& L, uint4 hm, uint4 qv, uint4 hd) {
-    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-    const uint32_t hw[4] = {hm.x, hm.y, hm.z, hm.w};
-    const float d = __half2float(__ushort_as_half((unsigned short)(hd.w & 0xFFFFu)));
-    const uint32_t lo8[2] = {hd.x, hd.y};
-    float acc = 0.0f;
+// One row: the lane's 32 nibble bytes (qa: half A, qb: half B), the header
+// word holding the int8 scales of sub-blocks 4g..4g+3 and the word holding d.
+__device__ __forceinline__ float q3k_lane_row(const Q3KLane& L, uint4 qa, uint4 qb, uint32_t scw, uint32_t dw) {
+    const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w};
+    const uint32_t wb[4] = {qb.x, qb.y, qb.z, qb.w};
+    int al[3] = {0, 0, 0}, ah[3] = {0, 0, 0}, bl[3] = {0, 0, 0}, bh[3] = {0, 0, 0};
 #pragma unroll
-    for (int s = 0; s < 4; s++) {
-        int a1 = 0, a2 = 0, a3 = 0;
+    for (int k = 0; k < 4; k++) {
+        const uint32_t lo = wa[k] & 0x0F0F0F0Fu, hi = wa[k] & 0xF0F0F0F0u;
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const uint32_t hq = (hw[c] >> (4 * L.h)) & 0x0F0F0F0Fu;
-            const uint32_t ql = (qw[c] >> (2 * s)) & 0x03030303u;
-            const uint32_t hb = (s <= 2 ? (hq << (2 - s)) : (hq >> 1)) & 0x04040404u;
-            const uint32_t q = ql | hb;  // q + 4 in 0..7
-            a1 = dp4a_us(q, L.p[0][s][c], a1);
-            a2 = dp4a_us(q, L.p[1][s][c], a2);
-            a3 = dp4a_us(q, L.p[2][s][c], a3);
+        for (int p = 0; p < 3; p++) {
+            al[p] = dp4a_us(lo, L.xa[p][k], al[p]);
+            ah[p] = dp4a_us(hi, L.xa[p][4 + k], ah[p]);
         }
-        // 6-bit scale of 16-element sub-block 8h + 2s + u
-        const int k = L.u + 2 * s;
-        const int lo4 = (int)((lo8[k >> 2] >> (8 * (k & 3) + 4 * L.h)) & 15u);
-        const int kb = L.u + 2 * (s & 1);
-        const int hi2 = (int)((hd.z >> (8 * kb + 2 * (2 * L.h + (s >> 1)))) & 3u);
-        const float scale = (float)((lo4 | (hi2 << 4)) - 32);
-        acc = fmaf(scale, fmaf(fix24(a1, a2, a3), L.sx[s], -4.0f * L.xs16[s]), acc);
     }
-    return d * acc;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const uint32_t lo = wb[k] & 0x0F0F0F0Fu, hi = wb[k] & 0xF0F0F0F0u;
+#pragma unroll
+        for (int p = 0; p < 3; p++) {
+            bl[p] = dp4a_us(lo, L.xb[p][k], bl[p]);
+            bh[p] = dp4a_us(hi, L.xb[p][4 + k], bh[p]);
+        }
+    }
+    const uint32_t sc = __byte_perm(scw, 0u, L.sel);
+    const float s0 = (float)((int)(sc << 24) >> 24), s1 = (float)((int)(sc << 16) >> 24);
+    const float s2 = (float)((int)(sc << 8) >> 24), s3 = (float)((int)sc >> 24);
+    float part = s0 * fmaf(fix24(al[0], al[1], al[2]), L.sxl, -L.xs[0]);
+    part = fmaf(s1, fmaf(fix24(bl[0], bl[1], bl[2]), L.sxl, -L.xs[1]), part);
+    part = fmaf(s2, fmaf(fix24(ah[0], ah[1], ah[2]), L.sxh, -L.xs[2]), part);
+    part = fmaf(s3, fmaf(fix24(bh[0], bh[1], bh[2]), L.sxh, -L.xs[3]), part);
+    return __half2float(__ushort_as_half((unsigned short)(dw & 0xFFFFu))) * part;
 }
 
 // ------------------------------------------------------------------- Q4_0

@@ -63,16 +63,17 @@ struct PipeParams {
     P2PArgs ar;
     int dev_w;            // 1: weights resolved on the device (dw)
     PipeDevWeights dw;
-    int sw;               // 1: stage silu(y_0) * y_1 into swq instead of writing y
-    XQ swq;
+    int sw;               // 1: SwiGLU staging epilogue (swg)
+    PipeSwiglu swg;
+    int cmb;              // 1: sparse-MoE combine epilogue (cm)
+    PipeCombine cm;
 };
 
-// This CTA's rows of a job; in whole 32-row blocks when the epilogue stages
-// SwiGLU blocks (sw).
-__device__ __forceinline__ void job_rows(const PipeJob& j, int sw, int64_t* rb, int* n) {
-    const int64_t unit = sw ? 32 : 1, units = j.out / unit;
-    const int64_t b = (int64_t)blockIdx.x * units / gridDim.x * unit;
-    const int64_t e = (int64_t)(blockIdx.x + 1) * units / gridDim.x * unit;
+// This CTA's rows of a job: an even split of the job's rows over the grid,
+// the same range for every job of one shape.
+__device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) {
+    const int64_t b = (int64_t)blockIdx.x * j.out / gridDim.x;
+    const int64_t e = (int64_t)(blockIdx.x + 1) * j.out / gridDim.x;
     *rb = b;
     *n = (int)(e - b);
 }
@@ -85,7 +86,7 @@ __device__ __forceinline__ void allreduce_rows(const PipeParams& p, const float*
     const PipeJob& jb = p.jobs[0];
     int64_t rb;
     int nrows;
-    job_rows(jb, p.sw, &rb, &nrows);
+    job_rows(jb, &rb, &nrows);
     uint8_t* own = p.ar.base[p.ar.rank];
     uint32_t* ctl = reinterpret_cast<uint32_t*>(own + kP2PCtlOff);  // epoch, done, err
     const uint32_t e = *reinterpret_cast<volatile uint32_t*>(ctl);
@@ -139,6 +140,79 @@ __device__ __forceinline__ void allreduce_rows(const PipeParams& p, const float*
     }
 }
 
+// SwiGLU staging after y is written (see PipeSwiglu): a thread per 32-row
+// block this CTA touched adds the CTA's gate and up rows of the block to the
+// block's arrival counter; the thread that brings it to 64 reads the block's
+// 32 gate and 32 up values back from L2, stages silu(g) * u
+// (xquant_swiglu_kernel's arithmetic) and zeroes the counter.
+__device__ __forceinline__ void swiglu_blocks(const PipeParams& p) {
+    __threadfence();  // this thread's y rows are visible before any count
+    __syncthreads();
+    const PipeJob& j0 = p.jobs[0];
+    int64_t rb;
+    int nrows;
+    job_rows(j0, &rb, &nrows);
+    if (nrows == 0) return;
+    const int64_t nb = j0.out / 32, b0 = rb / 32;
+    const int nbt = (int)((rb + nrows - 1) / 32 - b0 + 1), npair = p.njobs / 2;
+    for (int i = threadIdx.x; i < npair * nbt; i += blockDim.x) {
+        const int pr = i / nbt;
+        const int64_t b = b0 + i % nbt;
+        const int64_t lo = max(rb, 32 * b), hi = min(rb + nrows, 32 * b + 32);
+        const int add = 2 * (int)(hi - lo);
+        const int64_t row = p.swg.row0 + pr;
+        int* cnt = p.swg.cnt + row * nb + b;
+        __threadfence();
+        if (atomicAdd(cnt, add) + add != 64) continue;
+        __threadfence();
+        const float* g = p.jobs[2 * pr].y + 32 * b;
+        const float* u = p.jobs[2 * pr + 1].y + 32 * b;
+        float v[32];
+#pragma unroll
+        for (int k = 0; k < 32; k++) {
+            const float gv = __ldcg(g + k), uv = __ldcg(u + k);
+            v[k] = gv / (1.0f + expf(-gv)) * uv;
+        }
+        stage_block(v, row, b, j0.out, p.swg.xq.planes, p.swg.xq.stats);
+        atomicExch(cnt, 0);
+    }
+}
+
+// Sparse-MoE combine (see PipeCombine): the k slots of a token are
+// consecutive jobs over the same rows of this CTA, so every output row is
+// finished here: the slot outputs (partials summed in slice order, the bits
+// of y) weighted and summed in ascending expert order from zero.
+__device__ __forceinline__ void combine_rows(const PipeParams& p, const float* red) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // ids and wts of the routing kernel
+    const int k = p.cm.k, ntok = p.njobs / k;
+    int64_t rb;
+    int nrows;
+    job_rows(p.jobs[0], &rb, &nrows);
+    const int64_t H = p.jobs[0].out;
+    for (int tt = 0; tt < ntok; tt++) {
+        const int s0 = p.cm.slot0 + tt * k;
+        int ord[kMaxJobs];
+        for (int r = 0; r < k; r++) ord[r] = r;
+        for (int a = 1; a < k; a++)
+            for (int b = a; b > 0 && p.cm.ids[s0 + ord[b - 1]] > p.cm.ids[s0 + ord[b]]; b--) {
+                const int t = ord[b];
+                ord[b] = ord[b - 1];
+                ord[b - 1] = t;
+            }
+        float* out = p.cm.out + (int64_t)(s0 / k) * H;
+        for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
+            float acc = 0.0f;
+            for (int r = 0; r < k; r++) {
+                const int j = tt * k + ord[r];
+                float o = 0.0f;
+                for (int s = 0; s < p.S; s++) o += red[(j * nrows + i) * p.S + s];
+                acc = __fadd_rn(acc, __fmul_rn(o, p.cm.wts[s0 + ord[r]]));
+            }
+            out[rb + i] = acc;
+        }
+    }
+}
+
 template <int TYPE, int RPW>
 __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -170,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
                 const PipeJob& jb = p.jobs[j];
                 int64_t rb;
                 int nrows;
-                job_rows(jb, p.sw, &rb, &nrows);
+                job_rows(jb, &rb, &nrows);
                 const uint8_t* jqs = jb.qs;
                 const uint8_t* jhdr = jb.hdr;
                 if (p.dev_w) {
@@ -208,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
             const PipeJob& jb = p.jobs[j];
             int64_t rb;
             int nrows;
-            job_rows(jb, p.sw, &rb, &nrows);
+            job_rows(jb, &rb, &nrows);
             if (jb.xq.planes != cur_x) {  // jobs that share x keep the planes
                 lane_setup<TYPE>(L, o, p.nblk, p.in, jb.xq, s, lane);
                 cur_x = jb.xq.planes;
@@ -245,33 +319,15 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         allreduce_rows(p, red);
         return;
     }
-    if (p.sw) {
-        // gate rows at red[0 ..), up rows after them: one thread per 32-row
-        // block computes both sums in slice order (the bits of y), then
-        // silu(g) * u and its staged form (xquant_swiglu_kernel's arithmetic)
-        int64_t rb;
-        int nrows;
-        job_rows(p.jobs[0], 1, &rb, &nrows);
-        for (int b = threadIdx.x; b < nrows / 32; b += blockDim.x) {
-            float v[32];
-#pragma unroll 4
-            for (int k = 0; k < 32; k++) {
-                float g = 0.0f, u = 0.0f;
-                for (int s = 0; s < p.S; s++) {
-                    g += red[(32 * b + k) * p.S + s];
-                    u += red[(nrows + 32 * b + k) * p.S + s];
-                }
-                v[k] = g / (1.0f + expf(-g)) * u;
-            }
-            stage_block(v, 0, rb / 32 + b, p.jobs[0].out, p.swq.planes, p.swq.stats);
-        }
+    if (p.cmb) {
+        combine_rows(p, red);
         return;
     }
     int roff = 0;
     for (int j = 0; j < p.njobs; j++) {
         int64_t rb;
         int nrows;
-        job_rows(p.jobs[j], p.sw, &rb, &nrows);
+        job_rows(p.jobs[j], &rb, &nrows);
         const float* add = p.jobs[j].add;
         for (int t = threadIdx.x; t < nrows; t += blockDim.x) {
             float acc = 0.0f;
@@ -280,6 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         }
         roff += nrows;
     }
+    if (p.sw) swiglu_blocks(p);
 }
 
 template <int TYPE, int RPW>
@@ -327,7 +384,7 @@ bool pipe_supported(const rq_weight* w) {
 
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar,
-                       const PipeDevWeights* dw, const XQ* swiglu_to) {
+                       const PipeDevWeights* dw, const PipeSwiglu* sw, const PipeCombine* cmb) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "matvec pipeline: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     TypeInfo ti = type_info(w0->type);
@@ -344,12 +401,24 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
     p.err = err;
     p.dev_w = dw ? 1 : 0;
     if (dw) p.dw = *dw;
+    bool same_shape = true;
+    for (int j = 1; j < njobs; j++) same_shape = same_shape && ws[j]->out == w0->out;
+    bool any_add = false;
+    for (int j = 0; adds && j < njobs; j++) any_add = any_add || adds[j];
     p.sw = 0;
-    if (swiglu_to) {
-        if (njobs != 2 || ar || ws[0]->out != ws[1]->out || ws[0]->out % 32 || (adds && (adds[0] || adds[1])))
-            return set_error(RQ_ERR_INVALID, "matvec pipeline: SwiGLU staging needs gate and up of one shape");
+    p.cmb = 0;
+    if (sw) {
+        if (njobs % 2 || !same_shape || ar || cmb || any_add || w0->out % 32 || !sw->cnt || sw->row0 < 0)
+            return set_error(RQ_ERR_INVALID, "matvec pipeline: SwiGLU staging needs gate/up pairs of one shape");
         p.sw = 1;
-        p.swq = *swiglu_to;
+        p.swg = *sw;
+    }
+    if (cmb) {
+        if (cmb->k < 1 || njobs % cmb->k || cmb->slot0 < 0 || cmb->slot0 % cmb->k || !same_shape || ar || any_add ||
+            !cmb->ids || !cmb->wts || !cmb->out)
+            return set_error(RQ_ERR_INVALID, "matvec pipeline: combine needs whole tokens of one shape");
+        p.cmb = 1;
+        p.cm = *cmb;
     }
     p.nblk = w0->nblk;
     p.in = w0->in;
@@ -371,7 +440,7 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
     auto rows_cap = [&](int gr) {
         int64_t r = 0;
         for (int j = 0; j < njobs; j++)
-            r += swiglu_to ? (ws[j]->out / 32 + gr - 1) / gr * 32 : (ws[j]->out + gr - 1) / gr;
+            r += (ws[j]->out + gr - 1) / gr;
         return r;
     };
     while (rows_cap(grid) * p.S * 4 > 32 * 1024) grid *= 2;

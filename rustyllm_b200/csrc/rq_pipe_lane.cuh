@@ -113,19 +113,13 @@ __device__ __forceinline__ void lane_setup(typename LaneOf<TYPE>::T& L, LaneOffs
             o.qa = (uint32_t)(s * 1024) + 128u * sbl + 32u * (uint32_t)(lane & 3) + 16u * ((lane >> 2) & 1u);
             o.qb = o.qa ^ 16u;
         } else {
-            q3k_lane_setup(L, xq.planes, xq.stats, in, valid ? sb : 0, lane & 3);
-            if (!valid) {
-#pragma unroll
-                for (int q = 0; q < 3; q++)
-#pragma unroll
-                    for (int r = 0; r < 4; r++)
-#pragma unroll
-                        for (int c = 0; c < 4; c++) L.p[q][r][c] = 0u;
-#pragma unroll
-                for (int r = 0; r < 4; r++) L.sx[r] = L.xs16[r] = 0.0f;
-            }
-            o.qa = (uint32_t)(s * 768) + 96u * sbl + 16u * (uint32_t)L.u;  // hmask
-            o.qb = (uint32_t)(s * 768) + 96u * sbl + 32u + 32u * (uint32_t)L.h + 16u * (uint32_t)L.u;
+            // Q3_K, expanded: Q4_K's nibble offsets, 20-byte headers
+            q3k_lane_setup(L, xq.planes, xq.stats, in, valid ? sb : 0, lane & 3, (lane >> 2) & 1, valid);
+            o.qa = (uint32_t)(s * 1024) + 128u * sbl + 32u * (uint32_t)(lane & 3) + 16u * ((lane >> 2) & 1u);
+            o.qb = o.qa ^ 16u;
+            o.h = (uint32_t)(s * 8 * 20) + 20u * sbl + 4u * (uint32_t)(lane & 3);
+            o.hd = (uint32_t)(s * 8 * 20) + 20u * sbl + 16u;
+            return;
         }
         o.h = (uint32_t)(s * 128) + 16u * sbl;
     }
@@ -161,7 +155,8 @@ __device__ __forceinline__ float lane_row(const typename LaneOf<TYPE>::T& L, con
     } else if constexpr (TYPE == RQ_Q4_K) {
         return q4kp_lane_row(L, a, b, *reinterpret_cast<const uint4*>(h + o.h), 0.0f);
     } else if constexpr (TYPE == RQ_Q3_K) {
-        return q3k_lane_row(L, a, b, *reinterpret_cast<const uint4*>(h + o.h));
+        return q3k_lane_row(L, a, b, *reinterpret_cast<const uint32_t*>(h + o.h),
+                            *reinterpret_cast<const uint32_t*>(h + o.hd));
     } else {
         // a is the half selected by lane bit 2; swap back to blocks (b0, b0+1)
         const bool swap = (o.qa & 16u) != 0u;

@@ -266,7 +266,7 @@ bool tp_fused_enabled(int world) {
         if (e && strcmp(e, "1") == 0) return 1;
         return 2;  // default
     }();
-    return mode == 1 || (mode == 2 && world == 2);
+    return mode != 0 && (mode == 1 || world >= 2);
 }
 
 bool tp_p2p_args(const rq_ctx* ctx, P2PArgs* a) {

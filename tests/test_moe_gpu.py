@@ -49,6 +49,25 @@ def test_moe_matches_oracle(oracle, rq_ctx, T):
     assert rel_l2(y, y_ref) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("T", [1, 3])
+def test_moe_top3_combine_order(oracle, rq_ctx, T):
+    """top_k = 3 below four tokens: the down projections of a token's three
+    slots combine in ascending expert order inside the matvec epilogue
+    (with k = 3 the order changes the bits); T = 3 takes three gate/up
+    launches and two down launches."""
+    from rustyllm_b200.mixtral import SparseMoe
+    E, H, F = 8, 512, 1024
+    wr, blocks, experts = make_layer(oracle, rq_ctx, E, H, F, 12, seed=900 + T)
+    moe = SparseMoe(wr, experts, top_k=3)
+    x = np.random.default_rng(910 + T).standard_normal((T, H)).astype(np.float32)
+    y, ids, perm = moe.forward_with_routing(x)
+    y_ref, ids_ref, perm_ref, _ = oracle.moe_forward(x, wr, 12, blocks["w1"], blocks["w3"], blocks["w2"], F, k=3)
+    assert np.array_equal(ids, ids_ref)
+    assert np.array_equal(perm, perm_ref)
+    assert rel_l2(y, y_ref) <= REL_L2_TOL
+    moe.close()
+
+
 def test_moe_device_tensors_and_ties(oracle, rq_ctx):
     """Device in/out, and a router with exact ties (all-zero router row
     weights for some experts): the lower expert index must win."""
