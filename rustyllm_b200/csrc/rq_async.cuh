@@ -62,6 +62,11 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(mbar), "l"(policy)
         : "memory");
 }
+// bytes of global memory from src into L2 (no destination in this CTA);
+// src 16-byte aligned, bytes a multiple of 16
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));

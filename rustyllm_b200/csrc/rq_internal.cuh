@@ -220,11 +220,28 @@ struct PipeCombine {
     float* out;          // [tokens][out]
     int k, slot0;
 };
+// L2 prefetch of the weights the next launch in the stream will read: once
+// the producer has issued its last copy, it prefetches into L2 (bulk
+// prefetch, no shared memory) the first `budget` bytes of the rows its CTA
+// index will own in that launch (grid = the SM count), so HBM keeps
+// streaming through this launch's tail, the launch gap and the kernels in
+// between (attention).  A hint only: nothing reads the prefetched lines
+// except the next launch's ordinary copies.
+constexpr int kMaxNext = 3;
+struct PipeNext {
+    const uint8_t* qs[kMaxNext];
+    const uint8_t* hdr[kMaxNext];
+    int64_t out[kMaxNext];  // rows of each weight
+    uint32_t qrow, hrow;    // device bytes per row (quant part, header part)
+    int n;                  // weights (0: no prefetch)
+    uint32_t budget;        // bytes per CTA over all n weights
+};
+PipeNext pipe_next(const rq_weight* const* ws, int n, uint32_t budget);
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err = nullptr,
                        const float* const* adds = nullptr, const P2PArgs* ar = nullptr,
                        const PipeDevWeights* dw = nullptr, const PipeSwiglu* sw = nullptr,
-                       const PipeCombine* cmb = nullptr);
+                       const PipeCombine* cmb = nullptr, const PipeNext* next = nullptr);
 
 // small-M Q4_K matmul on the tensor cores (rq_mm_small.cu).  Activations are
 // staged per row as x / s = hi + lo (two f16 values per element, s a power of

@@ -21,6 +21,7 @@
 // QuantStreamCache::new does.
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -66,6 +67,7 @@ struct rq_llama {
     rq::XQ xq;      // Tmax rows of max(hidden, intermediate)
     rq::XQ xqd;     // one row of the local intermediate: the down projection's input at decode
     int* swcnt;     // [I / 32] arrival counters of the decode SwiGLU staging (zero between launches)
+    rq::PipeNext nx{};  // L2 prefetch hint for the decode matvec being launched (nx.n = 0: none)
     rq::XH xh;      // the same rows staged as f16 hi / lo (tensor-core prefill)
     // device state
     unsigned long long* best;  // packed (value, -index) of the argmax
@@ -422,6 +424,30 @@ int launch_simple(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream
     return cuda_error(cudaLaunchKernelExC(&cfg, fn, args), what);
 }
 
+// Decode (T = 1) prefetch hints: each matvec of the layer chain prefetches
+// into L2 the first rows of the weights the next matvec reads (see
+// PipeNext); the q/k/v matvec prefetches all of o_proj, whose launch waits
+// for attention.  RQ_L2_PREFETCH=0 turns the hints off.
+constexpr uint32_t kNextBudget = 128 * 1024;     // bytes per CTA across a launch boundary
+constexpr uint32_t kNextBudgetAttn = 288 * 1024; // q/k/v -> o: attention runs in between
+
+bool l2_prefetch_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("RQ_L2_PREFETCH");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+
+void set_next(rq_llama* m, const rq_weight* const* ws, int n, uint32_t budget) {
+    m->nx = PipeNext{};
+    if (n > 0 && l2_prefetch_enabled()) m->nx = pipe_next(ws, n, budget);
+}
+
+const PipeNext* next_hint(const rq_llama* m) { return m->nx.n > 0 ? &m->nx : nullptr; }
+
+
 // y_i[t] = x[t] W_i^T (+ add_i[t]) for the n weights (same in) and T staged rows.
 int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* const* ys,
                 const float* const* adds, cudaStream_t st) {
@@ -445,7 +471,9 @@ int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float
                     nj = 0;
                 }
             }
-        return nj ? launch_matvec_pipe(jw, jx, jy, nj, sm, st, m->derr, ja) : RQ_OK;
+        return nj ? launch_matvec_pipe(jw, jx, jy, nj, sm, st, m->derr, ja, nullptr, nullptr, nullptr, nullptr,
+                                       T == 1 ? next_hint(m) : nullptr)
+                  : RQ_OK;
     }
     for (int i = 0; i < n; i++) {
         if (adds && adds[i] && adds[i] != ys[i])
@@ -479,7 +507,9 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st, co
         const rq_weight* w1[1] = {w};
         float* y1[1] = {m->x};
         const float* a1[1] = {m->x};
-        if (staged) return launch_matvec_pipe(w1, &xin, y1, 1, m->ctx->sm_count, st, m->derr, a1);
+        if (staged)
+            return launch_matvec_pipe(w1, &xin, y1, 1, m->ctx->sm_count, st, m->derr, a1, nullptr, nullptr, nullptr,
+                                      nullptr, next_hint(m));
         return run_linears(m, 1, w1, T, y1, a1, st);
     }
     const rq_weight* w1[1] = {w};
@@ -488,12 +518,14 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st, co
         const XQ xq = xin;
         float* y = m->x;
         const float* add = m->R == 0 ? m->x : nullptr;
-        const int rc = launch_matvec_pipe(w1, &xq, &y, 1, m->ctx->sm_count, st, m->derr, &add, &ar);
+        const int rc = launch_matvec_pipe(w1, &xq, &y, 1, m->ctx->sm_count, st, m->derr, &add, &ar, nullptr,
+                                          nullptr, nullptr, next_hint(m));
         if (rc != kPipeNotFusable) return rc;
     }
     float* y1[1] = {m->part};
     const float* a1[1] = {m->R == 0 ? m->x : nullptr};
-    int rc = staged ? launch_matvec_pipe(w1, &xin, y1, 1, m->ctx->sm_count, st, m->derr, a1)
+    int rc = staged ? launch_matvec_pipe(w1, &xin, y1, 1, m->ctx->sm_count, st, m->derr, a1, nullptr, nullptr,
+                                         nullptr, nullptr, next_hint(m))
                     : run_linears(m, 1, w1, T, y1, a1, st);
     if (!rc) rc = tp_allreduce(m->ctx, m->part, m->x, T * m->cfg.hidden, 0, 0, st);
     return rc;
@@ -586,7 +618,9 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
                 if (!rc) rc = run_mm(m, 3, w3, T, y3, nullptr, st);
             } else {
                 rc = launch_xquant_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xq, st);
+                if (T == 1) set_next(m, &L.w[3], 1, kNextBudgetAttn);
                 if (!rc) rc = run_linears(m, 3, w3, T, y3, nullptr, st);
+                set_next(m, nullptr, 0, 0);
             }
             if (rc) return rc;
         }
@@ -630,7 +664,9 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
             rc = tc ? launch_xh_stage(m->att, T, nq, m->xh, st) : launch_xquant(m->att, T, nq, m->xq, st);
             if (rc) return rc;
         }
+        if (T == 1 && !tc) set_next(m, &L.w[4], 2, kNextBudget);
         rc = tc ? row_parallel_mm(m, L.w[3], T, st) : row_parallel(m, L.w[3], T, st);
+        set_next(m, nullptr, 0, 0);
         if (rc) return rc;
         {
             const rq_weight* w2[2] = {L.w[4], L.w[5]};
@@ -642,9 +678,14 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
                 rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
                 const XQ in2[2] = {m->xq, m->xq};
                 const PipeSwiglu sw{m->xqd, m->swcnt, 0};
+                set_next(m, &L.w[6], 1, kNextBudget);
                 if (!rc) rc = launch_matvec_pipe(w2, in2, y2, 2, m->ctx->sm_count, st, m->derr, nullptr, nullptr,
-                                                 nullptr, &sw);
+                                                 nullptr, &sw, nullptr, next_hint(m));
+                // down prefetches the next layer's q/k/v
+                if (l + 1 < c.n_layers) set_next(m, m->layers[l + 1].w, 3, kNextBudget);
+                else set_next(m, nullptr, 0, 0);
                 if (!rc) rc = row_parallel(m, L.w[6], T, st, &m->xqd);
+                set_next(m, nullptr, 0, 0);
                 if (rc) return rc;
                 continue;
             } else {

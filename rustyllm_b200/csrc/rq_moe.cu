@@ -21,6 +21,7 @@
 #include <algorithm>
 #include <vector>
 
+#include "rq_async.cuh"
 #include "rq_internal.cuh"
 #include "rq_mv_common.cuh"
 
@@ -72,15 +73,21 @@ namespace {
 // lane c (c < 8) accumulates x[8i+c] * w[8i+c] with a fused multiply-add in
 // ascending i, the eight lane sums are added left to right, and a tail of
 // H % 8 elements adds x*w with two roundings.  So the logits carry the bits
-// of the reference's CPU gate.  The chains are sequential by definition, so
-// the CTA first copies a chunk of x and of every expert's row into shared
-// memory with all its threads (coalesced 16-byte loads) and the eight chain
-// lanes of each warp then run from shared memory.
-constexpr int kRouterSmem = 40 * 1024;
+// of the reference's CPU gate.  The chains are sequential by definition
+// (H / 8 dependent FMAs each), so everything around them is kept off their
+// path: the CTA copies a chunk of x and of every expert's row into shared
+// memory with asynchronous 16-byte copies, all in flight at once (H = 4096
+// with 8 experts is one chunk), and each chain lane loads 16 operands into
+// registers before it runs their 16 FMAs.
+constexpr int kRouterSmem = 96 * 1024;
 
 __host__ __device__ inline int router_chunk(int E) {
     int ch = kRouterSmem / (4 + 2 * E);
     return ch - ch % 8;
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
 // With planes given, the CTA also stages its token's row of x for the
@@ -104,18 +111,29 @@ __global__ void router_kernel(const float* __restrict__ x, const __half* __restr
         const int64_t left = chunks8 * 8 - c0;
         const int n = (int)(left < ch ? left : ch);  // a multiple of 8
         __syncthreads();
-        for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = xr[c0 + i];
-        for (int r = 0; r < E; r++) {
-            const uint4* src = reinterpret_cast<const uint4*>(wr + (int64_t)r * H + c0);
-            uint4* dst = reinterpret_cast<uint4*>(ws + (size_t)r * ch);
-            for (int i = threadIdx.x; i < n / 8; i += blockDim.x) dst[i] = src[i];
+        // x rows and the F16 rows are 16-byte aligned (H % 32 == 0, c0 % 8 == 0)
+        for (int i = threadIdx.x; i < n / 4; i += blockDim.x) cp_async16(xs + 4 * i, xr + c0 + 4 * i);
+        for (int i = threadIdx.x; i < E * (n / 8); i += blockDim.x) {
+            const int r = i / (n / 8), q = i % (n / 8);
+            cp_async16(ws + (size_t)r * ch + 8 * q, wr + (int64_t)r * H + c0 + 8 * q);
         }
+        asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
         __syncthreads();
         if (e < E && lane < 8) {
             const __half* wrow = ws + (size_t)e * ch;
-#pragma unroll 8
-            for (int i = 0; i < n / 8; i++)
-                acc = __fmaf_rn(xs[8 * i + lane], __half2float(wrow[8 * i + lane]), acc);
+            const int n8 = n / 8;
+            int i0 = 0;
+            for (; i0 + 16 <= n8; i0 += 16) {
+                float xv[16], wv[16];
+#pragma unroll
+                for (int u = 0; u < 16; u++) {
+                    xv[u] = xs[8 * (i0 + u) + lane];
+                    wv[u] = __half2float(wrow[8 * (i0 + u) + lane]);
+                }
+#pragma unroll
+                for (int u = 0; u < 16; u++) acc = __fmaf_rn(xv[u], wv[u], acc);
+            }
+            for (; i0 < n8; i0++) acc = __fmaf_rn(xs[8 * i0 + lane], __half2float(wrow[8 * i0 + lane]), acc);
         }
     }
     if (e < E) {
@@ -563,6 +581,14 @@ int launch_router(rq_moe* m, const float* xs, int64_t T, const XQ* stage, cudaSt
     cudaLaunchConfig_t cfg = pdl(dim3((unsigned)T), dim3((unsigned)(32 * E)), st, attr);
     const int ch = router_chunk(E);
     cfg.dynamicSmemBytes = (size_t)ch * 4 + (size_t)E * ch * 2;
+    static bool attr_set[64] = {};  // per device, before the first launch
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRouterSmem);
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(router)");
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
     return cuda_error(cudaLaunchKernelEx(&cfg, router_kernel, xs, (const __half*)m->router, m->H, E, k, m->logits,
                                          m->ids, m->wts, stage ? stage->planes : (int8_t*)nullptr,
                                          stage ? stage->stats : (float4*)nullptr),

@@ -33,6 +33,8 @@
 // bits of the standalone one-shot all-reduce (rq_tp.cu), without its launch
 // and with only local reads after the wait.
 
+#include <string.h>
+
 #include <algorithm>
 
 #include "rq_async.cuh"
@@ -67,15 +69,38 @@ struct PipeParams {
     PipeSwiglu swg;
     int cmb;              // 1: sparse-MoE combine epilogue (cm)
     PipeCombine cm;
+    PipeNext nx;          // weights of the next launch to prefetch into L2 (nx.n = 0: none)
 };
 
 // This CTA's rows of a job: an even split of the job's rows over the grid,
 // the same range for every job of one shape.
+__device__ __forceinline__ int64_t split_point(uint32_t i, int64_t out) {
+    const uint64_t prod = (uint64_t)i * (uint64_t)out;
+    // 32-bit division when it fits (every shape of a model): the 64-bit one
+    // is a long instruction sequence on the producer's path to its first copy
+    return prod <= 0xffffffffull ? (int64_t)((uint32_t)prod / gridDim.x) : (int64_t)(prod / gridDim.x);
+}
 __device__ __forceinline__ void job_rows(const PipeJob& j, int64_t* rb, int* n) {
-    const int64_t b = (int64_t)blockIdx.x * j.out / gridDim.x;
-    const int64_t e = (int64_t)(blockIdx.x + 1) * j.out / gridDim.x;
+    const int64_t b = split_point(blockIdx.x, j.out);
+    const int64_t e = split_point(blockIdx.x + 1, j.out);
     *rb = b;
     *n = (int)(e - b);
+}
+
+// L2 prefetch of the next launch's weights (see PipeNext): this CTA index's
+// first rows of each weight in a grid of gridDim.x CTAs, the budget split
+// over the weights.
+__device__ __forceinline__ void prefetch_next(const PipeNext& nx) {
+    const uint32_t rowb = nx.qrow + nx.hrow;
+    const int64_t per = (int64_t)(nx.budget / (uint32_t)nx.n / rowb);
+    for (int i = 0; i < nx.n; i++) {
+        const int64_t b = (int64_t)blockIdx.x * nx.out[i] / gridDim.x;
+        const int64_t e = (int64_t)(blockIdx.x + 1) * nx.out[i] / gridDim.x;
+        const int64_t rows = min(e - b, per);
+        if (rows <= 0) continue;
+        bulk_prefetch_l2(nx.qs[i] + b * nx.qrow, (uint32_t)(rows * nx.qrow));
+        bulk_prefetch_l2(nx.hdr[i] + b * nx.hrow, (uint32_t)(rows * nx.hrow));
+    }
 }
 
 // The fused all-reduce epilogue of one job (see the file comment); red holds
@@ -223,10 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
     // the next kernel in the stream may launch now; it waits for this grid
     // before touching anything this grid writes
     asm volatile("griddepcontrol.launch_dependents;");
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < p.nstage; i++) {
-            mbar_init(full0 + 8 * i, 1);
-            mbar_init(empty0 + 8 * i, p.S * p.G);
+    if (warp == 0) {  // one lane per stage
+        if (lane < p.nstage) {
+            mbar_init(full0 + 8 * lane, 1);
+            mbar_init(empty0 + 8 * lane, p.S * p.G);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -264,6 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
                     bulk_g2s(dst + (uint32_t)p.RS * p.qrow, jhdr + row * p.hrow, hb, full0 + 8 * slot, pol);
                 }
             }
+            if (ok && p.nx.n > 0) prefetch_next(p.nx);
             // no bulk copy may still be landing when the CTA exits
             for (int k = max(0, it - p.nstage); k < it; k++)
                 if (!mbar_wait(full0 + 8 * (k % p.nstage), (k / p.nstage) & 1)) ok = false;
@@ -372,6 +398,26 @@ int launch_pipe_type(const PipeParams& p, int rpw, int grid, int threads, size_t
 
 }  // namespace
 
+PipeNext pipe_next(const rq_weight* const* ws, int n, uint32_t budget) {
+    PipeNext nx;
+    memset(&nx, 0, sizeof nx);
+    if (n < 1 || n > kMaxNext) return nx;
+    const TypeInfo ti = type_info(ws[0]->type);
+    for (int i = 0; i < n; i++)
+        if (ws[i]->type != ws[0]->type || ws[i]->in != ws[0]->in) return nx;
+    nx.qrow = (uint32_t)(ws[0]->nblk * ti.qs_bytes);
+    nx.hrow = (uint32_t)(ws[0]->nblk * ti.hdr_bytes);
+    if (nx.qrow % 16 || nx.hrow % 16) return nx;
+    for (int i = 0; i < n; i++) {
+        nx.qs[i] = ws[i]->qs;
+        nx.hdr[i] = ws[i]->hdr;
+        nx.out[i] = ws[i]->out;
+    }
+    nx.n = n;
+    nx.budget = budget;
+    return nx;
+}
+
 bool pipe_supported(const rq_weight* w) {
     TypeInfo ti = type_info(w->type);
     const int64_t S = (w->in + 2047) / 2048;
@@ -384,7 +430,8 @@ bool pipe_supported(const rq_weight* w) {
 
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar,
-                       const PipeDevWeights* dw, const PipeSwiglu* sw, const PipeCombine* cmb) {
+                       const PipeDevWeights* dw, const PipeSwiglu* sw, const PipeCombine* cmb,
+                       const PipeNext* next) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "matvec pipeline: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     TypeInfo ti = type_info(w0->type);
@@ -420,6 +467,8 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
         p.cmb = 1;
         p.cm = *cmb;
     }
+    memset(&p.nx, 0, sizeof p.nx);
+    if (next && next->n > 0 && next->n <= kMaxNext && next->qrow % 16 == 0 && next->hrow % 16 == 0) p.nx = *next;
     p.nblk = w0->nblk;
     p.in = w0->in;
     p.S = (int)((w0->in + 2047) / 2048);
