@@ -62,6 +62,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(mbar), "l"(policy)
         : "memory");
 }
+// 16 bytes from global src to this CTA's shared dst (both 16-byte aligned),
+// asynchronously: complete after cp.async.commit_group + wait_group
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 // bytes of global memory from src into L2 (no destination in this CTA);
 // src 16-byte aligned, bytes a multiple of 16
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {

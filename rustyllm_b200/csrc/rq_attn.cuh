@@ -10,10 +10,17 @@ namespace rq {
 
 constexpr int kAttnThreads = 480;  // threads that run one head
 
-// Shared floats the head needs: scores, roped q, new k, new v / output, and
-// the partial output sums of the position ranges.
+// Cached positions whose K and V rows the head copies into shared memory at
+// its start (asynchronously, one round trip for all of them, while RoPE
+// runs); later positions are read from the cache in place.
+__host__ __device__ inline int attn_tile(int64_t hd) { return hd > 128 ? 16 : 32; }
+__host__ __device__ inline int64_t attn_tile_off(int64_t max_seq, int64_t hd) {
+    return (max_seq + 3 * hd + (kAttnThreads / hd) * hd + 3) & ~(int64_t)3;
+}
+// Shared floats the head needs: scores, roped q, new k, new v / output, the
+// partial output sums of the position ranges, and the K / V tile.
 __host__ __device__ inline int64_t attn_smem_floats(int64_t max_seq, int64_t hd) {
-    return max_seq + 3 * hd + (kAttnThreads / hd) * hd;
+    return attn_tile_off(max_seq, hd) + 2 * (int64_t)attn_tile(hd) * hd;
 }
 
 // Head h of QAttn::forward (src/streaming_quantized.rs:201-257) for the one
@@ -45,6 +52,20 @@ __device__ __forceinline__ void attn_decode_head(const float* __restrict__ q, co
     const float* vs = v + (int64_t)kh * hd;
     float* K = kc + (int64_t)kh * max_seq * hd;
     float* V = vc + (int64_t)kh * max_seq * hd;
+    // K / V rows of the first np cached positions (written by earlier steps)
+    // into the tile, in flight while RoPE runs
+    const int np = min(pp, attn_tile(hd));
+    float* kt = sm + attn_tile_off(max_seq, hd);
+    float* vt = kt + (int64_t)attn_tile(hd) * hd;
+    {
+        const int chunks = np * hd / 4;  // 16-byte chunks per matrix (hd % 32 == 0)
+        for (int i = tid; i < 2 * chunks; i += nthr) {
+            const bool isv = i >= chunks;
+            const int c = isv ? i - chunks : i;
+            cp_async16((isv ? vt : kt) + 4 * c, (isv ? V : K) + 4 * c);
+        }
+        cp_async_commit();
+    }
     for (int i = tid; i < half; i += nthr) {
         const float c = cos_t[(int64_t)pp * half + i], s = sin_t[(int64_t)pp * half + i];
         const float a = qh[i], b = qh[i + half];
@@ -55,6 +76,7 @@ __device__ __forceinline__ void attn_decode_head(const float* __restrict__ q, co
         kn[i + half] = ka * s + kb * c;
     }
     for (int i = tid; i < hd; i += nthr) vn[i] = vs[i];
+    cp_async_wait_all();
     named_bar_sync(bar, nthr);
     if (h % rep == 0)
         for (int i = tid; i < hd; i += nthr) {
@@ -64,7 +86,7 @@ __device__ __forceinline__ void attn_decode_head(const float* __restrict__ q, co
     const int warp = tid >> 5, lane = tid & 31;
     const float inv_sqrt = 1.0f / sqrtf((float)hd);
     for (int j = warp; j < L; j += nw) {
-        const float* kj = j == pp ? kn : K + (int64_t)j * hd;
+        const float* kj = j == pp ? kn : j < np ? kt + (int64_t)j * hd : K + (int64_t)j * hd;
         float acc = 0.0f;
         for (int d = lane; d < hd; d += 32) acc = fmaf(qs[d], kj[d], acc);
 #pragma unroll
@@ -101,7 +123,8 @@ __device__ __forceinline__ void attn_decode_head(const float* __restrict__ q, co
         const int j0 = r * L / P, j1 = (r + 1) * L / P;
         float acc = 0.0f;
 #pragma unroll 4
-        for (int j = j0; j < j1; j++) acc = fmaf(sc[j], j == pp ? vn[d] : V[(int64_t)j * hd + d], acc);
+        for (int j = j0; j < j1; j++)
+            acc = fmaf(sc[j], j == pp ? vn[d] : j < np ? vt[(int64_t)j * hd + d] : V[(int64_t)j * hd + d], acc);
         part[r * hd + d] = acc;
     }
     named_bar_sync(bar, nthr);

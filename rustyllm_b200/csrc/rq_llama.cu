@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
     const int32_t* __restrict__ pos, int n_heads, int n_kv, int hd, int max_seq, int8_t* __restrict__ planes,
     float4* __restrict__ stats) {
     pdl_enter();
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     __shared__ float red[32];
     attn_decode_head(q, k, v, kc, vc, cos_t, sin_t, pos, n_heads, n_kv, hd, max_seq, planes, stats, (int)blockIdx.x,
                      (int)threadIdx.x, 0, sm, red);

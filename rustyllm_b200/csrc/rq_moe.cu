@@ -86,10 +86,6 @@ __host__ __device__ inline int router_chunk(int E) {
     return ch - ch % 8;
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-
 // With planes given, the CTA also stages its token's row of x for the
 // pipeline matvec (xquant_kernel's arithmetic) into row t of (planes, stats).
 __global__ void router_kernel(const float* __restrict__ x, const __half* __restrict__ wr, int64_t H,
@@ -117,7 +113,8 @@ __global__ void router_kernel(const float* __restrict__ x, const __half* __restr
             const int r = i / (n / 8), q = i % (n / 8);
             cp_async16(ws + (size_t)r * ch + 8 * q, wr + (int64_t)r * H + c0 + 8 * q);
         }
-        asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+        cp_async_commit();
+        cp_async_wait_all();
         __syncthreads();
         if (e < E && lane < 8) {
             const __half* wrow = ws + (size_t)e * ch;
