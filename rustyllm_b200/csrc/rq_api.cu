@@ -199,6 +199,7 @@ int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles) {
 // Bytes of activation staging at the start of ctx->ws for rq_linear's
 // kernel choice at M rows.
 size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
+    if (mm_i8_supported(w, M)) return xq2_bytes(M, w->in);
     const bool small_m = M >= kMinTensorM && mm_small_supported(w);
     return small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
 }
@@ -212,6 +213,12 @@ size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
 int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, int64_t M, cudaStream_t st) {
     uint8_t* ws = (uint8_t*)ctx->ws;
     int rc;
+    if (mm_i8_supported(w, M)) {  // M = 2..4: one pass on the int8 tensor cores
+        const XQ2 q = xq2_at(ws, M, w->in);
+        rc = launch_xq2_stage(xd, M, w->in, q, st);
+        if (!rc) rc = launch_mm_i8(&w, &yd, 1, M, q, ctx->sm_count, st, ctx->derr);
+        return rc;
+    }
     if (M >= kMinTensorM && mm_small_supported(w)) {
         const XH xh = xh_at(ws, M, w->in);
         rc = launch_xh_stage(xd, M, w->in, xh, st);

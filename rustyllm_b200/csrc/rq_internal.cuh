@@ -254,6 +254,25 @@ struct XH {
 };
 size_t xh_bytes(int64_t rows, int64_t in);
 XH xh_at(void* base, int64_t rows, int64_t in);
+
+// Q4_K matmul for two activation rows on the int8 tensor cores
+// (rq_mm_i8.cu).  Activations staged per token and 256-element super-block
+// as X = rint(x * 127*65536 / amax) split into three balanced bytes with
+// sx = amax / (127*65536), plus the f32 sum of every 32-element block.
+struct XQ2 {
+    int8_t* planes;  // [M][3][in]
+    float* sx;       // [M][in/256]
+    float* bsum;     // [M][in/32]
+};
+size_t xq2_bytes(int64_t M, int64_t in);
+XQ2 xq2_at(void* base, int64_t M, int64_t in);
+int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st);
+// whether weight w takes the int8 kernel for M rows (Q4_K, M = 2,
+// in = 2048 .. 8192 in steps of 2048)
+bool mm_i8_supported(const rq_weight* w, int64_t M);
+// y_j[M][out_j] = x W_j^T for up to kMaxJobs weights of the same in
+int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_t M, XQ2 xq, int sm_count,
+                 cudaStream_t st, int* err);
 int launch_xh_stage(const float* x, int64_t M, int64_t in, XH xh, cudaStream_t st);
 // the same staging of RMSNorm(x) * w, and of silu(gate) * up
 int launch_xh_stage_rmsnorm(const float* x, const float* w, float eps, int64_t M, int64_t in, XH xh,

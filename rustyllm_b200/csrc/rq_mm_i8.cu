@@ -1,0 +1,471 @@
+// rq_mm_i8.cu -- Q4_K matmul for two activation rows (the speculative
+// verify of a one-token draft, M = K + 1 = 2) on the int8 tensor cores:
+// mma.sync m16n8k32, u8 weights x s8 activations -> s32, one weight pass.
+//
+// The work is HBM-bound, so the kernel keeps the M=1 pipeline's data path --
+// one persistent CTA per SM owning a contiguous range of output rows, a
+// producer lane streaming whole rows into a ring of shared-memory stages with
+// bulk copies -- and replaces the per-row dp4a work by tensor-core tiles:
+//
+//   A (16 weight rows x 32 elements of K, u8): the 4-bit quants as they are.
+//     A lane's 8 bytes of a 32-byte nibble group give both sub-blocks of the
+//     group: low nibbles = sub-block 2c, high nibbles = 2c+1 (one mask or
+//     shift-and-mask per 4 weights, no conversion).  Stages hold 16 rows;
+//     each row is copied to its own shared-memory row padded by 32 bytes
+//     (quants) / 16 bytes (headers), so the 8 rows a warp-wide load touches
+//     fall in distinct banks.
+//   B (32 elements x 8 columns, s8): column n = plane n / 2 of token n % 2
+//     (columns 6, 7 zero), the activations staged in 24-bit fixed point as
+//     three balanced bytes X = 65536 x1 + 256 x2 + x3 with one scale per
+//     token and super-block (XQ2) -- the M=1 path's precision.  A warp owns a
+//     K-slice of at most 4 super-blocks and holds that slice's B fragments
+//     in registers for the whole launch.
+//
+// K-slot 4t + i of an MMA is element 8t + i of the sub-block and slot
+// 16 + 4t + i element 8t + 4 + i (t = the lane's quad position): a thread's
+// fragment registers then cover bytes 8t .. 8t+7 of a weight row and of an
+// activation row, so both operands are single 8-byte loads.  Per sub-block
+// the s32 tile is scaled by the row's 6-bit sc_j with an integer
+// multiply-add (exact: |sum| < 2^31 over a super-block), and once per
+// super-block the s32 sums become f32:
+//   y += d * sx_tok * pw_plane * S  -  dmin * sum_j m_j * bsum_j
+// with the min term from the f32 block sums of x.  At the end of a stage the
+// three planes of a token are added over the lane quad, and each warp
+// writes its K-slice partials of the 16 rows into a per-CTA table
+// [row][slice][token]; after the last stage the slices are summed in order
+// (deterministic) into y.  Every mbarrier wait is bounded (~1 s); on expiry
+// the kernel sets the error word, drains its copies and returns.
+
+#include <string.h>
+
+#include <algorithm>
+
+#include "rq_async.cuh"
+#include "rq_internal.cuh"
+
+namespace rq {
+
+// ---------------------------------------------------- activation staging
+
+constexpr float kXQ3Scale = 8323072.0f;  // 127 * 65536: the three balanced bytes of X stay in [-127, 127]
+
+size_t xq2_bytes(int64_t M, int64_t in) {
+    size_t b = ((size_t)M * 3 * (size_t)in + 255) & ~(size_t)255;
+    b += ((size_t)M * (size_t)(in / 256) * 4 + 255) & ~(size_t)255;
+    b += (size_t)M * (size_t)(in / 32) * 4;
+    return b;
+}
+
+XQ2 xq2_at(void* base, int64_t M, int64_t in) {
+    uint8_t* p = (uint8_t*)base;
+    XQ2 q;
+    q.planes = (int8_t*)p;
+    p += ((size_t)M * 3 * (size_t)in + 255) & ~(size_t)255;
+    q.sx = (float*)p;
+    p += ((size_t)M * (size_t)(in / 256) * 4 + 255) & ~(size_t)255;
+    q.bsum = (float*)p;
+    return q;
+}
+
+namespace {
+
+// One warp per (token, super-block): lane l holds elements 8l .. 8l+7.
+// X = rint(x * 127*65536 / amax) over the super-block, as three balanced
+// bytes X = 65536 x1 + 256 x2 + x3 (stage_block's digits, one scale per 256
+// elements instead of per 32); the f32 block sums are summed over the four
+// lanes of a 32-element block.
+__global__ void xq2_stage_kernel(const float* __restrict__ x, int64_t M, int64_t in, XQ2 q) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int lane = threadIdx.x & 31;
+    const int64_t nsb = in / 256;
+    const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (wid >= M * nsb) return;
+    const int64_t m = wid / nsb, sb = wid % nsb;
+    const float* src = x + m * in + sb * 256 + 8 * lane;
+    float v[8];
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = src[k];
+    }
+    float amax = 0.0f, s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        amax = fmaxf(amax, fabsf(v[k]));
+        s += v[k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    const float inv = amax > 0.0f ? kXQ3Scale / amax : 0.0f;
+    uint32_t p1[2] = {0u, 0u}, p2[2] = {0u, 0u}, p3[2] = {0u, 0u};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int X = __float2int_rn(v[k] * inv);
+        const int x3 = (X << 24) >> 24;  // balanced base-256 digits
+        const int t1 = (X - x3) >> 8;
+        const int x2 = (t1 << 24) >> 24;
+        const int x1 = (t1 - x2) >> 8;
+        p1[k / 4] |= (uint32_t)(x1 & 255) << (8 * (k % 4));
+        p2[k / 4] |= (uint32_t)(x2 & 255) << (8 * (k % 4));
+        p3[k / 4] |= (uint32_t)(x3 & 255) << (8 * (k % 4));
+    }
+    int8_t* base = q.planes + m * 3 * in + sb * 256 + 8 * lane;
+    *reinterpret_cast<uint2*>(base) = make_uint2(p1[0], p1[1]);
+    *reinterpret_cast<uint2*>(base + in) = make_uint2(p2[0], p2[1]);
+    *reinterpret_cast<uint2*>(base + 2 * in) = make_uint2(p3[0], p3[1]);
+    if ((lane & 3) == 0) q.bsum[m * (in / 32) + sb * 8 + lane / 4] = s;
+    if (lane == 0) q.sx[m * nsb + sb] = amax / kXQ3Scale;
+}
+
+// ------------------------------------------------------------------ matmul
+
+constexpr int kI8Cons = 8;         // consumer warps = K-slices
+constexpr int kI8Threads = 32 * (1 + kI8Cons);
+constexpr int kI8Rows = 16;        // weight rows per stage (one MMA tile)
+constexpr int kI8MaxSB = 4;        // super-blocks per K-slice (K <= 8192)
+constexpr int kI8QPad = 32, kI8HPad = 16;
+constexpr int kI8Smem = 227 * 1024;
+constexpr int kI8Bar = 2 * 16 * 8;  // up to 16 stages: full + empty barriers
+
+struct I8Job {
+    const uint8_t* qs;
+    const uint8_t* hdr;
+    float* y;       // [M][out]
+    int64_t out;
+};
+
+struct I8Params {
+    I8Job jobs[kMaxJobs];
+    int njobs, M;
+    int64_t in;
+    int nsb;                    // super-blocks per row
+    uint32_t qrow, hrow;        // device bytes per row
+    uint32_t qstride, hstride;  // padded shared-memory row strides
+    uint32_t stage_bytes, red_off, ring_off;
+    int nstage;
+    XQ2 xq;
+    int* err;
+};
+
+__device__ __forceinline__ void i8_rows(const I8Job& j, int64_t* rb, int* n) {
+    const int64_t b = (int64_t)blockIdx.x * j.out / gridDim.x;
+    const int64_t e = (int64_t)(blockIdx.x + 1) * j.out / gridDim.x;
+    *rb = b;
+    *n = (int)(e - b);
+}
+
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// byte j (compile-time) of a packed word, zero-extended
+template <int J>
+__device__ __forceinline__ int byte_of(uint32_t w) {
+    return (int)__byte_perm(w, 0u, 0x4440u + J);
+}
+
+__global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    float* red = reinterpret_cast<float*>(smem + p.red_off);
+    uint8_t* ring = smem + p.ring_off;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t full0 = smem_u32(smem), empty0 = full0 + 8 * 16;
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (warp == 0) {
+        if (lane < p.nstage) {
+            mbar_init(full0 + 8 * lane, 1);
+            mbar_init(empty0 + 8 * lane, kI8Cons);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            int it = 0, slot = 0, use = 0;
+            bool ok = true;
+            for (int j = 0; j < p.njobs && ok; j++) {
+                const I8Job& jb = p.jobs[j];
+                int64_t rb;
+                int nrows;
+                i8_rows(jb, &rb, &nrows);
+                for (int r0 = 0; r0 < nrows; r0 += kI8Rows, it++, slot = slot + 1 == p.nstage ? 0 : slot + 1,
+                         use += slot == 0) {
+                    if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
+                    const int rows = min(kI8Rows, nrows - r0);
+                    const uint32_t dst = smem_u32(ring) + (uint32_t)slot * p.stage_bytes;
+                    const uint32_t hdst = dst + (uint32_t)kI8Rows * p.qstride;
+                    mbar_expect_tx(full0 + 8 * slot, (uint32_t)rows * (p.qrow + p.hrow));
+                    for (int r = 0; r < rows; r++) {
+                        const int64_t row = rb + r0 + r;
+                        bulk_g2s(dst + (uint32_t)r * p.qstride, jb.qs + row * p.qrow, p.qrow, full0 + 8 * slot, pol);
+                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow, p.hrow, full0 + 8 * slot,
+                                 pol);
+                    }
+                }
+            }
+            for (int k = max(0, it - p.nstage); k < it; k++)
+                if (!mbar_wait(full0 + 8 * (k % p.nstage), (k / p.nstage) & 1)) ok = false;
+            if (!ok && p.err) atomicExch(p.err, 1);
+        }
+    } else {
+        const int w = warp - 1;                 // K-slice
+        const int g = lane >> 2, t = lane & 3;  // MMA group / quad position
+        const int M = p.M;
+        const int sb0 = w * p.nsb / kI8Cons, nsbw = (w + 1) * p.nsb / kI8Cons - sb0;
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        // B fragments of the slice: column g = plane g / 2 of token g % 2
+        // (columns 6, 7 zero), elements 8t .. 8t+7 of each sub-block
+        uint32_t bf[kI8MaxSB][8][2];
+        float coef[kI8MaxSB][2];  // sx * plane weight of columns 2t, 2t+1: plane t, tokens 0, 1
+        {
+            const int bp = g >> 1, bm = g & 1;
+            const bool bvalid = bp < 3 && bm < M;
+            const int8_t* bsrc = p.xq.planes + ((int64_t)bm * 3 + (bvalid ? bp : 0)) * p.in + 8 * t;
+#pragma unroll
+            for (int s = 0; s < kI8MaxSB; s++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    uint2 u = make_uint2(0u, 0u);
+                    if (bvalid && s < nsbw)
+                        u = *reinterpret_cast<const uint2*>(bsrc + ((int64_t)(sb0 + s) * 8 + j) * 32);
+                    bf[s][j][0] = u.x;
+                    bf[s][j][1] = u.y;
+                }
+            const float pw = t == 0 ? 65536.0f : t == 1 ? 256.0f : 1.0f;
+#pragma unroll
+            for (int s = 0; s < kI8MaxSB; s++)
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+                    coef[s][c] = (t < 3 && c < M && s < nsbw) ? p.xq.sx[(int64_t)c * p.nsb + sb0 + s] * pw : 0.0f;
+        }
+        const float* bsum_t = p.xq.bsum + (int64_t)t * (p.in / 32);  // this lane's token for the min term
+        const bool tvalid = t < M;
+        int slot = 0, use = 0, roff = 0;
+        bool ok = true;
+        for (int j = 0; j < p.njobs && ok; j++) {
+            const I8Job& jb = p.jobs[j];
+            int64_t rb;
+            int nrows;
+            i8_rows(jb, &rb, &nrows);
+            for (int r0 = 0; r0 < nrows; r0 += kI8Rows, slot = slot + 1 == p.nstage ? 0 : slot + 1, use += slot == 0) {
+                if (!mbar_wait(full0 + 8 * slot, use & 1)) {
+                    if (lane == 0 && p.err) atomicExch(p.err, 1);
+                    ok = false;
+                    break;
+                }
+                const uint8_t* sq = ring + (size_t)slot * p.stage_bytes;
+                const uint8_t* sh = sq + (size_t)kI8Rows * p.qstride;
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // rows g, g (cols 2t, 2t+1), g+8, g+8
+                float mn[2] = {0.0f, 0.0f};               // min term of token t, rows g and g+8
+#pragma unroll
+                for (int s = 0; s < kI8MaxSB; s++) {
+                    if (s < nsbw) {
+                        const int sb = sb0 + s;
+                        const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)g * p.hstride + sb * 16);
+                        const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)(g + 8) * p.hstride + sb * 16);
+                        // Q4_K 6-bit scales and mins, four per word
+                        const uint32_t scg0 = hg.y & 0x3F3F3F3Fu, mg0 = hg.z & 0x3F3F3F3Fu;
+                        const uint32_t scg1 = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
+                        const uint32_t mg1 = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
+                        const uint32_t sc80 = h8.y & 0x3F3F3F3Fu, m80 = h8.z & 0x3F3F3F3Fu;
+                        const uint32_t sc81 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
+                        const uint32_t m81 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
+                        int ai[4] = {0, 0, 0, 0};
+                        const uint8_t* qg = sq + (size_t)g * p.qstride + sb * 128 + 8 * t;
+                        const uint8_t* q8 = qg + 8 * (size_t)p.qstride;
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
+                            const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
+                            const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
+                                                     w8.y & 0x0F0F0F0Fu};
+                            const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
+                                                     (wg.y >> 4) & 0x0F0F0F0Fu, (w8.y >> 4) & 0x0F0F0F0Fu};
+                            int d[4];
+                            // sub-block 2c
+                            mma_u8s8(d, alo, bf[s][2 * c][0], bf[s][2 * c][1]);
+                            {
+                                const int sg = c < 2 ? (c == 0 ? byte_of<0>(scg0) : byte_of<2>(scg0))
+                                                     : (c == 2 ? byte_of<0>(scg1) : byte_of<2>(scg1));
+                                const int s8 = c < 2 ? (c == 0 ? byte_of<0>(sc80) : byte_of<2>(sc80))
+                                                     : (c == 2 ? byte_of<0>(sc81) : byte_of<2>(sc81));
+                                ai[0] += d[0] * sg;
+                                ai[1] += d[1] * sg;
+                                ai[2] += d[2] * s8;
+                                ai[3] += d[3] * s8;
+                            }
+                            // sub-block 2c + 1
+                            mma_u8s8(d, ahi, bf[s][2 * c + 1][0], bf[s][2 * c + 1][1]);
+                            {
+                                const int sg = c < 2 ? (c == 0 ? byte_of<1>(scg0) : byte_of<3>(scg0))
+                                                     : (c == 2 ? byte_of<1>(scg1) : byte_of<3>(scg1));
+                                const int s8 = c < 2 ? (c == 0 ? byte_of<1>(sc80) : byte_of<3>(sc80))
+                                                     : (c == 2 ? byte_of<1>(sc81) : byte_of<3>(sc81));
+                                ai[0] += d[0] * sg;
+                                ai[1] += d[1] * sg;
+                                ai[2] += d[2] * s8;
+                                ai[3] += d[3] * s8;
+                            }
+                        }
+                        const float2 ddg = __half22float2(*reinterpret_cast<const __half2*>(&hg.x));
+                        const float2 dd8 = __half22float2(*reinterpret_cast<const __half2*>(&h8.x));
+                        acc[0] = fmaf((float)ai[0], ddg.x * coef[s][0], acc[0]);
+                        acc[1] = fmaf((float)ai[1], ddg.x * coef[s][1], acc[1]);
+                        acc[2] = fmaf((float)ai[2], dd8.x * coef[s][0], acc[2]);
+                        acc[3] = fmaf((float)ai[3], dd8.x * coef[s][1], acc[3]);
+                        if (tvalid) {
+                            const float4 b0 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8);
+                            const float4 b1 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8 + 4);
+                            float sg = 0.0f, s8 = 0.0f;
+                            sg = fmaf((float)byte_of<0>(mg0), b0.x, sg); s8 = fmaf((float)byte_of<0>(m80), b0.x, s8);
+                            sg = fmaf((float)byte_of<1>(mg0), b0.y, sg); s8 = fmaf((float)byte_of<1>(m80), b0.y, s8);
+                            sg = fmaf((float)byte_of<2>(mg0), b0.z, sg); s8 = fmaf((float)byte_of<2>(m80), b0.z, s8);
+                            sg = fmaf((float)byte_of<3>(mg0), b0.w, sg); s8 = fmaf((float)byte_of<3>(m80), b0.w, s8);
+                            sg = fmaf((float)byte_of<0>(mg1), b1.x, sg); s8 = fmaf((float)byte_of<0>(m81), b1.x, s8);
+                            sg = fmaf((float)byte_of<1>(mg1), b1.y, sg); s8 = fmaf((float)byte_of<1>(m81), b1.y, s8);
+                            sg = fmaf((float)byte_of<2>(mg1), b1.z, sg); s8 = fmaf((float)byte_of<2>(m81), b1.z, s8);
+                            sg = fmaf((float)byte_of<3>(mg1), b1.w, sg); s8 = fmaf((float)byte_of<3>(m81), b1.w, s8);
+                            mn[0] = fmaf(ddg.y, sg, mn[0]);
+                            mn[1] = fmaf(dd8.y, s8, mn[1]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty0 + 8 * slot);
+                // the three planes of a token sit in lanes t = 0, 1, 2 of
+                // the quad (lane 3 holds zeros): sum over the quad
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 1);
+                    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 2);
+                }
+                const int qb = lane & ~3;
+                const float mA0 = __shfl_sync(0xffffffffu, mn[0], qb);
+                const float mA1 = __shfl_sync(0xffffffffu, mn[0], qb + 1);
+                const float mB0 = __shfl_sync(0xffffffffu, mn[1], qb);
+                const float mB1 = __shfl_sync(0xffffffffu, mn[1], qb + 1);
+                const int rows = min(kI8Rows, nrows - r0);
+                if (t == 0) {
+                    float* rg = red + ((int64_t)(roff + r0 + g) * kI8Cons + w) * M;
+                    float* r8 = red + ((int64_t)(roff + r0 + g + 8) * kI8Cons + w) * M;
+                    if (g < rows) {
+                        rg[0] = acc[0] - mA0;
+                        if (M > 1) rg[1] = acc[1] - mA1;
+                    }
+                    if (g + 8 < rows) {
+                        r8[0] = acc[2] - mB0;
+                        if (M > 1) r8[1] = acc[3] - mB1;
+                    }
+                }
+            }
+            roff += nrows;
+        }
+    }
+    __syncthreads();
+    int roff = 0;
+    for (int j = 0; j < p.njobs; j++) {
+        int64_t rb;
+        int nrows;
+        i8_rows(p.jobs[j], &rb, &nrows);
+        for (int e = threadIdx.x; e < nrows * p.M; e += blockDim.x) {
+            const int r = e / p.M, m = e % p.M;
+            float acc = 0.0f;
+            for (int s = 0; s < kI8Cons; s++) acc += red[((int64_t)(roff + r) * kI8Cons + s) * p.M + m];
+            p.jobs[j].y[(int64_t)m * p.jobs[j].out + rb + r] = acc;
+        }
+        roff += nrows;
+    }
+}
+
+}  // namespace
+
+bool mm_i8_supported(const rq_weight* w, int64_t M) {
+    if (w->type != RQ_Q4_K || M != 2) return false;
+    const int64_t nsb = w->in / 256;
+    return w->in % 256 == 0 && nsb % kI8Cons == 0 && nsb / kI8Cons <= kI8MaxSB;
+}
+
+int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st) {
+    const int64_t warps = M * (in / 256);
+    if (warps == 0) return RQ_OK;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((warps + 7) / 8));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_error(cudaLaunchKernelEx(&cfg, xq2_stage_kernel, x, M, in, q), "xq2 staging kernel");
+}
+
+int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_t M, XQ2 xq, int sm_count,
+                 cudaStream_t st, int* err) {
+    if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "int8 matmul: %d jobs", njobs);
+    const rq_weight* w0 = ws[0];
+    for (int j = 0; j < njobs; j++)
+        if (!mm_i8_supported(ws[j], M) || ws[j]->in != w0->in)
+            return set_error(RQ_ERR_INVALID, "int8 matmul: unsupported weight or M = %lld", (long long)M);
+    I8Params p;
+    memset(&p, 0, sizeof p);
+    p.njobs = njobs;
+    p.M = (int)M;
+    p.in = w0->in;
+    p.nsb = (int)(w0->in / 256);
+    p.qrow = (uint32_t)(w0->nblk * 128);
+    p.hrow = (uint32_t)(w0->nblk * 16);
+    p.qstride = p.qrow + kI8QPad;
+    p.hstride = p.hrow + kI8HPad;
+    p.stage_bytes = (uint32_t)(kI8Rows * (p.qstride + p.hstride) + 127) & ~127u;
+    p.xq = xq;
+    p.err = err;
+    int64_t max_out = 0;
+    for (int j = 0; j < njobs; j++) {
+        p.jobs[j] = I8Job{ws[j]->qs, ws[j]->hdr, ys[j], ws[j]->out};
+        max_out = std::max(max_out, ws[j]->out);
+    }
+    const int grid = (int)std::min<int64_t>(max_out, sm_count);
+    int64_t rows_cap = 0;
+    for (int j = 0; j < njobs; j++) rows_cap += (ws[j]->out + grid - 1) / grid;
+    const int64_t red_bytes = rows_cap * kI8Cons * M * 4;
+    p.red_off = kI8Bar;
+    p.ring_off = (uint32_t)((kI8Bar + red_bytes + 127) & ~(int64_t)127);
+    if (p.ring_off >= (uint32_t)kI8Smem) return set_error(RQ_ERR_UNSUPPORTED, "int8 matmul: partial table too large");
+    const int nstage = std::min<int>((int)((kI8Smem - p.ring_off) / p.stage_bytes), 16);
+    if (nstage < 2) return set_error(RQ_ERR_UNSUPPORTED, "int8 matmul: rows of %u bytes too large", p.qrow + p.hrow);
+    p.nstage = nstage;
+    const size_t smem = p.ring_off + (size_t)nstage * p.stage_bytes;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(mm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kI8Smem);
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(int8 matmul)");
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kI8Threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_error(cudaLaunchKernelEx(&cfg, mm_i8_kernel, p), "int8 matmul kernel");
+}
+
+}  // namespace rq

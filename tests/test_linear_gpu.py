@@ -92,6 +92,28 @@ def test_small_m_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
         assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("out,n_in,M", [(1, 2048, 2), (17, 4096, 2), (333, 8192, 2), (1040, 6144, 2),
+                                         (4096, 8192, 2), (150, 8192, 2), (8192, 8192, 2), (24, 8192, 3)])
+def test_int8_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
+    """Q4_K M = 2 with in = 2048..8192 runs on the int8 tensor-core kernel
+    (24-bit staged activations, one weight pass): single rows, ragged
+    16-row stages, fewer rows than SMs, every K-slice width (M = 3 takes the
+    other path); each row of y within 1e-4 of the f64-accumulated oracle."""
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200.linear import _linear
+    _, blocks = make_weight(oracle, 12, out, n_in, seed=out * 7 + M)
+    w = QWeight.upload(rq_ctx, 12, blocks, out, n_in)
+    x = np.random.default_rng(M + out).standard_normal((M, n_in)).astype(np.float32)
+    x[:, :256] *= 40.0  # one super-block of large values, one of small ones
+    x[:, 256:512] *= 1e-3
+    y = _linear(w, x)
+    ref = oracle.matmul_ref(12, blocks, out, n_in, x, acc64=True)
+    assert np.isfinite(y).all()
+    assert rel_l2(y, ref) <= REL_L2_TOL
+    for m in range(M):
+        assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
+
+
 @pytest.mark.parametrize("out,n_in,M", [(128, 8192, 9), (200, 768, 16), (1024, 8192, 12), (256, 28672, 9),
                                          (72, 256, 10), (1040, 4096, 16), (8192, 1024, 13), (300, 1280, 11)])
 def test_split_k_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
