@@ -266,13 +266,15 @@ struct XQ2 {
 };
 size_t xq2_bytes(int64_t M, int64_t in);
 XQ2 xq2_at(void* base, int64_t M, int64_t in);
-int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st);
+// stages x (M rows) or, with rms_w, RMSNorm(x) * rms_w (eps) into q
+int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st, const float* rms_w = nullptr,
+                     float eps = 0.0f);
 // whether weight w takes the int8 kernel for M rows (Q4_K, M = 2,
 // in = 2048 .. 8192 in steps of 2048)
 bool mm_i8_supported(const rq_weight* w, int64_t M);
-// y_j[M][out_j] = x W_j^T for up to kMaxJobs weights of the same in
+// y_j[M][out_j] = x W_j^T (+ add_j) for up to kMaxJobs weights of the same in
 int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_t M, XQ2 xq, int sm_count,
-                 cudaStream_t st, int* err);
+                 cudaStream_t st, int* err, const float* const* adds = nullptr);
 int launch_xh_stage(const float* x, int64_t M, int64_t in, XH xh, cudaStream_t st);
 // the same staging of RMSNorm(x) * w, and of silu(gate) * up
 int launch_xh_stage_rmsnorm(const float* x, const float* w, float eps, int64_t M, int64_t in, XH xh,

@@ -448,6 +448,18 @@ void set_next(rq_llama* m, const rq_weight* const* ws, int n, uint32_t budget) {
 const PipeNext* next_hint(const rq_llama* m) { return m->nx.n > 0 ? &m->nx : nullptr; }
 
 
+// Two-token forwards (the verify of a one-token draft) run the linears the
+// int8 tensor-core kernel takes in one weight pass (rq_mm_i8.cu), its
+// activation staging in m->xq's buffer.
+bool i8_ok(const rq_weight* const* ws, int n, int64_t T) {
+    if (T != 2) return false;
+    for (int i = 0; i < n; i++)
+        if (!mm_i8_supported(ws[i], 2)) return false;
+    return true;
+}
+
+XQ2 i8_stage(const rq_llama* m, int64_t in) { return xq2_at(m->xq.planes, 2, in); }
+
 // y_i[t] = x[t] W_i^T (+ add_i[t]) for the n weights (same in) and T staged rows.
 int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* const* ys,
                 const float* const* adds, cudaStream_t st) {
@@ -616,6 +628,10 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
             if (tc) {
                 rc = launch_xh_stage_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xh, st);
                 if (!rc) rc = run_mm(m, 3, w3, T, y3, nullptr, st);
+            } else if (i8_ok(w3, 3, T)) {
+                const XQ2 q2 = i8_stage(m, H);
+                rc = launch_xq2_stage(m->x, T, H, q2, st, L.rms1, c.rms_eps);
+                if (!rc) rc = launch_mm_i8(w3, y3, 3, T, q2, m->ctx->sm_count, st, m->derr);
             } else {
                 rc = launch_xquant_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xq, st);
                 if (T == 1) set_next(m, &L.w[3], 1, kNextBudgetAttn);
@@ -661,6 +677,17 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
             rc = launch_simple((const void*)attention_kernel, dim3((unsigned)nh, (unsigned)T), dim3(128),
                                (size_t)c.max_seq * sizeof(float), st, args2, "attention kernel");
             if (rc) return rc;
+            if (!tc && i8_ok(&L.w[3], 1, T)) {
+                // o on the int8 kernel: x (+)= att W^T, the residual in its epilogue
+                const XQ2 q2 = i8_stage(m, nq);
+                rc = launch_xq2_stage(m->att, T, nq, q2, st);
+                float* y1[1] = {m->W == 1 ? m->x : m->part};
+                const float* a1[1] = {m->R == 0 ? m->x : nullptr};
+                if (!rc) rc = launch_mm_i8(&L.w[3], y1, 1, T, q2, m->ctx->sm_count, st, m->derr, a1);
+                if (!rc && m->W > 1) rc = tp_allreduce(m->ctx, m->part, m->x, T * H, 0, 0, st);
+                if (rc) return rc;
+                goto mlp;
+            }
             rc = tc ? launch_xh_stage(m->att, T, nq, m->xh, st) : launch_xquant(m->att, T, nq, m->xq, st);
             if (rc) return rc;
         }
@@ -668,12 +695,17 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
         rc = tc ? row_parallel_mm(m, L.w[3], T, st) : row_parallel(m, L.w[3], T, st);
         set_next(m, nullptr, 0, 0);
         if (rc) return rc;
+    mlp:
         {
             const rq_weight* w2[2] = {L.w[4], L.w[5]};
             float* y2[2] = {m->g, m->u};
             if (tc) {
                 rc = launch_xh_stage_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xh, st);
                 if (!rc) rc = run_mm(m, 2, w2, T, y2, nullptr, st);
+            } else if (i8_ok(w2, 2, T)) {
+                const XQ2 q2 = i8_stage(m, H);
+                rc = launch_xq2_stage(m->x, T, H, q2, st, L.rms2, c.rms_eps);
+                if (!rc) rc = launch_mm_i8(w2, y2, 2, T, q2, m->ctx->sm_count, st, m->derr);
             } else if (swiglu_in_epilogue(m, L.w[4], L.w[5], T)) {
                 rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
                 const XQ in2[2] = {m->xq, m->xq};

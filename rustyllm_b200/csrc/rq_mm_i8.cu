@@ -70,19 +70,44 @@ XQ2 xq2_at(void* base, int64_t M, int64_t in) {
 namespace {
 
 // One warp per (token, super-block): lane l holds elements 8l .. 8l+7.
-// X = rint(x * 127*65536 / amax) over the super-block, as three balanced
+// X = rint(v * 127*65536 / amax) over the super-block, as three balanced
 // bytes X = 65536 x1 + 256 x2 + x3 (stage_block's digits, one scale per 256
-// elements instead of per 32); the f32 block sums are summed over the four
-// lanes of a 32-element block.
-__global__ void xq2_stage_kernel(const float* __restrict__ x, int64_t M, int64_t in, XQ2 q) {
+// elements instead of per 32), v = x or, with rms_w, the RMSNorm of x
+// (xquant_rmsnorm_kernel's formula and sum of squares); the f32 block sums
+// of v are summed over the four lanes of a 32-element block.  Grid
+// (ceil(nsb / 8), M), 256 threads: eight super-blocks of one token per CTA.
+__global__ void xq2_stage_kernel(const float* __restrict__ x, int64_t in, XQ2 q, const float* __restrict__ rms_w,
+                                 float eps) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
-    const int lane = threadIdx.x & 31;
-    const int64_t nsb = in / 256;
-    const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (wid >= M * nsb) return;
-    const int64_t m = wid / nsb, sb = wid % nsb;
-    const float* src = x + m * in + sb * 256 + 8 * lane;
+    __shared__ float wsum[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t nsb = in / 256, m = blockIdx.y;
+    const float* row = x + m * in;
+    float mden = 1.0f;
+    if (rms_w) {
+        float s2 = 0.0f;
+        if ((in & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+            const float4* r4 = reinterpret_cast<const float4*>(row);
+            for (int64_t i = threadIdx.x; i < in / 4; i += blockDim.x) {
+                const float4 v = r4[i];
+                s2 = fmaf(v.x, v.x, s2); s2 = fmaf(v.y, v.y, s2);
+                s2 = fmaf(v.z, v.z, s2); s2 = fmaf(v.w, v.w, s2);
+            }
+        } else {
+            for (int64_t i = threadIdx.x; i < in; i += blockDim.x) s2 = fmaf(row[i], row[i], s2);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        if (lane == 0) wsum[warp] = s2;
+        __syncthreads();
+        float tot = 0.0f;
+        for (int k = 0; k < 8; k++) tot += wsum[k];
+        mden = sqrtf(tot / (float)in + eps);
+    }
+    const int64_t sb = (int64_t)blockIdx.x * 8 + warp;
+    if (sb >= nsb) return;
+    const float* src = row + sb * 256 + 8 * lane;
     float v[8];
     if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
         const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
@@ -90,6 +115,10 @@ __global__ void xq2_stage_kernel(const float* __restrict__ x, int64_t M, int64_t
     } else {
 #pragma unroll
         for (int k = 0; k < 8; k++) v[k] = src[k];
+    }
+    if (rms_w) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = v[k] / mden * rms_w[sb * 256 + 8 * lane + k];
     }
     float amax = 0.0f, s = 0.0f;
 #pragma unroll
@@ -135,7 +164,8 @@ constexpr int kI8Bar = 2 * 16 * 8;  // up to 16 stages: full + empty barriers
 struct I8Job {
     const uint8_t* qs;
     const uint8_t* hdr;
-    float* y;       // [M][out]
+    float* y;          // [M][out]
+    const float* add;  // optional residual [M][out]: y = x W^T + add (may alias y)
     int64_t out;
 };
 
@@ -148,6 +178,7 @@ struct I8Params {
     uint32_t qstride, hstride;  // padded shared-memory row strides
     uint32_t stage_bytes, red_off, ring_off;
     int nstage;
+    int RS;                     // weight rows per stage (<= 16, the MMA tile)
     XQ2 xq;
     int* err;
 };
@@ -199,12 +230,12 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                 int64_t rb;
                 int nrows;
                 i8_rows(jb, &rb, &nrows);
-                for (int r0 = 0; r0 < nrows; r0 += kI8Rows, it++, slot = slot + 1 == p.nstage ? 0 : slot + 1,
+                for (int r0 = 0; r0 < nrows; r0 += p.RS, it++, slot = slot + 1 == p.nstage ? 0 : slot + 1,
                          use += slot == 0) {
                     if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
-                    const int rows = min(kI8Rows, nrows - r0);
+                    const int rows = min(p.RS, nrows - r0);
                     const uint32_t dst = smem_u32(ring) + (uint32_t)slot * p.stage_bytes;
-                    const uint32_t hdst = dst + (uint32_t)kI8Rows * p.qstride;
+                    const uint32_t hdst = dst + (uint32_t)p.RS * p.qstride;
                     mbar_expect_tx(full0 + 8 * slot, (uint32_t)rows * (p.qrow + p.hrow));
                     for (int r = 0; r < rows; r++) {
                         const int64_t row = rb + r0 + r;
@@ -249,8 +280,22 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                 for (int c = 0; c < 2; c++)
                     coef[s][c] = (t < 3 && c < M && s < nsbw) ? p.xq.sx[(int64_t)c * p.nsb + sb0 + s] * pw : 0.0f;
         }
-        const float* bsum_t = p.xq.bsum + (int64_t)t * (p.in / 32);  // this lane's token for the min term
+        // block sums of this lane's token (t < M) over the slice, for the min term
         const bool tvalid = t < M;
+        float bs[kI8MaxSB][8];
+        {
+            const float* bsum_t = p.xq.bsum + (int64_t)(tvalid ? t : 0) * (p.in / 32);
+#pragma unroll
+            for (int s = 0; s < kI8MaxSB; s++) {
+                float4 b0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), b1 = b0;
+                if (tvalid && s < nsbw) {
+                    b0 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)(sb0 + s) * 8);
+                    b1 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)(sb0 + s) * 8 + 4);
+                }
+                bs[s][0] = b0.x; bs[s][1] = b0.y; bs[s][2] = b0.z; bs[s][3] = b0.w;
+                bs[s][4] = b1.x; bs[s][5] = b1.y; bs[s][6] = b1.z; bs[s][7] = b1.w;
+            }
+        }
         int slot = 0, use = 0, roff = 0;
         bool ok = true;
         for (int j = 0; j < p.njobs && ok; j++) {
@@ -258,22 +303,25 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
             int64_t rb;
             int nrows;
             i8_rows(jb, &rb, &nrows);
-            for (int r0 = 0; r0 < nrows; r0 += kI8Rows, slot = slot + 1 == p.nstage ? 0 : slot + 1, use += slot == 0) {
+            for (int r0 = 0; r0 < nrows; r0 += p.RS, slot = slot + 1 == p.nstage ? 0 : slot + 1, use += slot == 0) {
                 if (!mbar_wait(full0 + 8 * slot, use & 1)) {
                     if (lane == 0 && p.err) atomicExch(p.err, 1);
                     ok = false;
                     break;
                 }
                 const uint8_t* sq = ring + (size_t)slot * p.stage_bytes;
-                const uint8_t* sh = sq + (size_t)kI8Rows * p.qstride;
+                const uint8_t* sh = sq + (size_t)p.RS * p.qstride;
+                const int rows = min(p.RS, nrows - r0);
+                // MMA rows past the stage's rows read its last row (results dropped)
+                const int rA = min(g, rows - 1), rB = min(g + 8, rows - 1);
                 float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // rows g, g (cols 2t, 2t+1), g+8, g+8
                 float mn[2] = {0.0f, 0.0f};               // min term of token t, rows g and g+8
 #pragma unroll
                 for (int s = 0; s < kI8MaxSB; s++) {
                     if (s < nsbw) {
                         const int sb = sb0 + s;
-                        const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)g * p.hstride + sb * 16);
-                        const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)(g + 8) * p.hstride + sb * 16);
+                        const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
+                        const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
                         // Q4_K 6-bit scales and mins, four per word
                         const uint32_t scg0 = hg.y & 0x3F3F3F3Fu, mg0 = hg.z & 0x3F3F3F3Fu;
                         const uint32_t scg1 = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
@@ -282,8 +330,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                         const uint32_t sc81 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
                         const uint32_t m81 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
                         int ai[4] = {0, 0, 0, 0};
-                        const uint8_t* qg = sq + (size_t)g * p.qstride + sb * 128 + 8 * t;
-                        const uint8_t* q8 = qg + 8 * (size_t)p.qstride;
+                        const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 8 * t;
+                        const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 8 * t;
 #pragma unroll
                         for (int c = 0; c < 4; c++) {
                             const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
@@ -324,18 +372,20 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                         acc[1] = fmaf((float)ai[1], ddg.x * coef[s][1], acc[1]);
                         acc[2] = fmaf((float)ai[2], dd8.x * coef[s][0], acc[2]);
                         acc[3] = fmaf((float)ai[3], dd8.x * coef[s][1], acc[3]);
-                        if (tvalid) {
-                            const float4 b0 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8);
-                            const float4 b1 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8 + 4);
+                        {
+                            // m_j as exact floats: byte j of the packed mins under
+                            // the exponent of 2^23, minus 2^23 (no conversion unit)
                             float sg = 0.0f, s8 = 0.0f;
-                            sg = fmaf((float)byte_of<0>(mg0), b0.x, sg); s8 = fmaf((float)byte_of<0>(m80), b0.x, s8);
-                            sg = fmaf((float)byte_of<1>(mg0), b0.y, sg); s8 = fmaf((float)byte_of<1>(m80), b0.y, s8);
-                            sg = fmaf((float)byte_of<2>(mg0), b0.z, sg); s8 = fmaf((float)byte_of<2>(m80), b0.z, s8);
-                            sg = fmaf((float)byte_of<3>(mg0), b0.w, sg); s8 = fmaf((float)byte_of<3>(m80), b0.w, s8);
-                            sg = fmaf((float)byte_of<0>(mg1), b1.x, sg); s8 = fmaf((float)byte_of<0>(m81), b1.x, s8);
-                            sg = fmaf((float)byte_of<1>(mg1), b1.y, sg); s8 = fmaf((float)byte_of<1>(m81), b1.y, s8);
-                            sg = fmaf((float)byte_of<2>(mg1), b1.z, sg); s8 = fmaf((float)byte_of<2>(m81), b1.z, s8);
-                            sg = fmaf((float)byte_of<3>(mg1), b1.w, sg); s8 = fmaf((float)byte_of<3>(m81), b1.w, s8);
+#pragma unroll
+                            for (int jj = 0; jj < 8; jj++) {
+                                const uint32_t wg = jj < 4 ? mg0 : mg1, w8 = jj < 4 ? m80 : m81;
+                                const float fg =
+                                    __uint_as_float(__byte_perm(wg, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                                const float f8 =
+                                    __uint_as_float(__byte_perm(w8, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                                sg = fmaf(fg, bs[s][jj], sg);
+                                s8 = fmaf(f8, bs[s][jj], s8);
+                            }
                             mn[0] = fmaf(ddg.y, sg, mn[0]);
                             mn[1] = fmaf(dd8.y, s8, mn[1]);
                         }
@@ -355,7 +405,6 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                 const float mA1 = __shfl_sync(0xffffffffu, mn[0], qb + 1);
                 const float mB0 = __shfl_sync(0xffffffffu, mn[1], qb);
                 const float mB1 = __shfl_sync(0xffffffffu, mn[1], qb + 1);
-                const int rows = min(kI8Rows, nrows - r0);
                 if (t == 0) {
                     float* rg = red + ((int64_t)(roff + r0 + g) * kI8Cons + w) * M;
                     float* r8 = red + ((int64_t)(roff + r0 + g + 8) * kI8Cons + w) * M;
@@ -382,7 +431,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
             const int r = e / p.M, m = e % p.M;
             float acc = 0.0f;
             for (int s = 0; s < kI8Cons; s++) acc += red[((int64_t)(roff + r) * kI8Cons + s) * p.M + m];
-            p.jobs[j].y[(int64_t)m * p.jobs[j].out + rb + r] = acc;
+            const int64_t o = (int64_t)m * p.jobs[j].out + rb + r;
+            p.jobs[j].y[o] = p.jobs[j].add ? acc + p.jobs[j].add[o] : acc;
         }
         roff += nrows;
     }
@@ -396,11 +446,11 @@ bool mm_i8_supported(const rq_weight* w, int64_t M) {
     return w->in % 256 == 0 && nsb % kI8Cons == 0 && nsb / kI8Cons <= kI8MaxSB;
 }
 
-int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st) {
-    const int64_t warps = M * (in / 256);
-    if (warps == 0) return RQ_OK;
+int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st, const float* rms_w,
+                     float eps) {
+    if (M == 0 || in < 256) return RQ_OK;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((warps + 7) / 8));
+    cfg.gridDim = dim3((unsigned)((in / 256 + 7) / 8), (unsigned)M);
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -408,11 +458,11 @@ int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_error(cudaLaunchKernelEx(&cfg, xq2_stage_kernel, x, M, in, q), "xq2 staging kernel");
+    return cuda_error(cudaLaunchKernelEx(&cfg, xq2_stage_kernel, x, in, q, rms_w, eps), "xq2 staging kernel");
 }
 
 int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_t M, XQ2 xq, int sm_count,
-                 cudaStream_t st, int* err) {
+                 cudaStream_t st, int* err, const float* const* adds) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "int8 matmul: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     for (int j = 0; j < njobs; j++)
@@ -428,12 +478,12 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     p.hrow = (uint32_t)(w0->nblk * 16);
     p.qstride = p.qrow + kI8QPad;
     p.hstride = p.hrow + kI8HPad;
-    p.stage_bytes = (uint32_t)(kI8Rows * (p.qstride + p.hstride) + 127) & ~127u;
+    const uint32_t rowb = p.qstride + p.hstride;
     p.xq = xq;
     p.err = err;
     int64_t max_out = 0;
     for (int j = 0; j < njobs; j++) {
-        p.jobs[j] = I8Job{ws[j]->qs, ws[j]->hdr, ys[j], ws[j]->out};
+        p.jobs[j] = I8Job{ws[j]->qs, ws[j]->hdr, ys[j], adds ? adds[j] : nullptr, ws[j]->out};
         max_out = std::max(max_out, ws[j]->out);
     }
     const int grid = (int)std::min<int64_t>(max_out, sm_count);
@@ -443,7 +493,14 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     p.red_off = kI8Bar;
     p.ring_off = (uint32_t)((kI8Bar + red_bytes + 127) & ~(int64_t)127);
     if (p.ring_off >= (uint32_t)kI8Smem) return set_error(RQ_ERR_UNSUPPORTED, "int8 matmul: partial table too large");
-    const int nstage = std::min<int>((int)((kI8Smem - p.ring_off) / p.stage_bytes), 16);
+    // rows per stage: the most (<= 16) that leave three stages in flight,
+    // else two stages of 16
+    const int64_t room = kI8Smem - (int64_t)p.ring_off;
+    int RS = (int)std::min<int64_t>(kI8Rows, room / (3 * (int64_t)rowb));
+    if (RS < 12) RS = kI8Rows;
+    p.RS = RS;
+    p.stage_bytes = ((uint32_t)RS * rowb + 127) & ~127u;
+    const int nstage = std::min<int>((int)(room / p.stage_bytes), 16);
     if (nstage < 2) return set_error(RQ_ERR_UNSUPPORTED, "int8 matmul: rows of %u bytes too large", p.qrow + p.hrow);
     p.nstage = nstage;
     const size_t smem = p.ring_off + (size_t)nstage * p.stage_bytes;
