@@ -208,8 +208,9 @@ size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
 // ctx->ws (small_m_staging_bytes) and runs the kernel rq_linear routes M to.
 // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 9..16:
 // the split-K tcgen05 kernel, one pass over the weights; M = 4..8 and
-// 17..23: one mma.sync pass per 8 rows; M = 2, 3: the M=1 pipeline once per
-// row is faster (it streams at ~5 TB/s).
+// 17..23: one mma.sync pass per 8 rows; M = 2 (Q4_K, in <= 8192): the int8
+// tensor-core kernel, one pass; M = 3 and the other M = 2 shapes: the M=1
+// pipeline once per row is faster (it streams at ~5 TB/s).
 int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, int64_t M, cudaStream_t st) {
     uint8_t* ws = (uint8_t*)ctx->ws;
     int rc;
