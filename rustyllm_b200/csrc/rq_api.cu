@@ -200,6 +200,7 @@ int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles) {
 // kernel choice at M rows.
 size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
     if (mm_i8_supported(w, M)) return xq2_bytes(M, w->in);
+    if (M == 3 && mm_i8_supported(w, 2)) return xq2_bytes(2, w->in) + 256 + xq_bytes(1, w->in);
     const bool small_m = M >= kMinTensorM && mm_small_supported(w);
     return small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
 }
@@ -214,10 +215,22 @@ size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
 int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, int64_t M, cudaStream_t st) {
     uint8_t* ws = (uint8_t*)ctx->ws;
     int rc;
-    if (mm_i8_supported(w, M)) {  // M = 2..4: one pass on the int8 tensor cores
+    if (mm_i8_supported(w, M)) {  // M = 2: one pass on the int8 tensor cores
         const XQ2 q = xq2_at(ws, M, w->in);
         rc = launch_xq2_stage(xd, M, w->in, q, st);
         if (!rc) rc = launch_mm_i8(&w, &yd, 1, M, q, ctx->sm_count, st, ctx->derr);
+        return rc;
+    }
+    if (M == 3 && mm_i8_supported(w, 2)) {  // rows 0, 1 on the int8 kernel, row 2 on the M=1 pipeline
+        const XQ2 q = xq2_at(ws, 2, w->in);
+        uint8_t* ws1 = ws + ((xq2_bytes(2, w->in) + 255) & ~(size_t)255);
+        XQ xq1;
+        xq1.planes = (int8_t*)ws1;
+        xq1.stats = (float4*)(ws1 + (((size_t)3 * w->in + 255) & ~(size_t)255));
+        rc = launch_xq2_stage(xd, 2, w->in, q, st);
+        if (!rc) rc = launch_mm_i8(&w, &yd, 1, 2, q, ctx->sm_count, st, ctx->derr);
+        if (!rc) rc = launch_xquant(xd + 2 * w->in, 1, w->in, xq1, st);
+        if (!rc) rc = launch_linear(w, xq1, yd + 2 * w->out, 1, ctx->sm_count, st, ctx->derr);
         return rc;
     }
     if (M >= kMinTensorM && mm_small_supported(w)) {
