@@ -730,7 +730,7 @@ def decode_70b(device: int, pk, new_tokens: int = 16, prompt_len: int = 20, pg=N
     # the current position, cache rolled back after each): their cost next
     # to one decode step sets the acceptance a draft model must reach
     verify_ms = {}
-    for kp1 in (2, 5, 9):
+    for kp1 in (2, 3, 5, 9):
         ids = np.array(toks[:kp1] + [0] * max(0, kp1 - len(toks)), dtype=np.int32)[:kp1]
         model.forward_all(ids, pos)
         model.truncate_caches(pos)
@@ -1054,15 +1054,16 @@ def fused_allreduce_default(world: int) -> bool:
     return os.environ.get("RQ_TP_FUSED") != "0" and world >= 2
 
 
-CASES = ("pipe_gate_up", "i8_gate_m2", "mm_gate_m8", "sk_gate_m16", "tc_gate_m128", "q3k_gate", "moe_t1", "moe_t16",
+CASES = ("pipe_gate_up", "i8_gate_m2", "i8_gate_m4", "mm_gate_m8", "sk_gate_m16", "tc_gate_m128", "q3k_gate", "moe_t1", "moe_t16",
          "attn_decode")
 
 
 def run_case(name: str) -> None:
     """A few launches of one kernel or layer for an ncu capture, at the
     bench's shapes: 'pipe_gate_up' (the gate+up rq_linear_batch of one 70B
-    layer, M=1), 'i8_gate_m2' (gate_proj 8192 -> 28672 at M=2, the int8
-    tensor-core kernel), 'mm_gate_m8' (gate_proj at M=8, mma.sync),
+    layer, M=1), 'i8_gate_m2' / 'i8_gate_m4' (gate_proj 8192 -> 28672 at
+    M=2 / 4, the int8 tensor-core kernel), 'mm_gate_m8' (gate_proj at M=8,
+    mma.sync),
     'sk_gate_m16' (M=16, split-K tcgen05), 'tc_gate_m128' (M=128, tiled
     tcgen05), 'q3k_gate' (the Q3_K gate_proj matvec), 'moe_t1' / 'moe_t16'
     (the Mixtral layer at T = 1 / 16), 'attn_decode' (a 4-layer 70B-shape
@@ -1113,7 +1114,7 @@ def run_case(name: str) -> None:
                                         arr([x.data_ptr()] * 2), arr([y.data_ptr() for y in ys]), s))
             nbytes = 2 * Q4K_BYTES(8192, 28672)
         else:
-            M = {"i8_gate_m2": 2, "mm_gate_m8": 8, "sk_gate_m16": 16, "q3k_gate": 1}.get(name, 128)
+            M = {"i8_gate_m2": 2, "i8_gate_m4": 4, "mm_gate_m8": 8, "sk_gate_m16": 16, "q3k_gate": 1}.get(name, 128)
             x = torch.randn(M, 8192, device="cuda", generator=g)
             y = torch.empty(M, 28672, device="cuda")
 

@@ -200,7 +200,6 @@ int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles) {
 // kernel choice at M rows.
 size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
     if (mm_i8_supported(w, M)) return xq2_bytes(M, w->in);
-    if (M == 3 && mm_i8_supported(w, 2)) return xq2_bytes(2, w->in) + 256 + xq_bytes(1, w->in);
     const bool small_m = M >= kMinTensorM && mm_small_supported(w);
     return small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
 }
@@ -209,28 +208,16 @@ size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
 // ctx->ws (small_m_staging_bytes) and runs the kernel rq_linear routes M to.
 // M >= 24: tcgen05 tiles of 128 weight rows x up to 112 tokens; M = 9..16:
 // the split-K tcgen05 kernel, one pass over the weights; M = 4..8 and
-// 17..23: one mma.sync pass per 8 rows; M = 2 (Q4_K, in <= 8192): the int8
-// tensor-core kernel, one pass; M = 3 and the other M = 2 shapes: the M=1
+// 17..23: one mma.sync pass per 8 rows; M = 2..4 (Q4_K, in <= 8192): the
+// int8 tensor-core kernel, one pass; the other M = 2, 3 shapes: the M=1
 // pipeline once per row is faster (it streams at ~5 TB/s).
 int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, int64_t M, cudaStream_t st) {
     uint8_t* ws = (uint8_t*)ctx->ws;
     int rc;
-    if (mm_i8_supported(w, M)) {  // M = 2: one pass on the int8 tensor cores
+    if (mm_i8_supported(w, M)) {  // M = 2..4: one pass on the int8 tensor cores
         const XQ2 q = xq2_at(ws, M, w->in);
         rc = launch_xq2_stage(xd, M, w->in, q, st);
         if (!rc) rc = launch_mm_i8(&w, &yd, 1, M, q, ctx->sm_count, st, ctx->derr);
-        return rc;
-    }
-    if (M == 3 && mm_i8_supported(w, 2)) {  // rows 0, 1 on the int8 kernel, row 2 on the M=1 pipeline
-        const XQ2 q = xq2_at(ws, 2, w->in);
-        uint8_t* ws1 = ws + ((xq2_bytes(2, w->in) + 255) & ~(size_t)255);
-        XQ xq1;
-        xq1.planes = (int8_t*)ws1;
-        xq1.stats = (float4*)(ws1 + (((size_t)3 * w->in + 255) & ~(size_t)255));
-        rc = launch_xq2_stage(xd, 2, w->in, q, st);
-        if (!rc) rc = launch_mm_i8(&w, &yd, 1, 2, q, ctx->sm_count, st, ctx->derr);
-        if (!rc) rc = launch_xquant(xd + 2 * w->in, 1, w->in, xq1, st);
-        if (!rc) rc = launch_linear(w, xq1, yd + 2 * w->out, 1, ctx->sm_count, st, ctx->derr);
         return rc;
     }
     if (M >= kMinTensorM && mm_small_supported(w)) {

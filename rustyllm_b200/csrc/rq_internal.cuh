@@ -269,7 +269,7 @@ XQ2 xq2_at(void* base, int64_t M, int64_t in);
 // stages x (M rows) or, with rms_w, RMSNorm(x) * rms_w (eps) into q
 int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st, const float* rms_w = nullptr,
                      float eps = 0.0f);
-// whether weight w takes the int8 kernel for M rows (Q4_K, M = 2,
+// whether weight w takes the int8 kernel for M rows (Q4_K, M = 2..4,
 // in = 2048 .. 8192 in steps of 2048)
 bool mm_i8_supported(const rq_weight* w, int64_t M);
 // y_j[M][out_j] = x W_j^T (+ add_j) for up to kMaxJobs weights of the same in

@@ -448,17 +448,17 @@ void set_next(rq_llama* m, const rq_weight* const* ws, int n, uint32_t budget) {
 const PipeNext* next_hint(const rq_llama* m) { return m->nx.n > 0 ? &m->nx : nullptr; }
 
 
-// Two-token forwards (the verify of a one-token draft) run the linears the
-// int8 tensor-core kernel takes in one weight pass (rq_mm_i8.cu), its
-// activation staging in m->xq's buffer.
+// Two- and three-token forwards (the verify of a one- or two-token draft)
+// run the linears the int8 tensor-core kernel takes in one weight pass
+// (rq_mm_i8.cu), its activation staging in m->xq's buffer.
 bool i8_ok(const rq_weight* const* ws, int n, int64_t T) {
-    if (T != 2) return false;
+    if (T != 2 && T != 3) return false;
     for (int i = 0; i < n; i++)
-        if (!mm_i8_supported(ws[i], 2)) return false;
+        if (!mm_i8_supported(ws[i], T)) return false;
     return true;
 }
 
-XQ2 i8_stage(const rq_llama* m, int64_t in) { return xq2_at(m->xq.planes, 2, in); }
+XQ2 i8_stage(const rq_llama* m, int64_t T, int64_t in) { return xq2_at(m->xq.planes, T, in); }
 
 // y_i[t] = x[t] W_i^T (+ add_i[t]) for the n weights (same in) and T staged rows.
 int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* const* ys,
@@ -629,7 +629,7 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
                 rc = launch_xh_stage_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xh, st);
                 if (!rc) rc = run_mm(m, 3, w3, T, y3, nullptr, st);
             } else if (i8_ok(w3, 3, T)) {
-                const XQ2 q2 = i8_stage(m, H);
+                const XQ2 q2 = i8_stage(m, T, H);
                 rc = launch_xq2_stage(m->x, T, H, q2, st, L.rms1, c.rms_eps);
                 if (!rc) rc = launch_mm_i8(w3, y3, 3, T, q2, m->ctx->sm_count, st, m->derr);
             } else {
@@ -679,7 +679,7 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
             if (rc) return rc;
             if (!tc && i8_ok(&L.w[3], 1, T)) {
                 // o on the int8 kernel: x (+)= att W^T, the residual in its epilogue
-                const XQ2 q2 = i8_stage(m, nq);
+                const XQ2 q2 = i8_stage(m, T, nq);
                 rc = launch_xq2_stage(m->att, T, nq, q2, st);
                 float* y1[1] = {m->W == 1 ? m->x : m->part};
                 const float* a1[1] = {m->R == 0 ? m->x : nullptr};
@@ -703,7 +703,7 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
                 rc = launch_xh_stage_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xh, st);
                 if (!rc) rc = run_mm(m, 2, w2, T, y2, nullptr, st);
             } else if (i8_ok(w2, 2, T)) {
-                const XQ2 q2 = i8_stage(m, H);
+                const XQ2 q2 = i8_stage(m, T, H);
                 rc = launch_xq2_stage(m->x, T, H, q2, st, L.rms2, c.rms_eps);
                 if (!rc) rc = launch_mm_i8(w2, y2, 2, T, q2, m->ctx->sm_count, st, m->derr);
             } else if (swiglu_in_epilogue(m, L.w[4], L.w[5], T)) {

@@ -158,7 +158,7 @@ constexpr int kI8Threads = 32 * (1 + kI8Cons);
 constexpr int kI8Rows = 16;        // weight rows per stage (one MMA tile)
 constexpr int kI8MaxSB = 4;        // super-blocks per K-slice (K <= 8192)
 constexpr int kI8QPad = 32, kI8HPad = 16;
-constexpr int kI8Smem = 227 * 1024;
+constexpr int kI8Smem = 226 * 1024;  // dynamic part; a few static bytes besides
 constexpr int kI8Bar = 2 * 16 * 8;  // up to 16 stages: full + empty barriers
 
 struct I8Job {
@@ -179,6 +179,8 @@ struct I8Params {
     uint32_t stage_bytes, red_off, ring_off;
     int nstage;
     int RS;                     // weight rows per stage (<= 16, the MMA tile)
+    uint32_t b_off, bstride;    // four-token kernel: staged activations [12][bstride] in shared memory
+    uint32_t pr_off;            // four-token kernel: per-stage partial sums [2][16][8][4]
     XQ2 xq;
     int* err;
 };
@@ -438,10 +440,241 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
     }
 }
 
+
+// ------------------------------------------------- three or four tokens
+//
+// The same data path and A operand; B has 12 columns, n = 4 p + m (plane p
+// of token m), in two column groups of 8 (two MMAs per sub-block).  The 12
+// activation rows are copied into shared memory once per CTA (a row per
+// column, padded by 32 bytes: conflict-free 8-byte fragment loads) instead
+// of registers.  The eight K-slice partials of a stage's rows are summed in
+// slice order through a small double-buffered table after a barrier of the
+// consumer warps, and y is written per stage.  A consumer that times out on
+// a stage raises a shared abort flag and every warp then skips the rest of
+// the work but still passes every barrier, so no barrier waits on a warp
+// that left.
+__global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* ring = smem + p.ring_off;
+    int8_t* bsm = reinterpret_cast<int8_t*>(smem + p.b_off);
+    float* pr = reinterpret_cast<float*>(smem + p.pr_off);
+    __shared__ int s_abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t full0 = smem_u32(smem), empty0 = full0 + 8 * 16;
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (warp == 0) {
+        if (lane < p.nstage) {
+            mbar_init(full0 + 8 * lane, 1);
+            mbar_init(empty0 + 8 * lane, kI8Cons);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x == 0) s_abort = 0;
+    __syncthreads();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            int it = 0, slot = 0, use = 0;
+            bool ok = true;
+            for (int j = 0; j < p.njobs && ok; j++) {
+                const I8Job& jb = p.jobs[j];
+                int64_t rb;
+                int nrows;
+                i8_rows(jb, &rb, &nrows);
+                for (int r0 = 0; r0 < nrows; r0 += p.RS, it++, slot = slot + 1 == p.nstage ? 0 : slot + 1,
+                         use += slot == 0) {
+                    if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
+                    const int rows = min(p.RS, nrows - r0);
+                    const uint32_t dst = smem_u32(ring) + (uint32_t)slot * p.stage_bytes;
+                    const uint32_t hdst = dst + (uint32_t)p.RS * p.qstride;
+                    mbar_expect_tx(full0 + 8 * slot, (uint32_t)rows * (p.qrow + p.hrow));
+                    for (int r = 0; r < rows; r++) {
+                        const int64_t row = rb + r0 + r;
+                        bulk_g2s(dst + (uint32_t)r * p.qstride, jb.qs + row * p.qrow, p.qrow, full0 + 8 * slot, pol);
+                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow, p.hrow, full0 + 8 * slot,
+                                 pol);
+                    }
+                }
+            }
+            for (int k = max(0, it - p.nstage); k < it; k++)
+                if (!mbar_wait(full0 + 8 * (k % p.nstage), (k / p.nstage) & 1)) ok = false;
+            if (!ok && p.err) atomicExch(p.err, 1);
+        }
+        return;
+    }
+    const int w = warp - 1, ct = threadIdx.x - 32;
+    const int g = lane >> 2, t = lane & 3;
+    const int M = p.M;
+    const int sb0 = w * p.nsb / kI8Cons, nsbw = (w + 1) * p.nsb / kI8Cons - sb0;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the activation rows into shared memory: column n = 4 p + m
+    {
+        const int64_t chunks = p.in / 16;  // 16-byte chunks per row
+        for (int64_t i = ct; i < (int64_t)3 * M * chunks; i += 32 * kI8Cons) {
+            const int64_t r = i / chunks, c = i % chunks;  // r = 3 m + p: the XQ2 row order
+            const int m = (int)(r / 3), pl = (int)(r % 3);
+            const uint4 v = *reinterpret_cast<const uint4*>(p.xq.planes + r * p.in + 16 * c);
+            *reinterpret_cast<uint4*>(bsm + (size_t)(4 * pl + m) * p.bstride + 16 * c) = v;
+        }
+    }
+    named_bar_sync(1, 32 * kI8Cons);
+    // B fragment columns of this lane and the f32 factors of its C columns
+    const int n0 = g, n1 = 8 + g;
+    const bool v0 = (n0 & 3) < M, v1 = (n1 >> 2) < 3 && (n1 & 3) < M;
+    const int8_t* bp0 = bsm + (size_t)(v0 ? n0 : 0) * p.bstride + 8 * t;
+    const int8_t* bp1 = bsm + (size_t)(v1 ? n1 : 0) * p.bstride + 8 * t;
+    // the f32 factors of this lane's C columns (sx * plane weight, zero for
+    // absent tokens) and its token's block sums are read per super-block
+    // (L1-resident) to keep registers for the MMA tiles
+    const int na0 = 2 * t, nb0 = 8 + 2 * t;  // first C column of the two groups
+    const float pwa = (na0 >> 2) == 0 ? 65536.0f : 256.0f;
+    const bool ca0 = (na0 & 3) < M, ca1 = ((na0 + 1) & 3) < M;
+    const bool cb0 = (nb0 >> 2) < 3 && (nb0 & 3) < M, cb1 = ((nb0 + 1) >> 2) < 3 && ((nb0 + 1) & 3) < M;
+    const float* sxa0 = p.xq.sx + (int64_t)(ca0 ? (na0 & 3) : 0) * p.nsb;
+    const float* sxa1 = p.xq.sx + (int64_t)(ca1 ? ((na0 + 1) & 3) : 0) * p.nsb;
+    const float* sxb0 = p.xq.sx + (int64_t)(cb0 ? (nb0 & 3) : 0) * p.nsb;
+    const float* sxb1 = p.xq.sx + (int64_t)(cb1 ? ((nb0 + 1) & 3) : 0) * p.nsb;
+    const bool tvalid = t < M;
+    const float* bsum_t = p.xq.bsum + (int64_t)(tvalid ? t : 0) * (p.in / 32);
+    int slot = 0, use = 0, par = 0;
+    for (int j = 0; j < p.njobs; j++) {
+        const I8Job& jb = p.jobs[j];
+        int64_t rb;
+        int nrows;
+        i8_rows(jb, &rb, &nrows);
+        for (int r0 = 0; r0 < nrows; r0 += p.RS, slot = slot + 1 == p.nstage ? 0 : slot + 1, use += slot == 0,
+                 par ^= 1) {
+            if (!*(volatile int*)&s_abort && !mbar_wait(full0 + 8 * slot, use & 1)) {
+                if (lane == 0 && p.err) atomicExch(p.err, 1);
+                *(volatile int*)&s_abort = 1;
+            }
+            const bool live = !*(volatile int*)&s_abort;
+            const uint8_t* sq = ring + (size_t)slot * p.stage_bytes;
+            const uint8_t* sh = sq + (size_t)p.RS * p.qstride;
+            const int rows = min(p.RS, nrows - r0);
+            const int rA = min(g, rows - 1), rB = min(g + 8, rows - 1);
+            float acc0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            float mn[2] = {0.0f, 0.0f};
+#pragma unroll
+            for (int s = 0; s < kI8MaxSB; s++) {
+                if (live && s < nsbw) {
+                    const int sb = sb0 + s;
+                    const float cf0 = ca0 ? __ldg(sxa0 + sb) * pwa : 0.0f, cf1 = ca1 ? __ldg(sxa1 + sb) * pwa : 0.0f;
+                    const float cg0 = cb0 ? __ldg(sxb0 + sb) : 0.0f, cg1 = cb1 ? __ldg(sxb1 + sb) : 0.0f;
+                    float4 bsa = make_float4(0.0f, 0.0f, 0.0f, 0.0f), bsb = bsa;
+                    if (tvalid) {
+                        bsa = __ldg(reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8));
+                        bsb = __ldg(reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8 + 4));
+                    }
+                    const float bsv[8] = {bsa.x, bsa.y, bsa.z, bsa.w, bsb.x, bsb.y, bsb.z, bsb.w};
+                    const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
+                    const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
+                    const uint32_t scg0 = hg.y & 0x3F3F3F3Fu, mg0 = hg.z & 0x3F3F3F3Fu;
+                    const uint32_t scg1 = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
+                    const uint32_t mg1 = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
+                    const uint32_t sc80 = h8.y & 0x3F3F3F3Fu, m80 = h8.z & 0x3F3F3F3Fu;
+                    const uint32_t sc81 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
+                    const uint32_t m81 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
+                    int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+                    const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 8 * t;
+                    const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 8 * t;
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
+                        const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
+                        const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
+                                                 w8.y & 0x0F0F0F0Fu};
+                        const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
+                                                 (wg.y >> 4) & 0x0F0F0F0Fu, (w8.y >> 4) & 0x0F0F0F0Fu};
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int sub = 2 * c + h;
+                            const int64_t ko = (int64_t)(sb * 8 + sub) * 32;
+                            uint2 b0 = make_uint2(0u, 0u), b1 = make_uint2(0u, 0u);
+                            if (v0) b0 = *reinterpret_cast<const uint2*>(bp0 + ko);
+                            if (v1) b1 = *reinterpret_cast<const uint2*>(bp1 + ko);
+                            int d0[4], d1[4];
+                            if (h == 0) {
+                                mma_u8s8(d0, alo, b0.x, b0.y);
+                                mma_u8s8(d1, alo, b1.x, b1.y);
+                            } else {
+                                mma_u8s8(d0, ahi, b0.x, b0.y);
+                                mma_u8s8(d1, ahi, b1.x, b1.y);
+                            }
+                            const uint32_t wgs = c < 2 ? scg0 : scg1, w8s = c < 2 ? sc80 : sc81;
+                            const int byte = (2 * c + h) & 3;
+                            const int sg = (int)__byte_perm(wgs, 0u, 0x4440u + byte);
+                            const int s8 = (int)__byte_perm(w8s, 0u, 0x4440u + byte);
+                            a0[0] += d0[0] * sg; a0[1] += d0[1] * sg; a0[2] += d0[2] * s8; a0[3] += d0[3] * s8;
+                            a1[0] += d1[0] * sg; a1[1] += d1[1] * sg; a1[2] += d1[2] * s8; a1[3] += d1[3] * s8;
+                        }
+                    }
+                    const float2 ddg = __half22float2(*reinterpret_cast<const __half2*>(&hg.x));
+                    const float2 dd8 = __half22float2(*reinterpret_cast<const __half2*>(&h8.x));
+                    acc0[0] = fmaf((float)a0[0], ddg.x * cf0, acc0[0]);
+                    acc0[1] = fmaf((float)a0[1], ddg.x * cf1, acc0[1]);
+                    acc0[2] = fmaf((float)a0[2], dd8.x * cf0, acc0[2]);
+                    acc0[3] = fmaf((float)a0[3], dd8.x * cf1, acc0[3]);
+                    acc1[0] = fmaf((float)a1[0], ddg.x * cg0, acc1[0]);
+                    acc1[1] = fmaf((float)a1[1], ddg.x * cg1, acc1[1]);
+                    acc1[2] = fmaf((float)a1[2], dd8.x * cg0, acc1[2]);
+                    acc1[3] = fmaf((float)a1[3], dd8.x * cg1, acc1[3]);
+                    float sgm = 0.0f, s8m = 0.0f;
+#pragma unroll
+                    for (int jj = 0; jj < 8; jj++) {
+                        const uint32_t wg = jj < 4 ? mg0 : mg1, w8 = jj < 4 ? m80 : m81;
+                        const float fg =
+                            __uint_as_float(__byte_perm(wg, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                        const float f8 =
+                            __uint_as_float(__byte_perm(w8, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                        sgm = fmaf(fg, bsv[jj], sgm);
+                        s8m = fmaf(f8, bsv[jj], s8m);
+                    }
+                    mn[0] = fmaf(ddg.y, sgm, mn[0]);
+                    mn[1] = fmaf(dd8.y, s8m, mn[1]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty0 + 8 * slot);
+            // token 2t + c (t < 2): plane 0 in acc0 here, plane 1 in acc0 of
+            // lane t + 2, plane 2 in acc1 here
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[i] = acc0[i] + __shfl_xor_sync(0xffffffffu, acc0[i], 2) + acc1[i];
+            const int qb = lane & ~3;
+            const float mA0 = __shfl_sync(0xffffffffu, mn[0], qb + ((2 * t) & 3));
+            const float mA1 = __shfl_sync(0xffffffffu, mn[0], qb + ((2 * t + 1) & 3));
+            const float mB0 = __shfl_sync(0xffffffffu, mn[1], qb + ((2 * t) & 3));
+            const float mB1 = __shfl_sync(0xffffffffu, mn[1], qb + ((2 * t + 1) & 3));
+            float* buf = pr + par * (kI8Rows * kI8Cons * 4);
+            if (t < 2) {
+                const int m0 = 2 * t, m1 = 2 * t + 1;
+                if (g < rows) {
+                    buf[(g * kI8Cons + w) * 4 + m0] = v[0] - mA0;
+                    buf[(g * kI8Cons + w) * 4 + m1] = v[1] - mA1;
+                }
+                if (g + 8 < rows) {
+                    buf[((g + 8) * kI8Cons + w) * 4 + m0] = v[2] - mB0;
+                    buf[((g + 8) * kI8Cons + w) * 4 + m1] = v[3] - mB1;
+                }
+            }
+            named_bar_sync(1, 32 * kI8Cons);
+            if (ct < rows * M && !*(volatile int*)&s_abort) {
+                const int r = ct / M, m = ct % M;
+                float acc = 0.0f;
+                for (int s = 0; s < kI8Cons; s++) acc += buf[(r * kI8Cons + s) * 4 + m];
+                const int64_t o = (int64_t)m * jb.out + rb + r0 + r;
+                jb.y[o] = jb.add ? acc + jb.add[o] : acc;
+            }
+        }
+    }
+}
+
 }  // namespace
 
 bool mm_i8_supported(const rq_weight* w, int64_t M) {
-    if (w->type != RQ_Q4_K || M != 2) return false;
+    if (w->type != RQ_Q4_K || M < 2 || M > 4) return false;
     const int64_t nsb = w->in / 256;
     return w->in % 256 == 0 && nsb % kI8Cons == 0 && nsb / kI8Cons <= kI8MaxSB;
 }
@@ -489,15 +722,24 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     const int grid = (int)std::min<int64_t>(max_out, sm_count);
     int64_t rows_cap = 0;
     for (int j = 0; j < njobs; j++) rows_cap += (ws[j]->out + grid - 1) / grid;
-    const int64_t red_bytes = rows_cap * kI8Cons * M * 4;
-    p.red_off = kI8Bar;
-    p.ring_off = (uint32_t)((kI8Bar + red_bytes + 127) & ~(int64_t)127);
+    const bool x4 = M > 2;  // three or four tokens: activations in shared memory, per-stage sums
+    if (x4) {
+        p.pr_off = kI8Bar;
+        p.b_off = (uint32_t)((p.pr_off + 2 * kI8Rows * kI8Cons * 4 * 4 + 127) & ~127u);
+        p.bstride = (uint32_t)(w0->in + 32);
+        p.ring_off = (uint32_t)((p.b_off + 12 * (int64_t)p.bstride + 127) & ~(int64_t)127);
+    } else {
+        const int64_t red_bytes = rows_cap * kI8Cons * M * 4;
+        p.red_off = kI8Bar;
+        p.ring_off = (uint32_t)((kI8Bar + red_bytes + 127) & ~(int64_t)127);
+    }
     if (p.ring_off >= (uint32_t)kI8Smem) return set_error(RQ_ERR_UNSUPPORTED, "int8 matmul: partial table too large");
     // rows per stage: the most (<= 16) that leave three stages in flight,
     // else two stages of 16
     const int64_t room = kI8Smem - (int64_t)p.ring_off;
     int RS = (int)std::min<int64_t>(kI8Rows, room / (3 * (int64_t)rowb));
-    if (RS < 12) RS = kI8Rows;
+    if (RS < 12) RS = (int)std::min<int64_t>(kI8Rows, room / (2 * (int64_t)rowb));
+    if (RS < 1) return set_error(RQ_ERR_UNSUPPORTED, "int8 matmul: rows of %u bytes too large", p.qrow + p.hrow);
     p.RS = RS;
     p.stage_bytes = ((uint32_t)RS * rowb + 127) & ~127u;
     const int nstage = std::min<int>((int)(room / p.stage_bytes), 16);
@@ -509,6 +751,8 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
         cudaError_t e = cudaFuncSetAttribute(mm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kI8Smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(mm_i8x4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kI8Smem);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(int8 matmul)");
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -522,7 +766,8 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_error(cudaLaunchKernelEx(&cfg, mm_i8_kernel, p), "int8 matmul kernel");
+    return cuda_error(x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel, p) : cudaLaunchKernelEx(&cfg, mm_i8_kernel, p),
+                      "int8 matmul kernel");
 }
 
 }  // namespace rq

@@ -91,3 +91,19 @@ def test_70b_geometry_two_token_verify(pair):
     for t in range(2):
         assert rel_l2(logits[t], ref_logits[12 + t]) <= LOGIT_TOL, t
     assert amax == ref_amax[12:].tolist()
+
+
+def test_70b_geometry_three_token_verify(pair):
+    """forward_all over 3 tokens (the verify of a two-token draft): q/k/v,
+    o and gate/up on the int8 kernel's twelve-column form; every position
+    within 1e-4 of the oracle, argmax equal."""
+    model, ref, _ = pair
+    rng = np.random.default_rng(23)
+    prompt = rng.integers(0, CFG["vocab"], size=12).astype(np.int32)
+    draft = rng.integers(0, CFG["vocab"], size=3).astype(np.int32)
+    model.forward(prompt, 0, want_logits=False)
+    logits, amax = model.forward_all(draft, 12, want_logits=True)
+    ref_logits, ref_amax = ref.forward_all(np.concatenate([prompt, draft]), 0)
+    for t in range(3):
+        assert rel_l2(logits[t], ref_logits[12 + t]) <= LOGIT_TOL, t
+    assert amax == ref_amax[12:].tolist()
