@@ -199,7 +199,7 @@ int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles) {
 // Bytes of activation staging at the start of ctx->ws for rq_linear's
 // kernel choice at M rows.
 size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
-    if (mm_i8_supported(w, M)) return xq2_bytes(M, w->in);
+    if (mm_i8_supported(w, M)) return xq2_bytes(M, w->in) + 256 + mm_i8_scratch_floats(w, M) * sizeof(float);
     const bool small_m = M >= kMinTensorM && mm_small_supported(w);
     return small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
 }
@@ -216,8 +216,9 @@ int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, i
     int rc;
     if (mm_i8_supported(w, M)) {  // M = 2..4: one pass on the int8 tensor cores
         const XQ2 q = xq2_at(ws, M, w->in);
+        float* part = (float*)(ws + ((xq2_bytes(M, w->in) + 255) & ~(size_t)255));
         rc = launch_xq2_stage(xd, M, w->in, q, st);
-        if (!rc) rc = launch_mm_i8(&w, &yd, 1, M, q, ctx->sm_count, st, ctx->derr);
+        if (!rc) rc = launch_mm_i8(&w, &yd, 1, M, q, ctx->sm_count, st, ctx->derr, nullptr, part, ctx->i8_cnt);
         return rc;
     }
     if (M >= kMinTensorM && mm_small_supported(w)) {
@@ -304,9 +305,13 @@ int rq_init(int device, rq_ctx** out) {
     c->sm_count = prop.multiProcessorCount;
     e = cudaMalloc(&c->derr, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(c->derr, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&c->i8_cnt, 256 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->i8_cnt, 0, 256 * sizeof(int));
     if (e == cudaSuccess) e = cudaHostAlloc(&c->err_host, sizeof(int), cudaHostAllocDefault);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         if (c->derr) cudaFree(c->derr);
+        if (c->i8_cnt) cudaFree(c->i8_cnt);
         delete c;
         return cuda_error(e, "rq_init: error word");
     }
@@ -340,6 +345,7 @@ int rq_destroy(rq_ctx* ctx) {
     if (ctx->sk_ws) cudaFree(ctx->sk_ws);
     if (ctx->sk_cnt) cudaFree(ctx->sk_cnt);
     if (ctx->derr) cudaFree(ctx->derr);
+    if (ctx->i8_cnt) cudaFree(ctx->i8_cnt);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     delete ctx;
     return RQ_OK;

@@ -110,6 +110,7 @@ struct rq_ctx {
     // rq_ctx_status reads it for asynchronous ones.
     int* derr = nullptr;
     int* err_host = nullptr;
+    int* i8_cnt = nullptr;   // int8 matmul split-K arrivals per row group (kept at zero between launches)
 };
 
 namespace rq {
@@ -270,11 +271,17 @@ XQ2 xq2_at(void* base, int64_t M, int64_t in);
 int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st, const float* rms_w = nullptr,
                      float eps = 0.0f);
 // whether weight w takes the int8 kernel for M rows (Q4_K, M = 2..4,
-// in = 2048 .. 8192 in steps of 2048)
+// in = 2048 .. 8192 in steps of 2048, or a multiple of 1024 up to 32768 with
+// K split over four CTAs per row group)
 bool mm_i8_supported(const rq_weight* w, int64_t M);
-// y_j[M][out_j] = x W_j^T (+ add_j) for up to kMaxJobs weights of the same in
+// scratch floats a launch on w needs for its split-K partial rows (0: none)
+size_t mm_i8_scratch_floats(const rq_weight* w, int64_t M);
+// y_j[M][out_j] = x W_j^T (+ add_j) for up to kMaxJobs weights of the same
+// in; a split K (one job) needs part (mm_i8_scratch_floats) and cnt (256
+// arrival counters, zero between launches, left zero)
 int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_t M, XQ2 xq, int sm_count,
-                 cudaStream_t st, int* err, const float* const* adds = nullptr);
+                 cudaStream_t st, int* err, const float* const* adds = nullptr, float* part = nullptr,
+                 int* cnt = nullptr);
 int launch_xh_stage(const float* x, int64_t M, int64_t in, XH xh, cudaStream_t st);
 // the same staging of RMSNorm(x) * w, and of silu(gate) * up
 int launch_xh_stage_rmsnorm(const float* x, const float* w, float eps, int64_t M, int64_t in, XH xh,

@@ -160,6 +160,7 @@ constexpr int kI8MaxSB = 4;        // super-blocks per K-slice (K <= 8192)
 constexpr int kI8QPad = 32, kI8HPad = 16;
 constexpr int kI8Smem = 226 * 1024;  // dynamic part; a few static bytes besides
 constexpr int kI8Bar = 2 * 16 * 8;  // up to 16 stages: full + empty barriers
+constexpr int kI8MaxRowGroups = 256;  // arrival counters a split K may use
 
 struct I8Job {
     const uint8_t* qs;
@@ -181,15 +182,51 @@ struct I8Params {
     int RS;                     // weight rows per stage (<= 16, the MMA tile)
     uint32_t b_off, bstride;    // four-token kernel: staged activations [12][bstride] in shared memory
     uint32_t pr_off;            // four-token kernel: per-stage partial sums [2][16][8][4]
+    int ks;                     // K-splits: CTA b takes K-range b % ks of row group b / ks
+    int nsbr;                   // super-blocks per full row (nsb: per K-range)
+    uint32_t qseg, hseg;        // device bytes of a K-range of a row
+    float* part;                // ks > 1: partial y [ks][M][out]
+    int* cnt;                   // ks > 1: arrivals per row group (zero between launches)
     XQ2 xq;
     int* err;
 };
 
-__device__ __forceinline__ void i8_rows(const I8Job& j, int64_t* rb, int* n) {
-    const int64_t b = (int64_t)blockIdx.x * j.out / gridDim.x;
-    const int64_t e = (int64_t)(blockIdx.x + 1) * j.out / gridDim.x;
+// rows of row group rg of nrg (the CTA's rows when K is not split)
+__device__ __forceinline__ void i8_rows(const I8Job& j, int rg, int nrg, int64_t* rb, int* n) {
+    const int64_t b = (int64_t)rg * j.out / nrg;
+    const int64_t e = (int64_t)(rg + 1) * j.out / nrg;
     *rb = b;
     *n = (int)(e - b);
+}
+
+// K-split reduction: this CTA's partial rows are in part; the last of the
+// ks CTAs of the row group to arrive sums the ks partials in split order
+// (deterministic) into y.  Run by `nthr` threads (ct = 0..nthr-1) that
+// synchronise with named barrier `bar`.
+__device__ __forceinline__ void i8_ksplit_finish(const I8Params& p, int rgi, int nrg, int ct, int nthr, int bar,
+                                                 int* s_last) {
+    __threadfence();
+    named_bar_sync(bar, nthr);
+    if (ct == 0) {
+        __threadfence();
+        const int old = atomicAdd(p.cnt + rgi, 1);
+        *s_last = old == p.ks - 1;
+        if (old == p.ks - 1) atomicExch(p.cnt + rgi, 0);
+    }
+    named_bar_sync(bar, nthr);
+    if (!*s_last) return;
+    __threadfence();
+    const I8Job& jb = p.jobs[0];
+    int64_t rb;
+    int nrows;
+    i8_rows(jb, rgi, nrg, &rb, &nrows);
+    for (int e = ct; e < nrows * p.M; e += nthr) {
+        const int r = e / p.M, m = e % p.M;
+        const int64_t o = (int64_t)m * jb.out + rb + r;
+        float acc = 0.0f;
+        for (int k = 0; k < p.ks; k++) acc += __ldcg(p.part + (int64_t)k * p.M * jb.out + o);
+        jb.y[o] = jb.add ? acc + jb.add[o] : acc;
+    }
 }
 
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -212,6 +249,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
     uint8_t* ring = smem + p.ring_off;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t full0 = smem_u32(smem), empty0 = full0 + 8 * 16;
+    // K-split: this CTA's row group and K-range (super-blocks kb0 .. kb0 + nsb)
+    const int ksi = blockIdx.x % p.ks, rgi = blockIdx.x / p.ks, nrg = gridDim.x / p.ks;
+    const int kb0 = ksi * p.nsb;
     asm volatile("griddepcontrol.launch_dependents;");
     if (warp == 0) {
         if (lane < p.nstage) {
@@ -231,19 +271,20 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                 const I8Job& jb = p.jobs[j];
                 int64_t rb;
                 int nrows;
-                i8_rows(jb, &rb, &nrows);
+                i8_rows(jb, rgi, nrg, &rb, &nrows);
                 for (int r0 = 0; r0 < nrows; r0 += p.RS, it++, slot = slot + 1 == p.nstage ? 0 : slot + 1,
                          use += slot == 0) {
                     if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
                     const int rows = min(p.RS, nrows - r0);
                     const uint32_t dst = smem_u32(ring) + (uint32_t)slot * p.stage_bytes;
                     const uint32_t hdst = dst + (uint32_t)p.RS * p.qstride;
-                    mbar_expect_tx(full0 + 8 * slot, (uint32_t)rows * (p.qrow + p.hrow));
+                    mbar_expect_tx(full0 + 8 * slot, (uint32_t)rows * (p.qseg + p.hseg));
                     for (int r = 0; r < rows; r++) {
                         const int64_t row = rb + r0 + r;
-                        bulk_g2s(dst + (uint32_t)r * p.qstride, jb.qs + row * p.qrow, p.qrow, full0 + 8 * slot, pol);
-                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow, p.hrow, full0 + 8 * slot,
-                                 pol);
+                        bulk_g2s(dst + (uint32_t)r * p.qstride, jb.qs + row * p.qrow + (int64_t)kb0 * 128, p.qseg,
+                                 full0 + 8 * slot, pol);
+                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow + (int64_t)kb0 * 16, p.hseg,
+                                 full0 + 8 * slot, pol);
                     }
                 }
             }
@@ -271,7 +312,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                 for (int j = 0; j < 8; j++) {
                     uint2 u = make_uint2(0u, 0u);
                     if (bvalid && s < nsbw)
-                        u = *reinterpret_cast<const uint2*>(bsrc + ((int64_t)(sb0 + s) * 8 + j) * 32);
+                        u = *reinterpret_cast<const uint2*>(bsrc + ((int64_t)(kb0 + sb0 + s) * 8 + j) * 32);
                     bf[s][j][0] = u.x;
                     bf[s][j][1] = u.y;
                 }
@@ -280,7 +321,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
             for (int s = 0; s < kI8MaxSB; s++)
 #pragma unroll
                 for (int c = 0; c < 2; c++)
-                    coef[s][c] = (t < 3 && c < M && s < nsbw) ? p.xq.sx[(int64_t)c * p.nsb + sb0 + s] * pw : 0.0f;
+                    coef[s][c] =
+                        (t < 3 && c < M && s < nsbw) ? p.xq.sx[(int64_t)c * p.nsbr + kb0 + sb0 + s] * pw : 0.0f;
         }
         // block sums of this lane's token (t < M) over the slice, for the min term
         const bool tvalid = t < M;
@@ -291,8 +333,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
             for (int s = 0; s < kI8MaxSB; s++) {
                 float4 b0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), b1 = b0;
                 if (tvalid && s < nsbw) {
-                    b0 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)(sb0 + s) * 8);
-                    b1 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)(sb0 + s) * 8 + 4);
+                    b0 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)(kb0 + sb0 + s) * 8);
+                    b1 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)(kb0 + sb0 + s) * 8 + 4);
                 }
                 bs[s][0] = b0.x; bs[s][1] = b0.y; bs[s][2] = b0.z; bs[s][3] = b0.w;
                 bs[s][4] = b1.x; bs[s][5] = b1.y; bs[s][6] = b1.z; bs[s][7] = b1.w;
@@ -304,7 +346,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
             const I8Job& jb = p.jobs[j];
             int64_t rb;
             int nrows;
-            i8_rows(jb, &rb, &nrows);
+            i8_rows(jb, rgi, nrg, &rb, &nrows);
             for (int r0 = 0; r0 < nrows; r0 += p.RS, slot = slot + 1 == p.nstage ? 0 : slot + 1, use += slot == 0) {
                 if (!mbar_wait(full0 + 8 * slot, use & 1)) {
                     if (lane == 0 && p.err) atomicExch(p.err, 1);
@@ -428,15 +470,22 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
     for (int j = 0; j < p.njobs; j++) {
         int64_t rb;
         int nrows;
-        i8_rows(p.jobs[j], &rb, &nrows);
+        i8_rows(p.jobs[j], rgi, nrg, &rb, &nrows);
         for (int e = threadIdx.x; e < nrows * p.M; e += blockDim.x) {
             const int r = e / p.M, m = e % p.M;
             float acc = 0.0f;
             for (int s = 0; s < kI8Cons; s++) acc += red[((int64_t)(roff + r) * kI8Cons + s) * p.M + m];
             const int64_t o = (int64_t)m * p.jobs[j].out + rb + r;
-            p.jobs[j].y[o] = p.jobs[j].add ? acc + p.jobs[j].add[o] : acc;
+            if (p.ks > 1)
+                p.part[(int64_t)ksi * p.M * p.jobs[j].out + o] = acc;
+            else
+                p.jobs[j].y[o] = p.jobs[j].add ? acc + p.jobs[j].add[o] : acc;
         }
         roff += nrows;
+    }
+    if (p.ks > 1) {
+        __shared__ int s_last;
+        i8_ksplit_finish(p, rgi, nrg, threadIdx.x, blockDim.x, 0, &s_last);
     }
 }
 
@@ -461,6 +510,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
     __shared__ int s_abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t full0 = smem_u32(smem), empty0 = full0 + 8 * 16;
+    // K-split: this CTA's row group and K-range (super-blocks kb0 .. kb0 + nsb)
+    const int ksi = blockIdx.x % p.ks, rgi = blockIdx.x / p.ks, nrg = gridDim.x / p.ks;
+    const int kb0 = ksi * p.nsb;
     asm volatile("griddepcontrol.launch_dependents;");
     if (warp == 0) {
         if (lane < p.nstage) {
@@ -481,19 +533,20 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                 const I8Job& jb = p.jobs[j];
                 int64_t rb;
                 int nrows;
-                i8_rows(jb, &rb, &nrows);
+                i8_rows(jb, rgi, nrg, &rb, &nrows);
                 for (int r0 = 0; r0 < nrows; r0 += p.RS, it++, slot = slot + 1 == p.nstage ? 0 : slot + 1,
                          use += slot == 0) {
                     if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
                     const int rows = min(p.RS, nrows - r0);
                     const uint32_t dst = smem_u32(ring) + (uint32_t)slot * p.stage_bytes;
                     const uint32_t hdst = dst + (uint32_t)p.RS * p.qstride;
-                    mbar_expect_tx(full0 + 8 * slot, (uint32_t)rows * (p.qrow + p.hrow));
+                    mbar_expect_tx(full0 + 8 * slot, (uint32_t)rows * (p.qseg + p.hseg));
                     for (int r = 0; r < rows; r++) {
                         const int64_t row = rb + r0 + r;
-                        bulk_g2s(dst + (uint32_t)r * p.qstride, jb.qs + row * p.qrow, p.qrow, full0 + 8 * slot, pol);
-                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow, p.hrow, full0 + 8 * slot,
-                                 pol);
+                        bulk_g2s(dst + (uint32_t)r * p.qstride, jb.qs + row * p.qrow + (int64_t)kb0 * 128, p.qseg,
+                                 full0 + 8 * slot, pol);
+                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow + (int64_t)kb0 * 16, p.hseg,
+                                 full0 + 8 * slot, pol);
                     }
                 }
             }
@@ -510,11 +563,11 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // the activation rows into shared memory: column n = 4 p + m
     {
-        const int64_t chunks = p.in / 16;  // 16-byte chunks per row
+        const int64_t chunks = (int64_t)p.nsb * 16;  // 16-byte chunks of the K-range
         for (int64_t i = ct; i < (int64_t)3 * M * chunks; i += 32 * kI8Cons) {
             const int64_t r = i / chunks, c = i % chunks;  // r = 3 m + p: the XQ2 row order
             const int m = (int)(r / 3), pl = (int)(r % 3);
-            const uint4 v = *reinterpret_cast<const uint4*>(p.xq.planes + r * p.in + 16 * c);
+            const uint4 v = *reinterpret_cast<const uint4*>(p.xq.planes + r * p.in + (int64_t)kb0 * 256 + 16 * c);
             *reinterpret_cast<uint4*>(bsm + (size_t)(4 * pl + m) * p.bstride + 16 * c) = v;
         }
     }
@@ -531,18 +584,18 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
     const float pwa = (na0 >> 2) == 0 ? 65536.0f : 256.0f;
     const bool ca0 = (na0 & 3) < M, ca1 = ((na0 + 1) & 3) < M;
     const bool cb0 = (nb0 >> 2) < 3 && (nb0 & 3) < M, cb1 = ((nb0 + 1) >> 2) < 3 && ((nb0 + 1) & 3) < M;
-    const float* sxa0 = p.xq.sx + (int64_t)(ca0 ? (na0 & 3) : 0) * p.nsb;
-    const float* sxa1 = p.xq.sx + (int64_t)(ca1 ? ((na0 + 1) & 3) : 0) * p.nsb;
-    const float* sxb0 = p.xq.sx + (int64_t)(cb0 ? (nb0 & 3) : 0) * p.nsb;
-    const float* sxb1 = p.xq.sx + (int64_t)(cb1 ? ((nb0 + 1) & 3) : 0) * p.nsb;
+    const float* sxa0 = p.xq.sx + (int64_t)(ca0 ? (na0 & 3) : 0) * p.nsbr + kb0;
+    const float* sxa1 = p.xq.sx + (int64_t)(ca1 ? ((na0 + 1) & 3) : 0) * p.nsbr + kb0;
+    const float* sxb0 = p.xq.sx + (int64_t)(cb0 ? (nb0 & 3) : 0) * p.nsbr + kb0;
+    const float* sxb1 = p.xq.sx + (int64_t)(cb1 ? ((nb0 + 1) & 3) : 0) * p.nsbr + kb0;
     const bool tvalid = t < M;
-    const float* bsum_t = p.xq.bsum + (int64_t)(tvalid ? t : 0) * (p.in / 32);
+    const float* bsum_t = p.xq.bsum + (int64_t)(tvalid ? t : 0) * (p.in / 32) + (int64_t)kb0 * 8;
     int slot = 0, use = 0, par = 0;
     for (int j = 0; j < p.njobs; j++) {
         const I8Job& jb = p.jobs[j];
         int64_t rb;
         int nrows;
-        i8_rows(jb, &rb, &nrows);
+        i8_rows(jb, rgi, nrg, &rb, &nrows);
         for (int r0 = 0; r0 < nrows; r0 += p.RS, slot = slot + 1 == p.nstage ? 0 : slot + 1, use += slot == 0,
                  par ^= 1) {
             if (!*(volatile int*)&s_abort && !mbar_wait(full0 + 8 * slot, use & 1)) {
@@ -665,18 +718,37 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                 float acc = 0.0f;
                 for (int s = 0; s < kI8Cons; s++) acc += buf[(r * kI8Cons + s) * 4 + m];
                 const int64_t o = (int64_t)m * jb.out + rb + r0 + r;
-                jb.y[o] = jb.add ? acc + jb.add[o] : acc;
+                if (p.ks > 1)
+                    p.part[(int64_t)ksi * M * jb.out + o] = acc;
+                else
+                    jb.y[o] = jb.add ? acc + jb.add[o] : acc;
             }
         }
+    }
+    if (p.ks > 1) {
+        __shared__ int s_last;
+        i8_ksplit_finish(p, rgi, nrg, ct, 32 * kI8Cons, 1, &s_last);
     }
 }
 
 }  // namespace
 
+// K-splits for a row of nsb super-blocks: 1 when each of the 8 K-slice warps
+// gets at most 4 super-blocks, else 4 (each CTA of a row group a quarter)
+static int i8_ksplits(int64_t nsb) { return nsb <= (int64_t)kI8Cons * kI8MaxSB ? 1 : 4; }
+
 bool mm_i8_supported(const rq_weight* w, int64_t M) {
-    if (w->type != RQ_Q4_K || M < 2 || M > 4) return false;
+    if (w->type != RQ_Q4_K || M < 2 || M > 4 || w->in % 256) return false;
     const int64_t nsb = w->in / 256;
-    return w->in % 256 == 0 && nsb % kI8Cons == 0 && nsb / kI8Cons <= kI8MaxSB;
+    const int ks = i8_ksplits(nsb);
+    if (nsb % ks) return false;
+    const int64_t per = nsb / ks;
+    // whole K-slices per warp when not split; split ranges up to 4 per warp
+    return ks == 1 ? (per % kI8Cons == 0 && per / kI8Cons <= kI8MaxSB) : per <= (int64_t)kI8Cons * kI8MaxSB;
+}
+
+size_t mm_i8_scratch_floats(const rq_weight* w, int64_t M) {
+    return i8_ksplits(w->in / 256) > 1 ? (size_t)4 * (size_t)M * (size_t)w->out : 0;
 }
 
 int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st, const float* rms_w,
@@ -695,7 +767,7 @@ int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t 
 }
 
 int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_t M, XQ2 xq, int sm_count,
-                 cudaStream_t st, int* err, const float* const* adds) {
+                 cudaStream_t st, int* err, const float* const* adds, float* part, int* cnt) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "int8 matmul: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     for (int j = 0; j < njobs; j++)
@@ -706,11 +778,19 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     p.njobs = njobs;
     p.M = (int)M;
     p.in = w0->in;
-    p.nsb = (int)(w0->in / 256);
+    p.nsbr = (int)(w0->in / 256);
+    p.ks = i8_ksplits(p.nsbr);
+    if (p.ks > 1 && (njobs != 1 || !part || !cnt))
+        return set_error(RQ_ERR_INVALID, "int8 matmul: a split K needs one job and scratch");
+    p.nsb = p.nsbr / p.ks;
+    p.part = part;
+    p.cnt = cnt;
     p.qrow = (uint32_t)(w0->nblk * 128);
     p.hrow = (uint32_t)(w0->nblk * 16);
-    p.qstride = p.qrow + kI8QPad;
-    p.hstride = p.hrow + kI8HPad;
+    p.qseg = (uint32_t)(p.nsb * 128);
+    p.hseg = (uint32_t)(p.nsb * 16);
+    p.qstride = p.qseg + kI8QPad;
+    p.hstride = p.hseg + kI8HPad;
     const uint32_t rowb = p.qstride + p.hstride;
     p.xq = xq;
     p.err = err;
@@ -719,14 +799,17 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
         p.jobs[j] = I8Job{ws[j]->qs, ws[j]->hdr, ys[j], adds ? adds[j] : nullptr, ws[j]->out};
         max_out = std::max(max_out, ws[j]->out);
     }
-    const int grid = (int)std::min<int64_t>(max_out, sm_count);
+    // row groups x K-splits CTAs (a multiple of ks)
+    const int nrg = (int)std::min<int64_t>(max_out, sm_count / p.ks);
+    const int grid = nrg * p.ks;
+    if (p.ks > 1 && nrg > kI8MaxRowGroups) return set_error(RQ_ERR_UNSUPPORTED, "int8 matmul: %d row groups", nrg);
     int64_t rows_cap = 0;
-    for (int j = 0; j < njobs; j++) rows_cap += (ws[j]->out + grid - 1) / grid;
+    for (int j = 0; j < njobs; j++) rows_cap += (ws[j]->out + nrg - 1) / nrg;
     const bool x4 = M > 2;  // three or four tokens: activations in shared memory, per-stage sums
     if (x4) {
         p.pr_off = kI8Bar;
         p.b_off = (uint32_t)((p.pr_off + 2 * kI8Rows * kI8Cons * 4 * 4 + 127) & ~127u);
-        p.bstride = (uint32_t)(w0->in + 32);
+        p.bstride = (uint32_t)(p.nsb * 256 + 32);
         p.ring_off = (uint32_t)((p.b_off + 12 * (int64_t)p.bstride + 127) & ~(int64_t)127);
     } else {
         const int64_t red_bytes = rows_cap * kI8Cons * M * 4;

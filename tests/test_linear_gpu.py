@@ -95,13 +95,15 @@ def test_small_m_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
 @pytest.mark.parametrize("out,n_in,M", [(1, 2048, 2), (17, 4096, 2), (333, 8192, 2), (1040, 6144, 2),
                                          (4096, 8192, 2), (150, 8192, 2), (8192, 8192, 2), (24, 8192, 3),
                                          (1040, 4096, 3), (28672, 8192, 3), (17, 2048, 4), (333, 8192, 4),
-                                         (8192, 6144, 4)])
+                                         (8192, 6144, 4), (8192, 28672, 2), (333, 28672, 3), (17, 28672, 4),
+                                         (1040, 10240, 2)])
 def test_int8_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
-    """Q4_K M = 2..4 with in = 2048..8192 runs on the int8 tensor-core kernel
+    """Q4_K M = 2..4 runs on the int8 tensor-core kernel
     (24-bit staged activations, one weight pass): single rows, ragged
     16-row stages, fewer rows than SMs, every K-slice width; M = 3, 4 on
-    its twelve-column form (activations in shared memory); each row of y
-    within 1e-4 of the f64-accumulated oracle."""
+    its twelve-column form (activations in shared memory); in > 8192 with K
+    split over four CTAs per row group; each row of y within 1e-4 of the
+    f64-accumulated oracle."""
     from rustyllm_b200 import QWeight
     from rustyllm_b200.linear import _linear
     _, blocks = make_weight(oracle, 12, out, n_in, seed=out * 7 + M)
