@@ -267,9 +267,10 @@ struct XQ2 {
 };
 size_t xq2_bytes(int64_t M, int64_t in);
 XQ2 xq2_at(void* base, int64_t M, int64_t in);
-// stages x (M rows) or, with rms_w, RMSNorm(x) * rms_w (eps) into q
+// stages x (M rows), with rms_w RMSNorm(x) * rms_w (eps), or with up
+// silu(x) * up into q
 int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st, const float* rms_w = nullptr,
-                     float eps = 0.0f);
+                     float eps = 0.0f, const float* up = nullptr);
 // whether weight w takes the int8 kernel for M rows (Q4_K, M = 2..4,
 // in = 2048 .. 8192 in steps of 2048, or a multiple of 1024 up to 32768 with
 // K split over four CTAs per row group)

@@ -68,6 +68,8 @@ struct rq_llama {
     rq::XQ xqd;     // one row of the local intermediate: the down projection's input at decode
     int* swcnt;     // [I / 32] arrival counters of the decode SwiGLU staging (zero between launches)
     rq::PipeNext nx{};  // L2 prefetch hint for the decode matvec being launched (nx.n = 0: none)
+    float* i8part;      // [4][3][hidden] split-K partial rows of the int8 down projection (T = 2, 3)
+    int* i8cnt;         // [256] its arrival counters (zero between launches)
     rq::XH xh;      // the same rows staged as f16 hi / lo (tensor-core prefill)
     // device state
     unsigned long long* best;  // packed (value, -index) of the argmax
@@ -729,6 +731,15 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
         if (tc) {
             rc = launch_xh_stage_swiglu(m->g, m->u, T, I, m->xh, st);
             if (!rc) rc = row_parallel_mm(m, L.w[6], T, st);
+        } else if (i8_ok(&L.w[6], 1, T)) {
+            // down on the int8 kernel (K split over four CTAs per row group)
+            const XQ2 q2 = i8_stage(m, T, I);
+            rc = launch_xq2_stage(m->g, T, I, q2, st, nullptr, 0.0f, m->u);
+            float* y1[1] = {m->W == 1 ? m->x : m->part};
+            const float* a1[1] = {m->R == 0 ? m->x : nullptr};
+            if (!rc)
+                rc = launch_mm_i8(&L.w[6], y1, 1, T, q2, m->ctx->sm_count, st, m->derr, a1, m->i8part, m->i8cnt);
+            if (!rc && m->W > 1) rc = tp_allreduce(m->ctx, m->part, m->x, T * H, 0, 0, st);
         } else {
             rc = launch_xquant_swiglu(m->g, m->u, T, I, m->xq, st);
             if (!rc) rc = row_parallel(m, L.w[6], T, st);
@@ -981,6 +992,9 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     uint8_t* xqdbuf = nullptr;
     if (!rc) rc = dalloc(m, &xqbuf, xq_bytes(T, maxin));
     if (!rc) rc = dalloc(m, &xqdbuf, xq_bytes(1, I));
+    if (!rc) rc = dalloc(m, &m->i8part, (size_t)(4 * 3 * H));
+    if (!rc) rc = dalloc(m, &m->i8cnt, 256);
+    if (!rc) rc = cuda_error(cudaMemset(m->i8cnt, 0, 256 * sizeof(int)), "counter reset");
     if (!rc) rc = dalloc(m, &m->swcnt, (size_t)(I / 32 + 1));
     if (!rc) rc = cuda_error(cudaMemset(m->swcnt, 0, sizeof(int) * (size_t)(I / 32 + 1)), "counter reset");
     if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "counter reset");

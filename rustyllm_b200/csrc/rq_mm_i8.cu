@@ -73,11 +73,12 @@ namespace {
 // X = rint(v * 127*65536 / amax) over the super-block, as three balanced
 // bytes X = 65536 x1 + 256 x2 + x3 (stage_block's digits, one scale per 256
 // elements instead of per 32), v = x or, with rms_w, the RMSNorm of x
-// (xquant_rmsnorm_kernel's formula and sum of squares); the f32 block sums
+// (xquant_rmsnorm_kernel's formula and sum of squares), or with up,
+// silu(x) * up (x the gate rows); the f32 block sums
 // of v are summed over the four lanes of a 32-element block.  Grid
 // (ceil(nsb / 8), M), 256 threads: eight super-blocks of one token per CTA.
 __global__ void xq2_stage_kernel(const float* __restrict__ x, int64_t in, XQ2 q, const float* __restrict__ rms_w,
-                                 float eps) {
+                                 float eps, const float* __restrict__ up) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     __shared__ float wsum[8];
@@ -119,6 +120,11 @@ __global__ void xq2_stage_kernel(const float* __restrict__ x, int64_t in, XQ2 q,
     if (rms_w) {
 #pragma unroll
         for (int k = 0; k < 8; k++) v[k] = v[k] / mden * rms_w[sb * 256 + 8 * lane + k];
+    }
+    if (up) {  // SwiGLU: x is the gate row, v = silu(gate) * up (xquant_swiglu_kernel's formula)
+        const float* u = up + m * in + sb * 256 + 8 * lane;
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = v[k] / (1.0f + expf(-v[k])) * u[k];
     }
     float amax = 0.0f, s = 0.0f;
 #pragma unroll
@@ -752,7 +758,7 @@ size_t mm_i8_scratch_floats(const rq_weight* w, int64_t M) {
 }
 
 int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t st, const float* rms_w,
-                     float eps) {
+                     float eps, const float* up) {
     if (M == 0 || in < 256) return RQ_OK;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((in / 256 + 7) / 8), (unsigned)M);
@@ -763,7 +769,7 @@ int launch_xq2_stage(const float* x, int64_t M, int64_t in, XQ2 q, cudaStream_t 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_error(cudaLaunchKernelEx(&cfg, xq2_stage_kernel, x, in, q, rms_w, eps), "xq2 staging kernel");
+    return cuda_error(cudaLaunchKernelEx(&cfg, xq2_stage_kernel, x, in, q, rms_w, eps, up), "xq2 staging kernel");
 }
 
 int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_t M, XQ2 xq, int sm_count,
