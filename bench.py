@@ -443,6 +443,7 @@ def other_formats(L, ctx, stream, timed, capture, dev, g, pk, with_cpu: bool) ->
     if with_cpu:
         res["q4_0_cpu_baseline"] = cpu_q4_0(host0["q4_0"])
     fmt(Q3_K, "q3_k", Q3K_BYTES)
+    res["q3_k_small_m"] = q3k_small_m(L, ctx, stream, timed, capture, dev, g, pk)
     # the other formats of the reference's quantizer (src/quantize.rs:29-37)
     fmt(8, "q8_0", lambda i, o: o * (i // 32) * 34)
     fmt(14, "q6_k", lambda i, o: o * (i // 256) * 210)
@@ -454,6 +455,57 @@ def other_formats(L, ctx, stream, timed, capture, dev, g, pk, with_cpu: bool) ->
 
 
 SMALL_M = (2, 3, 4, 8, 16, 24, 128, 512)
+Q3K_SMALL_M = (2, 8, 16, 128)
+
+
+def q3k_small_m(L, ctx, stream, timed, capture, dev, g, pk) -> dict:
+    """Q3_K matmul at the seven 70B layer shapes for a few M: one rq_linear
+    call per linear, graph-replayed over 4 rotating layer copies (1.5 GB).
+    M < 6 runs one M=1 pipeline pass per row, M >= 6 the tcgen05 kernel in
+    one weight pass.  GB/s counts the GGML weight bytes once."""
+    import torch
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200._lib import check
+    layers = []
+    for _ in range(N_COPIES):
+        row = []
+        for _, i, o in SHAPES:
+            wf = torch.randn(o, i, device=dev, generator=g) * 0.02
+            row.append(QWeight.quantize(ctx, Q3_K, wf))
+            del wf
+        layers.append(row)
+    nbytes_w = sum(Q3K_BYTES(i, o) for _, i, o in SHAPES)
+    res = {}
+    for M in Q3K_SMALL_M:
+        xs = [torch.randn(M, i, device=dev, generator=g) for _, i, _ in SHAPES]
+        ys = [torch.empty(M, o, device=dev) for _, _, o in SHAPES]
+
+        def layer(c, st, xs=xs, ys=ys, M=M):
+            for k in range(len(SHAPES)):
+                check(L.rq_linear(ctx.handle, layers[c][k].handle, xs[k].data_ptr(), ys[k].data_ptr(), M, st))
+
+        with torch.cuda.stream(stream):
+            for c in range(N_COPIES):
+                layer(c, stream.cuda_stream)
+        stream.synchronize()
+        gr = capture(lambda st: [layer(c, st) for c in range(N_COPIES)])
+        with torch.cuda.stream(stream):
+            gr.replay()
+        reps = 10
+        ms = timed(lambda r: gr.replay(), reps) / (reps * N_COPIES)
+        flops = 2 * M * sum(i * o for _, i, o in SHAPES)
+        kern = ("xh_stage + mm_tc_kernel<Q3_K> (tcgen05, one weight pass)" if M >= 6 else
+                "xquant + mv_pipe_kernel<Q3_K>, one pass per row")
+        res[str(M)] = {"ms_per_layer": round(ms, 4),
+                       "gbs": round((nbytes_w + 4 * M * sum(i + o for _, i, o in SHAPES)) / (ms / 1e3) / 1e9, 1),
+                       "tflops": round(flops / (ms / 1e3) / 1e12, 1), "kernel": kern}
+        del gr
+    for row in layers:
+        for w in row:
+            w.free()
+    res["note"] = ("7 rq_linear calls per 70B layer (Q3_K weights), 4 rotating layer copies; "
+                   "ms per layer")
+    return res
 
 
 def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g, pk, host_blocks) -> dict:
@@ -486,7 +538,9 @@ def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g, pk, host_bloc
         ms = timed(lambda r: gr.replay(), reps) / (reps * N_COPIES)
         nbytes = sum(Q4K_BYTES(i, o) + 4 * M * (i + o) for _, i, o in SHAPES)
         flops = 2 * M * sum(i * o for _, i, o in SHAPES)
-        kern = ("xquant + mv_pipe_kernel, one pass per row" if M <= 3 else
+        kern = ("xq2_stage + mm_i8_kernel (int8 mma.sync, one weight pass; down_proj K split 4 ways)" if M == 2 else
+                "xq2_stage + mm_i8x4_kernel (int8 mma.sync, one weight pass; down_proj K split 4 ways)"
+                if M <= 4 else
                 "xh_stage + mm_q4k_kernel (mma.sync)" if M <= 8 else
                 "xh_stage + mm_skinny_kernel (split-K tcgen05)" if M <= 16 else
                 "xh_stage + mm_q4k_kernel (mma.sync)" if M < 24 else "xh_stage + mm_tc_kernel (tcgen05)")
@@ -497,8 +551,8 @@ def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g, pk, host_bloc
                          roofline_tensor(flops, ms, pk, kern + ", 7 linears of a layer"))
         res[str(M)] = r
         del gr
-    res["note"] = ("7 rq_linear calls per layer, 4 rotating layer copies. M <= 3: activation staging + "
-                   "one M=1 pipeline pass per row; M = 4..8, 17..23: f16 hi/lo staging + the mma.sync "
+    res["note"] = ("7 rq_linear calls per layer, 4 rotating layer copies. M = 2..4: 24-bit int8-plane "
+                   "staging + the int8 mma.sync kernel, weights read once; M = 5..8, 17..23: f16 hi/lo staging + the mma.sync "
                    "tensor-core kernel, weights read once per 8-row tile; M = 9..16: split-K tcgen05; "
                    "M >= 24: the tiled tcgen05 kernel (exact sc*q weights in TMEM)")
     if host_blocks is not None:
@@ -1054,7 +1108,7 @@ def fused_allreduce_default(world: int) -> bool:
     return os.environ.get("RQ_TP_FUSED") != "0" and world >= 2
 
 
-CASES = ("pipe_gate_up", "i8_gate_m2", "i8_gate_m4", "mm_gate_m8", "sk_gate_m16", "tc_gate_m128", "q3k_gate", "moe_t1", "moe_t16",
+CASES = ("pipe_gate_up", "i8_gate_m2", "i8_gate_m4", "mm_gate_m8", "sk_gate_m16", "tc_gate_m128", "q3k_gate", "tc_q3k_gate_m128", "moe_t1", "moe_t16",
          "attn_decode")
 
 
@@ -1065,7 +1119,8 @@ def run_case(name: str) -> None:
     M=2 / 4, the int8 tensor-core kernel), 'mm_gate_m8' (gate_proj at M=8,
     mma.sync),
     'sk_gate_m16' (M=16, split-K tcgen05), 'tc_gate_m128' (M=128, tiled
-    tcgen05), 'q3k_gate' (the Q3_K gate_proj matvec), 'moe_t1' / 'moe_t16'
+    tcgen05), 'q3k_gate' (the Q3_K gate_proj matvec), 'tc_q3k_gate_m128'
+    (Q3_K gate_proj at M=128 on tcgen05), 'moe_t1' / 'moe_t16'
     (the Mixtral layer at T = 1 / 16), 'attn_decode' (a 4-layer 70B-shape
     model's decode steps: attention at head_dim 128).  Prints the per-call
     time measured without the profiler."""
@@ -1101,7 +1156,7 @@ def run_case(name: str) -> None:
             model.decode_step(s)
         nbytes = 0
     else:
-        qt = Q3_K if name == "q3k_gate" else Q4_K
+        qt = Q3_K if name in ("q3k_gate", "tc_q3k_gate_m128") else Q4_K
         ws = [QWeight.quantize(ctx, qt, torch.randn(28672, 8192, device="cuda", generator=g) * 0.02)
               for _ in range(2)]
         arr = lambda v: (ctypes.c_void_p * len(v))(*v)  # noqa: E731
@@ -1134,7 +1189,7 @@ def run_case(name: str) -> None:
     out = {"case": name, "us_per_call": round(ms * 1e3, 2)}
     if nbytes:
         out["weight_gbs"] = round(nbytes / (ms / 1e3) / 1e9, 1)
-    if name in ("tc_gate_m128", "sk_gate_m16"):
+    if name in ("tc_gate_m128", "tc_q3k_gate_m128", "sk_gate_m16"):
         M = 16 if name == "sk_gate_m16" else 128
         out["tflops"] = round(2 * M * 8192 * 28672 / (ms / 1e3) / 1e12, 1)
     print(json.dumps(out), flush=True)

@@ -200,7 +200,7 @@ int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles) {
 // kernel choice at M rows.
 size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
     if (mm_i8_supported(w, M)) return xq2_bytes(M, w->in) + 256 + mm_i8_scratch_floats(w, M) * sizeof(float);
-    const bool small_m = M >= kMinTensorM && mm_small_supported(w);
+    const bool small_m = (M >= kMinTensorM && mm_small_supported(w)) || q3k_tensor_m(w, M);
     return small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
 }
 
@@ -210,10 +210,18 @@ size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
 // the split-K tcgen05 kernel, one pass over the weights; M = 4..8 and
 // 17..23: one mma.sync pass per 8 rows; M = 2..4 (Q4_K, in <= 8192): the
 // int8 tensor-core kernel, one pass; the other M = 2, 3 shapes: the M=1
-// pipeline once per row is faster (it streams at ~5 TB/s).
+// pipeline once per row is faster (it streams at ~5 TB/s).  Q3_K from
+// M = kQ3TensorMinM: the tcgen05 kernel, one pass (below, a pass per row).
 int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, int64_t M, cudaStream_t st) {
     uint8_t* ws = (uint8_t*)ctx->ws;
     int rc;
+    if (q3k_tensor_m(w, M)) {
+        const XH xh = xh_at(ws, M, w->in);
+        rc = launch_xh_stage(xd, M, w->in, xh, st);
+        const MMJobDesc job{w, 0, (int)M, yd, nullptr};
+        if (!rc) rc = launch_mm_tc(&job, 1, xh, M, ctx->sm_count, st, ctx->derr);
+        return rc;
+    }
     if (mm_i8_supported(w, M)) {  // M = 2..4: one pass on the int8 tensor cores
         const XQ2 q = xq2_at(ws, M, w->in);
         float* part = (float*)(ws + ((xq2_bytes(M, w->in) + 255) & ~(size_t)255));

@@ -561,7 +561,15 @@ int run_mm(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float* con
            cudaStream_t st) {
     const int sm = m->ctx->sm_count;
     std::vector<MMJobDesc> jobs;
-    if (T >= kMinTcgenM) {
+    for (int i = 1; i < n; i++)
+        if (ws[i]->type != ws[0]->type) {  // one launch per weight type
+            for (int k = 0; k < n; k++) {
+                int rc = run_mm(m, 1, &ws[k], T, &ys[k], adds ? &adds[k] : nullptr, st);
+                if (rc) return rc;
+            }
+            return RQ_OK;
+        }
+    if (T >= kMinTcgenM || ws[0]->type == RQ_Q3_K) {  // Q3_K: tensor_prefill checked q3k_tensor_m
         for (int i = 0; i < n; i++) jobs.push_back(MMJobDesc{ws[i], 0, (int)T, ys[i], adds ? adds[i] : nullptr});
         return launch_mm_tc(jobs.data(), (int)jobs.size(), m->xh, T, sm, st, m->derr);
     }
@@ -595,12 +603,15 @@ int row_parallel_mm(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st)
     return rc;
 }
 
-// Prompt chunks of T >= kMinTensorM tokens with Q4_K weights run every
-// linear on the tensor cores, one pass over the weights per chunk.
+// Prompt chunks of T >= kMinTensorM tokens with Q4_K weights (Q3_K from
+// kQ3TensorMinM tokens, on the tcgen05 kernel) run every linear on the
+// tensor cores, one pass over the weights per chunk.
 bool tensor_prefill(const rq_llama* m, int64_t T, int64_t l) {
     if (T < kMinTensorM || !m->xh.v) return false;
-    for (int i = 0; i < 7; i++)
-        if (!mm_small_supported(m->layers[(size_t)l].w[i])) return false;
+    for (int i = 0; i < 7; i++) {
+        const rq_weight* w = m->layers[(size_t)l].w[i];
+        if (!mm_small_supported(w) && !q3k_tensor_m(w, T)) return false;
+    }
     return true;
 }
 

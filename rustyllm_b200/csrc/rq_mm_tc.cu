@@ -1,4 +1,4 @@
-// rq_mm_tc.cu -- Q4_K matmul for M >= 16 activation rows on the 5th-gen
+// rq_mm_tc.cu -- Q4_K / Q3_K matmul for M >= 16 activation rows on the 5th-gen
 // tensor cores: tcgen05.mma (kind::f16, f32 accumulators in TMEM).
 //
 // y[token][row] = x[token][:] . W[row][:] over K.  A CTA tile is 128 weight
@@ -22,6 +22,15 @@
 // TMEM accumulator sees at most 16 MMAs, which keeps the tensor core's own
 // accumulation rounding small).  After the last super-block
 // y = s * total (+ residual).
+//
+// Q3_K (expanded device layout: q + 4 in 0..7 as Q4_K-ordered nibbles, 16
+// signed int8 scales s_i per super-block, one per 16 elements, and d) runs
+// the same kernel: w = d * s_i * (q - 4), and A1 = (q - 4) s_i + 128 is an
+// integer in [4, 256] -- an exact f16 subnormal made by one multiply-add per
+// pair of elements -- while A2 holds sixteen 128s, so
+//     d * (P1 - P2) = d * sum_k (q - 4) s_i x_k
+// and the epilogue takes d for both d and dmin.  Its 20-byte headers come in
+// as 32-byte boxes from the 16-byte boundary at or below them.
 //
 // Warp roles (18 warps, one CTA per SM):
 //   0      TMA producer.  Ring R, one super-block per stage: the 128 rows'
@@ -74,11 +83,16 @@ constexpr int kMaxNT = 112;   // tokens per tile; the MMA's N is 2 nt (x_hi and 
 constexpr int kMaxR = 4, kMaxC = 8, kMaxA = 4;
 constexpr int kSmemBudgetTC = 226 * 1024;
 constexpr float kSub = 16777216.0f;  // 2^24: f16 subnormal n * 2^-24 -> n
+// header box per row and super-block: Q4_K's 16 bytes; Q3_K's 20 bytes
+// (16 int8 scales, f16 d, 2 pad) read as the 32-byte box from the 16-byte
+// boundary at or below them (TMA boxes start and end on 16-byte multiples)
+template <bool Q3>
+constexpr uint32_t kHdrBox = Q3 ? 32u : 16u;
 
 struct TCJob {
     float* y;
     const float* add;
-    const uint8_t* hdr;  // [out][nblk][16]
+    const uint8_t* hdr;  // [out][nblk][16] (Q3_K: [20])
     int64_t out;
     int tok0, M;
     int nt;              // tokens per tile (MMA N, a multiple of 16)
@@ -88,7 +102,7 @@ struct TCJob {
 
 struct alignas(64) TCParams {
     CUtensorMap wq[kMaxJobs];  // quant bytes [out][nblk*128], box 128 x 128, 128-byte swizzle
-    CUtensorMap wh[kMaxJobs];  // headers [out][nblk*16], box 16 x 128
+    CUtensorMap wh[kMaxJobs];  // headers [out][nblk*16], box 16 x 128 (Q3_K: [out][nblk*20], box 32 x 128)
     CUtensorMap xhi[kMaxJobs];  // staged x, hi plane [rows][in] f16, box 64 x nt_j, 128-byte swizzle
     CUtensorMap xlo[kMaxJobs];
     CUtensorMap bs;            // block sums [rows][nblk*16] f16, box 16 x box, 32-byte swizzle
@@ -118,6 +132,8 @@ __device__ __forceinline__ Tile tile_of(const TCParams& p, int t) {
     return Tile{j, local / p.jobs[j].ttiles, local % p.jobs[j].ttiles};
 }
 
+// Q3 = false: Q4_K weights; true: Q3_K in the expanded device layout
+template <bool Q3>
 __global__ void __launch_bounds__(kThreadsTC, 1) mm_tc_kernel(const __grid_constant__ TCParams p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -175,7 +191,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mm_tc_kernel(const __grid_const
         if (lane == 0) {
             const uint64_t pol_w = p.w_once ? policy_evict_first() : policy_evict_normal();
             const uint64_t pol_x = policy_evict_last();
-            const uint32_t rtx = kRowsTC * 128 + kRowsTC * 16 + 32u * (uint32_t)box;
+            const uint32_t rtx = kRowsTC * 128 + kRowsTC * kHdrBox<Q3> + 32u * (uint32_t)box;
             Ring rr, cr;
             int ri = 0, ci = 0;
             bool ok = true;
@@ -194,7 +210,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mm_tc_kernel(const __grid_const
                     const uint32_t fb = rfull0 + 8 * rs;
                     mbar_expect_tx(fb, rtx);
                     tma_load_2d(st, &p.wq[tl.j], sb * 128, row0, fb, pol_w);
-                    tma_load_2d(st + p.r_hdr, &p.wh[tl.j], sb * 16, row0, fb, pol_w);
+                    // Q3_K: the 20 header bytes of super-block sb lie in the
+                    // 32-byte box that starts at the 16-byte boundary below them
+                    tma_load_2d(st + p.r_hdr, &p.wh[tl.j], Q3 ? (sb * 20) & ~15 : sb * 16, row0, fb, pol_w);
                     tma_load_2d(st + p.r_b2, &p.bs, sb * 16, tok, fb, pol_x);
                     for (int cq = 0; cq < 4; cq++, ci++, cr.next(p.nc)) {
                         const int cs = cr.i, cu = cr.u;
@@ -291,8 +309,24 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mm_tc_kernel(const __grid_const
                 const int rs = rr.i, ru = rr.u;
                 if (ok && !wait_err(rfull0 + 8 * rs, ru & 1, p.err)) ok = false;
                 uint8_t* rst = ringr_p + (size_t)rs * p.r_bytes;
-                const uint4 hd = *reinterpret_cast<const uint4*>(rst + p.r_hdr + r * 16);
-                if (ok && h == 0) {
+                uint4 hd;
+                if constexpr (Q3) {
+                    // the 16 int8 scales at byte 4 (sb % 4) of the row's box
+                    const uint32_t* h4 =
+                        reinterpret_cast<const uint32_t*>(rst + p.r_hdr + r * 32 + 4 * (sb & 3));
+                    hd = make_uint4(h4[0], h4[1], h4[2], h4[3]);
+                } else {
+                    hd = *reinterpret_cast<const uint4*>(rst + p.r_hdr + r * 16);
+                }
+                if (ok && h == 0 && Q3) {
+                    // A2 row r: sixteen 128s (f16 subnormal 128 * 2^-24); with
+                    // the block sums it removes the +128 bias of A1
+                    const uint4 mv = make_uint4(0x00800080u, 0x00800080u, 0x00800080u, 0x00800080u);
+                    uint8_t* a2 = rst + p.r_a2 + (r >> 3) * 256 + (r & 7) * 32;
+                    *reinterpret_cast<uint4*>(a2) = mv;
+                    *reinterpret_cast<uint4*>(a2 + 16) = mv;
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                } else if (ok && h == 0) {
                     // A2 row r: [m_0..7, m_0..7] as f16 subnormals (32-byte
                     // swizzle; both 16-byte halves are equal)
                     uint32_t m[4];
@@ -314,14 +348,32 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mm_tc_kernel(const __grid_const
                     ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-wide
                     tmem_fence_after();
                     if (ok) {
-                        const uint32_t w = q4k_scales(q4k_scale_sel(cq), hd);
-                        const uint32_t sc = (w >> (8 * h)) & 0xFFu;
                         // this chunk's 32 quant bytes of row r: 16-byte chunks
                         // 2cq, 2cq+1 of the row's 128-byte-swizzled line
                         const uint8_t* qrow = rst + r * 128;
                         const uint4 qa = *reinterpret_cast<const uint4*>(qrow + (((2 * cq) ^ swz) << 4));
                         const uint4 qb = *reinterpret_cast<const uint4*>(qrow + (((2 * cq + 1) ^ swz) << 4));
                         const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                        // per 16-byte half: A = q * s + c in both 16-bit lanes.
+                        // Q4_K: s = sc_j (the half's 32-element sub-block), c = 0.
+                        // Q3_K: the halves are 16-element sub-blocks 4cq + 2h and
+                        // 4cq + 2h + 1 (q = stored q + 4 in 0..7, s the signed
+                        // scale): A = (q - 4) s + 128 = q s + (128 - 4 s) lies in
+                        // [4, 256] in each lane, so the packed 32-bit
+                        // multiply-add is exact whatever the sign of s.
+                        uint32_t sa, sb2, ca = 0u, cb = 0u;
+                        if constexpr (Q3) {
+                            const uint32_t sw = cq == 0 ? hd.x : cq == 1 ? hd.y : cq == 2 ? hd.z : hd.w;
+                            const int s0 = (int)(int8_t)(uint8_t)(sw >> (16 * h));
+                            const int s1 = (int)(int8_t)(uint8_t)(sw >> (16 * h + 8));
+                            sa = (uint32_t)s0;
+                            sb2 = (uint32_t)s1;
+                            ca = (uint32_t)(128 - 4 * s0) * 0x00010001u;
+                            cb = (uint32_t)(128 - 4 * s1) * 0x00010001u;
+                        } else {
+                            const uint32_t w = q4k_scales(q4k_scale_sel(cq), hd);
+                            sa = sb2 = (w >> (8 * h)) & 0xFFu;
+                        }
                         uint32_t o[16];
 #pragma unroll
                         for (int i = 0; i < 8; i++) {
@@ -331,8 +383,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mm_tc_kernel(const __grid_const
                                 u0 >>= 4;
                                 u1 >>= 4;
                             }
-                            o[2 * i] = (u0 & 0x000F000Fu) * sc;
-                            o[2 * i + 1] = (u1 & 0x000F000Fu) * sc;
+                            const uint32_t s = i < 4 ? sa : sb2, c = i < 4 ? ca : cb;
+                            o[2 * i] = (u0 & 0x000F000Fu) * s + c;
+                            o[2 * i + 1] = (u1 & 0x000F000Fu) * s + c;
                         }
                         // TMEM column c of the slot holds K positions 2c, 2c+1
                         tmem_st16u(lane_a + 32u * (uint32_t)as, o);
@@ -359,7 +412,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mm_tc_kernel(const __grid_const
             const TCJob& jb = p.jobs[tl.j];
             const int64_t row = (int64_t)tl.rt * kRowsTC + row_in;
             const bool live = row < jb.out;
-            const uint8_t* hrow = jb.hdr + (live ? row : 0) * (int64_t)nblk * 16;
+            // per super-block: Q4_K (d, dmin) at byte 0 of its 16 header
+            // bytes; Q3_K d at byte 16 of its 20 (the bias term scales by d)
+            constexpr int hb = Q3 ? 20 : 16, hoff = Q3 ? 16 : 0;
+            const uint8_t* hrow = jb.hdr + (live ? row : 0) * (int64_t)nblk * hb + hoff;
             const int nt0 = tl.tt * jb.nt;
             uint32_t dd = live ? __ldg(reinterpret_cast<const uint32_t*>(hrow)) : 0u;
             const int nt = jb.nt;
@@ -367,9 +423,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mm_tc_kernel(const __grid_const
                 const int b = br.i;
                 const bool first = sb == 0, last = sb == nblk - 1;
                 const uint32_t dd_next =
-                    (live && !last) ? __ldg(reinterpret_cast<const uint32_t*>(hrow + (sb + 1) * 16)) : 0u;
+                    (live && !last) ? __ldg(reinterpret_cast<const uint32_t*>(hrow + (sb + 1) * hb)) : 0u;
                 const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dd));
-                const float fd = dm.x * kSub, fm = -dm.y * kSub;
+                const float fd = dm.x * kSub, fm = -(Q3 ? dm.x : dm.y) * kSub;
                 if (ok && !wait_err(accfull0 + 8 * b, br.u & 1, p.err)) ok = false;
                 ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld / st are warp-wide
                 tmem_fence_after();
@@ -436,27 +492,35 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mm_tc_kernel(const __grid_const
 
 }  // namespace
 
-bool mm_tc_supported(const rq_weight* w) { return w->type == RQ_Q4_K; }
+// Q3_K headers are 20 bytes per super-block: the tensor map's row pitch
+// (nblk * 20 bytes) must be a multiple of 16
+bool mm_tc_supported(const rq_weight* w) {
+    return w->type == RQ_Q4_K || (w->type == RQ_Q3_K && w->nblk % 4 == 0);
+}
 
 int launch_mm_tc(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_count, cudaStream_t st, int* err) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "tensor-core matmul: %d jobs", njobs);
     const int64_t in = jobs[0].w->in, nblk = jobs[0].w->nblk;
+    const bool q3 = jobs[0].w->type == RQ_Q3_K;
     TCParams p;
     memset(&p, 0, sizeof p);
     int tiles = 0, box = 16;
     p.w_once = 1;
     for (int j = 0; j < njobs; j++) {
         const rq_weight* w = jobs[j].w;
-        if (w->type != RQ_Q4_K || w->in != in)
-            return set_error(RQ_ERR_INVALID, "tensor-core matmul: jobs need Q4_K weights with the same K");
+        if (!mm_tc_supported(w) || w->type != jobs[0].w->type || w->in != in)
+            return set_error(RQ_ERR_INVALID,
+                             "tensor-core matmul: jobs need Q4_K (or Q3_K, nblk %% 4 == 0) weights of one type "
+                             "with the same K");
         if (jobs[j].M < 1 || jobs[j].tok0 < 0 || jobs[j].tok0 + jobs[j].M > rows)
             return set_error(RQ_ERR_INVALID, "tensor-core matmul: token rows [%d, %d) of %lld", jobs[j].tok0,
                              jobs[j].tok0 + jobs[j].M, (long long)rows);
         int rc = encode(&p.wq[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, (uint64_t)(nblk * 128), (uint64_t)w->out,
                         (uint64_t)(nblk * 128), 128, kRowsTC, CU_TENSOR_MAP_SWIZZLE_128B, "quant bytes");
+        const uint64_t hrow = (uint64_t)nblk * (q3 ? 20 : 16);
         if (!rc)
-            rc = encode(&p.wh[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, w->hdr, (uint64_t)(nblk * 16), (uint64_t)w->out,
-                        (uint64_t)(nblk * 16), 16, kRowsTC, CU_TENSOR_MAP_SWIZZLE_NONE, "headers");
+            rc = encode(&p.wh[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, w->hdr, hrow, (uint64_t)w->out, hrow,
+                        q3 ? kHdrBox<true> : kHdrBox<false>, kRowsTC, CU_TENSOR_MAP_SWIZZLE_NONE, "headers");
         if (rc) return rc;
         TCJob& t = p.jobs[j];
         t.y = jobs[j].y;
@@ -520,11 +584,11 @@ int launch_mm_tc(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_c
     p.acol0 = p.tot_col + (uint32_t)box;
     p.tmem_cols = 32;
     while (p.tmem_cols < (int)p.acol0 + 32 * na) p.tmem_cols *= 2;
-    // R stage: quant 16 KB | headers 2 KB | B2 box x 32 B | A2 4 KB
+    // R stage: quant 16 KB | headers 2 KB (Q3_K 4 KB) | B2 box x 32 B | A2 4 KB
     // C stage: B1 hi, B1 lo nt x 128 B each (at most box); every tile 1024-aligned
     auto al = [](uint32_t v) { return (v + 1023u) & ~1023u; };
     p.r_hdr = kRowsTC * 128;
-    p.r_b2 = al(p.r_hdr + kRowsTC * 16);
+    p.r_b2 = al(p.r_hdr + kRowsTC * (q3 ? kHdrBox<true> : kHdrBox<false>));
     p.r_a2 = al(p.r_b2 + 32u * (uint32_t)box);
     p.r_bytes = al(p.r_a2 + kRowsTC * 32);
     p.c_bytes = al(2 * 128u * (uint32_t)box);
@@ -544,7 +608,10 @@ int launch_mm_tc(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_c
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(mm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudgetTC);
+        cudaError_t e =
+            cudaFuncSetAttribute(mm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudgetTC);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(mm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudgetTC);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(tensor-core matmul)");
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -558,7 +625,8 @@ int launch_mm_tc(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_c
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_error(cudaLaunchKernelEx(&cfg, mm_tc_kernel, p), "tensor-core matmul kernel");
+    return cuda_error(q3 ? cudaLaunchKernelEx(&cfg, mm_tc_kernel<true>, p) : cudaLaunchKernelEx(&cfg, mm_tc_kernel<false>, p),
+                      "tensor-core matmul kernel");
 }
 
 }  // namespace rq

@@ -166,6 +166,34 @@ def test_tcgen05_matmul_shapes(oracle, rq_ctx, out, n_in, M):
             assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("out,n_in,M", [(200, 1024, 6), (128, 2048, 24), (1040, 4096, 128), (333, 8192, 67),
+                                         (130, 28672, 40), (256, 8192, 300), (72, 1024, 16), (8192, 1024, 9),
+                                         (96, 768, 8)])
+def test_q3k_tcgen05_matmul_shapes(oracle, rq_ctx, out, n_in, M):
+    """Q3_K from M = 6 runs on the tcgen05 kernel in one weight pass
+    (A = (q - 4) s + 128 as exact f16 subnormals, the bias removed through
+    the block-sum MMA): 20-byte headers fetched as 32-byte boxes at every
+    offset within a 16-byte line, a partial last 128-row tile, token tiles
+    of 16..112, a long K, an all-zero and a small-scale activation row;
+    768 (three super-blocks: a header pitch that is no multiple of 16)
+    keeps a pipeline pass per row."""
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200.linear import _linear
+    _, blocks = make_weight(oracle, 11, out, n_in, seed=5 * out + M)
+    w = QWeight.upload(rq_ctx, 11, blocks, out, n_in)
+    x = np.random.default_rng(M + 11).standard_normal((M, n_in)).astype(np.float32)
+    x[M // 2] = 0.0
+    x[M - 1] *= 1e-3
+    y = _linear(w, x)
+    ref = oracle.matmul_ref(11, blocks, out, n_in, x, acc64=True)
+    assert np.isfinite(y).all()
+    assert rel_l2(y, ref) <= REL_L2_TOL
+    assert np.all(y[M // 2] == 0.0)
+    for m in range(M):
+        if m != M // 2:
+            assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
+
+
 @pytest.mark.parametrize("qtype", TYPES)
 def test_gpu_quantizer_matches_oracle_bytes(oracle, rq_ctx, qtype):
     import torch

@@ -47,6 +47,22 @@ def test_prompt_logits_and_greedy_tokens_match_oracle(oracle, rq_ctx, qtype, n_p
     assert gen == want
 
 
+@pytest.mark.parametrize("n_prompt", [7, 30])
+def test_q3k_prompt_on_tensor_cores_matches_oracle(oracle, rq_ctx, n_prompt):
+    """Q3_K layers whose every K is a multiple of 1024 run prompts of 6 or
+    more tokens on the tcgen05 kernel (one weight pass per chunk); the
+    logits and the greedy tokens still equal the oracle's."""
+    cfg = dict(CFG, hidden=1024, intermediate=2048, n_heads=8, n_kv_heads=2, head_dim=128)
+    model, ref = build(oracle, 11, seed=77 + n_prompt, cfg=cfg)
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(0, cfg["vocab"], size=n_prompt).astype(np.int32)
+    lg, nxt = model.forward(prompt, 0)
+    lr, nr = ref.forward(prompt, 0)
+    assert rel_l2(lg, lr) <= LOGIT_TOL
+    assert nxt == nr
+    assert model.generate(prompt, 8) == ref.generate(prompt, 8)
+
+
 def test_chunked_prompt_matches_one_pass(oracle, rq_ctx):
     """A prompt fed as chunks of 6 and 25 tokens (the second at position 6,
     attention over the cached keys) gives the one-pass logits and tokens."""
