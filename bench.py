@@ -455,14 +455,14 @@ def other_formats(L, ctx, stream, timed, capture, dev, g, pk, with_cpu: bool) ->
 
 
 SMALL_M = (2, 3, 4, 8, 16, 24, 128, 512)
-Q3K_SMALL_M = (2, 8, 16, 128)
+Q3K_SMALL_M = (2, 3, 4, 8, 16, 128)
 
 
 def q3k_small_m(L, ctx, stream, timed, capture, dev, g, pk) -> dict:
     """Q3_K matmul at the seven 70B layer shapes for a few M: one rq_linear
     call per linear, graph-replayed over 4 rotating layer copies (1.5 GB).
-    M < 6 runs one M=1 pipeline pass per row, M >= 6 the tcgen05 kernel in
-    one weight pass.  GB/s counts the GGML weight bytes once."""
+    M = 2..4 runs the int8 tensor-core kernels, M >= 6 the tcgen05 kernel,
+    each in one weight pass.  GB/s counts the GGML weight bytes once."""
     import torch
     from rustyllm_b200 import QWeight
     from rustyllm_b200._lib import check
@@ -495,6 +495,7 @@ def q3k_small_m(L, ctx, stream, timed, capture, dev, g, pk) -> dict:
         ms = timed(lambda r: gr.replay(), reps) / (reps * N_COPIES)
         flops = 2 * M * sum(i * o for _, i, o in SHAPES)
         kern = ("xh_stage + mm_tc_kernel<Q3_K> (tcgen05, one weight pass)" if M >= 6 else
+                "xq2_stage + mm_i8 kernels<Q3_K> (int8 mma.sync k16, one weight pass)" if M <= 4 else
                 "xquant + mv_pipe_kernel<Q3_K>, one pass per row")
         res[str(M)] = {"ms_per_layer": round(ms, 4),
                        "gbs": round((nbytes_w + 4 * M * sum(i + o for _, i, o in SHAPES)) / (ms / 1e3) / 1e9, 1),

@@ -191,6 +191,7 @@ struct I8Params {
     int ks;                     // K-splits: CTA b takes K-range b % ks of row group b / ks
     int nsbr;                   // super-blocks per full row (nsb: per K-range)
     uint32_t qseg, hseg;        // device bytes of a K-range of a row
+    uint32_t hsb;               // header bytes per super-block (Q4_K 16, Q3_K 20)
     float* part;                // ks > 1: partial y [ks][M][out]
     int* cnt;                   // ks > 1: arrivals per row group (zero between launches)
     XQ2 xq;
@@ -243,12 +244,35 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], ui
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// m16n8k16 s8 x s8 -> s32 (a Q3_K 16-element sub-block per MMA)
+__device__ __forceinline__ void mma_s8s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// Q3_K quants (q + 4 in 0..7, three bits of each nibble) -> 32 (q - 4) as
+// four signed bytes: the three bits moved to bits 5..7 of their byte, bit 7
+// flipped.  Low nibbles (lo) or high nibbles (hi) of the word.
+__device__ __forceinline__ uint32_t q3_lo(uint32_t w) { return ((w << 5) & 0xE0E0E0E0u) ^ 0x80808080u; }
+__device__ __forceinline__ uint32_t q3_hi(uint32_t w) { return ((w << 1) & 0xE0E0E0E0u) ^ 0x80808080u; }
+
+// signed byte J (compile-time) of a packed word
+template <int J>
+__device__ __forceinline__ int sbyte_of(uint32_t w) {
+    return (int)(int8_t)(uint8_t)(w >> (8 * J));
+}
+
 // byte j (compile-time) of a packed word, zero-extended
 template <int J>
 __device__ __forceinline__ int byte_of(uint32_t w) {
     return (int)__byte_perm(w, 0u, 0x4440u + J);
 }
 
+// Q3 = false: Q4_K; true: Q3_K in the expanded device layout (m16n8k16 per
+// 16-element sub-block, no min term)
+template <bool Q3>
 __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     float* red = reinterpret_cast<float*>(smem + p.red_off);
@@ -289,7 +313,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                         const int64_t row = rb + r0 + r;
                         bulk_g2s(dst + (uint32_t)r * p.qstride, jb.qs + row * p.qrow + (int64_t)kb0 * 128, p.qseg,
                                  full0 + 8 * slot, pol);
-                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow + (int64_t)kb0 * 16, p.hseg,
+                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow + (int64_t)kb0 * p.hsb, p.hseg,
                                  full0 + 8 * slot, pol);
                     }
                 }
@@ -305,24 +329,33 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
         const int sb0 = w * p.nsb / kI8Cons, nsbw = (w + 1) * p.nsb / kI8Cons - sb0;
         asm volatile("griddepcontrol.wait;" ::: "memory");
         // B fragments of the slice: column g = plane g / 2 of token g % 2
-        // (columns 6, 7 zero), elements 8t .. 8t+7 of each sub-block
+        // (columns 6, 7 zero), elements 8t .. 8t+7 of each 32-element
+        // sub-block (Q3_K: elements 4t .. 4t+3 and 16+4t .. 16+4t+3, the
+        // k16 fragments of its two 16-element sub-blocks)
         uint32_t bf[kI8MaxSB][8][2];
         float coef[kI8MaxSB][2];  // sx * plane weight of columns 2t, 2t+1: plane t, tokens 0, 1
         {
             const int bp = g >> 1, bm = g & 1;
             const bool bvalid = bp < 3 && bm < M;
-            const int8_t* bsrc = p.xq.planes + ((int64_t)bm * 3 + (bvalid ? bp : 0)) * p.in + 8 * t;
+            const int8_t* bsrc = p.xq.planes + ((int64_t)bm * 3 + (bvalid ? bp : 0)) * p.in + (Q3 ? 4 : 8) * t;
 #pragma unroll
             for (int s = 0; s < kI8MaxSB; s++)
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
                     uint2 u = make_uint2(0u, 0u);
-                    if (bvalid && s < nsbw)
-                        u = *reinterpret_cast<const uint2*>(bsrc + ((int64_t)(kb0 + sb0 + s) * 8 + j) * 32);
+                    if (bvalid && s < nsbw) {
+                        const int8_t* src = bsrc + ((int64_t)(kb0 + sb0 + s) * 8 + j) * 32;
+                        if constexpr (Q3)
+                            u = make_uint2(*reinterpret_cast<const uint32_t*>(src),
+                                           *reinterpret_cast<const uint32_t*>(src + 16));
+                        else
+                            u = *reinterpret_cast<const uint2*>(src);
+                    }
                     bf[s][j][0] = u.x;
                     bf[s][j][1] = u.y;
                 }
-            const float pw = t == 0 ? 65536.0f : t == 1 ? 256.0f : 1.0f;
+            // Q3_K: A carries 32 (q - 4), folded in here (exact)
+            const float pw = (t == 0 ? 65536.0f : t == 1 ? 256.0f : 1.0f) * (Q3 ? 0.03125f : 1.0f);
 #pragma unroll
             for (int s = 0; s < kI8MaxSB; s++)
 #pragma unroll
@@ -331,7 +364,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                         (t < 3 && c < M && s < nsbw) ? p.xq.sx[(int64_t)c * p.nsbr + kb0 + sb0 + s] * pw : 0.0f;
         }
         // block sums of this lane's token (t < M) over the slice, for the min term
-        const bool tvalid = t < M;
+        const bool tvalid = !Q3 && t < M;
         float bs[kI8MaxSB][8];
         {
             const float* bsum_t = p.xq.bsum + (int64_t)(tvalid ? t : 0) * (p.in / 32);
@@ -370,74 +403,114 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                 for (int s = 0; s < kI8MaxSB; s++) {
                     if (s < nsbw) {
                         const int sb = sb0 + s;
-                        const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
-                        const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
-                        // Q4_K 6-bit scales and mins, four per word
-                        const uint32_t scg0 = hg.y & 0x3F3F3F3Fu, mg0 = hg.z & 0x3F3F3F3Fu;
-                        const uint32_t scg1 = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
-                        const uint32_t mg1 = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
-                        const uint32_t sc80 = h8.y & 0x3F3F3F3Fu, m80 = h8.z & 0x3F3F3F3Fu;
-                        const uint32_t sc81 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
-                        const uint32_t m81 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
-                        int ai[4] = {0, 0, 0, 0};
-                        const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 8 * t;
-                        const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 8 * t;
+                        if constexpr (Q3) {
+                            // 16 int8 scales (word c: sub-blocks 4c .. 4c+3), then d
+                            const uint32_t* hg4 =
+                                reinterpret_cast<const uint32_t*>(sh + (size_t)rA * p.hstride + sb * 20);
+                            const uint32_t* h84 =
+                                reinterpret_cast<const uint32_t*>(sh + (size_t)rB * p.hstride + sb * 20);
+                            int ai[4] = {0, 0, 0, 0};
+                            const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 4 * t;
+                            const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 4 * t;
 #pragma unroll
-                        for (int c = 0; c < 4; c++) {
-                            const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
-                            const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
-                            const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
-                                                     w8.y & 0x0F0F0F0Fu};
-                            const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
-                                                     (wg.y >> 4) & 0x0F0F0F0Fu, (w8.y >> 4) & 0x0F0F0F0Fu};
-                            int d[4];
-                            // sub-block 2c
-                            mma_u8s8(d, alo, bf[s][2 * c][0], bf[s][2 * c][1]);
+                            for (int c = 0; c < 4; c++) {
+                                // bytes 4t.. of the group's two 16-byte halves: low
+                                // nibbles = sub-blocks 4c, 4c+1, high = 4c+2, 4c+3
+                                const uint32_t wg0 = *reinterpret_cast<const uint32_t*>(qg + 32 * c);
+                                const uint32_t wg1 = *reinterpret_cast<const uint32_t*>(qg + 32 * c + 16);
+                                const uint32_t w80 = *reinterpret_cast<const uint32_t*>(q8 + 32 * c);
+                                const uint32_t w81 = *reinterpret_cast<const uint32_t*>(q8 + 32 * c + 16);
+                                const uint32_t scg = hg4[c], sc8 = h84[c];
+                                int d[4];
+                                mma_s8s8_k16(d, q3_lo(wg0), q3_lo(w80), bf[s][2 * c][0]);
+                                ai[0] += d[0] * sbyte_of<0>(scg); ai[1] += d[1] * sbyte_of<0>(scg);
+                                ai[2] += d[2] * sbyte_of<0>(sc8); ai[3] += d[3] * sbyte_of<0>(sc8);
+                                mma_s8s8_k16(d, q3_lo(wg1), q3_lo(w81), bf[s][2 * c][1]);
+                                ai[0] += d[0] * sbyte_of<1>(scg); ai[1] += d[1] * sbyte_of<1>(scg);
+                                ai[2] += d[2] * sbyte_of<1>(sc8); ai[3] += d[3] * sbyte_of<1>(sc8);
+                                mma_s8s8_k16(d, q3_hi(wg0), q3_hi(w80), bf[s][2 * c + 1][0]);
+                                ai[0] += d[0] * sbyte_of<2>(scg); ai[1] += d[1] * sbyte_of<2>(scg);
+                                ai[2] += d[2] * sbyte_of<2>(sc8); ai[3] += d[3] * sbyte_of<2>(sc8);
+                                mma_s8s8_k16(d, q3_hi(wg1), q3_hi(w81), bf[s][2 * c + 1][1]);
+                                ai[0] += d[0] * sbyte_of<3>(scg); ai[1] += d[1] * sbyte_of<3>(scg);
+                                ai[2] += d[2] * sbyte_of<3>(sc8); ai[3] += d[3] * sbyte_of<3>(sc8);
+                            }
+                            const float dg = __half2float(*reinterpret_cast<const __half*>(hg4 + 4));
+                            const float d8 = __half2float(*reinterpret_cast<const __half*>(h84 + 4));
+                            acc[0] = fmaf((float)ai[0], dg * coef[s][0], acc[0]);
+                            acc[1] = fmaf((float)ai[1], dg * coef[s][1], acc[1]);
+                            acc[2] = fmaf((float)ai[2], d8 * coef[s][0], acc[2]);
+                            acc[3] = fmaf((float)ai[3], d8 * coef[s][1], acc[3]);
+                        } else {
+                            const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
+                            const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
+                            // Q4_K 6-bit scales and mins, four per word
+                            const uint32_t scg0 = hg.y & 0x3F3F3F3Fu, mg0 = hg.z & 0x3F3F3F3Fu;
+                            const uint32_t scg1 = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
+                            const uint32_t mg1 = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
+                            const uint32_t sc80 = h8.y & 0x3F3F3F3Fu, m80 = h8.z & 0x3F3F3F3Fu;
+                            const uint32_t sc81 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
+                            const uint32_t m81 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
+                            int ai[4] = {0, 0, 0, 0};
+                            const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 8 * t;
+                            const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 8 * t;
+    #pragma unroll
+                            for (int c = 0; c < 4; c++) {
+                                const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
+                                const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
+                                const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
+                                                         w8.y & 0x0F0F0F0Fu};
+                                const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
+                                                         (wg.y >> 4) & 0x0F0F0F0Fu, (w8.y >> 4) & 0x0F0F0F0Fu};
+                                int d[4];
+                                // sub-block 2c
+                                mma_u8s8(d, alo, bf[s][2 * c][0], bf[s][2 * c][1]);
+                                {
+                                    const int sg = c < 2 ? (c == 0 ? byte_of<0>(scg0) : byte_of<2>(scg0))
+                                                         : (c == 2 ? byte_of<0>(scg1) : byte_of<2>(scg1));
+                                    const int s8 = c < 2 ? (c == 0 ? byte_of<0>(sc80) : byte_of<2>(sc80))
+                                                         : (c == 2 ? byte_of<0>(sc81) : byte_of<2>(sc81));
+                                    ai[0] += d[0] * sg;
+                                    ai[1] += d[1] * sg;
+                                    ai[2] += d[2] * s8;
+                                    ai[3] += d[3] * s8;
+                                }
+                                // sub-block 2c + 1
+                                mma_u8s8(d, ahi, bf[s][2 * c + 1][0], bf[s][2 * c + 1][1]);
+                                {
+                                    const int sg = c < 2 ? (c == 0 ? byte_of<1>(scg0) : byte_of<3>(scg0))
+                                                         : (c == 2 ? byte_of<1>(scg1) : byte_of<3>(scg1));
+                                    const int s8 = c < 2 ? (c == 0 ? byte_of<1>(sc80) : byte_of<3>(sc80))
+                                                         : (c == 2 ? byte_of<1>(sc81) : byte_of<3>(sc81));
+                                    ai[0] += d[0] * sg;
+                                    ai[1] += d[1] * sg;
+                                    ai[2] += d[2] * s8;
+                                    ai[3] += d[3] * s8;
+                                }
+                            }
+                            const float2 ddg = __half22float2(*reinterpret_cast<const __half2*>(&hg.x));
+                            const float2 dd8 = __half22float2(*reinterpret_cast<const __half2*>(&h8.x));
+                            acc[0] = fmaf((float)ai[0], ddg.x * coef[s][0], acc[0]);
+                            acc[1] = fmaf((float)ai[1], ddg.x * coef[s][1], acc[1]);
+                            acc[2] = fmaf((float)ai[2], dd8.x * coef[s][0], acc[2]);
+                            acc[3] = fmaf((float)ai[3], dd8.x * coef[s][1], acc[3]);
                             {
-                                const int sg = c < 2 ? (c == 0 ? byte_of<0>(scg0) : byte_of<2>(scg0))
-                                                     : (c == 2 ? byte_of<0>(scg1) : byte_of<2>(scg1));
-                                const int s8 = c < 2 ? (c == 0 ? byte_of<0>(sc80) : byte_of<2>(sc80))
-                                                     : (c == 2 ? byte_of<0>(sc81) : byte_of<2>(sc81));
-                                ai[0] += d[0] * sg;
-                                ai[1] += d[1] * sg;
-                                ai[2] += d[2] * s8;
-                                ai[3] += d[3] * s8;
+                                // m_j as exact floats: byte j of the packed mins under
+                                // the exponent of 2^23, minus 2^23 (no conversion unit)
+                                float sg = 0.0f, s8 = 0.0f;
+    #pragma unroll
+                                for (int jj = 0; jj < 8; jj++) {
+                                    const uint32_t wg = jj < 4 ? mg0 : mg1, w8 = jj < 4 ? m80 : m81;
+                                    const float fg =
+                                        __uint_as_float(__byte_perm(wg, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                                    const float f8 =
+                                        __uint_as_float(__byte_perm(w8, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                                    sg = fmaf(fg, bs[s][jj], sg);
+                                    s8 = fmaf(f8, bs[s][jj], s8);
+                                }
+                                mn[0] = fmaf(ddg.y, sg, mn[0]);
+                                mn[1] = fmaf(dd8.y, s8, mn[1]);
                             }
-                            // sub-block 2c + 1
-                            mma_u8s8(d, ahi, bf[s][2 * c + 1][0], bf[s][2 * c + 1][1]);
-                            {
-                                const int sg = c < 2 ? (c == 0 ? byte_of<1>(scg0) : byte_of<3>(scg0))
-                                                     : (c == 2 ? byte_of<1>(scg1) : byte_of<3>(scg1));
-                                const int s8 = c < 2 ? (c == 0 ? byte_of<1>(sc80) : byte_of<3>(sc80))
-                                                     : (c == 2 ? byte_of<1>(sc81) : byte_of<3>(sc81));
-                                ai[0] += d[0] * sg;
-                                ai[1] += d[1] * sg;
-                                ai[2] += d[2] * s8;
-                                ai[3] += d[3] * s8;
-                            }
-                        }
-                        const float2 ddg = __half22float2(*reinterpret_cast<const __half2*>(&hg.x));
-                        const float2 dd8 = __half22float2(*reinterpret_cast<const __half2*>(&h8.x));
-                        acc[0] = fmaf((float)ai[0], ddg.x * coef[s][0], acc[0]);
-                        acc[1] = fmaf((float)ai[1], ddg.x * coef[s][1], acc[1]);
-                        acc[2] = fmaf((float)ai[2], dd8.x * coef[s][0], acc[2]);
-                        acc[3] = fmaf((float)ai[3], dd8.x * coef[s][1], acc[3]);
-                        {
-                            // m_j as exact floats: byte j of the packed mins under
-                            // the exponent of 2^23, minus 2^23 (no conversion unit)
-                            float sg = 0.0f, s8 = 0.0f;
-#pragma unroll
-                            for (int jj = 0; jj < 8; jj++) {
-                                const uint32_t wg = jj < 4 ? mg0 : mg1, w8 = jj < 4 ? m80 : m81;
-                                const float fg =
-                                    __uint_as_float(__byte_perm(wg, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
-                                const float f8 =
-                                    __uint_as_float(__byte_perm(w8, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
-                                sg = fmaf(fg, bs[s][jj], sg);
-                                s8 = fmaf(f8, bs[s][jj], s8);
-                            }
-                            mn[0] = fmaf(ddg.y, sg, mn[0]);
-                            mn[1] = fmaf(dd8.y, s8, mn[1]);
                         }
                     }
                 }
@@ -508,6 +581,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
 // a stage raises a shared abort flag and every warp then skips the rest of
 // the work but still passes every barrier, so no barrier waits on a warp
 // that left.
+template <bool Q3>
 __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem + p.ring_off;
@@ -551,7 +625,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                         const int64_t row = rb + r0 + r;
                         bulk_g2s(dst + (uint32_t)r * p.qstride, jb.qs + row * p.qrow + (int64_t)kb0 * 128, p.qseg,
                                  full0 + 8 * slot, pol);
-                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow + (int64_t)kb0 * 16, p.hseg,
+                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow + (int64_t)kb0 * p.hsb, p.hseg,
                                  full0 + 8 * slot, pol);
                     }
                 }
@@ -581,20 +655,24 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
     // B fragment columns of this lane and the f32 factors of its C columns
     const int n0 = g, n1 = 8 + g;
     const bool v0 = (n0 & 3) < M, v1 = (n1 >> 2) < 3 && (n1 & 3) < M;
-    const int8_t* bp0 = bsm + (size_t)(v0 ? n0 : 0) * p.bstride + 8 * t;
-    const int8_t* bp1 = bsm + (size_t)(v1 ? n1 : 0) * p.bstride + 8 * t;
+    // Q4_K: bytes 8t .. 8t+7 of a 32-element sub-block; Q3_K: bytes 4t ..
+    // 4t+3 of each 16-element half (the k16 fragments)
+    const int8_t* bp0 = bsm + (size_t)(v0 ? n0 : 0) * p.bstride + (Q3 ? 4 : 8) * t;
+    const int8_t* bp1 = bsm + (size_t)(v1 ? n1 : 0) * p.bstride + (Q3 ? 4 : 8) * t;
     // the f32 factors of this lane's C columns (sx * plane weight, zero for
     // absent tokens) and its token's block sums are read per super-block
     // (L1-resident) to keep registers for the MMA tiles
     const int na0 = 2 * t, nb0 = 8 + 2 * t;  // first C column of the two groups
-    const float pwa = (na0 >> 2) == 0 ? 65536.0f : 256.0f;
+    // plane weights; Q3_K's A carries 32 (q - 4): 1/32 folded in (exact)
+    const float pwa = ((na0 >> 2) == 0 ? 65536.0f : 256.0f) * (Q3 ? 0.03125f : 1.0f);
+    const float pwb = Q3 ? 0.03125f : 1.0f;
     const bool ca0 = (na0 & 3) < M, ca1 = ((na0 + 1) & 3) < M;
     const bool cb0 = (nb0 >> 2) < 3 && (nb0 & 3) < M, cb1 = ((nb0 + 1) >> 2) < 3 && ((nb0 + 1) & 3) < M;
     const float* sxa0 = p.xq.sx + (int64_t)(ca0 ? (na0 & 3) : 0) * p.nsbr + kb0;
     const float* sxa1 = p.xq.sx + (int64_t)(ca1 ? ((na0 + 1) & 3) : 0) * p.nsbr + kb0;
     const float* sxb0 = p.xq.sx + (int64_t)(cb0 ? (nb0 & 3) : 0) * p.nsbr + kb0;
     const float* sxb1 = p.xq.sx + (int64_t)(cb1 ? ((nb0 + 1) & 3) : 0) * p.nsbr + kb0;
-    const bool tvalid = t < M;
+    const bool tvalid = !Q3 && t < M;
     const float* bsum_t = p.xq.bsum + (int64_t)(tvalid ? t : 0) * (p.in / 32) + (int64_t)kb0 * 8;
     int slot = 0, use = 0, par = 0;
     for (int j = 0; j < p.njobs; j++) {
@@ -620,78 +698,125 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                 if (live && s < nsbw) {
                     const int sb = sb0 + s;
                     const float cf0 = ca0 ? __ldg(sxa0 + sb) * pwa : 0.0f, cf1 = ca1 ? __ldg(sxa1 + sb) * pwa : 0.0f;
-                    const float cg0 = cb0 ? __ldg(sxb0 + sb) : 0.0f, cg1 = cb1 ? __ldg(sxb1 + sb) : 0.0f;
-                    float4 bsa = make_float4(0.0f, 0.0f, 0.0f, 0.0f), bsb = bsa;
-                    if (tvalid) {
-                        bsa = __ldg(reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8));
-                        bsb = __ldg(reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8 + 4));
-                    }
-                    const float bsv[8] = {bsa.x, bsa.y, bsa.z, bsa.w, bsb.x, bsb.y, bsb.z, bsb.w};
-                    const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
-                    const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
-                    const uint32_t scg0 = hg.y & 0x3F3F3F3Fu, mg0 = hg.z & 0x3F3F3F3Fu;
-                    const uint32_t scg1 = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
-                    const uint32_t mg1 = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
-                    const uint32_t sc80 = h8.y & 0x3F3F3F3Fu, m80 = h8.z & 0x3F3F3F3Fu;
-                    const uint32_t sc81 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
-                    const uint32_t m81 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
-                    int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
-                    const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 8 * t;
-                    const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 8 * t;
+                    const float cg0 = cb0 ? __ldg(sxb0 + sb) * pwb : 0.0f, cg1 = cb1 ? __ldg(sxb1 + sb) * pwb : 0.0f;
+                    if constexpr (Q3) {
+                        const uint32_t* hg4 =
+                            reinterpret_cast<const uint32_t*>(sh + (size_t)rA * p.hstride + sb * 20);
+                        const uint32_t* h84 =
+                            reinterpret_cast<const uint32_t*>(sh + (size_t)rB * p.hstride + sb * 20);
+                        int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+                        const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 4 * t;
+                        const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 4 * t;
 #pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
-                        const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
-                        const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
-                                                 w8.y & 0x0F0F0F0Fu};
-                        const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
-                                                 (wg.y >> 4) & 0x0F0F0F0Fu, (w8.y >> 4) & 0x0F0F0F0Fu};
+                        for (int c = 0; c < 4; c++) {
+                            const uint32_t wq[4] = {*reinterpret_cast<const uint32_t*>(qg + 32 * c),
+                                                    *reinterpret_cast<const uint32_t*>(qg + 32 * c + 16),
+                                                    *reinterpret_cast<const uint32_t*>(q8 + 32 * c),
+                                                    *reinterpret_cast<const uint32_t*>(q8 + 32 * c + 16)};
+                            const uint32_t scg = hg4[c], sc8 = h84[c];
 #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const int sub = 2 * c + h;
-                            const int64_t ko = (int64_t)(sb * 8 + sub) * 32;
-                            uint2 b0 = make_uint2(0u, 0u), b1 = make_uint2(0u, 0u);
-                            if (v0) b0 = *reinterpret_cast<const uint2*>(bp0 + ko);
-                            if (v1) b1 = *reinterpret_cast<const uint2*>(bp1 + ko);
-                            int d0[4], d1[4];
-                            if (h == 0) {
-                                mma_u8s8(d0, alo, b0.x, b0.y);
-                                mma_u8s8(d1, alo, b1.x, b1.y);
-                            } else {
-                                mma_u8s8(d0, ahi, b0.x, b0.y);
-                                mma_u8s8(d1, ahi, b1.x, b1.y);
+                            for (int q = 0; q < 4; q++) {
+                                // sub-block 4c + q: low (q < 2) or high nibbles of
+                                // half q & 1; its elements are half q & 1 of
+                                // 32-element chunk 2c + q / 2
+                                const uint32_t ag = q < 2 ? q3_lo(wq[q & 1]) : q3_hi(wq[q & 1]);
+                                const uint32_t a8 = q < 2 ? q3_lo(wq[2 + (q & 1)]) : q3_hi(wq[2 + (q & 1)]);
+                                const int64_t ko = (int64_t)(sb * 8 + 2 * c + (q >> 1)) * 32 + 16 * (q & 1);
+                                uint32_t b0 = 0u, b1 = 0u;
+                                if (v0) b0 = *reinterpret_cast<const uint32_t*>(bp0 + ko);
+                                if (v1) b1 = *reinterpret_cast<const uint32_t*>(bp1 + ko);
+                                int d0[4], d1[4];
+                                mma_s8s8_k16(d0, ag, a8, b0);
+                                mma_s8s8_k16(d1, ag, a8, b1);
+                                const int sg = (int)(int8_t)(uint8_t)(scg >> (8 * q));
+                                const int s8 = (int)(int8_t)(uint8_t)(sc8 >> (8 * q));
+                                a0[0] += d0[0] * sg; a0[1] += d0[1] * sg; a0[2] += d0[2] * s8; a0[3] += d0[3] * s8;
+                                a1[0] += d1[0] * sg; a1[1] += d1[1] * sg; a1[2] += d1[2] * s8; a1[3] += d1[3] * s8;
                             }
-                            const uint32_t wgs = c < 2 ? scg0 : scg1, w8s = c < 2 ? sc80 : sc81;
-                            const int byte = (2 * c + h) & 3;
-                            const int sg = (int)__byte_perm(wgs, 0u, 0x4440u + byte);
-                            const int s8 = (int)__byte_perm(w8s, 0u, 0x4440u + byte);
-                            a0[0] += d0[0] * sg; a0[1] += d0[1] * sg; a0[2] += d0[2] * s8; a0[3] += d0[3] * s8;
-                            a1[0] += d1[0] * sg; a1[1] += d1[1] * sg; a1[2] += d1[2] * s8; a1[3] += d1[3] * s8;
                         }
+                        const float dg = __half2float(*reinterpret_cast<const __half*>(hg4 + 4));
+                        const float d8 = __half2float(*reinterpret_cast<const __half*>(h84 + 4));
+                        acc0[0] = fmaf((float)a0[0], dg * cf0, acc0[0]);
+                        acc0[1] = fmaf((float)a0[1], dg * cf1, acc0[1]);
+                        acc0[2] = fmaf((float)a0[2], d8 * cf0, acc0[2]);
+                        acc0[3] = fmaf((float)a0[3], d8 * cf1, acc0[3]);
+                        acc1[0] = fmaf((float)a1[0], dg * cg0, acc1[0]);
+                        acc1[1] = fmaf((float)a1[1], dg * cg1, acc1[1]);
+                        acc1[2] = fmaf((float)a1[2], d8 * cg0, acc1[2]);
+                        acc1[3] = fmaf((float)a1[3], d8 * cg1, acc1[3]);
+                    } else {
+                        float4 bsa = make_float4(0.0f, 0.0f, 0.0f, 0.0f), bsb = bsa;
+                        if (tvalid) {
+                            bsa = __ldg(reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8));
+                            bsb = __ldg(reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8 + 4));
+                        }
+                        const float bsv[8] = {bsa.x, bsa.y, bsa.z, bsa.w, bsb.x, bsb.y, bsb.z, bsb.w};
+                        const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
+                        const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
+                        const uint32_t scg0 = hg.y & 0x3F3F3F3Fu, mg0 = hg.z & 0x3F3F3F3Fu;
+                        const uint32_t scg1 = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
+                        const uint32_t mg1 = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
+                        const uint32_t sc80 = h8.y & 0x3F3F3F3Fu, m80 = h8.z & 0x3F3F3F3Fu;
+                        const uint32_t sc81 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
+                        const uint32_t m81 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
+                        int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+                        const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 8 * t;
+                        const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 8 * t;
+    #pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
+                            const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
+                            const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
+                                                     w8.y & 0x0F0F0F0Fu};
+                            const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
+                                                     (wg.y >> 4) & 0x0F0F0F0Fu, (w8.y >> 4) & 0x0F0F0F0Fu};
+    #pragma unroll
+                            for (int h = 0; h < 2; h++) {
+                                const int sub = 2 * c + h;
+                                const int64_t ko = (int64_t)(sb * 8 + sub) * 32;
+                                uint2 b0 = make_uint2(0u, 0u), b1 = make_uint2(0u, 0u);
+                                if (v0) b0 = *reinterpret_cast<const uint2*>(bp0 + ko);
+                                if (v1) b1 = *reinterpret_cast<const uint2*>(bp1 + ko);
+                                int d0[4], d1[4];
+                                if (h == 0) {
+                                    mma_u8s8(d0, alo, b0.x, b0.y);
+                                    mma_u8s8(d1, alo, b1.x, b1.y);
+                                } else {
+                                    mma_u8s8(d0, ahi, b0.x, b0.y);
+                                    mma_u8s8(d1, ahi, b1.x, b1.y);
+                                }
+                                const uint32_t wgs = c < 2 ? scg0 : scg1, w8s = c < 2 ? sc80 : sc81;
+                                const int byte = (2 * c + h) & 3;
+                                const int sg = (int)__byte_perm(wgs, 0u, 0x4440u + byte);
+                                const int s8 = (int)__byte_perm(w8s, 0u, 0x4440u + byte);
+                                a0[0] += d0[0] * sg; a0[1] += d0[1] * sg; a0[2] += d0[2] * s8; a0[3] += d0[3] * s8;
+                                a1[0] += d1[0] * sg; a1[1] += d1[1] * sg; a1[2] += d1[2] * s8; a1[3] += d1[3] * s8;
+                            }
+                        }
+                        const float2 ddg = __half22float2(*reinterpret_cast<const __half2*>(&hg.x));
+                        const float2 dd8 = __half22float2(*reinterpret_cast<const __half2*>(&h8.x));
+                        acc0[0] = fmaf((float)a0[0], ddg.x * cf0, acc0[0]);
+                        acc0[1] = fmaf((float)a0[1], ddg.x * cf1, acc0[1]);
+                        acc0[2] = fmaf((float)a0[2], dd8.x * cf0, acc0[2]);
+                        acc0[3] = fmaf((float)a0[3], dd8.x * cf1, acc0[3]);
+                        acc1[0] = fmaf((float)a1[0], ddg.x * cg0, acc1[0]);
+                        acc1[1] = fmaf((float)a1[1], ddg.x * cg1, acc1[1]);
+                        acc1[2] = fmaf((float)a1[2], dd8.x * cg0, acc1[2]);
+                        acc1[3] = fmaf((float)a1[3], dd8.x * cg1, acc1[3]);
+                        float sgm = 0.0f, s8m = 0.0f;
+    #pragma unroll
+                        for (int jj = 0; jj < 8; jj++) {
+                            const uint32_t wg = jj < 4 ? mg0 : mg1, w8 = jj < 4 ? m80 : m81;
+                            const float fg =
+                                __uint_as_float(__byte_perm(wg, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                            const float f8 =
+                                __uint_as_float(__byte_perm(w8, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                            sgm = fmaf(fg, bsv[jj], sgm);
+                            s8m = fmaf(f8, bsv[jj], s8m);
+                        }
+                        mn[0] = fmaf(ddg.y, sgm, mn[0]);
+                        mn[1] = fmaf(dd8.y, s8m, mn[1]);
                     }
-                    const float2 ddg = __half22float2(*reinterpret_cast<const __half2*>(&hg.x));
-                    const float2 dd8 = __half22float2(*reinterpret_cast<const __half2*>(&h8.x));
-                    acc0[0] = fmaf((float)a0[0], ddg.x * cf0, acc0[0]);
-                    acc0[1] = fmaf((float)a0[1], ddg.x * cf1, acc0[1]);
-                    acc0[2] = fmaf((float)a0[2], dd8.x * cf0, acc0[2]);
-                    acc0[3] = fmaf((float)a0[3], dd8.x * cf1, acc0[3]);
-                    acc1[0] = fmaf((float)a1[0], ddg.x * cg0, acc1[0]);
-                    acc1[1] = fmaf((float)a1[1], ddg.x * cg1, acc1[1]);
-                    acc1[2] = fmaf((float)a1[2], dd8.x * cg0, acc1[2]);
-                    acc1[3] = fmaf((float)a1[3], dd8.x * cg1, acc1[3]);
-                    float sgm = 0.0f, s8m = 0.0f;
-#pragma unroll
-                    for (int jj = 0; jj < 8; jj++) {
-                        const uint32_t wg = jj < 4 ? mg0 : mg1, w8 = jj < 4 ? m80 : m81;
-                        const float fg =
-                            __uint_as_float(__byte_perm(wg, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
-                        const float f8 =
-                            __uint_as_float(__byte_perm(w8, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
-                        sgm = fmaf(fg, bsv[jj], sgm);
-                        s8m = fmaf(f8, bsv[jj], s8m);
-                    }
-                    mn[0] = fmaf(ddg.y, sgm, mn[0]);
-                    mn[1] = fmaf(dd8.y, s8m, mn[1]);
                 }
             }
             __syncwarp();
@@ -744,11 +869,14 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
 static int i8_ksplits(int64_t nsb) { return nsb <= (int64_t)kI8Cons * kI8MaxSB ? 1 : 4; }
 
 bool mm_i8_supported(const rq_weight* w, int64_t M) {
-    if (w->type != RQ_Q4_K || M < 2 || M > 4 || w->in % 256) return false;
+    if ((w->type != RQ_Q4_K && w->type != RQ_Q3_K) || M < 2 || M > 4 || w->in % 256) return false;
     const int64_t nsb = w->in / 256;
     const int ks = i8_ksplits(nsb);
     if (nsb % ks) return false;
     const int64_t per = nsb / ks;
+    // Q3_K's 20-byte headers: a K-range's header bytes are whole 16-byte
+    // units (bulk copies) when it spans a multiple of 4 super-blocks
+    if (w->type == RQ_Q3_K && per % 4) return false;
     // whole K-slices per warp when not split; split ranges up to 4 per warp
     return ks == 1 ? (per % kI8Cons == 0 && per / kI8Cons <= kI8MaxSB) : per <= (int64_t)kI8Cons * kI8MaxSB;
 }
@@ -777,7 +905,7 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "int8 matmul: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     for (int j = 0; j < njobs; j++)
-        if (!mm_i8_supported(ws[j], M) || ws[j]->in != w0->in)
+        if (!mm_i8_supported(ws[j], M) || ws[j]->in != w0->in || ws[j]->type != w0->type)
             return set_error(RQ_ERR_INVALID, "int8 matmul: unsupported weight or M = %lld", (long long)M);
     I8Params p;
     memset(&p, 0, sizeof p);
@@ -791,10 +919,11 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     p.nsb = p.nsbr / p.ks;
     p.part = part;
     p.cnt = cnt;
+    p.hsb = w0->type == RQ_Q3_K ? 20u : 16u;
     p.qrow = (uint32_t)(w0->nblk * 128);
-    p.hrow = (uint32_t)(w0->nblk * 16);
+    p.hrow = (uint32_t)(w0->nblk * p.hsb);
     p.qseg = (uint32_t)(p.nsb * 128);
-    p.hseg = (uint32_t)(p.nsb * 16);
+    p.hseg = (uint32_t)(p.nsb * p.hsb);
     p.qstride = p.qseg + kI8QPad;
     p.hstride = p.hseg + kI8HPad;
     const uint32_t rowb = p.qstride + p.hstride;
@@ -839,9 +968,11 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(mm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kI8Smem);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(mm_i8x4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kI8Smem);
+        cudaError_t e = cudaSuccess;
+        const void* kerns[4] = {(const void*)mm_i8_kernel<false>, (const void*)mm_i8_kernel<true>,
+                                (const void*)mm_i8x4_kernel<false>, (const void*)mm_i8x4_kernel<true>};
+        for (int k = 0; k < 4 && e == cudaSuccess; k++)
+            e = cudaFuncSetAttribute(kerns[k], cudaFuncAttributeMaxDynamicSharedMemorySize, kI8Smem);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(int8 matmul)");
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -855,8 +986,12 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_error(x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel, p) : cudaLaunchKernelEx(&cfg, mm_i8_kernel, p),
-                      "int8 matmul kernel");
+    cudaError_t e;
+    if (w0->type == RQ_Q3_K)
+        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<true>, p) : cudaLaunchKernelEx(&cfg, mm_i8_kernel<true>, p);
+    else
+        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<false>, p) : cudaLaunchKernelEx(&cfg, mm_i8_kernel<false>, p);
+    return cuda_error(e, "int8 matmul kernel");
 }
 
 }  // namespace rq

@@ -166,6 +166,31 @@ def test_tcgen05_matmul_shapes(oracle, rq_ctx, out, n_in, M):
             assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("out,n_in,M", [(1, 2048, 2), (17, 4096, 2), (333, 8192, 3), (1040, 6144, 4),
+                                         (8192, 8192, 2), (8192, 28672, 2), (333, 28672, 3), (17, 28672, 4),
+                                         (28672, 8192, 4), (96, 1024, 3)])
+def test_q3k_int8_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
+    """Q3_K M = 2..4 runs on the int8 tensor-core kernels: one m16n8k16
+    s8 x s8 MMA per 16-element sub-block with A = 32 (q - 4) made by a
+    shift and a logic op, the signed scales applied by integer
+    multiply-add, no min term; 20-byte headers in 16-byte-aligned K-ranges
+    (in > 8192 split four ways).  1024 (four super-blocks per row, not a
+    whole K-slice per warp) keeps a pipeline pass per row."""
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200.linear import _linear
+    _, blocks = make_weight(oracle, 11, out, n_in, seed=out * 5 + M)
+    w = QWeight.upload(rq_ctx, 11, blocks, out, n_in)
+    x = np.random.default_rng(M + out + 1).standard_normal((M, n_in)).astype(np.float32)
+    x[:, :256] *= 40.0
+    x[:, 256:512] *= 1e-3
+    y = _linear(w, x)
+    ref = oracle.matmul_ref(11, blocks, out, n_in, x, acc64=True)
+    assert np.isfinite(y).all()
+    assert rel_l2(y, ref) <= REL_L2_TOL
+    for m in range(M):
+        assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
+
+
 @pytest.mark.parametrize("out,n_in,M", [(200, 1024, 6), (128, 2048, 24), (1040, 4096, 128), (333, 8192, 67),
                                          (130, 28672, 40), (256, 8192, 300), (72, 1024, 16), (8192, 1024, 9),
                                          (96, 768, 8)])

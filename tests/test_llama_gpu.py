@@ -47,12 +47,13 @@ def test_prompt_logits_and_greedy_tokens_match_oracle(oracle, rq_ctx, qtype, n_p
     assert gen == want
 
 
-@pytest.mark.parametrize("n_prompt", [7, 30])
-def test_q3k_prompt_on_tensor_cores_matches_oracle(oracle, rq_ctx, n_prompt):
-    """Q3_K layers whose every K is a multiple of 1024 run prompts of 6 or
-    more tokens on the tcgen05 kernel (one weight pass per chunk); the
-    logits and the greedy tokens still equal the oracle's."""
-    cfg = dict(CFG, hidden=1024, intermediate=2048, n_heads=8, n_kv_heads=2, head_dim=128)
+@pytest.mark.parametrize("n_prompt", [2, 3, 7, 30])
+def test_q3k_prompt_one_weight_pass_matches_oracle(oracle, rq_ctx, n_prompt):
+    """Q3_K layers whose every K is a multiple of 2048 run two- and
+    three-token forwards (speculative verify) on the int8 tensor-core
+    kernel and prompts of 6 or more tokens on the tcgen05 kernel, one weight
+    pass each; the logits and the greedy tokens still equal the oracle's."""
+    cfg = dict(CFG, hidden=2048, intermediate=4096, n_heads=16, n_kv_heads=4, head_dim=128)
     model, ref = build(oracle, 11, seed=77 + n_prompt, cfg=cfg)
     rng = np.random.default_rng(21)
     prompt = rng.integers(0, cfg["vocab"], size=n_prompt).astype(np.int32)
