@@ -442,6 +442,7 @@ def other_formats(L, ctx, stream, timed, capture, dev, g, pk, with_cpu: bool) ->
                                         "xquant + mv_pipe_kernel<Q4_0> 4096x4096 (9.4 MB: launch-latency bound)")
     if with_cpu:
         res["q4_0_cpu_baseline"] = cpu_q4_0(host0["q4_0"])
+    res["q4_0_small_m"] = q40_small_m(L, ctx, stream, timed, capture, dev, g)
     fmt(Q3_K, "q3_k", Q3K_BYTES)
     res["q3_k_small_m"] = q3k_small_m(L, ctx, stream, timed, capture, dev, g, pk)
     # the other formats of the reference's quantizer (src/quantize.rs:29-37)
@@ -456,6 +457,47 @@ def other_formats(L, ctx, stream, timed, capture, dev, g, pk, with_cpu: bool) ->
 
 SMALL_M = (2, 3, 4, 8, 16, 24, 128, 512)
 Q3K_SMALL_M = (2, 3, 4, 8, 16, 128)
+Q40_SMALL_M = (1, 2, 3, 4, 8, 16)
+
+
+def q40_small_m(L, ctx, stream, timed, capture, dev, g) -> dict:
+    """The 4096x4096 Q4_0 linear (config 1's weight) at M rows: one
+    rq_linear call, graph-replayed over 16 rotating copies (151 MB).
+    M = 2..4 run the int8 tensor-core kernels in one weight pass, larger M
+    one int8 launch per group of 2..4 rows.  GB/s counts the weight bytes
+    once per call."""
+    import torch
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200._lib import check
+    ws = []
+    for _ in range(16):
+        wf = torch.randn(4096, 4096, device=dev, generator=g) * 0.02
+        ws.append(QWeight.quantize(ctx, Q4_0, wf))
+        del wf
+    res = {}
+    for M in Q40_SMALL_M:
+        x = torch.randn(M, 4096, device=dev, generator=g)
+        y = torch.empty(M, 4096, device=dev)
+
+        def run(st, x=x, y=y, M=M):
+            for w in ws:
+                check(L.rq_linear(ctx.handle, w.handle, x.data_ptr(), y.data_ptr(), M, st))
+        with torch.cuda.stream(stream):
+            run(stream.cuda_stream)
+        stream.synchronize()
+        gr = capture(run)
+        with torch.cuda.stream(stream):
+            gr.replay()
+        reps = 10
+        ms = timed(lambda r: gr.replay(), reps) / (reps * len(ws))
+        res[str(M)] = {"us_per_call": round(ms * 1e3, 2),
+                       "gbs": round((Q40_BYTES(4096, 4096) + 4 * M * 8192) / (ms / 1e3) / 1e9, 1)}
+        del gr
+    for w in ws:
+        w.free()
+    res["note"] = ("rq_linear on the 4096x4096 Q4_0 weight, 16 rotating copies; M=1 the pipeline, "
+                   "M = 2..4 the int8 tensor-core kernels, larger M one int8 launch per 2..4 rows")
+    return res
 
 
 def q3k_small_m(L, ctx, stream, timed, capture, dev, g, pk) -> dict:

@@ -244,6 +244,15 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], ui
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// weight formats of the int8 kernels
+constexpr int kI8Q4K = 0, kI8Q3K = 1, kI8Q40 = 2;
+
+// signed s32 -> f32 for |v| < 2^22 without the conversion unit: v placed
+// in the mantissa of 1.5 * 2^23, minus 1.5 * 2^23 (exact)
+__device__ __forceinline__ float i2f_small(int v) {
+    return __int_as_float(0x4B400000 + v) - 12582912.0f;
+}
+
 // m16n8k16 s8 x s8 -> s32 (a Q3_K 16-element sub-block per MMA)
 __device__ __forceinline__ void mma_s8s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
     asm volatile(
@@ -270,10 +279,13 @@ __device__ __forceinline__ int byte_of(uint32_t w) {
     return (int)__byte_perm(w, 0u, 0x4440u + J);
 }
 
-// Q3 = false: Q4_K; true: Q3_K in the expanded device layout (m16n8k16 per
-// 16-element sub-block, no min term)
-template <bool Q3>
+// FMT kI8Q4K: Q4_K; kI8Q3K: Q3_K in the expanded device layout (m16n8k16
+// per 16-element sub-block, no min term); kI8Q40: Q4_0 (one m16n8k32 per
+// 32-element block, its f16 scale applied in f32, the -8 offset through the
+// block sums)
+template <int FMT>
 __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) {
+    constexpr bool Q3 = FMT == kI8Q3K, Q40 = FMT == kI8Q40;
     extern __shared__ __align__(128) uint8_t smem[];
     float* red = reinterpret_cast<float*>(smem + p.red_off);
     uint8_t* ring = smem + p.ring_off;
@@ -337,7 +349,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
         {
             const int bp = g >> 1, bm = g & 1;
             const bool bvalid = bp < 3 && bm < M;
-            const int8_t* bsrc = p.xq.planes + ((int64_t)bm * 3 + (bvalid ? bp : 0)) * p.in + (Q3 ? 4 : 8) * t;
+            const int8_t* bsrc =
+                p.xq.planes + ((int64_t)bm * 3 + (bvalid ? bp : 0)) * p.in + (Q3 || Q40 ? 4 : 8) * t;
 #pragma unroll
             for (int s = 0; s < kI8MaxSB; s++)
 #pragma unroll
@@ -345,7 +358,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                     uint2 u = make_uint2(0u, 0u);
                     if (bvalid && s < nsbw) {
                         const int8_t* src = bsrc + ((int64_t)(kb0 + sb0 + s) * 8 + j) * 32;
-                        if constexpr (Q3)
+                        if constexpr (Q3 || Q40)
                             u = make_uint2(*reinterpret_cast<const uint32_t*>(src),
                                            *reinterpret_cast<const uint32_t*>(src + 16));
                         else
@@ -375,8 +388,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                     b0 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)(kb0 + sb0 + s) * 8);
                     b1 = *reinterpret_cast<const float4*>(bsum_t + (int64_t)(kb0 + sb0 + s) * 8 + 4);
                 }
-                bs[s][0] = b0.x; bs[s][1] = b0.y; bs[s][2] = b0.z; bs[s][3] = b0.w;
-                bs[s][4] = b1.x; bs[s][5] = b1.y; bs[s][6] = b1.z; bs[s][7] = b1.w;
+                const float k8 = Q40 ? 8.0f : 1.0f;  // Q4_0: w = d (q - 8), the 8 folded in (exact)
+                bs[s][0] = b0.x * k8; bs[s][1] = b0.y * k8; bs[s][2] = b0.z * k8; bs[s][3] = b0.w * k8;
+                bs[s][4] = b1.x * k8; bs[s][5] = b1.y * k8; bs[s][6] = b1.z * k8; bs[s][7] = b1.w * k8;
             }
         }
         int slot = 0, use = 0, roff = 0;
@@ -441,6 +455,34 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
                             acc[1] = fmaf((float)ai[1], dg * coef[s][1], acc[1]);
                             acc[2] = fmaf((float)ai[2], d8 * coef[s][0], acc[2]);
                             acc[3] = fmaf((float)ai[3], d8 * coef[s][1], acc[3]);
+                        } else if constexpr (Q40) {
+                            // eight 32-element blocks: 16 quant bytes and an f16 d each
+                            const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
+                            const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
+                            const uint32_t dgw[4] = {hg.x, hg.y, hg.z, hg.w}, d8w[4] = {h8.x, h8.y, h8.z, h8.w};
+                            const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 4 * t;
+                            const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 4 * t;
+#pragma unroll
+                            for (int j = 0; j < 8; j++) {
+                                // bytes 4t..4t+3 of block j: low nibbles = elements
+                                // 4t.., high nibbles = 16+4t.. (K slots as the B
+                                // fragments)
+                                const uint32_t wg = *reinterpret_cast<const uint32_t*>(qg + 16 * j);
+                                const uint32_t w8 = *reinterpret_cast<const uint32_t*>(q8 + 16 * j);
+                                const uint32_t a[4] = {wg & 0x0F0F0F0Fu, w8 & 0x0F0F0F0Fu, (wg >> 4) & 0x0F0F0F0Fu,
+                                                       (w8 >> 4) & 0x0F0F0F0Fu};
+                                int d[4];
+                                mma_u8s8(d, a, bf[s][j][0], bf[s][j][1]);
+                                const float2 dgp = __half22float2(*reinterpret_cast<const __half2*>(&dgw[j >> 1]));
+                                const float2 d8p = __half22float2(*reinterpret_cast<const __half2*>(&d8w[j >> 1]));
+                                const float dg = (j & 1) ? dgp.y : dgp.x, d8 = (j & 1) ? d8p.y : d8p.x;
+                                acc[0] = fmaf(i2f_small(d[0]), dg * coef[s][0], acc[0]);
+                                acc[1] = fmaf(i2f_small(d[1]), dg * coef[s][1], acc[1]);
+                                acc[2] = fmaf(i2f_small(d[2]), d8 * coef[s][0], acc[2]);
+                                acc[3] = fmaf(i2f_small(d[3]), d8 * coef[s][1], acc[3]);
+                                mn[0] = fmaf(dg, bs[s][j], mn[0]);
+                                mn[1] = fmaf(d8, bs[s][j], mn[1]);
+                            }
                         } else {
                             const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
                             const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
@@ -581,8 +623,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
 // a stage raises a shared abort flag and every warp then skips the rest of
 // the work but still passes every barrier, so no barrier waits on a warp
 // that left.
-template <bool Q3>
+template <int FMT>
 __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p) {
+    constexpr bool Q3 = FMT == kI8Q3K, Q40 = FMT == kI8Q40;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem + p.ring_off;
     int8_t* bsm = reinterpret_cast<int8_t*>(smem + p.b_off);
@@ -657,8 +700,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
     const bool v0 = (n0 & 3) < M, v1 = (n1 >> 2) < 3 && (n1 & 3) < M;
     // Q4_K: bytes 8t .. 8t+7 of a 32-element sub-block; Q3_K: bytes 4t ..
     // 4t+3 of each 16-element half (the k16 fragments)
-    const int8_t* bp0 = bsm + (size_t)(v0 ? n0 : 0) * p.bstride + (Q3 ? 4 : 8) * t;
-    const int8_t* bp1 = bsm + (size_t)(v1 ? n1 : 0) * p.bstride + (Q3 ? 4 : 8) * t;
+    const int8_t* bp0 = bsm + (size_t)(v0 ? n0 : 0) * p.bstride + (Q3 || Q40 ? 4 : 8) * t;
+    const int8_t* bp1 = bsm + (size_t)(v1 ? n1 : 0) * p.bstride + (Q3 || Q40 ? 4 : 8) * t;
     // the f32 factors of this lane's C columns (sx * plane weight, zero for
     // absent tokens) and its token's block sums are read per super-block
     // (L1-resident) to keep registers for the MMA tiles
@@ -744,6 +787,59 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                         acc1[1] = fmaf((float)a1[1], dg * cg1, acc1[1]);
                         acc1[2] = fmaf((float)a1[2], d8 * cg0, acc1[2]);
                         acc1[3] = fmaf((float)a1[3], d8 * cg1, acc1[3]);
+                    } else if constexpr (Q40) {
+                        float bsv[8];
+                        {
+                            float4 bsa = make_float4(0.0f, 0.0f, 0.0f, 0.0f), bsb = bsa;
+                            if (tvalid) {
+                                bsa = __ldg(reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8));
+                                bsb = __ldg(reinterpret_cast<const float4*>(bsum_t + (int64_t)sb * 8 + 4));
+                            }
+                            bsv[0] = bsa.x; bsv[1] = bsa.y; bsv[2] = bsa.z; bsv[3] = bsa.w;
+                            bsv[4] = bsb.x; bsv[5] = bsb.y; bsv[6] = bsb.z; bsv[7] = bsb.w;
+                        }
+                        const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
+                        const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
+                        const uint32_t dgw[4] = {hg.x, hg.y, hg.z, hg.w}, d8w[4] = {h8.x, h8.y, h8.z, h8.w};
+                        const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 4 * t;
+                        const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 4 * t;
+                        float sgm = 0.0f, s8m = 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const uint32_t wg = *reinterpret_cast<const uint32_t*>(qg + 16 * j);
+                            const uint32_t w8 = *reinterpret_cast<const uint32_t*>(q8 + 16 * j);
+                            const uint32_t a[4] = {wg & 0x0F0F0F0Fu, w8 & 0x0F0F0F0Fu, (wg >> 4) & 0x0F0F0F0Fu,
+                                                   (w8 >> 4) & 0x0F0F0F0Fu};
+                            const int64_t ko = (int64_t)(sb * 8 + j) * 32;
+                            uint32_t b00 = 0u, b01 = 0u, b10 = 0u, b11 = 0u;
+                            if (v0) {
+                                b00 = *reinterpret_cast<const uint32_t*>(bp0 + ko);
+                                b01 = *reinterpret_cast<const uint32_t*>(bp0 + ko + 16);
+                            }
+                            if (v1) {
+                                b10 = *reinterpret_cast<const uint32_t*>(bp1 + ko);
+                                b11 = *reinterpret_cast<const uint32_t*>(bp1 + ko + 16);
+                            }
+                            int d0[4], d1[4];
+                            mma_u8s8(d0, a, b00, b01);
+                            mma_u8s8(d1, a, b10, b11);
+                            const float2 dgp = __half22float2(*reinterpret_cast<const __half2*>(&dgw[j >> 1]));
+                            const float2 d8p = __half22float2(*reinterpret_cast<const __half2*>(&d8w[j >> 1]));
+                            const float dg = (j & 1) ? dgp.y : dgp.x, d8 = (j & 1) ? d8p.y : d8p.x;
+                            acc0[0] = fmaf(i2f_small(d0[0]), dg * cf0, acc0[0]);
+                            acc0[1] = fmaf(i2f_small(d0[1]), dg * cf1, acc0[1]);
+                            acc0[2] = fmaf(i2f_small(d0[2]), d8 * cf0, acc0[2]);
+                            acc0[3] = fmaf(i2f_small(d0[3]), d8 * cf1, acc0[3]);
+                            acc1[0] = fmaf(i2f_small(d1[0]), dg * cg0, acc1[0]);
+                            acc1[1] = fmaf(i2f_small(d1[1]), dg * cg1, acc1[1]);
+                            acc1[2] = fmaf(i2f_small(d1[2]), d8 * cg0, acc1[2]);
+                            acc1[3] = fmaf(i2f_small(d1[3]), d8 * cg1, acc1[3]);
+                            sgm = fmaf(dg, bsv[j], sgm);
+                            s8m = fmaf(d8, bsv[j], s8m);
+                        }
+                        // Q4_0: w = d (q - 8)
+                        mn[0] = fmaf(8.0f, sgm, mn[0]);
+                        mn[1] = fmaf(8.0f, s8m, mn[1]);
                     } else {
                         float4 bsa = make_float4(0.0f, 0.0f, 0.0f, 0.0f), bsb = bsa;
                         if (tvalid) {
@@ -869,7 +965,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
 static int i8_ksplits(int64_t nsb) { return nsb <= (int64_t)kI8Cons * kI8MaxSB ? 1 : 4; }
 
 bool mm_i8_supported(const rq_weight* w, int64_t M) {
-    if ((w->type != RQ_Q4_K && w->type != RQ_Q3_K) || M < 2 || M > 4 || w->in % 256) return false;
+    if ((w->type != RQ_Q4_K && w->type != RQ_Q3_K && w->type != RQ_Q4_0) || M < 2 || M > 4 || w->in % 256)
+        return false;
     const int64_t nsb = w->in / 256;
     const int ks = i8_ksplits(nsb);
     if (nsb % ks) return false;
@@ -919,9 +1016,11 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     p.nsb = p.nsbr / p.ks;
     p.part = part;
     p.cnt = cnt;
+    // per 256 elements: 128 quant bytes (Q4_0: 8 blocks of 16) and 16
+    // header bytes (Q4_0: 8 f16 scales; Q3_K: 20)
     p.hsb = w0->type == RQ_Q3_K ? 20u : 16u;
-    p.qrow = (uint32_t)(w0->nblk * 128);
-    p.hrow = (uint32_t)(w0->nblk * p.hsb);
+    p.qrow = (uint32_t)(p.nsbr * 128);
+    p.hrow = (uint32_t)(p.nsbr * p.hsb);
     p.qseg = (uint32_t)(p.nsb * 128);
     p.hseg = (uint32_t)(p.nsb * p.hsb);
     p.qstride = p.qseg + kI8QPad;
@@ -969,9 +1068,10 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
         cudaError_t e = cudaSuccess;
-        const void* kerns[4] = {(const void*)mm_i8_kernel<false>, (const void*)mm_i8_kernel<true>,
-                                (const void*)mm_i8x4_kernel<false>, (const void*)mm_i8x4_kernel<true>};
-        for (int k = 0; k < 4 && e == cudaSuccess; k++)
+        const void* kerns[6] = {(const void*)mm_i8_kernel<kI8Q4K>,   (const void*)mm_i8_kernel<kI8Q3K>,
+                                (const void*)mm_i8_kernel<kI8Q40>,   (const void*)mm_i8x4_kernel<kI8Q4K>,
+                                (const void*)mm_i8x4_kernel<kI8Q3K>, (const void*)mm_i8x4_kernel<kI8Q40>};
+        for (int k = 0; k < 6 && e == cudaSuccess; k++)
             e = cudaFuncSetAttribute(kerns[k], cudaFuncAttributeMaxDynamicSharedMemorySize, kI8Smem);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(int8 matmul)");
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
@@ -988,9 +1088,14 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     cfg.numAttrs = 1;
     cudaError_t e;
     if (w0->type == RQ_Q3_K)
-        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<true>, p) : cudaLaunchKernelEx(&cfg, mm_i8_kernel<true>, p);
+        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<kI8Q3K>, p)
+               : cudaLaunchKernelEx(&cfg, mm_i8_kernel<kI8Q3K>, p);
+    else if (w0->type == RQ_Q4_0)
+        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<kI8Q40>, p)
+               : cudaLaunchKernelEx(&cfg, mm_i8_kernel<kI8Q40>, p);
     else
-        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<false>, p) : cudaLaunchKernelEx(&cfg, mm_i8_kernel<false>, p);
+        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<kI8Q4K>, p)
+               : cudaLaunchKernelEx(&cfg, mm_i8_kernel<kI8Q4K>, p);
     return cuda_error(e, "int8 matmul kernel");
 }
 

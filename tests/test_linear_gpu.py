@@ -191,6 +191,32 @@ def test_q3k_int8_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
         assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("out,n_in,M", [(1, 2048, 2), (17, 4096, 3), (333, 4096, 4), (4096, 4096, 2),
+                                         (4096, 4096, 3), (4096, 4096, 4), (1040, 28672, 2), (150, 28672, 4),
+                                         (4096, 4096, 5), (4096, 4096, 9), (130, 8192, 16), (72, 1024, 6)])
+def test_q4_0_int8_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
+    """Q4_0 (the ParallelQ4Linear format) at M >= 2 on the int8 tensor
+    cores: one m16n8k32 per 32-element block (low nibbles = elements 0..15,
+    high = 16..31, the K slots of the B fragments), its f16 scale applied to
+    the s32 tile in f32 and the -8 offset through the block sums; above four
+    rows one launch per group of 2..4 rows (5 -> 3 + 2, 9 -> 3 x 3, 16 ->
+    4 x 4); in > 8192 with K split four ways; 1024 (no whole K-slice per
+    warp) keeps a pipeline pass per row."""
+    from rustyllm_b200 import QWeight
+    from rustyllm_b200.linear import _linear
+    _, blocks = make_weight(oracle, 2, out, n_in, seed=out * 3 + M)
+    w = QWeight.upload(rq_ctx, 2, blocks, out, n_in)
+    x = np.random.default_rng(M + out + 2).standard_normal((M, n_in)).astype(np.float32)
+    x[:, :256] *= 40.0
+    x[:, 256:512] *= 1e-3
+    y = _linear(w, x)
+    ref = oracle.matmul_ref(2, blocks, out, n_in, x, acc64=True)
+    assert np.isfinite(y).all()
+    assert rel_l2(y, ref) <= REL_L2_TOL
+    for m in range(M):
+        assert rel_l2(y[m], ref[m]) <= REL_L2_TOL
+
+
 @pytest.mark.parametrize("out,n_in,M", [(200, 1024, 6), (128, 2048, 24), (1040, 4096, 128), (333, 8192, 67),
                                          (130, 28672, 40), (256, 8192, 300), (72, 1024, 16), (8192, 1024, 9),
                                          (96, 768, 8)])
