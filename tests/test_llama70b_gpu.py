@@ -76,34 +76,20 @@ def test_70b_geometry_verify_forward_logits(pair):
     assert amax == ref_amax[12:].tolist()
 
 
-def test_70b_geometry_two_token_verify(pair):
-    """forward_all over 2 tokens (the verify of a one-token draft): q/k/v,
-    o and gate/up run on the int8 tensor-core kernel in one weight pass
-    (down, in = 28672, two M=1 passes); both positions' logits within 1e-4
-    of the oracle, argmax equal."""
+@pytest.mark.parametrize("T", [2, 3, 4])
+def test_70b_geometry_small_verify(pair, T):
+    """forward_all over 2, 3 or 4 tokens (the verify of a one- to three-token
+    draft): all seven linears on the int8 tensor-core kernels in one weight
+    pass (two tokens: B fragments in registers; three and four: the
+    twelve-column form; down_proj, in = 28672, with K split over four CTAs
+    per row group); every position within 1e-4 of the oracle, argmax equal."""
     model, ref, _ = pair
-    rng = np.random.default_rng(22)
+    rng = np.random.default_rng(20 + T)
     prompt = rng.integers(0, CFG["vocab"], size=12).astype(np.int32)
-    draft = rng.integers(0, CFG["vocab"], size=2).astype(np.int32)
+    draft = rng.integers(0, CFG["vocab"], size=T).astype(np.int32)
     model.forward(prompt, 0, want_logits=False)
     logits, amax = model.forward_all(draft, 12, want_logits=True)
     ref_logits, ref_amax = ref.forward_all(np.concatenate([prompt, draft]), 0)
-    for t in range(2):
-        assert rel_l2(logits[t], ref_logits[12 + t]) <= LOGIT_TOL, t
-    assert amax == ref_amax[12:].tolist()
-
-
-def test_70b_geometry_three_token_verify(pair):
-    """forward_all over 3 tokens (the verify of a two-token draft): q/k/v,
-    o and gate/up on the int8 kernel's twelve-column form; every position
-    within 1e-4 of the oracle, argmax equal."""
-    model, ref, _ = pair
-    rng = np.random.default_rng(23)
-    prompt = rng.integers(0, CFG["vocab"], size=12).astype(np.int32)
-    draft = rng.integers(0, CFG["vocab"], size=3).astype(np.int32)
-    model.forward(prompt, 0, want_logits=False)
-    logits, amax = model.forward_all(draft, 12, want_logits=True)
-    ref_logits, ref_amax = ref.forward_all(np.concatenate([prompt, draft]), 0)
-    for t in range(3):
+    for t in range(T):
         assert rel_l2(logits[t], ref_logits[12 + t]) <= LOGIT_TOL, t
     assert amax == ref_amax[12:].tolist()

@@ -28,7 +28,7 @@ def _oracle(oracle, host, qtype=12):
     return ref
 
 
-@pytest.mark.parametrize("T", [2, 5, 12, 25])
+@pytest.mark.parametrize("T", [2, 4, 5, 12, 25])
 def test_forward_all_matches_oracle_per_position(oracle, rq_ctx, T):
     from rustyllm_b200.llama import random_model
     model, host = random_model(CFG, 12, seed=61, host_blocks=True)
