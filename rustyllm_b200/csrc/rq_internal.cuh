@@ -238,11 +238,30 @@ struct PipeNext {
     uint32_t budget;        // bytes per CTA over all n weights
 };
 PipeNext pipe_next(const rq_weight* const* ws, int n, uint32_t budget);
+// RMSNorm staging epilogue (one job whose y is the residual stream): the CTA
+// that completes a 32-row block of y (arrival counters, as PipeSwiglu)
+// stages v = y * w over the block into xq (the staging kernel's per-block
+// arithmetic) and writes the block's sum of squares to ss[block].  The norm's
+// 1 / sqrt(mean + eps) is not applied: the matvec that reads xq scales its
+// outputs by it (PipeRmsIn), which is the same linear map.
+struct PipeRms {
+    XQ xq;
+    float* ss;       // [out / 32] block sums of squares
+    int* cnt;        // [out / 32] arrival counters (zero between launches)
+    const float* w;  // RMSNorm weight [out]
+};
+// Outputs divided by sqrt(sum of ss[0..nb) / n + eps) (the sum in a fixed order).
+struct PipeRmsIn {
+    const float* ss;
+    int nb;
+    float n, eps;
+};
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err = nullptr,
                        const float* const* adds = nullptr, const P2PArgs* ar = nullptr,
                        const PipeDevWeights* dw = nullptr, const PipeSwiglu* sw = nullptr,
-                       const PipeCombine* cmb = nullptr, const PipeNext* next = nullptr);
+                       const PipeCombine* cmb = nullptr, const PipeNext* next = nullptr,
+                       const PipeRms* rms = nullptr, const PipeRmsIn* rsi = nullptr);
 
 // small-M Q4_K matmul on the tensor cores (rq_mm_small.cu).  Activations are
 // staged per row as x / s = hi + lo (two f16 values per element, s a power of

@@ -67,6 +67,9 @@ struct rq_llama {
     rq::XQ xq;      // Tmax rows of max(hidden, intermediate)
     rq::XQ xqd;     // one row of the local intermediate: the down projection's input at decode
     int* swcnt;     // [I / 32] arrival counters of the decode SwiGLU staging (zero between launches)
+    rq::XQ xqr;     // one row of the hidden size: the RMSNorm staging of the o / down epilogues at decode
+    float* rss;     // [H / 32] its block sums of squares
+    int* rcnt;      // [H / 32] its arrival counters (zero between launches)
     rq::PipeNext nx{};  // L2 prefetch hint for the decode matvec being launched (nx.n = 0: none)
     float* i8part;      // [4][4][hidden] split-K partial rows of the int8 down projection (T = 2..4)
     int* i8cnt;         // [256] its arrival counters (zero between launches)
@@ -515,15 +518,16 @@ int run_linears(rq_llama* m, int n, const rq_weight* const* ws, int64_t T, float
 // partial product (rank 0 also adds the residual) is summed into x by an
 // all-reduce -- at T = 1 on the pipeline inside the matvec kernel itself,
 // over the ranks' NVLink exchange regions.
-int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st, const XQ* staged = nullptr) {
+int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st, const XQ* staged = nullptr,
+                 const PipeRms* rms = nullptr) {
     const XQ xin = staged ? *staged : m->xq;
     if (m->W == 1) {
         const rq_weight* w1[1] = {w};
         float* y1[1] = {m->x};
         const float* a1[1] = {m->x};
-        if (staged)
+        if (staged || rms)  // rms: the next RMSNorm's input staged in the epilogue
             return launch_matvec_pipe(w1, &xin, y1, 1, m->ctx->sm_count, st, m->derr, a1, nullptr, nullptr, nullptr,
-                                      nullptr, next_hint(m));
+                                      nullptr, next_hint(m), rms);
         return run_linears(m, 1, w1, T, y1, a1, st);
     }
     const rq_weight* w1[1] = {w};
@@ -551,6 +555,28 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st, co
 // of 32.
 bool swiglu_in_epilogue(const rq_llama* m, const rq_weight* gate, const rq_weight* up, int64_t T) {
     return T == 1 && pipe_supported(gate) && pipe_supported(up) && gate->out == up->out && m->I_l % 32 == 0;
+}
+
+// Decode on one rank with every linear of layer l on the pipeline: the o
+// and down matvecs stage the next RMSNorm's input in their epilogue
+// (PipeRms) and the q/k/v and gate/up matvecs divide by its RMS
+// (PipeRmsIn), so no staging kernel runs between them (RQ_RMS_EPILOGUE=0
+// restores the staging kernels).
+bool rms_epilogue_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("RQ_RMS_EPILOGUE");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+bool rms_in_epilogue(const rq_llama* m, int64_t l, int64_t T) {
+    if (T != 1 || m->W != 1 || m->cfg.hidden % 32 || l < 0 || l >= m->cfg.n_layers || !rms_epilogue_enabled())
+        return false;
+    const rq_llama::Layer& L = m->layers[(size_t)l];
+    for (int i = 0; i < 7; i++)
+        if (!pipe_supported(L.w[i])) return false;
+    return swiglu_in_epilogue(m, L.w[4], L.w[5], T);
 }
 
 // y_i = x W_i^T (+ add_i) for the n Q4_K weights (same in) over the T rows
@@ -647,6 +673,14 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
                 const XQ2 q2 = i8_stage(m, T, H);
                 rc = launch_xq2_stage(m->x, T, H, q2, st, L.rms1, c.rms_eps);
                 if (!rc) rc = launch_mm_i8(w3, y3, 3, T, q2, m->ctx->sm_count, st, m->derr);
+            } else if (l > 0 && rms_in_epilogue(m, l - 1, T) && rms_in_epilogue(m, l, T)) {
+                // x * rms1 was staged by the previous down projection's epilogue
+                const XQ in3[3] = {m->xqr, m->xqr, m->xqr};
+                const PipeRmsIn ri{m->rss, (int)(H / 32), (float)H, c.rms_eps};
+                set_next(m, &L.w[3], 1, kNextBudgetAttn);
+                rc = launch_matvec_pipe(w3, in3, y3, 3, m->ctx->sm_count, st, m->derr, nullptr, nullptr, nullptr,
+                                        nullptr, nullptr, next_hint(m), nullptr, &ri);
+                set_next(m, nullptr, 0, 0);
             } else {
                 rc = launch_xquant_rmsnorm(m->x, L.rms1, c.rms_eps, T, H, m->xq, st);
                 if (T == 1) set_next(m, &L.w[3], 1, kNextBudgetAttn);
@@ -707,7 +741,12 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
             if (rc) return rc;
         }
         if (T == 1 && !tc) set_next(m, &L.w[4], 2, kNextBudget);
-        rc = tc ? row_parallel_mm(m, L.w[3], T, st) : row_parallel(m, L.w[3], T, st);
+        {
+            // o stages x * rms2 for gate/up in its epilogue where that is on
+            const PipeRms rms_o{m->xqr, m->rss, m->rcnt, L.rms2};
+            const bool ro = !tc && rms_in_epilogue(m, l, T);
+            rc = tc ? row_parallel_mm(m, L.w[3], T, st) : row_parallel(m, L.w[3], T, st, nullptr, ro ? &rms_o : nullptr);
+        }
         set_next(m, nullptr, 0, 0);
         if (rc) return rc;
     mlp:
@@ -722,16 +761,23 @@ int forward_device(rq_llama* m, int64_t T, bool want_logits, cudaStream_t st, bo
                 rc = launch_xq2_stage(m->x, T, H, q2, st, L.rms2, c.rms_eps);
                 if (!rc) rc = launch_mm_i8(w2, y2, 2, T, q2, m->ctx->sm_count, st, m->derr);
             } else if (swiglu_in_epilogue(m, L.w[4], L.w[5], T)) {
-                rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
-                const XQ in2[2] = {m->xq, m->xq};
+                // x * rms2 staged by o's epilogue, or the staging kernel
+                const bool rin = rms_in_epilogue(m, l, T);
+                if (!rin) rc = launch_xquant_rmsnorm(m->x, L.rms2, c.rms_eps, T, H, m->xq, st);
+                const XQ src = rin ? m->xqr : m->xq;
+                const XQ in2[2] = {src, src};
                 const PipeSwiglu sw{m->xqd, m->swcnt, 0};
+                const PipeRmsIn ri{m->rss, (int)(H / 32), (float)H, c.rms_eps};
                 set_next(m, &L.w[6], 1, kNextBudget);
                 if (!rc) rc = launch_matvec_pipe(w2, in2, y2, 2, m->ctx->sm_count, st, m->derr, nullptr, nullptr,
-                                                 nullptr, &sw, nullptr, next_hint(m));
-                // down prefetches the next layer's q/k/v
+                                                 nullptr, &sw, nullptr, next_hint(m), nullptr, rin ? &ri : nullptr);
+                // down prefetches the next layer's q/k/v and, where the next
+                // layer reads it, stages x * rms1 of that layer
                 if (l + 1 < c.n_layers) set_next(m, m->layers[l + 1].w, 3, kNextBudget);
                 else set_next(m, nullptr, 0, 0);
-                if (!rc) rc = row_parallel(m, L.w[6], T, st, &m->xqd);
+                const bool rout = rin && rms_in_epilogue(m, l + 1, T);
+                const PipeRms rms_d{m->xqr, m->rss, m->rcnt, rout ? m->layers[l + 1].rms1 : nullptr};
+                if (!rc) rc = row_parallel(m, L.w[6], T, st, &m->xqd, rout ? &rms_d : nullptr);
                 set_next(m, nullptr, 0, 0);
                 if (rc) return rc;
                 continue;
@@ -1010,6 +1056,11 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     if (!rc) rc = cuda_error(cudaMemset(m->i8cnt, 0, 256 * sizeof(int)), "counter reset");
     if (!rc) rc = dalloc(m, &m->swcnt, (size_t)(I / 32 + 1));
     if (!rc) rc = cuda_error(cudaMemset(m->swcnt, 0, sizeof(int) * (size_t)(I / 32 + 1)), "counter reset");
+    uint8_t* xqrbuf = nullptr;
+    if (!rc) rc = dalloc(m, &xqrbuf, xq_bytes(1, H));
+    if (!rc) rc = dalloc(m, &m->rss, (size_t)(H / 32 + 1));
+    if (!rc) rc = dalloc(m, &m->rcnt, (size_t)(H / 32 + 1));
+    if (!rc) rc = cuda_error(cudaMemset(m->rcnt, 0, sizeof(int) * (size_t)(H / 32 + 1)), "counter reset");
     if (!rc) rc = cuda_error(cudaDeviceSynchronize(), "counter reset");
     if (!rc && T >= kMinTensorM) rc = dalloc(m, &xhbuf, xh_bytes(T, maxin));
     if (!rc) rc = dalloc(m, &m->best, 1);
@@ -1030,6 +1081,8 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
         m->xq.stats = (float4*)(xqbuf + (((size_t)T * 3 * maxin + 255) & ~(size_t)255));
         m->xqd.planes = (int8_t*)xqdbuf;
         m->xqd.stats = (float4*)(xqdbuf + (((size_t)3 * I + 255) & ~(size_t)255));
+        m->xqr.planes = (int8_t*)xqrbuf;
+        m->xqr.stats = (float4*)(xqrbuf + (((size_t)3 * H + 255) & ~(size_t)255));
         m->xh = xhbuf ? xh_at(xhbuf, T, maxin) : XH{};
         // RoPE tables as QuantStreamCache::new computes them
         // (src/streaming_quantized.rs:104-118): inv_freq[i] =

@@ -70,6 +70,10 @@ struct PipeParams {
     int cmb;              // 1: sparse-MoE combine epilogue (cm)
     PipeCombine cm;
     PipeNext nx;          // weights of the next launch to prefetch into L2 (nx.n = 0: none)
+    int rms;              // 1: RMSNorm staging epilogue (rm)
+    PipeRms rm;
+    int rsi_on;           // 1: outputs divided by the staged vector's RMS (ri)
+    PipeRmsIn ri;
 };
 
 // This CTA's rows of a job: an even split of the job's rows over the grid,
@@ -203,6 +207,43 @@ __device__ __forceinline__ void swiglu_blocks(const PipeParams& p) {
     }
 }
 
+// RMSNorm staging (see PipeRms): after this CTA's y rows are written, each
+// 32-row block they touch gets the number of rows written added to its
+// arrival counter; the CTA that completes the block reads it back from L2,
+// stages y * w (stage_block, as the staging kernel) and stores the block's
+// sum of squares, then zeroes the counter.
+__device__ __forceinline__ void rms_blocks(const PipeParams& p) {
+    __threadfence();  // this thread's y rows are visible before any count
+    __syncthreads();
+    const PipeJob& j0 = p.jobs[0];
+    int64_t rb;
+    int nrows;
+    job_rows(j0, &rb, &nrows);
+    if (nrows == 0) return;
+    const int64_t b0 = rb / 32;
+    const int nbt = (int)((rb + nrows - 1) / 32 - b0 + 1);
+    for (int i = threadIdx.x; i < nbt; i += blockDim.x) {
+        const int64_t b = b0 + i;
+        const int64_t lo = max(rb, 32 * b), hi = min(rb + nrows, 32 * b + 32);
+        const int add = (int)(hi - lo);
+        int* cnt = p.rm.cnt + b;
+        __threadfence();
+        if (atomicAdd(cnt, add) + add != 32) continue;
+        __threadfence();
+        const float* x = j0.y + 32 * b;
+        float v[32], s2 = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 32; k++) {
+            const float xv = __ldcg(x + k);
+            s2 = fmaf(xv, xv, s2);
+            v[k] = xv * p.rm.w[32 * b + k];
+        }
+        stage_block(v, 0, b, j0.out, p.rm.xq.planes, p.rm.xq.stats);
+        p.rm.ss[b] = s2;
+        atomicExch(cnt, 0);
+    }
+}
+
 // Sparse-MoE combine (see PipeCombine): the k slots of a token are
 // consecutive jobs over the same rows of this CTA, so every output row is
 // finished here: the slot outputs (partials summed in slice order, the bits
@@ -241,6 +282,9 @@ __device__ __forceinline__ void combine_rows(const PipeParams& p, const float* r
 template <int TYPE, int RPW>
 __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
+    // the input's RMS divisor (rsi_on), after the barriers: the dynamic
+    // allocation already takes the whole shared-memory budget
+    float& s_rms = *reinterpret_cast<float*>(smem + kBarBytes);
     float* red = reinterpret_cast<float*>(smem + p.red_off);
     uint8_t* ring = smem + p.ring_off;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -301,6 +345,15 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         typename LaneOf<TYPE>::T L;
         LaneOffsets o;
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (p.rsi_on && c == 0) {
+            // the staged vector's RMS: lane sums in a fixed order, then a
+            // fixed shuffle tree (the same bits in every CTA and run)
+            float t = 0.0f;
+            for (int i = lane; i < p.ri.nb; i += 32) t += __ldcg(p.ri.ss + i);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+            if (lane == 0) s_rms = sqrtf(t / p.ri.n + p.ri.eps);
+        }
         const int8_t* cur_x = nullptr;
         int slot = 0, use = 0, roff = 0;
         bool ok = true;
@@ -350,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         return;
     }
     int roff = 0;
+    const float rdiv = p.rsi_on ? s_rms : 1.0f;
     for (int j = 0; j < p.njobs; j++) {
         int64_t rb;
         int nrows;
@@ -358,11 +412,13 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
         for (int t = threadIdx.x; t < nrows; t += blockDim.x) {
             float acc = 0.0f;
             for (int s = 0; s < p.S; s++) acc += red[(roff + t) * p.S + s];
+            if (p.rsi_on) acc = acc / rdiv;
             p.jobs[j].y[rb + t] = add ? acc + add[rb + t] : acc;
         }
         roff += nrows;
     }
     if (p.sw) swiglu_blocks(p);
+    if (p.rms) rms_blocks(p);
 }
 
 template <int TYPE, int RPW>
@@ -431,7 +487,7 @@ bool pipe_supported(const rq_weight* w) {
 int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* ys, int njobs,
                        int sm_count, cudaStream_t st, int* err, const float* const* adds, const P2PArgs* ar,
                        const PipeDevWeights* dw, const PipeSwiglu* sw, const PipeCombine* cmb,
-                       const PipeNext* next) {
+                       const PipeNext* next, const PipeRms* rms, const PipeRmsIn* rsi) {
     if (njobs < 1 || njobs > kMaxJobs) return set_error(RQ_ERR_INVALID, "matvec pipeline: %d jobs", njobs);
     const rq_weight* w0 = ws[0];
     TypeInfo ti = type_info(w0->type);
@@ -466,6 +522,20 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
             return set_error(RQ_ERR_INVALID, "matvec pipeline: combine needs whole tokens of one shape");
         p.cmb = 1;
         p.cm = *cmb;
+    }
+    p.rms = 0;
+    p.rsi_on = 0;
+    if (rms) {
+        if (njobs != 1 || ar || cmb || sw || w0->out % 32 || !rms->cnt || !rms->ss || !rms->w)
+            return set_error(RQ_ERR_INVALID, "matvec pipeline: RMSNorm staging needs one job of whole blocks");
+        p.rms = 1;
+        p.rm = *rms;
+    }
+    if (rsi) {
+        if (ar || cmb || !rsi->ss || rsi->nb < 1 || !(rsi->n > 0.0f))
+            return set_error(RQ_ERR_INVALID, "matvec pipeline: bad RMS input");
+        p.rsi_on = 1;
+        p.ri = *rsi;
     }
     memset(&p.nx, 0, sizeof p.nx);
     if (next && next->n > 0 && next->n <= kMaxNext && next->qrow % 16 == 0 && next->hrow % 16 == 0) p.nx = *next;
@@ -503,8 +573,8 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
         p.fuse = 1;
         p.ar = *ar;
     }
-    p.red_off = kBarBytes;
-    p.ring_off = (uint32_t)((kBarBytes + rows_cap(grid) * p.S * 4 + 127) & ~(int64_t)127);
+    p.red_off = kBarBytes + 16;  // 16 bytes of scalars after the barriers
+    p.ring_off = (uint32_t)((p.red_off + rows_cap(grid) * p.S * 4 + 127) & ~(int64_t)127);
     int nstage = (int)((kSmemBudget - p.ring_off) / p.stage_bytes);
     nstage = std::min(nstage, 32);
     if (nstage < 2) return set_error(RQ_ERR_UNSUPPORTED, "matvec pipeline: row of %u bytes too large", rowb);
