@@ -42,6 +42,7 @@
 
 #include "rq_async.cuh"
 #include "rq_internal.cuh"
+#include "rq_tcgen05.cuh"
 
 namespace rq {
 
@@ -628,9 +629,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
     constexpr bool Q3 = FMT == kI8Q3K, Q40 = FMT == kI8Q40;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem + p.ring_off;
-    int8_t* bsm = reinterpret_cast<int8_t*>(smem + p.b_off);
     float* pr = reinterpret_cast<float*>(smem + p.pr_off);
     __shared__ int s_abort;
+    __shared__ uint32_t s_tmem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t full0 = smem_u32(smem), empty0 = full0 + 8 * 16;
     // K-split: this CTA's row group and K-range (super-blocks kb0 .. kb0 + nsb)
@@ -645,7 +646,15 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (threadIdx.x == 0) s_abort = 0;
+    if (warp == 1) {  // the B fragments live in TMEM: 256 columns, freed by this warp at the end
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(256u)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc::tmem_fence_before();
     __syncthreads();
+    tc::tmem_fence_after();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -684,24 +693,52 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
     const int M = p.M;
     const int sb0 = w * p.nsb / kI8Cons, nsbw = (w + 1) * p.nsb / kI8Cons - sb0;
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // the activation rows into shared memory: column n = 4 p + m
-    {
-        const int64_t chunks = (int64_t)p.nsb * 16;  // 16-byte chunks of the K-range
-        for (int64_t i = ct; i < (int64_t)3 * M * chunks; i += 32 * kI8Cons) {
-            const int64_t r = i / chunks, c = i % chunks;  // r = 3 m + p: the XQ2 row order
-            const int m = (int)(r / 3), pl = (int)(r % 3);
-            const uint4 v = *reinterpret_cast<const uint4*>(p.xq.planes + r * p.in + (int64_t)kb0 * 256 + 16 * c);
-            *reinterpret_cast<uint4*>(bsm + (size_t)(4 * pl + m) * p.bstride + 16 * c) = v;
-        }
-    }
-    named_bar_sync(1, 32 * kI8Cons);
-    // B fragment columns of this lane and the f32 factors of its C columns
+    // B fragment columns of this lane: n0 = g and n1 = 8 + g, column n = 4 pl + m
+    // the XQ2 row 3 m + pl (n1 only for pl = 2; absent tokens are zeros)
     const int n0 = g, n1 = 8 + g;
     const bool v0 = (n0 & 3) < M, v1 = (n1 >> 2) < 3 && (n1 & 3) < M;
-    // Q4_K: bytes 8t .. 8t+7 of a 32-element sub-block; Q3_K: bytes 4t ..
-    // 4t+3 of each 16-element half (the k16 fragments)
-    const int8_t* bp0 = bsm + (size_t)(v0 ? n0 : 0) * p.bstride + (Q3 || Q40 ? 4 : 8) * t;
-    const int8_t* bp1 = bsm + (size_t)(v1 ? n1 : 0) * p.bstride + (Q3 || Q40 ? 4 : 8) * t;
+    // This warp's TMEM lanes (32 (warp % 4) ..) and columns (warps 5..8
+    // the second 128): per super-block s of the K-slice, 32 columns = for
+    // each 32-element sub-block the lane's two B words of column n0, then of
+    // n1 (Q4_K: bytes 8t .. 8t+7; Q3_K / Q4_0: bytes 4t .. 4t+3 of each
+    // 16-element half).  Filled once, read back per super-block with two
+    // tcgen05.ld of 16 columns, so the ring gets the shared memory.
+    const uint32_t tb = s_tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (warp >= 5 ? 128u : 0u);
+    {
+        constexpr int lo_off = (Q3 || Q40) ? 4 : 8;
+        const int8_t* src0 =
+            p.xq.planes + (int64_t)(v0 ? 3 * (n0 & 3) + (n0 >> 2) : 0) * p.in + (int64_t)kb0 * 256 + lo_off * t;
+        const int8_t* src1 =
+            p.xq.planes + (int64_t)(v1 ? 3 * (n1 & 3) + (n1 >> 2) : 0) * p.in + (int64_t)kb0 * 256 + lo_off * t;
+#pragma unroll
+        for (int s = 0; s < kI8MaxSB; s++) {
+            if (s < nsbw) {  // warp-uniform: tcgen05.st is warp-wide
+                uint32_t v[32];
+#pragma unroll
+                for (int sub = 0; sub < 8; sub++) {
+                    const int64_t ko = (int64_t)((sb0 + s) * 8 + sub) * 32;
+                    uint2 b0 = make_uint2(0u, 0u), b1 = make_uint2(0u, 0u);
+                    if constexpr (Q3 || Q40) {
+                        if (v0)
+                            b0 = make_uint2(*reinterpret_cast<const uint32_t*>(src0 + ko),
+                                            *reinterpret_cast<const uint32_t*>(src0 + ko + 16));
+                        if (v1)
+                            b1 = make_uint2(*reinterpret_cast<const uint32_t*>(src1 + ko),
+                                            *reinterpret_cast<const uint32_t*>(src1 + ko + 16));
+                    } else {
+                        if (v0) b0 = *reinterpret_cast<const uint2*>(src0 + ko);
+                        if (v1) b1 = *reinterpret_cast<const uint2*>(src1 + ko);
+                    }
+                    v[4 * sub] = b0.x;
+                    v[4 * sub + 1] = b0.y;
+                    v[4 * sub + 2] = b1.x;
+                    v[4 * sub + 3] = b1.y;
+                }
+                tc::tmem_st32u(tb + 32u * (uint32_t)s, v);
+            }
+        }
+        tc::tmem_wait_st();
+    }
     // the f32 factors of this lane's C columns (sx * plane weight, zero for
     // absent tokens) and its token's block sums are read per super-block
     // (L1-resident) to keep registers for the MMA tiles
@@ -729,7 +766,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                 if (lane == 0 && p.err) atomicExch(p.err, 1);
                 *(volatile int*)&s_abort = 1;
             }
-            const bool live = !*(volatile int*)&s_abort;
+            const bool live = __all_sync(0xffffffffu, !*(volatile int*)&s_abort);  // warp-uniform
             const uint8_t* sq = ring + (size_t)slot * p.stage_bytes;
             const uint8_t* sh = sq + (size_t)p.RS * p.qstride;
             const int rows = min(p.RS, nrows - r0);
@@ -740,6 +777,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
             for (int s = 0; s < kI8MaxSB; s++) {
                 if (live && s < nsbw) {
                     const int sb = sb0 + s;
+                    uint32_t bq[16];  // B words of half the super-block's sub-blocks (TMEM)
                     const float cf0 = ca0 ? __ldg(sxa0 + sb) * pwa : 0.0f, cf1 = ca1 ? __ldg(sxa1 + sb) * pwa : 0.0f;
                     const float cg0 = cb0 ? __ldg(sxb0 + sb) * pwb : 0.0f, cg1 = cb1 ? __ldg(sxb1 + sb) * pwb : 0.0f;
                     if constexpr (Q3) {
@@ -757,6 +795,10 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                                                     *reinterpret_cast<const uint32_t*>(q8 + 32 * c),
                                                     *reinterpret_cast<const uint32_t*>(q8 + 32 * c + 16)};
                             const uint32_t scg = hg4[c], sc8 = h84[c];
+                            if (c == 0 || c == 2) {  // B of 32-element chunks 2c .. 2c+3
+                                tc::tmem_ld16(tb + 32u * (uint32_t)s + 8u * (uint32_t)c, bq);
+                                tc::tmem_wait_ld();
+                            }
 #pragma unroll
                             for (int q = 0; q < 4; q++) {
                                 // sub-block 4c + q: low (q < 2) or high nibbles of
@@ -764,10 +806,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                                 // 32-element chunk 2c + q / 2
                                 const uint32_t ag = q < 2 ? q3_lo(wq[q & 1]) : q3_hi(wq[q & 1]);
                                 const uint32_t a8 = q < 2 ? q3_lo(wq[2 + (q & 1)]) : q3_hi(wq[2 + (q & 1)]);
-                                const int64_t ko = (int64_t)(sb * 8 + 2 * c + (q >> 1)) * 32 + 16 * (q & 1);
-                                uint32_t b0 = 0u, b1 = 0u;
-                                if (v0) b0 = *reinterpret_cast<const uint32_t*>(bp0 + ko);
-                                if (v1) b1 = *reinterpret_cast<const uint32_t*>(bp1 + ko);
+                                const int cj = (2 * c + (q >> 1)) & 3;  // chunk within the loaded half
+                                const uint32_t b0 = bq[4 * cj + (q & 1)], b1 = bq[4 * cj + 2 + (q & 1)];
                                 int d0[4], d1[4];
                                 mma_s8s8_k16(d0, ag, a8, b0);
                                 mma_s8s8_k16(d1, ag, a8, b1);
@@ -810,16 +850,12 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                             const uint32_t w8 = *reinterpret_cast<const uint32_t*>(q8 + 16 * j);
                             const uint32_t a[4] = {wg & 0x0F0F0F0Fu, w8 & 0x0F0F0F0Fu, (wg >> 4) & 0x0F0F0F0Fu,
                                                    (w8 >> 4) & 0x0F0F0F0Fu};
-                            const int64_t ko = (int64_t)(sb * 8 + j) * 32;
-                            uint32_t b00 = 0u, b01 = 0u, b10 = 0u, b11 = 0u;
-                            if (v0) {
-                                b00 = *reinterpret_cast<const uint32_t*>(bp0 + ko);
-                                b01 = *reinterpret_cast<const uint32_t*>(bp0 + ko + 16);
+                            if (j == 0 || j == 4) {  // B of blocks j .. j+3
+                                tc::tmem_ld16(tb + 32u * (uint32_t)s + 4u * (uint32_t)j, bq);
+                                tc::tmem_wait_ld();
                             }
-                            if (v1) {
-                                b10 = *reinterpret_cast<const uint32_t*>(bp1 + ko);
-                                b11 = *reinterpret_cast<const uint32_t*>(bp1 + ko + 16);
-                            }
+                            const uint32_t b00 = bq[4 * (j & 3)], b01 = bq[4 * (j & 3) + 1];
+                            const uint32_t b10 = bq[4 * (j & 3) + 2], b11 = bq[4 * (j & 3) + 3];
                             int d0[4], d1[4];
                             mma_u8s8(d0, a, b00, b01);
                             mma_u8s8(d1, a, b10, b11);
@@ -862,17 +898,19 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                         for (int c = 0; c < 4; c++) {
                             const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
                             const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
+                            if (c == 0 || c == 2) {  // B of sub-blocks 2c .. 2c+3
+                                tc::tmem_ld16(tb + 32u * (uint32_t)s + 8u * (uint32_t)c, bq);
+                                tc::tmem_wait_ld();
+                            }
                             const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
                                                      w8.y & 0x0F0F0F0Fu};
                             const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
                                                      (wg.y >> 4) & 0x0F0F0F0Fu, (w8.y >> 4) & 0x0F0F0F0Fu};
     #pragma unroll
                             for (int h = 0; h < 2; h++) {
-                                const int sub = 2 * c + h;
-                                const int64_t ko = (int64_t)(sb * 8 + sub) * 32;
-                                uint2 b0 = make_uint2(0u, 0u), b1 = make_uint2(0u, 0u);
-                                if (v0) b0 = *reinterpret_cast<const uint2*>(bp0 + ko);
-                                if (v1) b1 = *reinterpret_cast<const uint2*>(bp1 + ko);
+                                const int sub = (2 * c + h) & 3;  // within the loaded half
+                                const uint2 b0 = make_uint2(bq[4 * sub], bq[4 * sub + 1]);
+                                const uint2 b1 = make_uint2(bq[4 * sub + 2], bq[4 * sub + 3]);
                                 int d0[4], d1[4];
                                 if (h == 0) {
                                     mma_u8s8(d0, alo, b0.x, b0.y);
@@ -956,6 +994,12 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
         __shared__ int s_last;
         i8_ksplit_finish(p, rgi, nrg, ct, 32 * kI8Cons, 1, &s_last);
     }
+    // every consumer's TMEM reads have completed (each was waited for)
+    tc::tmem_fence_before();
+    named_bar_sync(1, 32 * kI8Cons);
+    tc::tmem_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(s_tmem), "r"(256u) : "memory");
 }
 
 }  // namespace
@@ -1040,11 +1084,9 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     int64_t rows_cap = 0;
     for (int j = 0; j < njobs; j++) rows_cap += (ws[j]->out + nrg - 1) / nrg;
     const bool x4 = M > 2;  // three or four tokens: activations in shared memory, per-stage sums
-    if (x4) {
+    if (x4) {  // per-stage partial table, then the ring (the activations live in TMEM)
         p.pr_off = kI8Bar;
-        p.b_off = (uint32_t)((p.pr_off + 2 * kI8Rows * kI8Cons * 4 * 4 + 127) & ~127u);
-        p.bstride = (uint32_t)(p.nsb * 256 + 32);
-        p.ring_off = (uint32_t)((p.b_off + 12 * (int64_t)p.bstride + 127) & ~(int64_t)127);
+        p.ring_off = (uint32_t)((p.pr_off + 2 * kI8Rows * kI8Cons * 4 * 4 + 127) & ~127u);
     } else {
         const int64_t red_bytes = rows_cap * kI8Cons * M * 4;
         p.red_off = kI8Bar;
