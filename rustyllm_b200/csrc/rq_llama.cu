@@ -114,6 +114,27 @@ __device__ __forceinline__ void pdl_enter() {
 
 // x[t][:] = f32(embed[tokens[t]][:])  (Embedding::forward over F16 weights
 // dequantized to f32 by GgufLayer::tensor)
+// The RMSNorm staging of PipeRms as a kernel (used when a tensor-parallel
+// o / down projection falls back to the separate all-reduce): thread b
+// stages x * w over block b and stores the block's sum of squares, the
+// epilogue's arithmetic.
+__global__ void rms_stage_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t H,
+                                 int8_t* __restrict__ planes, float4* __restrict__ stats, float* __restrict__ ss) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= H / 32) return;
+    float v[32], s2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 32; k++) {
+        const float xv = x[32 * b + k];
+        s2 = fmaf(xv, xv, s2);
+        v[k] = xv * w[32 * b + k];
+    }
+    stage_block(v, 0, b, H, planes, stats);
+    ss[b] = s2;
+}
+
 __global__ void embed_kernel(const __half* __restrict__ emb, const int32_t* __restrict__ tokens,
                              int64_t T, int64_t hidden, int64_t vocab, float* __restrict__ x) {
     pdl_enter();
@@ -537,7 +558,7 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st, co
         float* y = m->x;
         const float* add = m->R == 0 ? m->x : nullptr;
         const int rc = launch_matvec_pipe(w1, &xq, &y, 1, m->ctx->sm_count, st, m->derr, &add, &ar, nullptr,
-                                          nullptr, nullptr, next_hint(m));
+                                          nullptr, nullptr, next_hint(m), rms);
         if (rc != kPipeNotFusable) return rc;
     }
     float* y1[1] = {m->part};
@@ -546,6 +567,17 @@ int row_parallel(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st, co
                                          nullptr, nullptr, next_hint(m))
                     : run_linears(m, 1, w1, T, y1, a1, st);
     if (!rc) rc = tp_allreduce(m->ctx, m->part, m->x, T * m->cfg.hidden, 0, 0, st);
+    if (!rc && rms) {  // the staging the fused epilogue would have done
+        const float* x = m->x;
+        const float* wr = rms->w;
+        int64_t H = m->cfg.hidden;
+        int8_t* planes = rms->xq.planes;
+        float4* stats = rms->xq.stats;
+        float* ss = rms->ss;
+        void* args[] = {&x, &wr, &H, &planes, &stats, &ss};
+        rc = launch_simple((const void*)rms_stage_kernel, dim3((unsigned)((H / 32 + 127) / 128)), dim3(128), 0, st,
+                           args, "rms staging kernel");
+    }
     return rc;
 }
 
@@ -557,8 +589,9 @@ bool swiglu_in_epilogue(const rq_llama* m, const rq_weight* gate, const rq_weigh
     return T == 1 && pipe_supported(gate) && pipe_supported(up) && gate->out == up->out && m->I_l % 32 == 0;
 }
 
-// Decode on one rank with every linear of layer l on the pipeline: the o
-// and down matvecs stage the next RMSNorm's input in their epilogue
+// Decode with every linear of layer l on the pipeline: the o and down
+// matvecs (after their all-reduce under tensor parallelism, each rank
+// staging its own copy) stage the next RMSNorm's input in their epilogue
 // (PipeRms) and the q/k/v and gate/up matvecs divide by its RMS
 // (PipeRmsIn), so no staging kernel runs between them (RQ_RMS_EPILOGUE=0
 // restores the staging kernels).
@@ -571,8 +604,7 @@ bool rms_epilogue_enabled() {
     return on == 1;
 }
 bool rms_in_epilogue(const rq_llama* m, int64_t l, int64_t T) {
-    if (T != 1 || m->W != 1 || m->cfg.hidden % 32 || l < 0 || l >= m->cfg.n_layers || !rms_epilogue_enabled())
-        return false;
+    if (T != 1 || m->cfg.hidden % 32 || l < 0 || l >= m->cfg.n_layers || !rms_epilogue_enabled()) return false;
     const rq_llama::Layer& L = m->layers[(size_t)l];
     for (int i = 0; i < 7; i++)
         if (!pipe_supported(L.w[i])) return false;

@@ -396,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_pipe_kernel(const PipeParams p
     __syncthreads();
     if (p.fuse) {
         allreduce_rows(p, red);
+        if (p.rms) rms_blocks(p);  // every rank holds the summed rows: each stages its own copy
         return;
     }
     if (p.cmb) {
@@ -526,7 +527,7 @@ int launch_matvec_pipe(const rq_weight* const* ws, const XQ* xqs, float* const* 
     p.rms = 0;
     p.rsi_on = 0;
     if (rms) {
-        if (njobs != 1 || ar || cmb || sw || w0->out % 32 || !rms->cnt || !rms->ss || !rms->w)
+        if (njobs != 1 || cmb || sw || w0->out % 32 || !rms->cnt || !rms->ss || !rms->w)
             return set_error(RQ_ERR_INVALID, "matvec pipeline: RMSNorm staging needs one job of whole blocks");
         p.rms = 1;
         p.rm = *rms;
