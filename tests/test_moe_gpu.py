@@ -113,12 +113,12 @@ def mixtral_layer(oracle, rq_ctx):
             w.free()
 
 
-@pytest.mark.parametrize("T", [1, 16, 512])
+@pytest.mark.parametrize("T", [1, 8, 16, 512])
 def test_mixtral_geometry_matches_oracle(oracle, mixtral_layer, T):
     """Routing ids and permutation bit-exact and outputs within 1e-4 at the
-    configured Mixtral shapes: T=1 (two M=1 experts), T=16 (about 4 tokens
-    per expert: mma.sync tiles and M=1 jobs), T=512 (about 128 per expert:
-    tcgen05 tiles)."""
+    configured Mixtral shapes: T=1 (two M=1 experts), T=8 and T=16 (about 2
+    and 4 tokens per expert: mma.sync tiles and M=1 jobs), T=512 (about 128
+    per expert: tcgen05 tiles)."""
     from rustyllm_b200.mixtral import SparseMoe
     wr, blocks, experts = mixtral_layer
     moe = SparseMoe(wr, experts, top_k=2)
