@@ -827,7 +827,7 @@ def decode_70b(device: int, pk, new_tokens: int = 16, prompt_len: int = 20, pg=N
     # the current position, cache rolled back after each): their cost next
     # to one decode step sets the acceptance a draft model must reach
     verify_ms = {}
-    for kp1 in (2, 3, 4, 5, 9):
+    for kp1 in (2, 3, 4, 5, 8, 9):
         ids = np.array(toks[:kp1] + [0] * max(0, kp1 - len(toks)), dtype=np.int32)[:kp1]
         model.forward_all(ids, pos)
         model.truncate_caches(pos)

@@ -201,12 +201,12 @@ int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles) {
 // Q4_0 from M = 5: launches of two to four rows on the int8 kernels over
 // one staging (a weight pass per launch instead of per row)
 bool q40_row_groups(const rq_weight* w, int64_t M) {
-    return M > 4 && w->type == RQ_Q4_0 && mm_i8_supported(w, 4);
+    return M > 8 && w->type == RQ_Q4_0 && mm_i8_supported(w, 8);
 }
 
 size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
     if (mm_i8_supported(w, M)) return xq2_bytes(M, w->in) + 256 + mm_i8_scratch_floats(w, M) * sizeof(float);
-    if (q40_row_groups(w, M)) return xq2_bytes(M, w->in) + 256 + mm_i8_scratch_floats(w, 4) * sizeof(float);
+    if (q40_row_groups(w, M)) return xq2_bytes(M, w->in) + 256 + mm_i8_scratch_floats(w, 8) * sizeof(float);
     const bool small_m = (M >= kMinTensorM && mm_small_supported(w)) || q3k_tensor_m(w, M);
     return small_m ? xh_bytes(M, w->in) : xq_bytes(M, w->in);
 }
@@ -217,10 +217,10 @@ size_t small_m_staging_bytes(const rq_weight* w, int64_t M) {
 // the split-K tcgen05 kernel, one pass over the weights; M = 4..8 and
 // 17..23: one mma.sync pass per 8 rows; M = 2..4 (Q4_K, in <= 8192): the
 // int8 tensor-core kernel, one pass; the other M = 2, 3 shapes: the M=1
-// pipeline once per row is faster (it streams at ~5 TB/s).  Q3_K: M = 2..4
-// on the int8 kernels, from M = kQ3TensorMinM the tcgen05 kernel, one pass
-// each (M = 5: a pass per row).  Q4_0: M = 2..4 on the int8 kernels, above
-// that one int8 launch per group of 2..4 rows.
+// pipeline once per row is faster (it streams at ~5 TB/s).  M = 2..8 of
+// Q4_K, Q3_K and Q4_0 run the int8 kernels first; Q3_K from M = 9 the
+// tcgen05 kernel; Q4_0 above eight rows one int8 launch per group of 5..8
+// rows.
 int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, int64_t M, cudaStream_t st) {
     uint8_t* ws = (uint8_t*)ctx->ws;
     int rc;
@@ -238,11 +238,11 @@ int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, i
         if (!rc) rc = launch_mm_i8(&w, &yd, 1, M, q, ctx->sm_count, st, ctx->derr, nullptr, part, ctx->i8_cnt);
         return rc;
     }
-    if (q40_row_groups(w, M)) {  // ceil(M / 4) groups of 2..4 rows, sizes as even as possible
+    if (q40_row_groups(w, M)) {  // ceil(M / 8) groups of 5..8 rows, sizes as even as possible
         const XQ2 q = xq2_at(ws, M, w->in);
         float* part = (float*)(ws + ((xq2_bytes(M, w->in) + 255) & ~(size_t)255));
         rc = launch_xq2_stage(xd, M, w->in, q, st);
-        const int64_t n = (M + 3) / 4, nsb = w->in / 256;
+        const int64_t n = (M + 7) / 8, nsb = w->in / 256;
         for (int64_t g = 0, m0 = 0; g < n && !rc; g++) {
             const int64_t rows = M / n + (g < M % n ? 1 : 0);
             XQ2 qg = q;

@@ -340,10 +340,11 @@ int launch_mm_skinny(rq_ctx* ctx, const MMJobDesc* jobs, int njobs, XH xh, int64
 // grow ctx's split-K scratch to floats / tiles (never during stream capture)
 int ensure_skinny_scratch(rq_ctx* ctx, size_t floats, int tiles);
 bool mm_tc_supported(const rq_weight* w);
-// Q3_K rows from which one tcgen05 pass beats a pipeline pass per row
+// Q3_K rows from which one tcgen05 pass beats a pipeline pass per row (the
+// int8 kernels take precedence where they take the shape)
 constexpr int64_t kQ3TensorMinM = 6;
 inline bool q3k_tensor_m(const rq_weight* w, int64_t M) {
-    return M >= kQ3TensorMinM && w->type == RQ_Q3_K && mm_tc_supported(w);
+    return M >= kQ3TensorMinM && w->type == RQ_Q3_K && mm_tc_supported(w) && !mm_i8_supported(w, M);
 }
 int launch_mm_tc(const MMJobDesc* jobs, int njobs, XH xh, int64_t rows, int sm_count, cudaStream_t st,
                  int* err = nullptr);

@@ -71,7 +71,7 @@ struct rq_llama {
     float* rss;     // [H / 32] its block sums of squares
     int* rcnt;      // [H / 32] its arrival counters (zero between launches)
     rq::PipeNext nx{};  // L2 prefetch hint for the decode matvec being launched (nx.n = 0: none)
-    float* i8part;      // [4][4][hidden] split-K partial rows of the int8 down projection (T = 2..4)
+    float* i8part;      // [4][8][hidden] split-K partial rows of the int8 down projection (T = 2..8)
     int* i8cnt;         // [256] its arrival counters (zero between launches)
     rq::XH xh;      // the same rows staged as f16 hi / lo (tensor-core prefill)
     // device state
@@ -478,7 +478,7 @@ const PipeNext* next_hint(const rq_llama* m) { return m->nx.n > 0 ? &m->nx : nul
 // run the linears the int8 tensor-core kernel takes in one weight pass
 // (rq_mm_i8.cu), its activation staging in m->xq's buffer.
 bool i8_ok(const rq_weight* const* ws, int n, int64_t T) {
-    if (T < 2 || T > 4) return false;
+    if (T < 2 || T > 8) return false;
     for (int i = 0; i < n; i++)
         if (!mm_i8_supported(ws[i], T)) return false;
     return true;
@@ -672,7 +672,7 @@ bool tensor_prefill(const rq_llama* m, int64_t T, int64_t l) {
         if (!mm_small_supported(w) && !q3k_tensor_m(w, T)) return false;
         all_i8 = all_i8 && mm_i8_supported(w, T);
     }
-    return !all_i8;  // four tokens: the int8 kernels where every linear takes them
+    return !all_i8;  // up to eight tokens: the int8 kernels where every linear takes them
 }
 
 // One forward over the T tokens in m->tokens at device position *m->pos.
@@ -1083,7 +1083,7 @@ int rq_llama_create(rq_ctx* ctx, const rq_llama_config* cfg, rq_llama** out) {
     uint8_t* xqdbuf = nullptr;
     if (!rc) rc = dalloc(m, &xqbuf, xq_bytes(T, maxin));
     if (!rc) rc = dalloc(m, &xqdbuf, xq_bytes(1, I));
-    if (!rc) rc = dalloc(m, &m->i8part, (size_t)(4 * 4 * H));
+    if (!rc) rc = dalloc(m, &m->i8part, (size_t)(4 * 8 * H));
     if (!rc) rc = dalloc(m, &m->i8cnt, 256);
     if (!rc) rc = cuda_error(cudaMemset(m->i8cnt, 0, 256 * sizeof(int)), "counter reset");
     if (!rc) rc = dalloc(m, &m->swcnt, (size_t)(I / 32 + 1));

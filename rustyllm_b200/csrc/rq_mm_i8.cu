@@ -1002,6 +1002,413 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(s_tmem), "r"(256u) : "memory");
 }
 
+
+// ------------------------------------------------- five to eight tokens
+//
+// The same data path and A operand; B has 24 columns in three column groups
+// of 8, group p = activation plane p, column m = token m (absent tokens are
+// zeros), so every sub-block takes three MMAs and a lane's C columns 2t,
+// 2t+1 are tokens 2t, 2t+1 of every plane.  The lane's B words (per
+// 32-element sub-block: two words for each of the three groups) live in
+// TMEM: 512 columns, 256 per warp of a lane quarter, 64 per super-block
+// (two halves of four sub-blocks, 24 words each, at 32-column offsets),
+// filled once and read back with one 16- and one 8-column tcgen05.ld per
+// half super-block.  The eight K-slice partials of a stage's rows are summed
+// in slice order through a double-buffered table [row][slice][token] after
+// a barrier of the consumer warps, and y is written per stage.
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16p(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16p(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+constexpr int kI8x8Cols = 512;  // TMEM columns of the eight-token form
+
+template <int FMT>
+__global__ void __launch_bounds__(kI8Threads, 1) mm_i8x8_kernel(const I8Params p) {
+    constexpr bool Q3 = FMT == kI8Q3K, Q40 = FMT == kI8Q40;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* ring = smem + p.ring_off;
+    float* pr = reinterpret_cast<float*>(smem + p.pr_off);  // [2][kI8Rows][kI8Cons][8]
+    __shared__ int s_abort;
+    __shared__ uint32_t s_tmem;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t full0 = smem_u32(smem), empty0 = full0 + 8 * 16;
+    const int ksi = blockIdx.x % p.ks, rgi = blockIdx.x / p.ks, nrg = gridDim.x / p.ks;
+    const int kb0 = ksi * p.nsb;
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (warp == 0) {
+        if (lane < p.nstage) {
+            mbar_init(full0 + 8 * lane, 1);
+            mbar_init(empty0 + 8 * lane, kI8Cons);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x == 0) s_abort = 0;
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"((uint32_t)kI8x8Cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc::tmem_fence_before();
+    __syncthreads();
+    tc::tmem_fence_after();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            int it = 0, slot = 0, use = 0;
+            bool ok = true;
+            for (int j = 0; j < p.njobs && ok; j++) {
+                const I8Job& jb = p.jobs[j];
+                int64_t rb;
+                int nrows;
+                i8_rows(jb, rgi, nrg, &rb, &nrows);
+                for (int r0 = 0; r0 < nrows; r0 += p.RS, it++, slot = slot + 1 == p.nstage ? 0 : slot + 1,
+                         use += slot == 0) {
+                    if (use > 0 && !mbar_wait(empty0 + 8 * slot, (use - 1) & 1)) { ok = false; break; }
+                    const int rows = min(p.RS, nrows - r0);
+                    const uint32_t dst = smem_u32(ring) + (uint32_t)slot * p.stage_bytes;
+                    const uint32_t hdst = dst + (uint32_t)p.RS * p.qstride;
+                    mbar_expect_tx(full0 + 8 * slot, (uint32_t)rows * (p.qseg + p.hseg));
+                    for (int r = 0; r < rows; r++) {
+                        const int64_t row = rb + r0 + r;
+                        bulk_g2s(dst + (uint32_t)r * p.qstride, jb.qs + row * p.qrow + (int64_t)kb0 * 128, p.qseg,
+                                 full0 + 8 * slot, pol);
+                        bulk_g2s(hdst + (uint32_t)r * p.hstride, jb.hdr + row * p.hrow + (int64_t)kb0 * p.hsb, p.hseg,
+                                 full0 + 8 * slot, pol);
+                    }
+                }
+            }
+            for (int k = max(0, it - p.nstage); k < it; k++)
+                if (!mbar_wait(full0 + 8 * (k % p.nstage), (k / p.nstage) & 1)) ok = false;
+            if (!ok && p.err) atomicExch(p.err, 1);
+        }
+        return;
+    }
+    const int w = warp - 1, ct = threadIdx.x - 32;
+    const int g = lane >> 2, t = lane & 3;
+    const int M = p.M;
+    const int sb0 = w * p.nsb / kI8Cons, nsbw = (w + 1) * p.nsb / kI8Cons - sb0;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // B column g of group pl: token g of plane pl, XQ2 row 3 g + pl
+    const bool vb = g < M;
+    const uint32_t tb = s_tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (warp >= 5 ? 256u : 0u);
+    {
+        constexpr int lo_off = (Q3 || Q40) ? 4 : 8;
+        const int8_t* src = p.xq.planes + (int64_t)(vb ? 3 * g : 0) * p.in + (int64_t)kb0 * 256 + lo_off * t;
+#pragma unroll
+        for (int s = 0; s < kI8MaxSB; s++) {
+            if (s < nsbw) {  // warp-uniform: tcgen05.st is warp-wide
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    uint32_t v[24];
+#pragma unroll
+                    for (int sq = 0; sq < 4; sq++) {
+                        const int sub = 4 * hf + sq;
+                        const int64_t ko = (int64_t)((sb0 + s) * 8 + sub) * 32;
+#pragma unroll
+                        for (int pl = 0; pl < 3; pl++) {
+                            uint2 b = make_uint2(0u, 0u);
+                            if (vb) {
+                                const int8_t* sp = src + (int64_t)pl * p.in + ko;
+                                if constexpr (Q3 || Q40)
+                                    b = make_uint2(*reinterpret_cast<const uint32_t*>(sp),
+                                                   *reinterpret_cast<const uint32_t*>(sp + 16));
+                                else
+                                    b = *reinterpret_cast<const uint2*>(sp);
+                            }
+                            v[6 * sq + 2 * pl] = b.x;
+                            v[6 * sq + 2 * pl + 1] = b.y;
+                        }
+                    }
+                    const uint32_t col = tb + 64u * (uint32_t)s + 32u * (uint32_t)hf;
+                    tmem_st16p(col, v);
+                    tmem_st8u(col + 16u, v + 16);
+                }
+            }
+        }
+        tc::tmem_wait_st();
+    }
+    // f32 factors of this lane's C columns: token 2t + c of plane pl ->
+    // sx[token][sb] * plane weight (zero for absent tokens), read per
+    // super-block; Q3_K's A carries 32 (q - 4), folded in (exact)
+    const float kq = Q3 ? 0.03125f : 1.0f;
+    const float pw[3] = {65536.0f * kq, 256.0f * kq, 1.0f * kq};
+    const bool tv0 = 2 * t < M, tv1 = 2 * t + 1 < M;
+    const float* sx0 = p.xq.sx + (int64_t)(tv0 ? 2 * t : 0) * p.nsbr + kb0;
+    const float* sx1 = p.xq.sx + (int64_t)(tv1 ? 2 * t + 1 : 0) * p.nsbr + kb0;
+    const float* bs0 = p.xq.bsum + (int64_t)(tv0 ? 2 * t : 0) * (p.in / 32) + (int64_t)kb0 * 8;
+    const float* bs1 = p.xq.bsum + (int64_t)(tv1 ? 2 * t + 1 : 0) * (p.in / 32) + (int64_t)kb0 * 8;
+    int slot = 0, use = 0, par = 0;
+    for (int j = 0; j < p.njobs; j++) {
+        const I8Job& jb = p.jobs[j];
+        int64_t rb;
+        int nrows;
+        i8_rows(jb, rgi, nrg, &rb, &nrows);
+        for (int r0 = 0; r0 < nrows; r0 += p.RS, slot = slot + 1 == p.nstage ? 0 : slot + 1, use += slot == 0,
+                 par ^= 1) {
+            if (!*(volatile int*)&s_abort && !mbar_wait(full0 + 8 * slot, use & 1)) {
+                if (lane == 0 && p.err) atomicExch(p.err, 1);
+                *(volatile int*)&s_abort = 1;
+            }
+            const bool live = __all_sync(0xffffffffu, !*(volatile int*)&s_abort);  // warp-uniform
+            const uint8_t* sq = ring + (size_t)slot * p.stage_bytes;
+            const uint8_t* sh = sq + (size_t)p.RS * p.qstride;
+            const int rows = min(p.RS, nrows - r0);
+            const int rA = min(g, rows - 1), rB = min(g + 8, rows - 1);
+            float acc[3][4];
+#pragma unroll
+            for (int pl = 0; pl < 3; pl++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[pl][i] = 0.0f;
+            float mn[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};  // min / offset term: [row g, g+8][token 2t + c]
+#pragma unroll
+            for (int s = 0; s < kI8MaxSB; s++) {
+                if (live && s < nsbw) {
+                    const int sb = sb0 + s;
+                    const float x0 = tv0 ? __ldg(sx0 + sb) : 0.0f, x1 = tv1 ? __ldg(sx1 + sb) : 0.0f;
+                    float cf[3][2];
+#pragma unroll
+                    for (int pl = 0; pl < 3; pl++) {
+                        cf[pl][0] = x0 * pw[pl];
+                        cf[pl][1] = x1 * pw[pl];
+                    }
+                    const uint32_t colb = tb + 64u * (uint32_t)s;
+                    uint32_t bq[24];  // B words of four sub-blocks: [sub][plane][word]
+                    int a[3][4];
+#pragma unroll
+                    for (int pl = 0; pl < 3; pl++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) a[pl][i] = 0;
+                    if constexpr (Q3) {
+                        const uint32_t* hg4 =
+                            reinterpret_cast<const uint32_t*>(sh + (size_t)rA * p.hstride + sb * 20);
+                        const uint32_t* h84 =
+                            reinterpret_cast<const uint32_t*>(sh + (size_t)rB * p.hstride + sb * 20);
+                        const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 4 * t;
+                        const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 4 * t;
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            const uint32_t wq[4] = {*reinterpret_cast<const uint32_t*>(qg + 32 * c),
+                                                    *reinterpret_cast<const uint32_t*>(qg + 32 * c + 16),
+                                                    *reinterpret_cast<const uint32_t*>(q8 + 32 * c),
+                                                    *reinterpret_cast<const uint32_t*>(q8 + 32 * c + 16)};
+                            const uint32_t scg = hg4[c], sc8 = h84[c];
+                            if (c == 0 || c == 2) {  // B of 32-element chunks 2c .. 2c+3
+                                tmem_ld16p(colb + 16u * (uint32_t)c, bq);
+                                tmem_ld8(colb + 16u * (uint32_t)c + 16u, bq + 16);
+                                tc::tmem_wait_ld();
+                            }
+#pragma unroll
+                            for (int q = 0; q < 4; q++) {
+                                const uint32_t ag = q < 2 ? q3_lo(wq[q & 1]) : q3_hi(wq[q & 1]);
+                                const uint32_t a8 = q < 2 ? q3_lo(wq[2 + (q & 1)]) : q3_hi(wq[2 + (q & 1)]);
+                                const int cj = (2 * c + (q >> 1)) & 3;
+                                const int sg = (int)(int8_t)(uint8_t)(scg >> (8 * q));
+                                const int s8 = (int)(int8_t)(uint8_t)(sc8 >> (8 * q));
+#pragma unroll
+                                for (int pl = 0; pl < 3; pl++) {
+                                    int d[4];
+                                    mma_s8s8_k16(d, ag, a8, bq[6 * cj + 2 * pl + (q & 1)]);
+                                    a[pl][0] += d[0] * sg; a[pl][1] += d[1] * sg;
+                                    a[pl][2] += d[2] * s8; a[pl][3] += d[3] * s8;
+                                }
+                            }
+                        }
+                        const float dg = __half2float(*reinterpret_cast<const __half*>(hg4 + 4));
+                        const float d8 = __half2float(*reinterpret_cast<const __half*>(h84 + 4));
+#pragma unroll
+                        for (int pl = 0; pl < 3; pl++) {
+                            acc[pl][0] = fmaf((float)a[pl][0], dg * cf[pl][0], acc[pl][0]);
+                            acc[pl][1] = fmaf((float)a[pl][1], dg * cf[pl][1], acc[pl][1]);
+                            acc[pl][2] = fmaf((float)a[pl][2], d8 * cf[pl][0], acc[pl][2]);
+                            acc[pl][3] = fmaf((float)a[pl][3], d8 * cf[pl][1], acc[pl][3]);
+                        }
+                    } else if constexpr (Q40) {
+                        const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
+                        const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
+                        const uint32_t dgw[4] = {hg.x, hg.y, hg.z, hg.w}, d8w[4] = {h8.x, h8.y, h8.z, h8.w};
+                        const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 4 * t;
+                        const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 4 * t;
+#pragma unroll
+                        for (int jb8 = 0; jb8 < 8; jb8++) {
+                            const uint32_t wg = *reinterpret_cast<const uint32_t*>(qg + 16 * jb8);
+                            const uint32_t w8 = *reinterpret_cast<const uint32_t*>(q8 + 16 * jb8);
+                            const uint32_t am[4] = {wg & 0x0F0F0F0Fu, w8 & 0x0F0F0F0Fu, (wg >> 4) & 0x0F0F0F0Fu,
+                                                    (w8 >> 4) & 0x0F0F0F0Fu};
+                            if (jb8 == 0 || jb8 == 4) {  // B of blocks jb8 .. jb8+3
+                                tmem_ld16p(colb + 8u * (uint32_t)jb8, bq);
+                                tmem_ld8(colb + 8u * (uint32_t)jb8 + 16u, bq + 16);
+                                tc::tmem_wait_ld();
+                            }
+                            const float2 dgp = __half22float2(*reinterpret_cast<const __half2*>(&dgw[jb8 >> 1]));
+                            const float2 d8p = __half22float2(*reinterpret_cast<const __half2*>(&d8w[jb8 >> 1]));
+                            const float dg = (jb8 & 1) ? dgp.y : dgp.x, d8 = (jb8 & 1) ? d8p.y : d8p.x;
+                            const int jj = jb8 & 3;
+#pragma unroll
+                            for (int pl = 0; pl < 3; pl++) {
+                                int d[4];
+                                mma_u8s8(d, am, bq[6 * jj + 2 * pl], bq[6 * jj + 2 * pl + 1]);
+                                acc[pl][0] = fmaf(i2f_small(d[0]), dg * cf[pl][0], acc[pl][0]);
+                                acc[pl][1] = fmaf(i2f_small(d[1]), dg * cf[pl][1], acc[pl][1]);
+                                acc[pl][2] = fmaf(i2f_small(d[2]), d8 * cf[pl][0], acc[pl][2]);
+                                acc[pl][3] = fmaf(i2f_small(d[3]), d8 * cf[pl][1], acc[pl][3]);
+                            }
+                            // Q4_0: w = d (q - 8), the offset through the block sums
+                            const float b0v = tv0 ? __ldg(bs0 + (int64_t)sb * 8 + jb8) : 0.0f;
+                            const float b1v = tv1 ? __ldg(bs1 + (int64_t)sb * 8 + jb8) : 0.0f;
+                            mn[0][0] = fmaf(8.0f * dg, b0v, mn[0][0]);
+                            mn[0][1] = fmaf(8.0f * dg, b1v, mn[0][1]);
+                            mn[1][0] = fmaf(8.0f * d8, b0v, mn[1][0]);
+                            mn[1][1] = fmaf(8.0f * d8, b1v, mn[1][1]);
+                        }
+                    } else {
+                        const uint4 hg = *reinterpret_cast<const uint4*>(sh + (size_t)rA * p.hstride + sb * 16);
+                        const uint4 h8 = *reinterpret_cast<const uint4*>(sh + (size_t)rB * p.hstride + sb * 16);
+                        const uint32_t scg0 = hg.y & 0x3F3F3F3Fu, mg0 = hg.z & 0x3F3F3F3Fu;
+                        const uint32_t scg1 = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
+                        const uint32_t mg1 = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
+                        const uint32_t sc80 = h8.y & 0x3F3F3F3Fu, m80 = h8.z & 0x3F3F3F3Fu;
+                        const uint32_t sc81 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
+                        const uint32_t m81 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
+                        const uint8_t* qg = sq + (size_t)rA * p.qstride + sb * 128 + 8 * t;
+                        const uint8_t* q8 = sq + (size_t)rB * p.qstride + sb * 128 + 8 * t;
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
+                            const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
+                            if (c == 0 || c == 2) {  // B of sub-blocks 2c .. 2c+3
+                                tmem_ld16p(colb + 16u * (uint32_t)c, bq);
+                                tmem_ld8(colb + 16u * (uint32_t)c + 16u, bq + 16);
+                                tc::tmem_wait_ld();
+                            }
+                            const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
+                                                     w8.y & 0x0F0F0F0Fu};
+                            const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
+                                                     (wg.y >> 4) & 0x0F0F0F0Fu, (w8.y >> 4) & 0x0F0F0F0Fu};
+#pragma unroll
+                            for (int h = 0; h < 2; h++) {
+                                const int sub = (2 * c + h) & 3;  // within the loaded half
+                                const uint32_t wgs = c < 2 ? scg0 : scg1, w8s = c < 2 ? sc80 : sc81;
+                                const int byte = (2 * c + h) & 3;
+                                const int sg = (int)__byte_perm(wgs, 0u, 0x4440u + byte);
+                                const int s8 = (int)__byte_perm(w8s, 0u, 0x4440u + byte);
+#pragma unroll
+                                for (int pl = 0; pl < 3; pl++) {
+                                    int d[4];
+                                    if (h == 0)
+                                        mma_u8s8(d, alo, bq[6 * sub + 2 * pl], bq[6 * sub + 2 * pl + 1]);
+                                    else
+                                        mma_u8s8(d, ahi, bq[6 * sub + 2 * pl], bq[6 * sub + 2 * pl + 1]);
+                                    a[pl][0] += d[0] * sg; a[pl][1] += d[1] * sg;
+                                    a[pl][2] += d[2] * s8; a[pl][3] += d[3] * s8;
+                                }
+                            }
+                        }
+                        const float2 ddg = __half22float2(*reinterpret_cast<const __half2*>(&hg.x));
+                        const float2 dd8 = __half22float2(*reinterpret_cast<const __half2*>(&h8.x));
+#pragma unroll
+                        for (int pl = 0; pl < 3; pl++) {
+                            acc[pl][0] = fmaf((float)a[pl][0], ddg.x * cf[pl][0], acc[pl][0]);
+                            acc[pl][1] = fmaf((float)a[pl][1], ddg.x * cf[pl][1], acc[pl][1]);
+                            acc[pl][2] = fmaf((float)a[pl][2], dd8.x * cf[pl][0], acc[pl][2]);
+                            acc[pl][3] = fmaf((float)a[pl][3], dd8.x * cf[pl][1], acc[pl][3]);
+                        }
+                        // min term of tokens 2t, 2t+1: dmin * sum_j m_j bsum_j
+                        float4 b0a = make_float4(0.0f, 0.0f, 0.0f, 0.0f), b0b = b0a, b1a = b0a, b1b = b0a;
+                        if (tv0) {
+                            b0a = __ldg(reinterpret_cast<const float4*>(bs0 + (int64_t)sb * 8));
+                            b0b = __ldg(reinterpret_cast<const float4*>(bs0 + (int64_t)sb * 8 + 4));
+                        }
+                        if (tv1) {
+                            b1a = __ldg(reinterpret_cast<const float4*>(bs1 + (int64_t)sb * 8));
+                            b1b = __ldg(reinterpret_cast<const float4*>(bs1 + (int64_t)sb * 8 + 4));
+                        }
+                        const float bv0[8] = {b0a.x, b0a.y, b0a.z, b0a.w, b0b.x, b0b.y, b0b.z, b0b.w};
+                        const float bv1[8] = {b1a.x, b1a.y, b1a.z, b1a.w, b1b.x, b1b.y, b1b.z, b1b.w};
+                        float sg0 = 0.0f, sg1 = 0.0f, s80 = 0.0f, s81 = 0.0f;
+#pragma unroll
+                        for (int jj = 0; jj < 8; jj++) {
+                            const uint32_t mw = jj < 4 ? mg0 : mg1, mw8 = jj < 4 ? m80 : m81;
+                            const float fg =
+                                __uint_as_float(__byte_perm(mw, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                            const float f8 =
+                                __uint_as_float(__byte_perm(mw8, 0x4B000000u, 0x7650u + (jj & 3))) - 8388608.0f;
+                            sg0 = fmaf(fg, bv0[jj], sg0);
+                            sg1 = fmaf(fg, bv1[jj], sg1);
+                            s80 = fmaf(f8, bv0[jj], s80);
+                            s81 = fmaf(f8, bv1[jj], s81);
+                        }
+                        mn[0][0] = fmaf(ddg.y, sg0, mn[0][0]);
+                        mn[0][1] = fmaf(ddg.y, sg1, mn[0][1]);
+                        mn[1][0] = fmaf(dd8.y, s80, mn[1][0]);
+                        mn[1][1] = fmaf(dd8.y, s81, mn[1][1]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty0 + 8 * slot);
+            // tokens 2t, 2t+1 of rows g, g+8: the three planes summed
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[i] = acc[0][i] + acc[1][i] + acc[2][i];
+            float* buf = pr + par * (kI8Rows * kI8Cons * 8);
+            if (g < rows) {
+                if (tv0) buf[(g * kI8Cons + w) * 8 + 2 * t] = v[0] - mn[0][0];
+                if (tv1) buf[(g * kI8Cons + w) * 8 + 2 * t + 1] = v[1] - mn[0][1];
+            }
+            if (g + 8 < rows) {
+                if (tv0) buf[((g + 8) * kI8Cons + w) * 8 + 2 * t] = v[2] - mn[1][0];
+                if (tv1) buf[((g + 8) * kI8Cons + w) * 8 + 2 * t + 1] = v[3] - mn[1][1];
+            }
+            named_bar_sync(1, 32 * kI8Cons);
+            if (ct < rows * M && !*(volatile int*)&s_abort) {
+                const int r = ct / M, m = ct % M;
+                float sum = 0.0f;
+                for (int s = 0; s < kI8Cons; s++) sum += buf[(r * kI8Cons + s) * 8 + m];
+                const int64_t o = (int64_t)m * jb.out + rb + r0 + r;
+                if (p.ks > 1)
+                    p.part[(int64_t)ksi * M * jb.out + o] = sum;
+                else
+                    jb.y[o] = jb.add ? sum + jb.add[o] : sum;
+            }
+        }
+    }
+    if (p.ks > 1) {
+        __shared__ int s_last;
+        i8_ksplit_finish(p, rgi, nrg, ct, 32 * kI8Cons, 1, &s_last);
+    }
+    tc::tmem_fence_before();
+    named_bar_sync(1, 32 * kI8Cons);
+    tc::tmem_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(s_tmem), "r"((uint32_t)kI8x8Cols)
+                     : "memory");
+}
+
 }  // namespace
 
 // K-splits for a row of nsb super-blocks: 1 when each of the 8 K-slice warps
@@ -1009,7 +1416,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
 static int i8_ksplits(int64_t nsb) { return nsb <= (int64_t)kI8Cons * kI8MaxSB ? 1 : 4; }
 
 bool mm_i8_supported(const rq_weight* w, int64_t M) {
-    if ((w->type != RQ_Q4_K && w->type != RQ_Q3_K && w->type != RQ_Q4_0) || M < 2 || M > 4 || w->in % 256)
+    if ((w->type != RQ_Q4_K && w->type != RQ_Q3_K && w->type != RQ_Q4_0) || M < 2 || M > 8 || w->in % 256)
         return false;
     const int64_t nsb = w->in / 256;
     const int ks = i8_ksplits(nsb);
@@ -1083,10 +1490,12 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     if (p.ks > 1 && nrg > kI8MaxRowGroups) return set_error(RQ_ERR_UNSUPPORTED, "int8 matmul: %d row groups", nrg);
     int64_t rows_cap = 0;
     for (int j = 0; j < njobs; j++) rows_cap += (ws[j]->out + nrg - 1) / nrg;
-    const bool x4 = M > 2;  // three or four tokens: activations in shared memory, per-stage sums
-    if (x4) {  // per-stage partial table, then the ring (the activations live in TMEM)
+    // three to eight tokens: activations in TMEM, per-stage sums through a
+    // partial table [2][rows][slices][4 or 8 tokens] ahead of the ring
+    const bool x4 = M > 2, x8 = M > 4;
+    if (x4) {
         p.pr_off = kI8Bar;
-        p.ring_off = (uint32_t)((p.pr_off + 2 * kI8Rows * kI8Cons * 4 * 4 + 127) & ~127u);
+        p.ring_off = (uint32_t)((p.pr_off + 2 * kI8Rows * kI8Cons * (x8 ? 8 : 4) * 4 + 127) & ~127u);
     } else {
         const int64_t red_bytes = rows_cap * kI8Cons * M * 4;
         p.red_off = kI8Bar;
@@ -1110,10 +1519,12 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
         cudaError_t e = cudaSuccess;
-        const void* kerns[6] = {(const void*)mm_i8_kernel<kI8Q4K>,   (const void*)mm_i8_kernel<kI8Q3K>,
+        const void* kerns[9] = {(const void*)mm_i8_kernel<kI8Q4K>,   (const void*)mm_i8_kernel<kI8Q3K>,
                                 (const void*)mm_i8_kernel<kI8Q40>,   (const void*)mm_i8x4_kernel<kI8Q4K>,
-                                (const void*)mm_i8x4_kernel<kI8Q3K>, (const void*)mm_i8x4_kernel<kI8Q40>};
-        for (int k = 0; k < 6 && e == cudaSuccess; k++)
+                                (const void*)mm_i8x4_kernel<kI8Q3K>, (const void*)mm_i8x4_kernel<kI8Q40>,
+                                (const void*)mm_i8x8_kernel<kI8Q4K>, (const void*)mm_i8x8_kernel<kI8Q3K>,
+                                (const void*)mm_i8x8_kernel<kI8Q40>};
+        for (int k = 0; k < 9 && e == cudaSuccess; k++)
             e = cudaFuncSetAttribute(kerns[k], cudaFuncAttributeMaxDynamicSharedMemorySize, kI8Smem);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(int8 matmul)");
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
@@ -1130,14 +1541,17 @@ int launch_mm_i8(const rq_weight* const* ws, float* const* ys, int njobs, int64_
     cfg.numAttrs = 1;
     cudaError_t e;
     if (w0->type == RQ_Q3_K)
-        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<kI8Q3K>, p)
-               : cudaLaunchKernelEx(&cfg, mm_i8_kernel<kI8Q3K>, p);
+        e = x8 ? cudaLaunchKernelEx(&cfg, mm_i8x8_kernel<kI8Q3K>, p)
+               : x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<kI8Q3K>, p)
+                    : cudaLaunchKernelEx(&cfg, mm_i8_kernel<kI8Q3K>, p);
     else if (w0->type == RQ_Q4_0)
-        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<kI8Q40>, p)
-               : cudaLaunchKernelEx(&cfg, mm_i8_kernel<kI8Q40>, p);
+        e = x8 ? cudaLaunchKernelEx(&cfg, mm_i8x8_kernel<kI8Q40>, p)
+               : x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<kI8Q40>, p)
+                    : cudaLaunchKernelEx(&cfg, mm_i8_kernel<kI8Q40>, p);
     else
-        e = x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<kI8Q4K>, p)
-               : cudaLaunchKernelEx(&cfg, mm_i8_kernel<kI8Q4K>, p);
+        e = x8 ? cudaLaunchKernelEx(&cfg, mm_i8x8_kernel<kI8Q4K>, p)
+               : x4 ? cudaLaunchKernelEx(&cfg, mm_i8x4_kernel<kI8Q4K>, p)
+                    : cudaLaunchKernelEx(&cfg, mm_i8_kernel<kI8Q4K>, p);
     return cuda_error(e, "int8 matmul kernel");
 }
 

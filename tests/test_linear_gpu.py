@@ -96,12 +96,14 @@ def test_small_m_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
                                          (4096, 8192, 2), (150, 8192, 2), (8192, 8192, 2), (24, 8192, 3),
                                          (1040, 4096, 3), (28672, 8192, 3), (17, 2048, 4), (333, 8192, 4),
                                          (8192, 6144, 4), (8192, 28672, 2), (333, 28672, 3), (17, 28672, 4),
-                                         (1040, 10240, 2)])
+                                         (1040, 10240, 2), (17, 4096, 5), (333, 8192, 6), (8192, 8192, 7),
+                                         (28672, 8192, 8), (150, 28672, 8), (1040, 6144, 5)])
 def test_int8_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
     """Q4_K M = 2..4 runs on the int8 tensor-core kernel
     (24-bit staged activations, one weight pass): single rows, ragged
     16-row stages, fewer rows than SMs, every K-slice width; M = 3, 4 on
-    its twelve-column form (activations in shared memory); in > 8192 with K
+    its twelve-column form and M = 5..8 on the 24-column form (activations
+    in TMEM); in > 8192 with K
     split over four CTAs per row group; each row of y within 1e-4 of the
     f64-accumulated oracle."""
     from rustyllm_b200 import QWeight
@@ -168,7 +170,7 @@ def test_tcgen05_matmul_shapes(oracle, rq_ctx, out, n_in, M):
 
 @pytest.mark.parametrize("out,n_in,M", [(1, 2048, 2), (17, 4096, 2), (333, 8192, 3), (1040, 6144, 4),
                                          (8192, 8192, 2), (8192, 28672, 2), (333, 28672, 3), (17, 28672, 4),
-                                         (28672, 8192, 4), (96, 1024, 3)])
+                                         (28672, 8192, 4), (96, 1024, 3), (333, 8192, 6), (8192, 28672, 8)])
 def test_q3k_int8_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
     """Q3_K M = 2..4 runs on the int8 tensor-core kernels: one m16n8k16
     s8 x s8 MMA per 16-element sub-block with A = 32 (q - 4) made by a
@@ -193,15 +195,17 @@ def test_q3k_int8_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
 
 @pytest.mark.parametrize("out,n_in,M", [(1, 2048, 2), (17, 4096, 3), (333, 4096, 4), (4096, 4096, 2),
                                          (4096, 4096, 3), (4096, 4096, 4), (1040, 28672, 2), (150, 28672, 4),
-                                         (4096, 4096, 5), (4096, 4096, 9), (130, 8192, 16), (72, 1024, 6)])
+                                         (4096, 4096, 5), (4096, 4096, 8), (4096, 4096, 9), (130, 8192, 16),
+                                         (333, 28672, 7), (72, 1024, 6)])
 def test_q4_0_int8_tensor_core_shapes(oracle, rq_ctx, out, n_in, M):
     """Q4_0 (the ParallelQ4Linear format) at M >= 2 on the int8 tensor
     cores: one m16n8k32 per 32-element block (low nibbles = elements 0..15,
     high = 16..31, the K slots of the B fragments), its f16 scale applied to
-    the s32 tile in f32 and the -8 offset through the block sums; above four
-    rows one launch per group of 2..4 rows (5 -> 3 + 2, 9 -> 3 x 3, 16 ->
-    4 x 4); in > 8192 with K split four ways; 1024 (no whole K-slice per
-    warp) keeps a pipeline pass per row."""
+    the s32 tile in f32 and the -8 offset through the block sums; up to
+    eight rows in one launch (five to eight on the 24-column form), above
+    that one launch per group of up to eight rows (9 -> 5 + 4, 16 -> 8 + 8);
+    in > 8192 with K split four ways; 1024 (no whole K-slice per warp) keeps
+    a pipeline pass per row."""
     from rustyllm_b200 import QWeight
     from rustyllm_b200.linear import _linear
     _, blocks = make_weight(oracle, 2, out, n_in, seed=out * 3 + M)

@@ -76,13 +76,14 @@ def test_70b_geometry_verify_forward_logits(pair):
     assert amax == ref_amax[12:].tolist()
 
 
-@pytest.mark.parametrize("T", [2, 3, 4])
+@pytest.mark.parametrize("T", [2, 3, 4, 6, 8])
 def test_70b_geometry_small_verify(pair, T):
-    """forward_all over 2, 3 or 4 tokens (the verify of a one- to three-token
+    """forward_all over 2..8 tokens (the verify of a one- to seven-token
     draft): all seven linears on the int8 tensor-core kernels in one weight
     pass (two tokens: B fragments in registers; three and four: the
-    twelve-column form; down_proj, in = 28672, with K split over four CTAs
-    per row group); every position within 1e-4 of the oracle, argmax equal."""
+    twelve-column form; five to eight: the 24-column form; down_proj,
+    in = 28672, with K split over four CTAs per row group); every position
+    within 1e-4 of the oracle, argmax equal."""
     model, ref, _ = pair
     rng = np.random.default_rng(20 + T)
     prompt = rng.integers(0, CFG["vocab"], size=12).astype(np.int32)
