@@ -463,9 +463,9 @@ Q40_SMALL_M = (1, 2, 3, 4, 8, 16)
 def q40_small_m(L, ctx, stream, timed, capture, dev, g) -> dict:
     """The 4096x4096 Q4_0 linear (config 1's weight) at M rows: one
     rq_linear call, graph-replayed over 16 rotating copies (151 MB).
-    M = 2..4 run the int8 tensor-core kernels in one weight pass, larger M
-    one int8 launch per group of 2..4 rows.  GB/s counts the weight bytes
-    once per call."""
+    M = 2..8 run the int8 tensor-core kernels in one weight pass, larger M
+    one int8 launch per group of up to 8 rows.  GB/s counts the weight
+    bytes once per call."""
     import torch
     from rustyllm_b200 import QWeight
     from rustyllm_b200._lib import check
@@ -496,15 +496,16 @@ def q40_small_m(L, ctx, stream, timed, capture, dev, g) -> dict:
     for w in ws:
         w.free()
     res["note"] = ("rq_linear on the 4096x4096 Q4_0 weight, 16 rotating copies; M=1 the pipeline, "
-                   "M = 2..4 the int8 tensor-core kernels, larger M one int8 launch per 2..4 rows")
+                   "M = 2..8 the int8 tensor-core kernels, larger M one int8 launch per group of up to 8 rows")
     return res
 
 
 def q3k_small_m(L, ctx, stream, timed, capture, dev, g, pk) -> dict:
     """Q3_K matmul at the seven 70B layer shapes for a few M: one rq_linear
     call per linear, graph-replayed over 4 rotating layer copies (1.5 GB).
-    M = 2..4 runs the int8 tensor-core kernels, M >= 6 the tcgen05 kernel,
-    each in one weight pass.  GB/s counts the GGML weight bytes once."""
+    M = 2..8 runs the int8 tensor-core kernels, larger M the tcgen05
+    kernel, each in one weight pass.  GB/s counts the GGML weight bytes
+    once."""
     import torch
     from rustyllm_b200 import QWeight
     from rustyllm_b200._lib import check
@@ -536,9 +537,8 @@ def q3k_small_m(L, ctx, stream, timed, capture, dev, g, pk) -> dict:
         reps = 10
         ms = timed(lambda r: gr.replay(), reps) / (reps * N_COPIES)
         flops = 2 * M * sum(i * o for _, i, o in SHAPES)
-        kern = ("xh_stage + mm_tc_kernel<Q3_K> (tcgen05, one weight pass)" if M >= 6 else
-                "xq2_stage + mm_i8 kernels<Q3_K> (int8 mma.sync k16, one weight pass)" if M <= 4 else
-                "xquant + mv_pipe_kernel<Q3_K>, one pass per row")
+        kern = ("xq2_stage + mm_i8 kernels<Q3_K> (int8 mma.sync k16, one weight pass)" if M <= 8 else
+                "xh_stage + mm_tc_kernel<Q3_K> (tcgen05, one weight pass)")
         res[str(M)] = {"ms_per_layer": round(ms, 4),
                        "gbs": round((nbytes_w + 4 * M * sum(i + o for _, i, o in SHAPES)) / (ms / 1e3) / 1e9, 1),
                        "tflops": round(flops / (ms / 1e3) / 1e12, 1), "kernel": kern}
@@ -582,9 +582,10 @@ def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g, pk, host_bloc
         nbytes = sum(Q4K_BYTES(i, o) + 4 * M * (i + o) for _, i, o in SHAPES)
         flops = 2 * M * sum(i * o for _, i, o in SHAPES)
         kern = ("xq2_stage + mm_i8_kernel (int8 mma.sync, one weight pass; down_proj K split 4 ways)" if M == 2 else
-                "xq2_stage + mm_i8x4_kernel (int8 mma.sync, one weight pass; down_proj K split 4 ways)"
+                "xq2_stage + mm_i8x4_kernel (int8 mma.sync, B in TMEM, one weight pass; down_proj K split 4 ways)"
                 if M <= 4 else
-                "xh_stage + mm_q4k_kernel (mma.sync)" if M <= 8 else
+                "xq2_stage + mm_i8x8_kernel (int8 mma.sync, B in TMEM, one weight pass; down_proj K split 4 ways)"
+                if M <= 8 else
                 "xh_stage + mm_skinny_kernel (split-K tcgen05)" if M <= 16 else
                 "xh_stage + mm_q4k_kernel (mma.sync)" if M < 24 else "xh_stage + mm_tc_kernel (tcgen05)")
         r = {"ms_per_layer": round(ms, 4), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
@@ -594,8 +595,8 @@ def small_m_sweep(L, ctx, weights, stream, timed, capture, dev, g, pk, host_bloc
                          roofline_tensor(flops, ms, pk, kern + ", 7 linears of a layer"))
         res[str(M)] = r
         del gr
-    res["note"] = ("7 rq_linear calls per layer, 4 rotating layer copies. M = 2..4: 24-bit int8-plane "
-                   "staging + the int8 mma.sync kernel, weights read once; M = 5..8, 17..23: f16 hi/lo staging + the mma.sync "
+    res["note"] = ("7 rq_linear calls per layer, 4 rotating layer copies. M = 2..8: 24-bit int8-plane "
+                   "staging + the int8 mma.sync kernels, weights read once; M = 17..23: f16 hi/lo staging + the mma.sync "
                    "tensor-core kernel, weights read once per 8-row tile; M = 9..16: split-K tcgen05; "
                    "M >= 24: the tiled tcgen05 kernel (exact sc*q weights in TMEM)")
     if host_blocks is not None:
