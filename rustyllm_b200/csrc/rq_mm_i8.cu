@@ -612,6 +612,34 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8_kernel(const I8Params p) 
 }
 
 
+// TMEM loads / stores of 8 and 16 32-bit columns (32x32b: lane i of the
+// warp's lane quarter, one column per register)
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16p(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16p(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
 // ------------------------------------------------- three or four tokens
 //
 // The same data path and A operand; B has 12 columns, n = 4 p + m (plane p
@@ -777,7 +805,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
             for (int s = 0; s < kI8MaxSB; s++) {
                 if (live && s < nsbw) {
                     const int sb = sb0 + s;
-                    uint32_t bq[16];  // B words of half the super-block's sub-blocks (TMEM)
+                    // B words of the super-block's eight sub-blocks (TMEM): both halves
+                    // requested before one wait, so one load latency per super-block
+                    uint32_t bq[32];
                     const float cf0 = ca0 ? __ldg(sxa0 + sb) * pwa : 0.0f, cf1 = ca1 ? __ldg(sxa1 + sb) * pwa : 0.0f;
                     const float cg0 = cb0 ? __ldg(sxb0 + sb) * pwb : 0.0f, cg1 = cb1 ? __ldg(sxb1 + sb) * pwb : 0.0f;
                     if constexpr (Q3) {
@@ -795,10 +825,12 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                                                     *reinterpret_cast<const uint32_t*>(q8 + 32 * c),
                                                     *reinterpret_cast<const uint32_t*>(q8 + 32 * c + 16)};
                             const uint32_t scg = hg4[c], sc8 = h84[c];
-                            if (c == 0 || c == 2) {  // B of 32-element chunks 2c .. 2c+3
-                                tc::tmem_ld16(tb + 32u * (uint32_t)s + 8u * (uint32_t)c, bq);
+                            if (c == 0) {
+                                tmem_ld16p(tb + 32u * (uint32_t)s, bq);
+                                tmem_ld16p(tb + 32u * (uint32_t)s + 16u, bq + 16);
                                 tc::tmem_wait_ld();
                             }
+                            const uint32_t* bh = bq + 16 * (c >> 1);  // chunks 2c .. 2c+3
 #pragma unroll
                             for (int q = 0; q < 4; q++) {
                                 // sub-block 4c + q: low (q < 2) or high nibbles of
@@ -807,7 +839,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                                 const uint32_t ag = q < 2 ? q3_lo(wq[q & 1]) : q3_hi(wq[q & 1]);
                                 const uint32_t a8 = q < 2 ? q3_lo(wq[2 + (q & 1)]) : q3_hi(wq[2 + (q & 1)]);
                                 const int cj = (2 * c + (q >> 1)) & 3;  // chunk within the loaded half
-                                const uint32_t b0 = bq[4 * cj + (q & 1)], b1 = bq[4 * cj + 2 + (q & 1)];
+                                const uint32_t b0 = bh[4 * cj + (q & 1)], b1 = bh[4 * cj + 2 + (q & 1)];
                                 int d0[4], d1[4];
                                 mma_s8s8_k16(d0, ag, a8, b0);
                                 mma_s8s8_k16(d1, ag, a8, b1);
@@ -850,12 +882,13 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                             const uint32_t w8 = *reinterpret_cast<const uint32_t*>(q8 + 16 * j);
                             const uint32_t a[4] = {wg & 0x0F0F0F0Fu, w8 & 0x0F0F0F0Fu, (wg >> 4) & 0x0F0F0F0Fu,
                                                    (w8 >> 4) & 0x0F0F0F0Fu};
-                            if (j == 0 || j == 4) {  // B of blocks j .. j+3
-                                tc::tmem_ld16(tb + 32u * (uint32_t)s + 4u * (uint32_t)j, bq);
+                            if (j == 0) {
+                                tmem_ld16p(tb + 32u * (uint32_t)s, bq);
+                                tmem_ld16p(tb + 32u * (uint32_t)s + 16u, bq + 16);
                                 tc::tmem_wait_ld();
                             }
-                            const uint32_t b00 = bq[4 * (j & 3)], b01 = bq[4 * (j & 3) + 1];
-                            const uint32_t b10 = bq[4 * (j & 3) + 2], b11 = bq[4 * (j & 3) + 3];
+                            const uint32_t b00 = bq[4 * j], b01 = bq[4 * j + 1];
+                            const uint32_t b10 = bq[4 * j + 2], b11 = bq[4 * j + 3];
                             int d0[4], d1[4];
                             mma_u8s8(d0, a, b00, b01);
                             mma_u8s8(d1, a, b10, b11);
@@ -898,10 +931,12 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
                         for (int c = 0; c < 4; c++) {
                             const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
                             const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
-                            if (c == 0 || c == 2) {  // B of sub-blocks 2c .. 2c+3
-                                tc::tmem_ld16(tb + 32u * (uint32_t)s + 8u * (uint32_t)c, bq);
+                            if (c == 0) {
+                                tmem_ld16p(tb + 32u * (uint32_t)s, bq);
+                                tmem_ld16p(tb + 32u * (uint32_t)s + 16u, bq + 16);
                                 tc::tmem_wait_ld();
                             }
+                            const uint32_t* bh = bq + 16 * (c >> 1);  // sub-blocks 2c .. 2c+3
                             const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
                                                      w8.y & 0x0F0F0F0Fu};
                             const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
@@ -909,8 +944,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
     #pragma unroll
                             for (int h = 0; h < 2; h++) {
                                 const int sub = (2 * c + h) & 3;  // within the loaded half
-                                const uint2 b0 = make_uint2(bq[4 * sub], bq[4 * sub + 1]);
-                                const uint2 b1 = make_uint2(bq[4 * sub + 2], bq[4 * sub + 3]);
+                                const uint2 b0 = make_uint2(bh[4 * sub], bh[4 * sub + 1]);
+                                const uint2 b1 = make_uint2(bh[4 * sub + 2], bh[4 * sub + 3]);
                                 int d0[4], d1[4];
                                 if (h == 0) {
                                     mma_u8s8(d0, alo, b0.x, b0.y);
@@ -1016,32 +1051,6 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x4_kernel(const I8Params p
 // half super-block.  The eight K-slice partials of a stage's rows are summed
 // in slice order through a double-buffered table [row][slice][token] after
 // a barrier of the consumer warps, and y is written per stage.
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* v) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
-                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_ld16p(uint32_t taddr, uint32_t* r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_st16p(uint32_t taddr, const uint32_t* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-            taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
-}
 
 constexpr int kI8x8Cols = 512;  // TMEM columns of the eight-token form
 
@@ -1197,7 +1206,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x8_kernel(const I8Params p
                         cf[pl][1] = x1 * pw[pl];
                     }
                     const uint32_t colb = tb + 64u * (uint32_t)s;
-                    uint32_t bq[24];  // B words of four sub-blocks: [sub][plane][word]
+                    // B words of the eight sub-blocks, [half][sub][plane][word]: both
+                    // halves requested before one wait
+                    uint32_t bq[48];
                     int a[3][4];
 #pragma unroll
                     for (int pl = 0; pl < 3; pl++)
@@ -1217,11 +1228,14 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x8_kernel(const I8Params p
                                                     *reinterpret_cast<const uint32_t*>(q8 + 32 * c),
                                                     *reinterpret_cast<const uint32_t*>(q8 + 32 * c + 16)};
                             const uint32_t scg = hg4[c], sc8 = h84[c];
-                            if (c == 0 || c == 2) {  // B of 32-element chunks 2c .. 2c+3
-                                tmem_ld16p(colb + 16u * (uint32_t)c, bq);
-                                tmem_ld8(colb + 16u * (uint32_t)c + 16u, bq + 16);
+                            if (c == 0) {
+                                tmem_ld16p(colb, bq);
+                                tmem_ld8(colb + 16u, bq + 16);
+                                tmem_ld16p(colb + 32u, bq + 24);
+                                tmem_ld8(colb + 48u, bq + 40);
                                 tc::tmem_wait_ld();
                             }
+                            const uint32_t* bh = bq + 24 * (c >> 1);  // chunks 2c .. 2c+3
 #pragma unroll
                             for (int q = 0; q < 4; q++) {
                                 const uint32_t ag = q < 2 ? q3_lo(wq[q & 1]) : q3_hi(wq[q & 1]);
@@ -1232,7 +1246,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x8_kernel(const I8Params p
 #pragma unroll
                                 for (int pl = 0; pl < 3; pl++) {
                                     int d[4];
-                                    mma_s8s8_k16(d, ag, a8, bq[6 * cj + 2 * pl + (q & 1)]);
+                                    mma_s8s8_k16(d, ag, a8, bh[6 * cj + 2 * pl + (q & 1)]);
                                     a[pl][0] += d[0] * sg; a[pl][1] += d[1] * sg;
                                     a[pl][2] += d[2] * s8; a[pl][3] += d[3] * s8;
                                 }
@@ -1259,19 +1273,22 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x8_kernel(const I8Params p
                             const uint32_t w8 = *reinterpret_cast<const uint32_t*>(q8 + 16 * jb8);
                             const uint32_t am[4] = {wg & 0x0F0F0F0Fu, w8 & 0x0F0F0F0Fu, (wg >> 4) & 0x0F0F0F0Fu,
                                                     (w8 >> 4) & 0x0F0F0F0Fu};
-                            if (jb8 == 0 || jb8 == 4) {  // B of blocks jb8 .. jb8+3
-                                tmem_ld16p(colb + 8u * (uint32_t)jb8, bq);
-                                tmem_ld8(colb + 8u * (uint32_t)jb8 + 16u, bq + 16);
+                            if (jb8 == 0) {
+                                tmem_ld16p(colb, bq);
+                                tmem_ld8(colb + 16u, bq + 16);
+                                tmem_ld16p(colb + 32u, bq + 24);
+                                tmem_ld8(colb + 48u, bq + 40);
                                 tc::tmem_wait_ld();
                             }
                             const float2 dgp = __half22float2(*reinterpret_cast<const __half2*>(&dgw[jb8 >> 1]));
                             const float2 d8p = __half22float2(*reinterpret_cast<const __half2*>(&d8w[jb8 >> 1]));
                             const float dg = (jb8 & 1) ? dgp.y : dgp.x, d8 = (jb8 & 1) ? d8p.y : d8p.x;
+                            const uint32_t* bh = bq + 24 * (jb8 >> 2);
                             const int jj = jb8 & 3;
 #pragma unroll
                             for (int pl = 0; pl < 3; pl++) {
                                 int d[4];
-                                mma_u8s8(d, am, bq[6 * jj + 2 * pl], bq[6 * jj + 2 * pl + 1]);
+                                mma_u8s8(d, am, bh[6 * jj + 2 * pl], bh[6 * jj + 2 * pl + 1]);
                                 acc[pl][0] = fmaf(i2f_small(d[0]), dg * cf[pl][0], acc[pl][0]);
                                 acc[pl][1] = fmaf(i2f_small(d[1]), dg * cf[pl][1], acc[pl][1]);
                                 acc[pl][2] = fmaf(i2f_small(d[2]), d8 * cf[pl][0], acc[pl][2]);
@@ -1300,11 +1317,14 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x8_kernel(const I8Params p
                         for (int c = 0; c < 4; c++) {
                             const uint2 wg = *reinterpret_cast<const uint2*>(qg + 32 * c);
                             const uint2 w8 = *reinterpret_cast<const uint2*>(q8 + 32 * c);
-                            if (c == 0 || c == 2) {  // B of sub-blocks 2c .. 2c+3
-                                tmem_ld16p(colb + 16u * (uint32_t)c, bq);
-                                tmem_ld8(colb + 16u * (uint32_t)c + 16u, bq + 16);
+                            if (c == 0) {
+                                tmem_ld16p(colb, bq);
+                                tmem_ld8(colb + 16u, bq + 16);
+                                tmem_ld16p(colb + 32u, bq + 24);
+                                tmem_ld8(colb + 48u, bq + 40);
                                 tc::tmem_wait_ld();
                             }
+                            const uint32_t* bh = bq + 24 * (c >> 1);  // sub-blocks 2c .. 2c+3
                             const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu,
                                                      w8.y & 0x0F0F0F0Fu};
                             const uint32_t ahi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (w8.x >> 4) & 0x0F0F0F0Fu,
@@ -1320,9 +1340,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) mm_i8x8_kernel(const I8Params p
                                 for (int pl = 0; pl < 3; pl++) {
                                     int d[4];
                                     if (h == 0)
-                                        mma_u8s8(d, alo, bq[6 * sub + 2 * pl], bq[6 * sub + 2 * pl + 1]);
+                                        mma_u8s8(d, alo, bh[6 * sub + 2 * pl], bh[6 * sub + 2 * pl + 1]);
                                     else
-                                        mma_u8s8(d, ahi, bq[6 * sub + 2 * pl], bq[6 * sub + 2 * pl + 1]);
+                                        mma_u8s8(d, ahi, bh[6 * sub + 2 * pl], bh[6 * sub + 2 * pl + 1]);
                                     a[pl][0] += d[0] * sg; a[pl][1] += d[1] * sg;
                                     a[pl][2] += d[2] * s8; a[pl][3] += d[3] * s8;
                                 }
