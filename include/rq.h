@@ -170,9 +170,9 @@ RQ_API int rq_linear_allreduce(rq_ctx* ctx, const rq_weight* w, const float* x, 
  *     alignment; e.g. M <= 20 at in = 28672, M <= 73 at in = 8192); larger
  *     requests fail with RQ_ERR_INVALID and a message;
  *   - every row runs the M=1 matvec kernels, so results match rq_linear's
- *     within the linear parity tolerance (relative L2 <= 1e-4; for M = 1
- *     and 3 they are the same kernels, and for M = 2 unless rq_linear takes
- *     its int8 tensor-core kernel: Q4_K with in <= 8192); weights with no
+ *     within the linear parity tolerance (relative L2 <= 1e-4; the same
+ *     kernels at M = 1, while from M = 2 rq_linear takes its tensor-core
+ *     kernels where the weight's type and shape allow); weights with no
  *     M=1 pipeline shape --
  *     Q8_0 / Q5_K with in not a multiple of 256, Q6_K / Q2_K with in not a
  *     multiple of 1024, any type with in > 30720 other than Q4_0 / Q4_K /
