@@ -1152,16 +1152,16 @@ def fused_allreduce_default(world: int) -> bool:
     return os.environ.get("RQ_TP_FUSED") != "0" and world >= 2
 
 
-CASES = ("pipe_gate_up", "i8_gate_m2", "i8_gate_m4", "mm_gate_m8", "sk_gate_m16", "tc_gate_m128", "q3k_gate", "tc_q3k_gate_m128", "moe_t1", "moe_t16",
+CASES = ("pipe_gate_up", "i8_gate_m2", "i8_gate_m4", "i8_gate_m8", "mm_gate_m20", "sk_gate_m16", "tc_gate_m128", "q3k_gate", "tc_q3k_gate_m128", "moe_t1", "moe_t16",
          "attn_decode")
 
 
 def run_case(name: str) -> None:
     """A few launches of one kernel or layer for an ncu capture, at the
     bench's shapes: 'pipe_gate_up' (the gate+up rq_linear_batch of one 70B
-    layer, M=1), 'i8_gate_m2' / 'i8_gate_m4' (gate_proj 8192 -> 28672 at
-    M=2 / 4, the int8 tensor-core kernel), 'mm_gate_m8' (gate_proj at M=8,
-    mma.sync),
+    layer, M=1), 'i8_gate_m2' / 'i8_gate_m4' / 'i8_gate_m8' (gate_proj
+    8192 -> 28672 at M=2 / 4 / 8, the int8 tensor-core kernels),
+    'mm_gate_m20' (M=20, the mma.sync kernel in 8-row tiles),
     'sk_gate_m16' (M=16, split-K tcgen05), 'tc_gate_m128' (M=128, tiled
     tcgen05), 'q3k_gate' (the Q3_K gate_proj matvec), 'tc_q3k_gate_m128'
     (Q3_K gate_proj at M=128 on tcgen05), 'moe_t1' / 'moe_t16'
@@ -1213,7 +1213,8 @@ def run_case(name: str) -> None:
                                         arr([x.data_ptr()] * 2), arr([y.data_ptr() for y in ys]), s))
             nbytes = 2 * Q4K_BYTES(8192, 28672)
         else:
-            M = {"i8_gate_m2": 2, "i8_gate_m4": 4, "mm_gate_m8": 8, "sk_gate_m16": 16, "q3k_gate": 1}.get(name, 128)
+            M = {"i8_gate_m2": 2, "i8_gate_m4": 4, "i8_gate_m8": 8, "mm_gate_m20": 20, "sk_gate_m16": 16,
+                 "q3k_gate": 1}.get(name, 128)
             x = torch.randn(M, 8192, device="cuda", generator=g)
             y = torch.empty(M, 28672, device="cuda")
 
