@@ -140,6 +140,15 @@ RQ_API int rq_linear(rq_ctx* ctx, const rq_weight* w, const float* x, float* y, 
 RQ_API int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const float* const* x,
                            float* const* y, void* stream);
 
+/* A prefetch hint, no reference counterpart: the next M=1 pipeline launch
+ * of rq_linear / rq_linear_batch / rq_linear_allreduce on this context
+ * prefetches into L2, after its last weight copy, the first rows of these n
+ * (<= 3, of one type and in_features) weights -- the weights the caller
+ * multiplies next, as a layer loop knows them -- so HBM keeps streaming
+ * through the launch gap.  Consumed by that launch; n = 0 clears it.  No
+ * effect on results; captured into CUDA graphs like the launch itself. */
+RQ_API int rq_linear_prefetch_hint(rq_ctx* ctx, int n, const rq_weight* const* w);
+
 /* Row-parallel linear under tensor parallelism: y[M][out] = the sum over
  * the ranks of x_r[M][in] * W_r^T, where W_r is this rank's column slice of
  * the weight (the o_proj / down_proj shard) and x_r its slice of the input;

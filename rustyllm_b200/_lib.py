@@ -52,6 +52,7 @@ SIGNATURES = {
     "rq_ctx_status": (I, [P]),
     "rq_linear_allreduce": (I, [P, P, P, P, I64, P]),
     "rq_linear_batch": (I, [P, I, PP, PP, PP, P]),
+    "rq_linear_prefetch_hint": (I, [P, I, PP]),
 }
 
 class LlamaConfig(ctypes.Structure):

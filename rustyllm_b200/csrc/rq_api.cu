@@ -273,8 +273,18 @@ int linear_device(rq_ctx* ctx, const rq_weight* w, const float* xd, float* yd, i
     xq.planes = (int8_t*)ws;
     xq.stats = (float4*)(ws + (((size_t)M * 3 * w->in + 255) & ~(size_t)255));
     rc = launch_xquant(xd, M, w->in, xq, st);
-    if (!rc) rc = launch_linear(w, xq, yd, M, ctx->sm_count, st, ctx->derr);
+    const PipeNext nx = take_hint(ctx);
+    if (!rc) rc = launch_linear(w, xq, yd, M, ctx->sm_count, st, ctx->derr, &nx);
     return rc;
+}
+
+// bytes per CTA of the hinted weights' first rows (the decode loop's budget)
+constexpr uint32_t kHintBudget = 128 * 1024;
+
+PipeNext take_hint(rq_ctx* ctx) {
+    const PipeNext nx = pipe_next(ctx->hint_w, ctx->hint_n, kHintBudget);
+    ctx->hint_n = 0;
+    return nx;
 }
 
 int queue_error_readback(rq_ctx* ctx, cudaStream_t st) {
@@ -585,7 +595,9 @@ int rq_linear_allreduce(rq_ctx* ctx, const rq_weight* w, const float* x, float* 
         rc = launch_xquant(x, 1, w->in, xq, st);
         if (rc) return rc;
         const float* add = nullptr;
-        rc = launch_matvec_pipe(&w, &xq, &y, 1, ctx->sm_count, st, ctx->derr, &add, &ar);
+        const PipeNext nx = take_hint(ctx);
+        rc = launch_matvec_pipe(&w, &xq, &y, 1, ctx->sm_count, st, ctx->derr, &add, &ar, nullptr, nullptr, nullptr,
+                                &nx);
         if (rc != kPipeNotFusable) return rc;
     }
     // the partial product into the workspace's tail, then the all-reduce
@@ -641,7 +653,24 @@ int rq_linear_batch(rq_ctx* ctx, int n, const rq_weight* const* w, const float* 
     XQ xqs[kMaxJobs];
     for (int j = 0; j < n; j++)
         xqs[j] = XQ{xq.planes + (int64_t)row_of[j] * 3 * in, xq.stats + (int64_t)row_of[j] * (in / 32)};
-    return launch_matvec_pipe(w, xqs, y, n, ctx->sm_count, st, ctx->derr);
+    const PipeNext nx = take_hint(ctx);
+    return launch_matvec_pipe(w, xqs, y, n, ctx->sm_count, st, ctx->derr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                              &nx);
+}
+
+/* A hint, no reference counterpart: the next M=1 pipeline launch of
+ * rq_linear / rq_linear_batch / rq_linear_allreduce on this context
+ * prefetches into L2, after its last weight copy, the first rows of these
+ * n (<= 3) weights -- what the caller will multiply next (the decode loop
+ * does the same between its own launches).  n = 0 clears it.  No effect on
+ * results. */
+int rq_linear_prefetch_hint(rq_ctx* ctx, int n, const rq_weight* const* w) {
+    if (!ctx || n < 0 || n > 3 || (n > 0 && !w)) return set_error(RQ_ERR_INVALID, "rq_linear_prefetch_hint: bad argument");
+    for (int i = 0; i < n; i++)
+        if (!w[i]) return set_error(RQ_ERR_INVALID, "rq_linear_prefetch_hint: NULL weight %d", i);
+    for (int i = 0; i < n; i++) ctx->hint_w[i] = w[i];
+    ctx->hint_n = n;
+    return RQ_OK;
 }
 
 }  // extern "C"

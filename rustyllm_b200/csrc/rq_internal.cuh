@@ -111,6 +111,10 @@ struct rq_ctx {
     int* derr = nullptr;
     int* err_host = nullptr;
     int* i8_cnt = nullptr;   // int8 matmul split-K arrivals per row group (kept at zero between launches)
+    // rq_linear_prefetch_hint: weights whose first rows the next M=1
+    // pipeline launch of this context prefetches into L2 in its tail
+    const rq_weight* hint_w[3] = {nullptr, nullptr, nullptr};
+    int hint_n = 0;
 };
 
 namespace rq {
@@ -362,7 +366,10 @@ int launch_xquant_rmsnorm(const float* x, const float* w, float eps, int64_t M, 
 int launch_xquant_swiglu(const float* gate, const float* up, int64_t M, int64_t in, XQ xq,
                          cudaStream_t st);
 int launch_xquant_rows(const float* const* xs, int n, int64_t in, XQ xq, cudaStream_t st);
+struct PipeNext;
 int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, cudaStream_t st,
-                  int* err = nullptr);
+                  int* err = nullptr, const PipeNext* next = nullptr);
+// The context's prefetch hint as a PipeNext (and the hint cleared), or n = 0.
+PipeNext take_hint(rq_ctx* ctx);
 
 }  // namespace rq

@@ -342,7 +342,8 @@ int launch_xquant_rows(const float* const* xs, int n, int64_t in, XQ xq, cudaStr
     return launch_xquant_impl(rows, n, in, xq, st);
 }
 
-int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, cudaStream_t st, int* err) {
+int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, cudaStream_t st, int* err,
+                  const PipeNext* next) {
     if (pipe_supported(w)) {
         // every activation row is one job of the pipelined kernel
         for (int64_t m0 = 0; m0 < M; m0 += kMaxJobs) {
@@ -355,7 +356,9 @@ int launch_linear(const rq_weight* w, XQ xq, float* y, int64_t M, int sm_count, 
                 xqs[j] = XQ{xq.planes + (m0 + j) * 3 * w->in, xq.stats + (m0 + j) * (w->in / 32)};
                 ys[j] = y + (m0 + j) * w->out;
             }
-            int rc = launch_matvec_pipe(ws, xqs, ys, n, sm_count, st, err);
+            // the last launch prefetches the hinted weights
+            int rc = launch_matvec_pipe(ws, xqs, ys, n, sm_count, st, err, nullptr, nullptr, nullptr, nullptr,
+                                        nullptr, m0 + n == M ? next : nullptr);
             if (rc) return rc;
         }
         return RQ_OK;
