@@ -425,3 +425,34 @@ def test_linear_batch_matches_single_calls(oracle, rq_ctx, qtype):
     rc = L.rq_linear_batch(rq_ctx.handle, 2, arr([ws[0].handle.value, w2.handle.value]),
                            arr([x_shared.data_ptr()] * 2), arr([ys[0].data_ptr()] * 2), None)
     assert rc == 1
+
+
+def test_prefetch_hint_leaves_results_unchanged(oracle, rq_ctx):
+    """rq_linear_prefetch_hint only adds an L2 prefetch to the next pipeline
+    launch: the hinted call and the plain call give the same bits; bad
+    arguments are rejected."""
+    import ctypes
+    import torch
+    from rustyllm_b200 import QWeight, RqError
+    from rustyllm_b200._lib import check, lib
+    L = lib()
+    out, n_in = 1024, 4096
+    ws = []
+    for s in range(3):
+        _, blocks = make_weight(oracle, 12, out, n_in, seed=50 + s)
+        ws.append(QWeight.upload(rq_ctx, 12, blocks, out, n_in))
+    x = torch.randn(1, n_in, device="cuda")
+    y0 = torch.empty(1, out, device="cuda")
+    y1 = torch.empty(1, out, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    check(L.rq_linear(rq_ctx.handle, ws[0].handle, x.data_ptr(), y0.data_ptr(), 1, st))
+    arr = (ctypes.c_void_p * 2)(ws[1].handle.value, ws[2].handle.value)
+    check(L.rq_linear_prefetch_hint(rq_ctx.handle, 2, arr))
+    check(L.rq_linear(rq_ctx.handle, ws[0].handle, x.data_ptr(), y1.data_ptr(), 1, st))
+    torch.cuda.synchronize()
+    assert torch.equal(y0.view(torch.int32), y1.view(torch.int32))
+    with pytest.raises(RqError):
+        check(L.rq_linear_prefetch_hint(rq_ctx.handle, 4, arr))
+    check(L.rq_linear_prefetch_hint(rq_ctx.handle, 0, None))
+    for w in ws:
+        w.free()
