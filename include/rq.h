@@ -240,6 +240,13 @@ RQ_API int rq_moe_free(rq_moe* m);
  * sizes the layer's buffers).  From T = 4 on, the per-expert token counts
  * are read back to the host once (the reference reads its whole routing
  * table there, :284-286) to pick each segment's kernel. */
+/* Forwards of up to max_tokens tokens plan on the device (default and
+ * minimum 3): every routing slot becomes one M=1 matvec job whose expert
+ * the kernel reads from the routing table -- no host synchronisation,
+ * asynchronous and graph-capturable at that T, slower than the host plan
+ * from about 4 tokens (each slot streams its expert's weights). */
+RQ_API int rq_moe_set_device_plan(rq_moe* m, int64_t max_tokens);
+
 RQ_API int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
                           int32_t* expert_ids_out, int32_t* perm_out, void* stream);
 /* Expert-parallel forward over the communicator of ctx: expert e lives on

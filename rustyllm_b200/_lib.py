@@ -87,6 +87,7 @@ SIGNATURES.update({
     "rq_moe_create": (I, [P, I, I, I64, I64, P, PP, PP, PP, PP]),
     "rq_moe_free": (I, [P]),
     "rq_moe_forward": (I, [P, P, P, P, I64, P, P, P]),
+    "rq_moe_set_device_plan": (I, [P, I64]),
     "rq_moe_forward_ep": (I, [P, P, P, P, I64, P, P, P]),
     "rq_gguf_open": (I, [ctypes.c_char_p, PP]),
     "rq_gguf_open_memory": (I, [P, SZ, PP]),

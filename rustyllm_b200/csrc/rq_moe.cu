@@ -32,6 +32,7 @@ struct rq_moe {
     __half* router;  // [E][H], F16 as ParallelLinear::new stores it
     const uint8_t** wtab = nullptr;  // device [kind gate/up/down][qs/hdr][E] expert weight pointers
     std::vector<const rq_weight*> w1, w3, w2;  // NULL for experts of other ranks (expert parallel)
+    int64_t dev_plan_max = 3;  // forwards of up to this many tokens plan on the device (rq_moe_set_device_plan)
     // per-forward routing buffers, T tokens (S = T k slots), grown on demand
     int64_t cap_t = 0;
     float* logits = nullptr;     // [T][E]
@@ -764,6 +765,19 @@ int rq_moe_free(rq_moe* m) {
     return RQ_OK;
 }
 
+/* Forwards of up to max_tokens tokens plan on the device: every routing
+ * slot is one M=1 matvec job whose expert the kernel reads from the routing
+ * table, so no host synchronisation, asynchronous and graph-capturable at
+ * that T, but each slot streams its expert's weights (from about 4 tokens
+ * the host plan, which reads each touched expert once per segment, is
+ * faster).  Default and minimum 3 (below 4 tokens both plans are the same
+ * kernels and bits). */
+int rq_moe_set_device_plan(rq_moe* m, int64_t max_tokens) {
+    if (!m || max_tokens < 0) return set_error(RQ_ERR_INVALID, "rq_moe_set_device_plan: bad argument");
+    m->dev_plan_max = std::max<int64_t>(3, max_tokens);
+    return RQ_OK;
+}
+
 int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
                    int32_t* expert_ids_out, int32_t* perm_out, void* stream) {
     if (!ctx || !m || !x || !y) return set_error(RQ_ERR_INVALID, "rq_moe_forward: NULL argument");
@@ -777,7 +791,9 @@ int rq_moe_forward(rq_ctx* ctx, rq_moe* m, const float* x, float* y, int64_t T,
     const int64_t S = T * m->k;
     // below kMinTensorM tokens no expert gets a tensor-core segment, so the
     // kernel of every slot is known without the routing: plan on the device
-    bool dev_plan = T < kMinTensorM && m->k <= kMaxJobs && m->F % 32 == 0;
+    // (up to dev_plan_max tokens when the caller asks for it: every slot an
+    // M=1 job, asynchronous and graph-capturable at any T)
+    bool dev_plan = T <= std::max<int64_t>(kMinTensorM - 1, m->dev_plan_max) && m->k <= kMaxJobs && m->F % 32 == 0;
     for (int e = 0; e < m->E && dev_plan; e++)
         dev_plan = pipe_supported(m->w1[(size_t)e]) && pipe_supported(m->w3[(size_t)e]) &&
                    pipe_supported(m->w2[(size_t)e]);

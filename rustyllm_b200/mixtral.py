@@ -73,6 +73,11 @@ class SparseMoe:
 
     __call__ = forward
 
+    def set_device_plan(self, max_tokens: int) -> None:
+        """Forwards of up to max_tokens tokens plan on the device (no host
+        synchronisation, graph-capturable; slower from about 4 tokens)."""
+        check(_lib.lib().rq_moe_set_device_plan(self.handle, int(max_tokens)))
+
     def close(self):
         if self.handle:
             _lib.lib().rq_moe_free(self.handle)

@@ -132,17 +132,21 @@ def test_mixtral_geometry_matches_oracle(oracle, mixtral_layer, T):
     assert rel_l2(y, y_ref) <= REL_L2_TOL
 
 
-@pytest.mark.parametrize("T", [1, 2, 3])
-def test_moe_small_batches_stay_on_device_and_capture(oracle, rq_ctx, T):
-    """Below four tokens the layer runs without a host synchronisation: the
-    forward is captured in a CUDA graph, replayed on new inputs written into
-    the captured buffer, and every replay matches the oracle (ids bit-exact,
-    outputs within 1e-4) and the eager call bit for bit."""
+@pytest.mark.parametrize("T,plan", [(1, 0), (2, 0), (3, 0), (16, 16), (33, 64)])
+def test_moe_small_batches_stay_on_device_and_capture(oracle, rq_ctx, T, plan):
+    """Below four tokens -- and up to rq_moe_set_device_plan's bound when a
+    caller raises it (16 and 33 tokens here) -- the layer runs without a
+    host synchronisation: the forward is captured in a CUDA graph, replayed
+    on new inputs written into the captured buffer, and every replay matches
+    the oracle (ids bit-exact, outputs within 1e-4) and the eager call bit
+    for bit."""
     import torch
     from rustyllm_b200.mixtral import SparseMoe
     E, H, F = 8, 512, 1024
     wr, blocks, experts = make_layer(oracle, rq_ctx, E, H, F, 12, seed=300 + T)
     moe = SparseMoe(wr, experts, top_k=2)
+    if plan:
+        moe.set_device_plan(plan)
     x = torch.zeros(T, H, device="cuda")
     y = moe.forward(x)                      # sizes the layer's buffers
     s = torch.cuda.Stream()
