@@ -1025,8 +1025,9 @@ def run_gpu(args) -> None:
 
     # e2e: the public calls with host buffers -- every step copies its four
     # activation rows (one packed page-locked host buffer) to the device,
-    # runs the four calls, copies the seven outputs back to one page-locked
-    # host buffer and synchronises once.  The step (two copies, four calls)
+    # runs the four calls (each after the prefetch hint naming the next
+    # call's weights, as in the device-timed step), copies the seven outputs
+    # back to one page-locked host buffer and synchronises once.  The step (two copies, four calls)
     # is captured in a CUDA graph per layer copy, as a decoder would.
     nx = [8192, 8192 // world, 8192, 28672 // world]
     hxin = torch.randn(sum(nx), generator=torch.Generator().manual_seed(7)).pin_memory()
@@ -1056,6 +1057,7 @@ def run_gpu(args) -> None:
         for gi, grp in enumerate(groups):
             if gi == 1:
                 main.wait_event(rows_in)
+            hint(c, gi)
             launch_group(c, grp, main.cuda_stream, xs_e, ys_e)
             copy_stream.wait_stream(main)
             with torch.cuda.stream(copy_stream):
@@ -1124,7 +1126,7 @@ def run_gpu(args) -> None:
             "data": "synthetic: W ~ N(0,0.02) f32 quantized to Q4_K on device (seeded), x ~ N(0,1)",
             "config": headline_config(world),
             "method": ("value: each of the 4 calls after rq_linear_prefetch_hint naming the next call's weights "
-                       "(the next layer copy's q/k/v after down); e2e: the plain calls, no hints"),
+                       "(the next layer copy's q/k/v after down); e2e: the same calls and hints on host buffers"),
             "pct_of_hbm_peak_per_gpu": round(100 * value / world / pk["hbm_gbs"], 1),
             "per_shape_single_call_gbs": per_shape,
             "roofline": roofline_hbm(dom_bytes, dom_ms, pk,

@@ -663,7 +663,9 @@ int row_parallel_mm(rq_llama* m, const rq_weight* w, int64_t T, cudaStream_t st)
 
 // Prompt chunks of T >= kMinTensorM tokens with Q4_K weights (Q3_K from
 // kQ3TensorMinM tokens, on the tcgen05 kernel) run every linear on the
-// tensor cores, one pass over the weights per chunk.
+// f16 tensor-core kernels, one pass over the weights per chunk -- except
+// chunks whose seven linears all take the int8 kernels (up to eight tokens),
+// which stage the int8 planes instead (i8_ok).
 bool tensor_prefill(const rq_llama* m, int64_t T, int64_t l) {
     if (T < kMinTensorM || !m->xh.v) return false;
     bool all_i8 = true;
