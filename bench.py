@@ -660,9 +660,10 @@ def moe_sweep(device: int, pk, with_cpu: bool, seed: int = 4321) -> dict:
             r["tflops"] = round(flops / (ms / 1e3) / 1e12, 2)
             r["roofline"] = roofline_tensor(flops, ms, pk, "route + permute + expert tiles (mm_tc_kernel) + combine")
         else:
-            r["roofline"] = roofline_hbm(wb + 4 * T * H * 2, ms, pk,
-                                         "route + permute + expert products (M=1 pipeline / mma.sync) + combine",
-                                         f"moe_t{T}")
+            what = ("router (stages x) + gate/up matvec of the routed slots (SwiGLU staging epilogue) + down "
+                    "matvec (combine epilogue), planned on the device" if T < 4 else
+                    "route + permute + expert products (M=1 pipeline / mma.sync) + combine, planned on the host")
+            r["roofline"] = roofline_hbm(wb + 4 * T * H * 2, ms, pk, what, f"moe_t{T}")
         res[str(T)] = r
     res["config"] = "Mixtral-8x7B MoE layer: E=8, top-2, H=4096, F=14336, Q4_K experts, 1 GPU"
     moe.close()
